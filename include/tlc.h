@@ -1,0 +1,194 @@
+/*
+ * libtl_cuda: the C ABI under torchlite-cpp's matmul path on B200 (sm_100a).
+ *
+ * The reference library has no FFI: its operator API for this path is the C++
+ * free function  tl::Tensor tl::matmul(const Tensor&, const Tensor&)
+ * (include/tl/ops.h:24-26, src/ops.cpp:605-699) and the autograd node
+ * MatmulBackward (include/tl/autograd.h:177-182, src/autograd.cpp:341-384).
+ * The entry points below are what that C++ code binds to when it runs on the
+ * GPU: plain pointers, sizes and strides, status codes instead of exceptions
+ * (the C++ layer maps TLC_ERR_INVALID_ARGUMENT back to std::invalid_argument
+ * with the reference's message, available from tlc_last_error()).
+ *
+ * Pointers passed to the compute entry points are device pointers on the
+ * current CUDA device unless the function name ends in _host.  Streams are
+ * cudaStream_t passed as void* (NULL = the legacy default stream).
+ *
+ * Precision modes (argument `mode`):
+ *   TLC_MODE_EXACT   fp32 FFMA; every output element is the ascending-k chain
+ *                    c = fmaf(a[m,k], b[k,n], c) from c = 0, so results are
+ *                    bit-identical to the reference's gemm_blocked
+ *                    (src/ops.cpp:242-268), which compiles to that chain.
+ *   TLC_MODE_TF32    tcgen05 tensor cores, TF32 inputs, fp32 accumulation.
+ *   TLC_MODE_3XTF32  tcgen05, each operand split into TF32 hi + lo parts,
+ *                    three products accumulated in fp32 (near-fp32 accuracy).
+ *   TLC_MODE_DEFAULT the process default: environment variable TL_GEMM_MODE
+ *                    (exact | tf32 | 3xtf32), read once; exact if unset.
+ */
+#ifndef TLC_H
+#define TLC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TLC_MAX_DIMS 8
+
+typedef enum tlc_status {
+    TLC_OK = 0,
+    TLC_ERR_INVALID_ARGUMENT = 1, /* the reference throws std::invalid_argument here */
+    TLC_ERR_UNSUPPORTED = 2,
+    TLC_ERR_CUDA = 3,
+    TLC_ERR_OUT_OF_MEMORY = 4,
+    TLC_ERR_TIMEOUT = 5 /* a bounded wait inside a kernel gave up; see tlc_last_error() */
+} tlc_status;
+
+typedef enum tlc_mode {
+    TLC_MODE_DEFAULT = -1,
+    TLC_MODE_EXACT = 0,
+    TLC_MODE_TF32 = 1,
+    TLC_MODE_3XTF32 = 2
+} tlc_mode;
+
+/* A strided fp32 tensor view: the layout of tl::Tensor (include/tl/tensor.h:13-67:
+ * sizes_, strides_ in elements, data_ + offset_).  `data` points at element
+ * [0,...,0], i.e. storage + storage_offset. */
+typedef struct tlc_tensor {
+    float* data;
+    int32_t ndim;
+    int64_t sizes[TLC_MAX_DIMS];
+    int64_t strides[TLC_MAX_DIMS];
+} tlc_tensor;
+
+/* One batched, strided GEMM: for every batch index b (up to 3 batch dims,
+ * row-major order), C_b[m,n] = sum_k A_b[m,k] * B_b[k,n] with
+ *   A_b[m,k] = A[off_a(b) + m*a_rs + k*a_cs]     (a_cs == 1: row-major A;
+ *   B_b[k,n] = B[off_b(b) + k*b_rs + n*b_cs]      a_rs == 1: transposed view)
+ *   C_b[m,n] = C[off_c(b) + m*c_rs + n]
+ *   off_x(b) = sum_j idx_j(b) * x_bstride[j]     (0 = broadcast over that dim).
+ * Replaces the batch loop + get_broadcast_index + gemm_mt/gemm_tiled dispatch
+ * of src/ops.cpp:655-674 and the kernels it reaches (src/ops.cpp:242-602). */
+typedef struct tlc_gemm_desc {
+    int64_t M, N, K;
+    const float* A;
+    int64_t a_rs, a_cs;
+    const float* B;
+    int64_t b_rs, b_cs;
+    float* C;
+    int64_t c_rs;
+    int32_t batch_ndim;
+    int64_t batch_sizes[3];
+    int64_t a_bstride[3], b_bstride[3], c_bstride[3];
+} tlc_gemm_desc;
+
+/* ---- library ---------------------------------------------------------- */
+
+int tlc_version(void);
+const char* tlc_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none).  For
+ * TLC_ERR_INVALID_ARGUMENT it is the reference's exception text. */
+const char* tlc_last_error(void);
+/* Number of CUDA kernels this library has launched in this process. */
+uint64_t tlc_launch_count(void);
+/* Parse a mode name ("exact", "tf32", "3xtf32"); -1 if unknown. */
+int tlc_mode_from_string(const char* name);
+/* The mode TLC_MODE_DEFAULT resolves to. */
+int tlc_default_mode(void);
+
+/* ---- device-buffer backing for Tensor storage ----------------------------
+ * Storage of tl::Tensor is std::shared_ptr<std::vector<float>>
+ * (include/tl/tensor.h:53); these are the device and pinned-host allocation
+ * and copy primitives its CUDA backing uses. */
+int tlc_device_count(int* count);
+int tlc_set_device(int device);
+int tlc_get_device(int* device);
+int tlc_malloc(void** ptr, size_t bytes);
+int tlc_free(void* ptr);
+int tlc_malloc_host(void** ptr, size_t bytes); /* page-locked */
+int tlc_free_host(void* ptr);
+/* kind: 0 host->device, 1 device->host, 2 device->device (async on stream). */
+int tlc_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream);
+int tlc_memset_zero(void* dst, size_t bytes, void* stream);
+int tlc_stream_synchronize(void* stream);
+
+/* ---- tl::matmul ---------------------------------------------------------- */
+
+/* Shape rules of tl::matmul (src/ops.cpp:605-652): 1-D operands are squeezed
+ * ([K] -> [1,K] for a, [K] -> [K,1] for b), batch dims broadcast NumPy-style,
+ * and the squeezed dims are dropped from the result (src/ops.cpp:676-687).
+ * Writes the result rank and sizes.  Errors (TLC_ERR_INVALID_ARGUMENT):
+ *   "matmul: requires at least 1D tensors"      (src/ops.cpp:622)
+ *   "Incompatible dimensions for matmul"         (src/ops.cpp:635)
+ *   "Incompatible dimensions for broadcasting"   (src/ops.cpp:66)
+ * Host-only; touches no GPU. */
+int tlc_matmul_shape(const tlc_tensor* a, const tlc_tensor* b, int32_t* out_ndim,
+                     int64_t* out_sizes);
+
+/* out = tl::matmul(a, b) on the current device (src/ops.cpp:605-699).
+ * a and b are any strided views (transposed views are read in place);
+ * out must be contiguous with the shape tlc_matmul_shape reports.  K == 0
+ * gives zeros, as the reference's zero-initialised output does. */
+int tlc_matmul(const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out, int mode, void* stream);
+
+/* MatmulBackward::backward (src/autograd.cpp:341-384): given dC = grad (the
+ * shape of the matmul result), computes
+ *   dA = sum_to(dC . B^T, shape(a)),  dB = sum_to(A^T . dC, shape(b))
+ * with sum_to's order (src/autograd.cpp:24-36), then accumulate_grad
+ * (src/autograd.cpp:16-22): if `accumulate` is non-zero da/db already hold a
+ * gradient and receive da + dA (resp. db + dB); otherwise they are
+ * overwritten with 0 + dA.  da / db must be contiguous with the shapes of
+ * a / b; pass data == NULL to skip one of them. */
+int tlc_matmul_backward(const tlc_tensor* grad, const tlc_tensor* a, const tlc_tensor* b,
+                        tlc_tensor* da, tlc_tensor* db, int accumulate, int mode, void* stream);
+
+/* Host-buffer forms for callers whose tensors live in host memory (the
+ * unmodified reference Tensor): copies operands to the current device,
+ * computes, and copies the result back, all inside the call, which returns
+ * once the result is in `out`.  Same shapes and errors as above; views are
+ * strided host views (page-locked memory copies fastest).  The work runs on
+ * `stream` (NULL = a stream the library keeps per device). */
+int tlc_matmul_host(const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out, int mode,
+                    void* stream);
+int tlc_matmul_backward_host(const tlc_tensor* grad, const tlc_tensor* a, const tlc_tensor* b,
+                             tlc_tensor* da, tlc_tensor* db, int accumulate, int mode,
+                             void* stream);
+
+/* The GEMM core (see tlc_gemm_desc). */
+int tlc_gemm(const tlc_gemm_desc* desc, int mode, void* stream);
+
+/* ---- building blocks of the backward pass --------------------------------- */
+
+/* sum(input, dim, keepdim) of src/ops.cpp:1181-1233 for a contiguous input
+ * viewed as [outer, D, inner]: out[o,n] = sum over d ascending, from 0.0f. */
+int tlc_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner, void* stream);
+/* out = a + b element-wise (same shape, contiguous): src/ops.cpp:75-103. */
+int tlc_add(const float* a, const float* b, float* out, int64_t n, void* stream);
+/* Tensor::contiguous (src/tensor.cpp:174-193): copy a strided view into a
+ * dense row-major buffer. */
+int tlc_contiguous(const tlc_tensor* src, float* dst, void* stream);
+
+/* ---- multi-GPU partitioning ------------------------------------------------
+ * One process per GPU.  A batched GEMM is split over its flattened batch
+ * dimension, a single GEMM over output column blocks (operands replicated).
+ * These compute a rank's share; the rank then runs tlc_gemm on it. */
+
+/* Contiguous range [*begin, *end) of `count` units for `rank` of `world`
+ * (the first count % world ranks get one extra). */
+int tlc_shard_range(int64_t count, int world, int rank, int64_t* begin, int64_t* end);
+/* Column block of an N-wide output for `rank`, block edges rounded to a
+ * multiple of `align` columns (the last rank takes the remainder). */
+int tlc_shard_cols(int64_t N, int world, int rank, int64_t align, int64_t* begin, int64_t* end);
+/* After an all-gather of per-rank column blocks stored back to back
+ * (rank r's block is [M, w_r] row-major at offset M * col_begin[r]), write the
+ * row-major [M, N] result.  col_begin has world + 1 entries (col_begin[world] = N). */
+int tlc_gather_colblocks(const float* gathered, float* out, int64_t M, int64_t N, int world,
+                         const int64_t* col_begin, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TLC_H */

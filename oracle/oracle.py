@@ -1,0 +1,325 @@
+"""CPU oracle for torchlite-cpp's tl::matmul and MatmulBackward.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, the smoke check and the CPU
+baseline leg of bench.py, always as the checker, never as the product.
+
+The shape logic is a restatement of the reference front end in Python; the
+arithmetic runs in the C restatement (oracle/tl_oracle.c -> liboracle.so):
+
+  matmul            src/ops.cpp:605-699  (contiguous, 1-D squeeze, shape checks,
+                                          batch broadcast, per-batch GEMM,
+                                          unsqueeze of the result)
+  broadcast_shape   src/ops.cpp:55-72    (compute_broadcast_shape)
+  broadcast_offset  src/ops.cpp:32-52    (get_broadcast_index)
+  matmul_backward   src/autograd.cpp:341-384 (MatmulBackward::backward)
+  sum_to            src/autograd.cpp:24-36
+  sum_dim           src/ops.cpp:1181-1233
+  accumulate_grad   src/autograd.cpp:16-22
+
+``tlref`` gives the reference library itself (compiled from its sources into
+oracle/_ref by oracle/Makefile) for pinning this restatement.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_f32p = ctypes.POINTER(ctypes.c_float)
+_f64p = ctypes.POINTER(ctypes.c_double)
+_i64 = ctypes.c_int64
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"oracle library missing: {path} (run make -C oracle)")
+        L = ctypes.CDLL(path)
+        args = [_f32p, _i64, _i64, _f32p, _i64, _i64, _f32p, _i64, _i64, _i64, _i64, ctypes.c_int]
+        L.orc_gemm_chain.argtypes = args
+        L.orc_gemm_chain.restype = None
+        a64 = list(args)
+        a64[6] = _f64p
+        L.orc_gemm_f64.argtypes = a64
+        L.orc_gemm_f64.restype = None
+        L.orc_sum_dim.argtypes = [_f32p, _f32p, _i64, _i64, _i64]
+        L.orc_sum_dim.restype = None
+        L.orc_add.argtypes = [_f32p, _f32p, _f32p, _i64]
+        L.orc_add.restype = None
+        _lib = L
+    return _lib
+
+
+def _fp(x: np.ndarray):
+    return x.ctypes.data_as(_f32p)
+
+
+def default_threads() -> int:
+    return max(1, min(64, os.cpu_count() or 1))
+
+
+def gemm2d(a: np.ndarray, b: np.ndarray, nthreads: int | None = None) -> np.ndarray:
+    """One 2-D product C = A.B as the per-element fmaf chain of gemm_blocked
+    (src/ops.cpp:242-268).  A and B may be any strided float32 views."""
+    assert a.dtype == np.float32 and b.dtype == np.float32 and a.ndim == 2 and b.ndim == 2
+    M, K = a.shape
+    K2, N = b.shape
+    assert K == K2
+    c = np.empty((M, N), np.float32)
+    isz = 4
+    lib().orc_gemm_chain(_fp(a), a.strides[0] // isz, a.strides[1] // isz, _fp(b),
+                         b.strides[0] // isz, b.strides[1] // isz, _fp(c), N, M, N, K,
+                         nthreads or default_threads())
+    return c
+
+
+def gemm2d_f64(a: np.ndarray, b: np.ndarray, nthreads: int | None = None) -> np.ndarray:
+    """Double-precision product of float32 operands (error measurement only)."""
+    M, K = a.shape
+    _, N = b.shape
+    c = np.empty((M, N), np.float64)
+    isz = 4
+    lib().orc_gemm_f64(_fp(a), a.strides[0] // isz, a.strides[1] // isz, _fp(b),
+                       b.strides[0] // isz, b.strides[1] // isz,
+                       c.ctypes.data_as(_f64p), N, M, N, K, nthreads or default_threads())
+    return c
+
+
+def broadcast_shape(a, b):
+    """compute_broadcast_shape, src/ops.cpp:55-72."""
+    nd = max(len(a), len(b))
+    out = []
+    for i in range(nd):
+        sa = 1 if i < nd - len(a) else a[i - (nd - len(a))]
+        sb = 1 if i < nd - len(b) else b[i - (nd - len(b))]
+        if sa != sb and sa != 1 and sb != 1:
+            raise ValueError("Incompatible dimensions for broadcasting")
+        out.append(max(sa, sb))
+    return out
+
+
+def _batch_views(x: np.ndarray, batch_out):
+    """Yield the 2-D matrix of x used for each flat output batch index, in order
+    (get_broadcast_index, src/ops.cpp:32-52: size-1 and missing dims repeat)."""
+    bx = list(x.shape[:-2])
+    nd = len(batch_out)
+    full = [1] * (nd - len(bx)) + bx
+    xr = x.reshape(full + list(x.shape[-2:]))
+    idx = tuple(np.arange(s) if f != 1 else np.zeros(s, np.int64) for s, f in zip(batch_out, full))
+    if nd == 0:
+        yield xr
+        return
+    grid = np.stack(np.meshgrid(*idx, indexing="ij"), -1).reshape(-1, nd)
+    for g in grid:
+        yield xr[tuple(g)]
+
+
+def matmul(a: np.ndarray, b: np.ndarray, nthreads: int | None = None) -> np.ndarray:
+    """tl::matmul, src/ops.cpp:605-699."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    sq_a = sq_b = False
+    if a.ndim == 1:
+        a = a.reshape(1, a.shape[0])
+        sq_a = True
+    if b.ndim == 1:
+        b = b.reshape(b.shape[0], 1)
+        sq_b = True
+    if a.ndim < 2 or b.ndim < 2:
+        raise ValueError("matmul: requires at least 1D tensors")
+    M, K = a.shape[-2:]
+    K2, N = b.shape[-2:]
+    if K != K2:
+        raise ValueError("Incompatible dimensions for matmul")
+    batch_out = broadcast_shape(list(a.shape[:-2]), list(b.shape[:-2]))
+    out = np.empty(batch_out + [M, N], np.float32)
+    flat = out.reshape(int(np.prod(batch_out, dtype=np.int64)), M, N)
+    for i, (av, bv) in enumerate(zip(_batch_views(a, batch_out), _batch_views(b, batch_out))):
+        flat[i] = gemm2d(av, bv, nthreads)
+    if sq_a and sq_b:
+        return out.reshape(())
+    if sq_a:
+        return out.reshape(batch_out + [N])
+    if sq_b:
+        return out.reshape(batch_out + [M])
+    return out
+
+
+def sum_dim(x: np.ndarray, dim: int, keepdim: bool) -> np.ndarray:
+    """sum(input, dim, keepdim), src/ops.cpp:1181-1233 (sequential, from 0.0f)."""
+    x = np.ascontiguousarray(x, np.float32)
+    nd = x.ndim
+    if dim < 0:
+        dim += nd
+    if dim < 0 or dim >= nd:
+        raise ValueError("sum: dimension out of range")
+    outer = int(np.prod(x.shape[:dim], dtype=np.int64))
+    D = x.shape[dim]
+    inner = int(np.prod(x.shape[dim + 1:], dtype=np.int64))
+    shape = [s for i, s in enumerate(x.shape) if i != dim] if not keepdim else \
+        [1 if i == dim else s for i, s in enumerate(x.shape)]
+    out = np.empty(shape, np.float32)
+    lib().orc_sum_dim(_fp(x), _fp(out), outer, D, inner)
+    return out
+
+
+def sum_to(g: np.ndarray, target) -> np.ndarray:
+    """sum_to, src/autograd.cpp:24-36."""
+    while g.ndim > len(target):
+        g = sum_dim(g, 0, False)
+    for i, t in enumerate(target):
+        if t == 1 and g.shape[i] != 1:
+            g = sum_dim(g, i, True)
+    return g
+
+
+def add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Same-shape add (src/ops.cpp:75-103 without broadcasting)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    out = np.empty_like(a)
+    lib().orc_add(_fp(a), _fp(b), _fp(out), a.size)
+    return out
+
+
+def matmul_backward(grad: np.ndarray, a: np.ndarray, b: np.ndarray, nthreads: int | None = None):
+    """MatmulBackward::backward, src/autograd.cpp:341-384, followed by
+    accumulate_grad into empty grads (src/autograd.cpp:16-22: zeros + d).
+
+    a, b are the inputs as given to matmul (any strided views); returns
+    (dA, dB) with the shapes of a and b."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    sq_a, sq_b = a.ndim == 1, b.ndim == 1
+    g = np.asarray(grad, np.float32)
+    if sq_a:
+        # (..., N) -> (..., 1, N); a 0-D grad (vector . vector) becomes [1]
+        g = g.reshape(g.shape[:-1] + (1, g.shape[-1])) if g.ndim else g.reshape(1)
+    if sq_b:
+        g = g.reshape(g.shape + (1,))
+    A = a.reshape(1, a.shape[0]) if sq_a else a
+    B = b.reshape(b.shape[0], 1) if sq_b else b
+    At = np.swapaxes(A, -2, -1)
+    Bt = np.swapaxes(B, -2, -1)
+    da = sum_to(matmul(g, Bt, nthreads), list(A.shape))
+    db = sum_to(matmul(At, g, nthreads), list(B.shape))
+    if sq_a:
+        da = da.reshape(a.shape)
+    if sq_b:
+        db = db.reshape(b.shape)
+    da = add(np.zeros(a.shape, np.float32), da)
+    db = add(np.zeros(b.shape, np.float32), db)
+    return da, db
+
+
+# ---------------------------------------------------------------------------
+# The reference library itself (oracle/_ref), for pinning the restatement.
+# ---------------------------------------------------------------------------
+
+def _cpu_flags() -> set:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+class TLRef:
+    """ctypes view of oracle/_ref/libtlref_{v3,v4}.so (reference sources + ref_shim.cpp)."""
+
+    def __init__(self, path: str | None = None):
+        if path is None:
+            flags = _cpu_flags()
+            v4 = {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= flags
+            path = os.path.join(HERE, "_ref", "libtlref_v4.so" if v4 else "libtlref_v3.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.path = path
+        L = ctypes.CDLL(path)
+        i64p = ctypes.POINTER(_i64)
+        L.tlref_hardware_threads.restype = ctypes.c_int
+        L.tlref_matmul.argtypes = [_f32p, ctypes.c_int, i64p, ctypes.c_int, _f32p, ctypes.c_int,
+                                   i64p, ctypes.c_int, _f32p, _i64, ctypes.POINTER(ctypes.c_int),
+                                   i64p, ctypes.c_char_p, ctypes.c_int]
+        L.tlref_matmul.restype = ctypes.c_int
+        L.tlref_matmul_backward.argtypes = [_f32p, ctypes.c_int, i64p, ctypes.c_int, _f32p,
+                                            ctypes.c_int, i64p, ctypes.c_int, _f32p, ctypes.c_int,
+                                            i64p, _f32p, _i64, _f32p, _i64, ctypes.c_char_p,
+                                            ctypes.c_int]
+        L.tlref_matmul_backward.restype = ctypes.c_int
+        self.L = L
+
+    def hardware_threads(self) -> int:
+        return int(self.L.tlref_hardware_threads())
+
+    @staticmethod
+    def _shape(x):
+        return (_i64 * max(1, x.ndim))(*x.shape)
+
+    def matmul(self, a, b, trans_a=False, trans_b=False, out_cap=None):
+        """tl::matmul(A', B'); A', B' = transpose(-2,-1) views when trans_* is set."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        if out_cap is None:
+            out_cap = max(1, _guess_numel(a, b, trans_a, trans_b))
+        out = np.empty(out_cap, np.float32)
+        nd = ctypes.c_int(0)
+        sz = (_i64 * 16)()
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_matmul(_fp(a), a.ndim, self._shape(a), int(trans_a), _fp(b), b.ndim,
+                                 self._shape(b), int(trans_b), _fp(out), out_cap,
+                                 ctypes.byref(nd), sz, err, 256)
+        if rc == 1:
+            raise ValueError(err.value.decode())
+        if rc != 0:
+            raise RuntimeError(f"tlref_matmul rc={rc}")
+        shape = tuple(sz[i] for i in range(nd.value))
+        n = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        return out[:n].reshape(shape)
+
+    def matmul_backward(self, a, b, grad, trans_a=False, trans_b=False):
+        """Gradients of the stored leaves a, b for C = matmul(a', b'), dC = grad."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        g = np.ascontiguousarray(grad, np.float32)
+        da = np.empty(a.shape, np.float32)
+        db = np.empty(b.shape, np.float32)
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_matmul_backward(_fp(a), a.ndim, self._shape(a), int(trans_a), _fp(b),
+                                          b.ndim, self._shape(b), int(trans_b), _fp(g), g.ndim,
+                                          self._shape(g), _fp(da), max(1, da.size), _fp(db),
+                                          max(1, db.size), err, 256)
+        if rc == 1:
+            raise ValueError(err.value.decode())
+        if rc != 0:
+            raise RuntimeError(f"tlref_matmul_backward rc={rc}")
+        return da, db
+
+
+def _guess_numel(a, b, ta, tb):
+    sa = list(a.shape)
+    sb = list(b.shape)
+    if ta and len(sa) >= 2:
+        sa[-1], sa[-2] = sa[-2], sa[-1]
+    if tb and len(sb) >= 2:
+        sb[-1], sb[-2] = sb[-2], sb[-1]
+    M = sa[-2] if len(sa) >= 2 else 1
+    N = sb[-1] if len(sb) >= 2 else 1
+    try:
+        bo = broadcast_shape(sa[:-2], sb[:-2])
+    except ValueError:
+        bo = []
+    return int(np.prod(bo, dtype=np.int64)) * M * N
+
+
+def tlref(path: str | None = None) -> TLRef:
+    return TLRef(path)

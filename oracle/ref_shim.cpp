@@ -1,0 +1,97 @@
+// C entry points over the reference library itself, compiled from the
+// reference's own sources (see oracle/Makefile) into oracle/_ref/.
+//
+// TEST INFRASTRUCTURE ONLY: the tests use it to pin the C oracle
+// (oracle/tl_oracle.c) against the real tl::matmul / MatmulBackward, and the
+// CPU-baseline leg of bench.py times it.  The product never loads it.
+//
+// Every function builds reference tl::Tensor objects from flat host buffers,
+// runs the reference code path unchanged, and copies results out.
+#include <tl/autograd.h>
+#include <tl/ops.h>
+#include <tl/tensor.h>
+
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace {
+
+tl::Tensor make(const float* p, int nd, const int64_t* sz) {
+    std::vector<int64_t> s(sz, sz + nd);
+    tl::Tensor t(s);
+    if (t.numel() > 0) std::memcpy(t.data(), p, sizeof(float) * t.numel());
+    return t;
+}
+
+// Optionally view the last two dims transposed (tl::transpose, src/ops.cpp:702).
+tl::Tensor maybe_t(const tl::Tensor& t, int trans) {
+    return trans ? tl::transpose(t, -2, -1) : t;
+}
+
+int fail(const std::exception& e, char* err, int errlen) {
+    if (err && errlen > 0) {
+        std::strncpy(err, e.what(), errlen - 1);
+        err[errlen - 1] = 0;
+    }
+    return 1;
+}
+
+int copy_out(const tl::Tensor& t, float* out, int64_t cap, int* out_nd, int64_t* out_sz) {
+    tl::Tensor c = t.contiguous();
+    if (out_nd) *out_nd = (int)c.sizes().size();
+    if (out_sz)
+        for (size_t i = 0; i < c.sizes().size(); ++i) out_sz[i] = c.sizes()[i];
+    if (c.numel() > cap) return 2;
+    if (c.numel() > 0) std::memcpy(out, c.data(), sizeof(float) * c.numel());
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tlref_hardware_threads() { return (int)std::thread::hardware_concurrency(); }
+
+// out = tl::matmul(A', B') where A' / B' are A / B with their last two dims
+// transposed when trans_a / trans_b is set (the storage is given untransposed).
+int tlref_matmul(const float* a, int a_nd, const int64_t* a_sz, int trans_a, const float* b,
+                 int b_nd, const int64_t* b_sz, int trans_b, float* out, int64_t out_cap,
+                 int* out_nd, int64_t* out_sz, char* err, int errlen) {
+    try {
+        tl::Tensor A = maybe_t(make(a, a_nd, a_sz), trans_a);
+        tl::Tensor B = maybe_t(make(b, b_nd, b_sz), trans_b);
+        tl::Tensor C = tl::matmul(A, B);
+        return copy_out(C, out, out_cap, out_nd, out_sz);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+// C = tl::matmul(A', B'); C.grad() = dC; C.backward(); returns A.grad, B.grad
+// (gradients of the stored, untransposed leaves; a transposed view's grad
+// flows back through TransposeBackward exactly as in the reference).
+int tlref_matmul_backward(const float* a, int a_nd, const int64_t* a_sz, int trans_a,
+                          const float* b, int b_nd, const int64_t* b_sz, int trans_b,
+                          const float* grad, int g_nd, const int64_t* g_sz, float* da,
+                          int64_t da_cap, float* db, int64_t db_cap, char* err, int errlen) {
+    try {
+        tl::Tensor A = make(a, a_nd, a_sz);
+        tl::Tensor B = make(b, b_nd, b_sz);
+        A.set_requires_grad(true);
+        B.set_requires_grad(true);
+        tl::Tensor C = tl::matmul(maybe_t(A, trans_a), maybe_t(B, trans_b));
+        C.grad() = make(grad, g_nd, g_sz);
+        C.backward();
+        int rc = copy_out(A.grad(), da, da_cap, nullptr, nullptr);
+        if (rc) return rc;
+        return copy_out(B.grad(), db, db_cap, nullptr, nullptr);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+/*
+ * CPU oracle for the batched fp32 matmul path of torchlite-cpp.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product links or calls this file;
+ * only tests/, the smoke check and the CPU-baseline leg of bench.py load it,
+ * and only as the checker.
+ *
+ * It restates, in plain C, the arithmetic of the reference's CPU path:
+ *
+ *  - gemm_blocked (src/ops.cpp:242-268), the kernel that every x86 matmul path
+ *    ends in (gemm_tiled -> src/ops.cpp:383, gemm_packed -> src/ops.cpp:564).
+ *    Its loop nest zeroes C and then, for each 64-wide k-slab in ascending
+ *    order, does C[m,n] += A[m,k]*B[k,n] for k ascending.  Built with the
+ *    reference's Release flags (-O3 -march=native, GNU fp-contract=fast) the
+ *    multiply-add contracts to one fused multiply-add, so every output element
+ *    is the chain  c = 0;  for k = 0..K-1: c = fmaf(a[m,k], b[k,n], c).
+ *    orc_gemm_chain computes exactly that chain.
+ *
+ *  - sum over one dimension (src/ops.cpp:1181-1233): acc = 0.0f; acc += x[d]
+ *    for d ascending.  orc_sum_dim computes exactly that order.
+ *
+ *  - element-wise add (src/ops.cpp:75-103), used by accumulate_grad
+ *    (src/autograd.cpp:16-22): orc_add.
+ *
+ * Operands are strided 2-D views (row and column strides in elements), so the
+ * transposed views that MatmulBackward builds (src/autograd.cpp:370-371) are
+ * read in place; Tensor::contiguous (src/tensor.cpp:174-193) only copies, it
+ * does not change values, so reading through strides gives the same numbers.
+ *
+ * orc_gemm_f64 is not part of the reference: it is a double-precision product
+ * used to measure error for the tensor-core modes.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+
+typedef struct {
+    const float *A, *B;
+    float *C;
+    double *C64;
+    int64_t sam, sak, sbk, sbn, ldc;
+    int64_t M, N, K;
+    int64_t m0, m1;
+} orc_job;
+
+static void *chain_rows(void *p) {
+    const orc_job *j = (const orc_job *)p;
+    for (int64_t m = j->m0; m < j->m1; ++m) {
+        for (int64_t n = 0; n < j->N; ++n) {
+            float c = 0.0f;
+            const float *a = j->A + m * j->sam;
+            const float *b = j->B + n * j->sbn;
+            for (int64_t k = 0; k < j->K; ++k) c = fmaf(a[k * j->sak], b[k * j->sbk], c);
+            j->C[m * j->ldc + n] = c;
+        }
+    }
+    return NULL;
+}
+
+static void *f64_rows(void *p) {
+    const orc_job *j = (const orc_job *)p;
+    for (int64_t m = j->m0; m < j->m1; ++m) {
+        for (int64_t n = 0; n < j->N; ++n) {
+            double c = 0.0;
+            const float *a = j->A + m * j->sam;
+            const float *b = j->B + n * j->sbn;
+            for (int64_t k = 0; k < j->K; ++k) c += (double)a[k * j->sak] * (double)b[k * j->sbk];
+            j->C64[m * j->ldc + n] = c;
+        }
+    }
+    return NULL;
+}
+
+static void run_rows(void *(*fn)(void *), orc_job base, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if (base.M < nthreads) nthreads = (int)(base.M > 0 ? base.M : 1);
+    pthread_t th[256];
+    orc_job jobs[256];
+    int64_t per = (base.M + nthreads - 1) / nthreads;
+    int started = 0;
+    for (int t = 0; t < nthreads; ++t) {
+        jobs[t] = base;
+        jobs[t].m0 = (int64_t)t * per;
+        jobs[t].m1 = jobs[t].m0 + per < base.M ? jobs[t].m0 + per : base.M;
+        if (jobs[t].m0 >= base.M) break;
+        if (nthreads == 1 || pthread_create(&th[t], NULL, fn, &jobs[t]) != 0) {
+            fn(&jobs[t]);
+            th[t] = 0;
+        }
+        started = t + 1;
+    }
+    for (int t = 0; t < started; ++t)
+        if (th[t]) pthread_join(th[t], NULL);
+}
+
+/* C[m*ldc + n] = fmaf chain over k of A[m*sam + k*sak] * B[k*sbk + n*sbn]. */
+void orc_gemm_chain(const float *A, int64_t sam, int64_t sak, const float *B, int64_t sbk,
+                    int64_t sbn, float *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                    int nthreads) {
+    orc_job j = {A, B, C, NULL, sam, sak, sbk, sbn, ldc, M, N, K, 0, M};
+    run_rows(chain_rows, j, nthreads);
+}
+
+/* Same operands, double-precision accumulation (error measurement only). */
+void orc_gemm_f64(const float *A, int64_t sam, int64_t sak, const float *B, int64_t sbk,
+                  int64_t sbn, double *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                  int nthreads) {
+    orc_job j = {A, B, NULL, C, sam, sak, sbk, sbn, ldc, M, N, K, 0, M};
+    run_rows(f64_rows, j, nthreads);
+}
+
+/* out[o*inner + n] = sum over d ascending of in[o*D*inner + d*inner + n], from 0.0f. */
+void orc_sum_dim(const float *in, float *out, int64_t outer, int64_t D, int64_t inner) {
+    for (int64_t o = 0; o < outer; ++o)
+        for (int64_t n = 0; n < inner; ++n) {
+            float acc = 0.0f;
+            for (int64_t d = 0; d < D; ++d) acc += in[o * D * inner + d * inner + n];
+            out[o * inner + n] = acc;
+        }
+}
+
+/* out[i] = a[i] + b[i] (same shape). */
+void orc_add(const float *a, const float *b, float *out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = a[i] + b[i];
+}

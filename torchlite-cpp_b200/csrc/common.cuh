@@ -1,0 +1,122 @@
+// Shared internals of libtl_cuda: status/error plumbing, the normalised GEMM
+// problem the kernels consume, and launch bookkeeping.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/tlc.h"
+
+namespace tlc {
+
+// ---- errors -----------------------------------------------------------------
+
+// Records `msg` as this thread's last error and returns `status`.
+int set_error(int status, const std::string& msg);
+void clear_error();
+
+#define TLC_CUDA_TRY(expr)                                                              \
+    do {                                                                                \
+        cudaError_t e_ = (expr);                                                        \
+        if (e_ != cudaSuccess) {                                                        \
+            return ::tlc::set_error(e_ == cudaErrorMemoryAllocation ? TLC_ERR_OUT_OF_MEMORY \
+                                                                    : TLC_ERR_CUDA,     \
+                                    std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+        }                                                                               \
+    } while (0)
+
+#define TLC_TRY(expr)            \
+    do {                         \
+        int s_ = (expr);         \
+        if (s_ != TLC_OK) return s_; \
+    } while (0)
+
+// ---- launch bookkeeping ----------------------------------------------------------
+
+extern std::atomic<uint64_t> g_launches;
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// Checks the launch that was just made (configuration errors surface here).
+int check_launch(const char* what);
+
+// ---- the GEMM problem --------------------------------------------------------------
+
+constexpr int kMaxBatchDims = 3;
+
+// Normalised batched GEMM: C_b[m,n] = sum_k A_b[m,k] B_b[k,n]; all strides in
+// elements.  Either a_cs == 1 (A row-major, "K-major") or a_rs == 1 (A
+// column-major, "M-major"); likewise b_cs == 1 (B row-major, "N-major") or
+// b_rs == 1 (B column-major, "K-major").  C is row-major (c_cs == 1).
+struct Gemm {
+    int64_t M, N, K;
+    const float* A;
+    int64_t a_rs, a_cs;
+    const float* B;
+    int64_t b_rs, b_cs;
+    float* C;
+    int64_t c_rs;
+    int nb;                           // number of batch dims (0..3)
+    int64_t bsz[kMaxBatchDims];       // batch sizes, outermost first
+    int64_t abs_[kMaxBatchDims], bbs[kMaxBatchDims], cbs[kMaxBatchDims];
+    int64_t batch() const {
+        int64_t n = 1;
+        for (int i = 0; i < nb; ++i) n *= bsz[i];
+        return n;
+    }
+};
+
+// Flat batch index -> the three operand offsets (get_broadcast_index,
+// src/ops.cpp:32-52, with broadcast dims carrying stride 0).
+struct BatchOffsets {
+    int nb;
+    int64_t bsz[kMaxBatchDims];
+    int64_t as[kMaxBatchDims], bs[kMaxBatchDims], cs[kMaxBatchDims];
+    __host__ __device__ __forceinline__ void get(int64_t b, int64_t& oa, int64_t& ob,
+                                                 int64_t& oc) const {
+        oa = ob = oc = 0;
+#pragma unroll
+        for (int i = kMaxBatchDims - 1; i >= 0; --i) {
+            if (i < nb) {
+                int64_t idx = b % bsz[i];
+                b /= bsz[i];
+                oa += idx * as[i];
+                ob += idx * bs[i];
+                oc += idx * cs[i];
+            }
+        }
+    }
+};
+
+inline BatchOffsets batch_offsets(const Gemm& g) {
+    BatchOffsets o{};
+    o.nb = g.nb;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        o.bsz[i] = i < g.nb ? g.bsz[i] : 1;
+        o.as[i] = i < g.nb ? g.abs_[i] : 0;
+        o.bs[i] = i < g.nb ? g.bbs[i] : 0;
+        o.cs[i] = i < g.nb ? g.cbs[i] : 0;
+    }
+    return o;
+}
+
+// Kernels (each returns a tlc_status).
+int gemm_exact(const Gemm& g, cudaStream_t s);
+int gemm_tc(const Gemm& g, int mode, cudaStream_t s);
+int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
+                   cudaStream_t s);
+int launch_add(const float* a, const float* b, float* out, int64_t n, cudaStream_t s);
+int launch_zero_plus(const float* in, float* out, int64_t n, cudaStream_t s);
+int launch_strided_copy(const float* src, int nd, const int64_t* sizes, const int64_t* strides,
+                        float* dst, cudaStream_t s);
+int launch_fill_zero(float* p, int64_t n, cudaStream_t s);
+int launch_gather_colblocks(const float* g, float* out, int64_t M, int64_t N, int world,
+                            const int64_t* begin, cudaStream_t s);
+
+// Stream-ordered scratch memory from the device's memory pool.
+int scratch_alloc(void** p, size_t bytes, cudaStream_t s);
+void scratch_free(void* p, cudaStream_t s);
+
+}  // namespace tlc
