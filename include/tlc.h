@@ -112,7 +112,17 @@ int tlc_free_host(void* ptr);
 /* kind: 0 host->device, 1 device->host, 2 device->device (async on stream). */
 int tlc_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream);
 int tlc_memset_zero(void* dst, size_t bytes, void* stream);
+/* Waits for `stream`, then reports (and clears) a timeout that a kernel of
+ * this library recorded on the current device: TLC_ERR_TIMEOUT. */
 int tlc_stream_synchronize(void* stream);
+/* Synchronises the current device and reports (and clears) a recorded
+ * in-kernel timeout, like tlc_stream_synchronize. */
+int tlc_check_device_errors(void);
+/* Failure-detection self test: runs the tensor-core GEMM's bounded wait on an
+ * mbarrier that nothing arrives on, with the given limit.  A working bound
+ * returns TLC_ERR_TIMEOUT (and leaves the context usable); TLC_OK would mean
+ * the wait ended without its barrier completing. */
+int tlc_selftest_bounded_wait(uint64_t timeout_ns);
 
 /* ---- tl::matmul ---------------------------------------------------------- */
 

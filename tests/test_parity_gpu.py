@@ -19,7 +19,8 @@ DEV = "cuda:0"
 
 
 def dev(x):
-    return torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+    # np.array keeps 0-D inputs 0-D (np.ascontiguousarray would make them 1-D)
+    return torch.from_numpy(np.array(x, dtype=np.float32, order="C", copy=True)).to(DEV)
 
 
 def host(t):

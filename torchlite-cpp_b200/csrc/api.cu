@@ -350,11 +350,12 @@ int check_out(const tlc_tensor* out, const std::vector<int64_t>& shape, const ch
     if (!out) return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + " is NULL");
     if (out->ndim != (int)shape.size())
         return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + ": wrong rank");
+    const bool empty = std::find(shape.begin(), shape.end(), int64_t(0)) != shape.end();
     int64_t e = 1;
     for (int i = out->ndim - 1; i >= 0; --i) {
         if (out->sizes[i] != shape[i])
             return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + ": wrong shape");
-        if (out->sizes[i] != 1 && out->strides[i] != e)
+        if (!empty && out->sizes[i] != 1 && out->strides[i] != e)  // strides of empty tensors vary
             return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + " must be contiguous");
         e *= shape[i];
     }
@@ -619,10 +620,45 @@ int tlc_memset_zero(void* dst, size_t bytes, void* stream) {
     if (bytes) TLC_CUDA_TRY(cudaMemsetAsync(dst, 0, bytes, (cudaStream_t)stream));
     return TLC_OK;
 }
+namespace tlc {
+namespace {
+// Reads and clears the device error word of the current device.
+int take_device_error() {
+    int* w = nullptr;
+    TLC_TRY(tc_error_word(&w));
+    int v = 0;
+    TLC_CUDA_TRY(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) {
+        const int zero = 0;
+        TLC_CUDA_TRY(cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice));
+        return set_error(TLC_ERR_TIMEOUT,
+                         "a bounded wait inside a tensor-core GEMM kernel timed out (site " +
+                             std::to_string(v) + ")");
+    }
+    return TLC_OK;
+}
+}  // namespace
+}  // namespace tlc
+
 int tlc_stream_synchronize(void* stream) {
     clear_error();
     TLC_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
-    return TLC_OK;
+    return take_device_error();
+}
+
+int tlc_check_device_errors(void) {
+    clear_error();
+    TLC_CUDA_TRY(cudaDeviceSynchronize());
+    return take_device_error();
+}
+
+int tlc_selftest_bounded_wait(uint64_t timeout_ns) {
+    clear_error();
+    TLC_CUDA_TRY(cudaDeviceSynchronize());
+    TLC_TRY(take_device_error());
+    TLC_TRY(bounded_wait_selftest(timeout_ns, nullptr));
+    TLC_CUDA_TRY(cudaDeviceSynchronize());
+    return take_device_error();
 }
 
 int tlc_matmul_shape(const tlc_tensor* a, const tlc_tensor* b, int32_t* out_ndim,
@@ -723,7 +759,7 @@ int tlc_matmul_host(const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out, i
         if (n) TLC_CUDA_TRY(cudaMemcpyAsync(out->data, dc.t.data, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
     }
     TLC_CUDA_TRY(cudaStreamSynchronize(s));
-    return TLC_OK;
+    return take_device_error();
 }
 
 int tlc_matmul_backward_host(const tlc_tensor* grad, const tlc_tensor* a, const tlc_tensor* b,
@@ -762,7 +798,7 @@ int tlc_matmul_backward_host(const tlc_tensor* grad, const tlc_tensor* a, const 
         }
     }
     TLC_CUDA_TRY(cudaStreamSynchronize(s));
-    return TLC_OK;
+    return take_device_error();
 }
 
 int tlc_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,

@@ -115,6 +115,14 @@ int launch_fill_zero(float* p, int64_t n, cudaStream_t s);
 int launch_gather_colblocks(const float* g, float* out, int64_t M, int64_t N, int world,
                             const int64_t* begin, cudaStream_t s);
 
+// Copy a strided view into a destination with its own strides (same shape).
+int launch_strided_copy_to(const float* src, int nd, const int64_t* sizes, const int64_t* sstr,
+                           float* dst, const int64_t* dstr, cudaStream_t s);
+// Device error word written by bounded waits inside kernels (0 = none).
+int tc_error_word(int** p);
+// Launches a kernel whose bounded wait must time out (failure-detection test).
+int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s);
+
 // Stream-ordered scratch memory from the device's memory pool.
 int scratch_alloc(void** p, size_t bytes, cudaStream_t s);
 void scratch_free(void* p, cudaStream_t s);

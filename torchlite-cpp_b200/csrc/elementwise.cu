@@ -75,6 +75,22 @@ __global__ void strided_copy_kernel(const float* __restrict__ src, StridedView v
     }
 }
 
+// dst[offset_d(i)] = src[offset_s(i)] over the multi-index i of a shared shape.
+__global__ void strided_copy_to_kernel(const float* __restrict__ src, StridedView vs,
+                                       float* __restrict__ dst, StridedView vd, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t t = i, os = 0, od = 0;
+        for (int d = vs.nd - 1; d >= 0; --d) {
+            const int64_t c = t % vs.sizes[d];
+            t /= vs.sizes[d];
+            os += c * vs.strides[d];
+            od += c * vd.strides[d];
+        }
+        dst[od] = src[os];
+    }
+}
+
 struct ColBlocks {
     int world;
     int64_t begin[65];
@@ -134,6 +150,23 @@ int launch_strided_copy(const float* src, int nd, const int64_t* sizes, const in
     strided_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, v, dst, n);
     count_launch();
     return check_launch("strided_copy");
+}
+
+int launch_strided_copy_to(const float* src, int nd, const int64_t* sizes, const int64_t* sstr,
+                           float* dst, const int64_t* dstr, cudaStream_t s) {
+    StridedView vs{}, vd{};
+    vs.nd = vd.nd = nd;
+    int64_t n = 1;
+    for (int i = 0; i < nd; ++i) {
+        vs.sizes[i] = vd.sizes[i] = sizes[i];
+        vs.strides[i] = sstr[i];
+        vd.strides[i] = dstr[i];
+        n *= sizes[i];
+    }
+    if (n == 0) return TLC_OK;
+    strided_copy_to_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, vs, dst, vd, n);
+    count_launch();
+    return check_launch("strided_copy_to");
 }
 
 int launch_fill_zero(float* p, int64_t n, cudaStream_t s) {

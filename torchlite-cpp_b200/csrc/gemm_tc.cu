@@ -1,8 +1,798 @@
-// Tensor-core GEMM (TF32 / 3xTF32) on tcgen05: placeholder until the kernel lands.
+// Tensor-core GEMM for TLC_MODE_TF32 and TLC_MODE_3XTF32 on sm_100a (tcgen05).
+//
+// One persistent CTA per SM, 6 warps, warp-specialised:
+//   warp 0      TMA producer: one elected thread streams A and B k-blocks
+//               (32 fp32 = 128 bytes of k) into a ring of shared-memory stages
+//               with cp.async.bulk.tensor (128-byte swizzle), completion
+//               tracked by an mbarrier per stage (expect_tx bytes).
+//   warp 1      MMA issuer: allocates the tensor memory (TMEM), and one
+//               elected thread issues tcgen05.mma.kind::tf32 (M=128, N=BN,
+//               K=8 per instruction, 4 per k-block) into an fp32 accumulator
+//               in TMEM; tcgen05.commit frees each stage and publishes each
+//               finished accumulator.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each thread one row of
+//               the 128-row tile), store to global fp32 C.
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Operand layouts are read in place: A may be K-major (row-major [M,K]) or
+// M-major (a transposed view, storage [K,M]); B may be N-major (row-major
+// [K,N]) or K-major (a transposed view, storage [N,K], the X.W^T of Linear).
+// The instruction descriptor's per-operand major bits select the layout; an
+// MN-major tile is loaded as 32-element-wide column chunks so each shared
+// memory atom is 8 k-rows x 128 bytes.  Batch dims (up to 3, broadcast dims
+// with stride 0) are extra dimensions of the 5-D tensor maps, so ragged M, N
+// and K tails are zero-filled by TMA per batch entry and never read a
+// neighbouring matrix.
+//
+// 3xTF32 (Ootomo & Yokota, "Recovering single precision accuracy from Tensor
+// Cores while surpassing the FP32 theoretical peak performance", 2022): each
+// operand x is split as hi = round_to_tf32(x), lo = x - hi (exact in fp32) by
+// a pre-pass; the main loop then runs the k range three times, accumulating
+// lo(A).hi(B) + hi(A).lo(B) + hi(A).hi(B) into one fp32 TMEM accumulator.
+//
+// Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
+// waiting thread raises a CTA-wide abort flag and a device error word, every
+// role leaves its loop, in-flight TMA copies and MMAs are drained (again with
+// a bound), the TMEM is freed, and the host reports TLC_ERR_TIMEOUT.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 
 namespace tlc {
-int gemm_tc(const Gemm&, int, cudaStream_t) {
-    return set_error(TLC_ERR_UNSUPPORTED, "tensor-core modes are not built yet");
+
+__device__ int g_tc_error = 0;  // first failing wait site of any tensor-core launch
+
+namespace {
+
+constexpr int BM = 128;        // UMMA M
+constexpr int BK = 32;         // k per stage: 32 fp32 = one 128-byte swizzle row
+constexpr int UMMA_K = 8;      // k per tcgen05.mma.kind::tf32
+constexpr int NUM_THREADS = 192;
+
+struct TcParams {
+    CUtensorMap tmA[2];  // [0] A (TF32) or hi(A) (3xTF32); [1] lo(A)
+    CUtensorMap tmB[2];
+    float* C;
+    int64_t c_rs;
+    int64_t cbs[kMaxBatchDims];
+    int bsz[kMaxBatchDims];
+    int a_bc[kMaxBatchDims];  // 1: A indexes this batch dim, 0: broadcast (coordinate 0)
+    int b_bc[kMaxBatchDims];
+    int nb;
+    int M, N, K;
+    int m_tiles, n_tiles;
+    int64_t num_tiles;
+    int k_blocks;     // per pass
+    int passes;       // 1 (TF32) or 3 (3xTF32)
+    int a_mn, b_mn;   // 1: operand is MN-major in memory
+    int vec_c;        // float4 stores allowed
+    uint64_t timeout_ns;
+    int* err;
+};
+
+// ---- PTX wrappers ---------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase of `bar` with the given parity.  Gives up (returns
+// false) when the CTA's abort flag is raised or the deadline passes; in the
+// latter case it raises the flag and records `site` in the device error word.
+__device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t timeout_ns, int* err, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > timeout_ns) {
+                *abort_flag = 1;
+                atomicCAS(err, 0, site);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: start address, leading / stride byte
+// offsets (>> 4), sm_100 descriptor version 1 at bits 46-47, base offset 0
+// (atoms aligned to their size), layout type at bits 61-63:
+//   2 = 128-byte swizzle, 16-byte granules (K-major tiles: 8 rows x 128 B atoms)
+//   1 = 128-byte swizzle, 32-byte granules (MN-major TF32 tiles: 4 k-rows x
+//       128 B atoms; the only shared-memory layout MN-major TF32 accepts)
+constexpr uint64_t kSw128 = 2, kSw128Atom32 = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint64_t layout) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---- tile bookkeeping ----------------------------------------------------------------
+
+struct TileCoord {
+    int b, m, n;  // batch index, tile row, tile column
+};
+
+// Tiles in batch-major order; inside a batch, groups of 16 tile rows are
+// walked column by column so CTAs running together share A panels and
+// B panels in L2.
+__device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t t) {
+    const int64_t per_batch = (int64_t)p.m_tiles * p.n_tiles;
+    TileCoord c;
+    c.b = (int)(t / per_batch);
+    int r = (int)(t - (int64_t)c.b * per_batch);
+    constexpr int GM = 16;
+    const int group = r / (GM * p.n_tiles);
+    const int first_m = group * GM;
+    const int gm = min(GM, p.m_tiles - first_m);
+    const int in_group = r - group * GM * p.n_tiles;
+    c.m = first_m + in_group % gm;
+    c.n = in_group / gm;
+    return c;
+}
+
+__device__ __forceinline__ void batch_coords(const TcParams& p, int b, int (&idx)[kMaxBatchDims]) {
+#pragma unroll
+    for (int i = kMaxBatchDims - 1; i >= 0; --i) {
+        if (i < p.nb) {
+            idx[i] = b % p.bsz[i];
+            b /= p.bsz[i];
+        } else {
+            idx[i] = 0;
+        }
+    }
+}
+
+template <int BN>
+struct Smem {
+    static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
+    static constexpr int B_BYTES = BN * BK * 4;  // 32 KB (BN=256) / 16 KB (BN=128)
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+};
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    using S = Smem<BN>;
+    constexpr int STAGES = S::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the 128-byte-swizzle atoms.
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
+    uint64_t* full = bars;                 // [STAGES]
+    uint64_t* empty = bars + STAGES;       // [STAGES]
+    uint64_t* tfull = bars + 2 * STAGES;   // [2]
+    uint64_t* tempty = tfull + 2;          // [2]
+    uint64_t* drain = tempty + 2;          // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_map(&p.tmA[0]);
+        prefetch_map(&p.tmB[0]);
+        if (p.passes > 1) {
+            prefetch_map(&p.tmA[1]);
+            prefetch_map(&p.tmB[1]);
+        }
+    }
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(S::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int total_kb = p.k_blocks * p.passes;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            // outstanding[s]: parity of a load issued into stage s whose
+            // completion nobody has observed yet (-1: none).
+            int outstanding[STAGES];
+            for (int s = 0; s < STAGES; ++s) outstanding[s] = -1;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+                const TileCoord tc = tile_coord(p, t);
+                int bi[kMaxBatchDims];
+                batch_coords(p, tc.b, bi);
+                const int a0 = p.a_bc[0] ? bi[0] : 0, a1 = p.a_bc[1] ? bi[1] : 0,
+                          a2 = p.a_bc[2] ? bi[2] : 0;
+                const int b0 = p.b_bc[0] ? bi[0] : 0, b1 = p.b_bc[1] ? bi[1] : 0,
+                          b2 = p.b_bc[2] ? bi[2] : 0;
+                const int m0 = tc.m * BM, n0 = tc.n * BN;
+                for (int kb = 0; kb < total_kb; ++kb) {
+                    if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    // The stage's previous load was consumed (the MMA that read it finished).
+                    outstanding[stage] = -1;
+                    const int pass = kb / p.k_blocks;
+                    const int k0 = (kb - pass * p.k_blocks) * BK;
+                    // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
+                    const int pa = (p.passes > 1 && pass == 0) ? 1 : 0;
+                    const int pb = (p.passes > 1 && pass == 1) ? 1 : 0;
+                    uint8_t* sa = smem + stage * S::STAGE_BYTES;
+                    uint8_t* sb = sa + S::A_BYTES;
+                    mbar_expect_tx(&full[stage], S::STAGE_BYTES);
+                    if (p.a_mn) {
+                        for (int c = 0; c < BM / 32; ++c)
+                            tma_load_5d(sa + c * (32 * BK * 4), &p.tmA[pa], &full[stage], m0 + 32 * c,
+                                        k0, a0, a1, a2);
+                    } else {
+                        tma_load_5d(sa, &p.tmA[pa], &full[stage], k0, m0, a0, a1, a2);
+                    }
+                    if (p.b_mn) {
+                        for (int c = 0; c < BN / 32; ++c)
+                            tma_load_5d(sb + c * (32 * BK * 4), &p.tmB[pb], &full[stage], n0 + 32 * c,
+                                        k0, b0, b1, b2);
+                    } else {
+                        tma_load_5d(sb, &p.tmB[pb], &full[stage], k0, n0, b0, b1, b2);
+                    }
+                    outstanding[stage] = (int)phase;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                // Drain: wait (bounded) for loads still in flight into shared memory.
+                for (int s = 0; s < STAGES; ++s) {
+                    if (outstanding[s] < 0) continue;
+                    const uint64_t t0 = globaltimer();
+                    while (!mbar_try_wait(&full[s], (uint32_t)outstanding[s]) &&
+                           globaltimer() - t0 < p.timeout_ns) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            // kind::tf32: D fp32 (bits 4-5 = 1), A/B TF32 (bits 7-9, 10-12 = 2),
+            // A/B major (bits 15, 16), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+            const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) |
+                                   ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16) |
+                                   ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+            // MN-major tiles: 32-wide chunks of 32 k-rows (4 KB) side by side
+            // (leading byte offset), 8-row atoms (1 KB) along k (stride byte
+            // offset).  K-major tiles: 128-byte rows, 8-row atoms 1 KB apart.
+            const uint32_t chunk = 32 * BK * 4;
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t acc_phase[2] = {0, 0};
+            int acc = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+                if (!wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, p.timeout_ns, p.err, 2)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < total_kb; ++kb) {
+                    if (!wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * S::STAGE_BYTES);
+                    const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+                    for (int j = 0; j < BK / UMMA_K; ++j) {
+                        // MN-major: k-step j starts 8 k-rows (1 KB) further; chunks of
+                        // 32 MN elements are `chunk` bytes apart (leading offset), 4-row
+                        // k groups 512 B apart (stride offset).  K-major: 32 B further
+                        // along the 128-byte rows; 8-row atoms 1 KB apart.
+                        const uint64_t ad =
+                            p.a_mn ? smem_desc(sa + j * 1024, chunk, 512, kSw128Atom32)
+                                   : smem_desc(sa + j * UMMA_K * 4, 16, 1024, kSw128);
+                        const uint64_t bd =
+                            p.b_mn ? smem_desc(sb + j * 1024, chunk, 512, kSw128Atom32)
+                                   : smem_desc(sb + j * UMMA_K * 4, 16, 1024, kSw128);
+                        umma_tf32(d, ad, bd, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    }
+                    issued = true;
+                    umma_commit(&empty[stage]);  // frees the stage when these MMAs finish
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+                acc_phase[acc] ^= 1;
+                acc ^= 1;
+            }
+            if (!ok && issued) {
+                // Drain MMAs still reading shared memory / writing TMEM.
+                umma_commit(drain);
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < p.timeout_ns) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row_in_tile = q * 32 + lane;
+        uint32_t acc_phase[2] = {0, 0};
+        int acc = 0;
+        for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+            bool ok = true;
+            if (lane == 0)
+                ok = wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, p.timeout_ns, p.err, 4);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // the whole warp takes one branch
+            if (!ok) break;
+            tc_fence_after();
+            const TileCoord tc = tile_coord(p, t);
+            int bi[kMaxBatchDims];
+            batch_coords(p, tc.b, bi);
+            int64_t oc = 0;
+#pragma unroll
+            for (int i = 0; i < kMaxBatchDims; ++i) oc += (int64_t)bi[i] * p.cbs[i];
+            const int64_t row = (int64_t)tc.m * BM + row_in_tile;
+            const int n0 = tc.n * BN;
+            float* crow = p.C + oc + row * p.c_rs;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(taddr + c * 32, r);
+                tmem_wait_ld();
+                if (row < p.M) {
+                    const int col0 = n0 + c * 32;
+                    if (p.vec_c && col0 + 32 <= p.N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                   __uint_as_float(r[j + 2]),
+                                                   __uint_as_float(r[j + 3]));
+                            *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            acc_phase[acc] ^= 1;
+            acc ^= 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();  // .sync.aligned: the whole warp, converged
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(S::TMEM_COLS));
+    }
+}
+
+// hi = tf32 round-to-nearest(x) (low 13 mantissa bits zero), lo = x - hi
+// (exact in fp32): the 3xTF32 operand split.
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        uint32_t h;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+        const float hf = __uint_as_float(h);
+        hi[i] = hf;
+        lo[i] = __fsub_rn(v, hf);
+    }
+}
+
+// Tiny kernel for the failure-detection test: waits on an mbarrier that
+// nothing ever arrives on, with the same bounded wait as the GEMM, and
+// records the timeout in *err.
+__global__ void bounded_wait_selftest_kernel(uint64_t timeout_ns, int* err) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (!wait_bounded(&bar, 0, &abort_flag, timeout_ns, err, 99)) return;
+        *err = -1;  // unreachable unless the barrier completed
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// One operand as a 5-D tensor map: dims {inner, outer, batch0..2}.
+struct OperandMap {
+    const float* base;
+    int64_t inner, outer;     // extents (elements)
+    int64_t outer_stride;     // elements
+    int64_t bsz[kMaxBatchDims];
+    int64_t bstride[kMaxBatchDims];  // elements; 0 = broadcast
+    uint32_t box_inner, box_outer;
+    bool mn_major;  // MN-major TF32 tiles use 32-byte swizzle granules
+};
+
+int encode(CUtensorMap* map, const OperandMap& o) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    cuuint64_t dims[5], strides[4];
+    cuuint32_t box[5] = {o.box_inner, o.box_outer, 1, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    dims[0] = (cuuint64_t)o.inner;
+    dims[1] = (cuuint64_t)o.outer;
+    strides[0] = (cuuint64_t)o.outer_stride * 4;
+    cuuint64_t prev = strides[0] * dims[1];
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        const bool real = o.bstride[i] != 0 && o.bsz[i] > 1;
+        dims[2 + i] = real ? (cuuint64_t)o.bsz[i] : 1;
+        strides[1 + i] = real ? (cuuint64_t)o.bstride[i] * 4 : ((prev + 15) & ~cuuint64_t(15));
+        prev = strides[1 + i] * dims[2 + i];
+    }
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(o.base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    o.mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TLC_ERR_UNSUPPORTED,
+                         "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return TLC_OK;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Whether TMA can read the operand in place: 16-byte aligned base and
+// strides that are multiples of 4 floats.
+bool tma_ok(const float* base, int64_t outer_stride, const int64_t* bstr, int nb) {
+    if (!al16(base) || (outer_stride & 3)) return false;
+    for (int i = 0; i < nb; ++i)
+        if (bstr[i] & 3) return false;
+    return true;
+}
+
+int64_t span_elems(int64_t inner, int64_t outer, int64_t os, const int64_t* bsz,
+                   const int64_t* bstr, int nb) {
+    int64_t hi = (inner - 1) + (outer - 1) * os;
+    for (int i = 0; i < nb; ++i)
+        if (bstr[i]) hi += (bsz[i] - 1) * bstr[i];
+    return hi + 1;
+}
+
+struct TcScratch {
+    void* p[6] = {};
+    cudaStream_t s;
+    explicit TcScratch(cudaStream_t st) : s(st) {}
+    ~TcScratch() {
+        for (void* q : p) scratch_free(q, s);
+    }
+};
+
+int grid_split(int64_t n) {
+    int64_t g = (n + 255) / 256;
+    return (int)(g > 148 * 16 ? 148 * 16 : (g < 1 ? 1 : g));
+}
+
+// Re-lays an operand with unaligned strides/base as a dense [batch..., outer,
+// round4(inner)] buffer (zero padding), so TMA can read it.
+int repack(OperandMap& o, int nb, TcScratch& sc, int slot, cudaStream_t s) {
+    const int64_t pitch = (o.inner + 3) & ~int64_t(3);
+    int64_t total = pitch * o.outer;
+    int64_t bsz_eff[kMaxBatchDims];
+    for (int i = 0; i < nb; ++i) {
+        bsz_eff[i] = o.bstride[i] ? o.bsz[i] : 1;
+        total *= bsz_eff[i];
+    }
+    TLC_TRY(scratch_alloc(&sc.p[slot], sizeof(float) * (size_t)std::max<int64_t>(total, 1), s));
+    float* dst = static_cast<float*>(sc.p[slot]);
+    TLC_CUDA_TRY(cudaMemsetAsync(dst, 0, sizeof(float) * (size_t)total, s));
+    // Copy view [b0, b1, b2, outer, inner] -> dense with pitch.
+    int64_t sizes[5], sstr[5], dstr[5];
+    int nd = 0;
+    int64_t dense = pitch * o.outer;
+    int64_t dstride_b[kMaxBatchDims];
+    for (int i = nb - 1; i >= 0; --i) {
+        dstride_b[i] = dense;
+        dense *= bsz_eff[i];
+    }
+    for (int i = 0; i < nb; ++i) {
+        sizes[nd] = bsz_eff[i];
+        sstr[nd] = o.bstride[i];
+        dstr[nd] = dstride_b[i];
+        ++nd;
+    }
+    sizes[nd] = o.outer;
+    sstr[nd] = o.outer_stride;
+    dstr[nd] = pitch;
+    ++nd;
+    sizes[nd] = o.inner;
+    sstr[nd] = 1;
+    dstr[nd] = 1;
+    ++nd;
+    TLC_TRY(launch_strided_copy_to(o.base, nd, sizes, sstr, dst, dstr, s));
+    o.base = dst;
+    o.outer_stride = pitch;
+    for (int i = 0; i < nb; ++i) o.bstride[i] = o.bstride[i] ? dstride_b[i] : 0;
+    return TLC_OK;
+}
+
+template <int BN>
+int launch_tc(const TcParams& prm, cudaStream_t s) {
+    using S = Smem<BN>;
+    static int configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<BN>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+        configured[dev] = 1;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t grid = std::min<int64_t>(prm.num_tiles, sms);
+    tc_gemm_kernel<BN><<<(unsigned)grid, NUM_THREADS, S::TOTAL, s>>>(prm);
+    count_launch();
+    return check_launch("tc_gemm");
+}
+
+int* error_word() {
+    static int* words[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!words[dev]) {
+        int* p = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_tc_error) != cudaSuccess) return nullptr;
+        words[dev] = p;
+    }
+    return words[dev];
+}
+
+}  // namespace
+
+int tc_error_word(int** p) {
+    *p = error_word();
+    return *p ? TLC_OK : set_error(TLC_ERR_CUDA, "no device error word");
+}
+
+int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
+    if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
+    if (g.K == 0) return gemm_exact(g, s);  // writes zeros
+    if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX)
+        return set_error(TLC_ERR_UNSUPPORTED, "tensor-core GEMM: a dimension exceeds 2^31");
+
+    // Operand maps in memory order: A K-major = {K, M}, M-major = {M, K};
+    // B N-major = {N, K}, K-major = {K, N}.
+    const bool a_mn = g.a_cs != 1;  // a_rs == 1
+    const bool b_mn = g.b_cs == 1;  // else b_rs == 1
+    OperandMap A{}, B{};
+    A.base = g.A;
+    A.inner = a_mn ? g.M : g.K;
+    A.outer = a_mn ? g.K : g.M;
+    A.outer_stride = a_mn ? g.a_cs : g.a_rs;
+    B.base = g.B;
+    B.inner = b_mn ? g.N : g.K;
+    B.outer = b_mn ? g.K : g.N;
+    B.outer_stride = b_mn ? g.b_rs : g.b_cs;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        A.bsz[i] = B.bsz[i] = i < g.nb ? g.bsz[i] : 1;
+        A.bstride[i] = i < g.nb ? g.abs_[i] : 0;
+        B.bstride[i] = i < g.nb ? g.bbs[i] : 0;
+    }
+    const int BN = g.N > 128 ? 256 : 128;
+    A.box_inner = 32;
+    A.box_outer = a_mn ? BK : BM;
+    A.mn_major = a_mn;
+    B.box_inner = 32;
+    B.box_outer = b_mn ? BK : BN;
+    B.mn_major = b_mn;
+
+    TcScratch sc(s);
+    if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb)) TLC_TRY(repack(A, g.nb, sc, 0, s));
+    if (!tma_ok(B.base, B.outer_stride, B.bstride, g.nb)) TLC_TRY(repack(B, g.nb, sc, 1, s));
+
+    TcParams prm;
+    memset(&prm, 0, sizeof(prm));
+    const int passes = mode == TLC_MODE_3XTF32 ? 3 : 1;
+    if (passes == 3) {
+        // Split each operand's storage span into hi / lo planes of identical layout.
+        OperandMap* ops[2] = {&A, &B};
+        CUtensorMap* maps[2] = {prm.tmA, prm.tmB};
+        for (int o = 0; o < 2; ++o) {
+            const int64_t n = span_elems(ops[o]->inner, ops[o]->outer, ops[o]->outer_stride,
+                                         ops[o]->bsz, ops[o]->bstride, g.nb);
+            TLC_TRY(scratch_alloc(&sc.p[2 + 2 * o], sizeof(float) * (size_t)n, s));
+            TLC_TRY(scratch_alloc(&sc.p[3 + 2 * o], sizeof(float) * (size_t)n, s));
+            float* hi = static_cast<float*>(sc.p[2 + 2 * o]);
+            float* lo = static_cast<float*>(sc.p[3 + 2 * o]);
+            split_tf32_kernel<<<grid_split(n), 256, 0, s>>>(ops[o]->base, hi, lo, n);
+            count_launch();
+            TLC_TRY(check_launch("split_tf32"));
+            OperandMap h = *ops[o], l = *ops[o];
+            h.base = hi;
+            l.base = lo;
+            TLC_TRY(encode(&maps[o][0], h));
+            TLC_TRY(encode(&maps[o][1], l));
+        }
+    } else {
+        TLC_TRY(encode(&prm.tmA[0], A));
+        TLC_TRY(encode(&prm.tmB[0], B));
+    }
+
+    prm.C = g.C;
+    prm.c_rs = g.c_rs;
+    prm.nb = g.nb;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        prm.bsz[i] = i < g.nb ? (int)g.bsz[i] : 1;
+        prm.cbs[i] = i < g.nb ? g.cbs[i] : 0;
+        prm.a_bc[i] = (i < g.nb && A.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+        prm.b_bc[i] = (i < g.nb && B.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+    }
+    prm.M = (int)g.M;
+    prm.N = (int)g.N;
+    prm.K = (int)g.K;
+    prm.m_tiles = (int)((g.M + BM - 1) / BM);
+    prm.n_tiles = (int)((g.N + BN - 1) / BN);
+    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
+    prm.k_blocks = (int)((g.K + BK - 1) / BK);
+    prm.passes = passes;
+    prm.a_mn = a_mn ? 1 : 0;
+    prm.b_mn = b_mn ? 1 : 0;
+    prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
+    for (int i = 0; i < g.nb; ++i)
+        if (g.cbs[i] & 3) prm.vec_c = 0;
+    prm.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate wait
+    prm.err = error_word();
+    if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
+    for (int i = 0; i < g.nb; ++i)
+        if (g.bsz[i] > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "batch dim too large");
+    return BN == 256 ? launch_tc<256>(prm, s) : launch_tc<128>(prm, s);
+}
+
+int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
+    int* err = error_word();
+    if (!err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
+    bounded_wait_selftest_kernel<<<1, 32, 0, s>>>(timeout_ns, err);
+    count_launch();
+    return check_launch("bounded_wait_selftest");
+}
+
 }  // namespace tlc

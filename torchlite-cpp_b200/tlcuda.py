@@ -72,6 +72,8 @@ SIGNATURES = {
     "tlc_memcpy": ([_v, _v, _sz, _i, _v], _i),
     "tlc_memset_zero": ([_v, _sz, _v], _i),
     "tlc_stream_synchronize": ([_v], _i),
+    "tlc_check_device_errors": ([], _i),
+    "tlc_selftest_bounded_wait": ([ctypes.c_uint64], _i),
     "tlc_matmul_shape": ([_T, _T, _P(ctypes.c_int32), _P(_i64)], _i),
     "tlc_matmul": ([_T, _T, _T, _i, _v], _i),
     "tlc_matmul_backward": ([_T, _T, _T, _T, _T, _i, _i, _v], _i),
@@ -124,6 +126,16 @@ def mode_id(mode) -> int:
 
 def launch_count() -> int:
     return int(lib().tlc_launch_count())
+
+
+def check_device_errors():
+    """Synchronise the current device; raise if a kernel recorded a timeout."""
+    _check(lib().tlc_check_device_errors())
+
+
+def selftest_bounded_wait(timeout_ns: int) -> int:
+    """Status of the bounded-wait self test (TLC_ERR_TIMEOUT == 5 when it works)."""
+    return int(lib().tlc_selftest_bounded_wait(int(timeout_ns)))
 
 
 def _stream_ptr(stream):
