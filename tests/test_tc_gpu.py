@@ -126,13 +126,15 @@ def test_linear_full_size(mode):
 
 
 @pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
-def test_square_8192_sampled(mode):
+@pytest.mark.parametrize("n", [8192, 16384])
+def test_square_sampled(mode, n):
+    """The square sweep sizes, U[-1,1] seed 4: 16 sampled rows against float64."""
     g = torch.Generator(device=DEV).manual_seed(4)
-    A = torch.rand((8192, 8192), generator=g, device=DEV) * 2 - 1
-    B = torch.rand((8192, 8192), generator=g, device=DEV) * 2 - 1
+    A = torch.rand((n, n), generator=g, device=DEV) * 2 - 1
+    B = torch.rand((n, n), generator=g, device=DEV) * 2 - 1
     C = tlcuda.matmul(A, B, mode=mode)
     tlcuda.check_device_errors()
-    rows = torch.arange(0, 8192, 512, device=DEV)
+    rows = torch.arange(0, n, n // 16, device=DEV)
     a = A[rows].double().cpu().numpy()
     ref = a @ B.double().cpu().numpy()
     assert rel_fro(host(C[rows]), ref) <= TOL[mode]

@@ -19,8 +19,9 @@
 // M-major (a transposed view, storage [K,M]); B may be N-major (row-major
 // [K,N]) or K-major (a transposed view, storage [N,K], the X.W^T of Linear).
 // The instruction descriptor's per-operand major bits select the layout; an
-// MN-major tile is loaded as 32-element-wide column chunks so each shared
-// memory atom is 8 k-rows x 128 bytes.  Batch dims (up to 3, broadcast dims
+// MN-major tile is loaded as 32-element-wide column chunks with the 128-byte
+// swizzle of 32-byte granules (atoms of 4 k-rows x 128 bytes), the one
+// shared-memory layout MN-major TF32 operands accept.  Batch dims (up to 3, broadcast dims
 // with stride 0) are extra dimensions of the 5-D tensor maps, so ragged M, N
 // and K tails are zero-filled by TMA per batch entry and never read a
 // neighbouring matrix.
@@ -28,8 +29,11 @@
 // 3xTF32 (Ootomo & Yokota, "Recovering single precision accuracy from Tensor
 // Cores while surpassing the FP32 theoretical peak performance", 2022): each
 // operand x is split as hi = round_to_tf32(x), lo = x - hi (exact in fp32) by
-// a pre-pass; the main loop then runs the k range three times, accumulating
-// lo(A).hi(B) + hi(A).lo(B) + hi(A).hi(B) into one fp32 TMEM accumulator.
+// a pre-pass; the main loop then accumulates lo(A).hi(B) + hi(A).lo(B) +
+// hi(A).hi(B) in TMEM.  Because the tensor cores' fp32 accumulation error
+// grows with the chain length, 3xTF32 accumulates each 256-wide k chunk from
+// zero in its own (double-buffered) TMEM accumulator and the epilogue adds the
+// chunk results in fp32 round-to-nearest registers.
 //
 // Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
 // waiting thread raises a CTA-wide abort flag and a device error word, every
@@ -68,6 +72,8 @@ struct TcParams {
     int64_t num_tiles;
     int k_blocks;     // per pass
     int passes;       // 1 (TF32) or 3 (3xTF32)
+    int chunk_kb;     // k-blocks per accumulation chunk (== k_blocks: one chunk)
+    int num_chunks;
     int a_mn, b_mn;   // 1: operand is MN-major in memory
     int vec_c;        // float4 stores allowed
     uint64_t timeout_ns;
@@ -110,8 +116,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase of `bar` with the given parity.  Gives up (returns
 // false) when the CTA's abort flag is raised or the deadline passes; in the
 // latter case it raises the flag and records `site` in the device error word.
-__device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          uint64_t timeout_ns, int* err, int site) {
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag, uint64_t timeout_ns,
+                                             int* err, int site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
@@ -229,6 +236,27 @@ __device__ __forceinline__ void batch_coords(const TcParams& p, int b, int (&idx
     }
 }
 
+// Position of the i-th k-block load of a tile.  The k range is cut into
+// chunks of chunk_kb k-blocks; each chunk runs its passes back to back
+// (pass-major) and is accumulated from zero in its own TMEM accumulator, so
+// no tensor-core accumulation chain is longer than one chunk.
+struct KbPos {
+    int pass, kb;
+    bool first, last;  // first / last load of its chunk
+};
+__device__ __forceinline__ KbPos kb_pos(const TcParams& p, int i) {
+    const int per_chunk = p.passes * p.chunk_kb;
+    const int c = i / per_chunk;
+    const int r = i - c * per_chunk;
+    const int nc = min(p.chunk_kb, p.k_blocks - c * p.chunk_kb);
+    KbPos q;
+    q.pass = r / nc;
+    q.kb = c * p.chunk_kb + (r - q.pass * nc);
+    q.first = r == 0;
+    q.last = r == p.passes * nc - 1;
+    return q;
+}
+
 template <int BN>
 struct Smem {
     static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
@@ -240,8 +268,12 @@ struct Smem {
     static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
 };
 
-template <int BN>
+// CHUNKED (BN = 128 only): the epilogue keeps each thread's output row in
+// 128 registers and adds the chunk partials into it in fp32 round-to-nearest,
+// storing after the last chunk.  Otherwise a tile is one chunk.
+template <int BN, bool CHUNKED>
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    static_assert(!CHUNKED || BN == 128, "chunked accumulation keeps a 128-float row per thread");
     using S = Smem<BN>;
     constexpr int STAGES = S::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -322,8 +354,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     }
                     // The stage's previous load was consumed (the MMA that read it finished).
                     outstanding[stage] = -1;
-                    const int pass = kb / p.k_blocks;
-                    const int k0 = (kb - pass * p.k_blocks) * BK;
+                    const KbPos q = kb_pos(p, kb);
+                    const int pass = q.pass;
+                    const int k0 = q.kb * BK;
                     // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
                     const int pa = (p.passes > 1 && pass == 0) ? 1 : 0;
                     const int pb = (p.passes > 1 && pass == 1) ? 1 : 0;
@@ -381,13 +414,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             bool ok = true;
             bool issued = false;
             for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                if (!wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, p.timeout_ns, p.err, 2)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                uint32_t d = 0;
                 for (int kb = 0; kb < total_kb; ++kb) {
+                    const KbPos q = kb_pos(p, kb);
+                    if (q.first) {
+                        // a fresh accumulator for this chunk, once the epilogue drained it
+                        if (!wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, p.timeout_ns,
+                                          p.err, 2)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        d = tmem_base + (uint32_t)(acc * BN);
+                    }
                     if (!wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3)) {
                         ok = false;
                         break;
@@ -407,7 +446,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                         const uint64_t bd =
                             p.b_mn ? smem_desc(sb + j * 1024, chunk, 512, kSw128Atom32)
                                    : smem_desc(sb + j * UMMA_K * 4, 16, 1024, kSw128);
-                        umma_tf32(d, ad, bd, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                        umma_tf32(d, ad, bd, idesc, (!q.first || j > 0) ? 1u : 0u);
                     }
                     issued = true;
                     umma_commit(&empty[stage]);  // frees the stage when these MMAs finish
@@ -415,11 +454,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                         stage = 0;
                         phase ^= 1;
                     }
+                    if (q.last) {
+                        umma_commit(&tfull[acc]);  // chunk accumulator ready for the epilogue
+                        acc_phase[acc] ^= 1;
+                        acc ^= 1;
+                    }
                 }
-                if (!ok) break;
-                umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
-                acc_phase[acc] ^= 1;
-                acc ^= 1;
             }
             if (!ok && issued) {
                 // Drain MMAs still reading shared memory / writing TMEM.
@@ -435,13 +475,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         const int row_in_tile = q * 32 + lane;
         uint32_t acc_phase[2] = {0, 0};
         int acc = 0;
-        for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-            bool ok = true;
-            if (lane == 0)
-                ok = wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, p.timeout_ns, p.err, 4);
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // the whole warp takes one branch
-            if (!ok) break;
-            tc_fence_after();
+        bool ok = true;
+        for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
             const TileCoord tc = tile_coord(p, t);
             int bi[kMaxBatchDims];
             batch_coords(p, tc.b, bi);
@@ -451,34 +486,76 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             const int64_t row = (int64_t)tc.m * BM + row_in_tile;
             const int n0 = tc.n * BN;
             float* crow = p.C + oc + row * p.c_rs;
-            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(taddr + c * 32, r);
-                tmem_wait_ld();
-                if (row < p.M) {
-                    const int col0 = n0 + c * 32;
-                    if (p.vec_c && col0 + 32 <= p.N) {
+            float sum[CHUNKED ? BN : 1];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                   __uint_as_float(r[j + 2]),
-                                                   __uint_as_float(r[j + 3]));
-                            *reinterpret_cast<float4*>(crow + col0 + j) = v;
-                        }
-                    } else {
+            for (int j = 0; j < (CHUNKED ? BN : 1); ++j) sum[j] = 0.0f;
+            for (int ch = 0; ch < p.num_chunks; ++ch) {
+                if (lane == 0)
+                    ok = wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, p.timeout_ns, p.err, 4);
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // one branch per warp
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t taddr =
+                    tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+                if constexpr (CHUNKED) {
+#pragma unroll
+                    for (int c = 0; c < BN / 32; ++c) {
+                        uint32_t r[32];
+                        tmem_ld32(taddr + c * 32, r);
+                        tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
+                            sum[c * 32 + j] = __fadd_rn(sum[c * 32 + j], __uint_as_float(r[j]));
+                    }
+                } else {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; ++c) {
+                        uint32_t r[32];
+                        tmem_ld32(taddr + c * 32, r);
+                        tmem_wait_ld();
+                        if (row < p.M) {
+                            const int col0 = n0 + c * 32;
+                            if (p.vec_c && col0 + 32 <= p.N) {
+#pragma unroll
+                                for (int j = 0; j < 32; j += 4) {
+                                    float4 v = make_float4(
+                                        __uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                        __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                                    *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);
+                acc_phase[acc] ^= 1;
+                acc ^= 1;
+            }
+            if constexpr (CHUNKED) {
+                if (ok && row < p.M) {
+#pragma unroll
+                    for (int c = 0; c < BN / 32; ++c) {
+                        const int col0 = n0 + c * 32;
+                        if (p.vec_c && col0 + 32 <= p.N) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(crow + col0 + j) =
+                                    make_float4(sum[c * 32 + j], sum[c * 32 + j + 1],
+                                                sum[c * 32 + j + 2], sum[c * 32 + j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.N) crow[col0 + j] = sum[c * 32 + j];
+                        }
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
-            acc_phase[acc] ^= 1;
-            acc ^= 1;
         }
     }
 
@@ -654,21 +731,21 @@ int repack(OperandMap& o, int nb, TcScratch& sc, int slot, cudaStream_t s) {
     return TLC_OK;
 }
 
-template <int BN>
+template <int BN, bool CHUNKED>
 int launch_tc(const TcParams& prm, cudaStream_t s) {
     using S = Smem<BN>;
     static int configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<BN>,
+        TLC_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<BN, CHUNKED>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
         configured[dev] = 1;
     }
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t grid = std::min<int64_t>(prm.num_tiles, sms);
-    tc_gemm_kernel<BN><<<(unsigned)grid, NUM_THREADS, S::TOTAL, s>>>(prm);
+    tc_gemm_kernel<BN, CHUNKED><<<(unsigned)grid, NUM_THREADS, S::TOTAL, s>>>(prm);
     count_launch();
     return check_launch("tc_gemm");
 }
@@ -717,7 +794,9 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
         A.bstride[i] = i < g.nb ? g.abs_[i] : 0;
         B.bstride[i] = i < g.nb ? g.bbs[i] : 0;
     }
-    const int BN = g.N > 128 ? 256 : 128;
+    const int passes = mode == TLC_MODE_3XTF32 ? 3 : 1;
+    // 3xTF32 runs 128-wide tiles so the epilogue can hold a row of chunk sums.
+    const int BN = (passes == 1 && g.N > 128) ? 256 : 128;
     A.box_inner = 32;
     A.box_outer = a_mn ? BK : BM;
     A.mn_major = a_mn;
@@ -731,7 +810,6 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
 
     TcParams prm;
     memset(&prm, 0, sizeof(prm));
-    const int passes = mode == TLC_MODE_3XTF32 ? 3 : 1;
     if (passes == 3) {
         // Split each operand's storage span into hi / lo planes of identical layout.
         OperandMap* ops[2] = {&A, &B};
@@ -774,6 +852,13 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
     prm.k_blocks = (int)((g.K + BK - 1) / BK);
     prm.passes = passes;
+    // The tensor cores' fp32 accumulation error grows linearly with the
+    // length of the accumulation chain (measured: ~2.4e-9 x K relative,
+    // biased towards zero), which puts long-K 3xTF32 above 1e-5.  3xTF32
+    // therefore restarts the TMEM accumulator every 256 k (8 k-blocks) and
+    // sums the chunks in fp32 round-to-nearest; TF32 keeps one chain.
+    prm.chunk_kb = passes == 3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
+    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
     prm.a_mn = a_mn ? 1 : 0;
     prm.b_mn = b_mn ? 1 : 0;
     prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
@@ -784,7 +869,8 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
     for (int i = 0; i < g.nb; ++i)
         if (g.bsz[i] > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "batch dim too large");
-    return BN == 256 ? launch_tc<256>(prm, s) : launch_tc<128>(prm, s);
+    if (passes == 3) return launch_tc<128, true>(prm, s);
+    return BN == 256 ? launch_tc<256, false>(prm, s) : launch_tc<128, false>(prm, s);
 }
 
 int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
