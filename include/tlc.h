@@ -169,6 +169,25 @@ int tlc_matmul_backward_host(const tlc_tensor* grad, const tlc_tensor* a, const 
 /* The GEMM core (see tlc_gemm_desc). */
 int tlc_gemm(const tlc_gemm_desc* desc, int mode, void* stream);
 
+/* 3xTF32 GEMM that allocates no device memory.  No counterpart in the
+ * reference (its CPU path has no device memory to allocate); it exists for
+ * callers that may not let this library allocate: an application whose device
+ * memory all belongs to its own arena allocator, or a latency-critical loop
+ * where an allocation that can block or fail is not allowed.  Same arguments
+ * and result as tlc_gemm(desc, TLC_MODE_3XTF32, stream), except:
+ *  - the hi / lo split planes live in one 64 MiB device array inside the
+ *    library, held on every GPU that loads it until the process exits; A and
+ *    B together may span at most 8 Mi floats (minus 64-float padding per
+ *    plane); larger problems return TLC_ERR_INVALID_ARGUMENT;
+ *  - A and B must be 16-byte aligned with strides that are multiples of 4
+ *    floats (else TLC_ERR_UNSUPPORTED);
+ *  - the first call on a device looks up that array's device address (set-up
+ *    work), so make it before any stream capture;
+ *  - all calls share the array: calls that overlap on the GPU race, so
+ *    serialise them (each call rewrites every element it reads, so nothing
+ *    needs clearing between calls). */
+int tlc_gemm_3xtf32_noalloc(const tlc_gemm_desc* desc, void* stream);
+
 /* ---- building blocks of the backward pass --------------------------------- */
 
 /* sum(input, dim, keepdim) of src/ops.cpp:1181-1233 for a contiguous input

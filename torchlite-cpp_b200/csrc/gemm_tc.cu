@@ -881,4 +881,192 @@ int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
     return check_launch("bounded_wait_selftest");
 }
 
+// ---- 3xTF32 GEMM without any device allocation ---------------------------------------
+//
+// The regular 3xTF32 path takes its hi / lo operand planes from the stream-
+// ordered memory pool.  Some callers of this library may not let it allocate
+// device memory at all: a host application whose device memory is entirely
+// owned by its own arena allocator (memory taken behind its back breaks its
+// budget), or a latency-critical loop where an allocation that can block on
+// the device or fail under memory pressure is not acceptable.  For them,
+// tlc_gemm_3xtf32_noalloc runs the same split + tensor-core kernels with the
+// planes in this fixed, file-scope device array instead.
+//
+// Properties a caller must know:
+//  - Every GPU that loads the library holds these 64 MiB until the process exits.
+//  - Host code cannot use the array's name as a device address (it is a host-
+//    side stand-in); the device address comes from cudaGetSymbolAddress, taken
+//    once per device, with that device current, by the first call on it.  That
+//    first call therefore does set-up work and should come before any stream
+//    capture.
+//  - All calls share the one array and it keeps the last call's contents.
+//    Each call rewrites, with the split pre-pass, every element its GEMM then
+//    reads, so nothing has to start at zero; but two calls whose work overlaps
+//    on the GPU (different streams, or different host threads on one device)
+//    race on the array.  Serialise them.
+//  - Operands must already suit TMA (16-byte aligned, strides multiples of 4
+//    floats): unaligned operands would need a repacking copy, i.e. more memory.
+
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device, looked up once.
+int noalloc_scratch(float** out) {
+    static std::mutex mu;
+    static float* addr[64] = {};
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        float* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(TLC_ERR_CUDA, std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") +
+                                               cudaGetErrorString(e));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return TLC_OK;
+}
+
+int64_t pad64(int64_t n) { return (n + 63) & ~int64_t(63); }  // keeps planes 256-byte aligned
+
+int gemm_3xtf32_noalloc(const tlc_gemm_desc* d, cudaStream_t s) {
+    if (!d) return set_error(TLC_ERR_INVALID_ARGUMENT, "tlc_gemm_3xtf32_noalloc: desc is NULL");
+    if (d->M < 0 || d->N < 0 || d->K < 0 || d->batch_ndim < 0 || d->batch_ndim > 3)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "tlc_gemm_3xtf32_noalloc: bad sizes");
+    Gemm g{};
+    g.M = d->M;
+    g.N = d->N;
+    g.K = d->K;
+    g.A = d->A;
+    g.B = d->B;
+    g.C = d->C;
+    g.c_rs = d->c_rs;
+    g.a_rs = d->a_rs;
+    g.a_cs = d->a_cs;
+    g.b_rs = d->b_rs;
+    g.b_cs = d->b_cs;
+    g.nb = d->batch_ndim;
+    for (int i = 0; i < g.nb; ++i) {
+        if (d->batch_sizes[i] < 0)
+            return set_error(TLC_ERR_INVALID_ARGUMENT, "tlc_gemm_3xtf32_noalloc: bad batch size");
+        g.bsz[i] = d->batch_sizes[i];
+        g.abs_[i] = d->a_bstride[i];
+        g.bbs[i] = d->b_bstride[i];
+        g.cbs[i] = d->c_bstride[i];
+    }
+    if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
+    if (g.K == 0) return gemm_exact(g, s);  // writes zeros, uses no scratch
+    if (g.a_cs != 1 && g.a_rs != 1)
+        return set_error(TLC_ERR_INVALID_ARGUMENT,
+                         "tlc_gemm_3xtf32_noalloc: A needs a unit stride in one matrix dim");
+    if (g.b_cs != 1 && g.b_rs != 1)
+        return set_error(TLC_ERR_INVALID_ARGUMENT,
+                         "tlc_gemm_3xtf32_noalloc: B needs a unit stride in one matrix dim");
+    if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX)
+        return set_error(TLC_ERR_UNSUPPORTED, "tlc_gemm_3xtf32_noalloc: a dimension exceeds 2^31");
+    for (int i = 0; i < g.nb; ++i)
+        if (g.bsz[i] > INT32_MAX)
+            return set_error(TLC_ERR_UNSUPPORTED, "tlc_gemm_3xtf32_noalloc: batch dim too large");
+
+    const bool a_mn = g.a_cs != 1;
+    const bool b_mn = g.b_cs == 1;
+    OperandMap A{}, B{};
+    A.base = g.A;
+    A.inner = a_mn ? g.M : g.K;
+    A.outer = a_mn ? g.K : g.M;
+    A.outer_stride = a_mn ? g.a_cs : g.a_rs;
+    B.base = g.B;
+    B.inner = b_mn ? g.N : g.K;
+    B.outer = b_mn ? g.K : g.N;
+    B.outer_stride = b_mn ? g.b_rs : g.b_cs;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        A.bsz[i] = B.bsz[i] = i < g.nb ? g.bsz[i] : 1;
+        A.bstride[i] = i < g.nb ? g.abs_[i] : 0;
+        B.bstride[i] = i < g.nb ? g.bbs[i] : 0;
+    }
+    A.box_inner = B.box_inner = 32;
+    A.box_outer = a_mn ? BK : BM;
+    B.box_outer = b_mn ? BK : 128;
+    A.mn_major = a_mn;
+    B.mn_major = b_mn;
+    if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb) ||
+        !tma_ok(B.base, B.outer_stride, B.bstride, g.nb))
+        return set_error(TLC_ERR_UNSUPPORTED,
+                         "tlc_gemm_3xtf32_noalloc: operands must be 16-byte aligned with strides "
+                         "that are multiples of 4 floats (repacking them would need memory)");
+
+    const int64_t na = span_elems(A.inner, A.outer, A.outer_stride, A.bsz, A.bstride, g.nb);
+    const int64_t nb = span_elems(B.inner, B.outer, B.outer_stride, B.bsz, B.bstride, g.nb);
+    const int64_t need = 2 * (pad64(na) + pad64(nb));  // hi + lo plane of each operand
+    const int64_t cap = (int64_t)(kNoAllocScratchBytes / sizeof(float));
+    if (need > cap)
+        return set_error(TLC_ERR_INVALID_ARGUMENT,
+                         "tlc_gemm_3xtf32_noalloc: operands need " +
+                             std::to_string(need * 4 / 1024) + " KiB of split planes, above the " +
+                             std::to_string(kNoAllocScratchBytes >> 20) +
+                             " MiB static scratch; use tlc_gemm with TLC_MODE_3XTF32");
+
+    float* base = nullptr;
+    TLC_TRY(noalloc_scratch(&base));
+    float* planes[4] = {base, base + pad64(na), base + 2 * pad64(na),
+                        base + 2 * pad64(na) + pad64(nb)};  // A hi, A lo, B hi, B lo
+    TcParams prm;
+    memset(&prm, 0, sizeof(prm));
+    split_tf32_kernel<<<grid_split(na), 256, 0, s>>>(A.base, planes[0], planes[1], na);
+    count_launch();
+    TLC_TRY(check_launch("split_tf32"));
+    split_tf32_kernel<<<grid_split(nb), 256, 0, s>>>(B.base, planes[2], planes[3], nb);
+    count_launch();
+    TLC_TRY(check_launch("split_tf32"));
+    OperandMap ah = A, al = A, bh = B, bl = B;
+    ah.base = planes[0];
+    al.base = planes[1];
+    bh.base = planes[2];
+    bl.base = planes[3];
+    TLC_TRY(encode(&prm.tmA[0], ah));
+    TLC_TRY(encode(&prm.tmA[1], al));
+    TLC_TRY(encode(&prm.tmB[0], bh));
+    TLC_TRY(encode(&prm.tmB[1], bl));
+
+    prm.C = g.C;
+    prm.c_rs = g.c_rs;
+    prm.nb = g.nb;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        prm.bsz[i] = i < g.nb ? (int)g.bsz[i] : 1;
+        prm.cbs[i] = i < g.nb ? g.cbs[i] : 0;
+        prm.a_bc[i] = (i < g.nb && A.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+        prm.b_bc[i] = (i < g.nb && B.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+    }
+    prm.M = (int)g.M;
+    prm.N = (int)g.N;
+    prm.K = (int)g.K;
+    prm.m_tiles = (int)((g.M + BM - 1) / BM);
+    prm.n_tiles = (int)((g.N + 127) / 128);
+    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
+    prm.k_blocks = (int)((g.K + BK - 1) / BK);
+    prm.passes = 3;
+    prm.chunk_kb = std::min(prm.k_blocks, 8);
+    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
+    prm.a_mn = a_mn ? 1 : 0;
+    prm.b_mn = b_mn ? 1 : 0;
+    prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
+    for (int i = 0; i < g.nb; ++i)
+        if (g.cbs[i] & 3) prm.vec_c = 0;
+    prm.timeout_ns = 2000000000ull;
+    prm.err = error_word();
+    if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
+    return launch_tc<128, true>(prm, s);
+}
+
+}  // namespace
 }  // namespace tlc
+
+extern "C" int tlc_gemm_3xtf32_noalloc(const tlc_gemm_desc* desc, void* stream) {
+    tlc::clear_error();
+    return tlc::gemm_3xtf32_noalloc(desc, static_cast<cudaStream_t>(stream));
+}

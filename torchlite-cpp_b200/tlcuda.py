@@ -80,6 +80,7 @@ SIGNATURES = {
     "tlc_matmul_host": ([_T, _T, _T, _i, _v], _i),
     "tlc_matmul_backward_host": ([_T, _T, _T, _T, _T, _i, _i, _v], _i),
     "tlc_gemm": ([_P(GemmDesc), _i, _v], _i),
+    "tlc_gemm_3xtf32_noalloc": ([_P(GemmDesc), _v], _i),
     "tlc_sum_dim": ([_v, _v, _i64, _i64, _i64, _v], _i),
     "tlc_add": ([_v, _v, _v, _i64, _v], _i),
     "tlc_contiguous": ([_T, _v, _v], _i),
