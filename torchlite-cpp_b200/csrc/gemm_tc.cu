@@ -1,19 +1,29 @@
 // Tensor-core GEMM for TLC_MODE_TF32 and TLC_MODE_3XTF32 on sm_100a (tcgen05).
 //
-// One persistent CTA per SM, 6 warps, warp-specialised:
+// Persistent, warp-specialised kernel; 6 warps per CTA:
 //   warp 0      TMA producer: one elected thread streams A and B k-blocks
 //               (32 fp32 = 128 bytes of k) into a ring of shared-memory stages
 //               with cp.async.bulk.tensor (128-byte swizzle), completion
 //               tracked by an mbarrier per stage (expect_tx bytes).
-//   warp 1      MMA issuer: allocates the tensor memory (TMEM), and one
-//               elected thread issues tcgen05.mma.kind::tf32 (M=128, N=BN,
-//               K=8 per instruction, 4 per k-block) into an fp32 accumulator
-//               in TMEM; tcgen05.commit frees each stage and publishes each
-//               finished accumulator.
+//   warp 1      TMEM allocation; one elected thread of the leader CTA issues
+//               tcgen05.mma.kind::tf32 (K = 8 per instruction, 4 per k-block)
+//               into an fp32 accumulator in tensor memory; tcgen05.commit
+//               frees each stage and publishes each finished accumulator.
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (each thread one row of
-//               the 128-row tile), store to global fp32 C.
-// The accumulator is double-buffered in TMEM (2 x BN columns), so the
-// epilogue of tile i overlaps the main loop of tile i+1.
+//               128), store fp32 C.
+// The accumulator is double-buffered in TMEM, so the epilogue of one tile
+// overlaps the main loop of the next.
+//
+// CTA pairs (CG = 2, the default for problems with more than 128 rows): two
+// CTAs of a cluster share one M = 256 tcgen05.mma.cta_group::2.  Each CTA
+// loads its own 128 rows of A and its own half of the tile's B columns, so a
+// CTA moves 32 KB per k-block instead of 48 KB for the same 128 x 256 x 32 of
+// work, and six stages fit instead of four.  Both CTAs' TMA loads complete on
+// the leader CTA's full barrier; the leader issues the MMAs (reading both
+// CTAs' shared memory, writing both CTAs' TMEM) and commits each completion
+// to a barrier in each CTA with a unicast commit; each CTA's epilogue drains
+// its own TMEM rows and signals the leader.  No load uses cluster multicast:
+// every CTA fetches its own tiles.
 //
 // Operand layouts are read in place: A may be K-major (row-major [M,K]) or
 // M-major (a transposed view, storage [K,M]); B may be N-major (row-major
@@ -21,10 +31,10 @@
 // The instruction descriptor's per-operand major bits select the layout; an
 // MN-major tile is loaded as 32-element-wide column chunks with the 128-byte
 // swizzle of 32-byte granules (atoms of 4 k-rows x 128 bytes), the one
-// shared-memory layout MN-major TF32 operands accept.  Batch dims (up to 3, broadcast dims
-// with stride 0) are extra dimensions of the 5-D tensor maps, so ragged M, N
-// and K tails are zero-filled by TMA per batch entry and never read a
-// neighbouring matrix.
+// shared-memory layout MN-major TF32 operands accept.  Batch dims (up to 3,
+// broadcast dims with stride 0) are extra dimensions of the 5-D tensor maps,
+// so ragged M, N and K tails are zero-filled by TMA per batch entry and never
+// read a neighbouring matrix.
 //
 // 3xTF32 (Ootomo & Yokota, "Recovering single precision accuracy from Tensor
 // Cores while surpassing the FP32 theoretical peak performance", 2022): each
@@ -42,6 +52,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -52,7 +64,7 @@ __device__ int g_tc_error = 0;  // first failing wait site of any tensor-core la
 
 namespace {
 
-constexpr int BM = 128;        // UMMA M
+constexpr int BM = 128;        // rows of A (and of D) per CTA
 constexpr int BK = 32;         // k per stage: 32 fp32 = one 128-byte swizzle row
 constexpr int UMMA_K = 8;      // k per tcgen05.mma.kind::tf32
 constexpr int NUM_THREADS = 192;
@@ -90,6 +102,20 @@ __device__ __forceinline__ uint64_t globaltimer() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
@@ -100,6 +126,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
@@ -134,14 +164,27 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
     }
 }
 
-__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar,
+// TMA tile load into this CTA's shared memory.  CG = 2: completion is
+// reported to the barrier at `bar_cluster` (the leader CTA's, a cluster
+// address); CG = 1: to the local barrier.
+template <int CG>
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2, int c3, int c4) {
-    asm volatile(
-        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
-        "r"(smem_u32(bar))
-        : "memory");
+    if constexpr (CG == 2) {
+        asm volatile(
+            "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+            "r"(bar)
+            : "memory");
+    } else {
+        asm volatile(
+            "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+            "r"(bar)
+            : "memory");
+    }
 }
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -152,6 +195,28 @@ __device__ __forceinline__ void tc_fence_before() {
 }
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+template <int CG>
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+    if constexpr (CG == 2) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(slot)),
+                     "r"(cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(slot)),
+                     "r"(cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+}
+template <int CG>
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
+    if constexpr (CG == 2)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+    else
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
 }
 
 // Shared-memory matrix descriptor: start address, leading / stride byte
@@ -168,19 +233,35 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
            (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
 }
 
+template <int CG>
 __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                           uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    if constexpr (CG == 2) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    }
 }
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(bar))
-        : "memory");
+// Arrive on the barrier at cluster address `bar` once every MMA this thread
+// issued so far has completed.
+template <int CG>
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    if constexpr (CG == 2)
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+            : "memory");
+    else
+        asm volatile(
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+            : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -257,40 +338,51 @@ __device__ __forceinline__ KbPos kb_pos(const TcParams& p, int i) {
     return q;
 }
 
-template <int BN>
-struct Smem {
-    static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
-    static constexpr int B_BYTES = BN * BK * 4;  // 32 KB (BN=256) / 16 KB (BN=128)
+// Shapes of one kernel variant.  CG: CTAs per MMA (1, or a pair); UN: the
+// MMA's N (tile columns); each CTA holds 128 rows of A, UN / CG columns of B
+// and a 128 x UN fp32 accumulator (twice, double-buffered).
+template <int CG, int UN>
+struct Cfg {
+    static constexpr int B_COLS = UN / CG;
+    static constexpr int A_BYTES = BM * BK * 4;      // 16 KB
+    static constexpr int B_BYTES = B_COLS * BK * 4;  // 4 KB per 32 columns
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256) ? 4 : 6;
-    static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+    static constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+    static constexpr int TMEM_COLS = 2 * UN;
+    static constexpr int TILE_M = BM * CG;
     static constexpr int BAR_BYTES = 256;
     static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+    static_assert(TMEM_COLS <= 512, "two accumulators must fit in TMEM");
+    static_assert(B_COLS % 32 == 0 && B_COLS <= 256, "B tile columns");
 };
 
-// CHUNKED (BN = 128 only): the epilogue keeps each thread's output row in
+// CHUNKED (UN = 128 only): the epilogue keeps each thread's output row in
 // 128 registers and adds the chunk partials into it in fp32 round-to-nearest,
 // storing after the last chunk.  Otherwise a tile is one chunk.
-template <int BN, bool CHUNKED>
+template <int CG, int UN, bool CHUNKED>
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    static_assert(!CHUNKED || BN == 128, "chunked accumulation keeps a 128-float row per thread");
-    using S = Smem<BN>;
+    static_assert(!CHUNKED || UN == 128, "chunked accumulation keeps a 128-float row per thread");
+    using S = Cfg<CG, UN>;
     constexpr int STAGES = S::STAGES;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte-swizzle atoms.
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
-    uint64_t* full = bars;                 // [STAGES]
+    uint64_t* full = bars;                 // [STAGES]  (used in the leader CTA)
     uint64_t* empty = bars + STAGES;       // [STAGES]
     uint64_t* tfull = bars + 2 * STAGES;   // [2]
-    uint64_t* tempty = tfull + 2;          // [2]
+    uint64_t* tempty = tfull + 2;          // [2]       (used in the leader CTA)
     uint64_t* drain = tempty + 2;          // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int64_t unit = CG == 2 ? blockIdx.x / 2 : blockIdx.x;  // tile-walking unit (pair)
+    const int64_t units = CG == 2 ? gridDim.x / 2 : gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -299,7 +391,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+            mbar_init(&tempty[a], 4 * CG);  // one arrival per epilogue warp of each CTA
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -316,20 +408,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     }
     if (warp == 1) {
         __syncwarp();
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(tmem_slot)),
-                     "r"(S::TMEM_COLS));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tmem_alloc<CG>(tmem_slot, S::TMEM_COLS);
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // peer barriers initialised before any remote use
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     const int total_kb = p.k_blocks * p.passes;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
@@ -338,7 +428,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             int outstanding[STAGES];
             for (int s = 0; s < STAGES; ++s) outstanding[s] = -1;
             bool ok = true;
-            for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+            for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
                 const TileCoord tc = tile_coord(p, t);
                 int bi[kMaxBatchDims];
                 batch_coords(p, tc.b, bi);
@@ -346,7 +436,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                           a2 = p.a_bc[2] ? bi[2] : 0;
                 const int b0 = p.b_bc[0] ? bi[0] : 0, b1 = p.b_bc[1] ? bi[1] : 0,
                           b2 = p.b_bc[2] ? bi[2] : 0;
-                const int m0 = tc.m * BM, n0 = tc.n * BN;
+                const int m0 = tc.m * S::TILE_M + (int)rank * BM;       // this CTA's A rows
+                const int n0 = tc.n * UN + (int)rank * S::B_COLS;       // this CTA's B columns
                 for (int kb = 0; kb < total_kb; ++kb) {
                     if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1)) {
                         ok = false;
@@ -355,27 +446,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     // The stage's previous load was consumed (the MMA that read it finished).
                     outstanding[stage] = -1;
                     const KbPos q = kb_pos(p, kb);
-                    const int pass = q.pass;
                     const int k0 = q.kb * BK;
                     // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
-                    const int pa = (p.passes > 1 && pass == 0) ? 1 : 0;
-                    const int pb = (p.passes > 1 && pass == 1) ? 1 : 0;
+                    const int pa = (p.passes > 1 && q.pass == 0) ? 1 : 0;
+                    const int pb = (p.passes > 1 && q.pass == 1) ? 1 : 0;
                     uint8_t* sa = smem + stage * S::STAGE_BYTES;
                     uint8_t* sb = sa + S::A_BYTES;
-                    mbar_expect_tx(&full[stage], S::STAGE_BYTES);
+                    const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
+                                                : smem_u32(&full[stage]);
+                    if (leader) mbar_expect_tx(&full[stage], S::STAGE_BYTES * CG);
                     if (p.a_mn) {
                         for (int c = 0; c < BM / 32; ++c)
-                            tma_load_5d(sa + c * (32 * BK * 4), &p.tmA[pa], &full[stage], m0 + 32 * c,
-                                        k0, a0, a1, a2);
+                            tma_load_5d<CG>(sa + c * (32 * BK * 4), &p.tmA[pa], fb, m0 + 32 * c, k0,
+                                            a0, a1, a2);
                     } else {
-                        tma_load_5d(sa, &p.tmA[pa], &full[stage], k0, m0, a0, a1, a2);
+                        tma_load_5d<CG>(sa, &p.tmA[pa], fb, k0, m0, a0, a1, a2);
                     }
                     if (p.b_mn) {
-                        for (int c = 0; c < BN / 32; ++c)
-                            tma_load_5d(sb + c * (32 * BK * 4), &p.tmB[pb], &full[stage], n0 + 32 * c,
-                                        k0, b0, b1, b2);
+                        for (int c = 0; c < S::B_COLS / 32; ++c)
+                            tma_load_5d<CG>(sb + c * (32 * BK * 4), &p.tmB[pb], fb, n0 + 32 * c, k0,
+                                            b0, b1, b2);
                     } else {
-                        tma_load_5d(sb, &p.tmB[pb], &full[stage], k0, n0, b0, b1, b2);
+                        tma_load_5d<CG>(sb, &p.tmB[pb], fb, k0, n0, b0, b1, b2);
                     }
                     outstanding[stage] = (int)phase;
                     if (++stage == STAGES) {
@@ -384,8 +476,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     }
                 }
             }
-            if (!ok) {
-                // Drain: wait (bounded) for loads still in flight into shared memory.
+            if (!ok && leader) {
+                // Drain: wait (bounded) for loads still in flight into shared memory
+                // (the leader's full barriers count both CTAs' bytes).
                 for (int s = 0; s < STAGES; ++s) {
                     if (outstanding[s] < 0) continue;
                     const uint64_t t0 = globaltimer();
@@ -396,36 +489,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer (leader CTA) ----------------
+        if (lane == 0 && leader) {
             // kind::tf32: D fp32 (bits 4-5 = 1), A/B TF32 (bits 7-9, 10-12 = 2),
             // A/B major (bits 15, 16), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
             const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) |
                                    ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16) |
-                                   ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-            // MN-major tiles: 32-wide chunks of 32 k-rows (4 KB) side by side
-            // (leading byte offset), 8-row atoms (1 KB) along k (stride byte
-            // offset).  K-major tiles: 128-byte rows, 8-row atoms 1 KB apart.
-            const uint32_t chunk = 32 * BK * 4;
+                                   ((uint32_t)(UN >> 3) << 17) |
+                                   ((uint32_t)(S::TILE_M >> 4) << 24);
+            const uint32_t chunk = 32 * BK * 4;  // bytes between 32-wide MN chunks
             int stage = 0;
             uint32_t phase = 0;
             uint32_t acc_phase[2] = {0, 0};
             int acc = 0;
             bool ok = true;
             bool issued = false;
-            for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+            for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
                 uint32_t d = 0;
                 for (int kb = 0; kb < total_kb; ++kb) {
                     const KbPos q = kb_pos(p, kb);
                     if (q.first) {
-                        // a fresh accumulator for this chunk, once the epilogue drained it
+                        // a fresh accumulator for this chunk, once the epilogues drained it
                         if (!wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, p.timeout_ns,
                                           p.err, 2)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        d = tmem_base + (uint32_t)(acc * BN);
+                        d = tmem_base + (uint32_t)(acc * UN);
                     }
                     if (!wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3)) {
                         ok = false;
@@ -446,16 +537,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                         const uint64_t bd =
                             p.b_mn ? smem_desc(sb + j * 1024, chunk, 512, kSw128Atom32)
                                    : smem_desc(sb + j * UMMA_K * 4, 16, 1024, kSw128);
-                        umma_tf32(d, ad, bd, idesc, (!q.first || j > 0) ? 1u : 0u);
+                        umma_tf32<CG>(d, ad, bd, idesc, (!q.first || j > 0) ? 1u : 0u);
                     }
                     issued = true;
-                    umma_commit(&empty[stage]);  // frees the stage when these MMAs finish
+                    // free the stage in every CTA once these MMAs finish
+                    umma_commit<CG>(smem_u32(&empty[stage]));
+                    if constexpr (CG == 2) umma_commit<CG>(mapa(smem_u32(&empty[stage]), 1));
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                     if (q.last) {
-                        umma_commit(&tfull[acc]);  // chunk accumulator ready for the epilogue
+                        // chunk accumulator ready for the epilogues of both CTAs
+                        umma_commit<CG>(smem_u32(&tfull[acc]));
+                        if constexpr (CG == 2) umma_commit<CG>(mapa(smem_u32(&tfull[acc]), 1));
                         acc_phase[acc] ^= 1;
                         acc ^= 1;
                     }
@@ -463,32 +558,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             }
             if (!ok && issued) {
                 // Drain MMAs still reading shared memory / writing TMEM.
-                umma_commit(drain);
+                umma_commit<CG>(smem_u32(drain));
                 const uint64_t t0 = globaltimer();
                 while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < p.timeout_ns) {
                 }
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2..5, both CTAs) ----------------
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
+        const uint32_t tempty_leader[2] = {CG == 2 ? mapa(smem_u32(&tempty[0]), 0) : 0u,
+                                           CG == 2 ? mapa(smem_u32(&tempty[1]), 0) : 0u};
         uint32_t acc_phase[2] = {0, 0};
         int acc = 0;
         bool ok = true;
-        for (int64_t t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+        for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
             const TileCoord tc = tile_coord(p, t);
             int bi[kMaxBatchDims];
             batch_coords(p, tc.b, bi);
             int64_t oc = 0;
 #pragma unroll
             for (int i = 0; i < kMaxBatchDims; ++i) oc += (int64_t)bi[i] * p.cbs[i];
-            const int64_t row = (int64_t)tc.m * BM + row_in_tile;
-            const int n0 = tc.n * BN;
+            const int64_t row = (int64_t)tc.m * S::TILE_M + (int)rank * BM + row_in_tile;
+            const int n0 = tc.n * UN;
             float* crow = p.C + oc + row * p.c_rs;
-            float sum[CHUNKED ? BN : 1];
+            float sum[CHUNKED ? UN : 1];
 #pragma unroll
-            for (int j = 0; j < (CHUNKED ? BN : 1); ++j) sum[j] = 0.0f;
+            for (int j = 0; j < (CHUNKED ? UN : 1); ++j) sum[j] = 0.0f;
             for (int ch = 0; ch < p.num_chunks; ++ch) {
                 if (lane == 0)
                     ok = wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, p.timeout_ns, p.err, 4);
@@ -496,10 +593,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t taddr =
-                    tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+                    tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * UN);
                 if constexpr (CHUNKED) {
 #pragma unroll
-                    for (int c = 0; c < BN / 32; ++c) {
+                    for (int c = 0; c < UN / 32; ++c) {
                         uint32_t r[32];
                         tmem_ld32(taddr + c * 32, r);
                         tmem_wait_ld();
@@ -509,7 +606,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     }
                 } else {
 #pragma unroll 1
-                    for (int c = 0; c < BN / 32; ++c) {
+                    for (int c = 0; c < UN / 32; ++c) {
                         uint32_t r[32];
                         tmem_ld32(taddr + c * 32, r);
                         tmem_wait_ld();
@@ -533,14 +630,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[acc]);
+                if (lane == 0) {
+                    if (CG == 2 && !leader)
+                        mbar_arrive_remote(tempty_leader[acc]);
+                    else
+                        mbar_arrive(&tempty[acc]);
+                }
                 acc_phase[acc] ^= 1;
                 acc ^= 1;
             }
             if constexpr (CHUNKED) {
                 if (ok && row < p.M) {
 #pragma unroll
-                    for (int c = 0; c < BN / 32; ++c) {
+                    for (int c = 0; c < UN / 32; ++c) {
                         const int col0 = n0 + c * 32;
                         if (p.vec_c && col0 + 32 <= p.N) {
 #pragma unroll
@@ -561,11 +663,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 
     tc_fence_before();
     __syncthreads();
+    // CG = 2: neither CTA frees its TMEM or exits while the pair's MMAs or the
+    // peer's remote arrivals may still touch its memory.
+    if constexpr (CG == 2) cluster_sync();
     tc_fence_after();
     if (warp == 1) {
         __syncwarp();  // .sync.aligned: the whole warp, converged
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                     "r"(S::TMEM_COLS));
+        tmem_dealloc<CG>(tmem_base, S::TMEM_COLS);
     }
 }
 
@@ -731,25 +835,6 @@ int repack(OperandMap& o, int nb, TcScratch& sc, int slot, cudaStream_t s) {
     return TLC_OK;
 }
 
-template <int BN, bool CHUNKED>
-int launch_tc(const TcParams& prm, cudaStream_t s) {
-    using S = Smem<BN>;
-    static int configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<BN, CHUNKED>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-        configured[dev] = 1;
-    }
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t grid = std::min<int64_t>(prm.num_tiles, sms);
-    tc_gemm_kernel<BN, CHUNKED><<<(unsigned)grid, NUM_THREADS, S::TOTAL, s>>>(prm);
-    count_launch();
-    return check_launch("tc_gemm");
-}
-
 int* error_word() {
     static int* words[64] = {};
     int dev = 0;
@@ -761,6 +846,136 @@ int* error_word() {
         words[dev] = p;
     }
     return words[dev];
+}
+
+template <int CG, int UN, bool CHUNKED>
+int launch_variant(const TcParams& prm, cudaStream_t s) {
+    using S = Cfg<CG, UN>;
+    auto kernel = tc_gemm_kernel<CG, UN, CHUNKED>;
+    static int configured[64] = {};
+    static int max_units[64] = {};
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = S::TOTAL;
+    cfg.stream = s;
+    if (CG == 2) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    if (!configured[dev]) {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          S::TOTAL));
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int units = CG == 2 ? sms / 2 : sms;
+        if (CG == 2) {
+            // How many CTA pairs can be resident at once (pairs share a GPC).
+            int clusters = 0;
+            cfg.gridDim = dim3(2 * units, 1, 1);
+            if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess &&
+                clusters > 0)
+                units = std::min(units, clusters);
+            cudaGetLastError();
+        }
+        max_units[dev] = units;
+        configured[dev] = 1;
+    }
+    const int64_t units = std::min<int64_t>(prm.num_tiles, max_units[dev]);
+    cfg.gridDim = dim3((unsigned)(units * CG), 1, 1);
+    TLC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, prm));
+    count_launch();
+    return check_launch("tc_gemm");
+}
+
+// Fills the tile/launch fields of `prm` for a variant and launches it.
+// Pairs (CG = 2) for problems with more than 128 rows; 3xTF32 uses UN = 128
+// so its chunk sums fit in the epilogue's registers.
+int launch_tc(TcParams& prm, const Gemm& g, cudaStream_t s) {
+    const bool x3 = prm.passes == 3;
+    const int cg = g.M > 128 ? 2 : 1;
+    const int un = (!x3 && g.N > 128) ? 256 : 128;
+    prm.m_tiles = (int)((g.M + BM * cg - 1) / (BM * cg));
+    prm.n_tiles = (int)((g.N + un - 1) / un);
+    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
+    if (x3) return cg == 2 ? launch_variant<2, 128, true>(prm, s) : launch_variant<1, 128, true>(prm, s);
+    if (un == 256)
+        return cg == 2 ? launch_variant<2, 256, false>(prm, s) : launch_variant<1, 256, false>(prm, s);
+    return cg == 2 ? launch_variant<2, 128, false>(prm, s) : launch_variant<1, 128, false>(prm, s);
+}
+
+// The parts of TcParams that do not depend on the kernel variant.
+void fill_common(TcParams& prm, const Gemm& g, const OperandMap& A, const OperandMap& B,
+                 bool a_mn, bool b_mn, int passes) {
+    prm.C = g.C;
+    prm.c_rs = g.c_rs;
+    prm.nb = g.nb;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        prm.bsz[i] = i < g.nb ? (int)g.bsz[i] : 1;
+        prm.cbs[i] = i < g.nb ? g.cbs[i] : 0;
+        prm.a_bc[i] = (i < g.nb && A.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+        prm.b_bc[i] = (i < g.nb && B.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+    }
+    prm.M = (int)g.M;
+    prm.N = (int)g.N;
+    prm.K = (int)g.K;
+    prm.k_blocks = (int)((g.K + BK - 1) / BK);
+    prm.passes = passes;
+    // The tensor cores' fp32 accumulation error grows linearly with the
+    // length of the accumulation chain (measured: ~2.4e-9 x K relative,
+    // biased towards zero), which puts long-K 3xTF32 above 1e-5.  3xTF32
+    // therefore restarts the TMEM accumulator every 256 k (8 k-blocks) and
+    // sums the chunks in fp32 round-to-nearest; TF32 keeps one chain.
+    prm.chunk_kb = passes == 3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
+    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
+    prm.a_mn = a_mn ? 1 : 0;
+    prm.b_mn = b_mn ? 1 : 0;
+    prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
+    for (int i = 0; i < g.nb; ++i)
+        if (g.cbs[i] & 3) prm.vec_c = 0;
+    prm.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate wait
+}
+
+// A and B as tensor maps' operand descriptions (memory order: A K-major =
+// {K, M}, M-major = {M, K}; B N-major = {N, K}, K-major = {K, N}).  The box
+// of the outer dim is the tile extent a CTA loads; it is the same for every
+// variant's A (128 rows) and, for B, at most the largest B_COLS (128).
+void operand_maps(const Gemm& g, bool a_mn, bool b_mn, OperandMap& A, OperandMap& B,
+                  uint32_t b_box_cols) {
+    A = OperandMap{};
+    B = OperandMap{};
+    A.base = g.A;
+    A.inner = a_mn ? g.M : g.K;
+    A.outer = a_mn ? g.K : g.M;
+    A.outer_stride = a_mn ? g.a_cs : g.a_rs;
+    B.base = g.B;
+    B.inner = b_mn ? g.N : g.K;
+    B.outer = b_mn ? g.K : g.N;
+    B.outer_stride = b_mn ? g.b_rs : g.b_cs;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        A.bsz[i] = B.bsz[i] = i < g.nb ? g.bsz[i] : 1;
+        A.bstride[i] = i < g.nb ? g.abs_[i] : 0;
+        B.bstride[i] = i < g.nb ? g.bbs[i] : 0;
+    }
+    A.box_inner = B.box_inner = 32;
+    A.box_outer = a_mn ? BK : BM;
+    B.box_outer = b_mn ? BK : b_box_cols;
+    A.mn_major = a_mn;
+    B.mn_major = b_mn;
+}
+
+// B columns a CTA loads per stage for the variant launch_tc will pick.
+uint32_t b_cols_for(const Gemm& g, int passes) {
+    const int cg = g.M > 128 ? 2 : 1;
+    const int un = (passes == 1 && g.N > 128) ? 256 : 128;
+    return (uint32_t)(un / cg);
 }
 
 }  // namespace
@@ -775,34 +990,14 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     if (g.K == 0) return gemm_exact(g, s);  // writes zeros
     if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX)
         return set_error(TLC_ERR_UNSUPPORTED, "tensor-core GEMM: a dimension exceeds 2^31");
+    for (int i = 0; i < g.nb; ++i)
+        if (g.bsz[i] > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "batch dim too large");
 
-    // Operand maps in memory order: A K-major = {K, M}, M-major = {M, K};
-    // B N-major = {N, K}, K-major = {K, N}.
+    const int passes = mode == TLC_MODE_3XTF32 ? 3 : 1;
     const bool a_mn = g.a_cs != 1;  // a_rs == 1
     const bool b_mn = g.b_cs == 1;  // else b_rs == 1
-    OperandMap A{}, B{};
-    A.base = g.A;
-    A.inner = a_mn ? g.M : g.K;
-    A.outer = a_mn ? g.K : g.M;
-    A.outer_stride = a_mn ? g.a_cs : g.a_rs;
-    B.base = g.B;
-    B.inner = b_mn ? g.N : g.K;
-    B.outer = b_mn ? g.K : g.N;
-    B.outer_stride = b_mn ? g.b_rs : g.b_cs;
-    for (int i = 0; i < kMaxBatchDims; ++i) {
-        A.bsz[i] = B.bsz[i] = i < g.nb ? g.bsz[i] : 1;
-        A.bstride[i] = i < g.nb ? g.abs_[i] : 0;
-        B.bstride[i] = i < g.nb ? g.bbs[i] : 0;
-    }
-    const int passes = mode == TLC_MODE_3XTF32 ? 3 : 1;
-    // 3xTF32 runs 128-wide tiles so the epilogue can hold a row of chunk sums.
-    const int BN = (passes == 1 && g.N > 128) ? 256 : 128;
-    A.box_inner = 32;
-    A.box_outer = a_mn ? BK : BM;
-    A.mn_major = a_mn;
-    B.box_inner = 32;
-    B.box_outer = b_mn ? BK : BN;
-    B.mn_major = b_mn;
+    OperandMap A, B;
+    operand_maps(g, a_mn, b_mn, A, B, b_cols_for(g, passes));
 
     TcScratch sc(s);
     if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb)) TLC_TRY(repack(A, g.nb, sc, 0, s));
@@ -834,43 +1029,10 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
         TLC_TRY(encode(&prm.tmA[0], A));
         TLC_TRY(encode(&prm.tmB[0], B));
     }
-
-    prm.C = g.C;
-    prm.c_rs = g.c_rs;
-    prm.nb = g.nb;
-    for (int i = 0; i < kMaxBatchDims; ++i) {
-        prm.bsz[i] = i < g.nb ? (int)g.bsz[i] : 1;
-        prm.cbs[i] = i < g.nb ? g.cbs[i] : 0;
-        prm.a_bc[i] = (i < g.nb && A.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
-        prm.b_bc[i] = (i < g.nb && B.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
-    }
-    prm.M = (int)g.M;
-    prm.N = (int)g.N;
-    prm.K = (int)g.K;
-    prm.m_tiles = (int)((g.M + BM - 1) / BM);
-    prm.n_tiles = (int)((g.N + BN - 1) / BN);
-    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
-    prm.k_blocks = (int)((g.K + BK - 1) / BK);
-    prm.passes = passes;
-    // The tensor cores' fp32 accumulation error grows linearly with the
-    // length of the accumulation chain (measured: ~2.4e-9 x K relative,
-    // biased towards zero), which puts long-K 3xTF32 above 1e-5.  3xTF32
-    // therefore restarts the TMEM accumulator every 256 k (8 k-blocks) and
-    // sums the chunks in fp32 round-to-nearest; TF32 keeps one chain.
-    prm.chunk_kb = passes == 3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
-    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
-    prm.a_mn = a_mn ? 1 : 0;
-    prm.b_mn = b_mn ? 1 : 0;
-    prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
-    for (int i = 0; i < g.nb; ++i)
-        if (g.cbs[i] & 3) prm.vec_c = 0;
-    prm.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate wait
+    fill_common(prm, g, A, B, a_mn, b_mn, passes);
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
-    for (int i = 0; i < g.nb; ++i)
-        if (g.bsz[i] > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "batch dim too large");
-    if (passes == 3) return launch_tc<128, true>(prm, s);
-    return BN == 256 ? launch_tc<256, false>(prm, s) : launch_tc<128, false>(prm, s);
+    return launch_tc(prm, g, s);
 }
 
 int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
@@ -975,25 +1137,8 @@ int gemm_3xtf32_noalloc(const tlc_gemm_desc* d, cudaStream_t s) {
 
     const bool a_mn = g.a_cs != 1;
     const bool b_mn = g.b_cs == 1;
-    OperandMap A{}, B{};
-    A.base = g.A;
-    A.inner = a_mn ? g.M : g.K;
-    A.outer = a_mn ? g.K : g.M;
-    A.outer_stride = a_mn ? g.a_cs : g.a_rs;
-    B.base = g.B;
-    B.inner = b_mn ? g.N : g.K;
-    B.outer = b_mn ? g.K : g.N;
-    B.outer_stride = b_mn ? g.b_rs : g.b_cs;
-    for (int i = 0; i < kMaxBatchDims; ++i) {
-        A.bsz[i] = B.bsz[i] = i < g.nb ? g.bsz[i] : 1;
-        A.bstride[i] = i < g.nb ? g.abs_[i] : 0;
-        B.bstride[i] = i < g.nb ? g.bbs[i] : 0;
-    }
-    A.box_inner = B.box_inner = 32;
-    A.box_outer = a_mn ? BK : BM;
-    B.box_outer = b_mn ? BK : 128;
-    A.mn_major = a_mn;
-    B.mn_major = b_mn;
+    OperandMap A, B;
+    operand_maps(g, a_mn, b_mn, A, B, b_cols_for(g, 3));
     if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb) ||
         !tma_ok(B.base, B.outer_stride, B.bstride, g.nb))
         return set_error(TLC_ERR_UNSUPPORTED,
@@ -1032,35 +1177,10 @@ int gemm_3xtf32_noalloc(const tlc_gemm_desc* d, cudaStream_t s) {
     TLC_TRY(encode(&prm.tmA[1], al));
     TLC_TRY(encode(&prm.tmB[0], bh));
     TLC_TRY(encode(&prm.tmB[1], bl));
-
-    prm.C = g.C;
-    prm.c_rs = g.c_rs;
-    prm.nb = g.nb;
-    for (int i = 0; i < kMaxBatchDims; ++i) {
-        prm.bsz[i] = i < g.nb ? (int)g.bsz[i] : 1;
-        prm.cbs[i] = i < g.nb ? g.cbs[i] : 0;
-        prm.a_bc[i] = (i < g.nb && A.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
-        prm.b_bc[i] = (i < g.nb && B.bstride[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
-    }
-    prm.M = (int)g.M;
-    prm.N = (int)g.N;
-    prm.K = (int)g.K;
-    prm.m_tiles = (int)((g.M + BM - 1) / BM);
-    prm.n_tiles = (int)((g.N + 127) / 128);
-    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
-    prm.k_blocks = (int)((g.K + BK - 1) / BK);
-    prm.passes = 3;
-    prm.chunk_kb = std::min(prm.k_blocks, 8);
-    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
-    prm.a_mn = a_mn ? 1 : 0;
-    prm.b_mn = b_mn ? 1 : 0;
-    prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
-    for (int i = 0; i < g.nb; ++i)
-        if (g.cbs[i] & 3) prm.vec_c = 0;
-    prm.timeout_ns = 2000000000ull;
+    fill_common(prm, g, A, B, a_mn, b_mn, 3);
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
-    return launch_tc<128, true>(prm, s);
+    return launch_tc(prm, g, s);
 }
 
 }  // namespace
