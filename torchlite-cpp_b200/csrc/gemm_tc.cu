@@ -317,26 +317,35 @@ __device__ __forceinline__ void batch_coords(const TcParams& p, int b, int (&idx
     }
 }
 
-// Position of the i-th k-block load of a tile.  The k range is cut into
-// chunks of chunk_kb k-blocks; each chunk runs its passes back to back
-// (pass-major) and is accumulated from zero in its own TMEM accumulator, so
-// no tensor-core accumulation chain is longer than one chunk.
-struct KbPos {
-    int pass, kb;
-    bool first, last;  // first / last load of its chunk
+// Walks the k-block loads of one tile.  The k range is cut into chunks of
+// chunk_kb k-blocks; each chunk runs its passes back to back (pass-major) and
+// is accumulated from zero in its own TMEM accumulator, so no tensor-core
+// accumulation chain is longer than one chunk.  Incremental (no divisions):
+// the MMA thread's per-k-block instruction count bounds the MMA issue rate.
+struct KbIter {
+    int pass = 0, in_chunk = 0, chunk_start = 0, nc = 0;
+    __device__ __forceinline__ void start(const TcParams& p) {
+        pass = 0;
+        in_chunk = 0;
+        chunk_start = 0;
+        nc = min(p.chunk_kb, p.k_blocks);
+    }
+    __device__ __forceinline__ int kb() const { return chunk_start + in_chunk; }
+    __device__ __forceinline__ bool first() const { return pass == 0 && in_chunk == 0; }
+    __device__ __forceinline__ bool last(const TcParams& p) const {
+        return pass == p.passes - 1 && in_chunk == nc - 1;
+    }
+    __device__ __forceinline__ void next(const TcParams& p) {
+        if (++in_chunk == nc) {
+            in_chunk = 0;
+            if (++pass == p.passes) {
+                pass = 0;
+                chunk_start += p.chunk_kb;
+                nc = min(p.chunk_kb, p.k_blocks - chunk_start);
+            }
+        }
+    }
 };
-__device__ __forceinline__ KbPos kb_pos(const TcParams& p, int i) {
-    const int per_chunk = p.passes * p.chunk_kb;
-    const int c = i / per_chunk;
-    const int r = i - c * per_chunk;
-    const int nc = min(p.chunk_kb, p.k_blocks - c * p.chunk_kb);
-    KbPos q;
-    q.pass = r / nc;
-    q.kb = c * p.chunk_kb + (r - q.pass * nc);
-    q.first = r == 0;
-    q.last = r == p.passes * nc - 1;
-    return q;
-}
 
 // Shapes of one kernel variant.  CG: CTAs per MMA (1, or a pair); UN: the
 // MMA's N (tile columns); each CTA holds 128 rows of A, UN / CG columns of B
@@ -423,10 +432,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            // outstanding[s]: parity of a load issued into stage s whose
-            // completion nobody has observed yet (-1: none).
-            int outstanding[STAGES];
-            for (int s = 0; s < STAGES; ++s) outstanding[s] = -1;
+            // Bit s of pend: a load was issued into stage s and nobody has seen
+            // it complete yet; bit s of pend_par: the parity it completes with.
+            uint32_t pend = 0, pend_par = 0;
+            const uint32_t a_chunk_bytes = 32 * BK * 4;
             bool ok = true;
             for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
                 const TileCoord tc = tile_coord(p, t);
@@ -438,38 +447,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                           b2 = p.b_bc[2] ? bi[2] : 0;
                 const int m0 = tc.m * S::TILE_M + (int)rank * BM;       // this CTA's A rows
                 const int n0 = tc.n * UN + (int)rank * S::B_COLS;       // this CTA's B columns
-                for (int kb = 0; kb < total_kb; ++kb) {
+                KbIter it;
+                it.start(p);
+                for (int kb = 0; kb < total_kb; ++kb, it.next(p)) {
                     if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1)) {
                         ok = false;
                         break;
                     }
                     // The stage's previous load was consumed (the MMA that read it finished).
-                    outstanding[stage] = -1;
-                    const KbPos q = kb_pos(p, kb);
-                    const int k0 = q.kb * BK;
+                    pend &= ~(1u << stage);
+                    const int k0 = it.kb() * BK;
                     // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
-                    const int pa = (p.passes > 1 && q.pass == 0) ? 1 : 0;
-                    const int pb = (p.passes > 1 && q.pass == 1) ? 1 : 0;
+                    const int pa = (p.passes > 1 && it.pass == 0) ? 1 : 0;
+                    const int pb = (p.passes > 1 && it.pass == 1) ? 1 : 0;
                     uint8_t* sa = smem + stage * S::STAGE_BYTES;
                     uint8_t* sb = sa + S::A_BYTES;
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
                     if (leader) mbar_expect_tx(&full[stage], S::STAGE_BYTES * CG);
                     if (p.a_mn) {
+#pragma unroll
                         for (int c = 0; c < BM / 32; ++c)
-                            tma_load_5d<CG>(sa + c * (32 * BK * 4), &p.tmA[pa], fb, m0 + 32 * c, k0,
+                            tma_load_5d<CG>(sa + c * a_chunk_bytes, &p.tmA[pa], fb, m0 + 32 * c, k0,
                                             a0, a1, a2);
                     } else {
                         tma_load_5d<CG>(sa, &p.tmA[pa], fb, k0, m0, a0, a1, a2);
                     }
                     if (p.b_mn) {
+#pragma unroll
                         for (int c = 0; c < S::B_COLS / 32; ++c)
-                            tma_load_5d<CG>(sb + c * (32 * BK * 4), &p.tmB[pb], fb, n0 + 32 * c, k0,
+                            tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[pb], fb, n0 + 32 * c, k0,
                                             b0, b1, b2);
                     } else {
                         tma_load_5d<CG>(sb, &p.tmB[pb], fb, k0, n0, b0, b1, b2);
                     }
-                    outstanding[stage] = (int)phase;
+                    pend |= 1u << stage;
+                    pend_par = (pend_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
@@ -480,9 +493,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 // Drain: wait (bounded) for loads still in flight into shared memory
                 // (the leader's full barriers count both CTAs' bytes).
                 for (int s = 0; s < STAGES; ++s) {
-                    if (outstanding[s] < 0) continue;
+                    if (!(pend & (1u << s))) continue;
                     const uint64_t t0 = globaltimer();
-                    while (!mbar_try_wait(&full[s], (uint32_t)outstanding[s]) &&
+                    while (!mbar_try_wait(&full[s], (pend_par >> s) & 1u) &&
                            globaltimer() - t0 < p.timeout_ns) {
                     }
                 }
@@ -498,19 +511,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                                    ((uint32_t)(UN >> 3) << 17) |
                                    ((uint32_t)(S::TILE_M >> 4) << 24);
             const uint32_t chunk = 32 * BK * 4;  // bytes between 32-wide MN chunks
+            // Descriptors of stage 0, k-step 0; a stage / k-step moves only the
+            // start-address field (bits 0-13, address >> 4), so later ones are
+            // one add away.  MN-major: k-step j starts 8 k-rows (1 KB) further;
+            // chunks of 32 MN elements are `chunk` bytes apart (leading
+            // offset), 4-row k groups 512 B apart (stride offset).  K-major:
+            // 32 B further along the 128-byte rows; 8-row atoms 1 KB apart.
+            const uint32_t s0 = smem_u32(smem);
+            const uint64_t a_desc0 = p.a_mn ? smem_desc(s0, chunk, 512, kSw128Atom32)
+                                            : smem_desc(s0, 16, 1024, kSw128);
+            const uint64_t b_desc0 = p.b_mn ? smem_desc(s0 + S::A_BYTES, chunk, 512, kSw128Atom32)
+                                            : smem_desc(s0 + S::A_BYTES, 16, 1024, kSw128);
+            const uint32_t a_step = (p.a_mn ? 1024u : UMMA_K * 4u) >> 4;
+            const uint32_t b_step = (p.b_mn ? 1024u : UMMA_K * 4u) >> 4;
+            // empty[] of this CTA and (pairs) of the peer, as cluster addresses
+            const uint32_t empty_addr = smem_u32(&empty[0]);
+            const uint32_t empty_peer = CG == 2 ? mapa(empty_addr, 1) : 0u;
             int stage = 0;
             uint32_t phase = 0;
-            uint32_t acc_phase[2] = {0, 0};
+            uint32_t acc_ph = 0;  // bit a: phase parity of accumulator a
             int acc = 0;
             bool ok = true;
             bool issued = false;
             for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
                 uint32_t d = 0;
-                for (int kb = 0; kb < total_kb; ++kb) {
-                    const KbPos q = kb_pos(p, kb);
-                    if (q.first) {
+                KbIter it;
+                it.start(p);
+                for (int kb = 0; kb < total_kb; ++kb, it.next(p)) {
+                    const bool first = it.first();
+                    if (first) {
                         // a fresh accumulator for this chunk, once the epilogues drained it
-                        if (!wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, p.timeout_ns,
+                        if (!wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag, p.timeout_ns,
                                           p.err, 2)) {
                             ok = false;
                             break;
@@ -523,35 +554,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + stage * S::STAGE_BYTES);
-                    const uint32_t sb = sa + S::A_BYTES;
+                    const uint32_t soff = (uint32_t)(stage * S::STAGE_BYTES) >> 4;
+                    const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
 #pragma unroll
-                    for (int j = 0; j < BK / UMMA_K; ++j) {
-                        // MN-major: k-step j starts 8 k-rows (1 KB) further; chunks of
-                        // 32 MN elements are `chunk` bytes apart (leading offset), 4-row
-                        // k groups 512 B apart (stride offset).  K-major: 32 B further
-                        // along the 128-byte rows; 8-row atoms 1 KB apart.
-                        const uint64_t ad =
-                            p.a_mn ? smem_desc(sa + j * 1024, chunk, 512, kSw128Atom32)
-                                   : smem_desc(sa + j * UMMA_K * 4, 16, 1024, kSw128);
-                        const uint64_t bd =
-                            p.b_mn ? smem_desc(sb + j * 1024, chunk, 512, kSw128Atom32)
-                                   : smem_desc(sb + j * UMMA_K * 4, 16, 1024, kSw128);
-                        umma_tf32<CG>(d, ad, bd, idesc, (!q.first || j > 0) ? 1u : 0u);
-                    }
+                    for (int j = 0; j < BK / UMMA_K; ++j)
+                        umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
+                                      (!first || j > 0) ? 1u : 0u);
                     issued = true;
                     // free the stage in every CTA once these MMAs finish
-                    umma_commit<CG>(smem_u32(&empty[stage]));
-                    if constexpr (CG == 2) umma_commit<CG>(mapa(smem_u32(&empty[stage]), 1));
+                    umma_commit<CG>(empty_addr + 8u * stage);
+                    if constexpr (CG == 2) umma_commit<CG>(empty_peer + 8u * stage);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
-                    if (q.last) {
+                    if (it.last(p)) {
                         // chunk accumulator ready for the epilogues of both CTAs
                         umma_commit<CG>(smem_u32(&tfull[acc]));
                         if constexpr (CG == 2) umma_commit<CG>(mapa(smem_u32(&tfull[acc]), 1));
-                        acc_phase[acc] ^= 1;
+                        acc_ph ^= 1u << acc;
                         acc ^= 1;
                     }
                 }
@@ -568,9 +589,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         // ---------------- epilogue (warps 2..5, both CTAs) ----------------
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
-        const uint32_t tempty_leader[2] = {CG == 2 ? mapa(smem_u32(&tempty[0]), 0) : 0u,
-                                           CG == 2 ? mapa(smem_u32(&tempty[1]), 0) : 0u};
-        uint32_t acc_phase[2] = {0, 0};
+        const uint32_t tempty_leader = CG == 2 ? mapa(smem_u32(&tempty[0]), 0) : 0u;
+        uint32_t acc_ph = 0;  // bit a: phase parity of accumulator a
         int acc = 0;
         bool ok = true;
         for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
@@ -588,7 +608,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             for (int j = 0; j < (CHUNKED ? UN : 1); ++j) sum[j] = 0.0f;
             for (int ch = 0; ch < p.num_chunks; ++ch) {
                 if (lane == 0)
-                    ok = wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, p.timeout_ns, p.err, 4);
+                    ok = wait_bounded(&tfull[acc], (acc_ph >> acc) & 1u, abort_flag, p.timeout_ns, p.err, 4);
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // one branch per warp
                 if (!ok) break;
                 tc_fence_after();
@@ -632,11 +652,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 __syncwarp();
                 if (lane == 0) {
                     if (CG == 2 && !leader)
-                        mbar_arrive_remote(tempty_leader[acc]);
+                        mbar_arrive_remote(tempty_leader + 8u * acc);
                     else
                         mbar_arrive(&tempty[acc]);
                 }
-                acc_phase[acc] ^= 1;
+                acc_ph ^= 1u << acc;
                 acc ^= 1;
             }
             if constexpr (CHUNKED) {
