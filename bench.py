@@ -6,18 +6,25 @@
 For N > 1 launch one process per GPU with torch.distributed.run.  Prints ONE
 JSON line on rank 0.
 
-Workload (default "batched"): per GPU the batched GEMM
+Default workload "batched": per GPU the batched GEMM
 C[64,2048,2048] = A[64,2048,2048] . B[64,2048,2048], fp32 row-major,
-A, B ~ U[-1,1] (seed 4), the batch-sharded case of the scaling sweep: rank r
-owns its own 64 batch entries (weak scaling: the job at N GPUs is the
-batch-sharded GEMM of 64*N entries, no data-path collective).  A step is one
-call of tl::matmul's GEMM over that batch; each operand is 1 GiB, larger than
-the 126 MB L2, so no flush is needed between steps.
+A, B ~ U[-1,1] (seed 4), the batch-sharded case of the scaling sweep: each
+rank owns 64 batch entries of its own (weak scaling: the job at N GPUs is the
+batch-sharded GEMM of 64*N entries; no data-path collective).  Square
+workloads (square4096/8192/16384) are column-block sharded at N > 1 (strong
+scaling: every rank holds A and B, computes C[:, its block]; the NCCL
+all-gather that assembles C on every rank is timed separately as
+`gather_ms`).  linear / attention / broadcast time the other configurations
+(forward + backward where they have one) for reference.
 
-Metric: GEMM TFLOP/s = 2*batch*M*N*K / time, whole job.  `value` times the
-device-resident call (CUDA events on the launching stream, max over ranks);
-`e2e` times tlc_matmul_host (the host-buffer C entry point): page-locked host
-A, B in, host C out, copies inside the timed region.
+A step is one call of the GEMM entry point over the workload; every operand is
+at least 64 MiB and the batched operands are 1 GiB, above the 126 MB L2,
+so no flush runs between steps.
+
+Metric: GEMM TFLOP/s = useful FLOPs / time (2*batch*M*N*K per GEMM), whole
+job.  `value` times the device-resident call (CUDA events on the launching
+stream, max over ranks); `e2e` times tlc_matmul_host, the host-buffer C entry
+point: page-locked host A, B in, host C out, copies inside the timed region.
 """
 from __future__ import annotations
 
@@ -34,14 +41,15 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(REPO, "torchlite-cpp_b200")
 sys.path.insert(0, PKG)
 
-WORKLOADS = {
-    # name: (batch, M, N, K)
+# name: (batch, M, N, K) for the plain GEMM workloads
+GEMMS = {
     "batched": (64, 2048, 2048, 2048),
-    "square8192": (1, 8192, 8192, 8192),
     "square4096": (1, 4096, 4096, 4096),
+    "square8192": (1, 8192, 8192, 8192),
     "square16384": (1, 16384, 16384, 16384),
     "square512": (1, 512, 512, 512),
 }
+OTHER = ("linear", "attention", "broadcast")
 METRIC = "GEMM TFLOP/s (fp32-exact, TF32, 3xTF32) at 1/2/4/8 B200, % of peak"
 
 
@@ -54,7 +62,7 @@ def load_peaks():
 
 
 def peak_for(mode, peaks, src, sms, clock_mhz):
-    """Roofline denominator for a mode."""
+    """Roofline denominator (TFLOP/s) for a mode, with where it comes from."""
     if mode == "exact":
         # FP32 FFMA: 128 lanes x 2 FLOP per SM per clock at the max SM clock.
         # MEASURED_PEAKS.json has no FP32 figure, so this one is nominal.
@@ -81,8 +89,9 @@ class ClockSampler:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # let the sampler start before the timed region
         except OSError:
             self.proc = None
         return self
@@ -108,8 +117,15 @@ class ClockSampler:
         os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": max_mhz_default, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+        pw = [v for v in (num(r[3]) for r in rows) if v is not None]
         reasons = set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -118,6 +134,7 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else max_mhz_default,
+                "power_w_max": max(pw) if pw else None,
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
@@ -126,14 +143,12 @@ def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     if world > 1:
         import datetime
         import torch.distributed as dist
-        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
     return world, rank, local
 
 
@@ -153,20 +168,11 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
-def make_inputs(wl, rank, device):
-    import torch
-    batch, M, N, K = WORKLOADS[wl]
-    g = torch.Generator(device=device).manual_seed(4 + 1000 * rank)
-    shp_a = (batch, M, K) if batch > 1 else (M, K)
-    shp_b = (batch, K, N) if batch > 1 else (K, N)
-    A = torch.rand(shp_a, generator=g, device=device, dtype=torch.float32) * 2 - 1
-    B = torch.rand(shp_b, generator=g, device=device, dtype=torch.float32) * 2 - 1
-    return A, B
-
-
-def time_device(fn, steps, warmup, world, stream):
+def time_device(fn, steps, warmup, world, stream, count=None):
     """Per-step device time (ms): W warm-ups, then K steps between CUDA events
-    on `stream`, bracketed by barrier + synchronize; max over ranks."""
+    on `stream`, bracketed by barrier + synchronize; max over ranks.  With
+    `count` (a function returning a launch counter) also returns the number of
+    launches inside the timed region."""
     import torch
     for _ in range(warmup):
         fn()
@@ -174,39 +180,242 @@ def time_device(fn, steps, warmup, world, stream):
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = count() if count else 0
     e0.record(stream)
     for _ in range(steps):
         fn()
     e1.record(stream)
     torch.cuda.synchronize()
+    l1 = count() if count else 0
     barrier(world)
     ms = e0.elapsed_time(e1) / steps
-    return max_over_ranks(ms, world)
+    return max_over_ranks(ms, world), l1 - l0
 
 
-def cpu_reference_sample(wl, reps=3):
-    """The reference's own tl::matmul (oracle/_ref, compiled from its sources)
-    on a bounded sample of the workload: one 2048^3 batch entry (or a 256-row
-    slab of a square GEMM), min over reps (time_best, bench/bench_matmul.cpp:27-39)."""
+# ---- workloads -------------------------------------------------------------------------
+
+class Work:
+    """One workload on one rank: step(mode) runs it once; flops = useful FLOPs
+    of one step on this rank; job_flops = of the whole job."""
+    name = ""
+    scaling = "weak"
+    config = {}
+    flops = 0.0
+    job_flops = 0.0
+
+    def step(self, mode):
+        raise NotImplementedError
+
+
+class GemmWork(Work):
+    def __init__(self, name, world, rank, device):
+        import torch
+        import tldist
+        batch, M, N, K = GEMMS[name]
+        self.name = name
+        self.batch, self.M, self.N, self.K = batch, M, N, K
+        if batch > 1:
+            # batch-sharded, weak: every rank owns `batch` entries of its own
+            g = torch.Generator(device=device).manual_seed(4 + 1000 * rank)
+            self.A = torch.rand((batch, M, K), generator=g, device=device) * 2 - 1
+            self.B = torch.rand((batch, K, N), generator=g, device=device) * 2 - 1
+            self.C = torch.empty((batch, M, N), device=device)
+            self.Bv = self.B
+            self.scaling = "weak"
+            self.flops = 2.0 * batch * M * N * K
+            self.job_flops = self.flops * world
+            par = f"batch-sharded x{world}" if world > 1 else "single GPU"
+        else:
+            # column-block sharded, strong: same A, B on every rank
+            g = torch.Generator(device=device).manual_seed(4)
+            self.A = torch.rand((M, K), generator=g, device=device) * 2 - 1
+            self.B = torch.rand((K, N), generator=g, device=device) * 2 - 1
+            self.edges = tldist.col_blocks(N, world, 256)
+            c0, c1 = self.edges[rank], self.edges[rank + 1]
+            self.Bv = self.B[:, c0:c1]  # read in place, row stride N
+            self.C = torch.empty((M, c1 - c0), device=device)
+            self.scaling = "strong" if world > 1 else "weak"
+            self.flops = 2.0 * M * (c1 - c0) * K
+            self.job_flops = 2.0 * M * N * K
+            par = f"output-column-block sharded x{world}" if world > 1 else "single GPU"
+        self.config = {"workload": name, "batch_per_gpu": batch,
+                       "global_batch": batch * world if batch > 1 else 1,
+                       "M": M, "N": N, "K": K, "layout": "row-major A, B, C",
+                       "parallelism": par,
+                       "l2": "operands larger than L2 (126 MB), no flush"}
+
+    def step(self, mode):
+        import tlcuda
+        tlcuda.matmul(self.A, self.Bv, mode=mode, out=self.C)
+
+    def gather_ms(self, world, stream, iters=5):
+        """Square workloads at N > 1: the all-gather + reassembly of C."""
+        if self.batch > 1 or world == 1:
+            return None
+        import torch
+        import torch.distributed as dist
+        import tlcuda
+        M, N = self.M, self.N
+        w = self.edges[1] - self.edges[0]
+        if any(self.edges[q + 1] - self.edges[q] != w for q in range(world)):
+            return None
+        gathered = torch.empty((world * M * w,), device=self.C.device)
+        out = torch.empty((M, N), device=self.C.device)
+
+        def fn():
+            dist.all_gather_into_tensor(gathered, self.C.reshape(-1))
+            tlcuda.gather_colblocks(gathered, out, M, N, self.edges)
+        ms, _ = time_device(fn, iters, 2, world, stream)
+        return ms
+
+    def e2e(self, mode, stream):
+        """tlc_matmul_host on page-locked host buffers (this rank's share)."""
+        import torch
+        import tlcuda
+        ha = torch.empty(self.A.shape, dtype=torch.float32, pin_memory=True)
+        hb = torch.empty(self.Bv.shape, dtype=torch.float32, pin_memory=True)
+        hc = torch.empty(self.C.shape, dtype=torch.float32, pin_memory=True)
+        ha.copy_(self.A)
+        hb.copy_(self.Bv)
+
+        def fn():
+            tlcuda.matmul_host(ha, hb, mode=mode, out=hc, stream=stream)
+        return fn, int((ha.numel() + hb.numel()) * 4), int(hc.numel() * 4), (ha, hb, hc)
+
+
+class LinearWork(Work):
+    """Y = X.W^T + b fwd + bwd: X[4096,1024] ~ N(0,1), W[4096,1024] ~ U(-1/32,1/32),
+    dY ~ N(0,1); the GEMMs Y = X.W^T, dX = dY.W, dW^T = X^T.dY (bias: not a GEMM)."""
+    name = "linear"
+
+    def __init__(self, world, rank, device):
+        import torch
+        g = torch.Generator(device=device).manual_seed(2)
+        self.X = torch.randn((4096, 1024), generator=g, device=device)
+        self.W = (torch.rand((4096, 1024), generator=g, device=device) * 2 - 1) / 32
+        self.dY = torch.randn((4096, 4096), generator=g, device=device)
+        self.Y = torch.empty((4096, 4096), device=device)
+        self.dX = torch.empty((4096, 1024), device=device)
+        self.dWt = torch.empty((1024, 4096), device=device)
+        self.flops = 3 * 2.0 * 4096 * 4096 * 1024
+        self.job_flops = self.flops * world
+        self.config = {"workload": "linear", "X": [4096, 1024], "W": [4096, 1024],
+                       "gemms": "Y=X.W^T, dX=dY.W, dW^T=X^T.dY", "parallelism": "replicas"}
+
+    def step(self, mode):
+        import tlcuda
+        tlcuda.matmul(self.X, self.W.t(), mode=mode, out=self.Y)
+        tlcuda.matmul_backward(self.dY, self.X, self.W.t(), mode=mode, da=self.dX, db=self.dWt)
+
+
+class AttentionWork(Work):
+    """Encoder attention GEMMs: batch 16, seq 512, d_model 768, 12 heads of 64:
+    QKV [8192,768].[768,2304], scores [192,512,64].[192,64,512] (K^T read in
+    place), context [192,512,512].[192,512,64], out-proj [8192,768].[768,768];
+    activations ~ N(0,1), weights ~ N(0,0.02), softmax(scores/8) (computed once
+    at set-up with torch, not timed) feeds the context GEMM."""
+    name = "attention"
+
+    def __init__(self, world, rank, device):
+        import torch
+        import tlcuda
+        g = torch.Generator(device=device).manual_seed(3)
+        self.x = torch.randn((8192, 768), generator=g, device=device)
+        self.Wqkv = torch.randn((768, 2304), generator=g, device=device) * 0.02
+        self.Wo = torch.randn((768, 768), generator=g, device=device) * 0.02
+        self.q = torch.randn((192, 512, 64), generator=g, device=device)
+        self.k = torch.randn((192, 512, 64), generator=g, device=device)
+        self.v = torch.randn((192, 512, 64), generator=g, device=device)
+        s = tlcuda.matmul(self.q, self.k.transpose(1, 2), mode="exact")
+        self.P = torch.softmax(s / 8.0, dim=-1)
+        self.qkv = torch.empty((8192, 2304), device=device)
+        self.sc = torch.empty((192, 512, 512), device=device)
+        self.ctx = torch.empty((192, 512, 64), device=device)
+        self.o = torch.empty((8192, 768), device=device)
+        self.flops = 2.0 * (8192 * 768 * 2304 + 2 * 192 * 512 * 512 * 64 + 8192 * 768 * 768)
+        self.job_flops = self.flops * world
+        self.config = {"workload": "attention", "batch": 16, "seq": 512, "d_model": 768,
+                       "heads": 12, "parallelism": "replicas"}
+
+    def step(self, mode):
+        import tlcuda
+        tlcuda.matmul(self.x, self.Wqkv, mode=mode, out=self.qkv)
+        tlcuda.matmul(self.q, self.k.transpose(1, 2), mode=mode, out=self.sc)
+        tlcuda.matmul(self.P, self.v, mode=mode, out=self.ctx)
+        tlcuda.matmul(self.x, self.Wo, mode=mode, out=self.o)
+
+
+class BroadcastWork(Work):
+    """A[32,128,64] . B[64,128] (B broadcast) fwd + MatmulBackward, N(0,1) seed 1."""
+    name = "broadcast"
+
+    def __init__(self, world, rank, device):
+        import torch
+        g = torch.Generator(device=device).manual_seed(1)
+        self.A = torch.randn((32, 128, 64), generator=g, device=device)
+        self.B = torch.randn((64, 128), generator=g, device=device)
+        self.dC = torch.randn((32, 128, 128), generator=g, device=device)
+        self.C = torch.empty((32, 128, 128), device=device)
+        self.dA = torch.empty_like(self.A)
+        self.dB = torch.empty_like(self.B)
+        self.flops = 3 * 2.0 * 32 * 128 * 128 * 64
+        self.job_flops = self.flops * world
+        self.config = {"workload": "broadcast", "A": [32, 128, 64], "B": [64, 128],
+                       "parallelism": "replicas"}
+
+    def step(self, mode):
+        import tlcuda
+        tlcuda.matmul(self.A, self.B, mode=mode, out=self.C)
+        tlcuda.matmul_backward(self.dC, self.A, self.B, mode=mode, da=self.dA, db=self.dB)
+
+
+def make_work(name, world, rank, device):
+    if name in GEMMS:
+        return GemmWork(name, world, rank, device)
+    return {"linear": LinearWork, "attention": AttentionWork,
+            "broadcast": BroadcastWork}[name](world, rank, device)
+
+
+# ---- the reference's CPU path ----------------------------------------------------------
+
+def ref_sample(name):
+    """A bounded sample of the workload for the reference CPU matmul:
+    (a, b, useful FLOPs, description)."""
     import numpy as np
+    rng = np.random.default_rng(4)
+    if name in GEMMS:
+        batch, M, N, K = GEMMS[name]
+        rows = M if batch > 1 else min(M, 256)
+        what = "one batch entry" if batch > 1 else f"a {rows}-row slab"
+    elif name == "linear":
+        rows, K, N = 256, 1024, 4096
+        what = "a 256-row slab of Y = X.W^T"
+    elif name == "attention":
+        rows, K, N = 256, 768, 2304
+        what = "a 256-row slab of the QKV projection"
+    else:
+        rows, K, N = 128, 64, 128
+        what = "one batch entry of the broadcast forward"
+    a = rng.uniform(-1, 1, (rows, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    return a, b, 2.0 * rows * N * K, f"tl::matmul [{rows},{K}]x[{K},{N}] fp32, {what} of the workload"
+
+
+def cpu_reference_sample(name, reps=3):
+    """The reference's own tl::matmul (oracle/_ref, compiled from its sources),
+    min over reps (time_best, bench/bench_matmul.cpp:27-39)."""
     sys.path.insert(0, REPO)
     from oracle import oracle as O
     R = O.tlref()
-    batch, M, N, K = WORKLOADS[wl]
-    rows = M if batch > 1 else min(M, 256)
-    rng = np.random.default_rng(4)
-    a = rng.uniform(-1, 1, (rows, K)).astype(np.float32)
-    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    a, b, flops, what = ref_sample(name)
     best = float("inf")
     for _ in range(reps):
         t0 = time.perf_counter()
         R.matmul(a, b)
         best = min(best, time.perf_counter() - t0)
-    flops = 2.0 * rows * N * K
     return {"value": flops / best / 1e12, "unit": "TFLOP/s", "cores": R.hardware_threads(),
             "kind": "reference",
-            "sample": f"tl::matmul [{rows},{K}]x[{K},{N}] fp32 "
-                      f"({flops / 1e9:.1f} GFLOP), best of {reps}, "
+            "sample": f"{what} ({flops / 1e9:.2f} GFLOP), best of {reps}, "
                       f"{os.path.basename(R.path)} with std::thread::hardware_concurrency() threads"}
 
 
@@ -215,8 +424,6 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    wl = args.workload
-    import numpy as np
     sys.path.insert(0, REPO)
     from oracle import oracle as O
     try:
@@ -224,28 +431,23 @@ def run_reference_arm(args):
     except FileNotFoundError as e:
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not built: {e}"}))
         return 0
-    batch, M, N, K = WORKLOADS[wl]
-    rows = M if batch > 1 else min(M, 256)
-    rng = np.random.default_rng(4)
-    a = rng.uniform(-1, 1, (rows, K)).astype(np.float32)
-    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    a, b, flops, what = ref_sample(args.workload)
     for _ in range(args.warmup):
         R.matmul(a, b)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         R.matmul(a, b)
     dt = (time.perf_counter() - t0) / args.steps
-    flops = 2.0 * rows * N * K
     val = flops / dt / 1e12
-    sample = (f"each step: reference tl::matmul on [{rows},{K}]x[{K},{N}] fp32 "
-              f"({flops / 1e9:.1f} GFLOP), one {'batch entry' if batch > 1 else 'row slab'} "
-              f"of the workload, host wall clock")
+    sample = f"each step: {what} ({flops / 1e9:.2f} GFLOP), host wall clock"
+    cfg = {"workload": args.workload}
+    if args.workload in GEMMS:
+        batch, M, N, K = GEMMS[args.workload]
+        cfg.update({"batch": batch, "M": M, "N": N, "K": K, "sampled_rows": a.shape[0]})
     line = {"metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic U[-1,1] seed 4", "impl": "reference",
-            "config": {"workload": wl, "batch": batch, "M": M, "N": N, "K": K,
-                       "sampled_rows": rows},
+            "data": "synthetic U[-1,1] seed 4", "impl": "reference", "config": cfg,
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": R.hardware_threads(),
                              "kind": "reference", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -269,11 +471,7 @@ def run_ours(args):
     import tlcuda
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
-    wl = args.workload
-    batch, M, N, K = WORKLOADS[wl]
-    flops = 2.0 * batch * M * N * K
-    A, B = make_inputs(wl, rank, device)
-    C = torch.empty((batch, M, N) if batch > 1 else (M, N), device=device, dtype=torch.float32)
+    work = make_work(args.workload, world, rank, device)
     stream = torch.cuda.current_stream()
     modes = [args.mode] + [m for m in ("tf32", "3xtf32", "exact") if m != args.mode and args.all_modes]
     peaks, psrc = load_peaks()
@@ -283,52 +481,49 @@ def run_ours(args):
     launches = None
     clocks = None
     for mode in modes:
-        fn = lambda: tlcuda.matmul(A, B, mode=mode, out=C)  # noqa: E731
+        fn = lambda: work.step(mode)  # noqa: E731
         if mode == args.mode:
-            l0 = tlcuda.launch_count()
             with ClockSampler(local) as cs:
-                ms = time_device(fn, args.steps, args.warmup, world, stream)
+                ms, launches = time_device(fn, args.steps, args.warmup, world, stream,
+                                           tlcuda.launch_count)
             clocks = cs.summary(peaks.get("sm_max_mhz", 1965.0))
-            launches = (tlcuda.launch_count() - l0)
-            launches = launches * args.steps // (args.steps + args.warmup)
         else:
-            ms = time_device(fn, max(3, args.steps // 2), 3, world, stream)
+            ms, _ = time_device(fn, max(3, args.steps // 2), 3, world, stream)
         peak, pdesc = peak_for(mode, peaks, psrc, sms, peaks.get("sm_max_mhz", 1965.0))
-        per_gpu = flops / (ms * 1e-3) / 1e12
+        per_gpu = work.flops / (ms * 1e-3) / 1e12
         results[mode] = {"ms_per_step": ms, "tflops_per_gpu": per_gpu,
-                         "value": per_gpu * world, "roofline_frac": per_gpu / peak,
-                         "peak_tflops": peak, "peak_source": pdesc}
+                         "value": work.job_flops / (ms * 1e-3) / 1e12,
+                         "roofline_frac": per_gpu / peak, "peak_tflops": peak,
+                         "peak_source": pdesc}
 
     head = results[args.mode]
-    peak = head["peak_tflops"]
-    roofline = {"bound": "hbm" if False else "tensor", "achieved": head["tflops_per_gpu"],
-                "peak": peak, "unit": "TFLOP/s", "frac": head["tflops_per_gpu"] / peak,
-                "traffic": traffic_for(args.mode, wl), "peak_source": head["peak_source"],
-                "kernel_ms": head["ms_per_step"],
-                "algorithmic_flop_per_launch": flops}
+    roofline = {"bound": "tensor" if args.mode != "exact" else "fp32-fma",
+                "achieved": head["tflops_per_gpu"], "peak": head["peak_tflops"],
+                "unit": "TFLOP/s", "frac": head["roofline_frac"],
+                "traffic": traffic_for(args.mode, args.workload),
+                "peak_source": head["peak_source"], "kernel_ms": head["ms_per_step"],
+                "algorithmic_flop_per_launch": work.flops}
+
+    gather = work.gather_ms(world, stream) if isinstance(work, GemmWork) else None
 
     # End to end through the host-buffer C entry point (page-locked host memory).
     e2e = None
-    if not args.no_e2e:
-        ha = torch.empty(A.shape, dtype=torch.float32, pin_memory=True)
-        hb = torch.empty(B.shape, dtype=torch.float32, pin_memory=True)
-        hc = torch.empty(C.shape, dtype=torch.float32, pin_memory=True)
-        ha.copy_(A)
-        hb.copy_(B)
-        es = torch.cuda.Stream(device)
-        fn = lambda: tlcuda.matmul_host(ha, hb, mode=args.mode, out=hc, stream=es)  # noqa: E731
-        e_steps = max(3, min(args.steps, 10))
-        ms_e2e = time_device(fn, e_steps, 2, world, es)
-        e2e = {"value": flops * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": int((A.numel() + B.numel()) * 4),
-               "d2h_bytes_per_step": int(C.numel() * 4), "ms_per_step": ms_e2e,
-               "api": "tlc_matmul_host"}
-        del ha, hb, hc
+    if not args.no_e2e and isinstance(work, GemmWork):
+        try:
+            es = torch.cuda.Stream(device)
+            fn, hbytes, dbytes, keep = work.e2e(args.mode, es)
+            ms_e2e, _ = time_device(fn, max(3, min(args.steps, 10)), 2, world, es)
+            e2e = {"value": work.job_flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                   "h2d_bytes_per_step": hbytes, "d2h_bytes_per_step": dbytes,
+                   "ms_per_step": ms_e2e, "api": "tlc_matmul_host"}
+            del keep
+        except Exception as e:  # e.g. not enough page-locked host memory
+            e2e = {"value": None, "unavailable": repr(e)[:200]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_reference_sample(wl)
+            cpu = cpu_reference_sample(args.workload)
         except Exception as e:  # the oracle/_ref build is optional on a user's host
             cpu = {"value": None, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {e}"}
@@ -337,20 +532,13 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": head["value"], "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic U[-1,1], torch.Generator seed 4 + 1000*rank",
-            "mode": args.mode,
-            "config": {"workload": wl, "batch_per_gpu": batch, "global_batch": batch * world,
-                       "M": M, "N": N, "K": K, "layout": "row-major A, B, C",
-                       "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (1 GiB per operand), no flush"},
-            "roofline": roofline,
-            "modes": results,
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": launches,
-            "clocks": clocks,
+            "higher_is_better": True, "scaling": work.scaling, "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic, seeded torch.Generator (see config)",
+            "mode": args.mode, "config": work.config, "roofline": roofline, "modes": results,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
         }
+        if gather is not None:
+            line["gather_ms"] = gather
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist
@@ -366,7 +554,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--mode", default=os.environ.get("TL_BENCH_MODE", "tf32"),
                     choices=["exact", "tf32", "3xtf32"])
-    ap.add_argument("--workload", default="batched", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="batched", choices=sorted(GEMMS) + list(OTHER))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--all-modes", dest="all_modes", action="store_true", default=True)
     ap.add_argument("--head-only", dest="all_modes", action="store_false")
