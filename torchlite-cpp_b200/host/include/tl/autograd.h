@@ -1,0 +1,78 @@
+// Autograd for the matmul path (include/tl/autograd.h of torchlite-cpp):
+// the same GradFunction / track<> protocol, with MatmulBackward running
+// libtl_cuda's backward (dA = dC.B^T, dB = A^T.dC reduced with sum_to) on the
+// GPU, transposed operands read in place.
+#pragma once
+
+#include <tl/tensor.h>
+
+#include <cstdint>
+#include <initializer_list>
+#include <memory>
+#include <vector>
+
+namespace tl {
+
+inline bool& grad_enabled() {
+    static bool e = true;
+    return e;
+}
+
+struct NoGradGuard {
+    bool prev;
+    NoGradGuard() : prev(grad_enabled()) { grad_enabled() = false; }
+    ~NoGradGuard() { grad_enabled() = prev; }
+};
+
+class GradFunction {
+  public:
+    virtual ~GradFunction() = default;
+    virtual void backward(const Tensor& grad_output) = 0;
+    std::vector<Tensor> inputs;
+};
+
+// src/autograd.cpp:341-384
+class MatmulBackward : public GradFunction {
+  public:
+    Tensor a_cache, b_cache;  // the inputs as given (views; no contiguous copies)
+    bool squeeze_a = false, squeeze_b = false;
+    int mode = -1;
+    void backward(const Tensor& grad_output) override;
+};
+
+// src/autograd.cpp:131-133
+class TransposeBackward : public GradFunction {
+  public:
+    int64_t dim0 = 0, dim1 = 0;
+    void backward(const Tensor& grad_output) override;
+};
+
+class ReshapeBackward : public GradFunction {
+  public:
+    std::vector<int64_t> input_shape;
+    void backward(const Tensor& grad_output) override;
+};
+
+class AddBackward : public GradFunction {
+  public:
+    void backward(const Tensor& grad_output) override;
+};
+
+// grad += d (grad = zeros + d when empty), src/autograd.cpp:16-22
+void accumulate_grad(Tensor& t, const Tensor& grad);
+
+template <typename BackwardFn>
+std::shared_ptr<BackwardFn> track(Tensor& out, std::initializer_list<const Tensor*> inputs) {
+    if (!grad_enabled()) return nullptr;
+    out.requires_grad = true;
+    out.ensure_grad();
+    auto fn = std::make_shared<BackwardFn>();
+    for (auto* t : inputs) {
+        const_cast<Tensor*>(t)->ensure_grad();
+        fn->inputs.push_back(*const_cast<Tensor*>(t));  // shallow copy, shared grad_
+    }
+    out.grad_fn = fn;
+    return fn;
+}
+
+}  // namespace tl

@@ -1,0 +1,88 @@
+// Backward functions of the matmul path (src/autograd.cpp of torchlite-cpp).
+#include <tl/autograd.h>
+#include <tl/ops.h>
+
+#include <tlc.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace tl {
+
+namespace {
+
+void check(int status, const char* what) {
+    if (status == TLC_OK) return;
+    if (status == TLC_ERR_INVALID_ARGUMENT) throw std::invalid_argument(tlc_last_error());
+    throw std::runtime_error(std::string(what) + ": " + tlc_last_error());
+}
+
+tlc_tensor dview(const Tensor& t) {
+    tlc_tensor v{};
+    v.ndim = static_cast<int32_t>(t.sizes().size());
+    for (int i = 0; i < v.ndim; ++i) {
+        v.sizes[i] = t.sizes()[i];
+        v.strides[i] = t.strides()[i];
+    }
+    v.data = t.numel() > 0 ? const_cast<float*>(t.device_data()) : nullptr;
+    return v;
+}
+
+}  // namespace
+
+// src/autograd.cpp:16-22: the first gradient is zeros + d, later ones add.
+void accumulate_grad(Tensor& t, const Tensor& grad) {
+    if (!t.requires_grad) return;
+    if (t.grad().empty()) {
+        Tensor z = Tensor::device_empty(t.sizes());  // zeros, made on the device
+        if (z.numel() > 0)
+            check(tlc_memset_zero(z.device_data(), sizeof(float) * z.numel(), nullptr),
+                  "tlc_memset_zero");
+        t.grad() = add(z, grad);
+    } else {
+        t.grad() = add(t.grad(), grad);
+    }
+}
+
+// src/autograd.cpp:341-384: dA = sum_to(dC.B^T, A.shape), dB = sum_to(A^T.dC,
+// B.shape), 1-D operands unsqueezed and squeezed back; both products and the
+// sum_to reductions run in libtl_cuda (tlc_matmul_backward), which reads the
+// transposed operands in place.  A gradient nobody requires is not computed.
+void MatmulBackward::backward(const Tensor& grad_output) {
+    const bool want_a = inputs[0].requires_grad, want_b = inputs[1].requires_grad;
+    if (!want_a && !want_b) return;
+    tlc_tensor g = dview(grad_output), a = dview(a_cache), b = dview(b_cache);
+    Tensor da, db;
+    tlc_tensor vda{}, vdb{};
+    if (want_a) {
+        da = Tensor::device_empty(a_cache.sizes());
+        vda = dview(da);
+        if (!vda.data) vda.data = reinterpret_cast<float*>(16);  // empty: nothing is written
+    }
+    if (want_b) {
+        db = Tensor::device_empty(b_cache.sizes());
+        vdb = dview(db);
+        if (!vdb.data) vdb.data = reinterpret_cast<float*>(16);
+    }
+    check(tlc_matmul_backward(&g, &a, &b, want_a ? &vda : nullptr, want_b ? &vdb : nullptr, 0,
+                              mode, nullptr),
+          "tlc_matmul_backward");
+    if (want_a) accumulate_grad(inputs[0], da);
+    if (want_b) accumulate_grad(inputs[1], db);
+}
+
+// src/autograd.cpp:131-133
+void TransposeBackward::backward(const Tensor& grad_output) {
+    accumulate_grad(inputs[0], transpose(grad_output, dim0, dim1));
+}
+
+void ReshapeBackward::backward(const Tensor& grad_output) {
+    accumulate_grad(inputs[0], reshape(grad_output, input_shape));
+}
+
+void AddBackward::backward(const Tensor& grad_output) {
+    accumulate_grad(inputs[0], grad_output);
+    accumulate_grad(inputs[1], grad_output);
+}
+
+}  // namespace tl

@@ -1,0 +1,181 @@
+// tl:: ops of the matmul path over libtl_cuda (include/tlc.h).  Shapes, views
+// and error messages follow src/ops.cpp of torchlite-cpp; the arithmetic runs
+// on the GPU.
+#include <tl/autograd.h>
+#include <tl/ops.h>
+
+#include <tlc.h>
+
+#include <new>
+#include <stdexcept>
+#include <string>
+
+namespace tl {
+
+namespace {
+
+void check(int status, const char* what) {
+    if (status == TLC_OK) return;
+    if (status == TLC_ERR_INVALID_ARGUMENT) throw std::invalid_argument(tlc_last_error());
+    if (status == TLC_ERR_OUT_OF_MEMORY) throw std::bad_alloc();
+    throw std::runtime_error(std::string(what) + ": " + tlc_last_error());
+}
+
+// The C-ABI view of a tensor; `device` picks the device copy as data pointer.
+tlc_tensor view_of(const Tensor& t, bool device) {
+    tlc_tensor v{};
+    if (t.sizes().size() > TLC_MAX_DIMS) throw std::invalid_argument("matmul: more than 8 dims");
+    v.ndim = static_cast<int32_t>(t.sizes().size());
+    for (int i = 0; i < v.ndim; ++i) {
+        v.sizes[i] = t.sizes()[i];
+        v.strides[i] = t.strides()[i];
+    }
+    v.data = device && t.numel() > 0 ? const_cast<float*>(t.device_data()) : nullptr;
+    return v;
+}
+
+}  // namespace
+
+Tensor matmul(const Tensor& a_in, const Tensor& b_in) {
+    return matmul(a_in, b_in, TLC_MODE_DEFAULT);
+}
+
+// src/ops.cpp:605-699
+Tensor matmul(const Tensor& a_in, const Tensor& b_in, int mode) {
+    // shape rules and their exceptions first; they need no GPU
+    tlc_tensor va = view_of(a_in, false), vb = view_of(b_in, false);
+    int32_t nd = 0;
+    int64_t sz[TLC_MAX_DIMS];
+    check(tlc_matmul_shape(&va, &vb, &nd, sz), "tlc_matmul_shape");
+    Tensor out = Tensor::device_empty(std::vector<int64_t>(sz, sz + nd));
+    if (out.numel() > 0) {
+        va = view_of(a_in, true);
+        vb = view_of(b_in, true);
+        tlc_tensor vo = view_of(out, false);
+        vo.data = out.device_data();
+        check(tlc_matmul(&va, &vb, &vo, mode, nullptr), "tlc_matmul");
+    }
+    if (a_in.requires_grad || b_in.requires_grad) {
+        if (auto fn = track<MatmulBackward>(out, {&a_in, &b_in})) {
+            fn->a_cache = a_in;  // views are read in place: no contiguous copies
+            fn->b_cache = b_in;
+            fn->squeeze_a = a_in.sizes().size() == 1;
+            fn->squeeze_b = b_in.sizes().size() == 1;
+            fn->mode = mode;
+        }
+    }
+    return out;
+}
+
+// src/ops.cpp:702-730
+Tensor transpose(const Tensor& a, int64_t dim0, int64_t dim1) {
+    const int64_t ndim = static_cast<int64_t>(a.sizes().size());
+    if (dim0 < 0) dim0 += ndim;
+    if (dim1 < 0) dim1 += ndim;
+    if (dim0 < 0 || dim0 >= ndim || dim1 < 0 || dim1 >= ndim)
+        throw std::invalid_argument("tranpose: dimension out of range");
+    auto sizes = a.sizes();
+    auto strides = a.strides();
+    std::swap(sizes[dim0], sizes[dim1]);
+    std::swap(strides[dim0], strides[dim1]);
+    Tensor out = a.view(sizes, strides, a.storage_offset());
+    if (a.requires_grad) {
+        if (auto fn = track<TransposeBackward>(out, {&a})) {
+            fn->dim0 = dim0;
+            fn->dim1 = dim1;
+        }
+    }
+    return out;
+}
+
+// src/ops.cpp:732-767
+Tensor reshape(const Tensor& a, const std::vector<int64_t>& new_sizes) {
+    int64_t n = 1;
+    for (int64_t s : new_sizes) {
+        if (s < 0) throw std::invalid_argument("reshape: negative dims not allowed");
+        n *= s;
+    }
+    if (n != a.numel())
+        throw std::invalid_argument("reshape: new shape must have same number of elements");
+    Tensor c = a.is_contiguous() ? a : a.contiguous();
+    std::vector<int64_t> st(new_sizes.size());
+    int64_t s = 1;
+    for (int i = static_cast<int>(new_sizes.size()) - 1; i >= 0; --i) {
+        st[i] = s;
+        s *= new_sizes[i];
+    }
+    Tensor out = c.view(new_sizes, st, c.storage_offset());
+    if (a.requires_grad) {
+        if (auto fn = track<ReshapeBackward>(out, {&a})) fn->input_shape = a.sizes();
+    }
+    return out;
+}
+
+Tensor unsqueeze(const Tensor& input, int64_t dim) {
+    const int64_t nd = static_cast<int64_t>(input.sizes().size());
+    if (dim < 0) dim += nd + 1;
+    if (dim < 0 || dim > nd) throw std::invalid_argument("unsqueeze: dim out of range");
+    auto s = input.sizes();
+    s.insert(s.begin() + dim, 1);
+    return reshape(input, s);
+}
+
+Tensor squeeze(const Tensor& input, int64_t dim) {
+    const int64_t nd = static_cast<int64_t>(input.sizes().size());
+    if (dim < 0) dim += nd;
+    if (dim < 0 || dim >= nd) throw std::invalid_argument("squeeze: dim out of range");
+    if (input.sizes()[dim] != 1) throw std::invalid_argument("squeeze: dim is not size 1");
+    if (nd == 1) throw std::invalid_argument("squeeze: cannot squeeze 1D to 0D");
+    auto s = input.sizes();
+    s.erase(s.begin() + dim);
+    return reshape(input, s);
+}
+
+Tensor add(const Tensor& a_in, const Tensor& b_in) {
+    if (a_in.sizes() != b_in.sizes())
+        throw std::invalid_argument("add: shapes must match (broadcasting add is not on the GPU path)");
+    Tensor a = a_in.contiguous(), b = b_in.contiguous();
+    Tensor out = Tensor::device_empty(a.sizes());
+    if (out.numel() > 0)
+        check(tlc_add(a.device_data(), b.device_data(), out.device_data(), out.numel(), nullptr),
+              "tlc_add");
+    if (a_in.requires_grad || b_in.requires_grad) track<AddBackward>(out, {&a_in, &b_in});
+    return out;
+}
+
+Tensor sum(const Tensor& input, int64_t dim, bool keepdim) {
+    Tensor a = input.contiguous();
+    const auto& sizes = a.sizes();
+    const int64_t nd = static_cast<int64_t>(sizes.size());
+    if (dim < 0) dim += nd;
+    if (dim < 0 || dim >= nd) throw std::invalid_argument("sum: dimension out of range");
+    std::vector<int64_t> out_sizes;
+    int64_t outer = 1, inner = 1;
+    for (int64_t i = 0; i < nd; ++i) {
+        if (i == dim) {
+            if (keepdim) out_sizes.push_back(1);
+        } else {
+            out_sizes.push_back(sizes[i]);
+        }
+        if (i < dim) outer *= sizes[i];
+        if (i > dim) inner *= sizes[i];
+    }
+    Tensor out = Tensor::device_empty(out_sizes);
+    if (out.numel() > 0)
+        check(tlc_sum_dim(a.device_data(), out.device_data(), outer, sizes[dim], inner, nullptr),
+              "tlc_sum_dim");
+    return out;
+}
+
+Tensor zeros(const std::vector<int64_t>& sizes) { return Tensor(sizes); }
+
+Tensor full(const std::vector<int64_t>& sizes, float value) {
+    Tensor t(sizes);
+    float* p = t.data();
+    for (int64_t i = 0; i < t.numel(); ++i) p[i] = value;
+    return t;
+}
+
+Tensor ones(const std::vector<int64_t>& sizes) { return full(sizes, 1.0f); }
+
+}  // namespace tl
