@@ -44,6 +44,9 @@ sys.path.insert(0, PKG)
 # name: (batch, M, N, K) for the plain GEMM workloads
 GEMMS = {
     "batched": (64, 2048, 2048, 2048),
+    # 8 entries of the same shape (384 MiB of operands): the profiling stand-in
+    # for "batched", whose DRAM traffic per launch is 8x this one's
+    "batched8": (8, 2048, 2048, 2048),
     "square4096": (1, 4096, 4096, 4096),
     "square8192": (1, 8192, 8192, 8192),
     "square16384": (1, 16384, 16384, 16384),
