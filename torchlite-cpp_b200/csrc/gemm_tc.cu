@@ -335,6 +335,10 @@ struct KbIter {
     __device__ __forceinline__ bool last(const TcParams& p) const {
         return pass == p.passes - 1 && in_chunk == nc - 1;
     }
+    // k-block loads left in the current chunk (this one included)
+    __device__ __forceinline__ int left_in_chunk(const TcParams& p) const {
+        return (p.passes - pass - 1) * nc + (nc - in_chunk);
+    }
     __device__ __forceinline__ void next(const TcParams& p) {
         if (++in_chunk == nc) {
             in_chunk = 0;
@@ -355,7 +359,11 @@ struct Cfg {
     static constexpr int B_COLS = UN / CG;
     static constexpr int A_BYTES = BM * BK * 4;      // 16 KB
     static constexpr int B_BYTES = B_COLS * BK * 4;  // 4 KB per 32 columns
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int KB_BYTES = A_BYTES + B_BYTES;  // one k-block: [A | B]
+    // k-blocks per stage: one full-barrier wait and one commit serve SUBS
+    // k-blocks (the MMA thread's per-stage handshake costs as much as ~1 MMA)
+    static constexpr int SUBS = KB_BYTES <= 32 * 1024 ? 2 : 1;
+    static constexpr int STAGE_BYTES = SUBS * KB_BYTES;
     static constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
     static constexpr int TMEM_COLS = 2 * UN;
     static constexpr int TILE_M = BM * CG;
@@ -449,37 +457,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 const int n0 = tc.n * UN + (int)rank * S::B_COLS;       // this CTA's B columns
                 KbIter it;
                 it.start(p);
-                for (int kb = 0; kb < total_kb; ++kb, it.next(p)) {
+                for (int kb = 0; kb < total_kb;) {
                     if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1)) {
                         ok = false;
                         break;
                     }
                     // The stage's previous load was consumed (the MMA that read it finished).
                     pend &= ~(1u << stage);
-                    const int k0 = it.kb() * BK;
-                    // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
-                    const int pa = (p.passes > 1 && it.pass == 0) ? 1 : 0;
-                    const int pb = (p.passes > 1 && it.pass == 1) ? 1 : 0;
-                    uint8_t* sa = smem + stage * S::STAGE_BYTES;
-                    uint8_t* sb = sa + S::A_BYTES;
+                    // up to SUBS k-blocks of one accumulation chunk share the stage
+                    const int nsub = min(S::SUBS, it.left_in_chunk(p));
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
-                    if (leader) mbar_expect_tx(&full[stage], S::STAGE_BYTES * CG);
-                    if (p.a_mn) {
+                    if (leader) mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
+                    for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
+                        const int k0 = it.kb() * BK;
+                        // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
+                        const int pa = (p.passes > 1 && it.pass == 0) ? 1 : 0;
+                        const int pb = (p.passes > 1 && it.pass == 1) ? 1 : 0;
+                        uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES;
+                        uint8_t* sb = sa + S::A_BYTES;
+                        if (p.a_mn) {
 #pragma unroll
-                        for (int c = 0; c < BM / 32; ++c)
-                            tma_load_5d<CG>(sa + c * a_chunk_bytes, &p.tmA[pa], fb, m0 + 32 * c, k0,
-                                            a0, a1, a2);
-                    } else {
-                        tma_load_5d<CG>(sa, &p.tmA[pa], fb, k0, m0, a0, a1, a2);
-                    }
-                    if (p.b_mn) {
+                            for (int c = 0; c < BM / 32; ++c)
+                                tma_load_5d<CG>(sa + c * a_chunk_bytes, &p.tmA[pa], fb, m0 + 32 * c,
+                                                k0, a0, a1, a2);
+                        } else {
+                            tma_load_5d<CG>(sa, &p.tmA[pa], fb, k0, m0, a0, a1, a2);
+                        }
+                        if (p.b_mn) {
 #pragma unroll
-                        for (int c = 0; c < S::B_COLS / 32; ++c)
-                            tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[pb], fb, n0 + 32 * c, k0,
-                                            b0, b1, b2);
-                    } else {
-                        tma_load_5d<CG>(sb, &p.tmB[pb], fb, k0, n0, b0, b1, b2);
+                            for (int c = 0; c < S::B_COLS / 32; ++c)
+                                tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[pb], fb, n0 + 32 * c,
+                                                k0, b0, b1, b2);
+                        } else {
+                            tma_load_5d<CG>(sb, &p.tmB[pb], fb, k0, n0, b0, b1, b2);
+                        }
                     }
                     pend |= 1u << stage;
                     pend_par = (pend_par & ~(1u << stage)) | (phase << stage);
@@ -537,12 +549,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 uint32_t d = 0;
                 KbIter it;
                 it.start(p);
-                for (int kb = 0; kb < total_kb; ++kb, it.next(p)) {
-                    const bool first = it.first();
-                    if (first) {
+                for (int kb = 0; kb < total_kb;) {
+                    // the stage holds up to SUBS k-blocks of one chunk (as loaded)
+                    const int nsub = min(S::SUBS, it.left_in_chunk(p));
+                    if (it.first()) {
                         // a fresh accumulator for this chunk, once the epilogues drained it
-                        if (!wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag, p.timeout_ns,
-                                          p.err, 2)) {
+                        if (!wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag,
+                                          p.timeout_ns, p.err, 2)) {
                             ok = false;
                             break;
                         }
@@ -554,12 +567,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t soff = (uint32_t)(stage * S::STAGE_BYTES) >> 4;
-                    const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
+                    bool chunk_end = false;
+                    for (int s = 0; s < nsub; ++s, ++kb, it.next(p)) {
+                        const bool first = it.first();
+                        chunk_end = it.last(p);
+                        const uint32_t soff =
+                            (uint32_t)(stage * S::STAGE_BYTES + s * S::KB_BYTES) >> 4;
+                        const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
 #pragma unroll
-                    for (int j = 0; j < BK / UMMA_K; ++j)
-                        umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
-                                      (!first || j > 0) ? 1u : 0u);
+                        for (int j = 0; j < BK / UMMA_K; ++j)
+                            umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
+                                          (!first || j > 0) ? 1u : 0u);
+                    }
                     issued = true;
                     // free the stage in every CTA once these MMAs finish
                     umma_commit<CG>(empty_addr + 8u * stage);
@@ -568,7 +587,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                         stage = 0;
                         phase ^= 1;
                     }
-                    if (it.last(p)) {
+                    if (chunk_end) {
                         // chunk accumulator ready for the epilogues of both CTAs
                         umma_commit<CG>(smem_u32(&tfull[acc]));
                         if constexpr (CG == 2) umma_commit<CG>(mapa(smem_u32(&tfull[acc]), 1));
