@@ -263,6 +263,16 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
             "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
             : "memory");
 }
+// CTA pairs: one commit that arrives on the barrier at this shared offset in
+// both CTAs of the pair (a commit, not a load: no data crosses CTAs).
+__device__ __forceinline__ void umma_commit_both(uint32_t bar_local) {
+    const uint16_t both = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(bar_local),
+        "h"(both)
+        : "memory");
+}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -536,9 +546,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                                             : smem_desc(s0 + S::A_BYTES, 16, 1024, kSw128);
             const uint32_t a_step = (p.a_mn ? 1024u : UMMA_K * 4u) >> 4;
             const uint32_t b_step = (p.b_mn ? 1024u : UMMA_K * 4u) >> 4;
-            // empty[] of this CTA and (pairs) of the peer, as cluster addresses
             const uint32_t empty_addr = smem_u32(&empty[0]);
-            const uint32_t empty_peer = CG == 2 ? mapa(empty_addr, 1) : 0u;
             int stage = 0;
             uint32_t phase = 0;
             uint32_t acc_ph = 0;  // bit a: phase parity of accumulator a
@@ -581,16 +589,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     }
                     issued = true;
                     // free the stage in every CTA once these MMAs finish
-                    umma_commit<CG>(empty_addr + 8u * stage);
-                    if constexpr (CG == 2) umma_commit<CG>(empty_peer + 8u * stage);
+                    if constexpr (CG == 2)
+                        umma_commit_both(empty_addr + 8u * stage);
+                    else
+                        umma_commit<CG>(empty_addr + 8u * stage);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                     if (chunk_end) {
                         // chunk accumulator ready for the epilogues of both CTAs
-                        umma_commit<CG>(smem_u32(&tfull[acc]));
-                        if constexpr (CG == 2) umma_commit<CG>(mapa(smem_u32(&tfull[acc]), 1));
+                        if constexpr (CG == 2)
+                            umma_commit_both(smem_u32(&tfull[acc]));
+                        else
+                            umma_commit<CG>(smem_u32(&tfull[acc]));
                         acc_ph ^= 1u << acc;
                         acc ^= 1;
                     }
