@@ -203,3 +203,27 @@ def test_full_size_batched_sampled():
         assert bits_equal(host(C[bi, ::256]), O.gemm2d(a, b))
     del A, B, C, C2
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("shape_a,shape_b", [
+    ((40, 512, 512), (40, 512, 512)),    # chunks of batch entries
+    ((32, 1024, 512), (512, 256)),       # batch chunks, B shared by every entry
+    ((4100, 2048), (2048, 2048)),        # one GEMM: chunks of 256 rows of A and C
+])
+@pytest.mark.parametrize("pinned", [False, True])
+def test_host_buffer_pipelined(shape_a, shape_b, pinned):
+    """Problems above 64 MB go through the chunked upload / GEMM / download
+    pipeline; the result must equal the device-resident call bit for bit."""
+    g = torch.Generator(device=DEV).manual_seed(31)
+    A = torch.rand(shape_a, generator=g, device=DEV) * 2 - 1
+    B = torch.rand(shape_b, generator=g, device=DEV) * 2 - 1
+    ref = host(tlcuda.matmul(A, B))
+    ha, hb = A.cpu(), B.cpu()
+    if pinned:
+        ha, hb = ha.pin_memory(), hb.pin_memory()
+    out = torch.empty(ref.shape, dtype=torch.float32, pin_memory=pinned)
+    tlcuda.matmul_host(ha, hb, out=out)
+    assert bits_equal(out.numpy(), ref)
+    got = tlcuda.matmul_host(ha, hb, mode="tf32")
+    denom = np.linalg.norm(ref.astype(np.float64))
+    assert np.linalg.norm(got.astype(np.float64) - ref) / denom <= 1e-2

@@ -523,6 +523,157 @@ cudaStream_t host_stream() {
     return streams[dev];
 }
 
+// Upload and download streams per device for the pipelined host-buffer form.
+void copy_streams(cudaStream_t& in, cudaStream_t& out) {
+    static std::mutex mu;
+    static cudaStream_t s_in[64] = {}, s_out[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) {
+        in = out = nullptr;
+        return;
+    }
+    if (!s_in[dev]) cudaStreamCreateWithFlags(&s_in[dev], cudaStreamNonBlocking);
+    if (!s_out[dev]) cudaStreamCreateWithFlags(&s_out[dev], cudaStreamNonBlocking);
+    in = s_in[dev];
+    out = s_out[dev];
+}
+
+View dense_view(float* data, std::initializer_list<int64_t> sizes) {
+    return contiguous_view(data, std::vector<int64_t>(sizes));
+}
+
+// Events of one pipelined call, destroyed with it.
+struct Events {
+    std::vector<cudaEvent_t> ev;
+    cudaEvent_t make() {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        ev.push_back(e);
+        return e;
+    }
+    ~Events() {
+        for (auto e : ev) cudaEventDestroy(e);
+    }
+};
+
+constexpr int64_t kPipeMinBytes = 64ll << 20;  // smaller problems: one upload, one download
+constexpr int kPipeChunks = 8;
+
+// Host-buffer matmul with the transfers pipelined against the GEMMs: the
+// output is cut into chunks, along the flattened batch when every operand is
+// either batched like the output or one shared matrix, else along the rows of
+// A and C; chunk i's upload (stream `in`), GEMM (stream `s`) and download
+// (stream `out`) overlap with its neighbours', so the host link's two
+// directions and the GEMM run at once.  Operands and result must be dense
+// host buffers; returns TLC_ERR_UNSUPPORTED otherwise (the caller then takes
+// the sequential path).  Chunking does not change any element's arithmetic.
+int matmul_host_pipelined(const Plan& p, const View& ha, const View& hb, float* out_host, int mode,
+                          cudaStream_t s) {
+    if (!ha.contiguous() || !hb.contiguous()) return TLC_ERR_UNSUPPORTED;
+    const int64_t M = p.M, N = p.N, K = p.K;
+    const int64_t nbatch = prod(p.batch_out);
+    const int64_t bytes = 4 * (ha.numel() + hb.numel() + prod(p.full_out));
+    if (bytes < kPipeMinBytes || K == 0 || M == 0 || N == 0) return TLC_ERR_UNSUPPORTED;
+    auto batched_like_out = [&](const View& v) {
+        if (v.nd - 2 != (int)p.batch_out.size()) return false;
+        for (int i = 0; i < v.nd - 2; ++i)
+            if (v.sz[i] != p.batch_out[i]) return false;
+        return true;
+    };
+    auto plain = [&](const View& v) {
+        int64_t bp = 1;
+        for (int i = 0; i < v.nd - 2; ++i) bp *= v.sz[i];
+        return bp == 1;
+    };
+    const bool by_batch = nbatch >= 2 && (batched_like_out(p.a) || plain(p.a)) &&
+                          (batched_like_out(p.b) || plain(p.b));
+    const bool by_rows = nbatch == 1 && M >= 2 * 256;
+    if (!by_batch && !by_rows) return TLC_ERR_UNSUPPORTED;
+    const bool a_batched = by_batch && !plain(p.a), b_batched = by_batch && !plain(p.b);
+
+    cudaStream_t in = nullptr, out = nullptr;
+    copy_streams(in, out);
+    if (!in || !out) return TLC_ERR_UNSUPPORTED;
+    Scratch dA(s), dB(s), dC(s);
+    TLC_TRY(dA.alloc(sizeof(float) * ha.numel()));
+    TLC_TRY(dB.alloc(sizeof(float) * hb.numel()));
+    TLC_TRY(dC.alloc(sizeof(float) * prod(p.full_out)));
+    Events E;
+    cudaEvent_t ready = E.make();
+    if (!ready) return set_error(TLC_ERR_CUDA, "cudaEventCreate failed");
+    TLC_CUDA_TRY(cudaEventRecord(ready, s));  // the allocations precede every copy
+    TLC_CUDA_TRY(cudaStreamWaitEvent(in, ready, 0));
+    TLC_CUDA_TRY(cudaStreamWaitEvent(out, ready, 0));
+    // shared operands go up whole, first
+    if (!a_batched && !by_rows)
+        TLC_CUDA_TRY(cudaMemcpyAsync(dA.p, ha.data, sizeof(float) * ha.numel(), cudaMemcpyHostToDevice, in));
+    if (!b_batched)
+        TLC_CUDA_TRY(cudaMemcpyAsync(dB.p, hb.data, sizeof(float) * hb.numel(), cudaMemcpyHostToDevice, in));
+
+    const int64_t units = by_batch ? nbatch : (M + 255) / 256;  // batch entries or 256-row blocks
+    const int64_t chunks = std::min<int64_t>(kPipeChunks, units);
+    for (int64_t c = 0; c < chunks; ++c) {
+        int64_t u0, u1;
+        tlc_shard_range(units, (int)chunks, (int)c, &u0, &u1);
+        if (u1 <= u0) continue;
+        View a, b, o;
+        int64_t a_off = 0, a_n = 0, b_off = 0, b_n = 0, o_off, o_n;
+        if (by_batch) {
+            const int64_t cnt = u1 - u0;
+            if (a_batched) {
+                a_off = u0 * M * K;
+                a_n = cnt * M * K;
+                a = dense_view(dA.f() + a_off, {cnt, M, K});
+            } else {
+                a = dense_view(dA.f(), {M, K});
+            }
+            if (b_batched) {
+                b_off = u0 * K * N;
+                b_n = cnt * K * N;
+                b = dense_view(dB.f() + b_off, {cnt, K, N});
+            } else {
+                b = dense_view(dB.f(), {K, N});
+            }
+            o_off = u0 * M * N;
+            o_n = cnt * M * N;
+            o = dense_view(dC.f() + o_off, {cnt, M, N});
+        } else {
+            const int64_t r0 = u0 * 256, r1 = std::min(M, u1 * 256);
+            a_off = r0 * K;
+            a_n = (r1 - r0) * K;
+            a = dense_view(dA.f() + a_off, {r1 - r0, K});
+            b = dense_view(dB.f(), {K, N});
+            o_off = r0 * N;
+            o_n = (r1 - r0) * N;
+            o = dense_view(dC.f() + o_off, {r1 - r0, N});
+        }
+        if (a_n)
+            TLC_CUDA_TRY(cudaMemcpyAsync(dA.f() + a_off, ha.data + a_off, sizeof(float) * a_n,
+                                         cudaMemcpyHostToDevice, in));
+        if (b_n)
+            TLC_CUDA_TRY(cudaMemcpyAsync(dB.f() + b_off, hb.data + b_off, sizeof(float) * b_n,
+                                         cudaMemcpyHostToDevice, in));
+        cudaEvent_t up = E.make(), done = E.make();
+        if (!up || !done) return set_error(TLC_ERR_CUDA, "cudaEventCreate failed");
+        TLC_CUDA_TRY(cudaEventRecord(up, in));
+        TLC_CUDA_TRY(cudaStreamWaitEvent(s, up, 0));
+        Plan q;
+        TLC_TRY(plan_matmul(a, b, q));
+        TLC_TRY(matmul_planned(q, const_cast<float*>(o.data), mode, s));
+        TLC_CUDA_TRY(cudaEventRecord(done, s));
+        TLC_CUDA_TRY(cudaStreamWaitEvent(out, done, 0));
+        TLC_CUDA_TRY(cudaMemcpyAsync(out_host + o_off, o.data, sizeof(float) * o_n,
+                                     cudaMemcpyDeviceToHost, out));
+    }
+    cudaEvent_t drained = E.make();
+    if (!drained) return set_error(TLC_ERR_CUDA, "cudaEventCreate failed");
+    TLC_CUDA_TRY(cudaEventRecord(drained, out));
+    TLC_CUDA_TRY(cudaStreamWaitEvent(s, drained, 0));  // frees (on s) follow the downloads
+    return TLC_OK;
+}
+
 }  // namespace
 }  // namespace tlc
 
@@ -744,6 +895,15 @@ int tlc_matmul_host(const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out, i
     TLC_TRY(plan_matmul(va, vb, p));
     TLC_TRY(check_out(out, p.result, "out"));
     cudaStream_t s = stream ? (cudaStream_t)stream : host_stream();
+    {
+        const int st = matmul_host_pipelined(p, va, vb, out->data, m, s);
+        if (st == TLC_OK) {
+            TLC_CUDA_TRY(cudaStreamSynchronize(s));
+            return take_device_error();
+        }
+        if (st != TLC_ERR_UNSUPPORTED) return st;
+        clear_error();
+    }
     {
         DevCopy da(s), db(s), dc(s);
         TLC_TRY(da.up(a, s));
