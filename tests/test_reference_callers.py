@@ -1,0 +1,75 @@
+"""The reference library's own callers of tl::matmul on the GPU path.
+
+oracle/_ref/ref_callers_{v3,v4} is linked from the reference's objects
+(nn::Linear, MultiHeadAttention, MatmulBackward and the ops they use, compiled
+from the reference's sources) with tl::matmul redirected by the linker to
+torchlite-cpp_b200/integration/reference_matmul_gpu.cpp, which runs every
+product through libtl_cuda's host-buffer entry point.  The driver program
+(tests/integration/ref_callers_main.cpp) runs Linear forward/backward on 2-D
+and batched inputs, MultiHeadAttention forward/backward, a broadcast batched
+matmul and an X.W^T product on seeded inputs and writes every output and
+gradient as float32.
+
+With TLC_REFERENCE_MATMUL=1 the same binary calls the reference's own CPU
+matmul, so the two runs differ only in where the products are computed.
+Exact mode must give identical bits (the reference's src/ops.cpp:605-699
+matmul and src/autograd.cpp:341-384 backward, unmodified callers in
+src/nn.cpp:77-83 and src/nn.cpp:401-445); TF32 and 3xTF32 are held to
+relative Frobenius errors of 1e-2 and 1e-5 over the whole output.
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_DIR = os.path.join(ROOT, "oracle", "_ref")
+
+
+def _binary():
+    flags = O._cpu_flags()
+    v4 = {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= flags
+    path = os.path.join(REF_DIR, "ref_callers_v4" if v4 else "ref_callers_v3")
+    if not os.path.exists(path):
+        pytest.skip(f"{os.path.basename(path)} not built (needs the reference sources)")
+    return path
+
+
+def _run(tmp_path, name, env_extra):
+    out = tmp_path / f"{name}.bin"
+    env = dict(os.environ)
+    env.pop("TLC_REFERENCE_MATMUL", None)
+    env.update(env_extra)
+    r = subprocess.run([_binary(), str(out)], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    fields = r.stdout.split()
+    launches = int(fields[fields.index("launches") + 1])
+    return np.fromfile(out, dtype=np.float32), launches
+
+
+def test_reference_callers_cpu_run(tmp_path):
+    """The linked binary loads and runs its CPU arm without a GPU."""
+    y, launches = _run(tmp_path, "cpu", {"TLC_REFERENCE_MATMUL": "1"})
+    assert launches == 0
+    assert y.size == 213015 and np.isfinite(y).all() and np.abs(y).max() > 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode,tol", [("exact", 0.0), ("tf32", 1e-2), ("3xtf32", 1e-5)])
+def test_reference_callers_on_gpu(tmp_path, mode, tol):
+    ref, n0 = _run(tmp_path, "cpu", {"TLC_REFERENCE_MATMUL": "1"})
+    got, n1 = _run(tmp_path, mode, {"TL_GEMM_MODE": mode})
+    assert n0 == 0
+    assert n1 > 0, "no kernel of libtl_cuda ran: the matmuls did not reach the GPU"
+    assert got.shape == ref.shape
+    if tol == 0.0:
+        assert got.tobytes() == ref.tobytes(), (
+            f"{int((got.view(np.uint32) != ref.view(np.uint32)).sum())} floats differ")
+    else:
+        d = got.astype(np.float64) - ref
+        rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
+        assert rel <= tol, rel
