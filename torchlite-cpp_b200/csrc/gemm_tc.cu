@@ -1,16 +1,17 @@
 // Tensor-core GEMM for TLC_MODE_TF32 and TLC_MODE_3XTF32 on sm_100a (tcgen05).
 //
-// Persistent, warp-specialised kernel; 6 warps per CTA:
+// Persistent, warp-specialised kernel; 6 warps per CTA (10 for 3xTF32):
 //   warp 0      TMA producer: one elected thread streams A and B k-blocks
 //               (32 fp32 = 128 bytes of k) into a ring of shared-memory stages
 //               with cp.async.bulk.tensor (128-byte swizzle), completion
 //               tracked by an mbarrier per stage (expect_tx bytes).
 //   warp 1      TMEM allocation; one elected thread of the leader CTA issues
-//               tcgen05.mma.kind::tf32 (K = 8 per instruction, 4 per k-block)
-//               into an fp32 accumulator in tensor memory; tcgen05.commit
-//               frees each stage and publishes each finished accumulator.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (each thread one row of
-//               128), store fp32 C.
+//               tcgen05.mma.kind::tf32 (K = 8 per instruction, 4 per k-block
+//               and product) into an fp32 accumulator in tensor memory;
+//               tcgen05.commit frees each stage and publishes each finished
+//               accumulator.
+//   warps 2..   epilogue: tcgen05.ld the accumulator (each thread one row of
+//               128; with 8 epilogue warps, half a row), store fp32 C.
 // The accumulator is double-buffered in TMEM, so the epilogue of one tile
 // overlaps the main loop of the next.
 //
@@ -39,11 +40,14 @@
 // 3xTF32 (Ootomo & Yokota, "Recovering single precision accuracy from Tensor
 // Cores while surpassing the FP32 theoretical peak performance", 2022): each
 // operand x is split as hi = round_to_tf32(x), lo = x - hi (exact in fp32) by
-// a pre-pass; the main loop then accumulates lo(A).hi(B) + hi(A).lo(B) +
-// hi(A).hi(B) in TMEM.  Because the tensor cores' fp32 accumulation error
-// grows with the chain length, 3xTF32 accumulates each 256-wide k chunk from
-// zero in its own (double-buffered) TMEM accumulator and the epilogue adds the
-// chunk results in fp32 round-to-nearest registers.
+// a pre-pass.  A stage holds hi and lo tiles of A and B for a k-block, and the
+// MMA thread issues lo(A).hi(B), hi(A).lo(B) and hi(A).hi(B) from them, so
+// each tile is loaded once for three products (12 MMAs per stage handshake).
+// Because the tensor cores' fp32 accumulation error grows with the chain
+// length, 3xTF32 accumulates each 256-wide k chunk from zero in its own
+// (double-buffered) TMEM accumulator and the epilogue adds the chunk results
+// in fp32 round-to-nearest registers: 8 epilogue warps, two per TMEM lane
+// quarter, each holding half of a 256-column row.
 //
 // Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
 // waiting thread raises a CTA-wide abort flag and a device error word, every
@@ -67,7 +71,6 @@ namespace {
 constexpr int BM = 128;        // rows of A (and of D) per CTA
 constexpr int BK = 32;         // k per stage: 32 fp32 = one 128-byte swizzle row
 constexpr int UMMA_K = 8;      // k per tcgen05.mma.kind::tf32
-constexpr int NUM_THREADS = 192;
 
 struct TcParams {
     CUtensorMap tmA[2];  // [0] A (TF32) or hi(A) (3xTF32); [1] lo(A)
@@ -82,8 +85,7 @@ struct TcParams {
     int M, N, K;
     int m_tiles, n_tiles;
     int64_t num_tiles;
-    int k_blocks;     // per pass
-    int passes;       // 1 (TF32) or 3 (3xTF32)
+    int k_blocks;
     int chunk_kb;     // k-blocks per accumulation chunk (== k_blocks: one chunk)
     int num_chunks;
     int a_mn, b_mn;   // 1: operand is MN-major in memory
@@ -287,6 +289,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[31])
         : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -327,69 +338,71 @@ __device__ __forceinline__ void batch_coords(const TcParams& p, int b, int (&idx
     }
 }
 
-// Walks the k-block loads of one tile.  The k range is cut into chunks of
-// chunk_kb k-blocks; each chunk runs its passes back to back (pass-major) and
-// is accumulated from zero in its own TMEM accumulator, so no tensor-core
-// accumulation chain is longer than one chunk.  Incremental (no divisions):
-// the MMA thread's per-k-block instruction count bounds the MMA issue rate.
+// Walks the k-blocks of one tile in accumulation chunks of chunk_kb k-blocks.
+// Each chunk is accumulated from zero in its own TMEM accumulator, so no
+// tensor-core accumulation chain is longer than one chunk (TF32: one chunk
+// per tile).  Incremental (no divisions): the MMA thread's per-k-block
+// instruction count bounds the MMA issue rate.
 struct KbIter {
-    int pass = 0, in_chunk = 0, chunk_start = 0, nc = 0;
+    int in_chunk = 0, chunk_start = 0, nc = 0;
     __device__ __forceinline__ void start(const TcParams& p) {
-        pass = 0;
         in_chunk = 0;
         chunk_start = 0;
         nc = min(p.chunk_kb, p.k_blocks);
     }
     __device__ __forceinline__ int kb() const { return chunk_start + in_chunk; }
-    __device__ __forceinline__ bool first() const { return pass == 0 && in_chunk == 0; }
-    __device__ __forceinline__ bool last(const TcParams& p) const {
-        return pass == p.passes - 1 && in_chunk == nc - 1;
-    }
-    // k-block loads left in the current chunk (this one included)
-    __device__ __forceinline__ int left_in_chunk(const TcParams& p) const {
-        return (p.passes - pass - 1) * nc + (nc - in_chunk);
-    }
+    __device__ __forceinline__ bool first() const { return in_chunk == 0; }
+    __device__ __forceinline__ bool last() const { return in_chunk == nc - 1; }
+    // k-blocks left in the current chunk (this one included)
+    __device__ __forceinline__ int left_in_chunk() const { return nc - in_chunk; }
     __device__ __forceinline__ void next(const TcParams& p) {
         if (++in_chunk == nc) {
             in_chunk = 0;
-            if (++pass == p.passes) {
-                pass = 0;
-                chunk_start += p.chunk_kb;
-                nc = min(p.chunk_kb, p.k_blocks - chunk_start);
-            }
+            chunk_start += p.chunk_kb;
+            nc = min(p.chunk_kb, p.k_blocks - chunk_start);
         }
     }
 };
 
 // Shapes of one kernel variant.  CG: CTAs per MMA (1, or a pair); UN: the
-// MMA's N (tile columns); each CTA holds 128 rows of A, UN / CG columns of B
-// and a 128 x UN fp32 accumulator (twice, double-buffered).
-template <int CG, int UN>
+// MMA's N (tile columns); X3: 3xTF32.  Per k-block each CTA holds 128 rows of
+// A and UN / CG columns of B (X3: a hi and a lo copy of each, so the three
+// products of a k-block read four tiles loaded once); it accumulates into a
+// 128 x UN fp32 TMEM accumulator, double-buffered.
+template <int CG, int UN, bool X3>
 struct Cfg {
     static constexpr int B_COLS = UN / CG;
-    static constexpr int A_BYTES = BM * BK * 4;      // 16 KB
-    static constexpr int B_BYTES = B_COLS * BK * 4;  // 4 KB per 32 columns
-    static constexpr int KB_BYTES = A_BYTES + B_BYTES;  // one k-block: [A | B]
+    static constexpr int A_BYTES = BM * BK * 4;           // 16 KB
+    static constexpr int B_BYTES = B_COLS * BK * 4;       // 4 KB per 32 columns
+    static constexpr int PAIR_BYTES = A_BYTES + B_BYTES;  // [A | B]
+    // X3: [hi(A) | hi(B) | lo(A) | lo(B)]
+    static constexpr int KB_BYTES = (X3 ? 2 : 1) * PAIR_BYTES;
     // k-blocks per stage: one full-barrier wait and one commit serve SUBS
     // k-blocks (the MMA thread's per-stage handshake costs as much as ~1 MMA)
     static constexpr int SUBS = KB_BYTES <= 32 * 1024 ? 2 : 1;
     static constexpr int STAGE_BYTES = SUBS * KB_BYTES;
     static constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+    // X3 keeps every output row's chunk sums in registers: 8 epilogue warps,
+    // two per TMEM lane quarter, each holding half of the row's columns.
+    static constexpr int EPI_WARPS = X3 ? 8 : 4;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int EPI_COLS = UN * 4 / EPI_WARPS;  // accumulator columns per epilogue warp
     static constexpr int TMEM_COLS = 2 * UN;
     static constexpr int TILE_M = BM * CG;
     static constexpr int BAR_BYTES = 256;
     static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
     static_assert(TMEM_COLS <= 512, "two accumulators must fit in TMEM");
     static_assert(B_COLS % 32 == 0 && B_COLS <= 256, "B tile columns");
+    static_assert(STAGES >= 2, "at least two pipeline stages");
+    static_assert(EPI_COLS % 32 == 0, "epilogue columns in 32-column TMEM loads");
 };
 
-// CHUNKED (UN = 128 only): the epilogue keeps each thread's output row in
-// 128 registers and adds the chunk partials into it in fp32 round-to-nearest,
-// storing after the last chunk.  Otherwise a tile is one chunk.
-template <int CG, int UN, bool CHUNKED>
-__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    static_assert(!CHUNKED || UN == 128, "chunked accumulation keeps a 128-float row per thread");
-    using S = Cfg<CG, UN>;
+// X3: the epilogue adds the chunk partials of each output element into
+// registers in fp32 round-to-nearest and stores after the last chunk.
+template <int CG, int UN, bool X3>
+__global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    using S = Cfg<CG, UN, X3>;
     constexpr int STAGES = S::STAGES;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte-swizzle atoms.
@@ -418,7 +431,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4 * CG);  // one arrival per epilogue warp of each CTA
+            mbar_init(&tempty[a], S::EPI_WARPS * CG);  // one arrival per epilogue warp of each CTA
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -428,7 +441,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     if (warp == 0 && lane == 0) {
         prefetch_map(&p.tmA[0]);
         prefetch_map(&p.tmB[0]);
-        if (p.passes > 1) {
+        if constexpr (X3) {
             prefetch_map(&p.tmA[1]);
             prefetch_map(&p.tmB[1]);
         }
@@ -442,8 +455,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     if constexpr (CG == 2) cluster_sync();  // peer barriers initialised before any remote use
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-
-    const int total_kb = p.k_blocks * p.passes;
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
@@ -467,7 +478,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 const int n0 = tc.n * UN + (int)rank * S::B_COLS;       // this CTA's B columns
                 KbIter it;
                 it.start(p);
-                for (int kb = 0; kb < total_kb;) {
+                for (int kb = 0; kb < p.k_blocks;) {
                     if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1)) {
                         ok = false;
                         break;
@@ -475,32 +486,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     // The stage's previous load was consumed (the MMA that read it finished).
                     pend &= ~(1u << stage);
                     // up to SUBS k-blocks of one accumulation chunk share the stage
-                    const int nsub = min(S::SUBS, it.left_in_chunk(p));
+                    const int nsub = min(S::SUBS, it.left_in_chunk());
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
                     if (leader) mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
                     for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
                         const int k0 = it.kb() * BK;
-                        // pass 0: lo(A).hi(B), pass 1: hi(A).lo(B), pass 2: hi(A).hi(B)
-                        const int pa = (p.passes > 1 && it.pass == 0) ? 1 : 0;
-                        const int pb = (p.passes > 1 && it.pass == 1) ? 1 : 0;
-                        uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES;
-                        uint8_t* sb = sa + S::A_BYTES;
-                        if (p.a_mn) {
 #pragma unroll
-                            for (int c = 0; c < BM / 32; ++c)
-                                tma_load_5d<CG>(sa + c * a_chunk_bytes, &p.tmA[pa], fb, m0 + 32 * c,
-                                                k0, a0, a1, a2);
-                        } else {
-                            tma_load_5d<CG>(sa, &p.tmA[pa], fb, k0, m0, a0, a1, a2);
-                        }
-                        if (p.b_mn) {
+                        for (int h = 0; h < (X3 ? 2 : 1); ++h) {  // X3: hi, then lo planes
+                            uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
+                                          h * S::PAIR_BYTES;
+                            uint8_t* sb = sa + S::A_BYTES;
+                            if (p.a_mn) {
 #pragma unroll
-                            for (int c = 0; c < S::B_COLS / 32; ++c)
-                                tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[pb], fb, n0 + 32 * c,
-                                                k0, b0, b1, b2);
-                        } else {
-                            tma_load_5d<CG>(sb, &p.tmB[pb], fb, k0, n0, b0, b1, b2);
+                                for (int c = 0; c < BM / 32; ++c)
+                                    tma_load_5d<CG>(sa + c * a_chunk_bytes, &p.tmA[h], fb,
+                                                    m0 + 32 * c, k0, a0, a1, a2);
+                            } else {
+                                tma_load_5d<CG>(sa, &p.tmA[h], fb, k0, m0, a0, a1, a2);
+                            }
+                            if (p.b_mn) {
+#pragma unroll
+                                for (int c = 0; c < S::B_COLS / 32; ++c)
+                                    tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[h], fb,
+                                                    n0 + 32 * c, k0, b0, b1, b2);
+                            } else {
+                                tma_load_5d<CG>(sb, &p.tmB[h], fb, k0, n0, b0, b1, b2);
+                            }
                         }
                     }
                     pend |= 1u << stage;
@@ -546,6 +558,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                                             : smem_desc(s0 + S::A_BYTES, 16, 1024, kSw128);
             const uint32_t a_step = (p.a_mn ? 1024u : UMMA_K * 4u) >> 4;
             const uint32_t b_step = (p.b_mn ? 1024u : UMMA_K * 4u) >> 4;
+            constexpr uint32_t lo_off = S::PAIR_BYTES >> 4;  // hi -> lo copy of a tile
             const uint32_t empty_addr = smem_u32(&empty[0]);
             int stage = 0;
             uint32_t phase = 0;
@@ -557,9 +570,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 uint32_t d = 0;
                 KbIter it;
                 it.start(p);
-                for (int kb = 0; kb < total_kb;) {
+                for (int kb = 0; kb < p.k_blocks;) {
                     // the stage holds up to SUBS k-blocks of one chunk (as loaded)
-                    const int nsub = min(S::SUBS, it.left_in_chunk(p));
+                    const int nsub = min(S::SUBS, it.left_in_chunk());
                     if (it.first()) {
                         // a fresh accumulator for this chunk, once the epilogues drained it
                         if (!wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag,
@@ -578,14 +591,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                     bool chunk_end = false;
                     for (int s = 0; s < nsub; ++s, ++kb, it.next(p)) {
                         const bool first = it.first();
-                        chunk_end = it.last(p);
+                        chunk_end = it.last();
                         const uint32_t soff =
                             (uint32_t)(stage * S::STAGE_BYTES + s * S::KB_BYTES) >> 4;
                         const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
+                        if constexpr (X3) {
+                            // lo(A).hi(B) + hi(A).lo(B) + hi(A).hi(B): small terms first
 #pragma unroll
-                        for (int j = 0; j < BK / UMMA_K; ++j)
-                            umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
-                                          (!first || j > 0) ? 1u : 0u);
+                            for (int j = 0; j < BK / UMMA_K; ++j)
+                                umma_tf32<CG>(d, ad + lo_off + j * a_step, bd + j * b_step, idesc,
+                                              (!first || j > 0) ? 1u : 0u);
+#pragma unroll
+                            for (int j = 0; j < BK / UMMA_K; ++j)
+                                umma_tf32<CG>(d, ad + j * a_step, bd + lo_off + j * b_step, idesc, 1u);
+#pragma unroll
+                            for (int j = 0; j < BK / UMMA_K; ++j)
+                                umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc, 1u);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BK / UMMA_K; ++j)
+                                umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
+                                              (!first || j > 0) ? 1u : 0u);
+                        }
                     }
                     issued = true;
                     // free the stage in every CTA once these MMAs finish
@@ -617,8 +644,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5, both CTAs) ----------------
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        // ---------------- epilogue (warps 2.., both CTAs) ----------------
+        // A warp may access only TMEM lane quarter warp % 4; with 8 epilogue
+        // warps two share a quarter and split the columns.
+        const int q = warp & 3;
+        const int col_half = (warp - 2) >> 2;  // 0 with 4 epilogue warps
         const int row_in_tile = q * 32 + lane;
         const uint32_t tempty_leader = CG == 2 ? mapa(smem_u32(&tempty[0]), 0) : 0u;
         uint32_t acc_ph = 0;  // bit a: phase parity of accumulator a
@@ -632,32 +662,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 #pragma unroll
             for (int i = 0; i < kMaxBatchDims; ++i) oc += (int64_t)bi[i] * p.cbs[i];
             const int64_t row = (int64_t)tc.m * S::TILE_M + (int)rank * BM + row_in_tile;
-            const int n0 = tc.n * UN;
+            const int n0 = tc.n * UN + col_half * S::EPI_COLS;
             float* crow = p.C + oc + row * p.c_rs;
-            float sum[CHUNKED ? UN : 1];
+            float sum[X3 ? S::EPI_COLS : 1];
 #pragma unroll
-            for (int j = 0; j < (CHUNKED ? UN : 1); ++j) sum[j] = 0.0f;
+            for (int j = 0; j < (X3 ? S::EPI_COLS : 1); ++j) sum[j] = 0.0f;
             for (int ch = 0; ch < p.num_chunks; ++ch) {
                 if (lane == 0)
                     ok = wait_bounded(&tfull[acc], (acc_ph >> acc) & 1u, abort_flag, p.timeout_ns, p.err, 4);
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // one branch per warp
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t taddr =
-                    tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * UN);
-                if constexpr (CHUNKED) {
+                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) +
+                                       (uint32_t)(acc * UN + col_half * S::EPI_COLS);
+                if constexpr (X3) {
+                    // 16-column loads: the sums already hold EPI_COLS registers
 #pragma unroll
-                    for (int c = 0; c < UN / 32; ++c) {
-                        uint32_t r[32];
-                        tmem_ld32(taddr + c * 32, r);
+                    for (int c = 0; c < S::EPI_COLS / 16; ++c) {
+                        uint32_t r[16];
+                        tmem_ld16(taddr + c * 16, r);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            sum[c * 32 + j] = __fadd_rn(sum[c * 32 + j], __uint_as_float(r[j]));
+                        for (int j = 0; j < 16; ++j)
+                            sum[c * 16 + j] = __fadd_rn(sum[c * 16 + j], __uint_as_float(r[j]));
                     }
                 } else {
 #pragma unroll 1
-                    for (int c = 0; c < UN / 32; ++c) {
+                    for (int c = 0; c < S::EPI_COLS / 32; ++c) {
                         uint32_t r[32];
                         tmem_ld32(taddr + c * 32, r);
                         tmem_wait_ld();
@@ -690,10 +721,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 acc_ph ^= 1u << acc;
                 acc ^= 1;
             }
-            if constexpr (CHUNKED) {
+            if constexpr (X3) {
                 if (ok && row < p.M) {
 #pragma unroll
-                    for (int c = 0; c < UN / 32; ++c) {
+                    for (int c = 0; c < S::EPI_COLS / 32; ++c) {
                         const int col0 = n0 + c * 32;
                         if (p.vec_c && col0 + 32 <= p.N) {
 #pragma unroll
@@ -899,10 +930,10 @@ int* error_word() {
     return words[dev];
 }
 
-template <int CG, int UN, bool CHUNKED>
+template <int CG, int UN, bool X3>
 int launch_variant(const TcParams& prm, cudaStream_t s) {
-    using S = Cfg<CG, UN>;
-    auto kernel = tc_gemm_kernel<CG, UN, CHUNKED>;
+    using S = Cfg<CG, UN, X3>;
+    auto kernel = tc_gemm_kernel<CG, UN, X3>;
     static int configured[64] = {};
     static int max_units[64] = {};
     int dev = 0;
@@ -910,7 +941,7 @@ int launch_variant(const TcParams& prm, cudaStream_t s) {
     if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.blockDim = dim3(S::THREADS, 1, 1);
     cfg.dynamicSmemBytes = S::TOTAL;
     cfg.stream = s;
     if (CG == 2) {
@@ -946,17 +977,25 @@ int launch_variant(const TcParams& prm, cudaStream_t s) {
     return check_launch("tc_gemm");
 }
 
+// The variant for a problem: CTA pairs (CG = 2) for more than 128 rows;
+// N = 256 tiles for more than 128 columns, except single-CTA 3xTF32, whose
+// four 256-column tiles per k-block would leave two pipeline stages.
+void pick_variant(const Gemm& g, bool x3, int* cg, int* un) {
+    *cg = g.M > 128 ? 2 : 1;
+    *un = (g.N > 128 && !(x3 && *cg == 1)) ? 256 : 128;
+}
+
 // Fills the tile/launch fields of `prm` for a variant and launches it.
-// Pairs (CG = 2) for problems with more than 128 rows; 3xTF32 uses UN = 128
-// so its chunk sums fit in the epilogue's registers.
-int launch_tc(TcParams& prm, const Gemm& g, cudaStream_t s) {
-    const bool x3 = prm.passes == 3;
-    const int cg = g.M > 128 ? 2 : 1;
-    const int un = (!x3 && g.N > 128) ? 256 : 128;
+int launch_tc(TcParams& prm, const Gemm& g, bool x3, cudaStream_t s) {
+    int cg, un;
+    pick_variant(g, x3, &cg, &un);
     prm.m_tiles = (int)((g.M + BM * cg - 1) / (BM * cg));
     prm.n_tiles = (int)((g.N + un - 1) / un);
     prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
-    if (x3) return cg == 2 ? launch_variant<2, 128, true>(prm, s) : launch_variant<1, 128, true>(prm, s);
+    if (x3) {
+        if (cg == 1) return launch_variant<1, 128, true>(prm, s);
+        return un == 256 ? launch_variant<2, 256, true>(prm, s) : launch_variant<2, 128, true>(prm, s);
+    }
     if (un == 256)
         return cg == 2 ? launch_variant<2, 256, false>(prm, s) : launch_variant<1, 256, false>(prm, s);
     return cg == 2 ? launch_variant<2, 128, false>(prm, s) : launch_variant<1, 128, false>(prm, s);
@@ -964,7 +1003,7 @@ int launch_tc(TcParams& prm, const Gemm& g, cudaStream_t s) {
 
 // The parts of TcParams that do not depend on the kernel variant.
 void fill_common(TcParams& prm, const Gemm& g, const OperandMap& A, const OperandMap& B,
-                 bool a_mn, bool b_mn, int passes) {
+                 bool a_mn, bool b_mn, bool x3) {
     prm.C = g.C;
     prm.c_rs = g.c_rs;
     prm.nb = g.nb;
@@ -978,13 +1017,12 @@ void fill_common(TcParams& prm, const Gemm& g, const OperandMap& A, const Operan
     prm.N = (int)g.N;
     prm.K = (int)g.K;
     prm.k_blocks = (int)((g.K + BK - 1) / BK);
-    prm.passes = passes;
     // The tensor cores' fp32 accumulation error grows linearly with the
     // length of the accumulation chain (measured: ~2.4e-9 x K relative,
     // biased towards zero), which puts long-K 3xTF32 above 1e-5.  3xTF32
     // therefore restarts the TMEM accumulator every 256 k (8 k-blocks) and
     // sums the chunks in fp32 round-to-nearest; TF32 keeps one chain.
-    prm.chunk_kb = passes == 3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
+    prm.chunk_kb = x3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
     prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
     prm.a_mn = a_mn ? 1 : 0;
     prm.b_mn = b_mn ? 1 : 0;
@@ -1023,9 +1061,9 @@ void operand_maps(const Gemm& g, bool a_mn, bool b_mn, OperandMap& A, OperandMap
 }
 
 // B columns a CTA loads per stage for the variant launch_tc will pick.
-uint32_t b_cols_for(const Gemm& g, int passes) {
-    const int cg = g.M > 128 ? 2 : 1;
-    const int un = (passes == 1 && g.N > 128) ? 256 : 128;
+uint32_t b_cols_for(const Gemm& g, bool x3) {
+    int cg, un;
+    pick_variant(g, x3, &cg, &un);
     return (uint32_t)(un / cg);
 }
 
@@ -1044,11 +1082,11 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     for (int i = 0; i < g.nb; ++i)
         if (g.bsz[i] > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "batch dim too large");
 
-    const int passes = mode == TLC_MODE_3XTF32 ? 3 : 1;
+    const bool x3 = mode == TLC_MODE_3XTF32;
     const bool a_mn = g.a_cs != 1;  // a_rs == 1
     const bool b_mn = g.b_cs == 1;  // else b_rs == 1
     OperandMap A, B;
-    operand_maps(g, a_mn, b_mn, A, B, b_cols_for(g, passes));
+    operand_maps(g, a_mn, b_mn, A, B, b_cols_for(g, x3));
 
     TcScratch sc(s);
     if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb)) TLC_TRY(repack(A, g.nb, sc, 0, s));
@@ -1056,7 +1094,7 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
 
     TcParams prm;
     memset(&prm, 0, sizeof(prm));
-    if (passes == 3) {
+    if (x3) {
         // Split each operand's storage span into hi / lo planes of identical layout.
         OperandMap* ops[2] = {&A, &B};
         CUtensorMap* maps[2] = {prm.tmA, prm.tmB};
@@ -1080,10 +1118,10 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
         TLC_TRY(encode(&prm.tmA[0], A));
         TLC_TRY(encode(&prm.tmB[0], B));
     }
-    fill_common(prm, g, A, B, a_mn, b_mn, passes);
+    fill_common(prm, g, A, B, a_mn, b_mn, x3);
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
-    return launch_tc(prm, g, s);
+    return launch_tc(prm, g, x3, s);
 }
 
 int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
@@ -1189,7 +1227,7 @@ int gemm_3xtf32_noalloc(const tlc_gemm_desc* d, cudaStream_t s) {
     const bool a_mn = g.a_cs != 1;
     const bool b_mn = g.b_cs == 1;
     OperandMap A, B;
-    operand_maps(g, a_mn, b_mn, A, B, b_cols_for(g, 3));
+    operand_maps(g, a_mn, b_mn, A, B, b_cols_for(g, true));
     if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb) ||
         !tma_ok(B.base, B.outer_stride, B.bstride, g.nb))
         return set_error(TLC_ERR_UNSUPPORTED,
@@ -1228,10 +1266,10 @@ int gemm_3xtf32_noalloc(const tlc_gemm_desc* d, cudaStream_t s) {
     TLC_TRY(encode(&prm.tmA[1], al));
     TLC_TRY(encode(&prm.tmB[0], bh));
     TLC_TRY(encode(&prm.tmB[1], bl));
-    fill_common(prm, g, A, B, a_mn, b_mn, 3);
+    fill_common(prm, g, A, B, a_mn, b_mn, true);
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
-    return launch_tc(prm, g, s);
+    return launch_tc(prm, g, true, s);
 }
 
 }  // namespace
