@@ -3,7 +3,10 @@
 CPU: two gloo ranks run the partition plan (libtl_cuda's host-only
 tlc_shard_range / tlc_shard_cols), compute their shares with the oracle,
 all-gather them, and reassemble with the index rule of tlc_gather_colblocks;
-the result must equal the oracle's full product bit for bit.
+the result must equal the oracle's full product bit for bit.  They also run
+tldist.chained_batch_sum (the rank-to-rank chain that reduces a broadcast
+operand's gradient in batch order) on oracle per-entry products, which must
+equal the oracle's MatmulBackward dB bit for bit.
 GPU (1 device): tlc_gather_colblocks on blocks computed per simulated rank.
 GPU (2+ devices): the real NCCL path, one process per GPU.
 """
@@ -70,8 +73,17 @@ def _gloo_worker(rank, world, port, q):
         dist.all_gather(parts, torch.from_numpy(pad))
         C = np.concatenate([parts[r].numpy()[: sizes[r][1] - sizes[r][0]] for r in range(world)])
         ok_batch = np.array_equal(C.view(np.uint32), O.matmul(A, B).view(np.uint32))
+        # its backward: dB of the broadcast B through the order-keeping chain
+        # (per-entry products from the oracle, the chain and its sends as shipped)
+        import tldist
+        dC = inputs.normal(np.random.default_rng(9), (5, 9, 6))
+        G = O.matmul(np.ascontiguousarray(A[b0:b1].transpose(0, 2, 1)), dC[b0:b1])
+        sum0 = lambda st: torch.from_numpy(O.sum_dim(st.numpy(), 0, False))  # noqa: E731
+        dB = tldist.chained_batch_sum(torch.from_numpy(G), sum0=sum0).numpy()
+        ref_dA, ref_dB = O.matmul_backward(dC, A, B)
+        ok_bwd = np.array_equal(dB.view(np.uint32), ref_dB.view(np.uint32))
         dist.destroy_process_group()
-        q.put((rank, ok_cols, ok_batch, None))
+        q.put((rank, ok_cols, ok_batch and ok_bwd, None))
     except Exception as e:  # report, do not hang the parent
         q.put((rank, False, False, repr(e)))
 
@@ -135,6 +147,17 @@ def _nccl_worker(rank, world, port, q):
         B2 = torch.randn((96, 80), generator=g, device="cuda")
         C = tldist.batch_sharded_matmul(A3, B2, mode="exact", gather=True)
         ok2 = torch.equal(C, tlcuda.matmul(A3, B2, mode="exact"))
+        # backward of the batch split: dA shards local, dB of the broadcast B
+        # summed across ranks (exact: ordered chain, bit-identical; tf32:
+        # all-reduce, within the TF32 tolerance)
+        dC = torch.randn((7, 64, 80), generator=g, device="cuda")
+        b0, b1 = tldist.batch_shard(7, world, rank)
+        ref_dA, ref_dB = tlcuda.matmul_backward(dC, A3, B2, mode="exact")
+        dA, dB = tldist.batch_sharded_matmul_backward(dC[b0:b1], A3, B2, mode="exact")
+        ok2 = ok2 and torch.equal(dA, ref_dA[b0:b1]) and torch.equal(dB, ref_dB)
+        dA, dB = tldist.batch_sharded_matmul_backward(dC[b0:b1], A3, B2, mode="tf32")
+        rel = ((dB.double() - ref_dB.double()).norm() / ref_dB.double().norm()).item()
+        ok2 = ok2 and rel < 1e-2
         torch.cuda.synchronize()
         dist.destroy_process_group()
         q.put((rank, ok1, ok2, None))

@@ -247,6 +247,19 @@ def gemm(A, B, C, M, N, K, a_rs, a_cs, b_rs, b_cs, c_rs, batch=(), a_bs=(), b_bs
     _check(lib().tlc_gemm(ctypes.byref(d), mode_id(mode), _stream_ptr(stream)))
 
 
+def sum_dim0(stack, out=None, stream=None):
+    """sum over dim 0 of a contiguous CUDA tensor, ascending from 0.0f
+    (tlc_sum_dim with outer = 1): the reference's sum(x, 0) order."""
+    import torch
+    assert stack.is_contiguous()
+    if out is None:
+        out = torch.empty(stack.shape[1:], dtype=torch.float32, device=stack.device)
+    inner = out.numel()
+    _check(lib().tlc_sum_dim(ctypes.c_void_p(stack.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                             1, stack.shape[0], inner, _stream_ptr(stream)))
+    return out
+
+
 def shard_range(count, world, rank):
     b, e = ctypes.c_int64(), ctypes.c_int64()
     _check(lib().tlc_shard_range(count, world, rank, ctypes.byref(b), ctypes.byref(e)))

@@ -8,6 +8,13 @@ path of the GEMM itself.
                           batch dim: rank r computes batch entries
                           [begin_r, end_r) (tlc_shard_range); broadcast
                           operands are replicated.  Optional all-gather of C.
+  batch_sharded_matmul_backward
+                          MatmulBackward of the batch-split product: dA is
+                          local to each rank's entries; dB of a broadcast B
+                          is summed over all entries, by a rank-to-rank
+                          chain in batch order for exact mode (bit-identical
+                          to the reference's sequential sum_to) or by one
+                          NCCL all-reduce for the tensor-core modes.
   colblock_sharded_matmul a single GEMM split over output column blocks:
                           rank r computes C[:, c_r:c_{r+1}] = A . B[:, c_r:c_{r+1}]
                           with B's column block read in place (row stride N,
@@ -64,6 +71,66 @@ def batch_sharded_matmul(A, B, mode="tf32", gather=False, group=None):
         s, e = batch_shard(A.shape[0], P, q)
         keep.append(torch.arange(q * per, q * per + (e - s), device=C.device))
     return out[torch.cat(keep)]
+
+
+def chained_batch_sum(local_stack, sum0=None, group=None):
+    """The sum over dim 0 of the stack of all ranks' entries, in global entry
+    order, returned on every rank.  Rank r holds entries [begin_r, end_r) of
+    the global order (tlc_shard_range), as `local_stack`.
+
+    The reference reduces a broadcast operand's gradient with one sequential
+    sum from 0.0f over the batch (sum_to -> sum, src/autograd.cpp:24-36,
+    src/ops.cpp:1181-1233).  The chain keeps that order across ranks: rank r
+    receives the running sum of ranks < r, continues it over its own entries
+    and sends it on; the last rank broadcasts the total.  Continuing is
+    sum0([running, entries...]), i.e. (((0 + running) + e0) + e1)...; 0 + x
+    equals x bit for bit here because a running sum that starts at +0.0 is
+    never -0.0.  `sum0` sums a stack over dim 0 from 0.0f (default: the
+    library's tlc_sum_dim on the GPU)."""
+    import torch
+    import torch.distributed as dist
+    if sum0 is None:
+        sum0 = tlcuda.sum_dim0
+    P, r = world()
+    shape = tuple(local_stack.shape[1:])
+    run = torch.zeros((1,) + shape, dtype=local_stack.dtype, device=local_stack.device)
+    if P > 1 and r > 0:
+        dist.recv(run, src=r - 1, group=group)
+    total = sum0(torch.cat([run, local_stack]).contiguous())
+    if P == 1:
+        return total
+    if r < P - 1:
+        dist.send(total.contiguous(), dst=r + 1, group=group)
+    out = total.contiguous() if r == P - 1 else torch.empty(shape, dtype=local_stack.dtype,
+                                                           device=local_stack.device)
+    dist.broadcast(out, src=P - 1, group=group)
+    return out
+
+
+def batch_sharded_matmul_backward(dC, A, B, mode="tf32", group=None):
+    """MatmulBackward of batch_sharded_matmul(A, B): `dC` is this rank's
+    shard of the upstream gradient ([end-begin, M, N]); A [batch, M, K] and B
+    ([batch, K, N] or broadcast [K, N]) are the full operands, as given to the
+    forward.  Returns (dA shard [end-begin, M, K], dB), where dB is this
+    rank's shard for a batched B and the full [K, N] on every rank for a
+    broadcast B (src/autograd.cpp:341-384: dA = dC.B^T, dB = sum_to(A^T.dC))."""
+    import torch.distributed as dist
+    P, r = world()
+    b0, b1 = batch_shard(A.shape[0], P, r)
+    A_r = A[b0:b1]
+    if B.dim() == 3:  # every entry has its own B: nothing to exchange
+        return tlcuda.matmul_backward(dC, A_r, B[b0:b1], mode=mode)
+    dA, _ = tlcuda.matmul_backward(dC, A_r, B, mode=mode, need_b=False)
+    if P == 1:
+        _, dB = tlcuda.matmul_backward(dC, A_r, B, mode=mode, need_a=False)
+        return dA, dB
+    if mode == "exact":
+        # per-entry products A_b^T.dC_b, then the order-keeping chain
+        G = tlcuda.matmul(A_r.transpose(-1, -2), dC, mode=mode)
+        return dA, chained_batch_sum(G, group=group)
+    _, dB = tlcuda.matmul_backward(dC, A_r, B, mode=mode, need_a=False)  # local sum_to
+    dist.all_reduce(dB, group=group)
+    return dA, dB
 
 
 def colblock_sharded_matmul(A, B, mode="tf32", gather=False, align=256, group=None):
