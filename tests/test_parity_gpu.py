@@ -102,6 +102,37 @@ def test_ragged_layouts(M, N, K, ta, tb):
     assert bits_equal(got, ref)
 
 
+# Contiguous extents that are multiples of 4 floats: every layout below is read
+# by the TMA-fed exact kernel (ragged M / N / K tiles zero-filled by TMA).
+ALIGNED = [(4, 4, 4), (132, 260, 36), (300, 124, 1004), (260, 132, 4), (1000, 8, 300),
+           (128, 256, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K", ALIGNED)
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_aligned_layouts(M, N, K, ta, tb):
+    rng = np.random.default_rng(M * 5 + N * 11 + K)
+    a = inputs.normal(rng, (K, M) if ta else (M, K))
+    b = inputs.normal(rng, (N, K) if tb else (K, N))
+    an, bn = (a.T if ta else a), (b.T if tb else b)
+    got = host(tlcuda.matmul(T(dev(a), ta), T(dev(b), tb)))
+    assert bits_equal(got, O.matmul(an, bn))
+
+
+@pytest.mark.parametrize("tb", [False, True])
+def test_aligned_batched_broadcast(tb):
+    rng = np.random.default_rng(21)
+    a = inputs.normal(rng, (3, 1, 132, 68))
+    b = inputs.normal(rng, (1, 2, 36, 68) if tb else (1, 2, 68, 36))
+    bn = np.swapaxes(b, -1, -2) if tb else b
+    got = host(tlcuda.matmul(dev(a), T(dev(b), tb)))
+    assert bits_equal(got, O.matmul(a, bn))
+    g = inputs.normal(rng, got.shape)
+    da, db = tlcuda.matmul_backward(dev(g), dev(a), T(dev(b), tb))
+    oa, ob = O.matmul_backward(g, a, bn)
+    assert bits_equal(host(da), oa) and bits_equal(host(db), ob)
+
+
 def test_empty_and_k0():
     z = tlcuda.matmul(dev(np.ones((0, 4), np.float32)), dev(np.ones((4, 3), np.float32)))
     assert tuple(z.shape) == (0, 3)

@@ -12,16 +12,36 @@
 // c is never -0 (a chain started from +0 can only reach +0, never -0), so the
 // padding cannot change a bit.
 //
-// Tiling: 128x128 output tile per CTA, k-tiles of 16, 256 threads, each thread
-// an 8x8 register tile split 2x2 into 4x4 blocks (rows tm*4 and 32+tm*4 of the
-// warp's 64 rows, columns tn*4 and 16+tn*4 of its 32), so every shared-memory
-// read is a conflict-free 128-bit load.  Global loads go through registers
-// into a double-buffered shared-memory stage, transposing K-major operands on
-// the way so both operands sit k-major ([k][m], [k][n]) in shared memory.
+// Two kernels, one contract:
+//
+// exact_tma_kernel (operands TMA-readable: 16-byte aligned, strides multiples
+// of 4 floats).  128x128 output tile per CTA, 256 threads in 2 x 4 warps of
+// 64 x 32, each thread an 8 x 8 register tile.  k-tiles of 32 stream into a
+// 3-stage shared-memory ring with cp.async.bulk.tensor, one mbarrier per
+// stage; thread 0 issues the loads and a CTA barrier per k-tile guards slot
+// reuse, so the FFMA loop carries no global loads, shared stores or address
+// arithmetic.  Each operand keeps its memory layout in shared memory:
+//   K-major tile ([rows][32 k], a row-major A or the W^T view of a B):
+//     128-byte rows with the 128-byte swizzle (16-byte chunk c of row r at
+//     c ^ (r % 8)); a thread's 8 rows are 8 apart (its 8 B columns 4 apart),
+//     so a warp's 16-byte reads of 4 k-values (8-byte reads of 2 for B) hit
+//     distinct chunks: no bank conflicts.
+//   MN-major tile ([32 k][128 rows], an M-major A or a row-major B):
+//     dense; a warp reads consecutive 16-byte groups along m / n.
+// Two CTAs per SM (99 KB of shared memory and <= 128 registers each).
+//
+// exact_kernel (any other strides).  128x128 tile, k-tiles of 16, 256
+// threads, 8x8 per thread; global loads go through registers into a double-
+// buffered shared-memory stage, transposing K-major operands on the way so
+// both operands sit k-major ([k][m], [k][n]) in shared memory.
+//
 // Transposed operand layouts (an M-major A, a K-major B: the transpose views
-// MatmulBackward builds, src/autograd.cpp:370-371) are read in place by the
-// matching loader; nothing is materialised.
+// MatmulBackward builds, src/autograd.cpp:370-371) are read in place by both
+// kernels; nothing is materialised.
 #include "common.cuh"
+#include "tma.cuh"
+
+#include <cstring>
 
 namespace tlc {
 namespace {
@@ -203,6 +223,327 @@ __global__ void __launch_bounds__(NT, 2) exact_kernel(ExactParams p) {
     }
 }
 
+// ---- TMA-fed kernel ------------------------------------------------------------------
+
+constexpr int TBM = 128, TBN = 128, TBK = 32, TSTAGES = 3;
+constexpr int T_A_BYTES = TBM * TBK * 4;  // 16 KB
+constexpr int T_B_BYTES = TBN * TBK * 4;  // 16 KB
+constexpr int T_STAGE = T_A_BYTES + T_B_BYTES;
+constexpr int T_SMEM = TSTAGES * T_STAGE + 64 + 1024;  // + barriers, coordinates, alignment slack
+
+struct ExactTmaParams {
+    CUtensorMap tmA, tmB;
+    float* C;
+    int64_t c_rs;
+    int64_t cbs[kMaxBatchDims];
+    int bsz[kMaxBatchDims];
+    int a_bc[kMaxBatchDims];  // 1: A indexes this batch dim, 0: broadcast (coordinate 0)
+    int b_bc[kMaxBatchDims];
+    int nb;
+    int M, N, nk;
+    int64_t batch;
+    uint64_t timeout_ns;
+    int* err;
+};
+
+// Bounded wait for the phase of `bar` with the given parity; records `site`
+// in the device error word on expiry (2 s: far above any legitimate wait).
+__device__ __forceinline__ bool exact_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
+                                           int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 0 && globaltimer() - t0 > timeout_ns) {
+            atomicCAS(err, 0, 11);
+            return false;
+        }
+    }
+}
+
+// AK: A is K-major (row-major [M,K]); BKM: B is K-major ([N,K] storage).
+template <bool AK, bool BKM, bool VC>
+__global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant__ ExactTmaParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment: the 128-byte swizzle pattern repeats every 8 rows.
+    // Offsetting the shared array itself (no round trip through an integer)
+    // keeps the compiler aware that these are shared-memory addresses, so
+    // the tile reads compile to 32-bit-addressed shared loads.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TSTAGES * T_STAGE);
+    // thread 0's batch coordinates of the current entry: A's, then B's
+    int* coord = reinterpret_cast<int*>(full + TSTAGES);
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int wm = warp & 1, wn = warp >> 1;  // 2 x 4 warps of 64 x 32
+    const int tm = lane >> 2, tn = lane & 3;  // 8 x 4 lanes of 8 x 8
+    if (tid == 0) {
+        for (int s = 0; s < TSTAGES; ++s) mbar_init(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        prefetch_map(&p.tmA);
+        prefetch_map(&p.tmB);
+    }
+    __syncthreads();
+
+    const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * TBN;
+    uint32_t it0 = 0;                 // k-tiles this CTA consumed before the current entry
+    uint32_t pend = 0, pend_par = 0;  // thread 0: slots with a load it has not seen complete
+    bool bad = false;
+    for (int64_t b = blockIdx.z; b < p.batch; b += gridDim.z) {
+        int64_t oc = 0;  // this entry's C offset
+        {
+            int bi[kMaxBatchDims];
+            int64_t r = b;
+#pragma unroll
+            for (int i = kMaxBatchDims - 1; i >= 0; --i) {
+                if (i < p.nb) {
+                    bi[i] = (int)(r % p.bsz[i]);
+                    r /= p.bsz[i];
+                } else {
+                    bi[i] = 0;
+                }
+                oc += (int64_t)bi[i] * p.cbs[i];
+            }
+            if (tid == 0)
+#pragma unroll
+                for (int i = 0; i < kMaxBatchDims; ++i) {
+                    coord[i] = p.a_bc[i] ? bi[i] : 0;
+                    coord[3 + i] = p.b_bc[i] ? bi[i] : 0;
+                }
+        }
+        // Thread 0: load k-tile kt of this entry into its slot.
+        auto issue = [&](int kt) {
+            const uint32_t g = it0 + (uint32_t)kt;
+            const int slot = (int)(g % TSTAGES);
+            uint8_t* sa = smem + slot * T_STAGE;
+            mbar_expect_tx(&full[slot], T_STAGE);
+            const int k0 = kt * TBK;
+            if (AK)
+                tma_load_5d_local(sa, &p.tmA, &full[slot], k0, m0, coord[0], coord[1], coord[2]);
+            else
+                tma_load_5d_local(sa, &p.tmA, &full[slot], m0, k0, coord[0], coord[1], coord[2]);
+            if (BKM)
+                tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], k0, n0, coord[3], coord[4],
+                                  coord[5]);
+            else
+                tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], n0, k0, coord[3], coord[4],
+                                  coord[5]);
+            pend |= 1u << slot;
+            pend_par = (pend_par & ~(1u << slot)) | (((g / TSTAGES) & 1u) << slot);
+        };
+        // Slots of earlier entries are free: every thread passed the barrier
+        // after its last k-tile, except for the last slot, which this
+        // prologue does not touch.
+        if (tid == 0)
+            for (int kt = 0; kt < TSTAGES - 1 && kt < p.nk; ++kt) issue(kt);
+
+        float acc[8][8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+        for (int kt = 0; kt < p.nk; ++kt) {
+            // Everyone is done with k-tile kt-1, whose slot the next load reuses.
+            if (__syncthreads_or(bad)) {
+                bad = true;
+                break;
+            }
+            if (tid == 0 && kt + TSTAGES - 1 < p.nk) issue(kt + TSTAGES - 1);
+            const uint32_t g = it0 + (uint32_t)kt;
+            const int slot = (int)(g % TSTAGES);
+            if (!exact_wait(&full[slot], (g / TSTAGES) & 1u, p.timeout_ns, p.err)) {
+                bad = true;
+                continue;
+            }
+            if (tid == 0) pend &= ~(1u << slot);
+            const uint8_t* sa = smem + slot * T_STAGE;
+            const uint8_t* sb = sa + T_A_BYTES;
+#pragma unroll 2
+            for (int q = 0; q < TBK / 4; ++q) {  // groups of 4 k, ascending
+                // A: a[i][u] = A[row i][4q + u]
+                float a[8][4];
+                if (AK) {
+                    // row r = wm*64 + tm + 8i (r % 8 == tm): 16-byte chunk q of the row
+                    const uint8_t* pa = sa + (wm * 64 + tm) * 128 + ((q ^ tm) << 4);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 v = *reinterpret_cast<const float4*>(pa + i * 8 * 128);
+                        a[i][0] = v.x;
+                        a[i][1] = v.y;
+                        a[i][2] = v.z;
+                        a[i][3] = v.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint8_t* pa = sa + (4 * q + u) * (TBM * 4) + (wm * 64 + tm * 4) * 4;
+                        const float4 x = *reinterpret_cast<const float4*>(pa);
+                        const float4 y = *reinterpret_cast<const float4*>(pa + 32 * 4);
+                        a[0][u] = x.x; a[1][u] = x.y; a[2][u] = x.z; a[3][u] = x.w;
+                        a[4][u] = y.x; a[5][u] = y.y; a[6][u] = y.z; a[7][u] = y.w;
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {  // k = 4q + 2h, 4q + 2h + 1
+                    float bv[8][2];
+                    if (BKM) {
+                        // column c = wn*32 + tn + 4j (c % 8 == tn + 4 (j % 2))
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int c7 = tn + 4 * (j & 1);
+                            const float2 v = *reinterpret_cast<const float2*>(
+                                sb + (wn * 32 + tn + 4 * j) * 128 + ((q ^ c7) << 4) + h * 8);
+                            bv[j][0] = v.x;
+                            bv[j][1] = v.y;
+                        }
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            const uint8_t* pb =
+                                sb + (4 * q + 2 * h + t) * (TBN * 4) + (wn * 32 + tn * 4) * 4;
+                            const float4 x = *reinterpret_cast<const float4*>(pb);
+                            const float4 y = *reinterpret_cast<const float4*>(pb + 16 * 4);
+                            bv[0][t] = x.x; bv[1][t] = x.y; bv[2][t] = x.z; bv[3][t] = x.w;
+                            bv[4][t] = y.x; bv[5][t] = y.y; bv[6][t] = y.z; bv[7][t] = y.w;
+                        }
+                    }
+#pragma unroll
+                    for (int t = 0; t < 2; ++t)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                acc[i][j] = fmaf(a[i][2 * h + t], bv[j][t], acc[i][j]);
+                }
+            }
+        }
+        // One decision for the whole CTA: a thread that timed out on the last
+        // k-tile must not leave while the others go on to the next entry.
+        if (__syncthreads_or(bad)) {
+            bad = true;
+            break;
+        }
+        it0 += (uint32_t)p.nk;
+
+        float* Cb = p.C + oc;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = m0 + wm * 64 + (AK ? tm + 8 * i : (i < 4 ? tm * 4 + i : 32 + tm * 4 + (i - 4)));
+            if (row >= p.M) continue;
+            float* crow = Cb + (int64_t)row * p.c_rs;
+            if (BKM) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int col = n0 + wn * 32 + tn + 4 * j;
+                    if (col < p.N) crow[col] = acc[i][j];
+                }
+            } else {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int col = n0 + wn * 32 + h * 16 + tn * 4;
+                    if (VC && col + 3 < p.N) {
+                        *reinterpret_cast<float4*>(crow + col) = make_float4(
+                            acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (col + j < p.N) crow[col + j] = acc[i][4 * h + j];
+                    }
+                }
+            }
+        }
+    }
+    if (bad && tid == 0) {
+        // Drain: wait (bounded) for loads still in flight into shared memory.
+        for (int s = 0; s < TSTAGES; ++s) {
+            if (!(pend & (1u << s))) continue;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full[s], (pend_par >> s) & 1u) &&
+                   globaltimer() - t0 < p.timeout_ns) {
+            }
+        }
+    }
+}
+
+template <bool AK, bool BKM, bool VC>
+int launch_tma_variant(const ExactTmaParams& p, dim3 grid, cudaStream_t s) {
+    auto kernel = exact_tma_kernel<AK, BKM, VC>;
+    static int configured[64] = {};
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    if (!configured[dev]) {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T_SMEM));
+        configured[dev] = 1;
+    }
+    kernel<<<grid, NT, T_SMEM, s>>>(p);
+    count_launch();
+    return check_launch("gemm_exact_tma");
+}
+
+// The TMA kernel when both operands are TMA-readable in place; returns
+// TLC_ERR_UNSUPPORTED (without launching) otherwise.
+int gemm_exact_tma(const Gemm& g, bool ak, bool bkm, bool vc, cudaStream_t s) {
+    if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX - TBK) return TLC_ERR_UNSUPPORTED;
+    for (int i = 0; i < g.nb; ++i)
+        if (g.bsz[i] > INT32_MAX) return TLC_ERR_UNSUPPORTED;
+    const int64_t a_os = ak ? g.a_rs : g.a_cs, b_os = bkm ? g.b_cs : g.b_rs;
+    if (!tma_ok(g.A, a_os, g.abs_, g.nb) || !tma_ok(g.B, b_os, g.bbs, g.nb)) return TLC_ERR_UNSUPPORTED;
+    int* err = nullptr;
+    TLC_TRY(tc_error_word(&err));
+    ExactTmaParams p;
+    memset(&p, 0, sizeof(p));
+    int64_t bsz[kMaxBatchDims];
+    for (int i = 0; i < kMaxBatchDims; ++i) bsz[i] = i < g.nb ? g.bsz[i] : 1;
+    int64_t abst[kMaxBatchDims] = {}, bbst[kMaxBatchDims] = {};
+    for (int i = 0; i < g.nb; ++i) {
+        abst[i] = g.abs_[i];
+        bbst[i] = g.bbs[i];
+    }
+    // A K-major: {K, M} boxes {32, 128}, swizzled; M-major: {M, K} boxes {128, 32}.
+    if (ak)
+        TLC_TRY(encode_tiled(&p.tmA, g.A, g.K, g.M, a_os, bsz, abst, TBK, TBM, CU_TENSOR_MAP_SWIZZLE_128B));
+    else
+        TLC_TRY(encode_tiled(&p.tmA, g.A, g.M, g.K, a_os, bsz, abst, TBM, TBK, CU_TENSOR_MAP_SWIZZLE_NONE));
+    if (bkm)
+        TLC_TRY(encode_tiled(&p.tmB, g.B, g.K, g.N, b_os, bsz, bbst, TBK, TBN, CU_TENSOR_MAP_SWIZZLE_128B));
+    else
+        TLC_TRY(encode_tiled(&p.tmB, g.B, g.N, g.K, b_os, bsz, bbst, TBN, TBK, CU_TENSOR_MAP_SWIZZLE_NONE));
+    p.C = g.C;
+    p.c_rs = g.c_rs;
+    p.nb = g.nb;
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        p.bsz[i] = (int)bsz[i];
+        p.cbs[i] = i < g.nb ? g.cbs[i] : 0;
+        p.a_bc[i] = (i < g.nb && g.abs_[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+        p.b_bc[i] = (i < g.nb && g.bbs[i] != 0 && g.bsz[i] > 1) ? 1 : 0;
+    }
+    p.M = (int)g.M;
+    p.N = (int)g.N;
+    p.nk = (int)((g.K + TBK - 1) / TBK);
+    p.batch = g.batch();
+    p.timeout_ns = 2000000000ull;
+    p.err = err;
+    const int64_t gx = (g.N + TBN - 1) / TBN, gy = (g.M + TBM - 1) / TBM;
+    if (gy > 65535) return TLC_ERR_UNSUPPORTED;
+    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(p.batch < 65535 ? p.batch : 65535));
+    const int key = (ak ? 4 : 0) | (bkm ? 2 : 0) | (vc ? 1 : 0);
+    switch (key) {
+        case 0: return launch_tma_variant<false, false, false>(p, grid, s);
+        case 1: return launch_tma_variant<false, false, true>(p, grid, s);
+        case 2: return launch_tma_variant<false, true, false>(p, grid, s);
+        case 3: return launch_tma_variant<false, true, true>(p, grid, s);
+        case 4: return launch_tma_variant<true, false, false>(p, grid, s);
+        case 5: return launch_tma_variant<true, false, true>(p, grid, s);
+        case 6: return launch_tma_variant<true, true, false>(p, grid, s);
+        default: return launch_tma_variant<true, true, true>(p, grid, s);
+    }
+}
+
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <bool AK, bool BKM, bool VA, bool VB, bool VC>
@@ -263,6 +604,11 @@ int gemm_exact(const Gemm& g, cudaStream_t s) {
                     (bkm ? div4(g.K) && div4(g.b_cs) : div4(g.N) && div4(g.b_rs));
     const bool vc = aligned16(g.C) && bs_ok_c && div4(g.c_rs);
 
+    if (p.K > 0) {
+        const int st = gemm_exact_tma(g, ak, bkm, vc, s);
+        if (st != TLC_ERR_UNSUPPORTED) return st;
+        clear_error();
+    }
     const int64_t gx = (g.N + BN - 1) / BN, gy = (g.M + BM - 1) / BM;
     if (gy > 65535) return set_error(TLC_ERR_UNSUPPORTED, "gemm_exact: M too large");
     dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(p.batch < 65535 ? p.batch : 65535));

@@ -53,14 +53,12 @@
 // waiting thread raises a CTA-wide abort flag and a device error word, every
 // role leaves its loop, in-flight TMA copies and MMAs are drained (again with
 // a bound), the TMEM is freed, and the host reports TLC_ERR_TIMEOUT.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cstring>
 #include <mutex>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace tlc {
 
@@ -96,14 +94,6 @@ struct TcParams {
 
 // ---- PTX wrappers ---------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -118,31 +108,12 @@ __device__ __forceinline__ uint32_t mapa(uint32_t local, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
 }
 
 // Waits for the phase of `bar` with the given parity.  Gives up (returns
@@ -187,9 +158,6 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
             "r"(bar)
             : "memory");
     }
-}
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -790,19 +758,6 @@ __global__ void bounded_wait_selftest_kernel(uint64_t timeout_ns, int* err) {
 
 // ---- host side ------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
 
 // One operand as a 5-D tensor map: dims {inner, outer, batch0..2}.
 struct OperandMap {
@@ -816,41 +771,12 @@ struct OperandMap {
 };
 
 int encode(CUtensorMap* map, const OperandMap& o) {
-    auto fn = encode_fn();
-    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-    cuuint64_t dims[5], strides[4];
-    cuuint32_t box[5] = {o.box_inner, o.box_outer, 1, 1, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    dims[0] = (cuuint64_t)o.inner;
-    dims[1] = (cuuint64_t)o.outer;
-    strides[0] = (cuuint64_t)o.outer_stride * 4;
-    cuuint64_t prev = strides[0] * dims[1];
-    for (int i = 0; i < kMaxBatchDims; ++i) {
-        const bool real = o.bstride[i] != 0 && o.bsz[i] > 1;
-        dims[2 + i] = real ? (cuuint64_t)o.bsz[i] : 1;
-        strides[1 + i] = real ? (cuuint64_t)o.bstride[i] * 4 : ((prev + 15) & ~cuuint64_t(15));
-        prev = strides[1 + i] * dims[2 + i];
-    }
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(o.base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    o.mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(TLC_ERR_UNSUPPORTED,
-                         "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
-    return TLC_OK;
+    return encode_tiled(map, o.base, o.inner, o.outer, o.outer_stride, o.bsz, o.bstride,
+                        o.box_inner, o.box_outer,
+                        o.mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Whether TMA can read the operand in place: 16-byte aligned base and
-// strides that are multiples of 4 floats.
-bool tma_ok(const float* base, int64_t outer_stride, const int64_t* bstr, int nb) {
-    if (!al16(base) || (outer_stride & 3)) return false;
-    for (int i = 0; i < nb; ++i)
-        if (bstr[i] & 3) return false;
-    return true;
-}
 
 int64_t span_elems(int64_t inner, int64_t outer, int64_t os, const int64_t* bsz,
                    const int64_t* bstr, int nb) {

@@ -1,0 +1,115 @@
+// Tensor-map (TMA) and mbarrier helpers shared by the tensor-core kernel
+// (gemm_tc.cu) and the TMA-fed exact kernel (gemm_exact.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tlc {
+
+// ---- device side ----------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// TMA tile load of a 5-D box into this CTA's shared memory, completing on the
+// local barrier `bar`.
+__device__ __forceinline__ void tma_load_5d_local(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                  int c0, int c1, int c2, int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- host side --------------------------------------------------------------------
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// One fp32 operand as a 5-D tensor map: dims {inner, outer, batch0..2}, with
+// broadcast (stride 0) or absent batch dims collapsed to extent 1.  Strides
+// in elements.
+inline int encode_tiled(CUtensorMap* map, const float* base, int64_t inner, int64_t outer,
+                        int64_t outer_stride, const int64_t* bsz, const int64_t* bstride,
+                        uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    cuuint64_t dims[5], strides[4];
+    cuuint32_t box[5] = {box_inner, box_outer, 1, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    dims[0] = (cuuint64_t)inner;
+    dims[1] = (cuuint64_t)outer;
+    strides[0] = (cuuint64_t)outer_stride * 4;
+    cuuint64_t prev = strides[0] * dims[1];
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        const bool real = bstride[i] != 0 && bsz[i] > 1;
+        dims[2 + i] = real ? (cuuint64_t)bsz[i] : 1;
+        strides[1 + i] = real ? (cuuint64_t)bstride[i] * 4 : ((prev + 15) & ~cuuint64_t(15));
+        prev = strides[1 + i] * dims[2 + i];
+    }
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TLC_ERR_UNSUPPORTED,
+                         "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return TLC_OK;
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Whether TMA can read an operand in place: 16-byte aligned base and strides
+// that are multiples of 4 floats.
+inline bool tma_ok(const float* base, int64_t outer_stride, const int64_t* bstr, int nb) {
+    if (!al16(base) || (outer_stride & 3)) return false;
+    for (int i = 0; i < nb; ++i)
+        if (bstr[i] & 3) return false;
+    return true;
+}
+
+}  // namespace tlc
