@@ -229,7 +229,7 @@ constexpr int TBM = 128, TBN = 128, TBK = 32, TSTAGES = 3;
 constexpr int T_A_BYTES = TBM * TBK * 4;  // 16 KB
 constexpr int T_B_BYTES = TBN * TBK * 4;  // 16 KB
 constexpr int T_STAGE = T_A_BYTES + T_B_BYTES;
-constexpr int T_SMEM = TSTAGES * T_STAGE + 64 + 1024;  // + barriers, coordinates, alignment slack
+constexpr int T_SMEM = TSTAGES * T_STAGE + 256 + 1024;  // + barriers, cursor, alignment slack
 
 struct ExactTmaParams {
     CUtensorMap tmA, tmB;
@@ -246,22 +246,62 @@ struct ExactTmaParams {
     int* err;
 };
 
-// Bounded wait for the phase of `bar` with the given parity; records `site`
-// in the device error word on expiry (2 s: far above any legitimate wait).
-__device__ __forceinline__ bool exact_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
-                                           int* err) {
+// Packed fp32 pairs (sm_100 fma.rn.f32x2: two IEEE fused multiply-adds with
+// round-to-nearest in one instruction, each lane exactly fmaf).
+__device__ __forceinline__ uint64_t pack2(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& x, float& y) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
+}
+// d = a * b + d, element-wise on the pairs
+__device__ __forceinline__ void fma2(uint64_t& d, uint64_t a, uint64_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+
+// Bounded wait for the phase of `bar` with the given parity.  Gives up when
+// the CTA's abort flag is raised or the deadline passes (2 s: far above any
+// legitimate wait); on expiry it raises the flag and records `site` in the
+// device error word.
+__device__ __forceinline__ bool exact_wait(uint64_t* bar, uint32_t parity,
+                                           volatile int* abort_flag, uint64_t timeout_ns,
+                                           int* err, int site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 15) == 0 && globaltimer() - t0 > timeout_ns) {
-            atomicCAS(err, 0, 11);
-            return false;
+        if ((i & 15) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > timeout_ns) {
+                *abort_flag = 1;
+                atomicCAS(err, 0, site);
+                return false;
+            }
         }
     }
 }
 
+// Thread 0's load cursor (shared memory: it lives across the k-tile loop but
+// only thread 0 touches it, so it should not hold registers in every thread).
+struct IssueCursor {
+    int64_t entry;   // this CTA's entry number of the next load
+    int kt;          // its k-tile
+    int slot;        // ring slot of the next load
+    uint32_t phase;  // how often the ring wrapped before it (parity)
+    uint32_t pend, pend_par;  // slots with a load thread 0 has not seen complete, and their parity
+    int ca[kMaxBatchDims], cb[kMaxBatchDims];  // tensor-map batch coordinates of `entry`
+};
+
 // AK: A is K-major (row-major [M,K]); BKM: B is K-major ([N,K] storage).
+//
+// Each CTA walks a flat sequence of k-tiles: its batch entries blockIdx.z,
+// blockIdx.z + gridDim.z, ..., nk k-tiles each.  k-tile g lives in ring slot
+// g % TSTAGES.  full[s] completes when a slot's loads land; empty[s] when all
+// 8 warps finished reading it (one arrival per warp), and thread 0 waits on
+// it before reloading the slot.  So warps only wait for data, never for one
+// another at a CTA barrier.
 template <bool AK, bool BKM, bool VC>
 __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant__ ExactTmaParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -270,16 +310,26 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
     // keeps the compiler aware that these are shared-memory addresses, so
     // the tile reads compile to 32-bit-addressed shared loads.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TSTAGES * T_STAGE);
-    // thread 0's batch coordinates of the current entry: A's, then B's
-    int* coord = reinterpret_cast<int*>(full + TSTAGES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TSTAGES * T_STAGE);  // [TSTAGES]
+    uint64_t* empty = full + TSTAGES;                                        // [TSTAGES]
+    IssueCursor* cur = reinterpret_cast<IssueCursor*>(empty + TSTAGES);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(cur + 1);
 
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int wm = warp & 1, wn = warp >> 1;  // 2 x 4 warps of 64 x 32
     const int tm = lane >> 2, tn = lane & 3;  // 8 x 4 lanes of 8 x 8
     if (tid == 0) {
-        for (int s = 0; s < TSTAGES; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < TSTAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NT / 32);
+        }
+        *abort_flag = 0;
+        cur->entry = 0;
+        cur->kt = 0;
+        cur->slot = 0;
+        cur->phase = 0;
+        cur->pend = cur->pend_par = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         prefetch_map(&p.tmA);
@@ -288,77 +338,100 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
     __syncthreads();
 
     const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * TBN;
-    uint32_t it0 = 0;                 // k-tiles this CTA consumed before the current entry
-    uint32_t pend = 0, pend_par = 0;  // thread 0: slots with a load it has not seen complete
-    bool bad = false;
-    for (int64_t b = blockIdx.z; b < p.batch; b += gridDim.z) {
-        int64_t oc = 0;  // this entry's C offset
-        {
-            int bi[kMaxBatchDims];
-            int64_t r = b;
+    const int64_t n_entries = (p.batch - 1 - (int64_t)blockIdx.z) / gridDim.z + 1;
+    const int64_t total = n_entries * p.nk;
+
+    // Thread 0: load the next k-tile of the sequence into its slot, after the
+    // warps released the slot's previous k-tile (`wait_empty`).
+    auto issue_next = [&](bool wait_empty) -> bool {
+        IssueCursor& c = *cur;
+        if (wait_empty && !exact_wait(&empty[c.slot], c.phase ^ 1u, abort_flag, p.timeout_ns, p.err, 12))
+            return false;
+        if (c.kt == 0) {
+            int64_t r = (int64_t)blockIdx.z + c.entry * gridDim.z;
+#pragma unroll
+            for (int i = kMaxBatchDims - 1; i >= 0; --i) {
+                int idx = 0;
+                if (i < p.nb) {
+                    idx = (int)(r % p.bsz[i]);
+                    r /= p.bsz[i];
+                }
+                c.ca[i] = p.a_bc[i] ? idx : 0;
+                c.cb[i] = p.b_bc[i] ? idx : 0;
+            }
+        }
+        const int slot = c.slot;
+        uint8_t* sa = smem + slot * T_STAGE;
+        mbar_expect_tx(&full[slot], T_STAGE);
+        const int k0 = c.kt * TBK;
+        if (AK)
+            tma_load_5d_local(sa, &p.tmA, &full[slot], k0, m0, c.ca[0], c.ca[1], c.ca[2]);
+        else
+            tma_load_5d_local(sa, &p.tmA, &full[slot], m0, k0, c.ca[0], c.ca[1], c.ca[2]);
+        if (BKM)
+            tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], k0, n0, c.cb[0], c.cb[1], c.cb[2]);
+        else
+            tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], n0, k0, c.cb[0], c.cb[1], c.cb[2]);
+        c.pend |= 1u << slot;
+        c.pend_par = (c.pend_par & ~(1u << slot)) | (c.phase << slot);
+        if (++c.kt == p.nk) {
+            c.kt = 0;
+            ++c.entry;
+        }
+        if (++c.slot == TSTAGES) {
+            c.slot = 0;
+            c.phase ^= 1u;
+        }
+        return true;
+    };
+
+    bool ok = true;
+    if (tid == 0)
+        for (int64_t g = 0; g < TSTAGES - 1 && g < total; ++g) issue_next(false);  // fresh slots
+
+    // N-major B (PACKED): acc2[i][jp] holds row i, columns 2jp and 2jp + 1 of
+    // the thread's 8 as a packed pair for fma.rn.f32x2 (B's 16-byte groups
+    // give the column pairs, A's value is duplicated into both halves).  A
+    // K-major B has no column pairs in its loads: scalar FFMA into accs.
+    constexpr bool PACKED = !BKM;
+    uint64_t acc2[PACKED ? 8 : 1][PACKED ? 4 : 1];
+    float accs[PACKED ? 1 : 8][PACKED ? 1 : 8];
+    int64_t oc = 0;  // C offset of the current entry
+    int kt = 0;
+    int64_t entry = 0;
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int64_t g = 0; g < total; ++g) {
+        if (kt == 0) {
+            if constexpr (PACKED) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int jp = 0; jp < 4; ++jp) acc2[i][jp] = 0ull;  // +0.0f, +0.0f
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) accs[i][j] = 0.f;
+            }
+            int64_t r = (int64_t)blockIdx.z + entry * gridDim.z;
+            oc = 0;
 #pragma unroll
             for (int i = kMaxBatchDims - 1; i >= 0; --i) {
                 if (i < p.nb) {
-                    bi[i] = (int)(r % p.bsz[i]);
+                    oc += (r % p.bsz[i]) * p.cbs[i];
                     r /= p.bsz[i];
-                } else {
-                    bi[i] = 0;
                 }
-                oc += (int64_t)bi[i] * p.cbs[i];
             }
-            if (tid == 0)
-#pragma unroll
-                for (int i = 0; i < kMaxBatchDims; ++i) {
-                    coord[i] = p.a_bc[i] ? bi[i] : 0;
-                    coord[3 + i] = p.b_bc[i] ? bi[i] : 0;
-                }
         }
-        // Thread 0: load k-tile kt of this entry into its slot.
-        auto issue = [&](int kt) {
-            const uint32_t g = it0 + (uint32_t)kt;
-            const int slot = (int)(g % TSTAGES);
-            uint8_t* sa = smem + slot * T_STAGE;
-            mbar_expect_tx(&full[slot], T_STAGE);
-            const int k0 = kt * TBK;
-            if (AK)
-                tma_load_5d_local(sa, &p.tmA, &full[slot], k0, m0, coord[0], coord[1], coord[2]);
-            else
-                tma_load_5d_local(sa, &p.tmA, &full[slot], m0, k0, coord[0], coord[1], coord[2]);
-            if (BKM)
-                tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], k0, n0, coord[3], coord[4],
-                                  coord[5]);
-            else
-                tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], n0, k0, coord[3], coord[4],
-                                  coord[5]);
-            pend |= 1u << slot;
-            pend_par = (pend_par & ~(1u << slot)) | (((g / TSTAGES) & 1u) << slot);
-        };
-        // Slots of earlier entries are free: every thread passed the barrier
-        // after its last k-tile, except for the last slot, which this
-        // prologue does not touch.
-        if (tid == 0)
-            for (int kt = 0; kt < TSTAGES - 1 && kt < p.nk; ++kt) issue(kt);
-
-        float acc[8][8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-
-        for (int kt = 0; kt < p.nk; ++kt) {
-            // Everyone is done with k-tile kt-1, whose slot the next load reuses.
-            if (__syncthreads_or(bad)) {
-                bad = true;
-                break;
-            }
-            if (tid == 0 && kt + TSTAGES - 1 < p.nk) issue(kt + TSTAGES - 1);
-            const uint32_t g = it0 + (uint32_t)kt;
-            const int slot = (int)(g % TSTAGES);
-            if (!exact_wait(&full[slot], (g / TSTAGES) & 1u, p.timeout_ns, p.err)) {
-                bad = true;
-                continue;
-            }
-            if (tid == 0) pend &= ~(1u << slot);
+        // k-tile g + TSTAGES - 1 reuses the slot of k-tile g - 1
+        if (tid == 0 && g + TSTAGES - 1 < total && !issue_next(g >= 1)) ok = false;
+        if (!ok || !exact_wait(&full[slot], phase, abort_flag, p.timeout_ns, p.err, 11)) {
+            ok = false;
+            break;
+        }
+        if (tid == 0) cur->pend &= ~(1u << slot);
+        {
             const uint8_t* sa = smem + slot * T_STAGE;
             const uint8_t* sb = sa + T_A_BYTES;
 #pragma unroll 2
@@ -386,11 +459,10 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
                         a[4][u] = y.x; a[5][u] = y.y; a[6][u] = y.z; a[7][u] = y.w;
                     }
                 }
-#pragma unroll
                 for (int h = 0; h < 2; ++h) {  // k = 4q + 2h, 4q + 2h + 1
-                    float bv[8][2];
+                    float bv[8][2];  // bv[j][t] = B[4q + 2h + t][column j]
                     if (BKM) {
-                        // column c = wn*32 + tn + 4j (c % 8 == tn + 4 (j % 2))
+                        // column c = wn*32 + tn + 4j (c % 8 == tn + 4 (j % 2)): 8 bytes of chunk q
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const int c7 = tn + 4 * (j & 1);
@@ -411,34 +483,58 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
                         }
                     }
 #pragma unroll
-                    for (int t = 0; t < 2; ++t)
+                    for (int t = 0; t < 2; ++t) {  // one k
+                        if constexpr (PACKED) {
+                            // 32 packed FMAs: columns (2jp, 2jp + 1) of the 16-byte B groups
+                            uint64_t bp[4];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
+                            for (int jp = 0; jp < 4; ++jp) bp[jp] = pack2(bv[2 * jp][t], bv[2 * jp + 1][t]);
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                acc[i][j] = fmaf(a[i][2 * h + t], bv[j][t], acc[i][j]);
+                            for (int i = 0; i < 8; ++i) {
+                                const uint64_t ad = pack2(a[i][2 * h + t], a[i][2 * h + t]);
+#pragma unroll
+                                for (int jp = 0; jp < 4; ++jp) fma2(acc2[i][jp], ad, bp[jp]);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    accs[i][j] = fmaf(a[i][2 * h + t], bv[j][t], accs[i][j]);
+                        }
+                    }
                 }
             }
         }
-        // One decision for the whole CTA: a thread that timed out on the last
-        // k-tile must not leave while the others go on to the next entry.
-        if (__syncthreads_or(bad)) {
-            bad = true;
-            break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done with the slot
+        if (++slot == TSTAGES) {
+            slot = 0;
+            phase ^= 1u;
         }
-        it0 += (uint32_t)p.nk;
+        if (++kt < p.nk) continue;
+        kt = 0;
+        ++entry;
 
         float* Cb = p.C + oc;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int row = m0 + wm * 64 + (AK ? tm + 8 * i : (i < 4 ? tm * 4 + i : 32 + tm * 4 + (i - 4)));
             if (row >= p.M) continue;
+            float acc[8];
+            if constexpr (PACKED) {
+#pragma unroll
+                for (int jp = 0; jp < 4; ++jp) unpack2(acc2[i][jp], acc[2 * jp], acc[2 * jp + 1]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = accs[i][j];
+            }
             float* crow = Cb + (int64_t)row * p.c_rs;
             if (BKM) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const int col = n0 + wn * 32 + tn + 4 * j;
-                    if (col < p.N) crow[col] = acc[i][j];
+                    if (col < p.N) crow[col] = acc[j];
                 }
             } else {
 #pragma unroll
@@ -446,18 +542,19 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
                     const int col = n0 + wn * 32 + h * 16 + tn * 4;
                     if (VC && col + 3 < p.N) {
                         *reinterpret_cast<float4*>(crow + col) = make_float4(
-                            acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+                            acc[4 * h + 0], acc[4 * h + 1], acc[4 * h + 2], acc[4 * h + 3]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            if (col + j < p.N) crow[col + j] = acc[i][4 * h + j];
+                            if (col + j < p.N) crow[col + j] = acc[4 * h + j];
                     }
                 }
             }
         }
     }
-    if (bad && tid == 0) {
+    if (!ok && tid == 0) {
         // Drain: wait (bounded) for loads still in flight into shared memory.
+        const uint32_t pend = cur->pend, pend_par = cur->pend_par;
         for (int s = 0; s < TSTAGES; ++s) {
             if (!(pend & (1u << s))) continue;
             const uint64_t t0 = globaltimer();
