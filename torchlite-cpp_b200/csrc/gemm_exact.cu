@@ -15,20 +15,25 @@
 // Two kernels, one contract:
 //
 // exact_tma_kernel (operands TMA-readable: 16-byte aligned, strides multiples
-// of 4 floats).  128x128 output tile per CTA, 256 threads in 2 x 4 warps of
-// 64 x 32, each thread an 8 x 8 register tile.  k-tiles of 32 stream into a
-// 3-stage shared-memory ring with cp.async.bulk.tensor, one mbarrier per
-// stage; thread 0 issues the loads and a CTA barrier per k-tile guards slot
-// reuse, so the FFMA loop carries no global loads, shared stores or address
-// arithmetic.  Each operand keeps its memory layout in shared memory:
+// of 4 floats).  256 threads in 2 x 4 warps; k-tiles of 32 stream into a ring
+// of shared-memory stages with cp.async.bulk.tensor, one "full" mbarrier per
+// stage, and one "empty" mbarrier per stage that every warp arrives on when
+// done with it; thread 0 issues the loads.  The FFMA loop carries no global
+// loads, shared stores or address arithmetic, and warps never meet at a CTA
+// barrier.  Each operand keeps its memory layout in shared memory:
 //   K-major tile ([rows][32 k], a row-major A or the W^T view of a B):
 //     128-byte rows with the 128-byte swizzle (16-byte chunk c of row r at
 //     c ^ (r % 8)); a thread's 8 rows are 8 apart (its 8 B columns 4 apart),
 //     so a warp's 16-byte reads of 4 k-values (8-byte reads of 2 for B) hit
 //     distinct chunks: no bank conflicts.
-//   MN-major tile ([32 k][128 rows], an M-major A or a row-major B):
-//     dense; a warp reads consecutive 16-byte groups along m / n.
-// Two CTAs per SM (99 KB of shared memory and <= 128 registers each).
+//   MN-major tile ([32 k][rows], an M-major A or a row-major B): dense; a
+//     warp reads consecutive 16-byte groups along m / n.
+// With an N-major B the inner product runs on sm_100's packed fma.rn.f32x2
+// (two IEEE fmaf per instruction, same rounding, so the chains stay
+// bit-identical), on 128 x 256 tiles (8 x 16 per thread, one CTA per SM, four
+// stages) when N >= 256, else 128 x 128.  With a K-major B (no column pairs in
+// its loads) it is scalar FFMA.  128 x 128 tiles run 8 x 8 per thread, two
+// CTAs per SM, three stages.
 //
 // exact_kernel (any other strides).  128x128 tile, k-tiles of 16, 256
 // threads, 8x8 per thread; global loads go through registers into a double-
@@ -225,11 +230,23 @@ __global__ void __launch_bounds__(NT, 2) exact_kernel(ExactParams p) {
 
 // ---- TMA-fed kernel ------------------------------------------------------------------
 
-constexpr int TBM = 128, TBN = 128, TBK = 32, TSTAGES = 3;
-constexpr int T_A_BYTES = TBM * TBK * 4;  // 16 KB
-constexpr int T_B_BYTES = TBN * TBK * 4;  // 16 KB
-constexpr int T_STAGE = T_A_BYTES + T_B_BYTES;
-constexpr int T_SMEM = TSTAGES * T_STAGE + 256 + 1024;  // + barriers, cursor, alignment slack
+constexpr int TBM = 128, TBK = 32;
+
+// Tile shapes.  WIDE (N-major B): 128 x 256 output tile, thread tile 8 x 16,
+// one CTA per SM with a 4-stage ring (4 x 48 KB).  Otherwise (K-major B):
+// 128 x 128, thread tile 8 x 8, two CTAs per SM with 3-stage rings (3 x 32 KB).
+template <bool WIDE>
+struct TmaCfg {
+    static constexpr int BN = WIDE ? 256 : 128;
+    static constexpr int NJ = WIDE ? 16 : 8;     // columns per thread
+    static constexpr int WN = BN / 4;            // columns per warp (4 warps across)
+    static constexpr int STAGES = WIDE ? 4 : 3;
+    static constexpr int MIN_BLOCKS = WIDE ? 1 : 2;
+    static constexpr int A_BYTES = TBM * TBK * 4;
+    static constexpr int B_BYTES = BN * TBK * 4;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int SMEM = STAGES * STAGE + 256 + 1024;  // + barriers, cursor, alignment slack
+};
 
 struct ExactTmaParams {
     CUtensorMap tmA, tmB;
@@ -294,33 +311,49 @@ struct IssueCursor {
     int ca[kMaxBatchDims], cb[kMaxBatchDims];  // tensor-map batch coordinates of `entry`
 };
 
-// AK: A is K-major (row-major [M,K]); BKM: B is K-major ([N,K] storage).
+// AK: A is K-major (row-major [M,K]); BKM: B is K-major ([N,K] storage);
+// WIDE: 128 x 256 tiles (N-major B only; see TmaCfg).
 //
 // Each CTA walks a flat sequence of k-tiles: its batch entries blockIdx.z,
 // blockIdx.z + gridDim.z, ..., nk k-tiles each.  k-tile g lives in ring slot
-// g % TSTAGES.  full[s] completes when a slot's loads land; empty[s] when all
+// g % STAGES.  full[s] completes when a slot's loads land; empty[s] when all
 // 8 warps finished reading it (one arrival per warp), and thread 0 waits on
 // it before reloading the slot.  So warps only wait for data, never for one
 // another at a CTA barrier.
-template <bool AK, bool BKM, bool VC>
-__global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant__ ExactTmaParams p) {
+//
+// Thread (warp wm, wn; lane tm, tn) rows: wm*64 + tm + 8i when A is K-major,
+// wm*64 + {tm*4, 32 + tm*4} + 0..3 when M-major.  Columns: wn*WN + 16g +
+// tn*4 + 0..3 (g < NJ/4) for an N-major B, wn*32 + tn + 4j for a K-major B.
+//
+// N-major B (packed): the product runs on fma.rn.f32x2.  acc2[i][jp] holds row
+// i, columns 2jp and 2jp + 1 of the thread's NJ as a pair; B's 16-byte groups
+// give the column pairs, A's value is duplicated into both halves (one move
+// per A value and k, shared by NJ/2 packed FMAs).  A K-major B has no column
+// pairs in its loads: scalar FFMA into accs.
+template <bool AK, bool BKM, bool VC, bool WIDE>
+__global__ void __launch_bounds__(NT, TmaCfg<WIDE>::MIN_BLOCKS)
+    exact_tma_kernel(const __grid_constant__ ExactTmaParams p) {
+    static_assert(!(WIDE && BKM), "wide tiles need an N-major B");
+    constexpr bool PACKED = !BKM;
+    using S = TmaCfg<WIDE>;
+    constexpr int STAGES = S::STAGES, NJ = S::NJ, NJP = S::NJ / 2;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment: the 128-byte swizzle pattern repeats every 8 rows.
     // Offsetting the shared array itself (no round trip through an integer)
     // keeps the compiler aware that these are shared-memory addresses, so
     // the tile reads compile to 32-bit-addressed shared loads.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TSTAGES * T_STAGE);  // [TSTAGES]
-    uint64_t* empty = full + TSTAGES;                                        // [TSTAGES]
-    IssueCursor* cur = reinterpret_cast<IssueCursor*>(empty + TSTAGES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE);  // [STAGES]
+    uint64_t* empty = full + STAGES;                                        // [STAGES]
+    IssueCursor* cur = reinterpret_cast<IssueCursor*>(empty + STAGES);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(cur + 1);
 
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
-    const int wm = warp & 1, wn = warp >> 1;  // 2 x 4 warps of 64 x 32
-    const int tm = lane >> 2, tn = lane & 3;  // 8 x 4 lanes of 8 x 8
+    const int wm = warp & 1, wn = warp >> 1;  // 2 x 4 warps
+    const int tm = lane >> 2, tn = lane & 3;  // 8 x 4 lanes
     if (tid == 0) {
-        for (int s = 0; s < TSTAGES; ++s) {
+        for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NT / 32);
         }
@@ -337,7 +370,7 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
     }
     __syncthreads();
 
-    const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * TBN;
+    const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * S::BN;
     const int64_t n_entries = (p.batch - 1 - (int64_t)blockIdx.z) / gridDim.z + 1;
     const int64_t total = n_entries * p.nk;
 
@@ -361,24 +394,24 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
             }
         }
         const int slot = c.slot;
-        uint8_t* sa = smem + slot * T_STAGE;
-        mbar_expect_tx(&full[slot], T_STAGE);
+        uint8_t* sa = smem + slot * S::STAGE;
+        mbar_expect_tx(&full[slot], S::STAGE);
         const int k0 = c.kt * TBK;
         if (AK)
             tma_load_5d_local(sa, &p.tmA, &full[slot], k0, m0, c.ca[0], c.ca[1], c.ca[2]);
         else
             tma_load_5d_local(sa, &p.tmA, &full[slot], m0, k0, c.ca[0], c.ca[1], c.ca[2]);
         if (BKM)
-            tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], k0, n0, c.cb[0], c.cb[1], c.cb[2]);
+            tma_load_5d_local(sa + S::A_BYTES, &p.tmB, &full[slot], k0, n0, c.cb[0], c.cb[1], c.cb[2]);
         else
-            tma_load_5d_local(sa + T_A_BYTES, &p.tmB, &full[slot], n0, k0, c.cb[0], c.cb[1], c.cb[2]);
+            tma_load_5d_local(sa + S::A_BYTES, &p.tmB, &full[slot], n0, k0, c.cb[0], c.cb[1], c.cb[2]);
         c.pend |= 1u << slot;
         c.pend_par = (c.pend_par & ~(1u << slot)) | (c.phase << slot);
         if (++c.kt == p.nk) {
             c.kt = 0;
             ++c.entry;
         }
-        if (++c.slot == TSTAGES) {
+        if (++c.slot == STAGES) {
             c.slot = 0;
             c.phase ^= 1u;
         }
@@ -387,15 +420,10 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
 
     bool ok = true;
     if (tid == 0)
-        for (int64_t g = 0; g < TSTAGES - 1 && g < total; ++g) issue_next(false);  // fresh slots
+        for (int64_t g = 0; g < STAGES - 1 && g < total; ++g) issue_next(false);  // fresh slots
 
-    // N-major B (PACKED): acc2[i][jp] holds row i, columns 2jp and 2jp + 1 of
-    // the thread's 8 as a packed pair for fma.rn.f32x2 (B's 16-byte groups
-    // give the column pairs, A's value is duplicated into both halves).  A
-    // K-major B has no column pairs in its loads: scalar FFMA into accs.
-    constexpr bool PACKED = !BKM;
-    uint64_t acc2[PACKED ? 8 : 1][PACKED ? 4 : 1];
-    float accs[PACKED ? 1 : 8][PACKED ? 1 : 8];
+    uint64_t acc2[PACKED ? 8 : 1][PACKED ? NJP : 1];
+    float accs[PACKED ? 1 : 8][PACKED ? 1 : NJ];
     int64_t oc = 0;  // C offset of the current entry
     int kt = 0;
     int64_t entry = 0;
@@ -407,12 +435,12 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
 #pragma unroll
-                    for (int jp = 0; jp < 4; ++jp) acc2[i][jp] = 0ull;  // +0.0f, +0.0f
+                    for (int jp = 0; jp < NJP; ++jp) acc2[i][jp] = 0ull;  // +0.0f, +0.0f
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) accs[i][j] = 0.f;
+                    for (int j = 0; j < NJ; ++j) accs[i][j] = 0.f;
             }
             int64_t r = (int64_t)blockIdx.z + entry * gridDim.z;
             oc = 0;
@@ -424,16 +452,16 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
                 }
             }
         }
-        // k-tile g + TSTAGES - 1 reuses the slot of k-tile g - 1
-        if (tid == 0 && g + TSTAGES - 1 < total && !issue_next(g >= 1)) ok = false;
+        // k-tile g + STAGES - 1 reuses the slot of k-tile g - 1
+        if (tid == 0 && g + STAGES - 1 < total && !issue_next(g >= 1)) ok = false;
         if (!ok || !exact_wait(&full[slot], phase, abort_flag, p.timeout_ns, p.err, 11)) {
             ok = false;
             break;
         }
         if (tid == 0) cur->pend &= ~(1u << slot);
         {
-            const uint8_t* sa = smem + slot * T_STAGE;
-            const uint8_t* sb = sa + T_A_BYTES;
+            const uint8_t* sa = smem + slot * S::STAGE;
+            const uint8_t* sb = sa + S::A_BYTES;
 #pragma unroll 2
             for (int q = 0; q < TBK / 4; ++q) {  // groups of 4 k, ascending
                 // A: a[i][u] = A[row i][4q + u]
@@ -459,56 +487,51 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
                         a[4][u] = y.x; a[5][u] = y.y; a[6][u] = y.z; a[7][u] = y.w;
                     }
                 }
-                for (int h = 0; h < 2; ++h) {  // k = 4q + 2h, 4q + 2h + 1
-                    float bv[8][2];  // bv[j][t] = B[4q + 2h + t][column j]
-                    if (BKM) {
+                if constexpr (PACKED) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {  // one k: 8 x NJP packed FMAs
+                        const uint8_t* pb = sb + (4 * q + u) * (S::BN * 4) + (wn * S::WN + tn * 4) * 4;
+                        uint64_t bp[NJP];
+#pragma unroll
+                        for (int g4 = 0; g4 < NJ / 4; ++g4) {
+                            const float4 x = *reinterpret_cast<const float4*>(pb + g4 * 16 * 4);
+                            bp[2 * g4] = pack2(x.x, x.y);
+                            bp[2 * g4 + 1] = pack2(x.z, x.w);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const uint64_t ad = pack2(a[i][u], a[i][u]);
+#pragma unroll
+                            for (int jp = 0; jp < NJP; ++jp) fma2(acc2[i][jp], ad, bp[jp]);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {  // k = 4q + 2h, 4q + 2h + 1
                         // column c = wn*32 + tn + 4j (c % 8 == tn + 4 (j % 2)): 8 bytes of chunk q
+                        float bv[8][2];
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const int c7 = tn + 4 * (j & 1);
                             const float2 v = *reinterpret_cast<const float2*>(
-                                sb + (wn * 32 + tn + 4 * j) * 128 + ((q ^ c7) << 4) + h * 8);
+                                sb + (wn * S::WN + tn + 4 * j) * 128 + ((q ^ c7) << 4) + h * 8);
                             bv[j][0] = v.x;
                             bv[j][1] = v.y;
                         }
-                    } else {
 #pragma unroll
-                        for (int t = 0; t < 2; ++t) {
-                            const uint8_t* pb =
-                                sb + (4 * q + 2 * h + t) * (TBN * 4) + (wn * 32 + tn * 4) * 4;
-                            const float4 x = *reinterpret_cast<const float4*>(pb);
-                            const float4 y = *reinterpret_cast<const float4*>(pb + 16 * 4);
-                            bv[0][t] = x.x; bv[1][t] = x.y; bv[2][t] = x.z; bv[3][t] = x.w;
-                            bv[4][t] = y.x; bv[5][t] = y.y; bv[6][t] = y.z; bv[7][t] = y.w;
-                        }
-                    }
-#pragma unroll
-                    for (int t = 0; t < 2; ++t) {  // one k
-                        if constexpr (PACKED) {
-                            // 32 packed FMAs: columns (2jp, 2jp + 1) of the 16-byte B groups
-                            uint64_t bp[4];
-#pragma unroll
-                            for (int jp = 0; jp < 4; ++jp) bp[jp] = pack2(bv[2 * jp][t], bv[2 * jp + 1][t]);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const uint64_t ad = pack2(a[i][2 * h + t], a[i][2 * h + t]);
-#pragma unroll
-                                for (int jp = 0; jp < 4; ++jp) fma2(acc2[i][jp], ad, bp[jp]);
-                            }
-                        } else {
+                        for (int t = 0; t < 2; ++t)
 #pragma unroll
                             for (int i = 0; i < 8; ++i)
 #pragma unroll
                                 for (int j = 0; j < 8; ++j)
                                     accs[i][j] = fmaf(a[i][2 * h + t], bv[j][t], accs[i][j]);
-                        }
                     }
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done with the slot
-        if (++slot == TSTAGES) {
+        if (++slot == STAGES) {
             slot = 0;
             phase ^= 1u;
         }
@@ -521,33 +544,27 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
         for (int i = 0; i < 8; ++i) {
             const int row = m0 + wm * 64 + (AK ? tm + 8 * i : (i < 4 ? tm * 4 + i : 32 + tm * 4 + (i - 4)));
             if (row >= p.M) continue;
-            float acc[8];
+            float* crow = Cb + (int64_t)row * p.c_rs;
             if constexpr (PACKED) {
 #pragma unroll
-                for (int jp = 0; jp < 4; ++jp) unpack2(acc2[i][jp], acc[2 * jp], acc[2 * jp + 1]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = accs[i][j];
-            }
-            float* crow = Cb + (int64_t)row * p.c_rs;
-            if (BKM) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int col = n0 + wn * 32 + tn + 4 * j;
-                    if (col < p.N) crow[col] = acc[j];
-                }
-            } else {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int col = n0 + wn * 32 + h * 16 + tn * 4;
+                for (int g4 = 0; g4 < NJ / 4; ++g4) {
+                    float v[4];
+                    unpack2(acc2[i][2 * g4], v[0], v[1]);
+                    unpack2(acc2[i][2 * g4 + 1], v[2], v[3]);
+                    const int col = n0 + wn * S::WN + g4 * 16 + tn * 4;
                     if (VC && col + 3 < p.N) {
-                        *reinterpret_cast<float4*>(crow + col) = make_float4(
-                            acc[4 * h + 0], acc[4 * h + 1], acc[4 * h + 2], acc[4 * h + 3]);
+                        *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            if (col + j < p.N) crow[col + j] = acc[4 * h + j];
+                            if (col + j < p.N) crow[col + j] = v[j];
                     }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int col = n0 + wn * S::WN + tn + 4 * j;
+                    if (col < p.N) crow[col] = accs[i][j];
                 }
             }
         }
@@ -555,7 +572,7 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
     if (!ok && tid == 0) {
         // Drain: wait (bounded) for loads still in flight into shared memory.
         const uint32_t pend = cur->pend, pend_par = cur->pend_par;
-        for (int s = 0; s < TSTAGES; ++s) {
+        for (int s = 0; s < STAGES; ++s) {
             if (!(pend & (1u << s))) continue;
             const uint64_t t0 = globaltimer();
             while (!mbar_try_wait(&full[s], (pend_par >> s) & 1u) &&
@@ -565,18 +582,19 @@ __global__ void __launch_bounds__(NT, 2) exact_tma_kernel(const __grid_constant_
     }
 }
 
-template <bool AK, bool BKM, bool VC>
+template <bool AK, bool BKM, bool VC, bool WIDE>
 int launch_tma_variant(const ExactTmaParams& p, dim3 grid, cudaStream_t s) {
-    auto kernel = exact_tma_kernel<AK, BKM, VC>;
+    using S = TmaCfg<WIDE>;
+    auto kernel = exact_tma_kernel<AK, BKM, VC, WIDE>;
     static int configured[64] = {};
     int dev = 0;
     TLC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
     if (!configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T_SMEM));
+        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
         configured[dev] = 1;
     }
-    kernel<<<grid, NT, T_SMEM, s>>>(p);
+    kernel<<<grid, NT, S::SMEM, s>>>(p);
     count_launch();
     return check_launch("gemm_exact_tma");
 }
@@ -589,6 +607,10 @@ int gemm_exact_tma(const Gemm& g, bool ak, bool bkm, bool vc, cudaStream_t s) {
         if (g.bsz[i] > INT32_MAX) return TLC_ERR_UNSUPPORTED;
     const int64_t a_os = ak ? g.a_rs : g.a_cs, b_os = bkm ? g.b_cs : g.b_rs;
     if (!tma_ok(g.A, a_os, g.abs_, g.nb) || !tma_ok(g.B, b_os, g.bbs, g.nb)) return TLC_ERR_UNSUPPORTED;
+    // 256-column tiles for an N-major B at least that wide (a narrower B
+    // would leave most of a wide tile idle)
+    const bool wide = !bkm && g.N >= 256;
+    const int bn = wide ? TmaCfg<true>::BN : TmaCfg<false>::BN;
     int* err = nullptr;
     TLC_TRY(tc_error_word(&err));
     ExactTmaParams p;
@@ -601,14 +623,15 @@ int gemm_exact_tma(const Gemm& g, bool ak, bool bkm, bool vc, cudaStream_t s) {
         bbst[i] = g.bbs[i];
     }
     // A K-major: {K, M} boxes {32, 128}, swizzled; M-major: {M, K} boxes {128, 32}.
+    // B K-major: {K, N} boxes {32, 128}, swizzled; N-major: {N, K} boxes {256, 32}.
     if (ak)
         TLC_TRY(encode_tiled(&p.tmA, g.A, g.K, g.M, a_os, bsz, abst, TBK, TBM, CU_TENSOR_MAP_SWIZZLE_128B));
     else
         TLC_TRY(encode_tiled(&p.tmA, g.A, g.M, g.K, a_os, bsz, abst, TBM, TBK, CU_TENSOR_MAP_SWIZZLE_NONE));
     if (bkm)
-        TLC_TRY(encode_tiled(&p.tmB, g.B, g.K, g.N, b_os, bsz, bbst, TBK, TBN, CU_TENSOR_MAP_SWIZZLE_128B));
+        TLC_TRY(encode_tiled(&p.tmB, g.B, g.K, g.N, b_os, bsz, bbst, TBK, bn, CU_TENSOR_MAP_SWIZZLE_128B));
     else
-        TLC_TRY(encode_tiled(&p.tmB, g.B, g.N, g.K, b_os, bsz, bbst, TBN, TBK, CU_TENSOR_MAP_SWIZZLE_NONE));
+        TLC_TRY(encode_tiled(&p.tmB, g.B, g.N, g.K, b_os, bsz, bbst, bn, TBK, CU_TENSOR_MAP_SWIZZLE_NONE));
     p.C = g.C;
     p.c_rs = g.c_rs;
     p.nb = g.nb;
@@ -624,22 +647,25 @@ int gemm_exact_tma(const Gemm& g, bool ak, bool bkm, bool vc, cudaStream_t s) {
     p.batch = g.batch();
     p.timeout_ns = 2000000000ull;
     p.err = err;
-    const int64_t gx = (g.N + TBN - 1) / TBN, gy = (g.M + TBM - 1) / TBM;
+    const int64_t gx = (g.N + bn - 1) / bn, gy = (g.M + TBM - 1) / TBM;
     if (gy > 65535) return TLC_ERR_UNSUPPORTED;
     dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(p.batch < 65535 ? p.batch : 65535));
-    const int key = (ak ? 4 : 0) | (bkm ? 2 : 0) | (vc ? 1 : 0);
+    const int key = (wide ? 8 : 0) | (ak ? 4 : 0) | (bkm ? 2 : 0) | (vc ? 1 : 0);
     switch (key) {
-        case 0: return launch_tma_variant<false, false, false>(p, grid, s);
-        case 1: return launch_tma_variant<false, false, true>(p, grid, s);
-        case 2: return launch_tma_variant<false, true, false>(p, grid, s);
-        case 3: return launch_tma_variant<false, true, true>(p, grid, s);
-        case 4: return launch_tma_variant<true, false, false>(p, grid, s);
-        case 5: return launch_tma_variant<true, false, true>(p, grid, s);
-        case 6: return launch_tma_variant<true, true, false>(p, grid, s);
-        default: return launch_tma_variant<true, true, true>(p, grid, s);
+        case 0: return launch_tma_variant<false, false, false, false>(p, grid, s);
+        case 1: return launch_tma_variant<false, false, true, false>(p, grid, s);
+        case 2: return launch_tma_variant<false, true, false, false>(p, grid, s);
+        case 3: return launch_tma_variant<false, true, true, false>(p, grid, s);
+        case 4: return launch_tma_variant<true, false, false, false>(p, grid, s);
+        case 5: return launch_tma_variant<true, false, true, false>(p, grid, s);
+        case 6: return launch_tma_variant<true, true, false, false>(p, grid, s);
+        case 7: return launch_tma_variant<true, true, true, false>(p, grid, s);
+        case 8: return launch_tma_variant<false, false, false, true>(p, grid, s);
+        case 9: return launch_tma_variant<false, false, true, true>(p, grid, s);
+        case 12: return launch_tma_variant<true, false, false, true>(p, grid, s);
+        default: return launch_tma_variant<true, false, true, true>(p, grid, s);
     }
 }
-
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
