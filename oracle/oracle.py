@@ -52,6 +52,10 @@ def lib():
         L.orc_sum_dim.restype = None
         L.orc_add.argtypes = [_f32p, _f32p, _f32p, _i64]
         L.orc_add.restype = None
+        L.orc_softmax.argtypes = [_f32p, _f32p, _i64, _i64]
+        L.orc_softmax.restype = None
+        L.orc_softmax_backward.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, _i64]
+        L.orc_softmax_backward.restype = None
         _lib = L
     return _lib
 
@@ -188,6 +192,51 @@ def add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return out
 
 
+def add_bcast(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """tl::add with NumPy broadcasting (src/ops.cpp:74-103): one fp32 add per
+    output element, operands picked by get_broadcast_index (src/ops.cpp:32-52).
+    numpy's float32 add is the same correctly rounded addition."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    broadcast_shape(a.shape, b.shape)  # the reference's error for incompatible shapes
+    return np.add(a, b, dtype=np.float32)
+
+
+def scale(x: np.ndarray, s: float) -> np.ndarray:
+    """tl::scale (src/ops.cpp:963-983): out = x * s in fp32."""
+    return np.multiply(np.asarray(x, np.float32), np.float32(s), dtype=np.float32)
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    """tl::softmax over the last dim (src/ops.cpp:985-1037)."""
+    x = np.ascontiguousarray(x, np.float32)
+    if x.ndim == 0:
+        raise ValueError("Softmax requires at least 1D tensor")
+    out = np.empty_like(x)
+    D = x.shape[-1]
+    if D == 0 or x.size == 0:
+        return out
+    lib().orc_softmax(_fp(x), _fp(out), x.size // D, D)
+    return out
+
+
+# SoftmaxBackward's row dot as the reference's Release build rounds it: blocks
+# of SOFTMAX_BWD_VEC products rounded then added, the D mod SOFTMAX_BWD_VEC tail
+# fused (8: the x86-64-v4 / AVX-512 build, the ISA of the GPU hosts).
+SOFTMAX_BWD_VEC = 8
+
+
+def softmax_backward(grad: np.ndarray, y: np.ndarray, vec: int = SOFTMAX_BWD_VEC) -> np.ndarray:
+    """SoftmaxBackward (src/autograd.cpp:228-256) given the forward output y."""
+    g = np.ascontiguousarray(grad, np.float32)
+    y = np.ascontiguousarray(y, np.float32)
+    out = np.empty_like(y)
+    D = y.shape[-1] if y.ndim else 1
+    if y.size:
+        lib().orc_softmax_backward(_fp(g), _fp(y), _fp(out), y.size // D, D, vec)
+    return out
+
+
 def matmul_backward(grad: np.ndarray, a: np.ndarray, b: np.ndarray, nthreads: int | None = None):
     """MatmulBackward::backward, src/autograd.cpp:341-384, followed by
     accumulate_grad into empty grads (src/autograd.cpp:16-22: zeros + d).
@@ -256,6 +305,16 @@ class TLRef:
                                             i64p, _f32p, _i64, _f32p, _i64, ctypes.c_char_p,
                                             ctypes.c_int]
         L.tlref_matmul_backward.restype = ctypes.c_int
+        L.tlref_add.argtypes = [_f32p, ctypes.c_int, i64p, _f32p, ctypes.c_int, i64p, _f32p,
+                                _i64, ctypes.POINTER(ctypes.c_int), i64p, ctypes.c_char_p,
+                                ctypes.c_int]
+        L.tlref_add.restype = ctypes.c_int
+        L.tlref_scale.argtypes = [_f32p, ctypes.c_int, i64p, ctypes.c_float, _f32p, _i64,
+                                  ctypes.c_char_p, ctypes.c_int]
+        L.tlref_scale.restype = ctypes.c_int
+        L.tlref_softmax.argtypes = [_f32p, ctypes.c_int, i64p, _f32p, _f32p, _f32p, _i64,
+                                    ctypes.c_char_p, ctypes.c_int]
+        L.tlref_softmax.restype = ctypes.c_int
         self.L = L
 
     def hardware_threads(self) -> int:
@@ -303,6 +362,49 @@ class TLRef:
         if rc != 0:
             raise RuntimeError(f"tlref_matmul_backward rc={rc}")
         return da, db
+
+    def add(self, a, b):
+        """tl::add(a, b) with broadcasting."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        cap = max(1, a.size * max(1, b.size))
+        out = np.empty(cap, np.float32)
+        nd = ctypes.c_int(0)
+        sz = (_i64 * 16)()
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_add(_fp(a), a.ndim, self._shape(a), _fp(b), b.ndim, self._shape(b),
+                              _fp(out), cap, ctypes.byref(nd), sz, err, 256)
+        if rc == 1:
+            raise ValueError(err.value.decode())
+        if rc != 0:
+            raise RuntimeError(f"tlref_add rc={rc}")
+        shape = tuple(sz[i] for i in range(nd.value))
+        n = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        return out[:n].reshape(shape)
+
+    def scale(self, x, s):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(x.shape, np.float32)
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_scale(_fp(x), x.ndim, self._shape(x), float(s), _fp(out),
+                                max(1, out.size), err, 256)
+        if rc != 0:
+            raise RuntimeError(f"tlref_scale rc={rc}: {err.value.decode()}")
+        return out
+
+    def softmax(self, x, grad=None):
+        """y = tl::softmax(x); with grad, also x.grad after y.backward() (SoftmaxBackward
+        followed by accumulate_grad, i.e. 0 + dx)."""
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(x.shape, np.float32)
+        dx = np.empty(x.shape, np.float32)
+        g = None if grad is None else np.ascontiguousarray(grad, np.float32)
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_softmax(_fp(x), x.ndim, self._shape(x), None if g is None else _fp(g),
+                                  _fp(y), _fp(dx), max(1, x.size), err, 256)
+        if rc != 0:
+            raise RuntimeError(f"tlref_softmax rc={rc}: {err.value.decode()}")
+        return y if g is None else (y, dx)
 
 
 def _guess_numel(a, b, ta, tb):

@@ -94,4 +94,44 @@ int tlref_matmul_backward(const float* a, int a_nd, const int64_t* a_sz, int tra
     }
 }
 
+// out = tl::add(A, B) (broadcasting).
+int tlref_add(const float* a, int a_nd, const int64_t* a_sz, const float* b, int b_nd,
+              const int64_t* b_sz, float* out, int64_t out_cap, int* out_nd, int64_t* out_sz,
+              char* err, int errlen) {
+    try {
+        return copy_out(tl::add(make(a, a_nd, a_sz), make(b, b_nd, b_sz)), out, out_cap, out_nd,
+                        out_sz);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+// out = tl::scale(X, s).
+int tlref_scale(const float* x, int nd, const int64_t* sz, float s, float* out, int64_t out_cap,
+                char* err, int errlen) {
+    try {
+        return copy_out(tl::scale(make(x, nd, sz), s), out, out_cap, nullptr, nullptr);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+// y = tl::softmax(X); if grad: y.grad() = grad; y.backward(); dx = X.grad
+// (SoftmaxBackward, then accumulate_grad: 0 + d).
+int tlref_softmax(const float* x, int nd, const int64_t* sz, const float* grad, float* y,
+                  float* dx, int64_t cap, char* err, int errlen) {
+    try {
+        tl::Tensor X = make(x, nd, sz);
+        if (grad) X.set_requires_grad(true);
+        tl::Tensor Y = tl::softmax(X);
+        int rc = copy_out(Y, y, cap, nullptr, nullptr);
+        if (rc || !grad) return rc;
+        Y.grad() = make(grad, nd, sz);
+        Y.backward();
+        return copy_out(X.grad(), dx, cap, nullptr, nullptr);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
 }  // extern "C"

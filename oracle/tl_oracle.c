@@ -22,6 +22,20 @@
  *  - element-wise add (src/ops.cpp:75-103), used by accumulate_grad
  *    (src/autograd.cpp:16-22): orc_add.
  *
+ *  - softmax over the last dim (src/ops.cpp:985-1037): the row maximum
+ *    (first element, then strict >), e_j = expf(x_j - max) with the C
+ *    library's expf (what std::exp(float) calls), a sequential sum from 0.0f,
+ *    and e_j / sum: orc_softmax.
+ *
+ *  - SoftmaxBackward (src/autograd.cpp:228-256): dot = sum_j g_j * y_j from
+ *    0.0f in j order, then dx_i = y_i * (g_i - dot): orc_softmax_backward.
+ *    How the Release build rounds the dot depends on its vectorisation: GCC
+ *    vectorises the loop over blocks of `vec` elements (products rounded,
+ *    then added in order: dot = dot + rn(g_j * y_j)) and leaves the last
+ *    D mod vec elements to scalar code that it contracts to
+ *    dot = fmaf(g_j, y_j, dot).  vec = 8 for the x86-64-v4 (AVX-512) build,
+ *    4 for x86-64-v3; both measured against the compiled reference.
+ *
  * Operands are strided 2-D views (row and column strides in elements), so the
  * transposed views that MatmulBackward builds (src/autograd.cpp:370-371) are
  * read in place; Tensor::contiguous (src/tensor.cpp:174-193) only copies, it
@@ -124,4 +138,39 @@ void orc_sum_dim(const float *in, float *out, int64_t outer, int64_t D, int64_t 
 /* out[i] = a[i] + b[i] (same shape). */
 void orc_add(const float *a, const float *b, float *out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = a[i] + b[i];
+}
+
+/* softmax of each row of D floats (src/ops.cpp:985-1037). */
+void orc_softmax(const float *x, float *out, int64_t rows, int64_t D) {
+    for (int64_t r = 0; r < rows; ++r) {
+        const float *row = x + r * D;
+        float *o = out + r * D;
+        float mx = row[0];
+        for (int64_t j = 1; j < D; ++j)
+            if (row[j] > mx) mx = row[j];
+        float sum = 0.0f;
+        for (int64_t j = 0; j < D; ++j) {
+            o[j] = expf(row[j] - mx);
+            sum += o[j];
+        }
+        for (int64_t j = 0; j < D; ++j) o[j] /= sum;
+    }
+}
+
+/* SoftmaxBackward of each row of D floats (src/autograd.cpp:228-256); the
+ * first D - D mod vec products are rounded before they are added. */
+void orc_softmax_backward(const float *g, const float *y, float *dx, int64_t rows, int64_t D,
+                          int64_t vec) {
+    const int64_t nv = D - D % vec;
+    for (int64_t r = 0; r < rows; ++r) {
+        const float *gr = g + r * D, *yr = y + r * D;
+        float *o = dx + r * D;
+        float dot = 0.0f;
+        for (int64_t j = 0; j < nv; ++j) {
+            const float p = gr[j] * yr[j];
+            dot = dot + p;
+        }
+        for (int64_t j = nv; j < D; ++j) dot = fmaf(gr[j], yr[j], dot);
+        for (int64_t i = 0; i < D; ++i) o[i] = yr[i] * (gr[i] - dot);
+    }
 }
