@@ -199,6 +199,38 @@ int tlc_add(const float* a, const float* b, float* out, int64_t n, void* stream)
  * dense row-major buffer. */
 int tlc_contiguous(const tlc_tensor* src, float* dst, void* stream);
 
+/* ---- the glue around the GEMMs in Linear and attention ---------------------
+ * Device tensors; `out` is contiguous with the result's shape.  Element-wise
+ * results are bit-identical to the reference except tlc_softmax (see there). */
+
+/* out = scale * (a . b) + bias: tl::matmul fused with the tl::scale and
+ * tl::add that follow it in the reference's callers (Linear::forward,
+ * src/nn.cpp:77-83: add(matmul(x, W), b); MultiHeadAttention::forward,
+ * src/nn.cpp:423-424: scale(matmul(q, k^T), 1/sqrt(d))).  Each output is the
+ * product exactly as tlc_matmul computes it, then one fp32 multiply by
+ * `scale` (skipped when scale == 1), then one fp32 add of bias[n]: the same
+ * rounding as the separate ops.  `bias` is NULL or a 1-D tensor of length N. */
+int tlc_matmul_fused(const tlc_tensor* a, const tlc_tensor* b, float scale, const tlc_tensor* bias,
+                     tlc_tensor* out, int mode, void* stream);
+/* tl::add with NumPy broadcasting (src/ops.cpp:74-103); "Incompatible
+ * dimensions for broadcasting" as TLC_ERR_INVALID_ARGUMENT. */
+int tlc_add_tensors(const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out, void* stream);
+/* tl::scale (src/ops.cpp:963-983): out = x * scale. */
+int tlc_scale(const tlc_tensor* x, float scale, tlc_tensor* out, void* stream);
+/* tl::softmax over the last dim (src/ops.cpp:985-1037).  Same steps and
+ * order as the reference (row max, exp(x - max), sequential sum, divide); the
+ * exponential is CUDA's expf rather than the C library's, so outputs agree
+ * with the reference to a few ulp rather than bit for bit. */
+int tlc_softmax(const tlc_tensor* x, tlc_tensor* out, void* stream);
+/* SoftmaxBackward (src/autograd.cpp:228-256): dx = y * (grad - sum_j grad_j y_j)
+ * per row, with the row dot rounded as the reference's x86-64-v4 build rounds
+ * it (blocks of 8 rounded products added in order, the tail fused). */
+int tlc_softmax_backward(const tlc_tensor* grad, const tlc_tensor* y, tlc_tensor* dx, void* stream);
+/* sum_to (src/autograd.cpp:24-36): `out`'s shape is the target, a reduction of
+ * x's shape (leading dims dropped, dims of size 1 kept); sequential sums from
+ * 0.0f in the reference's order. */
+int tlc_sum_to(const tlc_tensor* x, tlc_tensor* out, void* stream);
+
 /* ---- multi-GPU partitioning ------------------------------------------------
  * One process per GPU.  A batched GEMM is split over its flattened batch
  * dimension, a single GEMM over output column blocks (operands replicated).

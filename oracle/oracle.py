@@ -96,7 +96,9 @@ def gemm2d_f64(a: np.ndarray, b: np.ndarray, nthreads: int | None = None) -> np.
 
 
 def broadcast_shape(a, b):
-    """compute_broadcast_shape, src/ops.cpp:55-72."""
+    """compute_broadcast_shape, src/ops.cpp:55-72, except that a size-0 dim
+    against a size-1 dim gives 0 (NumPy's rule; the reference takes the max, 1,
+    and then reads the empty operand out of bounds)."""
     nd = max(len(a), len(b))
     out = []
     for i in range(nd):
@@ -104,7 +106,7 @@ def broadcast_shape(a, b):
         sb = 1 if i < nd - len(b) else b[i - (nd - len(b))]
         if sa != sb and sa != 1 and sb != 1:
             raise ValueError("Incompatible dimensions for broadcasting")
-        out.append(max(sa, sb))
+        out.append(sb if sa == 1 else sa)
     return out
 
 

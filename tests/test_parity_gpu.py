@@ -140,6 +140,9 @@ def test_empty_and_k0():
     assert c.shape == (3, 5) and np.all(c == 0) and not np.signbit(c).any()
     c = host(tlcuda.matmul(dev(np.ones((2, 0, 4), np.float32)), dev(np.ones((4, 3), np.float32))))
     assert c.shape == (2, 0, 3)
+    # an empty batch dim against a broadcast one: an empty result (NumPy's rule)
+    z = tlcuda.matmul(dev(np.ones((0, 5, 6), np.float32)), dev(np.ones((1, 6, 7), np.float32)))
+    assert tuple(z.shape) == (0, 5, 7)
 
 
 def test_misaligned_and_strided_views():

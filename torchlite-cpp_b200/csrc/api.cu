@@ -148,7 +148,10 @@ struct Plan {
     std::vector<int64_t> result;      // after dropping squeezed dims
 };
 
-// compute_broadcast_shape, src/ops.cpp:55-72.
+// compute_broadcast_shape, src/ops.cpp:55-72, with one deliberate difference:
+// a size-0 dim against a size-1 dim gives 0 (NumPy's rule).  The reference
+// takes std::max and gets 1, then indexes the empty operand (an out-of-bounds
+// read); here that case yields an empty result instead.
 int broadcast_shape(const std::vector<int64_t>& a, const std::vector<int64_t>& b,
                     std::vector<int64_t>& out) {
     const size_t nd = std::max(a.size(), b.size());
@@ -158,7 +161,7 @@ int broadcast_shape(const std::vector<int64_t>& a, const std::vector<int64_t>& b
         const int64_t sb = i < nd - b.size() ? 1 : b[i - (nd - b.size())];
         if (sa != sb && sa != 1 && sb != 1)
             return set_error(TLC_ERR_INVALID_ARGUMENT, "Incompatible dimensions for broadcasting");
-        out[i] = std::max(sa, sb);
+        out[i] = sa == 1 ? sb : sa;
     }
     return TLC_OK;
 }
@@ -260,15 +263,26 @@ int resolve_mode(int mode, int& out) {
     return TLC_OK;
 }
 
-// C (contiguous, shape p.full_out) = A . B for a planned matmul.
-int matmul_planned(const Plan& p, float* C, int mode, cudaStream_t s) {
+// Per-element epilogue of a fused GEMM (see Gemm): c * scale, then + bias[n].
+struct Epilogue {
+    const float* bias = nullptr;  // [N], contiguous, device
+    float scale = 1.0f;
+    int apply_scale = 0;
+};
+
+// C (contiguous, shape p.full_out) = A . B for a planned matmul, followed by
+// the epilogue `ep`.
+int matmul_planned(const Plan& p, float* C, int mode, cudaStream_t s, const Epilogue& ep = Epilogue()) {
     const int64_t total = [&] {
         int64_t n = 1;
         for (int64_t v : p.full_out) n *= v;
         return n;
     }();
     if (total == 0) return TLC_OK;
-    if (p.K == 0) return launch_fill_zero(C, total, s);
+    if (p.K == 0) {
+        TLC_TRY(launch_fill_zero(C, total, s));
+        return launch_epilogue(C, total / p.N, p.N, ep.scale, ep.apply_scale != 0, ep.bias, s);
+    }
 
     Scratch sa(s), sb(s);
     View a = p.a, b = p.b;
@@ -331,6 +345,9 @@ int matmul_planned(const Plan& p, float* C, int mode, cudaStream_t s) {
     g.b_cs = b_cs;
     g.C = C;
     g.c_rs = p.N;
+    g.bias = ep.bias;
+    g.scale = ep.scale;
+    g.apply_scale = ep.apply_scale;
     std::vector<BatchDim> outer;
     const int keep = std::min<int>((int)dims.size(), kMaxBatchDims);
     const int n_outer = (int)dims.size() - keep;
@@ -980,6 +997,152 @@ int tlc_contiguous(const tlc_tensor* src, float* dst, void* stream) {
     View v;
     TLC_TRY(to_view(src, v, "src"));
     return launch_strided_copy(v.data, v.nd, v.sz, v.st, dst, (cudaStream_t)stream);
+}
+
+// ---- fused GEMM and the glue around it ----------------------------------------------
+
+namespace tlc {
+namespace {
+
+std::vector<int64_t> shape_of(const View& v) { return std::vector<int64_t>(v.sz, v.sz + v.nd); }
+
+// `v` itself when contiguous, else a contiguous copy in `sc`.
+int dense_input(const View& v, Scratch& sc, const float** out, cudaStream_t s) {
+    if (v.contiguous() || v.numel() == 0) {
+        *out = v.data;
+        return TLC_OK;
+    }
+    TLC_TRY(sc.alloc(sizeof(float) * (size_t)v.numel()));
+    TLC_TRY(launch_strided_copy(v.data, v.nd, v.sz, v.st, sc.f(), s));
+    *out = sc.f();
+    return TLC_OK;
+}
+
+// Broadcast strides of `v` against an output of rank nd (0 on broadcast dims).
+void bcast_strides(const View& v, int nd, int64_t* st) {
+    for (int i = 0; i < nd; ++i) {
+        const int iv = i - (nd - v.nd);
+        st[i] = (iv >= 0 && v.sz[iv] != 1) ? v.st[iv] : 0;
+    }
+}
+
+}  // namespace
+}  // namespace tlc
+
+using namespace tlc;
+
+int tlc_matmul_fused(const tlc_tensor* a, const tlc_tensor* b, float scale, const tlc_tensor* bias,
+                     tlc_tensor* out, int mode, void* stream) {
+    clear_error();
+    int m;
+    TLC_TRY(resolve_mode(mode, m));
+    cudaStream_t s = (cudaStream_t)stream;
+    View va, vb;
+    TLC_TRY(to_view(a, va, "a"));
+    TLC_TRY(to_view(b, vb, "b"));
+    Plan p;
+    TLC_TRY(plan_matmul(va, vb, p));
+    TLC_TRY(check_out(out, p.result, "out"));
+    Epilogue ep;
+    ep.scale = scale;
+    ep.apply_scale = scale != 1.0f ? 1 : 0;
+    Scratch sc(s);
+    if (bias) {
+        View vbias;
+        TLC_TRY(to_view(bias, vbias, "bias"));
+        if (vbias.nd != 1 || vbias.sz[0] != p.N)
+            return set_error(TLC_ERR_INVALID_ARGUMENT,
+                             "matmul_fused: bias must be a 1-D tensor of length N = " +
+                                 std::to_string(p.N));
+        TLC_TRY(dense_input(vbias, sc, &ep.bias, s));
+    }
+    return matmul_planned(p, out->data, m, s, ep);
+}
+
+int tlc_add_tensors(const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out, void* stream) {
+    clear_error();
+    View va, vb;
+    TLC_TRY(to_view(a, va, "a"));
+    TLC_TRY(to_view(b, vb, "b"));
+    std::vector<int64_t> shape;
+    TLC_TRY(broadcast_shape(shape_of(va), shape_of(vb), shape));
+    TLC_TRY(check_out(out, shape, "out"));
+    const int nd = (int)shape.size();
+    int64_t sa[TLC_MAX_DIMS] = {}, sb[TLC_MAX_DIMS] = {};
+    bcast_strides(va, nd, sa);
+    bcast_strides(vb, nd, sb);
+    return launch_elementwise(va.data, vb.data, 0.0f, out->data, prod(shape), nd, shape.data(), sa,
+                              sb, 0, (cudaStream_t)stream);
+}
+
+int tlc_scale(const tlc_tensor* x, float scale, tlc_tensor* out, void* stream) {
+    clear_error();
+    View vx;
+    TLC_TRY(to_view(x, vx, "x"));
+    const std::vector<int64_t> shape = shape_of(vx);
+    TLC_TRY(check_out(out, shape, "out"));
+    const int nd = (int)shape.size();
+    int64_t sa[TLC_MAX_DIMS] = {}, sb[TLC_MAX_DIMS] = {};
+    bcast_strides(vx, nd, sa);
+    return launch_elementwise(vx.data, nullptr, scale, out->data, prod(shape), nd, shape.data(), sa,
+                              sb, 1, (cudaStream_t)stream);
+}
+
+int tlc_softmax(const tlc_tensor* x, tlc_tensor* out, void* stream) {
+    clear_error();
+    cudaStream_t s = (cudaStream_t)stream;
+    View vx;
+    TLC_TRY(to_view(x, vx, "x"));
+    if (vx.nd == 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "Softmax requires at least 1D tensor");
+    const std::vector<int64_t> shape = shape_of(vx);
+    TLC_TRY(check_out(out, shape, "out"));
+    const int64_t D = shape.back(), n = prod(shape);
+    if (D == 0 || n == 0) return TLC_OK;
+    Scratch sc(s);
+    const float* xd;
+    TLC_TRY(dense_input(vx, sc, &xd, s));
+    return launch_softmax(xd, out->data, n / D, D, s);
+}
+
+int tlc_softmax_backward(const tlc_tensor* grad, const tlc_tensor* y, tlc_tensor* dx, void* stream) {
+    clear_error();
+    cudaStream_t s = (cudaStream_t)stream;
+    View vg, vy;
+    TLC_TRY(to_view(grad, vg, "grad"));
+    TLC_TRY(to_view(y, vy, "y"));
+    if (vy.nd == 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "softmax_backward: y must be at least 1-D");
+    const std::vector<int64_t> shape = shape_of(vy);
+    if (shape_of(vg) != shape)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "softmax_backward: grad and y differ in shape");
+    TLC_TRY(check_out(dx, shape, "dx"));
+    const int64_t D = shape.back(), n = prod(shape);
+    if (D == 0 || n == 0) return TLC_OK;
+    Scratch sg(s), sy(s);
+    const float *gd, *yd;
+    TLC_TRY(dense_input(vg, sg, &gd, s));
+    TLC_TRY(dense_input(vy, sy, &yd, s));
+    return launch_softmax_backward(gd, yd, dx->data, n / D, D, s);
+}
+
+int tlc_sum_to(const tlc_tensor* x, tlc_tensor* out, void* stream) {
+    clear_error();
+    cudaStream_t s = (cudaStream_t)stream;
+    View vx;
+    TLC_TRY(to_view(x, vx, "x"));
+    if (!out) return set_error(TLC_ERR_INVALID_ARGUMENT, "out is NULL");
+    const std::vector<int64_t> shape = shape_of(vx);
+    const std::vector<int64_t> target(out->sizes, out->sizes + std::max(0, std::min(out->ndim, TLC_MAX_DIMS)));
+    if (target.size() > shape.size())
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "sum_to: target has more dims than the input");
+    const size_t off = shape.size() - target.size();
+    for (size_t i = 0; i < target.size(); ++i)
+        if (target[i] != shape[off + i] && target[i] != 1)
+            return set_error(TLC_ERR_INVALID_ARGUMENT, "sum_to: target shape is not a reduction of the input");
+    TLC_TRY(check_out(out, target, "out"));
+    Scratch sc(s);
+    const float* xd;
+    TLC_TRY(dense_input(vx, sc, &xd, s));
+    return sum_to(xd, shape, target, out->data, s);
 }
 
 int tlc_shard_range(int64_t count, int world, int rank, int64_t* begin, int64_t* end) {

@@ -61,6 +61,12 @@ struct Gemm {
     int nb;                           // number of batch dims (0..3)
     int64_t bsz[kMaxBatchDims];       // batch sizes, outermost first
     int64_t abs_[kMaxBatchDims], bbs[kMaxBatchDims], cbs[kMaxBatchDims];
+    // Epilogue on each output element, in this order (each one IEEE fp32
+    // operation, as the reference's separate tl::scale / tl::add would do):
+    // c = c * scale if apply_scale; c = c + bias[n] if bias.
+    const float* bias = nullptr;  // [N], contiguous
+    float scale = 1.0f;
+    int apply_scale = 0;
     int64_t batch() const {
         int64_t n = 1;
         for (int i = 0; i < nb; ++i) n *= bsz[i];
@@ -114,6 +120,18 @@ int launch_strided_copy(const float* src, int nd, const int64_t* sizes, const in
 int launch_fill_zero(float* p, int64_t n, cudaStream_t s);
 int launch_gather_colblocks(const float* g, float* out, int64_t M, int64_t N, int world,
                             const int64_t* begin, cudaStream_t s);
+
+// Glue kernels (glue.cu).  kind 0: out = a + b, kind 1: out = a * s, over a
+// contiguous output of shape sz[0..nd) with operand strides sa / sb (0 on
+// broadcast dims).
+int launch_elementwise(const float* a, const float* b, float s, float* out, int64_t n, int nd,
+                       const int64_t* sz, const int64_t* sa, const int64_t* sb, int kind,
+                       cudaStream_t st);
+int launch_epilogue(float* C, int64_t rows, int64_t cols, float s, bool apply_scale,
+                    const float* bias, cudaStream_t st);
+int launch_softmax(const float* x, float* y, int64_t rows, int64_t D, cudaStream_t st);
+int launch_softmax_backward(const float* g, const float* y, float* dx, int64_t rows, int64_t D,
+                            cudaStream_t st);
 
 // Copy a strided view into a destination with its own strides (same shape).
 int launch_strided_copy_to(const float* src, int nd, const int64_t* sizes, const int64_t* sstr,

@@ -63,7 +63,19 @@ struct ExactParams {
     int64_t a_rs, a_cs, b_rs, b_cs, c_rs;
     BatchOffsets bo;
     int64_t batch;
+    const float* bias;  // epilogue (see Gemm): c * scale if apply_scale, + bias[col]
+    float scale;
+    int apply_scale;
 };
+
+// The GEMM epilogue on one output value: one IEEE fp32 operation per step,
+// as the reference's separate tl::scale / tl::add would round it.
+__device__ __forceinline__ float epilogue(float v, int64_t col, const float* bias, float scale,
+                                          int apply_scale) {
+    if (apply_scale) v = __fmul_rn(v, scale);
+    if (bias) v = __fadd_rn(v, bias[col]);
+    return v;
+}
 
 // Loads one operand k-tile into 8 registers.
 //  KMAJ = the operand's contiguous dimension is k: thread covers rows
@@ -213,14 +225,18 @@ __global__ void __launch_bounds__(NT, 2) exact_kernel(ExactParams p) {
             for (int h = 0; h < 2; ++h) {
                 const int64_t col = n0 + wn * 32 + h * 16 + tn * 4;
                 float* dst = Cb + row * p.c_rs + col;
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    v[j] = (col + j < p.N)
+                               ? epilogue(acc[i][4 * h + j], col + j, p.bias, p.scale, p.apply_scale)
+                               : 0.0f;
                 if (VC && col + 3 < p.N) {
-                    *reinterpret_cast<float4*>(dst) =
-                        make_float4(acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2],
-                                    acc[i][4 * h + 3]);
+                    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        if (col + j < p.N) dst[j] = acc[i][4 * h + j];
+                        if (col + j < p.N) dst[j] = v[j];
                 }
             }
         }
@@ -261,6 +277,9 @@ struct ExactTmaParams {
     int64_t batch;
     uint64_t timeout_ns;
     int* err;
+    const float* bias;  // epilogue (see Gemm)
+    float scale;
+    int apply_scale;
 };
 
 // Packed fp32 pairs (sm_100 fma.rn.f32x2: two IEEE fused multiply-adds with
@@ -552,6 +571,9 @@ __global__ void __launch_bounds__(NT, TmaCfg<WIDE>::MIN_BLOCKS)
                     unpack2(acc2[i][2 * g4], v[0], v[1]);
                     unpack2(acc2[i][2 * g4 + 1], v[2], v[3]);
                     const int col = n0 + wn * S::WN + g4 * 16 + tn * 4;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (col + j < p.N) v[j] = epilogue(v[j], col + j, p.bias, p.scale, p.apply_scale);
                     if (VC && col + 3 < p.N) {
                         *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
                     } else {
@@ -564,7 +586,7 @@ __global__ void __launch_bounds__(NT, TmaCfg<WIDE>::MIN_BLOCKS)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const int col = n0 + wn * S::WN + tn + 4 * j;
-                    if (col < p.N) crow[col] = accs[i][j];
+                    if (col < p.N) crow[col] = epilogue(accs[i][j], col, p.bias, p.scale, p.apply_scale);
                 }
             }
         }
@@ -647,6 +669,9 @@ int gemm_exact_tma(const Gemm& g, bool ak, bool bkm, bool vc, cudaStream_t s) {
     p.batch = g.batch();
     p.timeout_ns = 2000000000ull;
     p.err = err;
+    p.bias = g.bias;
+    p.scale = g.scale;
+    p.apply_scale = g.apply_scale;
     const int64_t gx = (g.N + bn - 1) / bn, gy = (g.M + TBM - 1) / TBM;
     if (gy > 65535) return TLC_ERR_UNSUPPORTED;
     dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(p.batch < 65535 ? p.batch : 65535));
@@ -708,6 +733,9 @@ int gemm_exact(const Gemm& g, cudaStream_t s) {
     p.c_rs = g.c_rs;
     p.bo = batch_offsets(g);
     p.batch = g.batch();
+    p.bias = g.bias;
+    p.scale = g.scale;
+    p.apply_scale = g.apply_scale;
     if (p.batch == 0 || p.M == 0 || p.N == 0) return TLC_OK;
 
     const bool ak = g.a_cs == 1;   // else a_rs == 1

@@ -90,7 +90,18 @@ struct TcParams {
     int vec_c;        // float4 stores allowed
     uint64_t timeout_ns;
     int* err;
+    const float* bias;  // epilogue (see Gemm): c * scale if apply_scale, + bias[col]
+    float scale;
+    int apply_scale;
 };
+
+// The GEMM epilogue on one output value: one IEEE fp32 operation per step,
+// as the reference's separate tl::scale / tl::add would round it.
+__device__ __forceinline__ float tc_epilogue(const TcParams& p, float v, int col) {
+    if (p.apply_scale) v = __fmul_rn(v, p.scale);
+    if (p.bias) v = __fadd_rn(v, p.bias[col]);
+    return v;
+}
 
 // ---- PTX wrappers ---------------------------------------------------------------
 
@@ -659,6 +670,12 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                         tmem_wait_ld();
                         if (row < p.M) {
                             const int col0 = n0 + c * 32;
+                            if (p.bias || p.apply_scale) {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    if (col0 + j < p.N)
+                                        r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j));
+                            }
                             if (p.vec_c && col0 + 32 <= p.N) {
 #pragma unroll
                                 for (int j = 0; j < 32; j += 4) {
@@ -691,6 +708,11 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
 #pragma unroll
                     for (int c = 0; c < S::EPI_COLS / 32; ++c) {
                         const int col0 = n0 + c * 32;
+                        if (p.bias || p.apply_scale) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.N) sum[c * 32 + j] = tc_epilogue(p, sum[c * 32 + j], col0 + j);
+                        }
                         if (p.vec_c && col0 + 32 <= p.N) {
 #pragma unroll
                             for (int j = 0; j < 32; j += 4)
@@ -953,6 +975,9 @@ void fill_common(TcParams& prm, const Gemm& g, const OperandMap& A, const Operan
     for (int i = 0; i < g.nb; ++i)
         if (g.cbs[i] & 3) prm.vec_c = 0;
     prm.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate wait
+    prm.bias = g.bias;
+    prm.scale = g.scale;
+    prm.apply_scale = g.apply_scale;
 }
 
 // A and B as tensor maps' operand descriptions (memory order: A K-major =

@@ -1,0 +1,201 @@
+// Device kernels for the glue around the GEMMs in Linear and attention:
+// tl::add with broadcasting (src/ops.cpp:74-103), tl::scale (:963-983),
+// tl::softmax (:985-1037), SoftmaxBackward (src/autograd.cpp:228-256), and
+// the in-place epilogue (scale, then bias) that the fused GEMM entry point
+// applies when K == 0.  All HBM-bound: grid-stride loops, coalesced along the
+// contiguous output.
+//
+// Rounding, element by element:
+//  - add, scale, the epilogue: one IEEE fp32 operation each, as in the
+//    reference: bit-identical.
+//  - softmax: the row max as the reference picks it (first element, then
+//    strictly greater: a NaN first element makes the row NaN, later NaNs are
+//    skipped), e = expf(x - max), their sum in j order from 0.0f, e / sum
+//    (IEEE division).  CUDA's expf is not the C library's, so results agree
+//    with the reference to a few ulp, not bit for bit.
+//  - SoftmaxBackward: bit-identical to the reference's x86-64-v4 build, whose
+//    vectorised row dot product adds rounded products g_j * y_j in order for
+//    the first D - D mod 8 elements and contracts the remaining ones into
+//    fmaf(g_j, y_j, dot): each warp walks its row in that order (the values
+//    reach lane 0 by shuffles), then dx_i = y_i * (g_i - dot).
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace tlc {
+namespace {
+
+constexpr int kEwMaxDims = TLC_MAX_DIMS;
+
+// Output index -> operand offsets for a contiguous output of shape sz[0..nd).
+struct EwIndex {
+    int nd;
+    int64_t sz[kEwMaxDims];
+    int64_t sa[kEwMaxDims], sb[kEwMaxDims];  // element strides, 0 on broadcast dims
+    __device__ __forceinline__ void offsets(int64_t i, int64_t& oa, int64_t& ob) const {
+        oa = ob = 0;
+#pragma unroll
+        for (int d = kEwMaxDims - 1; d >= 0; --d) {
+            if (d < nd) {
+                const int64_t c = i % sz[d];
+                i /= sz[d];
+                oa += c * sa[d];
+                ob += c * sb[d];
+            }
+        }
+    }
+};
+
+// kind 0: out = a + b;  kind 1: out = a * s
+__global__ void elementwise_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                   float s, float* __restrict__ out, int64_t n, EwIndex ix,
+                                   int kind) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t oa, ob;
+        ix.offsets(i, oa, ob);
+        out[i] = kind == 0 ? __fadd_rn(a[oa], b[ob]) : __fmul_rn(a[oa], s);
+    }
+}
+
+// C[r, c] = C[r, c] * s + bias[c] for a contiguous [rows, cols] block
+// (the GEMM epilogue on an all-zero product, K == 0).
+__global__ void epilogue_kernel(float* __restrict__ C, int64_t rows, int64_t cols, float s,
+                                int apply_scale, const float* __restrict__ bias) {
+    const int64_t n = rows * cols;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float v = C[i];
+        if (apply_scale) v = __fmul_rn(v, s);
+        if (bias) v = __fadd_rn(v, bias[i % cols]);
+        C[i] = v;
+    }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// One warp per row of D (rows contiguous).
+__global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
+                               int64_t D) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+         r += warps) {
+        const float* xr = x + r * D;
+        float* yr = y + r * D;
+        // max over the non-NaN values (fmaxf skips NaN); NaN if the first is NaN
+        float m = -INFINITY;
+        for (int64_t j = lane; j < D; j += 32) m = fmaxf(m, xr[j]);
+        m = warp_max(m);
+        const float x0 = xr[0];
+        if (x0 != x0) m = x0;
+        // e_j = exp(x_j - max), summed in j order from 0.0f as the reference
+        // does (every lane carries the same running sum; values by shuffle)
+        float s = 0.0f;
+        for (int64_t j0 = 0; j0 < D; j0 += 32) {
+            const int64_t j = j0 + lane;
+            const float e = j < D ? expf(__fsub_rn(xr[j], m)) : 0.0f;
+            if (j < D) yr[j] = e;
+            const int cnt = D - j0 < 32 ? (int)(D - j0) : 32;
+            for (int t = 0; t < cnt; ++t) s = __fadd_rn(s, __shfl_sync(0xffffffffu, e, t));
+        }
+        __syncwarp();
+        for (int64_t j = lane; j < D; j += 32) yr[j] = __fdiv_rn(yr[j], s);
+    }
+}
+
+// One warp per row: the reference build's dot order (blocks of 8 rounded
+// products added in order, fused tail), then dx = y * (g - dot).
+__global__ void softmax_backward_kernel(const float* __restrict__ g, const float* __restrict__ y,
+                                        float* __restrict__ dx, int64_t rows, int64_t D) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t nv = D - D % 8;
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+         r += warps) {
+        const float* gr = g + r * D;
+        const float* yr = y + r * D;
+        float dot = 0.0f;  // every lane carries the same running value
+        for (int64_t j0 = 0; j0 < D; j0 += 32) {
+            const int64_t j = j0 + lane;
+            const float gv = j < D ? gr[j] : 0.0f;
+            const float yv = j < D ? yr[j] : 0.0f;
+            const float p = __fmul_rn(gv, yv);
+            const int cnt = D - j0 < 32 ? (int)(D - j0) : 32;
+            for (int t = 0; t < cnt; ++t) {
+                if (j0 + t < nv) {
+                    dot = __fadd_rn(dot, __shfl_sync(0xffffffffu, p, t));
+                } else {
+                    const float gt = __shfl_sync(0xffffffffu, gv, t);
+                    const float yt = __shfl_sync(0xffffffffu, yv, t);
+                    dot = __fmaf_rn(gt, yt, dot);
+                }
+            }
+        }
+        float* o = dx + r * D;
+        for (int64_t j = lane; j < D; j += 32) o[j] = __fmul_rn(yr[j], __fsub_rn(gr[j], dot));
+    }
+}
+
+int grid_for(int64_t n, int per_block) {
+    const int64_t b = (n + per_block - 1) / per_block;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 32));
+}
+
+}  // namespace
+
+int launch_elementwise(const float* a, const float* b, float s, float* out, int64_t n, int nd,
+                       const int64_t* sz, const int64_t* sa, const int64_t* sb, int kind,
+                       cudaStream_t st) {
+    if (n == 0) return TLC_OK;
+    EwIndex ix{};
+    // merge adjacent dims that walk both operands as one; drop size-1 dims
+    int m = 0;
+    for (int d = 0; d < nd; ++d) {
+        if (sz[d] == 1) continue;
+        if (m > 0 && ix.sa[m - 1] == sa[d] * sz[d] && ix.sb[m - 1] == sb[d] * sz[d]) {
+            ix.sz[m - 1] *= sz[d];
+            ix.sa[m - 1] = sa[d];
+            ix.sb[m - 1] = sb[d];
+            continue;
+        }
+        ix.sz[m] = sz[d];
+        ix.sa[m] = sa[d];
+        ix.sb[m] = sb[d];
+        ++m;
+    }
+    ix.nd = m;
+    elementwise_kernel<<<grid_for(n, 256), 256, 0, st>>>(a, b, s, out, n, ix, kind);
+    count_launch();
+    return check_launch("elementwise");
+}
+
+int launch_epilogue(float* C, int64_t rows, int64_t cols, float s, bool apply_scale,
+                    const float* bias, cudaStream_t st) {
+    if (rows * cols == 0 || (!apply_scale && !bias)) return TLC_OK;
+    epilogue_kernel<<<grid_for(rows * cols, 256), 256, 0, st>>>(C, rows, cols, s, apply_scale ? 1 : 0,
+                                                               bias);
+    count_launch();
+    return check_launch("epilogue");
+}
+
+int launch_softmax(const float* x, float* y, int64_t rows, int64_t D, cudaStream_t st) {
+    if (rows == 0 || D == 0) return TLC_OK;
+    softmax_kernel<<<grid_for(rows, 8), 256, 0, st>>>(x, y, rows, D);
+    count_launch();
+    return check_launch("softmax");
+}
+
+int launch_softmax_backward(const float* g, const float* y, float* dx, int64_t rows, int64_t D,
+                            cudaStream_t st) {
+    if (rows == 0 || D == 0) return TLC_OK;
+    softmax_backward_kernel<<<grid_for(rows, 8), 256, 0, st>>>(g, y, dx, rows, D);
+    count_launch();
+    return check_launch("softmax_backward");
+}
+
+}  // namespace tlc

@@ -84,6 +84,12 @@ SIGNATURES = {
     "tlc_sum_dim": ([_v, _v, _i64, _i64, _i64, _v], _i),
     "tlc_add": ([_v, _v, _v, _i64, _v], _i),
     "tlc_contiguous": ([_T, _v, _v], _i),
+    "tlc_matmul_fused": ([_T, _T, ctypes.c_float, _T, _T, _i, _v], _i),
+    "tlc_add_tensors": ([_T, _T, _T, _v], _i),
+    "tlc_scale": ([_T, ctypes.c_float, _T, _v], _i),
+    "tlc_softmax": ([_T, _T, _v], _i),
+    "tlc_softmax_backward": ([_T, _T, _T, _v], _i),
+    "tlc_sum_to": ([_T, _T, _v], _i),
     "tlc_shard_range": ([_i64, _i, _i, _P(_i64), _P(_i64)], _i),
     "tlc_shard_cols": ([_i64, _i, _i, _i64, _P(_i64), _P(_i64)], _i),
     "tlc_gather_colblocks": ([_v, _v, _i64, _i64, _i, _P(_i64), _v], _i),
@@ -257,6 +263,79 @@ def sum_dim0(stack, out=None, stream=None):
     inner = out.numel()
     _check(lib().tlc_sum_dim(ctypes.c_void_p(stack.data_ptr()), ctypes.c_void_p(out.data_ptr()),
                              1, stack.shape[0], inner, _stream_ptr(stream)))
+    return out
+
+
+def matmul_fused(a, b, scale=1.0, bias=None, mode="exact", out=None, stream=None):
+    """scale * (a . b) + bias (bias: 1-D of length N, or None), fused into the GEMM."""
+    import torch
+    shape = matmul_shape(a, b)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=a.device)
+    va, vb, vo = view_of(a), view_of(b), view_of(out)
+    vbias = view_of(bias) if bias is not None else None
+    _check(lib().tlc_matmul_fused(ctypes.byref(va), ctypes.byref(vb), float(scale),
+                                  ctypes.byref(vbias) if vbias is not None else None,
+                                  ctypes.byref(vo), mode_id(mode), _stream_ptr(stream)))
+    return out
+
+
+def _broadcast(sa, sb):
+    nd = max(len(sa), len(sb))
+    out = []
+    for i in range(nd):
+        x = sa[i - (nd - len(sa))] if i >= nd - len(sa) else 1
+        y = sb[i - (nd - len(sb))] if i >= nd - len(sb) else 1
+        out.append(y if x == 1 else x)  # size 0 against 1 gives 0
+    return tuple(out)
+
+
+def add_tensors(a, b, out=None, stream=None):
+    """tl::add with broadcasting on CUDA tensors."""
+    import torch
+    if out is None:
+        out = torch.empty(_broadcast(tuple(a.shape), tuple(b.shape)), dtype=torch.float32,
+                          device=a.device)
+    va, vb, vo = view_of(a), view_of(b), view_of(out)
+    _check(lib().tlc_add_tensors(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vo),
+                                 _stream_ptr(stream)))
+    return out
+
+
+def scale(x, s, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty(tuple(x.shape), dtype=torch.float32, device=x.device)
+    vx, vo = view_of(x), view_of(out)
+    _check(lib().tlc_scale(ctypes.byref(vx), float(s), ctypes.byref(vo), _stream_ptr(stream)))
+    return out
+
+
+def softmax(x, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty(tuple(x.shape), dtype=torch.float32, device=x.device)
+    vx, vo = view_of(x), view_of(out)
+    _check(lib().tlc_softmax(ctypes.byref(vx), ctypes.byref(vo), _stream_ptr(stream)))
+    return out
+
+
+def softmax_backward(grad, y, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty(tuple(y.shape), dtype=torch.float32, device=y.device)
+    vg, vy, vo = view_of(grad), view_of(y), view_of(out)
+    _check(lib().tlc_softmax_backward(ctypes.byref(vg), ctypes.byref(vy), ctypes.byref(vo),
+                                      _stream_ptr(stream)))
+    return out
+
+
+def sum_to(x, target, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty(tuple(target), dtype=torch.float32, device=x.device)
+    vx, vo = view_of(x), view_of(out)
+    _check(lib().tlc_sum_to(ctypes.byref(vx), ctypes.byref(vo), _stream_ptr(stream)))
     return out
 
 
