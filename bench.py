@@ -288,7 +288,9 @@ class GemmWork(Work):
 
 class LinearWork(Work):
     """Y = X.W^T + b fwd + bwd: X[4096,1024] ~ N(0,1), W[4096,1024] ~ U(-1/32,1/32),
-    dY ~ N(0,1); the GEMMs Y = X.W^T, dX = dY.W, dW^T = X^T.dY (bias: not a GEMM)."""
+    b = 0, dY ~ N(0,1).  Forward: one GEMM with the bias add fused into its
+    epilogue; backward: dX = dY.W, dW^T = X^T.dY (MatmulBackward) and
+    db = sum_to(dY, [4096]) (AddBackward).  FLOPs count the three GEMMs."""
     name = "linear"
 
     def __init__(self, world, rank, device):
@@ -300,23 +302,27 @@ class LinearWork(Work):
         self.Y = torch.empty((4096, 4096), device=device)
         self.dX = torch.empty((4096, 1024), device=device)
         self.dWt = torch.empty((1024, 4096), device=device)
+        self.b = torch.zeros((4096,), device=device)
+        self.db = torch.empty((4096,), device=device)
         self.flops = 3 * 2.0 * 4096 * 4096 * 1024
         self.job_flops = self.flops * world
         self.config = {"workload": "linear", "X": [4096, 1024], "W": [4096, 1024],
-                       "gemms": "Y=X.W^T, dX=dY.W, dW^T=X^T.dY", "parallelism": "replicas"}
+                       "gemms": "Y=X.W^T+b (bias fused), dX=dY.W, dW^T=X^T.dY; db=sum_to(dY)",
+                       "parallelism": "replicas"}
 
     def step(self, mode):
         import tlcuda
-        tlcuda.matmul(self.X, self.W.t(), mode=mode, out=self.Y)
+        tlcuda.matmul_fused(self.X, self.W.t(), 1.0, self.b, mode=mode, out=self.Y)
         tlcuda.matmul_backward(self.dY, self.X, self.W.t(), mode=mode, da=self.dX, db=self.dWt)
+        tlcuda.sum_to(self.dY, (4096,), out=self.db)
 
 
 class AttentionWork(Work):
-    """Encoder attention GEMMs: batch 16, seq 512, d_model 768, 12 heads of 64:
+    """Encoder attention: batch 16, seq 512, d_model 768, 12 heads of 64:
     QKV [8192,768].[768,2304], scores [192,512,64].[192,64,512] (K^T read in
-    place), context [192,512,512].[192,512,64], out-proj [8192,768].[768,768];
-    activations ~ N(0,1), weights ~ N(0,0.02), softmax(scores/8) (computed once
-    at set-up with torch, not timed) feeds the context GEMM."""
+    place, the 1/8 scale fused into the GEMM epilogue), P = softmax(scores)
+    (device kernel), context P.[192,512,64], out-proj [8192,768].[768,768];
+    activations ~ N(0,1), weights ~ N(0,0.02).  FLOPs count the four GEMMs."""
     name = "attention"
 
     def __init__(self, world, rank, device):
@@ -329,8 +335,7 @@ class AttentionWork(Work):
         self.q = torch.randn((192, 512, 64), generator=g, device=device)
         self.k = torch.randn((192, 512, 64), generator=g, device=device)
         self.v = torch.randn((192, 512, 64), generator=g, device=device)
-        s = tlcuda.matmul(self.q, self.k.transpose(1, 2), mode="exact")
-        self.P = torch.softmax(s / 8.0, dim=-1)
+        self.P = torch.empty((192, 512, 512), device=device)
         self.qkv = torch.empty((8192, 2304), device=device)
         self.sc = torch.empty((192, 512, 512), device=device)
         self.ctx = torch.empty((192, 512, 64), device=device)
@@ -338,12 +343,14 @@ class AttentionWork(Work):
         self.flops = 2.0 * (8192 * 768 * 2304 + 2 * 192 * 512 * 512 * 64 + 8192 * 768 * 768)
         self.job_flops = self.flops * world
         self.config = {"workload": "attention", "batch": 16, "seq": 512, "d_model": 768,
-                       "heads": 12, "parallelism": "replicas"}
+                       "heads": 12, "glue": "scores scaled in the GEMM epilogue, softmax kernel",
+                       "parallelism": "replicas"}
 
     def step(self, mode):
         import tlcuda
         tlcuda.matmul(self.x, self.Wqkv, mode=mode, out=self.qkv)
-        tlcuda.matmul(self.q, self.k.transpose(1, 2), mode=mode, out=self.sc)
+        tlcuda.matmul_fused(self.q, self.k.transpose(1, 2), 0.125, None, mode=mode, out=self.sc)
+        tlcuda.softmax(self.sc, out=self.P)
         tlcuda.matmul(self.P, self.v, mode=mode, out=self.ctx)
         tlcuda.matmul(self.x, self.Wo, mode=mode, out=self.o)
 

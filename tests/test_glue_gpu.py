@@ -63,8 +63,12 @@ def test_scale(s):
     assert bits_equal(host(tlcuda.scale(dev(x).t(), s)), O.scale(x.T, s))
 
 
-SOFTMAX_SHAPES = [(1,), (7,), (5, 7), (2, 9), (3, 4, 64), (2, 512), (192, 33), (4, 1000), (3, 4096),
-                  (6, 1)]
+# row lengths covering every register bucket (<= 32, 64, 128, 256, 512, 1024) and the
+# streaming kernel above 1024
+SOFTMAX_SHAPES = [(1,), (7,), (5, 7), (2, 9), (3, 4, 64), (2, 100), (3, 200), (2, 512), (192, 33),
+                  (4, 1000), (3, 4096), (6, 1),
+                  # enough rows for the thread-per-row kernels (float4 and scalar rows)
+                  (24, 1024, 64), (19000, 37)]
 
 
 def softmax_close(got, ref):
@@ -98,7 +102,8 @@ def test_softmax_edge_rows():
 
 @pytest.mark.parametrize("shape,target", [((32, 64, 128), (64, 128)), ((4, 3, 5), (5,)),
                                           ((4, 3, 5), (1, 5)), ((4, 3, 5), (4, 1, 5)),
-                                          ((4096, 4096), (4096,)), ((7,), (7,))])
+                                          ((4096, 4096), (4096,)), ((7,), (7,)),
+                                          ((1000, 100), (100,)), ((4, 300, 40), (4, 1, 40))])
 def test_sum_to(shape, target):
     x = inputs.normal(np.random.default_rng(len(shape) + len(target)), shape)
     assert bits_equal(host(tlcuda.sum_to(dev(x), target)), O.sum_to(x, target))

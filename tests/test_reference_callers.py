@@ -16,6 +16,13 @@ Exact mode must give identical bits (the reference's src/ops.cpp:605-699
 matmul and src/autograd.cpp:341-384 backward, unmodified callers in
 src/nn.cpp:77-83 and src/nn.cpp:401-445); TF32 and 3xTF32 are held to
 relative Frobenius errors of 1e-2 and 1e-5 over the whole output.
+
+tests/integration/device_callers_main.cpp runs the same scenarios on the
+device-resident C++ tl:: layer (torchlite-cpp_b200/host: Linear with the
+bias add fused into its GEMM, attention with the 1/sqrt(d) scale fused and
+the softmax and its backward on the GPU); its outputs must equal the
+reference's bit for bit, except the attention block, which carries the
+softmax's few-ulp difference (CUDA's expf) and is held to 1e-5.
 """
 import os
 import subprocess
@@ -73,3 +80,40 @@ def test_reference_callers_on_gpu(tmp_path, mode, tol):
         d = got.astype(np.float64) - ref
         rel = np.linalg.norm(d) / np.linalg.norm(ref.astype(np.float64))
         assert rel <= tol, rel
+
+
+# (scenario, shapes of its outputs in dump order) of both callers programs
+SEGMENTS = [
+    ("linear", [(129, 257), (129, 300), (300, 257), (257,)]),
+    ("linear_batched", [(4, 33, 50), (4, 33, 70), (70, 50)]),
+    ("attention", [(2, 40, 96), (2, 40, 96), (96, 96), (96, 96)]),
+    ("broadcast_matmul", [(3, 20, 25), (3, 20, 30), (30, 25)]),
+    ("x_wt", [(65, 31), (65, 48), (31, 48)]),
+]
+DEVICE_BIN = os.path.join(ROOT, "torchlite-cpp_b200", "lib", "tl_device_callers")
+
+
+@pytest.mark.gpu
+def test_device_layer_runs_the_reference_callers(tmp_path):
+    if not os.path.exists(DEVICE_BIN):
+        pytest.skip("tl_device_callers not built")
+    ref, _ = _run(tmp_path, "cpu", {"TLC_REFERENCE_MATMUL": "1"})
+    out = tmp_path / "device.bin"
+    r = subprocess.run([DEVICE_BIN, str(out)], capture_output=True, text=True, timeout=300,
+                       env={k: v for k, v in os.environ.items() if k != "TL_GEMM_MODE"})
+    assert r.returncode == 0, r.stdout + r.stderr
+    got = np.fromfile(out, dtype=np.float32)
+    assert got.shape == ref.shape
+    off = 0
+    for name, shapes in SEGMENTS:
+        for shp in shapes:
+            n = int(np.prod(shp))
+            g, e = got[off:off + n], ref[off:off + n]
+            off += n
+            if name == "attention":
+                rel = np.linalg.norm(g.astype(np.float64) - e) / np.linalg.norm(e.astype(np.float64))
+                assert rel <= 1e-5, (name, shp, rel)
+            else:
+                assert g.tobytes() == e.tobytes(), (
+                    name, shp, int((g.view(np.uint32) != e.view(np.uint32)).sum()))
+    assert off == got.size

@@ -78,6 +78,14 @@ def build(jobs: int = 8, verbose: bool = False, ptxas_info: bool = False) -> dic
     if test_src and _stale(test_bin, test_src + host_hdr + [tl_so]):
         _run(["g++"] + CXX_FLAGS + ["-UNDEBUG", "-o", test_bin] + test_src +
              ["-L", LIB, "-ltorchlite_b200", "-ltl_cuda", "-Wl,-rpath,$ORIGIN"], verbose)
+    # The reference callers' scenarios on the device tl:: layer
+    # (tests/integration/device_callers_main.cpp, compared with the reference
+    # by tests/test_reference_callers.py).
+    dc_src = os.path.join(REPO, "tests", "integration", "device_callers_main.cpp")
+    dc_bin = os.path.join(LIB, "tl_device_callers")
+    if os.path.exists(dc_src) and _stale(dc_bin, [dc_src] + host_hdr + [tl_so]):
+        _run(["g++"] + CXX_FLAGS + ["-o", dc_bin, dc_src, "-L", LIB, "-ltorchlite_b200", "-ltl_cuda",
+              "-Wl,-rpath,$ORIGIN"], verbose)
     return logs
 
 

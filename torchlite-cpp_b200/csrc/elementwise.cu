@@ -38,6 +38,53 @@ __global__ void sum_dim_kernel(const float* __restrict__ in, float* __restrict__
     }
 }
 
+// The same sums when there are few outputs and long chains (e.g. a bias
+// gradient: D = 4096 rows into 4096 columns).  A block owns a strip of 32
+// consecutive outputs of one `o`; warps 1..7 stage SUM_ROWS rows of the strip
+// into a double-buffered shared tile (many loads in flight per thread), and
+// warp 0, one lane per output, adds each tile's rows in ascending d.  The
+// order of every sum is the reference's.
+constexpr int SUM_ROWS = 168;  // rows per tile: 24 per loader warp (2 tiles: 42 KB)
+__global__ void __launch_bounds__(256) sum_dim_strip_kernel(const float* __restrict__ in,
+                                                            float* __restrict__ out, int64_t outer,
+                                                            int64_t D, int64_t inner) {
+    __shared__ float tile[2][SUM_ROWS][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t strips = (inner + 31) / 32;
+    const int64_t o = blockIdx.x / strips;
+    const int64_t n0 = (blockIdx.x - o * strips) * 32;
+    const int64_t n = n0 + lane;
+    const bool col_ok = n < inner;
+    const float* base = in + o * D * inner + n;
+    const int64_t tiles = (D + SUM_ROWS - 1) / SUM_ROWS;
+    float acc = 0.0f;
+    // loaders: warp w (1..7) stages rows w - 1, w + 6, ... of each tile
+    auto stage = [&](int64_t t, int buf) {
+        const int64_t d0 = t * SUM_ROWS;
+        float v[SUM_ROWS / 7];
+#pragma unroll
+        for (int r = 0; r < SUM_ROWS / 7; ++r) {
+            const int64_t d = d0 + (warp - 1) + 7 * r;
+            v[r] = (col_ok && d < D) ? base[d * inner] : 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < SUM_ROWS / 7; ++r) tile[buf][(warp - 1) + 7 * r][lane] = v[r];
+    };
+    if (warp > 0 && tiles > 0) stage(0, 0);
+    __syncthreads();
+    for (int64_t t = 0; t < tiles; ++t) {
+        const int buf = (int)(t & 1);
+        if (warp > 0) {
+            if (t + 1 < tiles) stage(t + 1, buf ^ 1);
+        } else {
+            const int rows = (int)min((int64_t)SUM_ROWS, D - t * SUM_ROWS);
+            for (int r = 0; r < rows; ++r) acc = __fadd_rn(acc, tile[buf][r][lane]);
+        }
+        __syncthreads();
+    }
+    if (warp == 0 && col_ok) out[o * inner + n] = acc;
+}
+
 __global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b,
                            float* __restrict__ out, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -117,6 +164,13 @@ int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_
                    cudaStream_t s) {
     const int64_t n = outer * inner;
     if (n == 0) return TLC_OK;
+    // few outputs and long chains: the strip kernel keeps enough loads in flight
+    const int64_t strips = outer * ((inner + 31) / 32);
+    if (inner >= 32 && D >= 64 && n < 148 * 1024 && strips < (int64_t(1) << 31)) {
+        sum_dim_strip_kernel<<<(unsigned)strips, 256, 0, s>>>(in, out, outer, D, inner);
+        count_launch();
+        return check_launch("sum_dim_strip");
+    }
     sum_dim_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, out, outer, D, inner);
     count_launch();
     return check_launch("sum_dim");

@@ -26,6 +26,9 @@ namespace tlc {
 namespace {
 
 constexpr int kEwMaxDims = TLC_MAX_DIMS;
+// Rows from which the many-row kernels (a row per warp, block-shared
+// sequential sums) are used.
+constexpr int64_t kRowPerThread = 148 * 128;
 
 // Output index -> operand offsets for a contiguous output of shape sz[0..nd).
 struct EwIndex {
@@ -108,6 +111,201 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
     }
 }
 
+// The same for rows of at most 32 * VPL: each lane keeps its VPL values in
+// registers (element j = 32 i + lane), so a row is read once and written once.
+template <int VPL>
+__global__ void softmax_reg_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
+                                   int D) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+         r += warps) {
+        const float* xr = x + r * D;
+        float v[VPL];
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int j = 32 * i + lane;
+            v[i] = j < D ? xr[j] : -INFINITY;
+            m = fmaxf(m, v[i]);
+        }
+        m = warp_max(m);
+        const float x0 = __shfl_sync(0xffffffffu, v[0], 0);
+        if (x0 != x0) m = x0;
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int j0 = 32 * i;
+            v[i] = (j0 + lane < D) ? expf(__fsub_rn(v[i], m)) : 0.0f;
+            const int cnt = D - j0 < 32 ? D - j0 : 32;
+            for (int t = 0; t < cnt; ++t) s = __fadd_rn(s, __shfl_sync(0xffffffffu, v[i], t));
+        }
+        float* yr = y + r * D;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int j = 32 * i + lane;
+            if (j < D) yr[j] = __fdiv_rn(v[i], s);
+        }
+    }
+}
+
+// SoftmaxBackward for rows of at most 32 * VPL, g and y held in registers.
+template <int VPL>
+__global__ void softmax_backward_reg_kernel(const float* __restrict__ g, const float* __restrict__ y,
+                                            float* __restrict__ dx, int64_t rows, int D) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int nv = D - D % 8;
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+         r += warps) {
+        float gv[VPL], yv[VPL];
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int j = 32 * i + lane;
+            gv[i] = j < D ? g[r * D + j] : 0.0f;
+            yv[i] = j < D ? y[r * D + j] : 0.0f;
+        }
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int j0 = 32 * i;
+            const float p = __fmul_rn(gv[i], yv[i]);
+            const int cnt = D - j0 < 32 ? D - j0 : 32;
+            for (int t = 0; t < cnt; ++t) {
+                if (j0 + t < nv) {
+                    dot = __fadd_rn(dot, __shfl_sync(0xffffffffu, p, t));
+                } else {
+                    const float gt = __shfl_sync(0xffffffffu, gv[i], t);
+                    const float yt = __shfl_sync(0xffffffffu, yv[i], t);
+                    dot = __fmaf_rn(gt, yt, dot);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int j = 32 * i + lane;
+            if (j < D) dx[r * D + j] = __fmul_rn(yv[i], __fsub_rn(gv[i], dot));
+        }
+    }
+}
+
+// Many rows of at most 32 * VPL: a block of ROWS warps takes ROWS rows, one
+// per warp in registers (read once, written once).  Each warp computes its
+// row's max and e = exp(x - max) and parks e in a padded shared tile; lane r
+// of warp 0 then adds row r's e in j order (the reference's sequential sum,
+// one lane per row instead of a shuffle chain on all 32 lanes), and every
+// warp divides its registers by its row's sum.
+constexpr int SM_ROWS = 16;
+template <int VPL>
+__global__ void __launch_bounds__(SM_ROWS * 32) softmax_block_kernel(const float* __restrict__ x,
+                                                                     float* __restrict__ y,
+                                                                     int64_t rows, int D) {
+    extern __shared__ float sm[];
+    float* tile = sm;                      // [SM_ROWS][D + 1]
+    float* sums = sm + SM_ROWS * (D + 1);  // [SM_ROWS]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t r0 = (int64_t)blockIdx.x * SM_ROWS; r0 < rows; r0 += (int64_t)gridDim.x * SM_ROWS) {
+        const int64_t r = r0 + warp;
+        const bool valid = r < rows;
+        float v[VPL];
+        if (valid) {
+            const float* xr = x + r * D;
+            float m = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                const int j = 32 * i + lane;
+                v[i] = j < D ? xr[j] : -INFINITY;
+                m = fmaxf(m, v[i]);
+            }
+            m = warp_max(m);
+            const float x0 = __shfl_sync(0xffffffffu, v[0], 0);
+            if (x0 != x0) m = x0;
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                const int j = 32 * i + lane;
+                if (j < D) {
+                    v[i] = expf(__fsub_rn(v[i], m));
+                    tile[warp * (D + 1) + j] = v[i];
+                }
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && lane < SM_ROWS && r0 + lane < rows) {
+            const float* t = tile + lane * (D + 1);
+            float s = 0.0f;
+            for (int j = 0; j < D; ++j) s = __fadd_rn(s, t[j]);
+            sums[lane] = s;
+        }
+        __syncthreads();
+        if (valid) {
+            const float s = sums[warp];
+            float* yr = y + r * D;
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                const int j = 32 * i + lane;
+                if (j < D) yr[j] = __fdiv_rn(v[i], s);
+            }
+        }
+        __syncthreads();  // the tile and sums are reused by the next rows
+    }
+}
+
+// Many rows of at most 32 * VPL: SoftmaxBackward with the softmax's block
+// layout.  Each warp holds its row's g and y in registers and parks the
+// rounded products g_j * y_j (j < D - D mod 8) and the tail's g_j, y_j in
+// shared memory; lane r of warp 0 forms row r's dot in the reference build's
+// order; every warp then writes dx = y * (g - dot) from its registers.
+template <int VPL>
+__global__ void __launch_bounds__(SM_ROWS * 32) softmax_backward_block_kernel(
+    const float* __restrict__ g, const float* __restrict__ y, float* __restrict__ dx, int64_t rows,
+    int D) {
+    extern __shared__ float sm[];
+    float* tile = sm;                          // [SM_ROWS][D + 1] rounded products
+    float* tail_g = sm + SM_ROWS * (D + 1);    // [SM_ROWS][8]
+    float* tail_y = tail_g + SM_ROWS * 8;      // [SM_ROWS][8]
+    float* dots = tail_y + SM_ROWS * 8;        // [SM_ROWS]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nv = D - D % 8;
+    for (int64_t r0 = (int64_t)blockIdx.x * SM_ROWS; r0 < rows; r0 += (int64_t)gridDim.x * SM_ROWS) {
+        const int64_t r = r0 + warp;
+        const bool valid = r < rows;
+        float gv[VPL], yv[VPL];
+        if (valid) {
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                const int j = 32 * i + lane;
+                gv[i] = j < D ? g[r * D + j] : 0.0f;
+                yv[i] = j < D ? y[r * D + j] : 0.0f;
+                if (j < nv) {
+                    tile[warp * (D + 1) + j] = __fmul_rn(gv[i], yv[i]);
+                } else if (j < D) {
+                    tail_g[warp * 8 + (j - nv)] = gv[i];
+                    tail_y[warp * 8 + (j - nv)] = yv[i];
+                }
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && lane < SM_ROWS && r0 + lane < rows) {
+            const float* t = tile + lane * (D + 1);
+            float dot = 0.0f;
+            for (int j = 0; j < nv; ++j) dot = __fadd_rn(dot, t[j]);
+            for (int j = nv; j < D; ++j)
+                dot = __fmaf_rn(tail_g[lane * 8 + (j - nv)], tail_y[lane * 8 + (j - nv)], dot);
+            dots[lane] = dot;
+        }
+        __syncthreads();
+        if (valid) {
+            const float dot = dots[warp];
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                const int j = 32 * i + lane;
+                if (j < D) dx[r * D + j] = __fmul_rn(yv[i], __fsub_rn(gv[i], dot));
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // One warp per row: the reference build's dot order (blocks of 8 rounded
 // products added in order, fused tail), then dx = y * (g - dot).
 __global__ void softmax_backward_kernel(const float* __restrict__ g, const float* __restrict__ y,
@@ -183,17 +381,93 @@ int launch_epilogue(float* C, int64_t rows, int64_t cols, float s, bool apply_sc
     return check_launch("epilogue");
 }
 
-int launch_softmax(const float* x, float* y, int64_t rows, int64_t D, cudaStream_t st) {
-    if (rows == 0 || D == 0) return TLC_OK;
-    softmax_kernel<<<grid_for(rows, 8), 256, 0, st>>>(x, y, rows, D);
+
+template <int VPL>
+int launch_softmax_block(const float* x, float* y, int64_t rows, int D, cudaStream_t st) {
+    const size_t smem = sizeof(float) * (SM_ROWS * (size_t)(D + 1) + SM_ROWS);
+    static bool configured[64] = {};
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    if (!configured[dev]) {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(softmax_block_kernel<VPL>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)(sizeof(float) * (SM_ROWS * 1025 + SM_ROWS))));
+        configured[dev] = true;
+    }
+    const int64_t groups = (rows + SM_ROWS - 1) / SM_ROWS;
+    const int grid = (int)std::min<int64_t>(groups, 148 * 8);
+    softmax_block_kernel<VPL><<<grid, SM_ROWS * 32, smem, st>>>(x, y, rows, D);
     count_launch();
     return check_launch("softmax");
+}
+
+int launch_softmax(const float* x, float* y, int64_t rows, int64_t D, cudaStream_t st) {
+    if (rows == 0 || D == 0) return TLC_OK;
+    if (rows >= kRowPerThread && D <= 1024) {
+        const int d = (int)D;
+        if (D <= 32) return launch_softmax_block<1>(x, y, rows, d, st);
+        if (D <= 64) return launch_softmax_block<2>(x, y, rows, d, st);
+        if (D <= 128) return launch_softmax_block<4>(x, y, rows, d, st);
+        if (D <= 256) return launch_softmax_block<8>(x, y, rows, d, st);
+        if (D <= 512) return launch_softmax_block<16>(x, y, rows, d, st);
+        return launch_softmax_block<32>(x, y, rows, d, st);
+    }
+    const int gb = grid_for(rows, 8);
+    const int d = (int)std::min<int64_t>(D, 1 << 30);
+    if (D <= 32) softmax_reg_kernel<1><<<gb, 256, 0, st>>>(x, y, rows, d);
+    else if (D <= 64) softmax_reg_kernel<2><<<gb, 256, 0, st>>>(x, y, rows, d);
+    else if (D <= 128) softmax_reg_kernel<4><<<gb, 256, 0, st>>>(x, y, rows, d);
+    else if (D <= 256) softmax_reg_kernel<8><<<gb, 256, 0, st>>>(x, y, rows, d);
+    else if (D <= 512) softmax_reg_kernel<16><<<gb, 256, 0, st>>>(x, y, rows, d);
+    else if (D <= 1024) softmax_reg_kernel<32><<<gb, 256, 0, st>>>(x, y, rows, d);
+    else softmax_kernel<<<gb, 256, 0, st>>>(x, y, rows, D);
+    count_launch();
+    return check_launch("softmax");
+}
+
+template <int VPL>
+int launch_softmax_backward_block(const float* g, const float* y, float* dx, int64_t rows, int D,
+                                  cudaStream_t st) {
+    const size_t smem = sizeof(float) * (SM_ROWS * (size_t)(D + 1) + 2 * SM_ROWS * 8 + SM_ROWS);
+    static bool configured[64] = {};
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    if (!configured[dev]) {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(softmax_backward_block_kernel<VPL>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)(sizeof(float) * (SM_ROWS * 1025 + 2 * SM_ROWS * 8 + SM_ROWS))));
+        configured[dev] = true;
+    }
+    const int64_t groups = (rows + SM_ROWS - 1) / SM_ROWS;
+    const int grid = (int)std::min<int64_t>(groups, 148 * 8);
+    softmax_backward_block_kernel<VPL><<<grid, SM_ROWS * 32, smem, st>>>(g, y, dx, rows, D);
+    count_launch();
+    return check_launch("softmax_backward");
 }
 
 int launch_softmax_backward(const float* g, const float* y, float* dx, int64_t rows, int64_t D,
                             cudaStream_t st) {
     if (rows == 0 || D == 0) return TLC_OK;
-    softmax_backward_kernel<<<grid_for(rows, 8), 256, 0, st>>>(g, y, dx, rows, D);
+    if (rows >= kRowPerThread && D <= 1024) {
+        const int d = (int)D;
+        if (D <= 32) return launch_softmax_backward_block<1>(g, y, dx, rows, d, st);
+        if (D <= 64) return launch_softmax_backward_block<2>(g, y, dx, rows, d, st);
+        if (D <= 128) return launch_softmax_backward_block<4>(g, y, dx, rows, d, st);
+        if (D <= 256) return launch_softmax_backward_block<8>(g, y, dx, rows, d, st);
+        if (D <= 512) return launch_softmax_backward_block<16>(g, y, dx, rows, d, st);
+        return launch_softmax_backward_block<32>(g, y, dx, rows, d, st);
+    }
+    const int gb = grid_for(rows, 8);
+    const int d = (int)std::min<int64_t>(D, 1 << 30);
+    if (D <= 32) softmax_backward_reg_kernel<1><<<gb, 256, 0, st>>>(g, y, dx, rows, d);
+    else if (D <= 64) softmax_backward_reg_kernel<2><<<gb, 256, 0, st>>>(g, y, dx, rows, d);
+    else if (D <= 128) softmax_backward_reg_kernel<4><<<gb, 256, 0, st>>>(g, y, dx, rows, d);
+    else if (D <= 256) softmax_backward_reg_kernel<8><<<gb, 256, 0, st>>>(g, y, dx, rows, d);
+    else if (D <= 512) softmax_backward_reg_kernel<16><<<gb, 256, 0, st>>>(g, y, dx, rows, d);
+    else if (D <= 1024) softmax_backward_reg_kernel<32><<<gb, 256, 0, st>>>(g, y, dx, rows, d);
+    else softmax_backward_kernel<<<gb, 256, 0, st>>>(g, y, dx, rows, D);
     count_launch();
     return check_launch("softmax_backward");
 }

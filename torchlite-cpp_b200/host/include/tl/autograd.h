@@ -53,8 +53,35 @@ class ReshapeBackward : public GradFunction {
     void backward(const Tensor& grad_output) override;
 };
 
+// src/autograd.cpp:68-71: each input receives sum_to(grad, its shape)
 class AddBackward : public GradFunction {
   public:
+    void backward(const Tensor& grad_output) override;
+};
+
+// src/autograd.cpp:82-84
+class ScaleBackward : public GradFunction {
+  public:
+    float scalar = 1.0f;
+    void backward(const Tensor& grad_output) override;
+};
+
+// src/autograd.cpp:228-256 (row dot rounded as the reference's x86-64-v4 build)
+class SoftmaxBackward : public GradFunction {
+  public:
+    Tensor output_cache;
+    void backward(const Tensor& grad_output) override;
+};
+
+// matmul_add / matmul_scale: the reference's AddBackward or ScaleBackward
+// followed by MatmulBackward, in one node
+class FusedMatmulBackward : public GradFunction {
+  public:
+    Tensor a_cache, b_cache;
+    bool has_bias = false;  // inputs[2] is the bias
+    float scalar = 1.0f;
+    bool apply_scale = false;
+    int mode = -1;
     void backward(const Tensor& grad_output) override;
 };
 

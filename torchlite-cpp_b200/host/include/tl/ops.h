@@ -24,8 +24,22 @@ Tensor reshape(const Tensor& a, const std::vector<int64_t>& new_sizes);
 Tensor unsqueeze(const Tensor& input, int64_t dim);
 Tensor squeeze(const Tensor& input, int64_t dim);
 
-// element-wise addition of same-shape tensors (src/ops.cpp:75-103, no broadcast)
+// element-wise addition with NumPy broadcasting (src/ops.cpp:74-103)
 Tensor add(const Tensor& a, const Tensor& b);
+// scale a tensor by a factor (src/ops.cpp:963-983)
+Tensor scale(const Tensor& input, float scalar);
+// softmax over the last dim (src/ops.cpp:985-1037); CUDA's expf, so a few
+// ulp from the reference; its backward is bit-identical
+Tensor softmax(const Tensor& input);
+// reduce a gradient to a broadcast input's shape (sum_to, src/autograd.cpp:24-36)
+Tensor sum_to(const Tensor& grad, const std::vector<int64_t>& target_shape);
+
+// Fused forms of the reference's call sequences, same results and gradients:
+//   matmul_add(x, w, b)   == add(matmul(x, w), b)        (Linear::forward, src/nn.cpp:77-83)
+//   matmul_scale(q, k, s) == scale(matmul(q, k), s)      (MultiHeadAttention, src/nn.cpp:423-424)
+// The bias add / scale run in the GEMM's epilogue; b is 1-D of length N.
+Tensor matmul_add(const Tensor& a, const Tensor& b, const Tensor& bias);
+Tensor matmul_scale(const Tensor& a, const Tensor& b, float scalar);
 // sum along a dimension (src/ops.cpp:1181-1233); no autograd node
 Tensor sum(const Tensor& input, int64_t dim, bool keepdim = false);
 

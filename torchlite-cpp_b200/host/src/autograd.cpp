@@ -80,9 +80,43 @@ void ReshapeBackward::backward(const Tensor& grad_output) {
     accumulate_grad(inputs[0], reshape(grad_output, input_shape));
 }
 
+// src/autograd.cpp:68-71
 void AddBackward::backward(const Tensor& grad_output) {
-    accumulate_grad(inputs[0], grad_output);
-    accumulate_grad(inputs[1], grad_output);
+    if (inputs[0].requires_grad) accumulate_grad(inputs[0], sum_to(grad_output, inputs[0].sizes()));
+    if (inputs[1].requires_grad) accumulate_grad(inputs[1], sum_to(grad_output, inputs[1].sizes()));
+}
+
+// src/autograd.cpp:82-84
+void ScaleBackward::backward(const Tensor& grad_output) {
+    accumulate_grad(inputs[0], scale(grad_output, scalar));
+}
+
+// src/autograd.cpp:228-256
+void SoftmaxBackward::backward(const Tensor& grad_output) {
+    if (!inputs[0].requires_grad) return;
+    Tensor dx = Tensor::device_empty(output_cache.sizes());
+    if (dx.numel() > 0) {
+        tlc_tensor g = dview(grad_output), y = dview(output_cache), vd = dview(dx);
+        check(tlc_softmax_backward(&g, &y, &vd, nullptr), "tlc_softmax_backward");
+    }
+    accumulate_grad(inputs[0], dx);
+}
+
+// ScaleBackward (scale(grad, s)) or AddBackward (grad to the product unchanged,
+// sum_to(grad, [N]) to the bias), then MatmulBackward, as the reference's
+// separate nodes would run them.
+void FusedMatmulBackward::backward(const Tensor& grad_output) {
+    Tensor g = apply_scale ? scale(grad_output, scalar) : grad_output;
+    if (has_bias && inputs[2].requires_grad)
+        accumulate_grad(inputs[2], sum_to(grad_output, inputs[2].sizes()));
+    MatmulBackward mm;
+    mm.inputs = {inputs[0], inputs[1]};
+    mm.a_cache = a_cache;
+    mm.b_cache = b_cache;
+    mm.squeeze_a = a_cache.sizes().size() == 1;
+    mm.squeeze_b = b_cache.sizes().size() == 1;
+    mm.mode = mode;
+    mm.backward(g);
 }
 
 }  // namespace tl

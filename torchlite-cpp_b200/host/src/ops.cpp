@@ -6,6 +6,8 @@
 
 #include <tlc.h>
 
+#include <algorithm>
+#include <memory>
 #include <new>
 #include <stdexcept>
 #include <string>
@@ -131,16 +133,118 @@ Tensor squeeze(const Tensor& input, int64_t dim) {
     return reshape(input, s);
 }
 
+// The result shape of a broadcast (src/ops.cpp:55-72; a size-0 dim against a
+// size-1 dim gives 0).
+std::vector<int64_t> broadcast_sizes(const std::vector<int64_t>& a, const std::vector<int64_t>& b) {
+    const size_t nd = std::max(a.size(), b.size());
+    std::vector<int64_t> out(nd);
+    for (size_t i = 0; i < nd; ++i) {
+        const int64_t sa = i < nd - a.size() ? 1 : a[i - (nd - a.size())];
+        const int64_t sb = i < nd - b.size() ? 1 : b[i - (nd - b.size())];
+        if (sa != sb && sa != 1 && sb != 1)
+            throw std::invalid_argument("Incompatible dimensions for broadcasting");
+        out[i] = sa == 1 ? sb : sa;
+    }
+    return out;
+}
+
+// src/ops.cpp:74-103
 Tensor add(const Tensor& a_in, const Tensor& b_in) {
-    if (a_in.sizes() != b_in.sizes())
-        throw std::invalid_argument("add: shapes must match (broadcasting add is not on the GPU path)");
-    Tensor a = a_in.contiguous(), b = b_in.contiguous();
-    Tensor out = Tensor::device_empty(a.sizes());
-    if (out.numel() > 0)
-        check(tlc_add(a.device_data(), b.device_data(), out.device_data(), out.numel(), nullptr),
-              "tlc_add");
+    Tensor out = Tensor::device_empty(broadcast_sizes(a_in.sizes(), b_in.sizes()));
+    if (out.numel() > 0) {
+        tlc_tensor va = view_of(a_in, true), vb = view_of(b_in, true), vo = view_of(out, false);
+        vo.data = out.device_data();
+        check(tlc_add_tensors(&va, &vb, &vo, nullptr), "tlc_add_tensors");
+    }
     if (a_in.requires_grad || b_in.requires_grad) track<AddBackward>(out, {&a_in, &b_in});
     return out;
+}
+
+// src/ops.cpp:963-983
+Tensor scale(const Tensor& input, float scalar) {
+    Tensor out = Tensor::device_empty(input.sizes());
+    if (out.numel() > 0) {
+        tlc_tensor vx = view_of(input, true), vo = view_of(out, false);
+        vo.data = out.device_data();
+        check(tlc_scale(&vx, scalar, &vo, nullptr), "tlc_scale");
+    }
+    if (input.requires_grad) {
+        if (auto fn = track<ScaleBackward>(out, {&input})) fn->scalar = scalar;
+    }
+    return out;
+}
+
+// src/ops.cpp:985-1037
+Tensor softmax(const Tensor& input) {
+    if (input.sizes().empty()) throw std::invalid_argument("Softmax requires at least 1D tensor");
+    Tensor out = Tensor::device_empty(input.sizes());
+    if (out.numel() > 0) {
+        tlc_tensor vx = view_of(input, true), vo = view_of(out, false);
+        vo.data = out.device_data();
+        check(tlc_softmax(&vx, &vo, nullptr), "tlc_softmax");
+    }
+    if (input.requires_grad) {
+        if (auto fn = track<SoftmaxBackward>(out, {&input})) fn->output_cache = out;
+    }
+    return out;
+}
+
+// src/autograd.cpp:24-36
+Tensor sum_to(const Tensor& grad, const std::vector<int64_t>& target_shape) {
+    Tensor out = Tensor::device_empty(target_shape);
+    tlc_tensor vx = view_of(grad, true), vo = view_of(out, false);
+    vo.data = out.numel() > 0 ? out.device_data() : nullptr;
+    check(tlc_sum_to(&vx, &vo, nullptr), "tlc_sum_to");
+    return out;
+}
+
+namespace {
+
+Tensor matmul_fused(const Tensor& a_in, const Tensor& b_in, const Tensor* bias, float scalar,
+                    bool apply_scale, int mode) {
+    tlc_tensor va = view_of(a_in, false), vb = view_of(b_in, false);
+    int32_t nd = 0;
+    int64_t sz[TLC_MAX_DIMS];
+    check(tlc_matmul_shape(&va, &vb, &nd, sz), "tlc_matmul_shape");
+    Tensor out = Tensor::device_empty(std::vector<int64_t>(sz, sz + nd));
+    if (out.numel() > 0) {
+        va = view_of(a_in, true);
+        vb = view_of(b_in, true);
+        tlc_tensor vo = view_of(out, false);
+        vo.data = out.device_data();
+        tlc_tensor vbias{};
+        if (bias) vbias = view_of(*bias, true);
+        check(tlc_matmul_fused(&va, &vb, apply_scale ? scalar : 1.0f, bias ? &vbias : nullptr, &vo,
+                               mode, nullptr),
+              "tlc_matmul_fused");
+    }
+    const bool grads = a_in.requires_grad || b_in.requires_grad || (bias && bias->requires_grad);
+    if (grads) {
+        std::shared_ptr<FusedMatmulBackward> fn =
+            bias ? track<FusedMatmulBackward>(out, {&a_in, &b_in, bias})
+                 : track<FusedMatmulBackward>(out, {&a_in, &b_in});
+        if (fn) {
+            fn->a_cache = a_in;
+            fn->b_cache = b_in;
+            fn->has_bias = bias != nullptr;
+            fn->scalar = scalar;
+            fn->apply_scale = apply_scale;
+            fn->mode = mode;
+        }
+    }
+    return out;
+}
+
+}  // namespace
+
+Tensor matmul_add(const Tensor& a, const Tensor& b, const Tensor& bias) {
+    if (bias.sizes().size() != 1)
+        throw std::invalid_argument("matmul_add: bias must be 1-D");
+    return matmul_fused(a, b, &bias, 1.0f, false, TLC_MODE_DEFAULT);
+}
+
+Tensor matmul_scale(const Tensor& a, const Tensor& b, float scalar) {
+    return matmul_fused(a, b, nullptr, scalar, true, TLC_MODE_DEFAULT);
 }
 
 Tensor sum(const Tensor& input, int64_t dim, bool keepdim) {
