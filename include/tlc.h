@@ -43,7 +43,8 @@ typedef enum tlc_status {
     TLC_ERR_UNSUPPORTED = 2,
     TLC_ERR_CUDA = 3,
     TLC_ERR_OUT_OF_MEMORY = 4,
-    TLC_ERR_TIMEOUT = 5 /* a bounded wait inside a kernel gave up; see tlc_last_error() */
+    TLC_ERR_TIMEOUT = 5, /* a bounded wait inside a kernel gave up; see tlc_last_error() */
+    TLC_ERR_IO = 6       /* file error (the reference throws std::runtime_error here) */
 } tlc_status;
 
 typedef enum tlc_mode {
@@ -230,6 +231,21 @@ int tlc_softmax_backward(const tlc_tensor* grad, const tlc_tensor* y, tlc_tensor
  * x's shape (leading dims dropped, dims of size 1 kept); sequential sums from
  * 0.0f in the reference's order. */
 int tlc_sum_to(const tlc_tensor* x, tlc_tensor* out, void* stream);
+
+/* ---- TLMD model files straight to / from device memory --------------------
+ * load_model / save_model (src/model_io.cpp:7-94): "TLMD", int32 version 1,
+ * int64 count, then per tensor int64 ndim, int64 shape[ndim], float data.
+ * tlc_load_tlmd checks the header and each tensor's ndim and shape against
+ * `dst` (contiguous device tensors, in order) with the reference's messages
+ * (TLC_ERR_IO: "load_model: cannot open file: <path>", "... no TLMD magic
+ * header in <path>", "... unsupported version", "... tensor count mismatch",
+ * "... ndim mismatch", "... shape mismatch"; and "load_model: file truncated"
+ * for a file that ends early) and streams the data into device memory through
+ * page-locked staging buffers, reads overlapping copies.  tlc_save_tlmd
+ * writes device tensors (any strides) in the same format.  Both return when
+ * all copies are done. */
+int tlc_load_tlmd(const char* path, int32_t count, const tlc_tensor* dst, void* stream);
+int tlc_save_tlmd(const char* path, int32_t count, const tlc_tensor* src, void* stream);
 
 /* ---- multi-GPU partitioning ------------------------------------------------
  * One process per GPU.  A batched GEMM is split over its flattened batch

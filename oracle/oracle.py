@@ -317,6 +317,12 @@ class TLRef:
         L.tlref_softmax.argtypes = [_f32p, ctypes.c_int, i64p, _f32p, _f32p, _f32p, _i64,
                                     ctypes.c_char_p, ctypes.c_int]
         L.tlref_softmax.restype = ctypes.c_int
+        L.tlref_save_model.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                       i64p, _f32p, ctypes.c_char_p, ctypes.c_int]
+        L.tlref_save_model.restype = ctypes.c_int
+        L.tlref_load_model.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                       i64p, _f32p, ctypes.c_char_p, ctypes.c_int]
+        L.tlref_load_model.restype = ctypes.c_int
         self.L = L
 
     def hardware_threads(self) -> int:
@@ -392,6 +398,36 @@ class TLRef:
                                 max(1, out.size), err, 256)
         if rc != 0:
             raise RuntimeError(f"tlref_scale rc={rc}: {err.value.decode()}")
+        return out
+
+    @staticmethod
+    def _pack(shapes):
+        nd = (ctypes.c_int * max(1, len(shapes)))(*[len(s) for s in shapes])
+        flat = [d for s in shapes for d in s]
+        return nd, (_i64 * max(1, len(flat)))(*flat)
+
+    def save_model(self, path, tensors):
+        """tl::save_model of the given arrays (in order)."""
+        ts = [np.array(t, dtype=np.float32, order="C", copy=True) for t in tensors]  # keeps 0-D
+        nd, sh = self._pack([t.shape for t in ts])
+        data = np.concatenate([t.reshape(-1) for t in ts]) if ts else np.zeros(1, np.float32)
+        data = np.ascontiguousarray(data if data.size else np.zeros(1, np.float32))
+        err = ctypes.create_string_buffer(512)
+        if self.L.tlref_save_model(str(path).encode(), len(ts), nd, sh, _fp(data), err, 512):
+            raise RuntimeError(err.value.decode())
+
+    def load_model(self, path, shapes):
+        """tl::load_model into fresh tensors of these shapes; returns the arrays."""
+        nd, sh = self._pack(shapes)
+        sizes = [int(np.prod(s, dtype=np.int64)) for s in shapes]
+        data = np.zeros(max(1, sum(sizes)), np.float32)
+        err = ctypes.create_string_buffer(512)
+        if self.L.tlref_load_model(str(path).encode(), len(shapes), nd, sh, _fp(data), err, 512):
+            raise RuntimeError(err.value.decode())
+        out, off = [], 0
+        for s, n in zip(shapes, sizes):
+            out.append(data[off:off + n].reshape(s))
+            off += n
         return out
 
     def softmax(self, x, grad=None):

@@ -8,6 +8,7 @@
 // Every function builds reference tl::Tensor objects from flat host buffers,
 // runs the reference code path unchanged, and copies results out.
 #include <tl/autograd.h>
+#include <tl/model_io.h>
 #include <tl/ops.h>
 #include <tl/tensor.h>
 
@@ -129,6 +130,48 @@ int tlref_softmax(const float* x, int nd, const int64_t* sz, const float* grad, 
         Y.grad() = make(grad, nd, sz);
         Y.backward();
         return copy_out(X.grad(), dx, cap, nullptr, nullptr);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+// tl::save_model of `count` tensors (shapes flattened in `shapes`, data in
+// `data`, both in order); tl::load_model of a file into tensors of the given
+// shapes, data out in `data`.  Errors (std::runtime_error) as text in err.
+int tlref_save_model(const char* path, int count, const int* ndims, const int64_t* shapes,
+                     const float* data, char* err, int errlen) {
+    try {
+        std::vector<tl::Tensor> ts;
+        for (int i = 0; i < count; ++i) {
+            ts.push_back(make(data, ndims[i], shapes));
+            data += ts.back().numel();
+            shapes += ndims[i];
+        }
+        std::vector<tl::Tensor*> ps;
+        for (auto& t : ts) ps.push_back(&t);
+        tl::save_model(path, ps);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+int tlref_load_model(const char* path, int count, const int* ndims, const int64_t* shapes,
+                     float* data, char* err, int errlen) {
+    try {
+        std::vector<tl::Tensor> ts;
+        for (int i = 0; i < count; ++i) {
+            ts.push_back(tl::Tensor(std::vector<int64_t>(shapes, shapes + ndims[i])));
+            shapes += ndims[i];
+        }
+        std::vector<tl::Tensor*> ps;
+        for (auto& t : ts) ps.push_back(&t);
+        tl::load_model(path, ps);
+        for (auto& t : ts) {
+            if (t.numel()) std::memcpy(data, t.data(), sizeof(float) * t.numel());
+            data += t.numel();
+        }
+        return 0;
     } catch (const std::exception& e) {
         return fail(e, err, errlen);
     }

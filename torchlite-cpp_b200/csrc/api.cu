@@ -708,6 +708,7 @@ const char* tlc_status_string(int st) {
         case TLC_ERR_CUDA: return "CUDA error";
         case TLC_ERR_OUT_OF_MEMORY: return "out of memory";
         case TLC_ERR_TIMEOUT: return "kernel wait timed out";
+        case TLC_ERR_IO: return "I/O error";
         default: return "unknown status";
     }
 }

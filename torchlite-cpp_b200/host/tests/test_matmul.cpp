@@ -7,11 +7,13 @@
 //   tl_tests            all tests (needs a GPU)
 //   tl_tests --cpu      only the shape / exception tests (no GPU needed)
 #include <tl/autograd.h>
+#include <tl/model_io.h>
 #include <tl/ops.h>
 #include <tl/tensor.h>
 #include <tlc.h>
 
 #include <cmath>
+#include <cstdio>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -251,6 +253,35 @@ static void test_tensor_core_modes() {
     std::cout << "tf32 / 3xtf32 tolerance ok\n";
 }
 
+// tests/test_model_io.cpp of the reference: save, load into fresh tensors of
+// the same shapes (values identical), a shape mismatch throws runtime_error;
+// here the data moves straight between the file and device storage.
+static void test_model_io() {
+    tl::Tensor W({4, 8}), b({8}), s(std::vector<int64_t>{});
+    for (int64_t i = 0; i < W.numel(); ++i) W.data()[i] = 0.25f * i - 3.0f;
+    for (int64_t i = 0; i < b.numel(); ++i) b.data()[i] = -0.5f * i;
+    s.data()[0] = 7.0f;
+    tl::Tensor Wd = tl::matmul(W, tl::ones({8, 8}));  // a device-only tensor (product)
+    const std::string path = "tl_test_model_io.tl";
+    tl::save_model(path, {&W, &b, &s, &Wd});
+    tl::Tensor W2({4, 8}), b2({8}), s2(std::vector<int64_t>{}), Wd2({4, 8});
+    tl::load_model(path, {&W2, &b2, &s2, &Wd2});
+    for (int64_t i = 0; i < W.numel(); ++i) CHECK(same_bits(W.data()[i], W2.data()[i]));
+    for (int64_t i = 0; i < b.numel(); ++i) CHECK(same_bits(b.data()[i], b2.data()[i]));
+    CHECK(s2.data()[0] == 7.0f);
+    for (int64_t i = 0; i < Wd.numel(); ++i) CHECK(same_bits(Wd.data()[i], Wd2.data()[i]));
+    tl::Tensor wrong({4, 16});
+    bool threw = false;
+    try {
+        tl::load_model(path, {&wrong, &b2, &s2, &Wd2});
+    } catch (const std::runtime_error& e) {
+        threw = std::string(e.what()) == "load_model: shape mismatch";
+    }
+    CHECK(threw);
+    std::remove(path.c_str());
+    std::cout << "model_io ok\n";
+}
+
 int main(int argc, char** argv) {
     const bool cpu_only = argc > 1 && std::string(argv[1]) == "--cpu";
     test_errors();
@@ -260,6 +291,7 @@ int main(int argc, char** argv) {
     test_backward_levels();
     test_linear_backward_transposed();
     test_tensor_core_modes();
+    test_model_io();
     std::cout << "all tl:: tests passed\n";
     return 0;
 }

@@ -22,7 +22,7 @@ MAX_DIMS = 8
 
 MODES = {"exact": 0, "fp32": 0, "tf32": 1, "3xtf32": 2, "default": -1}
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "CUDA error",
-          4: "out of memory", 5: "kernel wait timed out"}
+          4: "out of memory", 5: "kernel wait timed out", 6: "I/O error"}
 
 
 class TLCError(RuntimeError):
@@ -90,6 +90,8 @@ SIGNATURES = {
     "tlc_softmax": ([_T, _T, _v], _i),
     "tlc_softmax_backward": ([_T, _T, _T, _v], _i),
     "tlc_sum_to": ([_T, _T, _v], _i),
+    "tlc_load_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
+    "tlc_save_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
     "tlc_shard_range": ([_i64, _i, _i, _P(_i64), _P(_i64)], _i),
     "tlc_shard_cols": ([_i64, _i, _i, _i64, _P(_i64), _P(_i64)], _i),
     "tlc_gather_colblocks": ([_v, _v, _i64, _i64, _i, _P(_i64), _v], _i),
@@ -337,6 +339,33 @@ def sum_to(x, target, out=None, stream=None):
     vx, vo = view_of(x), view_of(out)
     _check(lib().tlc_sum_to(ctypes.byref(vx), ctypes.byref(vo), _stream_ptr(stream)))
     return out
+
+
+def _views(tensors):
+    arr = (Tensor * max(1, len(tensors)))()
+    for i, t in enumerate(tensors):
+        arr[i] = view_of(t)
+    return arr
+
+
+def _io_stream(stream):
+    # torch's current stream when a GPU is there; otherwise the legacy stream
+    # (the file checks that fail before any copy need no device)
+    import torch
+    return _stream_ptr(stream) if torch.cuda.is_available() else None
+
+
+def load_tlmd(path, tensors, stream=None):
+    """load_model into CUDA tensors (contiguous, shapes as stored)."""
+    _check(lib().tlc_load_tlmd(str(path).encode(), len(tensors), _views(tensors),
+                               _io_stream(stream)))
+    return tensors
+
+
+def save_tlmd(path, tensors, stream=None):
+    """save_model from CUDA tensors."""
+    _check(lib().tlc_save_tlmd(str(path).encode(), len(tensors), _views(tensors),
+                               _io_stream(stream)))
 
 
 def shard_range(count, world, rank):
