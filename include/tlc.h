@@ -232,6 +232,31 @@ int tlc_softmax_backward(const tlc_tensor* grad, const tlc_tensor* y, tlc_tensor
  * 0.0f in the reference's order. */
 int tlc_sum_to(const tlc_tensor* x, tlc_tensor* out, void* stream);
 
+/* ---- conv2d ------------------------------------------------------------------
+ * conv2d (src/ops.cpp:1443-1548) and Conv2dBackward (src/autograd.cpp:386-517)
+ * for NCHW fp32 device tensors: input [N, C_in, H, W], weight
+ * [C_out, C_in/groups, kH, kW], bias [C_out] or NULL, out [N, C_out, H_out,
+ * W_out] with H_out = (H + 2*padding - kH) / stride + 1 (C++ division).
+ * im2col for all images and groups at once, then one batched GEMM per
+ * product in `mode`; exact mode is bit-identical to the reference, backward
+ * included (its per-image += order for the weight gradient, col2im's order
+ * for the input gradient, its (n, oh, ow) order for the bias gradient).
+ * Errors: the reference's ("conv2d: groups must be > 0", "conv2d: groups
+ * doesn't divide C_in", "conv2d: groups doesn't divide C_out",
+ * "conv2d: weight.sizes()[1] must equal C_in / groups"), plus non-4-D
+ * operands and stride < 1 (the reference would index out of range or divide
+ * by zero).  Backward outputs are contiguous and overwritten (0 + gradient,
+ * as accumulate_grad stores a first gradient); pass NULL to skip one. */
+int tlc_conv2d_shape(const tlc_tensor* input, const tlc_tensor* weight, int64_t stride,
+                     int64_t padding, int64_t groups, int64_t* out_sizes);
+int tlc_conv2d(const tlc_tensor* input, const tlc_tensor* weight, const tlc_tensor* bias,
+               int64_t stride, int64_t padding, int64_t groups, tlc_tensor* out, int mode,
+               void* stream);
+int tlc_conv2d_backward(const tlc_tensor* grad_output, const tlc_tensor* input,
+                        const tlc_tensor* weight, int64_t stride, int64_t padding, int64_t groups,
+                        tlc_tensor* d_input, tlc_tensor* d_weight, tlc_tensor* d_bias, int mode,
+                        void* stream);
+
 /* ---- TLMD model files straight to / from device memory --------------------
  * load_model / save_model (src/model_io.cpp:7-94): "TLMD", int32 version 1,
  * int64 count, then per tensor int64 ndim, int64 shape[ndim], float data.

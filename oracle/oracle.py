@@ -222,6 +222,96 @@ def softmax(x: np.ndarray) -> np.ndarray:
     return out
 
 
+def _conv_out(H, W, kH, kW, stride, padding):
+    # (H + 2p - kH) / stride + 1 with C++'s truncating division
+    def tdiv(a, b):
+        return -((-a) // b) if a < 0 else a // b
+    return tdiv(H + 2 * padding - kH, stride) + 1, tdiv(W + 2 * padding - kW, stride) + 1
+
+
+def _im2col(x_n, c0, C_in_g, kH, kW, stride, padding, H_out, W_out):
+    """col [C_in_g*kH*kW, H_out*W_out] of image x_n [C_in, H, W], channels
+    c0.. (src/ops.cpp:1479-1511): zero outside the image."""
+    _, H, W = x_n.shape
+    col = np.zeros((C_in_g * kH * kW, H_out * W_out), np.float32)
+    oh = np.arange(H_out)[:, None]
+    ow = np.arange(W_out)[None, :]
+    for c in range(C_in_g):
+        for kh in range(kH):
+            for kw in range(kW):
+                ih = oh * stride - padding + kh
+                iw = ow * stride - padding + kw
+                ok = (ih >= 0) & (ih < H) & (iw >= 0) & (iw < W)
+                v = np.zeros((H_out, W_out), np.float32)
+                v[ok] = x_n[c0 + c][np.broadcast_to(ih, ok.shape)[ok], np.broadcast_to(iw, ok.shape)[ok]]
+                col[c * kH * kW + kh * kW + kw] = v.reshape(-1)
+    return col
+
+
+def conv2d(x, w, b, stride=1, padding=0, groups=1):
+    """conv2d, src/ops.cpp:1443-1548: per image and group, W_g . im2col
+    (gemm_blocked's chain), then add(result, bias[1, C_out, 1, 1])."""
+    x = np.asarray(x, np.float32)
+    w = np.asarray(w, np.float32)
+    N, C_in, H, W = x.shape
+    C_out, C_in_g, kH, kW = w.shape
+    C_out_g = C_out // groups
+    H_out, W_out = _conv_out(H, W, kH, kW, stride, padding)
+    wr = np.ascontiguousarray(w.reshape(C_out, -1))
+    out = np.zeros((N, C_out, H_out * W_out), np.float32)
+    for n in range(N):
+        for g in range(groups):
+            col = _im2col(x[n], g * C_in_g, C_in_g, kH, kW, stride, padding, H_out, W_out)
+            out[n, g * C_out_g:(g + 1) * C_out_g] = gemm2d(wr[g * C_out_g:(g + 1) * C_out_g], col)
+    out = out.reshape(N, C_out, H_out, W_out)
+    if b is not None and np.asarray(b).size:
+        out = np.add(out, np.asarray(b, np.float32).reshape(1, C_out, 1, 1), dtype=np.float32)
+    return out
+
+
+def conv2d_backward(go, x, w, stride=1, padding=0, groups=1):
+    """Conv2dBackward, src/autograd.cpp:386-517, then accumulate_grad (0 + d):
+    (d_input, d_weight, d_bias)."""
+    go = np.asarray(go, np.float32)
+    x = np.asarray(x, np.float32)
+    w = np.asarray(w, np.float32)
+    N, C_in, H, W = x.shape
+    C_out, C_in_g, kH, kW = w.shape
+    C_out_g = C_out // groups
+    H_out, W_out = go.shape[2], go.shape[3]
+    patch = C_in_g * kH * kW
+    wr = np.ascontiguousarray(w.reshape(C_out, patch))
+    gw = np.zeros((C_out, patch), np.float32)
+    gi = np.zeros((N, C_in, H, W), np.float32)
+    gb = np.zeros((C_out,), np.float32)
+    oh = np.arange(H_out)[:, None]
+    ow = np.arange(W_out)[None, :]
+    for n in range(N):
+        go_n = go[n].reshape(C_out, H_out * W_out)
+        for g in range(groups):
+            go_ng = np.ascontiguousarray(go_n[g * C_out_g:(g + 1) * C_out_g])
+            col = _im2col(x[n], g * C_in_g, C_in_g, kH, kW, stride, padding, H_out, W_out)
+            band = slice(g * C_out_g, (g + 1) * C_out_g)
+            gw[band] = np.add(gw[band], gemm2d(go_ng, np.ascontiguousarray(col.T)), dtype=np.float32)
+            gcol = gemm2d(np.ascontiguousarray(wr[band].T), go_ng)
+            # col2im in the reference's loop order: per pixel, (kh, kw) ascending
+            for kh in range(kH):
+                for kw in range(kW):
+                    ih = np.broadcast_to(oh * stride - padding + kh, (H_out, W_out))
+                    iw = np.broadcast_to(ow * stride - padding + kw, (H_out, W_out))
+                    ok = (ih >= 0) & (ih < H) & (iw >= 0) & (iw < W)
+                    for c in range(C_in_g):
+                        vals = gcol[c * kH * kW + kh * kW + kw].reshape(H_out, W_out)
+                        ch = gi[n, g * C_in_g + c]
+                        ch[ih[ok], iw[ok]] = np.add(ch[ih[ok], iw[ok]], vals[ok], dtype=np.float32)
+    flat = go.reshape(N, C_out, H_out * W_out)
+    for n in range(N):
+        for hw in range(H_out * W_out):
+            gb = np.add(gb, flat[n, :, hw], dtype=np.float32)
+    z = np.float32(0.0)
+    return gi + z, gw.reshape(w.shape) + z, gb + z
+
+
 # SoftmaxBackward's row dot as the reference's Release build rounds it: blocks
 # of SOFTMAX_BWD_VEC products rounded then added, the D mod SOFTMAX_BWD_VEC tail
 # fused (8: the x86-64-v4 / AVX-512 build, the ISA of the GPU hosts).
@@ -323,6 +413,9 @@ class TLRef:
         L.tlref_load_model.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                        i64p, _f32p, ctypes.c_char_p, ctypes.c_int]
         L.tlref_load_model.restype = ctypes.c_int
+        L.tlref_conv2d.argtypes = [_f32p, i64p, _f32p, i64p, _f32p, _i64, _i64, _i64, _f32p, _f32p,
+                                   _f32p, _f32p, _f32p, ctypes.c_char_p, ctypes.c_int]
+        L.tlref_conv2d.restype = ctypes.c_int
         self.L = L
 
     def hardware_threads(self) -> int:
@@ -429,6 +522,28 @@ class TLRef:
             out.append(data[off:off + n].reshape(s))
             off += n
         return out
+
+    def conv2d(self, x, w, b, stride=1, padding=0, groups=1, grad=None):
+        """tl::conv2d; with grad also (x.grad, w.grad, b.grad) after backward."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        bb = None if b is None else np.ascontiguousarray(b, np.float32)
+        N, C_in, H, W = x.shape
+        C_out, _, kH, kW = w.shape
+        H_out, W_out = _conv_out(H, W, kH, kW, stride, padding)
+        out = np.empty((N, C_out, max(H_out, 0), max(W_out, 0)), np.float32)
+        g = None if grad is None else np.ascontiguousarray(grad, np.float32)
+        dx = np.empty_like(x)
+        dw = np.empty_like(w)
+        db = np.empty((C_out,), np.float32)
+        err = ctypes.create_string_buffer(512)
+        rc = self.L.tlref_conv2d(_fp(x), (_i64 * 4)(*x.shape), _fp(w), (_i64 * 4)(*w.shape),
+                                 None if bb is None else _fp(bb), stride, padding, groups,
+                                 None if g is None else _fp(g), _fp(out), _fp(dx), _fp(dw), _fp(db),
+                                 err, 512)
+        if rc:
+            raise ValueError(err.value.decode())
+        return out if g is None else (out, dx, dw, db)
 
     def softmax(self, x, grad=None):
         """y = tl::softmax(x); with grad, also x.grad after y.backward() (SoftmaxBackward

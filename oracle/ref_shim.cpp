@@ -177,4 +177,33 @@ int tlref_load_model(const char* path, int count, const int* ndims, const int64_
     }
 }
 
+// out = tl::conv2d(X, W, b, stride, padding, groups); with grad: out.grad() =
+// grad, out.backward(), then X.grad, W.grad, b.grad.  b may be NULL (empty).
+int tlref_conv2d(const float* x, const int64_t* xs, const float* w, const int64_t* ws,
+                 const float* b, int64_t stride, int64_t padding, int64_t groups,
+                 const float* grad, float* out, float* dx, float* dw, float* db, char* err,
+                 int errlen) {
+    try {
+        tl::Tensor X = make(x, 4, xs), W = make(w, 4, ws);
+        const int64_t cout[1] = {ws[0]};
+        tl::Tensor B = b ? make(b, 1, cout) : tl::Tensor();
+        if (grad) {
+            X.set_requires_grad(true);
+            W.set_requires_grad(true);
+            if (b) B.set_requires_grad(true);
+        }
+        tl::Tensor Y = tl::conv2d(X, W, B, stride, padding, groups);
+        int rc = copy_out(Y, out, Y.numel() ? Y.numel() : 1, nullptr, nullptr);
+        if (rc || !grad) return rc;
+        Y.grad() = make(grad, 4, Y.sizes().data());
+        Y.backward();
+        rc = copy_out(X.grad(), dx, X.numel(), nullptr, nullptr);
+        if (!rc) rc = copy_out(W.grad(), dw, W.numel(), nullptr, nullptr);
+        if (!rc && b) rc = copy_out(B.grad(), db, B.numel(), nullptr, nullptr);
+        return rc;
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
 }  // extern "C"

@@ -1,7 +1,8 @@
 // The scenarios of ref_callers_main.cpp (Linear forward + backward on 2-D and
 // batched inputs, MultiHeadAttention forward + backward, a broadcast batched
 // matmul, X . W^T), written against the device-resident C++ tl:: layer
-// (torchlite-cpp_b200/host) instead of the reference library: the same seeded
+// (torchlite-cpp_b200/host) instead of the reference library (and a grouped,
+// strided Conv2d through tl::conv2d): the same seeded
 // inputs in the same order, the same ops in the reference's order
 // (src/nn.cpp:77-83 Linear::forward, :401-445 MultiHeadAttention::forward),
 // with Linear's bias add and the attention scale fused into their GEMMs.
@@ -131,6 +132,21 @@ int main(int argc, char** argv) {
         dump(y);
         dump(x.grad());
         dump(w.grad());
+    }
+    {
+        tl::Tensor w = filled({6, 2, 3, 3}, 0.2f);
+        tl::Tensor b = filled({6}, 0.1f);
+        w.set_requires_grad(true);
+        b.set_requires_grad(true);
+        tl::Tensor x = filled({2, 4, 9, 11});
+        x.set_requires_grad(true);
+        tl::Tensor y = tl::conv2d(x, w, b, 2, 1, 2);
+        y.grad() = filled(y.sizes());
+        y.backward();
+        dump(y);
+        dump(x.grad());
+        dump(w.grad());
+        dump(b.grad());
     }
     std::FILE* f = std::fopen(argv[1], "wb");
     if (!f) return 3;

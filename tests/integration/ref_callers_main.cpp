@@ -123,6 +123,24 @@ int main(int argc, char** argv) {
         dump(x.grad());
         dump(w.grad());
     }
+    {  // nn::Conv2d (im2col + matmul, src/ops.cpp:1443-1548) forward and backward
+        tl::nn::Conv2d conv(4, 6, 3, 2, 1, 2);
+        tl::Tensor w = filled({6, 2, 3, 3}, 0.2f);
+        tl::Tensor b = filled({6}, 0.1f);
+        w.set_requires_grad(true);
+        b.set_requires_grad(true);
+        conv.set_weight(w);
+        conv.set_bias(b);
+        tl::Tensor x = filled({2, 4, 9, 11});
+        x.set_requires_grad(true);
+        tl::Tensor y = conv.forward(x);
+        y.grad() = filled(y.sizes());
+        y.backward();
+        dump(y);
+        dump(x.grad());
+        dump(grad_of(conv.weight()));
+        dump(grad_of(conv.bias()));
+    }
     std::FILE* f = std::fopen(argv[1], "wb");
     if (!f) return 3;
     std::fwrite(g_out.data(), sizeof(float), g_out.size(), f);

@@ -1,0 +1,127 @@
+"""conv2d (src/ops.cpp:1443-1548) and Conv2dBackward (src/autograd.cpp:386-517).
+
+CPU: the oracle's restatement (im2col, gemm_blocked's chain, col2im in the
+reference's loop order, the (n, oh, ow) bias chain) equals the reference
+library compiled from its sources, bit for bit, forward and backward.
+GPU: libtl_cuda's im2col + batched GEMM path (tlc_conv2d / _backward) equals
+the oracle bit for bit in exact mode; TF32 / 3xTF32 within their GEMM
+tolerances; the reference's error texts."""
+import numpy as np
+import pytest
+
+import inputs
+from oracle import oracle as O
+
+# (N, C_in, H, W, C_out, k, stride, padding, groups)
+CASES = [
+    (2, 3, 8, 8, 4, 3, 1, 1, 1),
+    (1, 4, 7, 9, 6, 3, 2, 0, 2),
+    (3, 6, 5, 5, 6, 1, 1, 0, 3),
+    (2, 2, 6, 6, 4, 5, 2, 2, 1),
+    (1, 8, 10, 10, 8, 3, 1, 1, 8),   # depthwise
+    (2, 3, 4, 4, 2, 3, 3, 0, 1),     # stride larger than the step the kernel needs
+    (1, 1, 2, 2, 1, 3, 2, 0, 1),     # input smaller than the kernel: (2 - 3) / 2 + 1 = 1 (C++ division)
+]
+
+
+def bits_equal(x, y):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.ascontiguousarray(y, np.float32)
+    return x.shape == y.shape and np.array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
+def case_data(case, seed):
+    N, C, H, W, Co, k, s, p, g = case
+    rng = np.random.default_rng(seed)
+    x = inputs.normal(rng, (N, C, H, W))
+    w = inputs.normal(rng, (Co, C // g, k, k))
+    b = inputs.normal(rng, (Co,))
+    return x, w, b, s, p, g
+
+
+def ref():
+    try:
+        return O.tlref()
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref not built")
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_matches_reference(case):
+    R = ref()
+    x, w, b, s, p, g = case_data(case, 7)
+    y = O.conv2d(x, w, b, s, p, g)
+    go = inputs.normal(np.random.default_rng(8), y.shape)
+    y_r, dx_r, dw_r, db_r = R.conv2d(x, w, b, s, p, g, grad=go)
+    assert bits_equal(y, y_r)
+    dx, dw, db = O.conv2d_backward(go, x, w, s, p, g)
+    assert bits_equal(dx, dx_r) and bits_equal(dw, dw_r) and bits_equal(db, db_r)
+
+
+def test_reference_errors():
+    R = ref()
+    x = np.ones((1, 4, 5, 5), np.float32)
+    for w, g, msg in [(np.ones((4, 4, 3, 3), np.float32), 0, "conv2d: groups must be > 0"),
+                      (np.ones((4, 4, 3, 3), np.float32), 3, "conv2d: groups doesn't divide C_in"),
+                      (np.ones((3, 2, 3, 3), np.float32), 2, "conv2d: groups doesn't divide C_out"),
+                      (np.ones((4, 3, 3, 3), np.float32), 2,
+                       "conv2d: weight.sizes()[1] must equal C_in / groups"),
+                      (np.ones((4, 4, 9, 3), np.float32), 1, "Tensor size must be positive integer"),
+                      (np.ones((4, 4, 9, 9), np.float32), 1, "reshape: negative dims not allowed")]:
+        with pytest.raises(ValueError) as e:
+            R.conv2d(x, w, None, 1, 0, g)
+        assert str(e.value) == msg
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES)
+def test_device_conv2d_exact(case):
+    torch = pytest.importorskip("torch")
+    import tlcuda
+    x, w, b, s, p, g = case_data(case, 11)
+    X, Wt, B = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    y = tlcuda.conv2d(X, Wt, B, s, p, g, mode="exact")
+    torch.cuda.synchronize()
+    assert bits_equal(y.cpu().numpy(), O.conv2d(x, w, b, s, p, g))
+    go = inputs.normal(np.random.default_rng(12), tuple(y.shape))
+    dx, dw, db = tlcuda.conv2d_backward(torch.from_numpy(go).cuda(), X, Wt, s, p, g, mode="exact")
+    torch.cuda.synchronize()
+    ox, ow_, ob = O.conv2d_backward(go, x, w, s, p, g)
+    assert bits_equal(dx.cpu().numpy(), ox)
+    assert bits_equal(dw.cpu().numpy(), ow_)
+    assert bits_equal(db.cpu().numpy(), ob)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode,tol", [("tf32", 1e-2), ("3xtf32", 1e-5)])
+def test_device_conv2d_tensor_cores(mode, tol):
+    torch = pytest.importorskip("torch")
+    import tlcuda
+    x, w, b, s, p, g = case_data((4, 32, 28, 28, 64, 3, 1, 1, 1), 13)
+    X, Wt, B = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    ref64 = torch.nn.functional.conv2d(X.double(), Wt.double(), B.double(), s, p, 1, g)
+    y = tlcuda.conv2d(X, Wt, B, s, p, g, mode=mode).double()
+    assert ((y - ref64).norm() / ref64.norm()).item() <= tol
+    go = torch.randn(tuple(y.shape), device="cuda")
+    Xd, Wd = X.double().requires_grad_(), Wt.double().requires_grad_()
+    torch.nn.functional.conv2d(Xd, Wd, None, s, p, 1, g).backward(go.double())
+    dx, dw, db = tlcuda.conv2d_backward(go, X, Wt, s, p, g, mode=mode)
+    assert ((dx.double() - Xd.grad).norm() / Xd.grad.norm()).item() <= tol
+    assert ((dw.double() - Wd.grad).norm() / Wd.grad.norm()).item() <= tol
+
+
+def test_library_errors_match_reference():
+    """The shape checks run on the host (tlc_conv2d_shape): the reference's texts."""
+    import tlcuda
+    x = np.ones((1, 4, 5, 5), np.float32)
+    for w, g, msg in [(np.ones((4, 4, 3, 3), np.float32), 0, "conv2d: groups must be > 0"),
+                      (np.ones((4, 4, 3, 3), np.float32), 3, "conv2d: groups doesn't divide C_in"),
+                      (np.ones((3, 2, 3, 3), np.float32), 2, "conv2d: groups doesn't divide C_out"),
+                      (np.ones((4, 3, 3, 3), np.float32), 2,
+                       "conv2d: weight.sizes()[1] must equal C_in / groups"),
+                      (np.ones((4, 4, 9, 3), np.float32), 1, "Tensor size must be positive integer"),
+                      (np.ones((4, 4, 9, 9), np.float32), 1, "reshape: negative dims not allowed")]:
+        vx, vw = tlcuda.view_of(x), tlcuda.view_of(w)
+        sz = (tlcuda.ctypes.c_int64 * 4)()
+        st = tlcuda.lib().tlc_conv2d_shape(tlcuda.ctypes.byref(vx), tlcuda.ctypes.byref(vw), 1, 0, g, sz)
+        assert st == 1 and tlcuda.lib().tlc_last_error().decode() == msg

@@ -62,7 +62,8 @@ def test_reference_callers_cpu_run(tmp_path):
     """The linked binary loads and runs its CPU arm without a GPU."""
     y, launches = _run(tmp_path, "cpu", {"TLC_REFERENCE_MATMUL": "1"})
     assert launches == 0
-    assert y.size == 213015 and np.isfinite(y).all() and np.abs(y).max() > 0
+    assert y.size == sum(int(np.prod(shp)) for _, shapes in SEGMENTS for shp in shapes)
+    assert np.isfinite(y).all() and np.abs(y).max() > 0
 
 
 @pytest.mark.gpu
@@ -89,6 +90,7 @@ SEGMENTS = [
     ("attention", [(2, 40, 96), (2, 40, 96), (96, 96), (96, 96)]),
     ("broadcast_matmul", [(3, 20, 25), (3, 20, 30), (30, 25)]),
     ("x_wt", [(65, 31), (65, 48), (31, 48)]),
+    ("conv2d", [(2, 6, 5, 6), (2, 4, 9, 11), (6, 2, 3, 3), (6,)]),
 ]
 DEVICE_BIN = os.path.join(ROOT, "torchlite-cpp_b200", "lib", "tl_device_callers")
 

@@ -1,0 +1,451 @@
+// conv2d (src/ops.cpp:1443-1548 of torchlite-cpp) and Conv2dBackward
+// (src/autograd.cpp:386-517) on the GPU: im2col into one column buffer for
+// all images and groups, then ONE batched GEMM per product instead of the
+// reference's per-image, per-group matmul calls.
+//
+// The reference per image n and group g:
+//   col_ng [patch, HW] = im2col (patch p = c*kH*kW + kh*kW + kw, c local to g)
+//   out[n, g] = W_g [C_out_g, patch] . col_ng                (matmul)
+//   out += bias (broadcast add over N, H_out, W_out)
+// backward, grad_w / grad_input / grad_bias from zeros:
+//   grad_w[g] += dO_ng . col_ng^T            for n = 0, 1, ... (in order)
+//   grad_col  = W_g^T . dO_ng;  grad_input[pixel] += grad_col[...] in the
+//               loop order c, kh, kw, oh, ow (col2im)
+//   grad_bias[c] += dO[n, c, oh, ow] for n, oh, ow in order
+// Here:
+//   forward   im2col_kernel -> col [N, groups, patch, HW]; one GEMM with batch
+//             dims (N, groups), W_g broadcast over n (stride 0); bias: one add
+//             kernel.  Every output is the same ascending-patch chain.
+//   grad_w    one GEMM G[n, g] = dO_ng . col_ng^T (col read transposed in
+//             place), then a sequential sum over n (the reference's +=).
+//   grad_in   one GEMM grad_col[n, g] = W_g^T . dO_ng (W read transposed in
+//             place), then col2im as a gather: each input pixel adds its
+//             contributions in (kh, kw) order, the order in which the
+//             reference's loop reaches that pixel; no atomics.
+//   grad_bias one chain per channel over (n, oh, ow), the reference's order.
+// In exact mode all of it is bit-identical to the reference.
+#include "common.cuh"
+
+#include <algorithm>
+#include <string>
+
+namespace tlc {
+namespace {
+
+struct ConvShape {
+    int64_t N, C_in, H, W, C_out, kH, kW, stride, padding, groups;
+    int64_t C_in_g, C_out_g, H_out, W_out, patch, HW;
+};
+
+// col[n, g, p, hw] = input[n, g*C_in_g + c, ih, iw] or 0 outside the image.
+// One block row per (n, g, p) line of HW outputs: the patch decode happens
+// once per block, threads walk hw with 32-bit index math (writes coalesced;
+// reads along iw for consecutive ow).
+__global__ void im2col_kernel(const float* __restrict__ in, float* __restrict__ col, ConvShape s) {
+    const int64_t lines = s.N * s.groups * s.patch;
+    const int HW = (int)s.HW, W_out = (int)s.W_out, H = (int)s.H, W = (int)s.W;
+    const int stride = (int)s.stride, pad = (int)s.padding;
+    const int khw = (int)(s.kH * s.kW), kW = (int)s.kW;
+    for (int64_t line = blockIdx.x; line < lines; line += gridDim.x) {
+        const int p = (int)(line % s.patch);
+        const int64_t ng = line / s.patch;
+        const int g = (int)(ng % s.groups);
+        const int64_t n = ng / s.groups;
+        const int c = g * (int)s.C_in_g + p / khw;
+        const int kh = (p % khw) / kW, kw = p % kW;
+        const float* src = in + (n * s.C_in + c) * (int64_t)H * W;
+        float* dst = col + line * s.HW;
+        for (int hw = threadIdx.x; hw < HW; hw += blockDim.x) {
+            const int oh = hw / W_out, ow = hw - oh * W_out;
+            const int ih = oh * stride - pad + kh, iw = ow * stride - pad + kw;
+            dst[hw] = (ih >= 0 && ih < H && iw >= 0 && iw < W) ? src[ih * W + iw] : 0.0f;
+        }
+    }
+}
+
+// grad_in[n, c, ih, iw] = 0 + sum over (kh, kw) ascending of grad_col at the
+// (oh, ow) that read this pixel.  One block per (n, c) plane.
+__global__ void col2im_kernel(const float* __restrict__ gcol, float* __restrict__ gin, ConvShape s) {
+    const int64_t planes = s.N * s.C_in;
+    const int H = (int)s.H, W = (int)s.W, HW = (int)s.HW, H_out = (int)s.H_out, W_out = (int)s.W_out;
+    const int stride = (int)s.stride, pad = (int)s.padding, kH = (int)s.kH, kW = (int)s.kW;
+    for (int64_t plane = blockIdx.x; plane < planes; plane += gridDim.x) {
+        const int c = (int)(plane % s.C_in);
+        const int64_t n = plane / s.C_in;
+        const int g = c / (int)s.C_in_g, cl = c % (int)s.C_in_g;
+        const float* base = gcol + ((n * s.groups + g) * s.patch + (int64_t)cl * kH * kW) * s.HW;
+        float* dst = gin + plane * (int64_t)H * W;
+        for (int pix = threadIdx.x; pix < H * W; pix += blockDim.x) {
+            const int ih = pix / W, iw = pix - ih * W;
+            float acc = 0.0f;
+            for (int kh = 0; kh < kH; ++kh) {
+                const int th = ih + pad - kh;
+                if (th < 0 || th % stride) continue;
+                const int oh = th / stride;
+                if (oh >= H_out) continue;
+                for (int kw = 0; kw < kW; ++kw) {
+                    const int tw = iw + pad - kw;
+                    if (tw < 0 || tw % stride) continue;
+                    const int ow = tw / stride;
+                    if (ow >= W_out) continue;
+                    acc = __fadd_rn(acc, base[(int64_t)(kh * kW + kw) * HW + oh * W_out + ow]);
+                }
+            }
+            dst[pix] = acc;
+        }
+    }
+}
+
+// grad_bias[c] = 0 + dO[n, c, hw] for n, then hw, ascending: a chain of
+// N * HW dependent adds per channel.  One block per channel: warp 1 stages
+// the chain's values, BIAS_TILE at a time, into a double-buffered shared
+// ring (coalesced reads of each image's HW run); lane 0 of warp 0 adds
+// them in order.
+constexpr int BIAS_TILE = 1024;
+__global__ void __launch_bounds__(64) bias_grad_kernel(const float* __restrict__ go, float* __restrict__ gb,
+                                                       ConvShape s) {
+    __shared__ float tile[2][BIAS_TILE];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t total = s.N * s.HW;
+    const int64_t tiles = (total + BIAS_TILE - 1) / BIAS_TILE;
+    for (int64_t c = blockIdx.x; c < s.C_out; c += gridDim.x) {
+        // value j of the chain: dO[j / HW, c, j % HW]
+        auto stage = [&](int64_t t, int buf) {
+            const int64_t j0 = t * BIAS_TILE;
+            for (int k = lane; k < BIAS_TILE; k += 32) {
+                const int64_t j = j0 + k;
+                float v = 0.0f;
+                if (j < total) {
+                    const int64_t n = j / s.HW, hw = j - n * s.HW;
+                    v = go[(n * s.C_out + c) * s.HW + hw];
+                }
+                tile[buf][k] = v;
+            }
+        };
+        if (warp == 1 && tiles > 0) stage(0, 0);
+        __syncthreads();
+        float acc = 0.0f;
+        for (int64_t t = 0; t < tiles; ++t) {
+            const int buf = (int)(t & 1);
+            if (warp == 1) {
+                if (t + 1 < tiles) stage(t + 1, buf ^ 1);
+            } else if (lane == 0) {
+                const int cnt = (int)min((int64_t)BIAS_TILE, total - t * BIAS_TILE);
+                for (int k = 0; k < cnt; ++k) acc = __fadd_rn(acc, tile[buf][k]);
+            }
+            __syncthreads();
+        }
+        if (warp == 0 && lane == 0) gb[c] = acc;
+        __syncthreads();
+    }
+}
+
+int resolve(int mode, int& out) {
+    if (mode == TLC_MODE_DEFAULT) mode = tlc_default_mode();
+    if (mode != TLC_MODE_EXACT && mode != TLC_MODE_TF32 && mode != TLC_MODE_3XTF32)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "unknown GEMM mode " + std::to_string(mode));
+    out = mode;
+    return TLC_OK;
+}
+
+int gemm(const Gemm& g, int mode, cudaStream_t s) {
+    if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
+    if (mode == TLC_MODE_EXACT || g.K == 0) return gemm_exact(g, s);
+    return gemm_tc(g, mode, s);
+}
+
+bool dense(const tlc_tensor* t) {
+    int64_t e = 1, n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= t->sizes[i];
+    if (n == 0) return true;
+    for (int i = t->ndim - 1; i >= 0; --i) {
+        if (t->sizes[i] != 1 && t->strides[i] != e) return false;
+        e *= t->sizes[i];
+    }
+    return true;
+}
+
+// Shape checks of src/ops.cpp:1444-1465, with the reference's messages.
+int conv_shape(const tlc_tensor* in, const tlc_tensor* w, int64_t stride, int64_t padding, int64_t groups,
+               ConvShape& s) {
+    if (!in || !w) return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: input or weight is NULL");
+    if (in->ndim != 4 || w->ndim != 4)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: input and weight must be 4-D");
+    s.N = in->sizes[0];
+    s.C_in = in->sizes[1];
+    s.H = in->sizes[2];
+    s.W = in->sizes[3];
+    s.C_out = w->sizes[0];
+    s.kH = w->sizes[2];
+    s.kW = w->sizes[3];
+    s.stride = stride;
+    s.padding = padding;
+    s.groups = groups;
+    if (groups <= 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: groups must be > 0");
+    if (s.C_in % groups != 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: groups doesn't divide C_in");
+    if (s.C_out % groups != 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: groups doesn't divide C_out");
+    if (w->sizes[1] != s.C_in / groups)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: weight.sizes()[1] must equal C_in / groups");
+    if (stride <= 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: stride must be > 0");
+    if (padding < 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d: padding must be >= 0");
+    s.C_in_g = s.C_in / groups;
+    s.C_out_g = s.C_out / groups;
+    // (H + 2p - kH) / stride + 1 with C++'s truncating division, as the
+    // reference computes it.  A negative result fails there in one of two
+    // places: the [N, C_out, H_out * W_out] buffer (a negative product) or
+    // the final reshape to [N, C_out, H_out, W_out] (both negative).
+    s.H_out = (s.H + 2 * padding - s.kH) / stride + 1;
+    s.W_out = (s.W + 2 * padding - s.kW) / stride + 1;
+    if (s.H_out < 0 || s.W_out < 0)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, s.H_out * s.W_out < 0
+                                                       ? "Tensor size must be positive integer"
+                                                       : "reshape: negative dims not allowed");
+    s.patch = s.C_in_g * s.kH * s.kW;
+    s.HW = s.H_out * s.W_out;
+    // the kernels index within one image plane / column line in 32 bits
+    if (s.H * s.W > INT32_MAX || s.HW > INT32_MAX || s.patch > INT32_MAX || s.kH * s.kW > INT32_MAX)
+        return set_error(TLC_ERR_UNSUPPORTED, "conv2d: an image plane above 2^31 elements");
+    return TLC_OK;
+}
+
+struct Buf {
+    void* p = nullptr;
+    cudaStream_t s;
+    explicit Buf(cudaStream_t st) : s(st) {}
+    ~Buf() { scratch_free(p, s); }
+    float* f() const { return static_cast<float*>(p); }
+};
+
+// input (and weight) as dense NCHW: the tensor itself or a contiguous copy
+int dense_copy(const tlc_tensor* t, Buf& b, const float** out, cudaStream_t s) {
+    if (dense(t)) {
+        *out = t->data;
+        return TLC_OK;
+    }
+    int64_t n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= t->sizes[i];
+    TLC_TRY(scratch_alloc(&b.p, sizeof(float) * (size_t)n, s));
+    TLC_TRY(launch_strided_copy(t->data, t->ndim, t->sizes, t->strides, b.f(), s));
+    *out = b.f();
+    return TLC_OK;
+}
+
+int check_dense_out(const tlc_tensor* t, const int64_t* sizes, int nd, const char* name) {
+    if (!t) return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + " is NULL");
+    if (t->ndim != nd) return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + ": wrong rank");
+    int64_t n = 1;
+    for (int i = 0; i < nd; ++i) {
+        if (t->sizes[i] != sizes[i]) return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + ": wrong shape");
+        n *= sizes[i];
+    }
+    if (!dense(t)) return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + " must be contiguous");
+    if (n > 0 && !t->data) return set_error(TLC_ERR_INVALID_ARGUMENT, std::string(name) + ": NULL data");
+    return TLC_OK;
+}
+
+// col [N, groups, patch, HW] of a dense input
+int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
+    const int64_t n = s.N * s.groups * s.patch * s.HW;
+    TLC_TRY(scratch_alloc(&col.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
+    if (n) {
+        const int64_t lines = s.N * s.groups * s.patch;
+        im2col_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
+        count_launch();
+        TLC_TRY(check_launch("im2col"));
+    }
+    return TLC_OK;
+}
+
+int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bias, int64_t stride,
+            int64_t padding, int64_t groups, tlc_tensor* out, int mode, cudaStream_t st) {
+    ConvShape s;
+    TLC_TRY(conv_shape(in_t, w_t, stride, padding, groups, s));
+    const int64_t osz[4] = {s.N, s.C_out, s.H_out, s.W_out};
+    TLC_TRY(check_dense_out(out, osz, 4, "out"));
+    const tlc_tensor* b = (bias && bias->ndim > 0) ? bias : nullptr;
+    if (b) {
+        int64_t nb = 1;
+        for (int i = 0; i < b->ndim; ++i) nb *= b->sizes[i];
+        if (nb != s.C_out)  // reshape(bias, {1, C_out, 1, 1}), src/ops.cpp:1524
+            return set_error(TLC_ERR_INVALID_ARGUMENT, "reshape: new shape must have same number of elements");
+    }
+    if (s.N * s.C_out * s.HW == 0) return TLC_OK;
+    Buf bin(st), bw(st), col(st), bb(st);
+    const float *in, *w;
+    TLC_TRY(dense_copy(in_t, bin, &in, st));
+    TLC_TRY(dense_copy(w_t, bw, &w, st));
+    TLC_TRY(make_col(in, s, col, st));
+    // out[n, g] (C_out_g x HW) = W_g (C_out_g x patch) . col[n, g] (patch x HW)
+    Gemm g{};
+    g.M = s.C_out_g;
+    g.N = s.HW;
+    g.K = s.patch;
+    g.A = w;
+    g.a_rs = s.patch;
+    g.a_cs = 1;
+    g.B = col.f();
+    g.b_rs = s.HW;
+    g.b_cs = 1;
+    g.C = out->data;
+    g.c_rs = s.HW;
+    g.nb = 2;
+    g.bsz[0] = s.N;
+    g.bsz[1] = s.groups;
+    g.abs_[0] = 0;
+    g.abs_[1] = s.C_out_g * s.patch;
+    g.bbs[0] = s.groups * s.patch * s.HW;
+    g.bbs[1] = s.patch * s.HW;
+    g.cbs[0] = s.C_out * s.HW;
+    g.cbs[1] = s.C_out_g * s.HW;
+    TLC_TRY(gemm(g, mode, st));
+    if (b) {
+        // add(result, reshape(bias, {1, C_out, 1, 1})): in place, out = out + bias[c]
+        const float* bd;
+        TLC_TRY(dense_copy(b, bb, &bd, st));
+        const int64_t sz[3] = {s.N, s.C_out, s.HW};
+        const int64_t sa[3] = {s.C_out * s.HW, s.HW, 1}, sbias[3] = {0, 1, 0};
+        TLC_TRY(launch_elementwise(out->data, bd, 0.0f, out->data, s.N * s.C_out * s.HW, 3, sz, sa, sbias,
+                                   0, st));
+    }
+    return TLC_OK;
+}
+
+int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w_t, int64_t stride,
+             int64_t padding, int64_t groups, tlc_tensor* d_in, tlc_tensor* d_w, tlc_tensor* d_b, int mode,
+             cudaStream_t st) {
+    ConvShape s;
+    TLC_TRY(conv_shape(in_t, w_t, stride, padding, groups, s));
+    const int64_t osz[4] = {s.N, s.C_out, s.H_out, s.W_out};
+    if (!go_t || go_t->ndim != 4)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d_backward: grad_output must be 4-D");
+    for (int i = 0; i < 4; ++i)
+        if (go_t->sizes[i] != osz[i])
+            return set_error(TLC_ERR_INVALID_ARGUMENT, "conv2d_backward: grad_output has the wrong shape");
+    if (d_in) TLC_TRY(check_dense_out(d_in, in_t->sizes, 4, "d_input"));
+    if (d_w) TLC_TRY(check_dense_out(d_w, w_t->sizes, 4, "d_weight"));
+    const int64_t bsz[1] = {s.C_out};
+    if (d_b) TLC_TRY(check_dense_out(d_b, bsz, 1, "d_bias"));
+    Buf bgo(st), bin(st), bw(st), col(st), prod(st), gcol(st);
+    const float *go, *in, *w;
+    TLC_TRY(dense_copy(go_t, bgo, &go, st));
+    TLC_TRY(dense_copy(in_t, bin, &in, st));
+    TLC_TRY(dense_copy(w_t, bw, &w, st));
+    if (d_w) {
+        // G[n, g] (C_out_g x patch) = dO[n, g] (C_out_g x HW) . col[n, g]^T, then sum over n
+        if (s.N * s.C_out * s.patch == 0) {
+            if (s.C_out * s.patch) TLC_TRY(launch_fill_zero(d_w->data, s.C_out * s.patch, st));
+        } else {
+            TLC_TRY(make_col(in, s, col, st));
+            TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(s.N * s.C_out * s.patch), st));
+            Gemm g{};
+            g.M = s.C_out_g;
+            g.N = s.patch;
+            g.K = s.HW;
+            g.A = go;
+            g.a_rs = s.HW;
+            g.a_cs = 1;
+            g.B = col.f();  // col[n, g] read as its transpose: (hw, p) at p*HW + hw
+            g.b_rs = 1;
+            g.b_cs = s.HW;
+            g.C = prod.f();
+            g.c_rs = s.patch;
+            g.nb = 2;
+            g.bsz[0] = s.N;
+            g.bsz[1] = s.groups;
+            g.abs_[0] = s.C_out * s.HW;
+            g.abs_[1] = s.C_out_g * s.HW;
+            g.bbs[0] = s.groups * s.patch * s.HW;
+            g.bbs[1] = s.patch * s.HW;
+            g.cbs[0] = s.C_out * s.patch;
+            g.cbs[1] = s.C_out_g * s.patch;
+            if (s.HW == 0) {
+                TLC_TRY(launch_fill_zero(prod.f(), s.N * s.C_out * s.patch, st));
+            } else {
+                TLC_TRY(gemm(g, mode, st));
+            }
+            // grad_w = 0 + G[0] + G[1] + ... (the reference's += over images)
+            TLC_TRY(launch_sum_dim(prod.f(), d_w->data, 1, s.N, s.C_out * s.patch, st));
+        }
+    }
+    if (d_in) {
+        const int64_t ni = s.N * s.C_in * s.H * s.W;
+        if (ni) {
+            const int64_t nc = s.N * s.groups * s.patch * s.HW;
+            TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)std::max<int64_t>(nc, 1), st));
+            if (nc) {
+                // grad_col[n, g] (patch x HW) = W_g^T (patch x C_out_g) . dO[n, g] (C_out_g x HW)
+                Gemm g{};
+                g.M = s.patch;
+                g.N = s.HW;
+                g.K = s.C_out_g;
+                g.A = w;  // W_g read as its transpose: (p, o) at o*patch + p
+                g.a_rs = 1;
+                g.a_cs = s.patch;
+                g.B = go;
+                g.b_rs = s.HW;
+                g.b_cs = 1;
+                g.C = gcol.f();
+                g.c_rs = s.HW;
+                g.nb = 2;
+                g.bsz[0] = s.N;
+                g.bsz[1] = s.groups;
+                g.abs_[0] = 0;
+                g.abs_[1] = s.C_out_g * s.patch;
+                g.bbs[0] = s.C_out * s.HW;
+                g.bbs[1] = s.C_out_g * s.HW;
+                g.cbs[0] = s.groups * s.patch * s.HW;
+                g.cbs[1] = s.patch * s.HW;
+                TLC_TRY(gemm(g, mode, st));
+            }
+            col2im_kernel<<<(unsigned)std::min<int64_t>(s.N * s.C_in, 148 * 64), 256, 0, st>>>(
+                gcol.f(), d_in->data, s);
+            count_launch();
+            TLC_TRY(check_launch("col2im"));
+        }
+    }
+    if (d_b && s.C_out) {
+        bias_grad_kernel<<<(unsigned)std::min<int64_t>(s.C_out, 148 * 16), 64, 0, st>>>(go, d_b->data, s);
+        count_launch();
+        TLC_TRY(check_launch("conv bias grad"));
+    }
+    return TLC_OK;
+}
+
+}  // namespace
+}  // namespace tlc
+
+using namespace tlc;
+
+extern "C" int tlc_conv2d_shape(const tlc_tensor* input, const tlc_tensor* weight, int64_t stride,
+                                int64_t padding, int64_t groups, int64_t* out_sizes) {
+    clear_error();
+    ConvShape s;
+    TLC_TRY(conv_shape(input, weight, stride, padding, groups, s));
+    if (out_sizes) {
+        out_sizes[0] = s.N;
+        out_sizes[1] = s.C_out;
+        out_sizes[2] = s.H_out;
+        out_sizes[3] = s.W_out;
+    }
+    return TLC_OK;
+}
+
+extern "C" int tlc_conv2d(const tlc_tensor* input, const tlc_tensor* weight, const tlc_tensor* bias,
+                          int64_t stride, int64_t padding, int64_t groups, tlc_tensor* out, int mode,
+                          void* stream) {
+    clear_error();
+    int m;
+    TLC_TRY(resolve(mode, m));
+    return forward(input, weight, bias, stride, padding, groups, out, m, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tlc_conv2d_backward(const tlc_tensor* grad_output, const tlc_tensor* input,
+                                   const tlc_tensor* weight, int64_t stride, int64_t padding,
+                                   int64_t groups, tlc_tensor* d_input, tlc_tensor* d_weight,
+                                   tlc_tensor* d_bias, int mode, void* stream) {
+    clear_error();
+    int m;
+    TLC_TRY(resolve(mode, m));
+    return backward(grad_output, input, weight, stride, padding, groups, d_input, d_weight, d_bias, m,
+                    static_cast<cudaStream_t>(stream));
+}

@@ -73,6 +73,15 @@ class SoftmaxBackward : public GradFunction {
     void backward(const Tensor& grad_output) override;
 };
 
+// src/autograd.cpp:386-517 (inputs: input, weight, bias)
+class Conv2dBackward : public GradFunction {
+  public:
+    Tensor input_cache, weight_cache;
+    int64_t stride = 1, padding = 0, groups = 1;
+    int mode = -1;
+    void backward(const Tensor& grad_output) override;
+};
+
 // matmul_add / matmul_scale: the reference's AddBackward or ScaleBackward
 // followed by MatmulBackward, in one node
 class FusedMatmulBackward : public GradFunction {

@@ -40,6 +40,12 @@ Tensor sum_to(const Tensor& grad, const std::vector<int64_t>& target_shape);
 // The bias add / scale run in the GEMM's epilogue; b is 1-D of length N.
 Tensor matmul_add(const Tensor& a, const Tensor& b, const Tensor& bias);
 Tensor matmul_scale(const Tensor& a, const Tensor& b, float scalar);
+
+// 2-D convolution of NCHW tensors (src/ops.cpp:1443-1548): im2col + one
+// batched GEMM on the GPU; bias empty or [C_out].  Throws the reference's
+// std::invalid_argument messages.
+Tensor conv2d(const Tensor& input, const Tensor& weight, const Tensor& bias, int64_t stride = 1,
+              int64_t padding = 0, int64_t groups = 1);
 // sum along a dimension (src/ops.cpp:1181-1233); no autograd node
 Tensor sum(const Tensor& input, int64_t dim, bool keepdim = false);
 

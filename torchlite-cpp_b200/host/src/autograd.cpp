@@ -102,6 +102,35 @@ void SoftmaxBackward::backward(const Tensor& grad_output) {
     accumulate_grad(inputs[0], dx);
 }
 
+// src/autograd.cpp:386-517: all three gradients from libtl_cuda in the
+// reference's summation orders, then accumulate_grad.
+void Conv2dBackward::backward(const Tensor& grad_output) {
+    const bool want_i = inputs[0].requires_grad, want_w = inputs[1].requires_grad;
+    const bool want_b = inputs.size() > 2 && inputs[2].requires_grad && !inputs[2].empty();
+    if (!want_i && !want_w && !want_b) return;
+    Tensor di, dw, db;
+    tlc_tensor vdi{}, vdw{}, vdb{};
+    if (want_i) {
+        di = Tensor::device_empty(input_cache.sizes());
+        vdi = dview(di);
+    }
+    if (want_w) {
+        dw = Tensor::device_empty(weight_cache.sizes());
+        vdw = dview(dw);
+    }
+    if (want_b) {
+        db = Tensor::device_empty({weight_cache.sizes()[0]});
+        vdb = dview(db);
+    }
+    tlc_tensor g = dview(grad_output), x = dview(input_cache), w = dview(weight_cache);
+    check(tlc_conv2d_backward(&g, &x, &w, stride, padding, groups, want_i ? &vdi : nullptr,
+                              want_w ? &vdw : nullptr, want_b ? &vdb : nullptr, mode, nullptr),
+          "tlc_conv2d_backward");
+    if (want_i) accumulate_grad(inputs[0], di);
+    if (want_w) accumulate_grad(inputs[1], dw);
+    if (want_b) accumulate_grad(inputs[2], db);
+}
+
 // ScaleBackward (scale(grad, s)) or AddBackward (grad to the product unchanged,
 // sum_to(grad, [N]) to the bias), then MatmulBackward, as the reference's
 // separate nodes would run them.

@@ -247,6 +247,36 @@ Tensor matmul_scale(const Tensor& a, const Tensor& b, float scalar) {
     return matmul_fused(a, b, nullptr, scalar, true, TLC_MODE_DEFAULT);
 }
 
+// src/ops.cpp:1443-1548
+Tensor conv2d(const Tensor& input, const Tensor& weight, const Tensor& bias, int64_t stride,
+              int64_t padding, int64_t groups) {
+    tlc_tensor vi = view_of(input, false), vw = view_of(weight, false);
+    int64_t sz[4];
+    check(tlc_conv2d_shape(&vi, &vw, stride, padding, groups, sz), "tlc_conv2d_shape");
+    Tensor out = Tensor::device_empty(std::vector<int64_t>(sz, sz + 4));
+    if (out.numel() > 0) {
+        vi = view_of(input, true);
+        vw = view_of(weight, true);
+        tlc_tensor vb{}, vo = view_of(out, false);
+        vo.data = out.device_data();
+        if (!bias.empty()) vb = view_of(bias, true);
+        check(tlc_conv2d(&vi, &vw, bias.empty() ? nullptr : &vb, stride, padding, groups, &vo,
+                         TLC_MODE_DEFAULT, nullptr),
+              "tlc_conv2d");
+    }
+    if (input.requires_grad || weight.requires_grad) {
+        if (auto fn = track<Conv2dBackward>(out, {&input, &weight, &bias})) {
+            fn->input_cache = input;
+            fn->weight_cache = weight;
+            fn->stride = stride;
+            fn->padding = padding;
+            fn->groups = groups;
+            fn->mode = TLC_MODE_DEFAULT;
+        }
+    }
+    return out;
+}
+
 Tensor sum(const Tensor& input, int64_t dim, bool keepdim) {
     Tensor a = input.contiguous();
     const auto& sizes = a.sizes();

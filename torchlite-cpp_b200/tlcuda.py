@@ -90,6 +90,9 @@ SIGNATURES = {
     "tlc_softmax": ([_T, _T, _v], _i),
     "tlc_softmax_backward": ([_T, _T, _T, _v], _i),
     "tlc_sum_to": ([_T, _T, _v], _i),
+    "tlc_conv2d_shape": ([_T, _T, _i64, _i64, _i64, _P(_i64)], _i),
+    "tlc_conv2d": ([_T, _T, _T, _i64, _i64, _i64, _T, _i, _v], _i),
+    "tlc_conv2d_backward": ([_T, _T, _T, _i64, _i64, _i64, _T, _T, _T, _i, _v], _i),
     "tlc_load_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
     "tlc_save_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
     "tlc_shard_range": ([_i64, _i, _i, _P(_i64), _P(_i64)], _i),
@@ -339,6 +342,38 @@ def sum_to(x, target, out=None, stream=None):
     vx, vo = view_of(x), view_of(out)
     _check(lib().tlc_sum_to(ctypes.byref(vx), ctypes.byref(vo), _stream_ptr(stream)))
     return out
+
+
+def conv2d(x, w, bias=None, stride=1, padding=0, groups=1, mode="exact", out=None, stream=None):
+    """tl::conv2d on CUDA NCHW tensors."""
+    import torch
+    vx, vw = view_of(x), view_of(w)
+    sz = (ctypes.c_int64 * 4)()
+    _check(lib().tlc_conv2d_shape(ctypes.byref(vx), ctypes.byref(vw), stride, padding, groups, sz))
+    if out is None:
+        out = torch.empty(tuple(sz), dtype=torch.float32, device=x.device)
+    vb = view_of(bias) if bias is not None else None
+    vo = view_of(out)
+    _check(lib().tlc_conv2d(ctypes.byref(vx), ctypes.byref(vw), ctypes.byref(vb) if vb else None,
+                            stride, padding, groups, ctypes.byref(vo), mode_id(mode),
+                            _stream_ptr(stream)))
+    return out
+
+
+def conv2d_backward(grad, x, w, stride=1, padding=0, groups=1, mode="exact", need=(True, True, True),
+                    stream=None):
+    """Conv2dBackward: (d_input, d_weight, d_bias), None where not requested."""
+    import torch
+    outs = [torch.empty(tuple(x.shape), device=x.device) if need[0] else None,
+            torch.empty(tuple(w.shape), device=x.device) if need[1] else None,
+            torch.empty((w.shape[0],), device=x.device) if need[2] else None]
+    views = [view_of(o) if o is not None else None for o in outs]
+    vg, vx, vw = view_of(grad), view_of(x), view_of(w)
+    _check(lib().tlc_conv2d_backward(ctypes.byref(vg), ctypes.byref(vx), ctypes.byref(vw), stride,
+                                     padding, groups,
+                                     *[ctypes.byref(v) if v else None for v in views],
+                                     mode_id(mode), _stream_ptr(stream)))
+    return tuple(outs)
 
 
 def _views(tensors):
