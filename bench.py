@@ -52,7 +52,7 @@ GEMMS = {
     "square16384": (1, 16384, 16384, 16384),
     "square512": (1, 512, 512, 512),
 }
-OTHER = ("linear", "attention", "broadcast")
+OTHER = ("linear", "attention", "broadcast", "flash")
 METRIC = "GEMM TFLOP/s (fp32-exact, TF32, 3xTF32) at 1/2/4/8 B200, % of peak"
 
 
@@ -379,11 +379,56 @@ class BroadcastWork(Work):
         tlcuda.matmul_backward(self.dC, self.A, self.B, mode=mode, da=self.dA, db=self.dB)
 
 
+class FlashWork(Work):
+    """flash_attention forward + FlashAttentionBackward on batch 16 x 12 heads,
+    S = 2048, d = 64 ([16,12,2048,64] Q, K, V, dO ~ N(0,1), seed 5), scale 1/8:
+    the fused FFMA forward kernel, then the backward's five batched GEMMs (in
+    the mode) and its elementwise kernels.  FLOPs: forward 4*S*S*d per head
+    (Q.K^T and P.V), backward 10*S*S*d (Q.K^T recomputed, dV, dP, dQ, dK)."""
+    name = "flash"
+
+    def __init__(self, world, rank, device):
+        import torch
+        g = torch.Generator(device=device).manual_seed(5)
+        shape = (16, 12, 2048, 64)
+        self.q, self.k, self.v, self.dO = (torch.randn(shape, generator=g, device=device)
+                                           for _ in range(4))
+        self.o = torch.empty(shape, device=device)
+        self.lse = torch.empty(shape[:-1], device=device)
+        self.dq, self.dk, self.dv = (torch.empty(shape, device=device) for _ in range(3))
+        heads, S, d = 192, 2048, 64
+        self.fwd_flops = 4.0 * heads * S * S * d
+        self.flops = self.fwd_flops + 10.0 * heads * S * S * d
+        self.job_flops = self.flops * world
+        self.config = {"workload": "flash", "batch": 16, "heads": 12, "S": 2048, "d": 64,
+                       "sm_scale": 0.125, "forward": "fused FFMA kernel (fp32 exact arithmetic)",
+                       "backward": "5 batched GEMMs in the mode + elementwise kernels",
+                       "parallelism": "replicas"}
+
+    def forward(self):
+        import tlcuda
+        tlcuda.flash_attention(self.q, self.k, self.v, 0.125, out=self.o, lse=self.lse)
+
+    def step(self, mode):
+        import tlcuda
+        self.forward()
+        tlcuda.flash_attention_backward(self.dO, self.q, self.k, self.v, self.o, self.lse, 0.125,
+                                        mode=mode, dq=self.dq, dk=self.dk, dv=self.dv)
+
+    def forward_roofline(self, world, stream, peak, steps=10):
+        """The forward kernel alone against the FP32 FFMA peak (peak_for("exact"))."""
+        ms, _ = time_device(self.forward, steps, 3, world, stream)
+        ach = self.fwd_flops / (ms * 1e-3) / 1e12
+        return {"kernel": "flash_fwd_kernel<64>", "ms": ms, "achieved": ach, "peak": peak[0],
+                "unit": "TFLOP/s", "frac": ach / peak[0], "bound": "fp32-fma",
+                "peak_source": peak[1], "algorithmic_flop_per_launch": self.fwd_flops}
+
+
 def make_work(name, world, rank, device):
     if name in GEMMS:
         return GemmWork(name, world, rank, device)
-    return {"linear": LinearWork, "attention": AttentionWork,
-            "broadcast": BroadcastWork}[name](world, rank, device)
+    return {"linear": LinearWork, "attention": AttentionWork, "broadcast": BroadcastWork,
+            "flash": FlashWork}[name](world, rank, device)
 
 
 # ---- the reference's CPU path ----------------------------------------------------------
@@ -411,22 +456,40 @@ def ref_sample(name):
     return a, b, 2.0 * rows * N * K, f"tl::matmul [{rows},{K}]x[{K},{N}] fp32, {what} of the workload"
 
 
+def ref_job(name, R):
+    """(callable, useful FLOPs, description) of one bounded sample on the
+    reference library R: tl::matmul for the GEMM workloads; for "flash" one
+    head of the workload (S = 2048, d = 64) through tl::flash_attention and
+    FlashAttentionBackward (bench/bench_attention.cpp's single-head call)."""
+    if name == "flash":
+        import numpy as np
+        rng = np.random.default_rng(5)
+        q, k, v, g = (rng.standard_normal((2048, 64)).astype(np.float32) for _ in range(4))
+        flops = 14.0 * 2048 * 2048 * 64
+        return (lambda: R.flash_attention(q, k, v, 0.125, grad=g), flops,
+                f"tl::flash_attention + backward on one head [2048,64] of the workload "
+                f"({flops / 1e9:.2f} GFLOP)")
+    a, b, flops, what = ref_sample(name)
+    return lambda: R.matmul(a, b), flops, f"{what} ({flops / 1e9:.2f} GFLOP)"
+
+
 def cpu_reference_sample(name, reps=3):
-    """The reference's own tl::matmul (oracle/_ref, compiled from its sources),
+    """The reference's own CPU path (oracle/_ref, compiled from its sources),
     min over reps (time_best, bench/bench_matmul.cpp:27-39)."""
     sys.path.insert(0, REPO)
     from oracle import oracle as O
     R = O.tlref()
-    a, b, flops, what = ref_sample(name)
+    fn, flops, what = ref_job(name, R)
     best = float("inf")
     for _ in range(reps):
         t0 = time.perf_counter()
-        R.matmul(a, b)
+        fn()
         best = min(best, time.perf_counter() - t0)
-    return {"value": flops / best / 1e12, "unit": "TFLOP/s", "cores": R.hardware_threads(),
-            "kind": "reference",
-            "sample": f"{what} ({flops / 1e9:.2f} GFLOP), best of {reps}, "
-                      f"{os.path.basename(R.path)} with std::thread::hardware_concurrency() threads"}
+    cores = R.hardware_threads() if name != "flash" else 1
+    return {"value": flops / best / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+            "sample": f"{what}, best of {reps}, {os.path.basename(R.path)}"
+                      + (" (single-threaded code path)" if name == "flash"
+                         else " with std::thread::hardware_concurrency() threads")}
 
 
 def run_reference_arm(args):
@@ -441,24 +504,27 @@ def run_reference_arm(args):
     except FileNotFoundError as e:
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not built: {e}"}))
         return 0
-    a, b, flops, what = ref_sample(args.workload)
+    fn, flops, what = ref_job(args.workload, R)
     for _ in range(args.warmup):
-        R.matmul(a, b)
+        fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        R.matmul(a, b)
+        fn()
     dt = (time.perf_counter() - t0) / args.steps
     val = flops / dt / 1e12
-    sample = f"each step: {what} ({flops / 1e9:.2f} GFLOP), host wall clock"
+    sample = f"each step: {what}, host wall clock"
     cfg = {"workload": args.workload}
     if args.workload in GEMMS:
         batch, M, N, K = GEMMS[args.workload]
-        cfg.update({"batch": batch, "M": M, "N": N, "K": K, "sampled_rows": a.shape[0]})
+        cfg.update({"batch": batch, "M": M, "N": N, "K": K,
+                    "sampled_rows": M if batch > 1 else min(M, 256)})
     line = {"metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic U[-1,1] seed 4", "impl": "reference", "config": cfg,
-            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": R.hardware_threads(),
+            "data": "synthetic N(0,1) seed 5" if args.workload == "flash" else "synthetic U[-1,1] seed 4",
+            "impl": "reference", "config": cfg,
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s",
+                             "cores": 1 if args.workload == "flash" else R.hardware_threads(),
                              "kind": "reference", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -515,6 +581,10 @@ def run_ours(args):
                 "algorithmic_flop_per_launch": work.flops}
 
     gather = work.gather_ms(world, stream) if isinstance(work, GemmWork) else None
+    fwd = None
+    if isinstance(work, FlashWork):
+        fwd = work.forward_roofline(world, stream, peak_for("exact", peaks, psrc, sms,
+                                                            peaks.get("sm_max_mhz", 1965.0)))
 
     # End to end through the host-buffer C entry point (page-locked host memory).
     e2e = None
@@ -549,6 +619,8 @@ def run_ours(args):
         }
         if gather is not None:
             line["gather_ms"] = gather
+        if fwd is not None:
+            line["forward"] = fwd
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist

@@ -257,6 +257,28 @@ int tlc_conv2d_backward(const tlc_tensor* grad_output, const tlc_tensor* input,
                         tlc_tensor* d_input, tlc_tensor* d_weight, tlc_tensor* d_bias, int mode,
                         void* stream);
 
+/* ---- attention ---------------------------------------------------------------
+ * flash_attention (src/ops.cpp:1040-1137): out = softmax(q . k^T * sm_scale) . v
+ * for q, k, v, out contiguous [..., S, d] device tensors of one shape (every
+ * leading index a separate head; the reference takes one head [S, d]),
+ * d <= 128.  One fused fp32 kernel, 64 x 64 query / key tiles with the
+ * reference's online-softmax update, no S x S buffer.  `lse` ([..., S],
+ * contiguous, or NULL) receives L = m + log(l), the reference's L_cache.
+ * FlashAttentionBackward (src/autograd.cpp:575-669): d_q, d_k, d_v from
+ * grad_out, the forward's inputs, out and lse, through batched GEMMs in
+ * `mode` (S x S scratch per head, at most 1 GiB per buffer); outputs are
+ * overwritten.  Both agree with the reference to its own bar (1e-4 against
+ * the materialised softmax path): expf / logf and the order of the softmax
+ * sums differ from the C library's.  Errors: shapes that differ, non-contiguous
+ * operands, fewer than 2 dims (TLC_ERR_INVALID_ARGUMENT); d > 128
+ * (TLC_ERR_UNSUPPORTED). */
+int tlc_flash_attention(const tlc_tensor* q, const tlc_tensor* k, const tlc_tensor* v,
+                        float sm_scale, tlc_tensor* out, tlc_tensor* lse, void* stream);
+int tlc_flash_attention_backward(const tlc_tensor* grad_out, const tlc_tensor* q,
+                                 const tlc_tensor* k, const tlc_tensor* v, const tlc_tensor* out,
+                                 const tlc_tensor* lse, float sm_scale, tlc_tensor* d_q,
+                                 tlc_tensor* d_k, tlc_tensor* d_v, int mode, void* stream);
+
 /* ---- TLMD model files straight to / from device memory --------------------
  * load_model / save_model (src/model_io.cpp:7-94): "TLMD", int32 version 1,
  * int64 count, then per tensor int64 ndim, int64 shape[ndim], float data.

@@ -56,6 +56,12 @@ def lib():
         L.orc_softmax.restype = None
         L.orc_softmax_backward.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, _i64]
         L.orc_softmax_backward.restype = None
+        L.orc_flash_attention.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p,
+                                          _f32p, _i64]
+        L.orc_flash_attention.restype = None
+        L.orc_flash_attention_backward.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64,
+                                                   _i64, ctypes.c_float, _f32p, _f32p, _f32p, _i64]
+        L.orc_flash_attention_backward.restype = None
         _lib = L
     return _lib
 
@@ -329,6 +335,44 @@ def softmax_backward(grad: np.ndarray, y: np.ndarray, vec: int = SOFTMAX_BWD_VEC
     return out
 
 
+# The dots over the head dimension in flash_attention / FlashAttentionBackward
+# round like SoftmaxBackward's (same loop shape, same vectorisation).
+FLASH_VEC = SOFTMAX_BWD_VEC
+
+
+def _heads(x):
+    x = np.ascontiguousarray(x, np.float32)
+    S, d = x.shape[-2], x.shape[-1]
+    return x.reshape(-1, S, d), S, d
+
+
+def flash_attention(q, k, v, scale, vec: int = FLASH_VEC):
+    """flash_attention (src/ops.cpp:1040-1137) per head of [..., S, d]:
+    returns (O, L) with L = m + log(l), the reference's L_cache."""
+    shape = np.shape(q)
+    (qh, S, d), (kh, _, _), (vh, _, _) = _heads(q), _heads(k), _heads(v)
+    o = np.empty_like(qh)
+    lse = np.empty(qh.shape[:2], np.float32)
+    for h in range(qh.shape[0]):
+        lib().orc_flash_attention(_fp(qh[h]), _fp(kh[h]), _fp(vh[h]), S, d, float(scale),
+                                  _fp(o[h]), _fp(lse[h]), vec)
+    return o.reshape(shape), lse.reshape(shape[:-1])
+
+
+def flash_attention_backward(dout, q, k, v, o, lse, scale, vec: int = FLASH_VEC):
+    """FlashAttentionBackward (src/autograd.cpp:575-669) per head: (dQ, dK, dV)."""
+    shape = np.shape(q)
+    (gh, S, d) = _heads(dout)
+    qh, kh, vh, oh = (_heads(t)[0] for t in (q, k, v, o))
+    lh = np.ascontiguousarray(lse, np.float32).reshape(-1, S)
+    dq, dk, dv = (np.empty_like(qh) for _ in range(3))
+    for h in range(qh.shape[0]):
+        lib().orc_flash_attention_backward(_fp(gh[h]), _fp(qh[h]), _fp(kh[h]), _fp(vh[h]),
+                                           _fp(oh[h]), _fp(lh[h]), S, d, float(scale),
+                                           _fp(dq[h]), _fp(dk[h]), _fp(dv[h]), vec)
+    return dq.reshape(shape), dk.reshape(shape), dv.reshape(shape)
+
+
 def matmul_backward(grad: np.ndarray, a: np.ndarray, b: np.ndarray, nthreads: int | None = None):
     """MatmulBackward::backward, src/autograd.cpp:341-384, followed by
     accumulate_grad into empty grads (src/autograd.cpp:16-22: zeros + d).
@@ -416,6 +460,10 @@ class TLRef:
         L.tlref_conv2d.argtypes = [_f32p, i64p, _f32p, i64p, _f32p, _i64, _i64, _i64, _f32p, _f32p,
                                    _f32p, _f32p, _f32p, ctypes.c_char_p, ctypes.c_int]
         L.tlref_conv2d.restype = ctypes.c_int
+        L.tlref_flash_attention.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, ctypes.c_float, _f32p,
+                                            _f32p, _f32p, _f32p, _f32p, ctypes.c_char_p,
+                                            ctypes.c_int]
+        L.tlref_flash_attention.restype = ctypes.c_int
         self.L = L
 
     def hardware_threads(self) -> int:
@@ -544,6 +592,22 @@ class TLRef:
         if rc:
             raise ValueError(err.value.decode())
         return out if g is None else (out, dx, dw, db)
+
+    def flash_attention(self, q, k, v, scale, grad=None):
+        """O = tl::flash_attention(Q, K, V, scale) on [S, d]; with grad also
+        (Q.grad, K.grad, V.grad) after O.backward()."""
+        q, k, v = (np.ascontiguousarray(t, np.float32) for t in (q, k, v))
+        S, d = q.shape
+        out = np.empty_like(q)
+        dq, dk, dv = (np.empty_like(q) for _ in range(3))
+        g = None if grad is None else np.ascontiguousarray(grad, np.float32)
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_flash_attention(_fp(q), _fp(k), _fp(v), S, d, float(scale),
+                                          None if g is None else _fp(g), _fp(out), _fp(dq),
+                                          _fp(dk), _fp(dv), err, 256)
+        if rc:
+            raise RuntimeError(f"tlref_flash_attention rc={rc}: {err.value.decode()}")
+        return out if g is None else (out, dq, dk, dv)
 
     def softmax(self, x, grad=None):
         """y = tl::softmax(x); with grad, also x.grad after y.backward() (SoftmaxBackward

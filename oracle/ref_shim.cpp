@@ -206,4 +206,32 @@ int tlref_conv2d(const float* x, const int64_t* xs, const float* w, const int64_
     }
 }
 
+// O = tl::flash_attention(Q, K, V, scale) on [S, d]; with grad: O.grad() =
+// grad, O.backward() (FlashAttentionBackward, then accumulate_grad), then
+// Q.grad, K.grad, V.grad.
+int tlref_flash_attention(const float* q, const float* k, const float* v, int64_t S, int64_t d,
+                          float scale, const float* grad, float* out, float* dq, float* dk,
+                          float* dv, char* err, int errlen) {
+    try {
+        const int64_t sz[2] = {S, d};
+        tl::Tensor Q = make(q, 2, sz), K = make(k, 2, sz), V = make(v, 2, sz);
+        if (grad) {
+            Q.set_requires_grad(true);
+            K.set_requires_grad(true);
+            V.set_requires_grad(true);
+        }
+        tl::Tensor O = tl::flash_attention(Q, K, V, scale);
+        int rc = copy_out(O, out, S * d, nullptr, nullptr);
+        if (rc || !grad) return rc;
+        O.grad() = make(grad, 2, sz);
+        O.backward();
+        rc = copy_out(Q.grad(), dq, S * d, nullptr, nullptr);
+        if (!rc) rc = copy_out(K.grad(), dk, S * d, nullptr, nullptr);
+        if (!rc) rc = copy_out(V.grad(), dv, S * d, nullptr, nullptr);
+        return rc;
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
 }  // extern "C"

@@ -36,6 +36,18 @@
  *    dot = fmaf(g_j, y_j, dot).  vec = 8 for the x86-64-v4 (AVX-512) build,
  *    4 for x86-64-v3; both measured against the compiled reference.
  *
+ *  - flash_attention (src/ops.cpp:1040-1137) and FlashAttentionBackward
+ *    (src/autograd.cpp:575-669): 64 x 64 query / key tiles, each score
+ *    T = dot(q_i, k_j) * scale, the online softmax (m_new = max(m, max_j T),
+ *    corr = expf(m - m_new), p = expf(T - m_new), l = fmaf(l, corr, sum p),
+ *    O = O * corr then O = fmaf(p, v_j, O) per key), O = O * (1 / l),
+ *    L = m + logf(l); the backward recomputes P = expf(T - L_i) and
+ *    accumulates dV, dQ, dK per (i, j) pair in the reference's order:
+ *    orc_flash_attention / orc_flash_attention_backward.  Each dot over d
+ *    rounds the way the Release build's vectorisation does (the first
+ *    d - d mod vec products rounded and added in order, the tail fused), as
+ *    for SoftmaxBackward's dot.
+ *
  * Operands are strided 2-D views (row and column strides in elements), so the
  * transposed views that MatmulBackward builds (src/autograd.cpp:370-371) are
  * read in place; Tensor::contiguous (src/tensor.cpp:174-193) only copies, it
@@ -173,4 +185,114 @@ void orc_softmax_backward(const float *g, const float *y, float *dx, int64_t row
         for (int64_t j = nv; j < D; ++j) dot = fmaf(gr[j], yr[j], dot);
         for (int64_t i = 0; i < D; ++i) o[i] = yr[i] * (gr[i] - dot);
     }
+}
+
+/* dot over d in the Release build's rounding (see the header): the first
+ * d - d mod vec products rounded and added in order, the tail fused; vec <= 0
+ * means a plain fused chain. */
+static float vdot(const float *a, const float *b, int64_t d, int64_t vec) {
+    const int64_t nv = vec > 0 ? d - d % vec : 0;
+    float dot = 0.0f;
+    for (int64_t c = 0; c < nv; ++c) {
+        const float p = a[c] * b[c];
+        dot = dot + p;
+    }
+    for (int64_t c = nv; c < d; ++c) dot = fmaf(a[c], b[c], dot);
+    return dot;
+}
+
+/* flash_attention (src/ops.cpp:1040-1137) on one head: q, k, v, o [S, d],
+ * lse [S] (the reference's L_cache). */
+void orc_flash_attention(const float *q, const float *k, const float *v, int64_t S, int64_t d,
+                         float scale, float *o, float *lse, int64_t vec) {
+    enum { B = 64 };
+    float *T = malloc(sizeof(float) * B * B);
+    float *m = malloc(sizeof(float) * B), *l = malloc(sizeof(float) * B);
+    float *acc = malloc(sizeof(float) * B * (d > 0 ? d : 1));
+    for (int64_t i0 = 0; i0 < S; i0 += B) {
+        const int64_t qr = S - i0 < B ? S - i0 : B;
+        for (int64_t i = 0; i < qr; ++i) {
+            m[i] = -INFINITY;
+            l[i] = 0.0f;
+            for (int64_t c = 0; c < d; ++c) acc[i * d + c] = 0.0f;
+        }
+        for (int64_t j0 = 0; j0 < S; j0 += B) {
+            const int64_t kr = S - j0 < B ? S - j0 : B;
+            for (int64_t i = 0; i < qr; ++i)
+                for (int64_t j = 0; j < kr; ++j)
+                    T[i * B + j] = vdot(q + (i0 + i) * d, k + (j0 + j) * d, d, vec) * scale;
+            for (int64_t i = 0; i < qr; ++i) {
+                float mb = -INFINITY;
+                for (int64_t j = 0; j < kr; ++j) mb = mb < T[i * B + j] ? T[i * B + j] : mb;  /* std::max(mb, t) */
+                const float mn = m[i] < mb ? mb : m[i];  /* std::max(m, mb) */
+                const float corr = expf(m[i] - mn);
+                float rs = 0.0f;
+                for (int64_t j = 0; j < kr; ++j) {
+                    const float p = expf(T[i * B + j] - mn);
+                    T[i * B + j] = p;
+                    rs = rs + p;
+                }
+                l[i] = fmaf(l[i], corr, rs);
+                float *a = acc + i * d;
+                for (int64_t c = 0; c < d; ++c) a[c] = a[c] * corr;
+                for (int64_t j = 0; j < kr; ++j) {
+                    const float p = T[i * B + j];
+                    const float *vr = v + (j0 + j) * d;
+                    for (int64_t c = 0; c < d; ++c) a[c] = fmaf(p, vr[c], a[c]);
+                }
+                m[i] = mn;
+            }
+        }
+        for (int64_t i = 0; i < qr; ++i) {
+            const float inv = 1.0f / l[i];
+            for (int64_t c = 0; c < d; ++c) o[(i0 + i) * d + c] = acc[i * d + c] * inv;
+            lse[i0 + i] = m[i] + logf(l[i]);
+        }
+    }
+    free(T);
+    free(m);
+    free(l);
+    free(acc);
+}
+
+/* FlashAttentionBackward (src/autograd.cpp:575-669) on one head; dq, dk, dv
+ * are overwritten (the reference starts them from zeros). */
+void orc_flash_attention_backward(const float *dout, const float *q, const float *k,
+                                  const float *v, const float *o, const float *lse, int64_t S,
+                                  int64_t d, float scale, float *dq, float *dk, float *dv,
+                                  int64_t vec) {
+    enum { B = 64 };
+    float *D = malloc(sizeof(float) * (S > 0 ? S : 1));
+    float *P = malloc(sizeof(float) * B * B);
+    for (int64_t i = 0; i < S * d; ++i) dq[i] = dk[i] = dv[i] = 0.0f;
+    for (int64_t i = 0; i < S; ++i) D[i] = vdot(dout + i * d, o + i * d, d, vec);
+    for (int64_t i0 = 0; i0 < S; i0 += B) {
+        const int64_t qr = S - i0 < B ? S - i0 : B;
+        for (int64_t j0 = 0; j0 < S; j0 += B) {
+            const int64_t kr = S - j0 < B ? S - j0 : B;
+            for (int64_t i = 0; i < qr; ++i)
+                for (int64_t j = 0; j < kr; ++j) {
+                    const float t = vdot(q + (i0 + i) * d, k + (j0 + j) * d, d, vec) * scale;
+                    P[i * B + j] = expf(t - lse[i0 + i]);
+                }
+            for (int64_t i = 0; i < qr; ++i) {
+                const float *doi = dout + (i0 + i) * d, *qi = q + (i0 + i) * d;
+                float *dqi = dq + (i0 + i) * d;
+                const float Di = D[i0 + i];
+                for (int64_t j = 0; j < kr; ++j) {
+                    const float p = P[i * B + j];
+                    const float *vr = v + (j0 + j) * d, *kr_ = k + (j0 + j) * d;
+                    float *dvj = dv + (j0 + j) * d, *dkj = dk + (j0 + j) * d;
+                    const float dp = vdot(doi, vr, d, vec);
+                    const float ds = p * (dp - Di);
+                    const float sds = scale * ds;
+                    for (int64_t c = 0; c < d; ++c) dvj[c] = fmaf(p, doi[c], dvj[c]);
+                    for (int64_t c = 0; c < d; ++c) dqi[c] = fmaf(sds, kr_[c], dqi[c]);
+                    for (int64_t c = 0; c < d; ++c) dkj[c] = fmaf(sds, qi[c], dkj[c]);
+                }
+            }
+        }
+    }
+    free(D);
+    free(P);
 }

@@ -82,6 +82,16 @@ class Conv2dBackward : public GradFunction {
     void backward(const Tensor& grad_output) override;
 };
 
+// src/autograd.cpp:575-669 (inputs: Q, K, V); the caches as the reference keeps
+// them (contiguous Q, K, V, the output O and L = m + log(l) per row)
+class FlashAttentionBackward : public GradFunction {
+  public:
+    Tensor Q_cache, K_cache, V_cache, O_cache, L_cache;
+    float sm_scale = 1.0f;
+    int mode = -1;
+    void backward(const Tensor& grad_output) override;
+};
+
 // matmul_add / matmul_scale: the reference's AddBackward or ScaleBackward
 // followed by MatmulBackward, in one node
 class FusedMatmulBackward : public GradFunction {

@@ -46,6 +46,12 @@ Tensor matmul_scale(const Tensor& a, const Tensor& b, float scalar);
 // std::invalid_argument messages.
 Tensor conv2d(const Tensor& input, const Tensor& weight, const Tensor& bias, int64_t stride = 1,
               int64_t padding = 0, int64_t groups = 1);
+// flash attention (src/ops.cpp:1040-1137): out = softmax(Q . K^T * sm_scale) . V
+// for [S, d] tensors (or [..., S, d], one head per leading index), d <= 128:
+// one fused device kernel with the reference's 64 x 64 tiles and online
+// softmax; FlashAttentionBackward in the process default GEMM mode.  Agrees
+// with the reference to its own 1e-4 bar (CUDA's expf / logf).
+Tensor flash_attention(const Tensor& Q, const Tensor& K, const Tensor& V, float sm_scale);
 // sum along a dimension (src/ops.cpp:1181-1233); no autograd node
 Tensor sum(const Tensor& input, int64_t dim, bool keepdim = false);
 

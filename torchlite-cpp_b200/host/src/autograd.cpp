@@ -102,6 +102,25 @@ void SoftmaxBackward::backward(const Tensor& grad_output) {
     accumulate_grad(inputs[0], dx);
 }
 
+// src/autograd.cpp:575-669: dQ, dK, dV from libtl_cuda (recomputed
+// probabilities, batched GEMMs), then accumulate_grad into Q, K, V.
+void FlashAttentionBackward::backward(const Tensor& grad_output) {
+    Tensor dq = Tensor::device_empty(Q_cache.sizes()), dk = Tensor::device_empty(Q_cache.sizes()),
+           dv = Tensor::device_empty(Q_cache.sizes());
+    if (dq.numel() > 0) {
+        Tensor g = grad_output.contiguous();
+        tlc_tensor vg = dview(g), vq = dview(Q_cache), vk = dview(K_cache), vv = dview(V_cache),
+                   vo = dview(O_cache), vl = dview(L_cache), vdq = dview(dq), vdk = dview(dk),
+                   vdv = dview(dv);
+        check(tlc_flash_attention_backward(&vg, &vq, &vk, &vv, &vo, &vl, sm_scale, &vdq, &vdk, &vdv,
+                                           mode, nullptr),
+              "tlc_flash_attention_backward");
+    }
+    if (inputs[0].requires_grad) accumulate_grad(inputs[0], dq);
+    if (inputs[1].requires_grad) accumulate_grad(inputs[1], dk);
+    if (inputs[2].requires_grad) accumulate_grad(inputs[2], dv);
+}
+
 // src/autograd.cpp:386-517: all three gradients from libtl_cuda in the
 // reference's summation orders, then accumulate_grad.
 void Conv2dBackward::backward(const Tensor& grad_output) {

@@ -36,6 +36,15 @@ tlc_tensor view_of(const Tensor& t, bool device) {
     return v;
 }
 
+// The same storage and view without the autograd links: what a node keeps of
+// its own output, so that the node and the output do not own each other.
+Tensor detached(const Tensor& t) {
+    Tensor d = t;
+    d.grad_fn.reset();
+    d.requires_grad = false;
+    return d;
+}
+
 }  // namespace
 
 Tensor matmul(const Tensor& a_in, const Tensor& b_in) {
@@ -184,7 +193,7 @@ Tensor softmax(const Tensor& input) {
         check(tlc_softmax(&vx, &vo, nullptr), "tlc_softmax");
     }
     if (input.requires_grad) {
-        if (auto fn = track<SoftmaxBackward>(out, {&input})) fn->output_cache = out;
+        if (auto fn = track<SoftmaxBackward>(out, {&input})) fn->output_cache = detached(out);
     }
     return out;
 }
@@ -275,6 +284,31 @@ Tensor conv2d(const Tensor& input, const Tensor& weight, const Tensor& bias, int
         }
     }
     return out;
+}
+
+// src/ops.cpp:1040-1137
+Tensor flash_attention(const Tensor& Q, const Tensor& K, const Tensor& V, float sm_scale) {
+    if (Q.sizes().size() < 2) throw std::invalid_argument("flash_attention: tensors must be at least 2-D [S, d]");
+    Tensor Qc = Q.contiguous(), Kc = K.contiguous(), Vc = V.contiguous();
+    Tensor O = Tensor::device_empty(Qc.sizes());
+    Tensor L = Tensor::device_empty(std::vector<int64_t>(Qc.sizes().begin(), Qc.sizes().end() - 1));
+    tlc_tensor vq = view_of(Qc, true), vk = view_of(Kc, true), vv = view_of(Vc, true);
+    tlc_tensor vo = view_of(O, false), vl = view_of(L, false);
+    if (O.numel() > 0) vo.data = O.device_data();
+    if (L.numel() > 0) vl.data = L.device_data();
+    check(tlc_flash_attention(&vq, &vk, &vv, sm_scale, &vo, &vl, nullptr), "tlc_flash_attention");
+    if (Q.requires_grad || K.requires_grad || V.requires_grad) {
+        if (auto fn = track<FlashAttentionBackward>(O, {&Q, &K, &V})) {
+            fn->Q_cache = Qc;
+            fn->K_cache = Kc;
+            fn->V_cache = Vc;
+            fn->O_cache = detached(O);
+            fn->L_cache = L;
+            fn->sm_scale = sm_scale;
+            fn->mode = TLC_MODE_DEFAULT;
+        }
+    }
+    return O;
 }
 
 Tensor sum(const Tensor& input, int64_t dim, bool keepdim) {

@@ -20,6 +20,7 @@
 #include <iostream>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #define CHECK(cond)                                                              \
     do {                                                                         \
@@ -282,6 +283,50 @@ static void test_model_io() {
     std::cout << "model_io ok\n";
 }
 
+// tests/test_ops.cpp:651-704 of the reference: flash attention against the
+// materialised path (scaled matmul, softmax, matmul), forward and the
+// gradients of backward() seeded with ones, S = 80 crossing the 64-row tile.
+static void test_flash_attention() {
+    const int64_t S = 80, d = 16;
+    uint32_t st = 12345u;
+    auto fill = [&](tl::Tensor& t) {
+        for (int64_t i = 0; i < t.numel(); ++i) {
+            st = st * 1664525u + 1013904223u;
+            t.data()[i] = ((st >> 8) & 0xFFFF) / 16384.0f - 2.0f;
+        }
+    };
+    tl::Tensor Q({S, d}), K({S, d}), V({S, d});
+    fill(Q);
+    fill(K);
+    fill(V);
+    const float sm_scale = 1.0f / std::sqrt((float)d);
+    {
+        tl::Tensor scores = tl::scale(tl::matmul(Q, tl::transpose(K, 0, 1)), sm_scale);
+        tl::Tensor ref = tl::matmul(tl::softmax(scores), V);
+        tl::Tensor flash = tl::flash_attention(Q, K, V, sm_scale);
+        CHECK(flash.sizes()[0] == S && flash.sizes()[1] == d);
+        for (int64_t i = 0; i < S * d; ++i) CHECK(is_close(flash.data()[i], ref.data()[i], 1e-4f));
+    }
+    Q.set_requires_grad(true);
+    K.set_requires_grad(true);
+    V.set_requires_grad(true);
+    tl::Tensor ref = tl::matmul(tl::softmax(tl::scale(tl::matmul(Q, tl::transpose(K, 0, 1)), sm_scale)), V);
+    ref.backward();
+    std::vector<float> dq(Q.grad().data(), Q.grad().data() + S * d),
+        dk(K.grad().data(), K.grad().data() + S * d), dv(V.grad().data(), V.grad().data() + S * d);
+    Q.grad() = tl::Tensor();
+    K.grad() = tl::Tensor();
+    V.grad() = tl::Tensor();
+    tl::Tensor flash = tl::flash_attention(Q, K, V, sm_scale);
+    flash.backward();
+    for (int64_t i = 0; i < S * d; ++i) {
+        CHECK(is_close(Q.grad().data()[i], dq[i], 1e-4f));
+        CHECK(is_close(K.grad().data()[i], dk[i], 1e-4f));
+        CHECK(is_close(V.grad().data()[i], dv[i], 1e-4f));
+    }
+    std::cout << "flash_attention ok\n";
+}
+
 int main(int argc, char** argv) {
     const bool cpu_only = argc > 1 && std::string(argv[1]) == "--cpu";
     test_errors();
@@ -292,6 +337,7 @@ int main(int argc, char** argv) {
     test_linear_backward_transposed();
     test_tensor_core_modes();
     test_model_io();
+    test_flash_attention();
     std::cout << "all tl:: tests passed\n";
     return 0;
 }

@@ -93,6 +93,9 @@ SIGNATURES = {
     "tlc_conv2d_shape": ([_T, _T, _i64, _i64, _i64, _P(_i64)], _i),
     "tlc_conv2d": ([_T, _T, _T, _i64, _i64, _i64, _T, _i, _v], _i),
     "tlc_conv2d_backward": ([_T, _T, _T, _i64, _i64, _i64, _T, _T, _T, _i, _v], _i),
+    "tlc_flash_attention": ([_T, _T, _T, ctypes.c_float, _T, _T, _v], _i),
+    "tlc_flash_attention_backward": ([_T, _T, _T, _T, _T, _T, ctypes.c_float, _T, _T, _T, _i, _v],
+                                     _i),
     "tlc_load_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
     "tlc_save_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
     "tlc_shard_range": ([_i64, _i, _i, _P(_i64), _P(_i64)], _i),
@@ -374,6 +377,35 @@ def conv2d_backward(grad, x, w, stride=1, padding=0, groups=1, mode="exact", nee
                                      *[ctypes.byref(v) if v else None for v in views],
                                      mode_id(mode), _stream_ptr(stream)))
     return tuple(outs)
+
+
+def flash_attention(q, k, v, sm_scale, out=None, lse=None, stream=None):
+    """tl::flash_attention on CUDA [..., S, d] tensors (every leading index a
+    head): returns (out, lse), lse = m + log(l) per row, what the backward needs."""
+    import torch
+    if out is None:
+        out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty(tuple(q.shape[:-1]), dtype=torch.float32, device=q.device)
+    vq, vk, vv, vo, vl = (view_of(t) for t in (q, k, v, out, lse))
+    _check(lib().tlc_flash_attention(ctypes.byref(vq), ctypes.byref(vk), ctypes.byref(vv),
+                                     float(sm_scale), ctypes.byref(vo), ctypes.byref(vl),
+                                     _stream_ptr(stream)))
+    return out, lse
+
+
+def flash_attention_backward(grad, q, k, v, out, lse, sm_scale, mode="exact", dq=None, dk=None,
+                             dv=None, stream=None):
+    """FlashAttentionBackward: (dq, dk, dv)."""
+    import torch
+    dq, dk, dv = (t if t is not None else torch.empty(tuple(q.shape), device=q.device)
+                  for t in (dq, dk, dv))
+    vs = [view_of(t) for t in (grad, q, k, v, out, lse)]
+    vd = [view_of(t) for t in (dq, dk, dv)]
+    _check(lib().tlc_flash_attention_backward(*[ctypes.byref(x) for x in vs], float(sm_scale),
+                                              *[ctypes.byref(x) for x in vd], mode_id(mode),
+                                              _stream_ptr(stream)))
+    return dq, dk, dv
 
 
 def _views(tensors):
