@@ -401,26 +401,31 @@ class FlashWork(Work):
         self.flops = self.fwd_flops + 10.0 * heads * S * S * d
         self.job_flops = self.flops * world
         self.config = {"workload": "flash", "batch": 16, "heads": 12, "S": 2048, "d": 64,
-                       "sm_scale": 0.125, "forward": "fused FFMA kernel (fp32 exact arithmetic)",
+                       "sm_scale": 0.125,
+                       "forward": "fused kernel: tcgen05 TF32 in tf32 mode, FFMA otherwise",
                        "backward": "5 batched GEMMs in the mode + elementwise kernels",
                        "parallelism": "replicas"}
 
-    def forward(self):
+    def forward(self, mode):
         import tlcuda
-        tlcuda.flash_attention(self.q, self.k, self.v, 0.125, out=self.o, lse=self.lse)
+        tlcuda.flash_attention(self.q, self.k, self.v, 0.125, out=self.o, lse=self.lse, mode=mode)
 
     def step(self, mode):
         import tlcuda
-        self.forward()
+        self.forward(mode)
         tlcuda.flash_attention_backward(self.dO, self.q, self.k, self.v, self.o, self.lse, 0.125,
                                         mode=mode, dq=self.dq, dk=self.dk, dv=self.dv)
 
-    def forward_roofline(self, world, stream, peak, steps=10):
-        """The forward kernel alone against the FP32 FFMA peak (peak_for("exact"))."""
-        ms, _ = time_device(self.forward, steps, 3, world, stream)
+    def forward_roofline(self, world, stream, mode, peak, steps=10):
+        """The forward kernel alone against its peak: tf32 the tensor-core
+        kernel (flash_tc_kernel) against TF32, else the FFMA kernel
+        (flash_fwd_kernel<64>) against the FP32 FFMA peak."""
+        ms, _ = time_device(lambda: self.forward(mode), steps, 3, world, stream)
         ach = self.fwd_flops / (ms * 1e-3) / 1e12
-        return {"kernel": "flash_fwd_kernel<64>", "ms": ms, "achieved": ach, "peak": peak[0],
-                "unit": "TFLOP/s", "frac": ach / peak[0], "bound": "fp32-fma",
+        tc = mode == "tf32"
+        return {"kernel": "flash_tc_kernel" if tc else "flash_fwd_kernel<64>", "mode": mode,
+                "ms": ms, "achieved": ach, "peak": peak[0], "unit": "TFLOP/s",
+                "frac": ach / peak[0], "bound": "tensor" if tc else "fp32-fma",
                 "peak_source": peak[1], "algorithmic_flop_per_launch": self.fwd_flops}
 
 
@@ -583,8 +588,10 @@ def run_ours(args):
     gather = work.gather_ms(world, stream) if isinstance(work, GemmWork) else None
     fwd = None
     if isinstance(work, FlashWork):
-        fwd = work.forward_roofline(world, stream, peak_for("exact", peaks, psrc, sms,
-                                                            peaks.get("sm_max_mhz", 1965.0)))
+        fmode = args.mode if args.mode == "tf32" else "exact"
+        fwd = [work.forward_roofline(world, stream, m, peak_for(m, peaks, psrc, sms,
+                                                                peaks.get("sm_max_mhz", 1965.0)))
+               for m in dict.fromkeys((fmode, "exact"))]
 
     # End to end through the host-buffer C entry point (page-locked host memory).
     e2e = None

@@ -261,8 +261,11 @@ int tlc_conv2d_backward(const tlc_tensor* grad_output, const tlc_tensor* input,
  * flash_attention (src/ops.cpp:1040-1137): out = softmax(q . k^T * sm_scale) . v
  * for q, k, v, out contiguous [..., S, d] device tensors of one shape (every
  * leading index a separate head; the reference takes one head [S, d]),
- * d <= 128.  One fused fp32 kernel, 64 x 64 query / key tiles with the
- * reference's online-softmax update, no S x S buffer.  `lse` ([..., S],
+ * d <= 128, no S x S buffer.  TLC_MODE_EXACT / _3XTF32: one fused fp32 FFMA
+ * kernel with the reference's 64 x 64 tiles and online-softmax update;
+ * TLC_MODE_TF32 with 32 <= d <= 64 (d % 4 == 0, 16-byte aligned q, k, v): the
+ * same update around tcgen05 TF32 products (scores in tensor memory), within
+ * the TF32 tolerance; other TF32 cases run the FFMA kernel.  `lse` ([..., S],
  * contiguous, or NULL) receives L = m + log(l), the reference's L_cache.
  * FlashAttentionBackward (src/autograd.cpp:575-669): d_q, d_k, d_v from
  * grad_out, the forward's inputs, out and lse, through batched GEMMs in
@@ -273,7 +276,7 @@ int tlc_conv2d_backward(const tlc_tensor* grad_output, const tlc_tensor* input,
  * operands, fewer than 2 dims (TLC_ERR_INVALID_ARGUMENT); d > 128
  * (TLC_ERR_UNSUPPORTED). */
 int tlc_flash_attention(const tlc_tensor* q, const tlc_tensor* k, const tlc_tensor* v,
-                        float sm_scale, tlc_tensor* out, tlc_tensor* lse, void* stream);
+                        float sm_scale, tlc_tensor* out, tlc_tensor* lse, int mode, void* stream);
 int tlc_flash_attention_backward(const tlc_tensor* grad_out, const tlc_tensor* q,
                                  const tlc_tensor* k, const tlc_tensor* v, const tlc_tensor* out,
                                  const tlc_tensor* lse, float sm_scale, tlc_tensor* d_q,

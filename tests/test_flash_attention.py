@@ -5,7 +5,9 @@ CPU: the oracle's restatement (64 x 64 tiles, online softmax, the Release
 build's rounding of each dot over d) equals the reference compiled from its
 sources bit for bit, forward and backward, on tile-crossing and ragged shapes;
 the library's argument checks.
-GPU: tlc_flash_attention / _backward against the oracle.  The reference's own
+GPU: tlc_flash_attention / _backward against the oracle (exact mode: the
+FFMA forward kernel; tf32: the tensor-core forward, checked to the TF32
+tolerance).  The reference's own
 bar for flash attention is 1e-4 per element against the materialised softmax
 path (tests/test_ops.cpp:651-704); the device path keeps to
 |gpu - oracle| <= FA_ATOL + FA_RTOL * |oracle| per element (CUDA's expf and
@@ -76,7 +78,7 @@ def test_library_argument_checks():
         vl = tlcuda.view_of(lse) if lse is not None else None
         return L.tlc_flash_attention(tlcuda.ctypes.byref(vq), tlcuda.ctypes.byref(vk),
                                      tlcuda.ctypes.byref(vk), 1.0, tlcuda.ctypes.byref(vo),
-                                     tlcuda.ctypes.byref(vl) if vl else None, None)
+                                     tlcuda.ctypes.byref(vl) if vl else None, 0, None)
 
     assert call(np.ones((4, 9), np.float32), np.ones((4, 8), np.float32)) == 1
     assert "shapes differ" in L.tlc_last_error().decode()
@@ -87,7 +89,7 @@ def test_library_argument_checks():
     big = np.ones((2, 129), np.float32)
     vb = tlcuda.view_of(big)
     st = L.tlc_flash_attention(*(tlcuda.ctypes.byref(vb) for _ in range(3)), 1.0,
-                               tlcuda.ctypes.byref(vb), None, None)
+                               tlcuda.ctypes.byref(vb), None, 0, None)
     assert st == 2 and "head dim above 128" in L.tlc_last_error().decode()
 
 
@@ -132,9 +134,10 @@ def test_device_unaligned_operands():
         t = flat[1 + i * q.size:1 + (i + 1) * q.size].view(q.shape)
         t.copy_(torch.from_numpy(a))
         views.append(t)
-    out, _ = tlcuda.flash_attention(*views, sc)
-    ok, e = close(out.cpu().numpy(), O.flash_attention(q, k, v, sc)[0])
-    assert ok, e
+    for mode in ("exact", "tf32"):  # tf32 too: unaligned operands take the FFMA kernel
+        out, _ = tlcuda.flash_attention(*views, sc, mode=mode)
+        ok, e = close(out.cpu().numpy(), O.flash_attention(q, k, v, sc)[0])
+        assert ok, (mode, e)
 
 
 @pytest.mark.gpu
@@ -161,29 +164,65 @@ def test_device_matches_materialised_path():
         assert (got - want).abs().max().item() <= 1e-4
 
 
+# TF32 forward (tensor-core kernel): relative Frobenius error of O and L
+# against the oracle / fp64 within the TF32 tolerance
+TF32_TOL = 1e-2
+TF32_CASES = [((), 80, 64), ((2, 3), 300, 64), ((4,), 1000, 32), ((2,), 129, 48), ((), 1, 64),
+              ((), 64, 40), ((3,), 257, 64)]
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,S,d", TF32_CASES)
+def test_device_tf32_forward(heads, S, d):
+    """mode tf32: the tensor-core forward (32 <= d <= 64) against the oracle."""
+    torch = pytest.importorskip("torch")
+    import tlcuda
+    q, k, v, _, sc = case_data(heads, S, d, 25)
+    Q, K, V = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    launches = tlcuda.launch_count()
+    out, lse = tlcuda.flash_attention(Q, K, V, sc, mode="tf32")
+    assert tlcuda.lib().tlc_check_device_errors() == 0  # no bounded wait gave up
+    assert tlcuda.launch_count() == launches + 1
+    o_o, l_o = O.flash_attention(q, k, v, sc)
+    assert rel(out.cpu().numpy(), o_o) <= TF32_TOL
+    # L = m + log(l) is a log-sum of scores: its TF32 error is absolute (the
+    # scores' rounding), so it is bounded against max(1, |L|), not |L| alone
+    dl = np.abs(lse.cpu().numpy().astype(np.float64) - l_o)
+    assert dl.max() <= TF32_TOL * max(1.0, float(np.abs(l_o).max()))
+    assert np.isfinite(out.cpu().numpy()).all()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode,tol", [("exact", 1e-5), ("3xtf32", 1e-5), ("tf32", 1e-2)])
 def test_device_large_against_fp64(mode, tol):
     """A multi-head case too large for the oracle: 8 heads of S = 2048, d = 64,
-    against torch's fp64 materialised attention and its autograd."""
+    against torch's fp64 materialised attention and its autograd; the forward
+    in the same mode (tf32: the tensor-core kernel)."""
     torch = pytest.importorskip("torch")
     import tlcuda
     g = torch.Generator(device="cuda").manual_seed(24)
     Q, K, V, G = (torch.randn((8, 2048, 64), generator=g, device="cuda") for _ in range(4))
     sc = 0.125
-    out, lse = tlcuda.flash_attention(Q, K, V, sc)
+    out, lse = tlcuda.flash_attention(Q, K, V, sc, mode=mode)
     dq, dk, dv = tlcuda.flash_attention_backward(G, Q, K, V, out, lse, sc, mode=mode)
     Qd, Kd, Vd = (t.double().requires_grad_() for t in (Q, K, V))
     ref = torch.softmax(Qd @ Kd.transpose(1, 2) * sc, -1) @ Vd
     ref.backward(G.double())
 
-    def rel(a, b):
+    def trel(a, b):
         return ((a.double() - b).norm() / b.norm()).item()
-    assert rel(out, ref.detach()) <= 1e-6
+    ftol = 1e-6 if mode != "tf32" else TF32_TOL
+    assert trel(out, ref.detach()) <= ftol
     lse_ref = torch.logsumexp(Qd.detach() @ Kd.detach().transpose(1, 2) * sc, -1)
-    assert rel(lse, lse_ref) <= 1e-6
+    assert trel(lse, lse_ref) <= ftol
     for got, want in ((dq, Qd.grad), (dk, Kd.grad), (dv, Vd.grad)):
-        assert rel(got, want) <= tol, (mode, rel(got, want))
+        assert trel(got, want) <= tol, (mode, trel(got, want))
 
 
 @pytest.mark.gpu

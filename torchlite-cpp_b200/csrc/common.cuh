@@ -130,6 +130,11 @@ int launch_elementwise(const float* a, const float* b, float s, float* out, int6
 int launch_epilogue(float* C, int64_t rows, int64_t cols, float s, bool apply_scale,
                     const float* bias, cudaStream_t st);
 int launch_softmax(const float* x, float* y, int64_t rows, int64_t D, cudaStream_t st);
+// Attention forward on the tensor cores (flash_tc.cu): q, k, v, o [heads, S, d]
+// contiguous, lse [heads, S] or NULL.
+bool flash_tc_supported(int d, const float* q, const float* k, const float* v);
+int flash_forward_tc(const float* q, const float* k, const float* v, float* o, float* lse,
+                     int64_t heads, int S, int d, float scale, cudaStream_t s);
 int launch_softmax_backward(const float* g, const float* y, float* dx, int64_t rows, int64_t D,
                             cudaStream_t st);
 

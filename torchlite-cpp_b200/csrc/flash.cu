@@ -2,7 +2,8 @@
 // FlashAttentionBackward (src/autograd.cpp:575-669) on the GPU, for one head
 // [S, d] as the reference takes it, or a batch of heads [..., S, d].
 //
-// Forward: one fused kernel, fp32 FFMA, no S x S buffer.  A CTA owns 64
+// Forward (TLC_MODE_EXACT and _3XTF32, and TF32 where the tensor-core kernel
+// of flash_tc.cu does not apply): one fused kernel, fp32 FFMA, no S x S buffer.  A CTA owns 64
 // query rows; for each 64-key tile it computes T = (Q_i . K_j^T) * scale
 // (each dot an ascending-c fmaf chain), then the reference's online-softmax
 // update per row: m_new = max(m, max_j T), corr = exp(m - m_new),
@@ -341,8 +342,11 @@ constexpr int64_t kBwdChunkBytes = int64_t(1) << 30;
 using namespace tlc;
 
 extern "C" int tlc_flash_attention(const tlc_tensor* q, const tlc_tensor* k, const tlc_tensor* v,
-                                   float sm_scale, tlc_tensor* out, tlc_tensor* lse, void* stream) {
+                                   float sm_scale, tlc_tensor* out, tlc_tensor* lse, int mode,
+                                   void* stream) {
     clear_error();
+    int m;
+    TLC_TRY(resolve(mode, m));
     if (!out) return set_error(TLC_ERR_INVALID_ARGUMENT, "flash_attention: out is NULL");
     Heads h;
     const tlc_tensor* ts[4] = {q, k, v, out};
@@ -355,6 +359,8 @@ extern "C" int tlc_flash_attention(const tlc_tensor* q, const tlc_tensor* k, con
     if (h.heads * h.S == 0) return TLC_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     float* l = lse ? lse->data : nullptr;
+    if (m == TLC_MODE_TF32 && flash_tc_supported(h.d, q->data, k->data, v->data))
+        return flash_forward_tc(q->data, k->data, v->data, out->data, l, h.heads, h.S, h.d, sm_scale, s);
     if (h.d <= 32) return launch_fwd<32>(q->data, k->data, v->data, out->data, l, h, sm_scale, s);
     if (h.d <= 64) return launch_fwd<64>(q->data, k->data, v->data, out->data, l, h, sm_scale, s);
     return launch_fwd<128>(q->data, k->data, v->data, out->data, l, h, sm_scale, s);

@@ -296,7 +296,8 @@ Tensor flash_attention(const Tensor& Q, const Tensor& K, const Tensor& V, float 
     tlc_tensor vo = view_of(O, false), vl = view_of(L, false);
     if (O.numel() > 0) vo.data = O.device_data();
     if (L.numel() > 0) vl.data = L.device_data();
-    check(tlc_flash_attention(&vq, &vk, &vv, sm_scale, &vo, &vl, nullptr), "tlc_flash_attention");
+    check(tlc_flash_attention(&vq, &vk, &vv, sm_scale, &vo, &vl, TLC_MODE_DEFAULT, nullptr),
+          "tlc_flash_attention");
     if (Q.requires_grad || K.requires_grad || V.requires_grad) {
         if (auto fn = track<FlashAttentionBackward>(O, {&Q, &K, &V})) {
             fn->Q_cache = Qc;

@@ -93,7 +93,7 @@ SIGNATURES = {
     "tlc_conv2d_shape": ([_T, _T, _i64, _i64, _i64, _P(_i64)], _i),
     "tlc_conv2d": ([_T, _T, _T, _i64, _i64, _i64, _T, _i, _v], _i),
     "tlc_conv2d_backward": ([_T, _T, _T, _i64, _i64, _i64, _T, _T, _T, _i, _v], _i),
-    "tlc_flash_attention": ([_T, _T, _T, ctypes.c_float, _T, _T, _v], _i),
+    "tlc_flash_attention": ([_T, _T, _T, ctypes.c_float, _T, _T, _i, _v], _i),
     "tlc_flash_attention_backward": ([_T, _T, _T, _T, _T, _T, ctypes.c_float, _T, _T, _T, _i, _v],
                                      _i),
     "tlc_load_tlmd": ([ctypes.c_char_p, ctypes.c_int32, _T, _v], _i),
@@ -379,9 +379,10 @@ def conv2d_backward(grad, x, w, stride=1, padding=0, groups=1, mode="exact", nee
     return tuple(outs)
 
 
-def flash_attention(q, k, v, sm_scale, out=None, lse=None, stream=None):
+def flash_attention(q, k, v, sm_scale, out=None, lse=None, mode="exact", stream=None):
     """tl::flash_attention on CUDA [..., S, d] tensors (every leading index a
-    head): returns (out, lse), lse = m + log(l) per row, what the backward needs."""
+    head): returns (out, lse), lse = m + log(l) per row, what the backward needs.
+    mode "tf32" runs the tensor-core kernel where it applies (32 <= d <= 64)."""
     import torch
     if out is None:
         out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
@@ -390,7 +391,7 @@ def flash_attention(q, k, v, sm_scale, out=None, lse=None, stream=None):
     vq, vk, vv, vo, vl = (view_of(t) for t in (q, k, v, out, lse))
     _check(lib().tlc_flash_attention(ctypes.byref(vq), ctypes.byref(vk), ctypes.byref(vv),
                                      float(sm_scale), ctypes.byref(vo), ctypes.byref(vl),
-                                     _stream_ptr(stream)))
+                                     mode_id(mode), _stream_ptr(stream)))
     return out, lse
 
 
