@@ -17,13 +17,14 @@
 //               block accumulator per query tile.
 //   warps 2-5   softmax for query tile 0, warps 6-9 for query tile 1; thread
 //               = one query row (TMEM lane).  Per key block: tcgen05.ld the
-//               score row, t = s * scale (masked to -inf past S),
-//               m_new = max(m, max t), corr = exp(m - m_new),
-//               p = exp(t - m_new), l = l * corr + sum p, p written into the
-//               P tile in shared memory (the K-major A operand of P.V, same
-//               swizzle as a TMA tile); then, once P.V is done,
-//               o = o * corr + O_blk in registers.  At the end
-//               O = o * (1 / l), L = m + log(l).
+//               score row, t = s * scale (masked to -inf past S), in log2
+//               units; m_new = max(m, max t), corr = exp(m - m_new),
+//               p = exp(t - m_new), l = l * corr + sum p (max and sum as
+//               trees); p is written into the P tile in shared memory (the
+//               K-major A operand of P.V, same swizzle as a TMA tile) after
+//               the previous block's O_blk has been folded into registers
+//               (o = o * corr + O_blk), so each P.V runs under the next
+//               block's softmax.  At the end O = o * (1 / l), L = m + log(l).
 // The two query tiles' softmax warps share the SM's exp units and alternate
 // with each other's tensor-core work.  Every mbarrier wait is bounded (a
 // %globaltimer deadline, an abort flag, the device error word), as in the
@@ -283,6 +284,9 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         }
     } else {
         // ---------------- softmax (warps 2-5: tile 0, 6-9: tile 1) ----------------
+        // Scores are kept in log2 units (u = s * scale * log2 e, so exp(t - m) =
+        // exp2(u - m2)).  O_blk of block j is folded into o while block j + 1's
+        // probabilities are computed, so P.V(j) runs under softmax(j + 1).
         const int t = (warp - 2) >> 2;
         const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
         const int r = quarter * 32 + lane;
@@ -290,72 +294,98 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
         uint8_t* prow = smem + OFF_P + t * P_BYTES + r * 128;
         const int sw = r & 7;
+        const float sl2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
         float o[FD];
 #pragma unroll
         for (int c = 0; c < FD; ++c) o[c] = 0.0f;
-        float m = -INFINITY, l = 0.0f;
+        float m2 = -INFINITY, l = 0.0f, corr_prev = 0.0f;
         bool ok = true;
+        // o = o * corr + O_blk of the block whose P.V completes with parity `par`
+        auto fold_block = [&](uint32_t par, bool release) -> bool {
+            if (!warp_wait(&o_full[t], par, abort_flag, p, 31)) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int h = 0; h < FD / 16; ++h) {
+                uint32_t ob[16];
+                tmem_ld16(lane_base + (uint32_t)(256 + t * 64 + 16 * h), ob);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                    o[16 * h + c] = fmaf(o[16 * h + c], corr_prev, __uint_as_float(ob[c]));
+            }
+            if (release) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_empty[t]);
+            }
+            return true;
+        };
         for (int j = 0; j < p.nk; ++j) {
             const int b = j & 1;
             ok = warp_wait(&s_full[2 * t + b], (uint32_t)(j >> 1) & 1u, abort_flag, p, 30);
             if (!ok) break;
             tc_fence_after();
-            uint32_t s[FK];
+            float u[FK];
             {
-                uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-                uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+                uint32_t s0[32], s1[32];
                 tmem_ld32(lane_base + (uint32_t)(t * 128 + b * 64), s0);
                 tmem_ld32(lane_base + (uint32_t)(t * 128 + b * 64 + 32), s1);
                 tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    u[c] = __fmul_rn(__uint_as_float(s0[c]), sl2);
+                    u[32 + c] = __fmul_rn(__uint_as_float(s1[c]), sl2);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[2 * t + b]);
-            // the reference's row update: T = dot * scale; block max; m_new; corr; p; l
-            const int valid = min(FK, p.S - j * FK);
-            float mb = -INFINITY;
+            const int valid = p.S - j * FK;
+            if (valid < FK) {  // the tail block: keys past S take no weight
 #pragma unroll
-            for (int c = 0; c < FK; ++c) {
-                const float v = c < valid ? __fmul_rn(__uint_as_float(s[c]), p.scale) : -INFINITY;
-                s[c] = __float_as_uint(v);
-                mb = mb < v ? v : mb;
+                for (int c = 0; c < FK; ++c)
+                    if (c >= valid) u[c] = -INFINITY;
             }
-            const float m_new = m < mb ? mb : m;
-            const float corr = expf(__fsub_rn(m, m_new));
-            float rs = 0.0f;
+            // row max and sum as trees (max is exact in any order)
+            float mx[16];
 #pragma unroll
-            for (int c = 0; c < FK; ++c) {
-                const float e = expf(__fsub_rn(__uint_as_float(s[c]), m_new));
-                s[c] = __float_as_uint(e);
-                rs = __fadd_rn(rs, e);
+            for (int c = 0; c < 16; ++c) mx[c] = fmaxf(fmaxf(u[c], u[c + 16]), fmaxf(u[c + 32], u[c + 48]));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int c = 0; c < w; ++c) mx[c] = fmaxf(mx[c], mx[c + w]);
+            const float m_new = fmaxf(m2, mx[0]);
+            const float corr = exp2f(__fsub_rn(m2, m_new));
+#pragma unroll
+            for (int c = 0; c < FK; ++c) u[c] = exp2f(__fsub_rn(u[c], m_new));
+            float sm[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) sm[c] = (u[c] + u[c + 16]) + (u[c + 32] + u[c + 48]);
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int c = 0; c < w; ++c) sm[c] += sm[c + w];
+            // fold the previous block (its P.V ran during this block's softmax);
+            // that also frees the P tile for this block's probabilities
+            if (j > 0) {
+                ok = fold_block((uint32_t)(j - 1) & 1u, true);
+                if (!ok) break;
             }
-            l = fmaf(l, corr, rs);
-            m = m_new;
+            l = fmaf(l, corr, sm[0]);
+            m2 = m_new;
+            corr_prev = corr;
             // P row into the swizzled K-major tile: keys c..c+3 are 16-byte granule
             // (c % 32) / 4 of the row's 128-byte line in block c / 32
 #pragma unroll
             for (int c = 0; c < FK; c += 4) {
                 uint8_t* dst = prow + (c >> 5) * (P_BYTES / 2) + ((((c & 31) >> 2) ^ sw) << 4);
-                *reinterpret_cast<uint4*>(dst) = make_uint4(s[c], s[c + 1], s[c + 2], s[c + 3]);
+                *reinterpret_cast<float4*>(dst) = make_float4(u[c], u[c + 1], u[c + 2], u[c + 3]);
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[t]);
-            ok = warp_wait(&o_full[t], (uint32_t)j & 1u, abort_flag, p, 31);
-            if (!ok) break;
-            tc_fence_after();
-#pragma unroll
-            for (int h = 0; h < FD / 32; ++h) {
-                uint32_t ob[32];
-                tmem_ld32(lane_base + (uint32_t)(256 + t * 64 + 32 * h), ob);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 32; ++c) o[32 * h + c] = fmaf(o[32 * h + c], corr, __uint_as_float(ob[c]));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&o_empty[t]);
         }
+        if (ok) ok = fold_block((uint32_t)(p.nk - 1) & 1u, false);
         if (ok && row < p.S) {
             const float inv = __fdiv_rn(1.0f, l);
             float* orow = p.O + ((int64_t)head * p.S + row) * p.d;
@@ -371,7 +401,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 for (int c = 0; c < FD; ++c)
                     if (c < p.d) orow[c] = __fmul_rn(o[c], inv);
             }
-            if (p.L) p.L[(int64_t)head * p.S + row] = __fadd_rn(m, logf(l));
+            // L = m + log(l) with m = m2 * ln 2 back in the scores' units
+            if (p.L) p.L[(int64_t)head * p.S + row] = __fadd_rn(__fmul_rn(m2, 0.6931471805599453f), logf(l));
         }
     }
 
