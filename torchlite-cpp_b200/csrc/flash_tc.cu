@@ -2,33 +2,38 @@
 // tensor cores: TLC_MODE_TF32, head dim 32 <= d <= 64 with d % 4 == 0 and
 // 16-byte aligned operands (the TMA tiles' requirements).
 //
-// One CTA per SM-resident block owns two 128-row query tiles of one head and
-// walks the head's keys in blocks of 64, as the reference's tiles do (its
-// 64 x 64 query tiles become 128-row tiles; the per-row arithmetic is the
-// same online softmax).  10 warps:
+// One CTA per SM owns two 128-row query tiles of one head and walks the
+// head's keys in blocks of 64, as the reference's tiles do (its 64 x 64
+// query tiles become 128-row tiles; the per-row arithmetic is the same online
+// softmax).  19 warps:
 //   warp 0      TMA producer: Q tiles once, then K and V blocks into two
-//               rings (3 K stages, 2 V stages), 128-byte swizzle; V is loaded
+//               rings (4 K stages, 3 V stages), 128-byte swizzle; V is loaded
 //               key-major with 32-byte swizzle granules (the MN-major operand
 //               of P.V).
-//   warp 1      TMEM owner and MMA issuer (one thread): S_t = Q_t . K_j^T
-//               (M = 128, N = 64, K = d) into a double-buffered TMEM score
-//               tile per query tile, issued one key block ahead;
-//               O_t,blk = P_t . V_j (M = 128, N = 64, K = 64 keys) into a TMEM
-//               block accumulator per query tile.
-//   warps 2-5   softmax for query tile 0, warps 6-9 for query tile 1; thread
-//               = one query row (TMEM lane).  Per key block: tcgen05.ld the
-//               score row, t = s * scale (masked to -inf past S), in log2
-//               units; m_new = max(m, max t), corr = exp(m - m_new),
-//               p = exp(t - m_new), l = l * corr + sum p (max and sum as
-//               trees); p is written into the P tile in shared memory (the
-//               K-major A operand of P.V, same swizzle as a TMA tile) after
-//               the previous block's O_blk has been folded into registers
-//               (o = o * corr + O_blk), so each P.V runs under the next
-//               block's softmax.  At the end O = o * (1 / l), L = m + log(l).
-// The two query tiles' softmax warps share the SM's exp units and alternate
-// with each other's tensor-core work.  Every mbarrier wait is bounded (a
-// %globaltimer deadline, an abort flag, the device error word), as in the
-// GEMM kernel.
+//   warp 1      TMEM owner; MMA issuer (one thread) of query tile 0, warp 18
+//               the same for tile 1: S_t = Q_t . K_j^T
+//               (M = 128, N = 64, K = d) into one of three TMEM score buffers
+//               per query tile, issued one key block ahead;
+//               O_t += P_t . V_j (M = 128, N = 64, K = 64 keys) into a TMEM
+//               accumulator, with A = P read from tensor memory.
+//   warps 2-9   softmax for query tile 0, warps 10-17 for query tile 1: two
+//               warps per TMEM lane quarter, thread = (query row, half of the
+//               keys).  Per key block: tcgen05.ld the half row of scores,
+//               t = s * scale (masked to -inf past S) in log2 units; the two
+//               halves exchange their maxima (shared memory, 64-thread named
+//               barrier); p = exp(t - m), l = l * corr + sum p (partial per
+//               half); p is stored over the scores in TMEM (tcgen05.st), where
+//               P.V reads it, and P.V accumulates O in TMEM: no shared-memory
+//               round trip for P and no per-block wait on P.V.  The running
+//               maximum m moves only when a block's maximum exceeds it by more
+//               than a factor 2^8 (conditional rescaling, as FlashAttention-4
+//               does); then O and l are rescaled by exp(m_old - m_new) in
+//               place.  At the end O = o * (1 / l), L = m + log(l).
+// The score / probability buffers are reused three blocks later, after the
+// MMA thread's commit for the P.V that read them.  Every mbarrier wait is
+// bounded (a %globaltimer deadline, an abort flag, the device error word),
+// as in the GEMM kernel, and the named-barrier syncs are taken the same
+// number of times by both warps of a pair on every path.
 #include <algorithm>
 #include <cstring>
 
@@ -43,19 +48,30 @@ constexpr int FQ = 128;      // query rows per tile (TMEM lanes)
 constexpr int FK = 64;       // keys per block
 constexpr int FD = 64;       // head dim of the tiles (d <= 64, zero-filled)
 constexpr int NQ = 2;        // query tiles per CTA
-constexpr int KST = 3;       // K ring stages
-constexpr int VST = 2;       // V ring stages
+constexpr int KST = 4;       // K ring stages
+constexpr int VST = 3;       // V ring stages
+constexpr int SPB = 3;       // score / probability buffers per query tile in TMEM
 constexpr int Q_BYTES = FQ * FD * 4;   // 2 boxes [128 rows x 32 dims] of 16 KB
 constexpr int K_BYTES = FK * FD * 4;   // 2 boxes [64 keys x 32 dims] of 8 KB
 constexpr int V_BYTES = FK * FD * 4;   // 2 chunks [64 keys x 32 dims] of 8 KB (MN-major)
-constexpr int P_BYTES = FQ * FK * 4;   // 2 blocks [128 rows x 32 keys] of 16 KB
 constexpr int OFF_K = NQ * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
-constexpr int OFF_P = OFF_V + VST * V_BYTES;
-constexpr int OFF_BAR = OFF_P + NQ * P_BYTES;
-constexpr int SMEM = OFF_BAR + 256 + 1024;  // barriers + 1 KB alignment slack
-constexpr int THREADS = 64 + NQ * 128;
-constexpr int TMEM_COLS = 512;  // S[t][2] at t*128 + b*64, O_blk[t] at 256 + t*64
+constexpr int OFF_X = OFF_V + VST * V_BYTES;  // row-max exchange: [2 parities][NQ][2 halves][128]
+constexpr int X_BYTES = 2 * NQ * 2 * FQ * 4;
+constexpr int OFF_BAR = OFF_X + X_BYTES;
+constexpr int BAR_BYTES = 8 * (1 + 2 * KST + 2 * VST + 2 * SPB * NQ + 3 * NQ) + 8;  // + TMEM slot, abort flag
+constexpr int SMEM = OFF_BAR + 512 + 1024;  // barriers + 1 KB alignment slack
+static_assert(BAR_BYTES <= 512, "barrier area");
+constexpr int SM_WARPS = 8;                 // softmax warps per query tile: 2 per TMEM lane quarter
+constexpr int MMA2_WARP = 2 + NQ * SM_WARPS;  // the MMA warp of query tile 1 (tile 0: warp 1)
+constexpr int THREADS = 32 * (MMA2_WARP + 1);
+// TMEM: tile t owns columns t*256 ..: S/P buffer b at t*256 + b*64, O at t*256 + 192
+constexpr int TMEM_COLS = 512;
+constexpr int TILE_COLS = 256, O_COL = SPB * FK;
+// The running row maximum (log2 units) moves only when a block's maximum
+// exceeds it by more than this; probabilities stay <= 2^8 in between.
+constexpr float kRescaleLog2 = 8.0f;
+constexpr uint32_t kSleepNs = 100000;  // a waiting thread sleeps up to 100 us per poll
 static_assert(SMEM <= 232448, "shared memory per CTA");
 
 struct FtParams {
@@ -79,7 +95,7 @@ __device__ __forceinline__ void fence_async_smem() {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           const FtParams& p, int site) {
     bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = wait_bounded(bar, parity, abort_flag, p.timeout_ns, p.err, site);
+    if ((threadIdx.x & 31) == 0) ok = wait_bounded(bar, parity, abort_flag, p.timeout_ns, p.err, site, kSleepNs);
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
@@ -92,13 +108,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     uint64_t* k_empty = k_full + KST;         // [KST]
     uint64_t* v_full = k_empty + KST;         // [VST]
     uint64_t* v_empty = v_full + VST;         // [VST]
-    uint64_t* s_full = v_empty + VST;         // [NQ][2]
-    uint64_t* s_empty = s_full + 2 * NQ;      // [NQ][2]
-    uint64_t* p_full = s_empty + 2 * NQ;      // [NQ]
+    uint64_t* s_full = v_empty + VST;         // [NQ][SPB]
+    uint64_t* s_empty = s_full + SPB * NQ;    // [NQ][SPB]
+    uint64_t* p_full = s_empty + SPB * NQ;    // [NQ]
     uint64_t* o_full = p_full + NQ;           // [NQ]
-    uint64_t* o_empty = o_full + NQ;          // [NQ]
-    uint64_t* drain = o_empty + NQ;           // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* drain = o_full + NQ;            // [NQ]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + NQ);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,22 +124,21 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         mbar_init(q_full, 1);
         for (int s = 0; s < KST; ++s) {
             mbar_init(&k_full[s], 1);
-            mbar_init(&k_empty[s], 1);
+            mbar_init(&k_empty[s], NQ);  // a commit from each tile's MMA thread
         }
         for (int s = 0; s < VST; ++s) {
             mbar_init(&v_full[s], 1);
-            mbar_init(&v_empty[s], 1);
+            mbar_init(&v_empty[s], NQ);
         }
         for (int t = 0; t < NQ; ++t) {
-            for (int b = 0; b < 2; ++b) {
-                mbar_init(&s_full[2 * t + b], 1);
-                mbar_init(&s_empty[2 * t + b], 4);  // one arrival per softmax warp
+            for (int b = 0; b < SPB; ++b) {
+                mbar_init(&s_full[SPB * t + b], 1);
+                mbar_init(&s_empty[SPB * t + b], 1);  // committed after the P.V that read it
             }
-            mbar_init(&p_full[t], 4);
+            mbar_init(&p_full[t], SM_WARPS);
             mbar_init(&o_full[t], 1);
-            mbar_init(&o_empty[t], 4);
         }
-        mbar_init(drain, 1);
+        for (int t = 0; t < NQ; ++t) mbar_init(&drain[t], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
@@ -157,7 +171,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             for (int j = 0; ok && j < p.nk; ++j) {
                 const int ks = j % KST, vs = j % VST;
                 const uint32_t kph = (uint32_t)(j / KST) & 1u, vph = (uint32_t)(j / VST) & 1u;
-                if (!wait_bounded(&k_empty[ks], kph ^ 1u, abort_flag, p.timeout_ns, p.err, 21)) {
+                if (!wait_bounded(&k_empty[ks], kph ^ 1u, abort_flag, p.timeout_ns, p.err, 21, kSleepNs)) {
                     ok = false;
                     break;
                 }
@@ -168,7 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                                    smem_u32(&k_full[ks]), 32 * c, j * FK, head, 0, 0);
                 pend_k |= 1u << ks;
                 par_k = (par_k & ~(1u << ks)) | (kph << ks);
-                if (!wait_bounded(&v_empty[vs], vph ^ 1u, abort_flag, p.timeout_ns, p.err, 22)) {
+                if (!wait_bounded(&v_empty[vs], vph ^ 1u, abort_flag, p.timeout_ns, p.err, 22, kSleepNs)) {
                     ok = false;
                     break;
                 }
@@ -201,28 +215,33 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                     }
             }
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == 1 || warp == MMA2_WARP) {
+        // ---------------- MMA issuers: one thread per query tile ----------------
+        // Each tile's chain (S, softmax, P, P.V) runs at its own pace;
+        // the tiles share only the K and V rings, whose empty barriers take a
+        // commit from both.
+        const int mt = warp == 1 ? 0 : 1;
         if (lane == 0) {
             // kind::tf32, fp32 D; N = 64 (bits 17-22, >> 3), M = 128 (bits 24-28, >> 4);
-            // S: A (Q) and B (K) K-major; P.V: A (P) K-major, B (V) MN-major (bit 16).
+            // S: A (Q) and B (K) K-major; P.V: A (P, in TMEM) K-major, B (V) MN-major (bit 16).
             const uint32_t idesc_s = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(FK >> 3) << 17) |
                                      ((uint32_t)(FQ >> 4) << 24);
             const uint32_t idesc_pv = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) |
                                       ((uint32_t)(FD >> 3) << 17) | ((uint32_t)(FQ >> 4) << 24);
             const uint32_t sq = smem_u32(smem), sk = smem_u32(smem + OFF_K),
-                           sv = smem_u32(smem + OFF_V), sp = smem_u32(smem + OFF_P);
-            bool ok = wait_bounded(q_full, 0, abort_flag, p.timeout_ns, p.err, 23);
+                           sv = smem_u32(smem + OFF_V);
+            bool ok = wait_bounded(q_full, 0, abort_flag, p.timeout_ns, p.err, 23, kSleepNs);
             bool issued = false;
             tc_fence_after();
-            // S_t(j) = Q_t . K_j^T into S buffer (t, j & 1): 8 MMAs of K = 8 over d = 64
+            // S_t(j) = Q_t . K_j^T into buffer (t, j % SPB): 8 MMAs of K = 8 over d = 64,
+            // once the P.V that last read that buffer is done
             auto issue_s = [&](int t, int j) -> bool {
-                const int b = j & 1;
-                if (!wait_bounded(&s_empty[2 * t + b], ((uint32_t)(j >> 1) & 1u) ^ 1u, abort_flag,
-                                  p.timeout_ns, p.err, 24))
+                const int b = j % SPB;
+                if (!wait_bounded(&s_empty[SPB * t + b], ((uint32_t)(j / SPB) & 1u) ^ 1u, abort_flag,
+                                  p.timeout_ns, p.err, 24, kSleepNs))
                     return false;
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(t * 128 + b * 64);
+                const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
                 const uint32_t qa = sq + t * Q_BYTES, ka = sk + (j % KST) * K_BYTES;
 #pragma unroll
                 for (int s = 0; s < FD / 8; ++s) {
@@ -230,179 +249,218 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                     const uint64_t bd = smem_desc(ka + (s >> 2) * (K_BYTES / 2) + (s & 3) * 32, 16, 1024, kSw128);
                     umma_tf32<1>(d, ad, bd, idesc_s, s > 0 ? 1u : 0u);
                 }
-                umma_commit<1>(smem_u32(&s_full[2 * t + b]));
+                umma_commit<1>(smem_u32(&s_full[SPB * t + b]));
                 issued = true;
                 return true;
             };
-            // O_blk_t = P_t . V_j: 8 MMAs of K = 8 over the 64 keys
+            // O_t += P_t . V_j: A = the probabilities the softmax wrote over the
+            // scores in TMEM, B = V from shared memory; 8 MMAs of K = 8 keys
+            // (the first block's first MMA starts O from zero)
             auto issue_pv = [&](int t, int j) -> bool {
-                if (!wait_bounded(&p_full[t], (uint32_t)j & 1u, abort_flag, p.timeout_ns, p.err, 25))
-                    return false;
-                if (!wait_bounded(&o_empty[t], ((uint32_t)j & 1u) ^ 1u, abort_flag, p.timeout_ns, p.err, 26))
+                if (!wait_bounded(&p_full[t], (uint32_t)j & 1u, abort_flag, p.timeout_ns, p.err, 25, kSleepNs))
                     return false;
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(256 + t * 64);
-                const uint32_t pa = sp + t * P_BYTES, va = sv + (j % VST) * V_BYTES;
+                const int b = j % SPB;
+                const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + O_COL);
+                const uint32_t pa = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
+                const uint32_t va = sv + (j % VST) * V_BYTES;
 #pragma unroll
                 for (int s = 0; s < FK / 8; ++s) {
-                    const uint64_t ad = smem_desc(pa + (s >> 2) * (P_BYTES / 2) + (s & 3) * 32, 16, 1024, kSw128);
                     const uint64_t bd = smem_desc(va + s * 1024, V_BYTES / 2, 512, kSw128Atom32);
-                    umma_tf32<1>(d, ad, bd, idesc_pv, s > 0 ? 1u : 0u);
+                    umma_tf32_tmem_a(d, pa + 8 * s, bd, idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
                 }
                 umma_commit<1>(smem_u32(&o_full[t]));
+                umma_commit<1>(smem_u32(&s_empty[SPB * t + b]));
                 issued = true;
                 return true;
             };
-            if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27);
+            if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27, kSleepNs);
             if (ok) tc_fence_after();
-            for (int t = 0; ok && t < NQ; ++t) ok = issue_s(t, 0);
+            if (ok) ok = issue_s(mt, 0);
             if (ok) umma_commit<1>(smem_u32(&k_empty[0]));
             for (int j = 0; ok && j < p.nk; ++j) {
-                const bool more = j + 1 < p.nk;
-                if (more) {
+                if (j + 1 < p.nk) {  // the next block's scores, one block ahead
                     const int ks = (j + 1) % KST;
                     ok = wait_bounded(&k_full[ks], (uint32_t)((j + 1) / KST) & 1u, abort_flag,
-                                      p.timeout_ns, p.err, 28);
-                    if (ok) ok = issue_s(0, j + 1);
+                                      p.timeout_ns, p.err, 28, kSleepNs);
+                    if (ok) ok = issue_s(mt, j + 1);
+                    if (ok) umma_commit<1>(smem_u32(&k_empty[ks]));
                 }
                 if (ok) ok = wait_bounded(&v_full[j % VST], (uint32_t)(j / VST) & 1u, abort_flag,
-                                          p.timeout_ns, p.err, 29);
-                if (ok) ok = issue_pv(0, j);
-                if (ok && more) {
-                    ok = issue_s(1, j + 1);
-                    if (ok) umma_commit<1>(smem_u32(&k_empty[(j + 1) % KST]));
-                }
-                if (ok) ok = issue_pv(1, j);
+                                          p.timeout_ns, p.err, 29, kSleepNs);
+                if (ok) ok = issue_pv(mt, j);
                 if (ok) umma_commit<1>(smem_u32(&v_empty[j % VST]));
             }
             if (!ok && issued) {
-                umma_commit<1>(smem_u32(drain));
+                umma_commit<1>(smem_u32(&drain[mt]));
                 const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < p.timeout_ns) {
+                while (!mbar_try_wait(&drain[mt], 0) && globaltimer() - t0 < p.timeout_ns) {
                 }
             }
         }
     } else {
-        // ---------------- softmax (warps 2-5: tile 0, 6-9: tile 1) ----------------
-        // Scores are kept in log2 units (u = s * scale * log2 e, so exp(t - m) =
-        // exp2(u - m2)).  O_blk of block j is folded into o while block j + 1's
-        // probabilities are computed, so P.V(j) runs under softmax(j + 1).
-        const int t = (warp - 2) >> 2;
-        const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
+        // ---------------- softmax (warps 2-9: tile 0, 10-17: tile 1) ----------------
+        // Two warps per TMEM lane quarter: thread (row r, half h) owns keys
+        // 32h .. 32h + 31 of each score block and O columns 32h .. 32h + 31.
+        // The halves of a row exchange their block maxima through shared
+        // memory (a 64-thread named barrier per lane quarter); each keeps its
+        // own partial row sum, added at the end.  Scores are kept in log2
+        // units (u = s * scale * log2 e, so exp(t - m) = 2^(u - m2)).
+        // O accumulates in TMEM across blocks.  The reference maximum m2
+        // moves only when a block's maximum exceeds it by more than
+        // kRescaleLog2; then (rarely, after the first blocks) this thread
+        // waits for the previous P.V and rescales its O columns and l by
+        // 2^(m2_old - m2_new) in place.  The sums are the reference's up to
+        // that common factor, which the final O / l and L = m + log(l) cancel.
+        const int wt = warp - 2;
+        const int t = wt / SM_WARPS;
+        const int h = (wt % SM_WARPS) >> 2;  // key / column half
+        const int quarter = warp & 3;        // the TMEM lane quarter this warp may access
         const int r = quarter * 32 + lane;
         const int row = q0 + t * FQ + r;
         const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-        uint8_t* prow = smem + OFF_P + t * P_BYTES + r * 128;
-        const int sw = r & 7;
-        const float sl2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
-        float o[FD];
-#pragma unroll
-        for (int c = 0; c < FD; ++c) o[c] = 0.0f;
-        float m2 = -INFINITY, l = 0.0f, corr_prev = 0.0f;
+        const uint32_t o_addr = lane_base + (uint32_t)(t * TILE_COLS + O_COL + 32 * h);
+        float* xchg = reinterpret_cast<float*>(smem + OFF_X);  // [par][t][h][row]
+        const int bar_id = 1 + t * 4 + quarter;              // named barrier of the two halves
+        const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
+        const bool fast = sl2 > 0.0f;  // max(s) * sl2 == max(s * sl2): one FFMA per probability
+        float m2 = -INFINITY, l = 0.0f;
         bool ok = true;
-        // o = o * corr + O_blk of the block whose P.V completes with parity `par`
-        auto fold_block = [&](uint32_t par, bool release) -> bool {
-            if (!warp_wait(&o_full[t], par, abort_flag, p, 31)) return false;
-            tc_fence_after();
-#pragma unroll
-            for (int h = 0; h < FD / 16; ++h) {
-                uint32_t ob[16];
-                tmem_ld16(lane_base + (uint32_t)(256 + t * 64 + 16 * h), ob);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    o[16 * h + c] = fmaf(o[16 * h + c], corr_prev, __uint_as_float(ob[c]));
-            }
-            if (release) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&o_empty[t]);
-            }
-            return true;
+        auto ex2 = [](float x) {
+            float y;
+            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+            return y;
         };
+        // Both warps of a row pair execute the same number of named-barrier
+        // syncs whatever happens (a bar.sync has no time limit): after a
+        // failed wait a warp stops waiting and computing but still takes
+        // every sync, and each of its waits is bounded.
         for (int j = 0; j < p.nk; ++j) {
-            const int b = j & 1;
-            ok = warp_wait(&s_full[2 * t + b], (uint32_t)(j >> 1) & 1u, abort_flag, p, 30);
-            if (!ok) break;
-            tc_fence_after();
-            float u[FK];
-            {
-                uint32_t s0[32], s1[32];
-                tmem_ld32(lane_base + (uint32_t)(t * 128 + b * 64), s0);
-                tmem_ld32(lane_base + (uint32_t)(t * 128 + b * 64 + 32), s1);
+            const int b = j % SPB;
+            const uint32_t sp_addr = lane_base + (uint32_t)(t * TILE_COLS + b * FK + 32 * h);
+            if (ok) ok = warp_wait(&s_full[SPB * t + b], (uint32_t)(j / SPB) & 1u, abort_flag, p, 30);
+            float u[32];
+            if (ok) {
+                tc_fence_after();
+                uint32_t sv[32];
+                tmem_ld32(sp_addr, sv);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    u[c] = __fmul_rn(__uint_as_float(s0[c]), sl2);
-                    u[32 + c] = __fmul_rn(__uint_as_float(s1[c]), sl2);
-                }
+                for (int c = 0; c < 32; ++c) u[c] = __uint_as_float(sv[c]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) u[c] = 0.0f;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[2 * t + b]);
-            const int valid = p.S - j * FK;
-            if (valid < FK) {  // the tail block: keys past S take no weight
+            const int valid = p.S - j * FK - 32 * h;  // keys of this half inside S
+            const bool plain = fast && valid >= 32;
+            if (!plain) {
+                // general form: u = s * sl2, keys past S at -inf
 #pragma unroll
-                for (int c = 0; c < FK; ++c)
-                    if (c >= valid) u[c] = -INFINITY;
+                for (int c = 0; c < 32; ++c) u[c] = c < valid ? __fmul_rn(u[c], sl2) : -INFINITY;
             }
-            // row max and sum as trees (max is exact in any order)
-            float mx[16];
+            float mx[8];
 #pragma unroll
-            for (int c = 0; c < 16; ++c) mx[c] = fmaxf(fmaxf(u[c], u[c + 16]), fmaxf(u[c + 32], u[c + 48]));
+            for (int c = 0; c < 8; ++c) mx[c] = fmaxf(fmaxf(u[c], u[c + 8]), fmaxf(u[c + 16], u[c + 24]));
 #pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
+            for (int w = 4; w > 0; w >>= 1)
 #pragma unroll
                 for (int c = 0; c < w; ++c) mx[c] = fmaxf(mx[c], mx[c + w]);
-            const float m_new = fmaxf(m2, mx[0]);
-            const float corr = exp2f(__fsub_rn(m2, m_new));
+            const float mine = plain ? __fmul_rn(mx[0], sl2) : mx[0];
+            // exchange buffers alternate by block parity: a half can write block
+            // j + 1's maximum while the other still reads block j's
+            float* xb = xchg + (((j & 1) * NQ + t) * 2) * FQ;
+            xb[h * FQ + r] = mine;
+            asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+            const float m_blk = fmaxf(mine, xb[(h ^ 1) * FQ + r]);
+            // both halves of the row take the same decision from the same values
+            const bool move = m_blk > m2 + kRescaleLog2;
+            const float m_new = move ? m_blk : m2;
+            const float corr = move ? ex2(m2 - m_new) : 1.0f;
+            if (plain) {
 #pragma unroll
-            for (int c = 0; c < FK; ++c) u[c] = exp2f(__fsub_rn(u[c], m_new));
-            float sm[16];
+                for (int c = 0; c < 32; ++c) u[c] = ex2(fmaf(u[c], sl2, -m_new));
+            } else {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) sm[c] = (u[c] + u[c + 16]) + (u[c + 32] + u[c + 48]);
+                for (int c = 0; c < 32; ++c) u[c] = ex2(u[c] - m_new);
+            }
+            float sm[8];
 #pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
+            for (int c = 0; c < 8; ++c) sm[c] = (u[c] + u[c + 8]) + (u[c + 16] + u[c + 24]);
+#pragma unroll
+            for (int w = 4; w > 0; w >>= 1)
 #pragma unroll
                 for (int c = 0; c < w; ++c) sm[c] += sm[c + w];
-            // fold the previous block (its P.V ran during this block's softmax);
-            // that also frees the P tile for this block's probabilities
-            if (j > 0) {
-                ok = fold_block((uint32_t)(j - 1) & 1u, true);
-                if (!ok) break;
-            }
             l = fmaf(l, corr, sm[0]);
             m2 = m_new;
-            corr_prev = corr;
-            // P row into the swizzled K-major tile: keys c..c+3 are 16-byte granule
-            // (c % 32) / 4 of the row's 128-byte line in block c / 32
+            // rescale O in TMEM where the maximum moved (not before the first
+            // P.V, which starts O from zero): after the previous P.V is done,
+            // before this block's P.V is issued (that waits for p_full)
+            if (ok && j > 0 && __any_sync(0xffffffffu, move)) {
+                ok = warp_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p, 31);
+                if (ok) {
+                    tc_fence_after();
+                    uint32_t ov[32];
+                    tmem_ld32(o_addr, ov);
+                    tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < FK; c += 4) {
-                uint8_t* dst = prow + (c >> 5) * (P_BYTES / 2) + ((((c & 31) >> 2) ^ sw) << 4);
-                *reinterpret_cast<float4*>(dst) = make_float4(u[c], u[c + 1], u[c + 2], u[c + 3]);
+                    for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__fmul_rn(__uint_as_float(ov[c]), corr));
+                    tmem_st32(o_addr, ov);
+                }
             }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[t]);
+            if (ok) {
+                // the probabilities over this half's scores, in place in TMEM: the
+                // A operand (lane = row, column = key) of P.V
+                uint32_t pv[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) pv[c] = __float_as_uint(u[c]);
+                tmem_st32(sp_addr, pv);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[t]);
+            }
         }
-        if (ok) ok = fold_block((uint32_t)(p.nk - 1) & 1u, false);
+        // O after the last P.V.  A parity wait tells apart only the current and
+        // the previous phase: block nk - 1's scores being done implies P.V of
+        // block nk - 3 is, so wait for nk - 2's phase, then for nk - 1's.  (In
+        // the loop, the rescale's wait for block j - 1 comes after block j's
+        // scores, which imply P.V of block j - 2, for the same reason.)
+        float o[32];
+        if (ok && p.nk >= 2) ok = warp_wait(&o_full[t], (uint32_t)(p.nk - 2) & 1u, abort_flag, p, 32);
+        if (ok) ok = warp_wait(&o_full[t], (uint32_t)(p.nk - 1) & 1u, abort_flag, p, 33);
+        if (ok) {
+            tc_fence_after();
+            uint32_t ov[32];
+            tmem_ld32(o_addr, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __uint_as_float(ov[c]);
+        }
+        // the row sum: this half's partial plus the other's
+        float* xl = xchg + (t * 2) * FQ;  // parity-0 buffer; every max read is done
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+        xl[h * FQ + r] = l;
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+        const float lsum = l + xl[(h ^ 1) * FQ + r];
         if (ok && row < p.S) {
-            const float inv = __fdiv_rn(1.0f, l);
-            float* orow = p.O + ((int64_t)head * p.S + row) * p.d;
+            const float inv = __fdiv_rn(1.0f, lsum);
+            float* orow = p.O + ((int64_t)head * p.S + row) * p.d + 32 * h;
+            const int dc = p.d - 32 * h;  // this half's columns inside d
             if (p.vec_o) {
 #pragma unroll
-                for (int c = 0; c < FD; c += 4)
-                    if (c < p.d)
+                for (int c = 0; c < 32; c += 4)
+                    if (c < dc)
                         *reinterpret_cast<float4*>(orow + c) =
                             make_float4(__fmul_rn(o[c], inv), __fmul_rn(o[c + 1], inv),
                                         __fmul_rn(o[c + 2], inv), __fmul_rn(o[c + 3], inv));
             } else {
 #pragma unroll
-                for (int c = 0; c < FD; ++c)
-                    if (c < p.d) orow[c] = __fmul_rn(o[c], inv);
+                for (int c = 0; c < 32; ++c)
+                    if (c < dc) orow[c] = __fmul_rn(o[c], inv);
             }
             // L = m + log(l) with m = m2 * ln 2 back in the scores' units
-            if (p.L) p.L[(int64_t)head * p.S + row] = __fadd_rn(__fmul_rn(m2, 0.6931471805599453f), logf(l));
+            if (p.L && h == 0)
+                p.L[(int64_t)head * p.S + row] = __fadd_rn(__fmul_rn(m2, 0.6931471805599453f), logf(lsum));
         }
     }
 

@@ -28,17 +28,35 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
                  : "memory");
 }
 
+// mbarrier.try_wait with a suspend-time hint: a thread whose phase is not yet
+// complete sleeps in hardware until it completes or `ns` pass, instead of
+// returning at once (a spinning waiter takes issue slots from the warps
+// sharing its scheduler).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase of `bar` with the given parity.  Gives up (returns
 // false) when the CTA's abort flag is raised or the deadline passes; in the
 // latter case it raises the flag and records `site` in the device error word.
+// sleep_ns > 0: each poll may sleep that long (see mbar_try_wait_sleep).
 __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
                                              volatile int* abort_flag, uint64_t timeout_ns,
-                                             int* err, int site) {
+                                             int* err, int site, uint32_t sleep_ns = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 15) == 0) {
+        if (sleep_ns ? mbar_try_wait_sleep(bar, parity, sleep_ns) : mbar_try_wait(bar, parity))
+            return true;
+        if (sleep_ns || (i & 15) == 0) {
             if (*abort_flag) return false;
             if (globaltimer() - t0 > timeout_ns) {
                 *abort_flag = 1;
@@ -132,6 +150,16 @@ __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint6
             "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
     }
 }
+// The same with A read from tensor memory (lane = row, one 32-bit column per
+// k element) instead of a shared-memory descriptor; single CTA.
+__device__ __forceinline__ void umma_tf32_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 // Arrive on the barrier at cluster address `bar` once every MMA this thread
 // issued so far has completed.
 template <int CG>
@@ -180,6 +208,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Store 32 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+        "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+        "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+        "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 }  // namespace tlc
