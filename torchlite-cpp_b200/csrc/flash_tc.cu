@@ -71,7 +71,9 @@ constexpr int TILE_COLS = 256, O_COL = SPB * FK;
 // The running row maximum (log2 units) moves only when a block's maximum
 // exceeds it by more than this; probabilities stay <= 2^8 in between.
 constexpr float kRescaleLog2 = 8.0f;
-constexpr uint32_t kSleepNs = 100000;  // a waiting thread sleeps up to 100 us per poll
+// How long a waiting thread may sleep per poll (it wakes when the phase
+// completes): producer, MMA issuers, softmax warps.
+constexpr uint32_t kSleepNs = 100000, kSleepMma = 100000, kSleepSm = 100000;
 static_assert(SMEM <= 232448, "shared memory per CTA");
 
 struct FtParams {
@@ -95,7 +97,7 @@ __device__ __forceinline__ void fence_async_smem() {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           const FtParams& p, int site) {
     bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = wait_bounded(bar, parity, abort_flag, p.timeout_ns, p.err, site, kSleepNs);
+    if ((threadIdx.x & 31) == 0) ok = wait_bounded(bar, parity, abort_flag, p.timeout_ns, p.err, site, kSleepSm);
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
@@ -228,9 +230,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                                      ((uint32_t)(FQ >> 4) << 24);
             const uint32_t idesc_pv = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) |
                                       ((uint32_t)(FD >> 3) << 17) | ((uint32_t)(FQ >> 4) << 24);
-            const uint32_t sq = smem_u32(smem), sk = smem_u32(smem + OFF_K),
-                           sv = smem_u32(smem + OFF_V);
-            bool ok = wait_bounded(q_full, 0, abort_flag, p.timeout_ns, p.err, 23, kSleepNs);
+            // descriptors of Q tile 0, K stage 0, V stage 0; any other tile, stage
+            // or k-step only moves the start-address field (address >> 4)
+            const uint64_t q_desc = smem_desc(smem_u32(smem), 16, 1024, kSw128);
+            const uint64_t k_desc = smem_desc(smem_u32(smem + OFF_K), 16, 1024, kSw128);
+            const uint64_t v_desc = smem_desc(smem_u32(smem + OFF_V), V_BYTES / 2, 512, kSw128Atom32);
+            bool ok = wait_bounded(q_full, 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
             bool issued = false;
             tc_fence_after();
             // S_t(j) = Q_t . K_j^T into buffer (t, j % SPB): 8 MMAs of K = 8 over d = 64,
@@ -238,17 +243,17 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             auto issue_s = [&](int t, int j) -> bool {
                 const int b = j % SPB;
                 if (!wait_bounded(&s_empty[SPB * t + b], ((uint32_t)(j / SPB) & 1u) ^ 1u, abort_flag,
-                                  p.timeout_ns, p.err, 24, kSleepNs))
+                                  p.timeout_ns, p.err, 24, kSleepMma))
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
-                const uint32_t qa = sq + t * Q_BYTES, ka = sk + (j % KST) * K_BYTES;
+                const uint64_t qd = q_desc + (uint32_t)((t * Q_BYTES) >> 4);
+                const uint64_t kd = k_desc + (uint32_t)(((j % KST) * K_BYTES) >> 4);
 #pragma unroll
-                for (int s = 0; s < FD / 8; ++s) {
-                    const uint64_t ad = smem_desc(qa + (s >> 2) * (Q_BYTES / 2) + (s & 3) * 32, 16, 1024, kSw128);
-                    const uint64_t bd = smem_desc(ka + (s >> 2) * (K_BYTES / 2) + (s & 3) * 32, 16, 1024, kSw128);
-                    umma_tf32<1>(d, ad, bd, idesc_s, s > 0 ? 1u : 0u);
-                }
+                for (int s = 0; s < FD / 8; ++s)
+                    umma_tf32<1>(d, qd + (uint32_t)(((s >> 2) * (Q_BYTES / 2) + (s & 3) * 32) >> 4),
+                                 kd + (uint32_t)(((s >> 2) * (K_BYTES / 2) + (s & 3) * 32) >> 4), idesc_s,
+                                 s > 0 ? 1u : 0u);
                 umma_commit<1>(smem_u32(&s_full[SPB * t + b]));
                 issued = true;
                 return true;
@@ -257,24 +262,23 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             // scores in TMEM, B = V from shared memory; 8 MMAs of K = 8 keys
             // (the first block's first MMA starts O from zero)
             auto issue_pv = [&](int t, int j) -> bool {
-                if (!wait_bounded(&p_full[t], (uint32_t)j & 1u, abort_flag, p.timeout_ns, p.err, 25, kSleepNs))
+                if (!wait_bounded(&p_full[t], (uint32_t)j & 1u, abort_flag, p.timeout_ns, p.err, 25, kSleepMma))
                     return false;
                 tc_fence_after();
                 const int b = j % SPB;
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + O_COL);
                 const uint32_t pa = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
-                const uint32_t va = sv + (j % VST) * V_BYTES;
+                const uint64_t vd = v_desc + (uint32_t)(((j % VST) * V_BYTES) >> 4);
 #pragma unroll
-                for (int s = 0; s < FK / 8; ++s) {
-                    const uint64_t bd = smem_desc(va + s * 1024, V_BYTES / 2, 512, kSw128Atom32);
-                    umma_tf32_tmem_a(d, pa + 8 * s, bd, idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
-                }
+                for (int s = 0; s < FK / 8; ++s)
+                    umma_tf32_tmem_a(d, pa + 8 * s, vd + (uint32_t)((s * 1024) >> 4), idesc_pv,
+                                     (j > 0 || s > 0) ? 1u : 0u);
                 umma_commit<1>(smem_u32(&o_full[t]));
                 umma_commit<1>(smem_u32(&s_empty[SPB * t + b]));
                 issued = true;
                 return true;
             };
-            if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27, kSleepNs);
+            if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27, kSleepMma);
             if (ok) tc_fence_after();
             if (ok) ok = issue_s(mt, 0);
             if (ok) umma_commit<1>(smem_u32(&k_empty[0]));
@@ -282,12 +286,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 if (j + 1 < p.nk) {  // the next block's scores, one block ahead
                     const int ks = (j + 1) % KST;
                     ok = wait_bounded(&k_full[ks], (uint32_t)((j + 1) / KST) & 1u, abort_flag,
-                                      p.timeout_ns, p.err, 28, kSleepNs);
+                                      p.timeout_ns, p.err, 28, kSleepMma);
                     if (ok) ok = issue_s(mt, j + 1);
                     if (ok) umma_commit<1>(smem_u32(&k_empty[ks]));
                 }
                 if (ok) ok = wait_bounded(&v_full[j % VST], (uint32_t)(j / VST) & 1u, abort_flag,
-                                          p.timeout_ns, p.err, 29, kSleepNs);
+                                          p.timeout_ns, p.err, 29, kSleepMma);
                 if (ok) ok = issue_pv(mt, j);
                 if (ok) umma_commit<1>(smem_u32(&v_empty[j % VST]));
             }
