@@ -199,6 +199,64 @@ def test_device_tf32_forward(heads, S, d):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("heads,S,d", TF32_CASES)
+def test_device_tf32_backward(heads, S, d):
+    """mode tf32: the fused tensor-core backward (prep + dK/dV + dQ kernels,
+    32 <= d <= 64) against the oracle, relative Frobenius error per gradient."""
+    torch = pytest.importorskip("torch")
+    import tlcuda
+    q, k, v, g, sc = case_data(heads, S, d, 26)
+    Q, K, V, G = (torch.from_numpy(a).cuda() for a in (q, k, v, g))
+    o_o, l_o = O.flash_attention(q, k, v, sc)
+    Oo, Lo = torch.from_numpy(o_o).cuda(), torch.from_numpy(l_o).cuda()
+    launches = tlcuda.launch_count()
+    dq, dk, dv = tlcuda.flash_attention_backward(G, Q, K, V, Oo, Lo, sc, mode="tf32")
+    assert tlcuda.lib().tlc_check_device_errors() == 0  # no bounded wait gave up
+    assert tlcuda.launch_count() == launches + 3
+    for name, got, want in zip("QKV", (dq, dk, dv), O.flash_attention_backward(g, q, k, v, o_o, l_o, sc)):
+        got = got.cpu().numpy()
+        if S == 1 and name in "QK":
+            # one key: P = 1 and dP = D, so dS = 0 and dQ = dK = 0 exactly; the
+            # device's dP - D is a TF32 rounding, bounded by |dO| |V| |K or Q| * scale
+            other = k if name == "Q" else q
+            bound = TF32_TOL * float(sc) * np.linalg.norm(g) * np.linalg.norm(v) * np.linalg.norm(other)
+            assert np.linalg.norm(got) <= bound, (name, np.linalg.norm(got), bound)
+            continue
+        e = rel(got, want)
+        assert e <= TF32_TOL, (name, e)
+
+
+@pytest.mark.gpu
+def test_device_tf32_backward_low_scores():
+    """Rows whose scores all lie far below zero (L << 0): keys past S must not
+    turn exp(-L) into inf * 0 in the dQ kernel."""
+    torch = pytest.importorskip("torch")
+    import tlcuda
+    S, d = 100, 64
+    rng = np.random.default_rng(27)
+    q = inputs.normal(rng, (S, d))
+    k = -np.abs(q[:, :1]) * 0 + inputs.normal(rng, (S, d))
+    v, g = inputs.normal(rng, (S, d)), inputs.normal(rng, (S, d))
+    q = q * 0 + 1.0  # every query the same, keys shifted so all scores are << 0
+    k = (k - 30.0).astype(np.float32)
+    q = q.astype(np.float32)
+    sc = np.float32(0.125)
+    o_o, l_o = O.flash_attention(q, k, v, sc)
+    assert l_o.max() < -50
+    Q, K, V, G, Oo, Lo = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (q, k, v, g, o_o, l_o))
+    dq, dk, dv = tlcuda.flash_attention_backward(G, Q, K, V, Oo, Lo, sc, mode="tf32")
+    assert tlcuda.lib().tlc_check_device_errors() == 0
+    # Scores near -240: TF32's relative rounding (~5e-4) of each score is an
+    # absolute error of ~0.1 in the exponent, ~10 % in P, for any TF32 path.
+    # What this case checks is that the result stays finite (without the
+    # masking, padded keys give 0 * inf = NaN); the bound only catches garbage.
+    for name, got, want in zip("QKV", (dq, dk, dv), O.flash_attention_backward(g, q, k, v, o_o, l_o, sc)):
+        got = got.cpu().numpy()
+        assert np.isfinite(got).all(), name
+        assert rel(got, want) <= 0.5, (name, rel(got, want))
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("mode,tol", [("exact", 1e-5), ("3xtf32", 1e-5), ("tf32", 1e-2)])
 def test_device_large_against_fp64(mode, tol):
     """A multi-head case too large for the oracle: 8 heads of S = 2048, d = 64,

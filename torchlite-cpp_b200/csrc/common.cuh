@@ -135,6 +135,11 @@ int launch_softmax(const float* x, float* y, int64_t rows, int64_t D, cudaStream
 bool flash_tc_supported(int d, const float* q, const float* k, const float* v);
 int flash_forward_tc(const float* q, const float* k, const float* v, float* o, float* lse,
                      int64_t heads, int S, int d, float scale, cudaStream_t s);
+// Attention backward on the tensor cores (flash_bwd_tc.cu); ptrs: every operand.
+bool flash_bwd_tc_supported(int d, const float* const* ptrs, int n);
+int flash_backward_tc(const float* dout, const float* q, const float* k, const float* v,
+                      const float* o, const float* lse, float* dq, float* dk, float* dv,
+                      int64_t heads, int S, int d, float scale, cudaStream_t s);
 int launch_softmax_backward(const float* g, const float* y, float* dx, int64_t rows, int64_t D,
                             cudaStream_t st);
 

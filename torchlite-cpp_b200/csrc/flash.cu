@@ -14,8 +14,9 @@
 // 4 x (DM/16) block of O in registers; row max and row sum are shuffles
 // among the 16 threads that share a row.
 //
-// Backward: the reference's recompute scheme as batched GEMMs on the device
-// (mode as for tl::matmul), per chunk of heads: D = rowsum(dO * O);
+// Backward, TLC_MODE_TF32 with 32 <= d <= 64: the fused tensor-core kernels of
+// flash_bwd_tc.cu.  Otherwise the reference's recompute scheme as batched
+// GEMMs on the device (mode as for tl::matmul), per chunk of heads: D = rowsum(dO * O);
 // T = Q . K^T; P = exp(T * scale - L); dV = P^T . dO; dP = dO . V^T;
 // dS' = scale * (P * (dP - D)); dQ = dS' . K; dK = dS'^T . Q.  The sums over
 // keys (dQ) and queries (dV, dK) run in ascending order as the reference's
@@ -384,6 +385,11 @@ extern "C" int tlc_flash_attention_backward(const tlc_tensor* grad_out, const tl
     const int64_t S = h.S, d = h.d, sd = S * d, ss = S * S;
     if (h.heads * sd == 0) return TLC_OK;  // every gradient is empty
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float* ops[9] = {grad_out->data, q->data, k->data, v->data, out->data, lse->data,
+                           dq->data, dk->data, dv->data};
+    if (m == TLC_MODE_TF32 && flash_bwd_tc_supported(h.d, ops, 9))
+        return flash_backward_tc(grad_out->data, q->data, k->data, v->data, out->data, lse->data, dq->data,
+                                 dk->data, dv->data, h.heads, h.S, h.d, sm_scale, s);
     const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(h.heads, kBwdChunkBytes / (ss * 4)));
     Buf T(s), dP(s), D(s);
     TLC_TRY(scratch_alloc(&T.p, sizeof(float) * (size_t)(chunk * ss), s));

@@ -1,0 +1,673 @@
+// FlashAttentionBackward (src/autograd.cpp:575-669 of torchlite-cpp) on the
+// tensor cores: TLC_MODE_TF32, head dim 32 <= d <= 64 (d % 4 == 0, 16-byte
+// aligned operands), one launch of each kernel below after a small prep.
+//
+// The reference recomputes, per 64 x 64 tile pair, S = Q_i . K_j^T * scale,
+// P = exp(S - L_i), dP = dO_i . V_j^T, dS = P * (dP - D_i) (D = rowsum(dO * O))
+// and accumulates dV_j += P^T . dO_i, dK_j += scale * dS^T . Q_i and
+// dQ_i += scale * dS . K_j.  Here every product is a tcgen05.mma with fp32
+// accumulators in tensor memory; no S x S intermediate leaves the SM.
+//
+//   fa_bwd_prep_kernel   D = rowsum(dO * O) and L2 = L * log2(e) into
+//                        [heads, S_pad] scratch (S_pad = S rounded up to 128),
+//                        zero past S.
+//   flash_bwd_dkdv_kernel  one CTA per (head, 128 keys).  K, V tiles stay in
+//                        shared memory; query blocks of 64 stream through a
+//                        two-stage TMA ring, each as Q and dO twice (K-major
+//                        for S^T = K . Q^T and dP^T = V . dO^T, MN-major for
+//                        dV += P^T . dO and dK += dS^T . Q) with their L2, D.
+//                        Eight elementwise warps (two per TMEM lane quarter,
+//                        thread = key, half the block's queries) turn S^T,
+//                        dP^T into P^T = 2^(S^T * scale * log2 e - L2) and
+//                        dS^T = P^T * (dP^T - D) * scale in place in TMEM,
+//                        where the next two MMAs read them as their A
+//                        operand.  dK, dV accumulate in TMEM over all query
+//                        blocks and are written once.
+//   flash_bwd_dq_kernel  one CTA per (head, 128 queries): the same with the
+//                        roles exchanged, S = Q . K^T and dP = dO . V^T per
+//                        block of 64 keys (K, V K-major and K MN-major in a
+//                        three-stage ring), dS in place in TMEM, dQ += dS . K.
+//
+// Rows past S: TMA fills Q, K, V, dO rows past S with zeros and the padded
+// L2, D are zero there, so every product term that involves such a row is
+// zero, and rows past S are not stored.  The one exception is dS for keys
+// past S in the dQ kernel, set to zero outright: there exp(-L) could overflow
+// (a row whose scores all lie far below zero) and make 0 * inf.
+//
+// Both kernels follow the forward kernel's protocol (flash_tc.cu): per-buffer
+// full / empty mbarriers, every wait bounded (%globaltimer deadline, abort
+// flag, the device error word), MMA completion tracked with tcgen05.commit.
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+namespace tlc {
+namespace {
+
+constexpr int BD = 64;          // head dim of the tiles (d <= 64, zero-filled)
+constexpr int TR = 128;         // rows of a CTA's fixed tile = TMEM lanes = MMA M
+constexpr int TB = 64;          // rows of a streamed block = MMA N / K
+constexpr int EW_WARPS = 8;     // elementwise warps: two per TMEM lane quarter
+constexpr int THREADS = 64 + 32 * EW_WARPS;
+constexpr int TILE128 = TR * BD * 4;  // [128 x 64] K-major: 2 boxes [128 x 32] of 16 KB
+constexpr int TILE64 = TB * BD * 4;   // [64 x 64]: 2 boxes / chunks [64 x 32] of 8 KB
+constexpr uint32_t kSleep = 100000;   // a waiting thread sleeps up to 100 us per poll
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+static_assert(BD == TB, "the block width doubles as the head-dim tile in the descriptors");
+
+// kind::tf32, fp32 D, M = 128, N = 64; A K-major (smem or TMEM), B K-major
+// (bit 16 clear) or MN-major (bit 16 set).
+constexpr uint32_t kIdescKK = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TB >> 3) << 17) |
+                              ((uint32_t)(TR >> 4) << 24);
+constexpr uint32_t kIdescKM = kIdescKK | (1u << 16);
+
+struct BwdParams {
+    CUtensorMap m[6];
+    const float* L2;  // [heads, S_pad]
+    const float* D;   // [heads, S_pad]
+    float* out0;      // dK (dkdv kernel) / dQ (dq kernel)
+    float* out1;      // dV (dkdv kernel)
+    int S, S_pad, d, tiles, nblk;
+    float scale;
+    int* err;
+};
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ bool wait_b(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                       const BwdParams& p, int site) {
+    return wait_bounded(bar, parity, abort_flag, kTimeoutNs, p.err, site, kSleep);
+}
+
+// lane 0 waits, the warp follows
+__device__ __forceinline__ bool warp_wait_b(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                            const BwdParams& p, int site) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = wait_b(bar, parity, abort_flag, p, site);
+    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// Shared-memory descriptor of k-step s (8 columns of 4 bytes) of a K-major
+// tile made of two [rows x 32] SW128 boxes of `box` bytes each.
+__device__ __forceinline__ uint64_t kmajor_step(uint64_t desc0, int box, int s) {
+    return desc0 + (uint32_t)((((s >> 2) * box) + (s & 3) * 32) >> 4);
+}
+// k-step s (8 k-rows) of an MN-major tile: +1 KB per step.
+__device__ __forceinline__ uint64_t mnmajor_step(uint64_t desc0, int s) {
+    return desc0 + (uint32_t)((s * 1024) >> 4);
+}
+
+// Final drain after a failed wait: wait (bounded) for loads still in flight
+// into a full barrier of parity `par`.
+__device__ __forceinline__ void drain_full(uint64_t* bar, uint32_t par) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, par) && globaltimer() - t0 < kTimeoutNs) {
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// dK, dV.  m[0] K (K-major, box 128 rows), m[1] V (K-major, 128), m[2] Q
+// (K-major, 64), m[3] Q (MN-major, 64), m[4] dO (K-major, 64), m[5] dO (MN-major, 64).
+constexpr int QST = 2;  // query-block ring stages
+constexpr int DKV_OFF_K = 0, DKV_OFF_V = TILE128, DKV_OFF_RING = 2 * TILE128;
+// a stage: Qk | Qm | dOk | dOm | L2 (64 floats) | D (64 floats), padded to 1 KB so every
+// stage's swizzled tiles start on a 1 KB boundary
+constexpr int DKV_STAGE = 4 * TILE64 + 1024;
+static_assert(DKV_STAGE % 1024 == 0 && 2 * TB * 4 <= 1024, "stage layout");
+constexpr int DKV_OFF_BAR = DKV_OFF_RING + QST * DKV_STAGE;
+constexpr int DKV_SMEM = DKV_OFF_BAR + 256 + 1024;
+static_assert(DKV_SMEM <= 232448, "shared memory per CTA");
+static_assert(8 * (1 + 2 * QST + 2 * 4 + 2 + 1) + 8 <= 256, "barrier area");
+// TMEM: S^T / P^T buffer b at b * 64, dP^T / dS^T buffer b at 128 + b * 64, dV at 256, dK at 320
+constexpr int TMEM_COLS = 512;
+
+__global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DKV_OFF_BAR);
+    uint64_t* kv_full = bars;              // [1]
+    uint64_t* q_full = kv_full + 1;        // [QST]
+    uint64_t* q_empty = q_full + QST;      // [QST]
+    uint64_t* s_full = q_empty + QST;      // [2]  S^T and dP^T of a block computed
+    uint64_t* s_empty = s_full + 2;        // [2]  dV / dK of that buffer done
+    uint64_t* e_full = s_empty + 2;        // [2]  P^T, dS^T written (per buffer)
+    uint64_t* acc_full = e_full + 2;       // [1]  every dV, dK product done
+    uint64_t* drain = acc_full + 1;        // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = blockIdx.x / p.tiles;
+    const int k0 = (blockIdx.x - head * p.tiles) * TR;
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int s = 0; s < QST; ++s) {
+            mbar_init(&q_full[s], 1);
+            mbar_init(&q_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], 1);
+            mbar_init(&e_full[b], EW_WARPS);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0)
+        for (int i = 0; i < 6; ++i) prefetch_map(&p.m[i]);
+    if (warp == 1) {
+        __syncwarp();
+        tmem_alloc<1>(tmem_slot, TMEM_COLS);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            mbar_expect_tx(kv_full, 2 * TILE128);
+            for (int c = 0; c < 2; ++c) {
+                tma_load_5d<1>(smem + DKV_OFF_K + c * (TILE128 / 2), &p.m[0], smem_u32(kv_full), 32 * c, k0, head, 0, 0);
+                tma_load_5d<1>(smem + DKV_OFF_V + c * (TILE128 / 2), &p.m[1], smem_u32(kv_full), 32 * c, k0, head, 0, 0);
+            }
+            uint32_t pend = 0, par = 0;
+            bool ok = true;
+            for (int i = 0; i < p.nblk; ++i) {
+                const int st = i % QST;
+                const uint32_t ph = (uint32_t)(i / QST) & 1u;
+                if (!wait_b(&q_empty[st], ph ^ 1u, abort_flag, p, 41)) {
+                    ok = false;
+                    break;
+                }
+                pend &= ~(1u << st);
+                uint8_t* sb = smem + DKV_OFF_RING + st * DKV_STAGE;
+                mbar_expect_tx(&q_full[st], 4 * TILE64 + 2 * TB * 4);
+                const uint32_t fb = smem_u32(&q_full[st]);
+                for (int c = 0; c < 2; ++c) {
+                    tma_load_5d<1>(sb + c * (TILE64 / 2), &p.m[2], fb, 32 * c, i * TB, head, 0, 0);
+                    tma_load_5d<1>(sb + TILE64 + c * (TILE64 / 2), &p.m[3], fb, 32 * c, i * TB, head, 0, 0);
+                    tma_load_5d<1>(sb + 2 * TILE64 + c * (TILE64 / 2), &p.m[4], fb, 32 * c, i * TB, head, 0, 0);
+                    tma_load_5d<1>(sb + 3 * TILE64 + c * (TILE64 / 2), &p.m[5], fb, 32 * c, i * TB, head, 0, 0);
+                }
+                const int64_t lo = (int64_t)head * p.S_pad + (int64_t)i * TB;
+                bulk_load(sb + 4 * TILE64, p.L2 + lo, TB * 4, &q_full[st]);
+                bulk_load(sb + 4 * TILE64 + TB * 4, p.D + lo, TB * 4, &q_full[st]);
+                pend |= 1u << st;
+                par = (par & ~(1u << st)) | (ph << st);
+            }
+            if (!ok) {
+                drain_full(kv_full, 0);
+                for (int s = 0; s < QST; ++s)
+                    if (pend & (1u << s)) drain_full(&q_full[s], (par >> s) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint64_t k_desc = smem_desc(smem_u32(smem + DKV_OFF_K), 16, 1024, kSw128);
+            const uint64_t v_desc = smem_desc(smem_u32(smem + DKV_OFF_V), 16, 1024, kSw128);
+            const uint64_t r_kdesc = smem_desc(smem_u32(smem + DKV_OFF_RING), 16, 1024, kSw128);
+            const uint64_t r_mdesc = smem_desc(smem_u32(smem + DKV_OFF_RING), TILE64 / 2, 512, kSw128Atom32);
+            bool ok = wait_b(kv_full, 0, abort_flag, p, 42);
+            bool issued = false;
+            // S^T = K . Q_i^T and dP^T = V . dO_i^T into buffer i & 1
+            auto issue_s = [&](int i) -> bool {
+                const int b = i & 1, st = i % QST;
+                if (!wait_b(&q_full[st], (uint32_t)(i / QST) & 1u, abort_flag, p, 43)) return false;
+                if (!wait_b(&s_empty[b], ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag, p, 44)) return false;
+                tc_fence_after();
+                const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
+                const uint32_t ds = tmem_base + (uint32_t)(b * TB), dp = tmem_base + (uint32_t)(128 + b * TB);
+#pragma unroll
+                for (int s = 0; s < BD / 8; ++s)
+                    umma_tf32<1>(ds, kmajor_step(k_desc, TILE128 / 2, s),
+                                 kmajor_step(r_kdesc + soff, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
+#pragma unroll
+                for (int s = 0; s < BD / 8; ++s)
+                    umma_tf32<1>(dp, kmajor_step(v_desc, TILE128 / 2, s),
+                                 kmajor_step(r_kdesc + soff + (uint32_t)((2 * TILE64) >> 4), TILE64 / 2, s),
+                                 kIdescKK, s > 0 ? 1u : 0u);
+                umma_commit<1>(smem_u32(&s_full[b]));
+                issued = true;
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int i = 0; ok && i < p.nblk; ++i) {
+                const int b = i & 1, st = i % QST;
+                if (i + 1 < p.nblk) ok = issue_s(i + 1);
+                if (ok) ok = wait_b(&e_full[b], (uint32_t)(i >> 1) & 1u, abort_flag, p, 45);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
+                const uint32_t pa = tmem_base + (uint32_t)(b * TB), dsa = tmem_base + (uint32_t)(128 + b * TB);
+                // dV += P^T . dO_i (B = dO MN-major), dK += dS^T . Q_i (B = Q MN-major)
+#pragma unroll
+                for (int s = 0; s < TB / 8; ++s)
+                    umma_tf32_tmem_a(tmem_base + 256u, pa + 8 * s,
+                                     mnmajor_step(r_mdesc + soff + (uint32_t)((3 * TILE64) >> 4), s), kIdescKM,
+                                     (i > 0 || s > 0) ? 1u : 0u);
+#pragma unroll
+                for (int s = 0; s < TB / 8; ++s)
+                    umma_tf32_tmem_a(tmem_base + 320u, dsa + 8 * s,
+                                     mnmajor_step(r_mdesc + soff + (uint32_t)(TILE64 >> 4), s), kIdescKM,
+                                     (i > 0 || s > 0) ? 1u : 0u);
+                umma_commit<1>(smem_u32(&s_empty[b]));
+                umma_commit<1>(smem_u32(&q_empty[st]));
+            }
+            if (ok) umma_commit<1>(smem_u32(acc_full));
+            if (!ok && issued) {
+                umma_commit<1>(smem_u32(drain));
+                drain_full(drain, 0);
+            }
+        }
+    } else {
+        // ---------------- elementwise (warps 2-9) ----------------
+        const int h = (warp - 2) >> 2;   // half of the block's 64 queries
+        const int quarter = warp & 3;    // the TMEM lane quarter this warp may access
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        const float sl2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
+        bool ok = true;
+        for (int i = 0; i < p.nblk && ok; ++i) {
+            const int b = i & 1, st = i % QST;
+            ok = warp_wait_b(&s_full[b], (uint32_t)(i >> 1) & 1u, abort_flag, p, 46);
+            // this block's L2, D landed in the stage (the stage is refilled only
+            // after this block's dK product, which waits for this warp)
+            if (ok) ok = warp_wait_b(&q_full[st], (uint32_t)(i / QST) & 1u, abort_flag, p, 48);
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t sv[32], dv[32];
+            const uint32_t sa = lane_base + (uint32_t)(b * TB + 32 * h);
+            const uint32_t pa = lane_base + (uint32_t)(128 + b * TB + 32 * h);
+            tmem_ld32(sa, sv);
+            tmem_ld32(pa, dv);
+            const float* lt = reinterpret_cast<const float*>(smem + DKV_OFF_RING + st * DKV_STAGE + 4 * TILE64) + 32 * h;
+            const float* dt = lt + TB;
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -lt[c]));
+                const float g = __fmul_rn(__fmul_rn(pr, __fsub_rn(__uint_as_float(dv[c]), dt[c])), p.scale);
+                sv[c] = __float_as_uint(pr);
+                dv[c] = __float_as_uint(g);
+            }
+            tmem_st32(sa, sv);
+            tmem_st32(pa, dv);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&e_full[b]);
+        }
+        // dK, dV rows of this CTA's keys: this half's 32 columns of each
+        if (ok) ok = warp_wait_b(acc_full, 0, abort_flag, p, 47);
+        const int key = k0 + r;
+        if (ok) {
+            tc_fence_after();
+            uint32_t vv[32], kk[32];
+            tmem_ld32(lane_base + (uint32_t)(256 + 32 * h), vv);
+            tmem_ld32(lane_base + (uint32_t)(320 + 32 * h), kk);
+            tmem_wait_ld();
+            if (key < p.S) {
+                const int dc = p.d - 32 * h;
+                float* dvrow = p.out1 + ((int64_t)head * p.S + key) * p.d + 32 * h;
+                float* dkrow = p.out0 + ((int64_t)head * p.S + key) * p.d + 32 * h;
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    if (c < dc) {
+                        dvrow[c] = __uint_as_float(vv[c]);
+                        dkrow[c] = __uint_as_float(kk[c]);
+                    }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc<1>(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// dQ.  m[0] Q (K-major, box 128 rows), m[1] dO (K-major, 128), m[2] K (K-major,
+// 64), m[3] V (K-major, 64), m[4] K (MN-major, 64).
+constexpr int KST = 3;  // key-block ring stages
+constexpr int DQ_OFF_Q = 0, DQ_OFF_DO = TILE128, DQ_OFF_RING = 2 * TILE128;
+constexpr int DQ_STAGE = 3 * TILE64;  // Kk | Vk | Km
+constexpr int DQ_OFF_BAR = DQ_OFF_RING + KST * DQ_STAGE;
+constexpr int DQ_SMEM = DQ_OFF_BAR + 256 + 1024;
+static_assert(DQ_SMEM <= 232448, "shared memory per CTA");
+static_assert(8 * (1 + 2 * KST + 2 * 4 + 2 + 1) + 8 <= 256, "barrier area");
+// TMEM: S / dS buffer b at b * 64, dP buffer b at 128 + b * 64, dQ at 256
+
+__global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DQ_OFF_BAR);
+    uint64_t* q_full = bars;               // [1]  Q and dO tiles
+    uint64_t* k_full = q_full + 1;         // [KST]
+    uint64_t* k_empty = k_full + KST;      // [KST]
+    uint64_t* s_full = k_empty + KST;      // [2]  S and dP of a block computed
+    uint64_t* s_empty = s_full + 2;        // [2]  dQ product of that buffer done
+    uint64_t* e_full = s_empty + 2;        // [2]  dS written (per buffer)
+    uint64_t* acc_full = e_full + 2;       // [1]
+    uint64_t* drain = acc_full + 1;        // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = blockIdx.x / p.tiles;
+    const int q0 = (blockIdx.x - head * p.tiles) * TR;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < KST; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], 1);
+            mbar_init(&e_full[b], EW_WARPS);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0)
+        for (int i = 0; i < 5; ++i) prefetch_map(&p.m[i]);
+    if (warp == 1) {
+        __syncwarp();
+        tmem_alloc<1>(tmem_slot, TMEM_COLS);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            mbar_expect_tx(q_full, 2 * TILE128);
+            for (int c = 0; c < 2; ++c) {
+                tma_load_5d<1>(smem + DQ_OFF_Q + c * (TILE128 / 2), &p.m[0], smem_u32(q_full), 32 * c, q0, head, 0, 0);
+                tma_load_5d<1>(smem + DQ_OFF_DO + c * (TILE128 / 2), &p.m[1], smem_u32(q_full), 32 * c, q0, head, 0, 0);
+            }
+            uint32_t pend = 0, par = 0;
+            bool ok = true;
+            for (int j = 0; j < p.nblk; ++j) {
+                const int st = j % KST;
+                const uint32_t ph = (uint32_t)(j / KST) & 1u;
+                if (!wait_b(&k_empty[st], ph ^ 1u, abort_flag, p, 51)) {
+                    ok = false;
+                    break;
+                }
+                pend &= ~(1u << st);
+                uint8_t* sb = smem + DQ_OFF_RING + st * DQ_STAGE;
+                mbar_expect_tx(&k_full[st], DQ_STAGE);
+                const uint32_t fb = smem_u32(&k_full[st]);
+                for (int c = 0; c < 2; ++c) {
+                    tma_load_5d<1>(sb + c * (TILE64 / 2), &p.m[2], fb, 32 * c, j * TB, head, 0, 0);
+                    tma_load_5d<1>(sb + TILE64 + c * (TILE64 / 2), &p.m[3], fb, 32 * c, j * TB, head, 0, 0);
+                    tma_load_5d<1>(sb + 2 * TILE64 + c * (TILE64 / 2), &p.m[4], fb, 32 * c, j * TB, head, 0, 0);
+                }
+                pend |= 1u << st;
+                par = (par & ~(1u << st)) | (ph << st);
+            }
+            if (!ok) {
+                drain_full(q_full, 0);
+                for (int s = 0; s < KST; ++s)
+                    if (pend & (1u << s)) drain_full(&k_full[s], (par >> s) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint64_t q_desc = smem_desc(smem_u32(smem + DQ_OFF_Q), 16, 1024, kSw128);
+            const uint64_t do_desc = smem_desc(smem_u32(smem + DQ_OFF_DO), 16, 1024, kSw128);
+            const uint64_t r_kdesc = smem_desc(smem_u32(smem + DQ_OFF_RING), 16, 1024, kSw128);
+            const uint64_t r_mdesc = smem_desc(smem_u32(smem + DQ_OFF_RING), TILE64 / 2, 512, kSw128Atom32);
+            bool ok = wait_b(q_full, 0, abort_flag, p, 52);
+            bool issued = false;
+            // S = Q . K_j^T and dP = dO . V_j^T into buffer j & 1
+            auto issue_s = [&](int j) -> bool {
+                const int b = j & 1, st = j % KST;
+                if (!wait_b(&k_full[st], (uint32_t)(j / KST) & 1u, abort_flag, p, 53)) return false;
+                if (!wait_b(&s_empty[b], ((uint32_t)(j >> 1) & 1u) ^ 1u, abort_flag, p, 54)) return false;
+                tc_fence_after();
+                const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
+                const uint32_t ds = tmem_base + (uint32_t)(b * TB), dp = tmem_base + (uint32_t)(128 + b * TB);
+#pragma unroll
+                for (int s = 0; s < BD / 8; ++s)
+                    umma_tf32<1>(ds, kmajor_step(q_desc, TILE128 / 2, s),
+                                 kmajor_step(r_kdesc + soff, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
+#pragma unroll
+                for (int s = 0; s < BD / 8; ++s)
+                    umma_tf32<1>(dp, kmajor_step(do_desc, TILE128 / 2, s),
+                                 kmajor_step(r_kdesc + soff + (uint32_t)(TILE64 >> 4), TILE64 / 2, s),
+                                 kIdescKK, s > 0 ? 1u : 0u);
+                umma_commit<1>(smem_u32(&s_full[b]));
+                issued = true;
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < p.nblk; ++j) {
+                const int b = j & 1, st = j % KST;
+                if (j + 1 < p.nblk) ok = issue_s(j + 1);
+                if (ok) ok = wait_b(&e_full[b], (uint32_t)(j >> 1) & 1u, abort_flag, p, 55);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
+                const uint32_t dsa = tmem_base + (uint32_t)(b * TB);
+                // dQ += dS . K_j (A = dS in TMEM, B = K MN-major)
+#pragma unroll
+                for (int s = 0; s < TB / 8; ++s)
+                    umma_tf32_tmem_a(tmem_base + 256u, dsa + 8 * s,
+                                     mnmajor_step(r_mdesc + soff + (uint32_t)((2 * TILE64) >> 4), s), kIdescKM,
+                                     (j > 0 || s > 0) ? 1u : 0u);
+                umma_commit<1>(smem_u32(&s_empty[b]));
+                umma_commit<1>(smem_u32(&k_empty[st]));
+            }
+            if (ok) umma_commit<1>(smem_u32(acc_full));
+            if (!ok && issued) {
+                umma_commit<1>(smem_u32(drain));
+                drain_full(drain, 0);
+            }
+        }
+    } else {
+        // ---------------- elementwise (warps 2-9) ----------------
+        const int h = (warp - 2) >> 2;   // half of the block's 64 keys
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int row = q0 + r;          // < S_pad: tiles * 128 <= S_pad
+        const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        const float sl2 = p.scale * 1.4426950408889634f;
+        const float l2 = p.L2[(int64_t)head * p.S_pad + row];
+        const float dr = p.D[(int64_t)head * p.S_pad + row];
+        bool ok = true;
+        for (int j = 0; j < p.nblk && ok; ++j) {
+            const int b = j & 1;
+            ok = warp_wait_b(&s_full[b], (uint32_t)(j >> 1) & 1u, abort_flag, p, 56);
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t sv[32], dv[32];
+            const uint32_t sa = lane_base + (uint32_t)(b * TB + 32 * h);
+            tmem_ld32(sa, sv);
+            tmem_ld32(lane_base + (uint32_t)(128 + b * TB + 32 * h), dv);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float pr = ex2(fmaf(__uint_as_float(sv[c]), sl2, -l2));
+                sv[c] = __float_as_uint(__fmul_rn(__fmul_rn(pr, __fsub_rn(__uint_as_float(dv[c]), dr)), p.scale));
+            }
+            // keys past S: K, V rows there are zero, but exp(-L) may overflow for a
+            // row whose scores are all far below zero; their dS is zero outright
+            const int valid = p.S - j * TB - 32 * h;
+            if (valid < 32) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    if (c >= valid) sv[c] = 0u;
+            }
+            tmem_st32(sa, sv);  // dS over S: the A operand of dQ += dS . K
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&e_full[b]);
+        }
+        if (ok) ok = warp_wait_b(acc_full, 0, abort_flag, p, 57);
+        if (ok) {
+            tc_fence_after();
+            uint32_t qv[32];
+            tmem_ld32(lane_base + (uint32_t)(256 + 32 * h), qv);
+            tmem_wait_ld();
+            if (row < p.S) {
+                const int dc = p.d - 32 * h;
+                float* qrow = p.out0 + ((int64_t)head * p.S + row) * p.d + 32 * h;
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    if (c < dc) qrow[c] = __uint_as_float(qv[c]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc<1>(tmem_base, TMEM_COLS);
+    }
+}
+
+// D = rowsum(dO * O) and L2 = L * log2(e) per row into [heads, S_pad], zero past S.
+__global__ void fa_bwd_prep_kernel(const float* __restrict__ dO, const float* __restrict__ O,
+                                   const float* __restrict__ L, float* __restrict__ D,
+                                   float* __restrict__ L2, int64_t heads, int S, int S_pad, int d) {
+    const int64_t n = heads * S_pad;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t hd = i / S_pad;
+        const int row = (int)(i - hd * S_pad);
+        float acc = 0.0f, l2 = 0.0f;
+        if (row < S) {
+            const int64_t r = hd * S + row;
+            for (int c = 0; c < d; ++c) acc = fmaf(dO[r * d + c], O[r * d + c], acc);
+            l2 = __fmul_rn(L[r], 1.4426950408889634f);
+        }
+        D[i] = acc;
+        L2[i] = l2;
+    }
+}
+
+template <typename K>
+int configure(K kernel, int smem, bool* done) {
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    if (!done[dev]) {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        done[dev] = true;
+    }
+    return TLC_OK;
+}
+
+}  // namespace
+
+bool flash_bwd_tc_supported(int d, const float* const* ptrs, int n) {
+    if (d < 32 || d > BD || d % 4 != 0) return false;
+    for (int i = 0; i < n; ++i)
+        if (!al16(ptrs[i])) return false;
+    return true;
+}
+
+int flash_backward_tc(const float* dout, const float* q, const float* k, const float* v,
+                      const float* o, const float* lse, float* dq, float* dk, float* dv,
+                      int64_t heads, int S, int d, float scale, cudaStream_t s) {
+    static bool cfg_dkdv[64] = {}, cfg_dq[64] = {};
+    TLC_TRY(configure(flash_bwd_dkdv_kernel, DKV_SMEM, cfg_dkdv));
+    TLC_TRY(configure(flash_bwd_dq_kernel, DQ_SMEM, cfg_dq));
+    if (heads > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "flash_attention_backward: too many heads");
+    const int tiles = (S + TR - 1) / TR;
+    const int S_pad = tiles * TR;
+    const int64_t grid = (int64_t)tiles * heads;
+    if (grid > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "flash_attention_backward: too many tiles");
+    void* scratch = nullptr;
+    TLC_TRY(scratch_alloc(&scratch, sizeof(float) * 2 * (size_t)(heads * S_pad), s));
+    float* Dp = static_cast<float*>(scratch);
+    float* L2p = Dp + heads * S_pad;
+    int rc = TLC_OK;
+    do {
+        const int64_t n = heads * S_pad;
+        const int pg = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32));
+        fa_bwd_prep_kernel<<<pg, 256, 0, s>>>(dout, o, lse, Dp, L2p, heads, S, S_pad, d);
+        count_launch();
+        if ((rc = check_launch("flash_attention_backward")) != TLC_OK) break;
+
+        const int64_t bsz[kMaxBatchDims] = {heads, 1, 1};
+        const int64_t bstr[kMaxBatchDims] = {(int64_t)S * d, 0, 0};
+        BwdParams p;
+        memset(&p, 0, sizeof(p));
+        p.L2 = L2p;
+        p.D = Dp;
+        p.S = S;
+        p.S_pad = S_pad;
+        p.d = d;
+        p.tiles = tiles;
+        p.nblk = S_pad / TB;
+        p.scale = scale;
+        if ((rc = tc_error_word(&p.err)) != TLC_OK) break;
+        const CUtensorMapSwizzle K_SW = CU_TENSOR_MAP_SWIZZLE_128B, M_SW = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+        // dK, dV
+        if ((rc = encode_tiled(&p.m[0], k, d, S, d, bsz, bstr, 32, TR, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[1], v, d, S, d, bsz, bstr, 32, TR, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[2], q, d, S, d, bsz, bstr, 32, TB, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[3], q, d, S, d, bsz, bstr, 32, TB, M_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[4], dout, d, S, d, bsz, bstr, 32, TB, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[5], dout, d, S, d, bsz, bstr, 32, TB, M_SW)) != TLC_OK) break;
+        p.out0 = dk;
+        p.out1 = dv;
+        flash_bwd_dkdv_kernel<<<(unsigned)grid, THREADS, DKV_SMEM, s>>>(p);
+        count_launch();
+        if ((rc = check_launch("flash_attention_backward (dK, dV)")) != TLC_OK) break;
+        // dQ
+        if ((rc = encode_tiled(&p.m[0], q, d, S, d, bsz, bstr, 32, TR, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[1], dout, d, S, d, bsz, bstr, 32, TR, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[2], k, d, S, d, bsz, bstr, 32, TB, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[3], v, d, S, d, bsz, bstr, 32, TB, K_SW)) != TLC_OK) break;
+        if ((rc = encode_tiled(&p.m[4], k, d, S, d, bsz, bstr, 32, TB, M_SW)) != TLC_OK) break;
+        p.out0 = dq;
+        p.out1 = nullptr;
+        flash_bwd_dq_kernel<<<(unsigned)grid, THREADS, DQ_SMEM, s>>>(p);
+        count_launch();
+        rc = check_launch("flash_attention_backward (dQ)");
+    } while (false);
+    scratch_free(scratch, s);
+    return rc;
+}
+
+}  // namespace tlc

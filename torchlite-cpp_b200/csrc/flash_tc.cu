@@ -59,7 +59,7 @@ constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_X = OFF_V + VST * V_BYTES;  // row-max exchange: [2 parities][NQ][2 halves][128]
 constexpr int X_BYTES = 2 * NQ * 2 * FQ * 4;
 constexpr int OFF_BAR = OFF_X + X_BYTES;
-constexpr int BAR_BYTES = 8 * (1 + 2 * KST + 2 * VST + 2 * SPB * NQ + 3 * NQ) + 8;  // + TMEM slot, abort flag
+constexpr int BAR_BYTES = 8 * (1 + 2 * KST + 2 * VST + 3 * SPB * NQ + 2 * NQ) + 8;  // + TMEM slot, abort flag
 constexpr int SMEM = OFF_BAR + 512 + 1024;  // barriers + 1 KB alignment slack
 static_assert(BAR_BYTES <= 512, "barrier area");
 constexpr int SM_WARPS = 8;                 // softmax warps per query tile: 2 per TMEM lane quarter
@@ -112,8 +112,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     uint64_t* v_empty = v_full + VST;         // [VST]
     uint64_t* s_full = v_empty + VST;         // [NQ][SPB]
     uint64_t* s_empty = s_full + SPB * NQ;    // [NQ][SPB]
-    uint64_t* p_full = s_empty + SPB * NQ;    // [NQ]
-    uint64_t* o_full = p_full + NQ;           // [NQ]
+    // p_full is per buffer: a softmax warp may finish block j + 1 before the
+    // MMA thread has looked at block j, and a parity wait tells apart only
+    // two consecutive phases of one barrier
+    uint64_t* p_full = s_empty + SPB * NQ;    // [NQ][SPB]
+    uint64_t* o_full = p_full + SPB * NQ;     // [NQ]
     uint64_t* drain = o_full + NQ;            // [NQ]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + NQ);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -136,8 +139,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             for (int b = 0; b < SPB; ++b) {
                 mbar_init(&s_full[SPB * t + b], 1);
                 mbar_init(&s_empty[SPB * t + b], 1);  // committed after the P.V that read it
+                mbar_init(&p_full[SPB * t + b], SM_WARPS);
             }
-            mbar_init(&p_full[t], SM_WARPS);
             mbar_init(&o_full[t], 1);
         }
         for (int t = 0; t < NQ; ++t) mbar_init(&drain[t], 1);
@@ -262,10 +265,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             // scores in TMEM, B = V from shared memory; 8 MMAs of K = 8 keys
             // (the first block's first MMA starts O from zero)
             auto issue_pv = [&](int t, int j) -> bool {
-                if (!wait_bounded(&p_full[t], (uint32_t)j & 1u, abort_flag, p.timeout_ns, p.err, 25, kSleepMma))
+                const int b = j % SPB;
+                if (!wait_bounded(&p_full[SPB * t + b], (uint32_t)(j / SPB) & 1u, abort_flag, p.timeout_ns,
+                                  p.err, 25, kSleepMma))
                     return false;
                 tc_fence_after();
-                const int b = j % SPB;
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + O_COL);
                 const uint32_t pa = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
                 const uint64_t vd = v_desc + (uint32_t)(((j % VST) * V_BYTES) >> 4);
@@ -421,7 +425,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&p_full[t]);
+                if (lane == 0) mbar_arrive(&p_full[SPB * t + b]);
             }
         }
         // O after the last P.V.  A parity wait tells apart only the current and
