@@ -6,19 +6,22 @@
 // head's keys in blocks of 64, as the reference's tiles do (its 64 x 64
 // query tiles become 128-row tiles; the per-row arithmetic is the same online
 // softmax).  19 warps:
-//   warp 0      TMA producer: Q tiles once, then K and V blocks into two
-//               rings (4 K stages, 3 V stages), 128-byte swizzle; V is loaded
-//               key-major with 32-byte swizzle granules (the MN-major operand
-//               of P.V).
+//   warp 0      TMA producer: K and V blocks into two rings (4 K stages, 3 V
+//               stages), 128-byte swizzle; V is loaded key-major with 32-byte
+//               swizzle granules (the MN-major operand of P.V).
 //   warp 1      TMEM owner; MMA issuer (one thread) of query tile 0, warp 18
-//               the same for tile 1: S_t = Q_t . K_j^T
-//               (M = 128, N = 64, K = d) into one of three TMEM score buffers
-//               per query tile, issued one key block ahead;
+//               the same for tile 1: S_t = Q_t . K_j^T (M = 128, N = 64,
+//               K = d) with A = Q_t in tensor memory, into one of two TMEM
+//               score buffers per query tile, issued one key block ahead;
 //               O_t += P_t . V_j (M = 128, N = 64, K = 64 keys) into a TMEM
-//               accumulator, with A = P read from tensor memory.
+//               accumulator, with A = P read from tensor memory.  Both
+//               products take their A operand from TMEM: an N = 64 product
+//               whose A comes from shared memory runs at about a third of the
+//               rate.
 //   warps 2-9   softmax for query tile 0, warps 10-17 for query tile 1: two
 //               warps per TMEM lane quarter, thread = (query row, half of the
-//               keys).  Per key block: tcgen05.ld the half row of scores,
+//               keys).  First each writes its half of its Q row into TMEM.
+//               Per key block: tcgen05.ld the half row of scores,
 //               t = s * scale (masked to -inf past S) in log2 units; the two
 //               halves exchange their maxima (shared memory, 64-thread named
 //               barrier); p = exp(t - m), l = l * corr + sum p (partial per
@@ -29,10 +32,11 @@
 //               than a factor 2^8 (conditional rescaling, as FlashAttention-4
 //               does); then O and l are rescaled by exp(m_old - m_new) in
 //               place.  At the end O = o * (1 / l), L = m + log(l).
-// The score / probability buffers are reused three blocks later, after the
-// MMA thread's commit for the P.V that read them.  Every mbarrier wait is
-// bounded (a %globaltimer deadline, an abort flag, the device error word),
-// as in the GEMM kernel, and the named-barrier syncs are taken the same
+// TMEM per query tile (256 of the 512 columns): Q 64, two score /
+// probability buffers of 64, O 64.  A buffer is reused two blocks later,
+// after the MMA thread's commit for the P.V that read it.  Every mbarrier
+// wait is bounded (a %globaltimer deadline, an abort flag, the device error
+// word), as in the GEMM kernel, and the named-barrier syncs are taken the same
 // number of times by both warps of a pair on every path.
 #include <algorithm>
 #include <cstring>
@@ -50,16 +54,15 @@ constexpr int FD = 64;       // head dim of the tiles (d <= 64, zero-filled)
 constexpr int NQ = 2;        // query tiles per CTA
 constexpr int KST = 4;       // K ring stages
 constexpr int VST = 3;       // V ring stages
-constexpr int SPB = 3;       // score / probability buffers per query tile in TMEM
-constexpr int Q_BYTES = FQ * FD * 4;   // 2 boxes [128 rows x 32 dims] of 16 KB
+constexpr int SPB = 2;       // score / probability buffers per query tile in TMEM
 constexpr int K_BYTES = FK * FD * 4;   // 2 boxes [64 keys x 32 dims] of 8 KB
 constexpr int V_BYTES = FK * FD * 4;   // 2 chunks [64 keys x 32 dims] of 8 KB (MN-major)
-constexpr int OFF_K = NQ * Q_BYTES;
+constexpr int OFF_K = 0;  // Q lives in TMEM (written by the softmax warps)
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_X = OFF_V + VST * V_BYTES;  // row-max exchange: [2 parities][NQ][2 halves][128]
 constexpr int X_BYTES = 2 * NQ * 2 * FQ * 4;
 constexpr int OFF_BAR = OFF_X + X_BYTES;
-constexpr int BAR_BYTES = 8 * (1 + 2 * KST + 2 * VST + 3 * SPB * NQ + 2 * NQ) + 8;  // + TMEM slot, abort flag
+constexpr int BAR_BYTES = 8 * (NQ + 2 * KST + 2 * VST + 3 * SPB * NQ + 2 * NQ) + 8;  // + TMEM slot, abort flag
 constexpr int SMEM = OFF_BAR + 512 + 1024;  // barriers + 1 KB alignment slack
 static_assert(BAR_BYTES <= 512, "barrier area");
 constexpr int SM_WARPS = 8;                 // softmax warps per query tile: 2 per TMEM lane quarter
@@ -67,7 +70,8 @@ constexpr int MMA2_WARP = 2 + NQ * SM_WARPS;  // the MMA warp of query tile 1 (t
 constexpr int THREADS = 32 * (MMA2_WARP + 1);
 // TMEM: tile t owns columns t*256 ..: S/P buffer b at t*256 + b*64, O at t*256 + 192
 constexpr int TMEM_COLS = 512;
-constexpr int TILE_COLS = 256, O_COL = SPB * FK;
+constexpr int TILE_COLS = 256, Q_COL = 0, SP_COL = FD, O_COL = SP_COL + SPB * FK;
+static_assert(O_COL + FD <= TILE_COLS, "TMEM columns of a query tile");
 // The running row maximum (log2 units) moves only when a block's maximum
 // exceeds it by more than this; probabilities stay <= 2^8 in between.
 constexpr float kRescaleLog2 = 8.0f;
@@ -77,7 +81,8 @@ constexpr uint32_t kSleepNs = 100000, kSleepMma = 100000, kSleepSm = 100000;
 static_assert(SMEM <= 232448, "shared memory per CTA");
 
 struct FtParams {
-    CUtensorMap tmQ, tmK, tmV;
+    CUtensorMap tmK, tmV;
+    const float* Qp;  // q rows, read once into TMEM
     float* O;
     float* L;
     int S, d;
@@ -105,8 +110,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint64_t* q_full = bars;                  // [1]
-    uint64_t* k_full = q_full + 1;            // [KST]
+    uint64_t* a_full = bars;                  // [NQ]  Q rows of the tile in TMEM
+    uint64_t* k_full = a_full + NQ;           // [KST]
     uint64_t* k_empty = k_full + KST;         // [KST]
     uint64_t* v_full = k_empty + KST;         // [VST]
     uint64_t* v_empty = v_full + VST;         // [VST]
@@ -126,7 +131,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     const int q0 = (blockIdx.x - head * p.tiles) * (NQ * FQ);
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int t = 0; t < NQ; ++t) mbar_init(&a_full[t], SM_WARPS);
         for (int s = 0; s < KST; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], NQ);  // a commit from each tile's MMA thread
@@ -149,7 +154,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         fence_async_smem();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_map(&p.tmQ);
         prefetch_map(&p.tmK);
         prefetch_map(&p.tmV);
     }
@@ -165,12 +169,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            const uint32_t qb = smem_u32(q_full);
-            mbar_expect_tx(q_full, NQ * Q_BYTES);
-            for (int t = 0; t < NQ; ++t)
-                for (int c = 0; c < FD / 32; ++c)
-                    tma_load_5d<1>(smem + t * Q_BYTES + c * (Q_BYTES / 2), &p.tmQ, qb, 32 * c,
-                                   q0 + t * FQ, head, 0, 0);
             uint32_t pend_k = 0, par_k = 0, pend_v = 0, par_v = 0;
             bool ok = true;
             for (int j = 0; ok && j < p.nk; ++j) {
@@ -201,9 +199,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             }
             if (!ok) {
                 // loads still in flight land before the CTA frees anything
-                const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < p.timeout_ns) {
-                }
                 for (int s = 0; s < KST; ++s)
                     if (pend_k & (1u << s)) {
                         const uint64_t t1 = globaltimer();
@@ -233,12 +228,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                                      ((uint32_t)(FQ >> 4) << 24);
             const uint32_t idesc_pv = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) |
                                       ((uint32_t)(FD >> 3) << 17) | ((uint32_t)(FQ >> 4) << 24);
-            // descriptors of Q tile 0, K stage 0, V stage 0; any other tile, stage
-            // or k-step only moves the start-address field (address >> 4)
-            const uint64_t q_desc = smem_desc(smem_u32(smem), 16, 1024, kSw128);
+            // descriptors of K stage 0, V stage 0; any other stage or k-step only
+            // moves the start-address field (address >> 4)
             const uint64_t k_desc = smem_desc(smem_u32(smem + OFF_K), 16, 1024, kSw128);
             const uint64_t v_desc = smem_desc(smem_u32(smem + OFF_V), V_BYTES / 2, 512, kSw128Atom32);
-            bool ok = wait_bounded(q_full, 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
+            bool ok = wait_bounded(&a_full[mt], 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
             bool issued = false;
             tc_fence_after();
             // S_t(j) = Q_t . K_j^T into buffer (t, j % SPB): 8 MMAs of K = 8 over d = 64,
@@ -249,14 +243,16 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                                   p.timeout_ns, p.err, 24, kSleepMma))
                     return false;
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
-                const uint64_t qd = q_desc + (uint32_t)((t * Q_BYTES) >> 4);
+                const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + SP_COL + b * FK);
+                const uint32_t qa = tmem_base + (uint32_t)(t * TILE_COLS + Q_COL);
                 const uint64_t kd = k_desc + (uint32_t)(((j % KST) * K_BYTES) >> 4);
+                // A = Q from TMEM: an N = 64 product whose A comes from shared
+                // memory runs at about a third of this rate
 #pragma unroll
                 for (int s = 0; s < FD / 8; ++s)
-                    umma_tf32<1>(d, qd + (uint32_t)(((s >> 2) * (Q_BYTES / 2) + (s & 3) * 32) >> 4),
-                                 kd + (uint32_t)(((s >> 2) * (K_BYTES / 2) + (s & 3) * 32) >> 4), idesc_s,
-                                 s > 0 ? 1u : 0u);
+                    umma_tf32_tmem_a(d, qa + 8 * s,
+                                     kd + (uint32_t)(((s >> 2) * (K_BYTES / 2) + (s & 3) * 32) >> 4), idesc_s,
+                                     s > 0 ? 1u : 0u);
                 umma_commit<1>(smem_u32(&s_full[SPB * t + b]));
                 issued = true;
                 return true;
@@ -271,7 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + O_COL);
-                const uint32_t pa = tmem_base + (uint32_t)(t * TILE_COLS + b * FK);
+                const uint32_t pa = tmem_base + (uint32_t)(t * TILE_COLS + SP_COL + b * FK);
                 const uint64_t vd = v_desc + (uint32_t)(((j % VST) * V_BYTES) >> 4);
 #pragma unroll
                 for (int s = 0; s < FK / 8; ++s)
@@ -332,6 +328,29 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         const int bar_id = 1 + t * 4 + quarter;              // named barrier of the two halves
         const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
         const bool fast = sl2 > 0.0f;  // max(s) * sl2 == max(s * sl2): one FFMA per probability
+        // this tile's Q rows into TMEM, this half's 32 columns: the A operand of S
+        {
+            uint32_t qv[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) qv[c] = 0u;
+            if (row < p.S) {
+                const float4* src = reinterpret_cast<const float4*>(p.Qp + ((int64_t)head * p.S + row) * p.d + 32 * h);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    if (32 * h + 4 * c < p.d) {
+                        const float4 x = __ldg(src + c);
+                        qv[4 * c] = __float_as_uint(x.x);
+                        qv[4 * c + 1] = __float_as_uint(x.y);
+                        qv[4 * c + 2] = __float_as_uint(x.z);
+                        qv[4 * c + 3] = __float_as_uint(x.w);
+                    }
+            }
+            tmem_st32(lane_base + (uint32_t)(t * TILE_COLS + Q_COL + 32 * h), qv);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[t]);
+        }
         float m2 = -INFINITY, l = 0.0f;
         bool ok = true;
         auto ex2 = [](float x) {
@@ -345,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         // every sync, and each of its waits is bounded.
         for (int j = 0; j < p.nk; ++j) {
             const int b = j % SPB;
-            const uint32_t sp_addr = lane_base + (uint32_t)(t * TILE_COLS + b * FK + 32 * h);
+            const uint32_t sp_addr = lane_base + (uint32_t)(t * TILE_COLS + SP_COL + b * FK + 32 * h);
             if (ok) ok = warp_wait(&s_full[SPB * t + b], (uint32_t)(j / SPB) & 1u, abort_flag, p, 30);
             float u[32];
             if (ok) {
@@ -502,9 +521,9 @@ int flash_forward_tc(const float* q, const float* k, const float* v, float* o, f
     memset(&p, 0, sizeof(p));
     const int64_t bsz[kMaxBatchDims] = {heads, 1, 1};
     const int64_t bstr[kMaxBatchDims] = {(int64_t)S * d, 0, 0};
-    TLC_TRY(encode_tiled(&p.tmQ, q, d, S, d, bsz, bstr, 32, FQ, CU_TENSOR_MAP_SWIZZLE_128B));
     TLC_TRY(encode_tiled(&p.tmK, k, d, S, d, bsz, bstr, 32, FK, CU_TENSOR_MAP_SWIZZLE_128B));
     TLC_TRY(encode_tiled(&p.tmV, v, d, S, d, bsz, bstr, 32, FK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+    p.Qp = q;
     p.O = o;
     p.L = lse;
     p.S = S;
