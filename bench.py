@@ -381,10 +381,12 @@ class BroadcastWork(Work):
 
 class FlashWork(Work):
     """flash_attention forward + FlashAttentionBackward on batch 16 x 12 heads,
-    S = 2048, d = 64 ([16,12,2048,64] Q, K, V, dO ~ N(0,1), seed 5), scale 1/8:
-    the fused FFMA forward kernel, then the backward's five batched GEMMs (in
-    the mode) and its elementwise kernels.  FLOPs: forward 4*S*S*d per head
-    (Q.K^T and P.V), backward 10*S*S*d (Q.K^T recomputed, dV, dP, dQ, dK)."""
+    S = 2048, d = 64 ([16,12,2048,64] Q, K, V, dO ~ N(0,1), seed 5), scale 1/8.
+    TF32 mode: the tcgen05 forward, then the fused tcgen05 backward (prep,
+    dK/dV, dQ kernels); exact / 3xTF32: the FFMA forward, then five batched
+    GEMMs in the mode and elementwise kernels.  FLOPs: forward 4*S*S*d per
+    head (Q.K^T and P.V), backward 10*S*S*d (Q.K^T recomputed, dV, dP, dQ, dK;
+    the fused dQ kernel recomputes S and dP once more, not counted)."""
     name = "flash"
 
     def __init__(self, world, rank, device, batch=16):
@@ -404,7 +406,7 @@ class FlashWork(Work):
         self.config = {"workload": self.name, "batch": batch, "heads": 12, "S": 2048, "d": 64,
                        "sm_scale": 0.125,
                        "forward": "fused kernel: tcgen05 TF32 in tf32 mode, FFMA otherwise",
-                       "backward": "5 batched GEMMs in the mode + elementwise kernels",
+                       "backward": "tf32: fused tcgen05 dK/dV and dQ kernels; exact, 3xtf32: 5 batched GEMMs in the mode + elementwise kernels",
                        "parallelism": "replicas"}
 
     def forward(self, mode):

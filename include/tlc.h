@@ -268,9 +268,11 @@ int tlc_conv2d_backward(const tlc_tensor* grad_output, const tlc_tensor* input,
  * the TF32 tolerance; other TF32 cases run the FFMA kernel.  `lse` ([..., S],
  * contiguous, or NULL) receives L = m + log(l), the reference's L_cache.
  * FlashAttentionBackward (src/autograd.cpp:575-669): d_q, d_k, d_v from
- * grad_out, the forward's inputs, out and lse, through batched GEMMs in
- * `mode` (S x S scratch per head, at most 1 GiB per buffer); outputs are
- * overwritten.  Both agree with the reference to its own bar (1e-4 against
+ * grad_out, the forward's inputs, out and lse; outputs are overwritten.
+ * TLC_MODE_TF32 with 32 <= d <= 64 (d % 4 == 0, 16-byte aligned operands):
+ * two fused tcgen05 kernels (dK / dV per key tile, dQ per query tile), no
+ * S x S buffer; otherwise batched GEMMs in `mode` (S x S scratch per head, at
+ * most 1 GiB per buffer).  Both agree with the reference to its own bar (1e-4 against
  * the materialised softmax path): expf / logf and the order of the softmax
  * sums differ from the C library's.  Errors: shapes that differ, non-contiguous
  * operands, fewer than 2 dims (TLC_ERR_INVALID_ARGUMENT); d > 128
