@@ -52,7 +52,7 @@ GEMMS = {
     "square16384": (1, 16384, 16384, 16384),
     "square512": (1, 512, 512, 512),
 }
-OTHER = ("linear", "attention", "broadcast", "flash", "flash4")
+OTHER = ("linear", "attention", "broadcast", "flash", "flash4", "conv")
 METRIC = "GEMM TFLOP/s (fp32-exact, TF32, 3xTF32) at 1/2/4/8 B200, % of peak"
 
 
@@ -432,13 +432,41 @@ class FlashWork(Work):
                 "peak_source": peak[1], "algorithmic_flop_per_launch": self.fwd_flops}
 
 
+class ConvWork(Work):
+    """conv2d forward + Conv2dBackward, a ResNet-style 3x3 layer: x [32,64,56,56],
+    W [64,64,3,3], b [64], stride 1, padding 1 (x, dO ~ N(0,1), W ~ N(0,0.05^2),
+    b ~ N(0,1), seed 6): im2col, the batched GEMMs in the mode, col2im and the
+    bias gradient.  FLOPs: 2*N*C_out*H*W*C_in*k*k forward, twice that backward
+    (dW and dX)."""
+    name = "conv"
+
+    def __init__(self, world, rank, device):
+        import torch
+        g = torch.Generator(device=device).manual_seed(6)
+        self.x = torch.randn((32, 64, 56, 56), generator=g, device=device)
+        self.w = torch.randn((64, 64, 3, 3), generator=g, device=device) * 0.05
+        self.b = torch.randn((64,), generator=g, device=device)
+        self.go = torch.randn((32, 64, 56, 56), generator=g, device=device)
+        self.y = torch.empty((32, 64, 56, 56), device=device)
+        fwd = 2.0 * 32 * 64 * 56 * 56 * 64 * 9
+        self.flops = 3 * fwd
+        self.job_flops = self.flops * world
+        self.config = {"workload": "conv", "x": [32, 64, 56, 56], "W": [64, 64, 3, 3], "stride": 1,
+                       "padding": 1, "groups": 1, "parallelism": "replicas"}
+
+    def step(self, mode):
+        import tlcuda
+        tlcuda.conv2d(self.x, self.w, self.b, 1, 1, 1, mode=mode, out=self.y)
+        tlcuda.conv2d_backward(self.go, self.x, self.w, 1, 1, 1, mode=mode)
+
+
 def make_work(name, world, rank, device):
     if name in GEMMS:
         return GemmWork(name, world, rank, device)
     if name == "flash4":  # the profiling stand-in for "flash": batch 4 instead of 16
         return FlashWork(world, rank, device, batch=4)
     return {"linear": LinearWork, "attention": AttentionWork, "broadcast": BroadcastWork,
-            "flash": FlashWork}[name](world, rank, device)
+            "flash": FlashWork, "conv": ConvWork}[name](world, rank, device)
 
 
 # ---- the reference's CPU path ----------------------------------------------------------
@@ -479,6 +507,16 @@ def ref_job(name, R):
         return (lambda: R.flash_attention(q, k, v, 0.125, grad=g), flops,
                 f"tl::flash_attention + backward on one head [2048,64] of the workload "
                 f"({flops / 1e9:.2f} GFLOP)")
+    if name == "conv":
+        import numpy as np
+        rng = np.random.default_rng(6)
+        x = rng.standard_normal((2, 64, 56, 56)).astype(np.float32)
+        w = (rng.standard_normal((64, 64, 3, 3)) * 0.05).astype(np.float32)
+        b = rng.standard_normal((64,)).astype(np.float32)
+        g = rng.standard_normal((2, 64, 56, 56)).astype(np.float32)
+        flops = 3 * 2.0 * 2 * 64 * 56 * 56 * 64 * 9
+        return (lambda: R.conv2d(x, w, b, 1, 1, 1, grad=g), flops,
+                f"tl::conv2d + Conv2dBackward on 2 of the 32 images ({flops / 1e9:.2f} GFLOP)")
     a, b, flops, what = ref_sample(name)
     return lambda: R.matmul(a, b), flops, f"{what} ({flops / 1e9:.2f} GFLOP)"
 

@@ -97,14 +97,16 @@ __global__ void col2im_kernel(const float* __restrict__ gcol, float* __restrict_
 }
 
 // grad_bias[c] = 0 + dO[n, c, hw] for n, then hw, ascending: a chain of
-// N * HW dependent adds per channel.  One block per channel: warp 1 stages
+// N * HW dependent adds per channel.  One block per channel: warps 1-7 stage
 // the chain's values, BIAS_TILE at a time, into a double-buffered shared
-// ring (coalesced reads of each image's HW run); lane 0 of warp 0 adds
-// them in order.
-constexpr int BIAS_TILE = 1024;
-__global__ void __launch_bounds__(64) bias_grad_kernel(const float* __restrict__ go, float* __restrict__ gb,
-                                                       ConvShape s) {
-    __shared__ float tile[2][BIAS_TILE];
+// ring (coalesced reads of each image's HW run); lane 0 of warp 0 adds them
+// in order, loading each group of 8 before its adds so the loads stay off
+// the chain.
+constexpr int BIAS_TILE = 2048;
+constexpr int BIAS_THREADS = 256, BIAS_STAGERS = BIAS_THREADS - 32;
+__global__ void __launch_bounds__(BIAS_THREADS) bias_grad_kernel(const float* __restrict__ go,
+                                                                 float* __restrict__ gb, ConvShape s) {
+    __shared__ __align__(16) float tile[2][BIAS_TILE];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t total = s.N * s.HW;
     const int64_t tiles = (total + BIAS_TILE - 1) / BIAS_TILE;
@@ -112,30 +114,72 @@ __global__ void __launch_bounds__(64) bias_grad_kernel(const float* __restrict__
         // value j of the chain: dO[j / HW, c, j % HW]
         auto stage = [&](int64_t t, int buf) {
             const int64_t j0 = t * BIAS_TILE;
-            for (int k = lane; k < BIAS_TILE; k += 32) {
+            for (int k = (int)threadIdx.x - 32; k < BIAS_TILE; k += BIAS_STAGERS) {
                 const int64_t j = j0 + k;
                 float v = 0.0f;
                 if (j < total) {
                     const int64_t n = j / s.HW, hw = j - n * s.HW;
-                    v = go[(n * s.C_out + c) * s.HW + hw];
+                    v = __ldg(go + (n * s.C_out + c) * s.HW + hw);
                 }
                 tile[buf][k] = v;
             }
         };
-        if (warp == 1 && tiles > 0) stage(0, 0);
+        if (warp > 0 && tiles > 0) stage(0, 0);
         __syncthreads();
         float acc = 0.0f;
         for (int64_t t = 0; t < tiles; ++t) {
             const int buf = (int)(t & 1);
-            if (warp == 1) {
+            if (warp > 0) {
                 if (t + 1 < tiles) stage(t + 1, buf ^ 1);
             } else if (lane == 0) {
+                // the same ascending chain; each group of 8 values is loaded
+                // before its adds, so the loads are off the chain's critical path
                 const int cnt = (int)min((int64_t)BIAS_TILE, total - t * BIAS_TILE);
-                for (int k = 0; k < cnt; ++k) acc = __fadd_rn(acc, tile[buf][k]);
+                const float4* t4 = reinterpret_cast<const float4*>(tile[buf]);
+                int k = 0;
+#pragma unroll 4
+                for (; k + 8 <= cnt; k += 8) {
+                    const float4 a = t4[k >> 2], b = t4[(k >> 2) + 1];
+                    acc = __fadd_rn(acc, a.x);
+                    acc = __fadd_rn(acc, a.y);
+                    acc = __fadd_rn(acc, a.z);
+                    acc = __fadd_rn(acc, a.w);
+                    acc = __fadd_rn(acc, b.x);
+                    acc = __fadd_rn(acc, b.y);
+                    acc = __fadd_rn(acc, b.z);
+                    acc = __fadd_rn(acc, b.w);
+                }
+                for (; k < cnt; ++k) acc = __fadd_rn(acc, tile[buf][k]);
             }
             __syncthreads();
         }
         if (warp == 0 && lane == 0) gb[c] = acc;
+        __syncthreads();
+    }
+}
+
+// Non-exact modes: the bias gradient as a tree.  One block per (channel c,
+// image n) sums dO[n, c, :] (a contiguous run of HW values) into
+// part[c * N + n]; the sums over images follow (launch_sum_dim).  Within the
+// modes' tolerance of the reference's chain, and the same on every run.
+__global__ void __launch_bounds__(256) bias_part_kernel(const float* __restrict__ go, float* __restrict__ part,
+                                                        ConvShape s) {
+    __shared__ float red[8];
+    const int64_t pairs = s.C_out * s.N;
+    for (int64_t i = blockIdx.x; i < pairs; i += gridDim.x) {
+        const int64_t c = i / s.N, n = i - c * s.N;
+        const float* src = go + (n * s.C_out + c) * s.HW;
+        float acc = 0.0f;
+        for (int64_t k = threadIdx.x; k < s.HW; k += blockDim.x) acc += src[k];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t = 0.0f;
+            for (int w = 0; w < 8; ++w) t += red[w];
+            part[i] = t;
+        }
         __syncthreads();
     }
 }
@@ -325,7 +369,7 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
     if (d_w) TLC_TRY(check_dense_out(d_w, w_t->sizes, 4, "d_weight"));
     const int64_t bsz[1] = {s.C_out};
     if (d_b) TLC_TRY(check_dense_out(d_b, bsz, 1, "d_bias"));
-    Buf bgo(st), bin(st), bw(st), col(st), prod(st), gcol(st);
+    Buf bgo(st), bin(st), bw(st), col(st), prod(st), gcol(st), bpart(st);
     const float *go, *in, *w;
     TLC_TRY(dense_copy(go_t, bgo, &go, st));
     TLC_TRY(dense_copy(in_t, bin, &in, st));
@@ -404,9 +448,19 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
         }
     }
     if (d_b && s.C_out) {
-        bias_grad_kernel<<<(unsigned)std::min<int64_t>(s.C_out, 148 * 16), 64, 0, st>>>(go, d_b->data, s);
-        count_launch();
-        TLC_TRY(check_launch("conv bias grad"));
+        if (mode == TLC_MODE_EXACT || s.N * s.HW == 0) {
+            // the reference's order: one ascending chain per channel
+            bias_grad_kernel<<<(unsigned)std::min<int64_t>(s.C_out, 148 * 16), BIAS_THREADS, 0, st>>>(go, d_b->data, s);
+            count_launch();
+            TLC_TRY(check_launch("conv bias grad"));
+        } else {
+            TLC_TRY(scratch_alloc(&bpart.p, sizeof(float) * (size_t)(s.C_out * s.N), st));
+            bias_part_kernel<<<(unsigned)std::min<int64_t>(s.C_out * s.N, 148 * 16), 256, 0, st>>>(
+                go, bpart.f(), s);
+            count_launch();
+            TLC_TRY(check_launch("conv bias grad"));
+            TLC_TRY(launch_sum_dim(bpart.f(), d_b->data, s.C_out, s.N, 1, st));
+        }
     }
     return TLC_OK;
 }
