@@ -39,8 +39,11 @@
 //
 // 3xTF32 (Ootomo & Yokota, "Recovering single precision accuracy from Tensor
 // Cores while surpassing the FP32 theoretical peak performance", 2022): each
-// operand x is split as hi = round_to_tf32(x), lo = x - hi (exact in fp32) by
-// a pre-pass.  A stage holds hi and lo tiles of A and B for a k-block, and the
+// operand x is split as hi + lo.  kind::tf32 reads an fp32 input truncated to
+// TF32 (measured), so hi is the operand itself and a pre-pass writes only
+// lo = x - trunc_tf32(x) (exact in fp32); the allocation-free entry point
+// splits as hi = round_to_tf32(x), lo = x - hi into its fixed array instead.
+// A stage holds hi and lo tiles of A and B for a k-block, and the
 // MMA thread issues lo(A).hi(B), hi(A).lo(B) and hi(A).hi(B) from them, so
 // each tile is loaded once for three products (12 MMAs per stage handshake).
 // Because the tensor cores' fp32 accumulation error grows with the chain
@@ -583,6 +586,16 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
     }
 }
 
+// lo = x - trunc_tf32(x) (exact in fp32): the 3xTF32 low part when the high
+// part is the operand itself, which the tensor cores read truncated to TF32.
+__global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        lo[i] = __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xFFFFE000u));
+    }
+}
+
 // Tiny kernel for the failure-detection test: waits on an mbarrier that
 // nothing ever arrives on, with the same bounded wait as the GEMM, and
 // records the timeout in *err.
@@ -869,23 +882,22 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     TcParams prm;
     memset(&prm, 0, sizeof(prm));
     if (x3) {
-        // Split each operand's storage span into hi / lo planes of identical layout.
+        // hi is the operand itself: kind::tf32 reads an fp32 input truncated to
+        // TF32 (its low 13 mantissa bits ignored).  Only lo = x - trunc(x),
+        // exact in fp32, is written, into a plane of the operand's layout.
         OperandMap* ops[2] = {&A, &B};
         CUtensorMap* maps[2] = {prm.tmA, prm.tmB};
         for (int o = 0; o < 2; ++o) {
             const int64_t n = span_elems(ops[o]->inner, ops[o]->outer, ops[o]->outer_stride,
                                          ops[o]->bsz, ops[o]->bstride, g.nb);
-            TLC_TRY(scratch_alloc(&sc.p[2 + 2 * o], sizeof(float) * (size_t)n, s));
-            TLC_TRY(scratch_alloc(&sc.p[3 + 2 * o], sizeof(float) * (size_t)n, s));
-            float* hi = static_cast<float*>(sc.p[2 + 2 * o]);
-            float* lo = static_cast<float*>(sc.p[3 + 2 * o]);
-            split_tf32_kernel<<<grid_split(n), 256, 0, s>>>(ops[o]->base, hi, lo, n);
+            TLC_TRY(scratch_alloc(&sc.p[2 + o], sizeof(float) * (size_t)n, s));
+            float* lo = static_cast<float*>(sc.p[2 + o]);
+            split_lo_kernel<<<grid_split(n), 256, 0, s>>>(ops[o]->base, lo, n);
             count_launch();
-            TLC_TRY(check_launch("split_tf32"));
-            OperandMap h = *ops[o], l = *ops[o];
-            h.base = hi;
+            TLC_TRY(check_launch("split_tf32_lo"));
+            OperandMap l = *ops[o];
             l.base = lo;
-            TLC_TRY(encode(&maps[o][0], h));
+            TLC_TRY(encode(&maps[o][0], *ops[o]));
             TLC_TRY(encode(&maps[o][1], l));
         }
     } else {
