@@ -73,6 +73,10 @@ namespace {
 constexpr int BM = 128;        // rows of A (and of D) per CTA
 constexpr int BK = 32;         // k per stage: 32 fp32 = one 128-byte swizzle row
 constexpr int UMMA_K = 8;      // k per tcgen05.mma.kind::tf32
+// A waiting thread sleeps up to this long per poll (it wakes when the phase
+// completes), so idle waiters leave their schedulers' issue slots to the MMA
+// and TMA threads.
+constexpr uint32_t kGemmSleepNs = 20000;
 
 struct TcParams {
     CUtensorMap tmA[2];  // [0] A (TF32) or hi(A) (3xTF32); [1] lo(A)
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                 KbIter it;
                 it.start(p);
                 for (int kb = 0; kb < p.k_blocks;) {
-                    if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1)) {
+                    if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1, kGemmSleepNs)) {
                         ok = false;
                         break;
                     }
@@ -381,14 +385,14 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     if (it.first()) {
                         // a fresh accumulator for this chunk, once the epilogues drained it
                         if (!wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag,
-                                          p.timeout_ns, p.err, 2)) {
+                                          p.timeout_ns, p.err, 2, kGemmSleepNs)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         d = tmem_base + (uint32_t)(acc * UN);
                     }
-                    if (!wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3)) {
+                    if (!wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3, kGemmSleepNs)) {
                         ok = false;
                         break;
                     }
@@ -474,7 +478,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
             for (int j = 0; j < (X3 ? S::EPI_COLS : 1); ++j) sum[j] = 0.0f;
             for (int ch = 0; ch < p.num_chunks; ++ch) {
                 if (lane == 0)
-                    ok = wait_bounded(&tfull[acc], (acc_ph >> acc) & 1u, abort_flag, p.timeout_ns, p.err, 4);
+                    ok = wait_bounded(&tfull[acc], (acc_ph >> acc) & 1u, abort_flag, p.timeout_ns, p.err, 4, kGemmSleepNs);
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // one branch per warp
                 if (!ok) break;
                 tc_fence_after();
