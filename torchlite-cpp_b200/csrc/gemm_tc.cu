@@ -30,9 +30,12 @@
 // M-major (a transposed view, storage [K,M]); B may be N-major (row-major
 // [K,N]) or K-major (a transposed view, storage [N,K], the X.W^T of Linear).
 // The instruction descriptor's per-operand major bits select the layout; an
-// MN-major tile is loaded as 32-element-wide column chunks with the 128-byte
+// MN-major tile is held as 32-element-wide column chunks with the 128-byte
 // swizzle of 32-byte granules (atoms of 4 k-rows x 128 bytes), the one
-// shared-memory layout MN-major TF32 operands accept.  Batch dims (up to 3,
+// shared-memory layout MN-major TF32 operands accept.  When the MN extent is a
+// multiple of 32 (and there are at most two batch dims), the tensor map has a
+// chunk dimension and one TMA instruction loads all chunks of a k-block;
+// otherwise each chunk is its own load.  Batch dims (up to 3,
 // broadcast dims with stride 0) are extra dimensions of the 5-D tensor maps,
 // so ragged M, N and K tails are zero-filled by TMA per batch entry and never
 // read a neighbouring matrix.
@@ -95,6 +98,7 @@ struct TcParams {
     int chunk_kb;     // k-blocks per accumulation chunk (== k_blocks: one chunk)
     int num_chunks;
     int a_mn, b_mn;   // 1: operand is MN-major in memory
+    int a_chunked, b_chunked;  // 1: MN-major map with a chunk dim: one load per k-block
     int vec_c;        // float4 stores allowed
     uint64_t timeout_ns;
     int* err;
@@ -199,11 +203,15 @@ struct Cfg {
     static constexpr int TMEM_COLS = 2 * UN;
     static constexpr int TILE_M = BM * CG;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+    // TF32: each epilogue warp turns its 32 rows x 32 columns around in shared
+    // memory so that one store instruction writes four whole 128-byte rows.
+    static constexpr int EPI_STAGE_BYTES = X3 ? 0 : EPI_WARPS * 32 * 32 * 4;
+    static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + EPI_STAGE_BYTES + 1024;  // + alignment slack
     static_assert(TMEM_COLS <= 512, "two accumulators must fit in TMEM");
     static_assert(B_COLS % 32 == 0 && B_COLS <= 256, "B tile columns");
     static_assert(STAGES >= 2, "at least two pipeline stages");
     static_assert(EPI_COLS % 32 == 0, "epilogue columns in 32-column TMEM loads");
+    static_assert(TOTAL <= 227 * 1024, "dynamic shared memory per CTA");
 };
 
 // X3: the epilogue adds the chunk partials of each output element into
@@ -306,7 +314,9 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
                                           h * S::PAIR_BYTES;
                             uint8_t* sb = sa + S::A_BYTES;
-                            if (p.a_mn) {
+                            if (p.a_chunked) {
+                                tma_load_5d<CG>(sa, &p.tmA[h], fb, 0, k0, m0 >> 5, a0, a1);
+                            } else if (p.a_mn) {
 #pragma unroll
                                 for (int c = 0; c < BM / 32; ++c)
                                     tma_load_5d<CG>(sa + c * a_chunk_bytes, &p.tmA[h], fb,
@@ -314,7 +324,9 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             } else {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, k0, m0, a0, a1, a2);
                             }
-                            if (p.b_mn) {
+                            if (p.b_chunked) {
+                                tma_load_5d<CG>(sb, &p.tmB[h], fb, 0, k0, n0 >> 5, b0, b1);
+                            } else if (p.b_mn) {
 #pragma unroll
                                 for (int c = 0; c < S::B_COLS / 32; ++c)
                                     tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[h], fb,
@@ -496,32 +508,50 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             sum[c * 16 + j] = __fadd_rn(sum[c * 16 + j], __uint_as_float(r[j]));
                     }
                 } else {
+                    // This warp's 32 x 32 staging square: 128-byte rows whose
+                    // 16-byte chunks are XOR-swizzled by row, so both the
+                    // row-per-thread writes and the row-per-8-lanes reads
+                    // touch every bank once per 16-byte column.
+                    float* stg = reinterpret_cast<float*>(smem + STAGES * S::STAGE_BYTES + S::BAR_BYTES) +
+                                 (warp - 2) * 32 * 32;
+                    const int64_t row0 = row - lane;  // the warp's first output row
 #pragma unroll 1
                     for (int c = 0; c < S::EPI_COLS / 32; ++c) {
                         uint32_t r[32];
                         tmem_ld32(taddr + c * 32, r);
                         tmem_wait_ld();
-                        if (row < p.M) {
-                            const int col0 = n0 + c * 32;
+                        const int col0 = n0 + c * 32;
+                        if (p.vec_c && col0 + 32 <= p.N) {  // warp-uniform
+                            if (p.bias || p.apply_scale) {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j));
+                            }
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                *reinterpret_cast<uint4*>(stg + lane * 32 + ((j ^ (lane & 7)) << 2)) =
+                                    make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                            __syncwarp();
+                            const int sub = lane & 7;
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                const int rr = it * 4 + (lane >> 3);
+                                const float4 v =
+                                    *reinterpret_cast<const float4*>(stg + rr * 32 + ((sub ^ (rr & 7)) << 2));
+                                if (row0 + rr < p.M)
+                                    *reinterpret_cast<float4*>(p.C + oc + (row0 + rr) * p.c_rs + col0 + sub * 4) = v;
+                            }
+                            __syncwarp();
+                        } else if (row < p.M) {
                             if (p.bias || p.apply_scale) {
 #pragma unroll
                                 for (int j = 0; j < 32; ++j)
                                     if (col0 + j < p.N)
                                         r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j));
                             }
-                            if (p.vec_c && col0 + 32 <= p.N) {
 #pragma unroll
-                                for (int j = 0; j < 32; j += 4) {
-                                    float4 v = make_float4(
-                                        __uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                        __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                                    *reinterpret_cast<float4*>(crow + col0 + j) = v;
-                                }
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 32; ++j)
-                                    if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
-                            }
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
                         }
                     }
                 }
@@ -630,9 +660,15 @@ struct OperandMap {
     int64_t bstride[kMaxBatchDims];  // elements; 0 = broadcast
     uint32_t box_inner, box_outer;
     bool mn_major;  // MN-major TF32 tiles use 32-byte swizzle granules
+    // MN-major with inner % 32 == 0 and at most two batch dims: 32-wide chunks
+    // per box (the map steps over chunks in its third dim), else 0
+    uint32_t box_chunks;
 };
 
 int encode(CUtensorMap* map, const OperandMap& o) {
+    if (o.box_chunks)
+        return encode_chunked(map, o.base, o.inner, o.outer, o.outer_stride, o.bsz, o.bstride,
+                              o.box_outer, o.box_chunks, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     return encode_tiled(map, o.base, o.inner, o.outer, o.outer_stride, o.bsz, o.bstride,
                         o.box_inner, o.box_outer,
                         o.mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
@@ -814,6 +850,8 @@ void fill_common(TcParams& prm, const Gemm& g, const OperandMap& A, const Operan
     prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
     prm.a_mn = a_mn ? 1 : 0;
     prm.b_mn = b_mn ? 1 : 0;
+    prm.a_chunked = A.box_chunks ? 1 : 0;
+    prm.b_chunked = B.box_chunks ? 1 : 0;
     prm.vec_c = (al16(g.C) && (g.c_rs & 3) == 0) ? 1 : 0;
     for (int i = 0; i < g.nb; ++i)
         if (g.cbs[i] & 3) prm.vec_c = 0;
@@ -849,6 +887,12 @@ void operand_maps(const Gemm& g, bool a_mn, bool b_mn, OperandMap& A, OperandMap
     B.box_outer = b_mn ? BK : b_box_cols;
     A.mn_major = a_mn;
     B.mn_major = b_mn;
+    // Fewer, larger TMA boxes feed the tensor cores faster (measured: a
+    // 2048^3 batch with N-major B at 4 boxes per k-block runs 3-4 % slower
+    // than with K-major B at 1).  Whole 32-wide chunks only: a partial last
+    // chunk would read past the end of a row.
+    if (a_mn && g.M % 32 == 0 && g.nb <= 2) A.box_chunks = BM / 32;
+    if (b_mn && g.N % 32 == 0 && g.nb <= 2) B.box_chunks = b_box_cols / 32;
 }
 
 // B columns a CTA loads per stage for the variant launch_tc will pick.

@@ -104,6 +104,38 @@ inline int encode_tiled(CUtensorMap* map, const float* base, int64_t inner, int6
     return TLC_OK;
 }
 
+// An MN-major fp32 operand whose contiguous extent `inner` is a multiple of
+// 32, viewed as {32, outer, inner / 32, batch0, batch1}: the third dim steps
+// over 32-element (128-byte) column chunks.  One box {32, box_outer,
+// box_chunks} then lands in shared memory as box_chunks consecutive
+// [box_outer][32] tiles, the layout of box_chunks separate 32-wide loads, in
+// one TMA instruction.  At most two batch dims (the caller checks).
+inline int encode_chunked(CUtensorMap* map, const float* base, int64_t inner, int64_t outer,
+                          int64_t outer_stride, const int64_t* bsz, const int64_t* bstride,
+                          uint32_t box_outer, uint32_t box_chunks, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    if (inner % 32) return set_error(TLC_ERR_UNSUPPORTED, "chunked tensor map: inner extent % 32");
+    cuuint64_t dims[5] = {32, (cuuint64_t)outer, (cuuint64_t)(inner / 32), 1, 1};
+    cuuint64_t strides[4] = {(cuuint64_t)outer_stride * 4, 128, 0, 0};
+    cuuint32_t box[5] = {32, box_outer, box_chunks, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    cuuint64_t prev = strides[0] * dims[1];
+    for (int i = 0; i < 2; ++i) {
+        const bool real = bstride[i] != 0 && bsz[i] > 1;
+        dims[3 + i] = real ? (cuuint64_t)bsz[i] : 1;
+        strides[2 + i] = real ? (cuuint64_t)bstride[i] * 4 : ((prev + 15) & ~cuuint64_t(15));
+        prev = strides[2 + i] * dims[3 + i];
+    }
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TLC_ERR_UNSUPPORTED,
+                         "cuTensorMapEncodeTiled (chunked) failed (" + std::to_string((int)r) + ")");
+    return TLC_OK;
+}
+
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Whether TMA can read an operand in place: 16-byte aligned base and strides
