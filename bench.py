@@ -77,17 +77,63 @@ def peak_for(mode, peaks, src, sms, clock_mhz):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """SM clock, power and clock-event reasons sampled DURING the timed region.
+
+    NVML (pynvml) is polled every 5 ms from a thread; only the samples taken
+    between window_start() (just before the timed steps are enqueued) and
+    window_end() (after the closing synchronize) count, so a short timed
+    region is not drowned by idle samples around it.  Without pynvml,
+    nvidia-smi is polled every 50 ms with host timestamps instead."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+    Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
+        self.samples = []  # (host time, sm MHz, max MHz, power W, set of reasons)
+        self.t0 = self.t1 = None
+        self.thread = None
         self.proc = None
         self.f = None
 
+    def _nvml_handle(self, nv):
+        """The NVML device of CUDA device `index` (by UUID: NVML numbers GPUs
+        without regard to CUDA_VISIBLE_DEVICES)."""
+        try:
+            import torch
+            u = str(torch.cuda.get_device_properties(self.index).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-") else "GPU-" + u)
+        except Exception:  # noqa: BLE001
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _nvml_loop(self, nv, h, stop):
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception:  # noqa: BLE001 - a failed query ends sampling
+                return
+            self.samples.append((time.time(), sm, mx, pw,
+                                 {n for b, n in self.REASONS.items() if bits & b}))
+            time.sleep(0.005)
+
     def __enter__(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._nvml_handle(nv)
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, self.stop),
+                                           daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - no NVML binding or device: nvidia-smi below
+            self.thread = None
         try:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
@@ -99,46 +145,66 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def window_start(self):
+        self.t0 = time.time()
+
+    def window_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *a):
+        if self.thread:
+            self.stop.set()
+            self.thread.join(2)
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self._read_smi()
 
-    def summary(self, max_mhz_default):
-        if not self.proc or not self.f:
-            return {"sm_mhz": None, "sm_max_mhz": max_mhz_default, "reasons": ["unsampled"]}
-        self.f.flush()
-        rows = []
-        with open(self.f.name) as fh:
-            for line in fh:
-                p = [x.strip() for x in line.split(",")]
-                if len(p) >= 9:
-                    rows.append(p)
-        os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": max_mhz_default, "reasons": ["unsampled"]}
+    def _read_smi(self):
+        import datetime
 
         def num(x):
             try:
                 return float(x)
             except ValueError:
                 return None
-        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
-        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
-        pw = [v for v in (num(r[3]) for r in rows) if v is not None]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
+        with open(self.f.name) as fh:
+            for line in fh:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 8:
+                    continue
+                try:
+                    t = datetime.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+                self.samples.append((t, num(p[1]), num(p[2]), num(p[3]),
+                                     {n for n, v in zip(names, p[4:8]) if v.lower() == "active"}))
+        os.unlink(self.f.name)
+
+    def summary(self, max_mhz_default):
+        rows = self.samples
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+            if not inside:  # region shorter than one sampling interval: the next sample
+                after = [r for r in rows if r[0] >= self.t0]
+                inside = after[:1]
+            rows = inside
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": max_mhz_default, "reasons": ["unsampled"]}
+        sm = [r[1] for r in rows if r[1] is not None]
+        mx = [r[2] for r in rows if r[2] is not None]
+        pw = [r[3] for r in rows if r[3] is not None]
+        reasons = set().union(*(r[4] for r in rows))
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else max_mhz_default,
                 "power_w_max": max(pw) if pw else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows),
+                "source": "nvml" if self.thread else "nvidia-smi",
+                "window_ms": round((self.t1 - self.t0) * 1e3, 1) if self.t0 and self.t1 else None}
 
 
 def dist_setup():
@@ -171,11 +237,12 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
-def time_device(fn, steps, warmup, world, stream, count=None):
+def time_device(fn, steps, warmup, world, stream, count=None, clocks=None):
     """Per-step device time (ms): W warm-ups, then K steps between CUDA events
     on `stream`, bracketed by barrier + synchronize; max over ranks.  With
     `count` (a function returning a launch counter) also returns the number of
-    launches inside the timed region."""
+    launches inside the timed region; `clocks` (a ClockSampler) is told where
+    the timed region starts and ends."""
     import torch
     for _ in range(warmup):
         fn()
@@ -184,11 +251,15 @@ def time_device(fn, steps, warmup, world, stream, count=None):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     l0 = count() if count else 0
+    if clocks:
+        clocks.window_start()
     e0.record(stream)
     for _ in range(steps):
         fn()
     e1.record(stream)
     torch.cuda.synchronize()
+    if clocks:
+        clocks.window_end()
     l1 = count() if count else 0
     barrier(world)
     ms = e0.elapsed_time(e1) / steps
@@ -610,7 +681,7 @@ def run_ours(args):
         if mode == args.mode:
             with ClockSampler(local) as cs:
                 ms, launches = time_device(fn, args.steps, args.warmup, world, stream,
-                                           tlcuda.launch_count)
+                                           tlcuda.launch_count, clocks=cs)
             clocks = cs.summary(peaks.get("sm_max_mhz", 1965.0))
         else:
             ms, _ = time_device(fn, max(3, args.steps // 2), 3, world, stream)

@@ -50,3 +50,20 @@ def test_our_arm_line():
     assert e2e["value"] > 0 and e2e["h2d_bytes_per_step"] > 0 and e2e["d2h_bytes_per_step"] > 0
     assert line["gpu_launches"] >= line["steps"]
     assert "sm_mhz" in line["clocks"] and "reasons" in line["clocks"]
+
+
+def test_clock_window_keeps_only_timed_samples():
+    """The clock record counts only samples inside the timed region; a region
+    shorter than one sampling interval takes the first sample after its start."""
+    sys.path.insert(0, REPO)
+    import bench
+    cs = bench.ClockSampler(0)
+    cs.samples = [(0.0, 1965, 1965, 200.0, set()), (1.0, 1400, 1965, 990.0, {"sw_power_cap"}),
+                  (2.0, 1300, 1965, 995.0, {"sw_power_cap"}), (3.0, 1965, 1965, 210.0, set())]
+    cs.t0, cs.t1 = 0.5, 2.5
+    s = cs.summary(1965.0)
+    assert s["samples"] == 2 and s["sm_mhz"] == 1350 and s["reasons"] == ["sw_power_cap"]
+    assert s["power_w_max"] == 995.0
+    cs.t0, cs.t1 = 2.2, 2.3
+    s = cs.summary(1965.0)
+    assert s["samples"] == 1 and s["sm_mhz"] == 1965 and s["reasons"] == []
