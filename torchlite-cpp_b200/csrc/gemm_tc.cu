@@ -1,15 +1,19 @@
 // Tensor-core GEMM for TLC_MODE_TF32 and TLC_MODE_3XTF32 on sm_100a (tcgen05).
 //
 // Persistent, warp-specialised kernel; 6 warps per CTA (10 for 3xTF32):
-//   warp 0      TMA producer: one elected thread streams A and B k-blocks
-//               (32 fp32 = 128 bytes of k) into a ring of shared-memory stages
-//               with cp.async.bulk.tensor (128-byte swizzle), completion
-//               tracked by an mbarrier per stage (expect_tx bytes).
-//   warp 1      TMEM allocation; one elected thread of the leader CTA issues
-//               tcgen05.mma.kind::tf32 (K = 8 per instruction, 4 per k-block
-//               and product) into an fp32 accumulator in tensor memory;
-//               tcgen05.commit frees each stage and publishes each finished
-//               accumulator.
+//   warp 0      TMA producer: the warp waits for free stages together and one
+//               elected lane streams A and B k-blocks (32 fp32 = 128 bytes of
+//               k) into a ring of shared-memory stages with
+//               cp.async.bulk.tensor (128-byte swizzle), completion tracked by
+//               an mbarrier per stage (expect_tx bytes).
+//   warp 1      TMEM allocation; in the leader CTA the whole warp runs the MMA
+//               loop, every lane polling the stage barriers, and one elected
+//               lane issues tcgen05.mma.kind::tf32 (K = 8 per instruction, 4
+//               per k-block and product) into an fp32 accumulator in tensor
+//               memory; tcgen05.commit from the same lane frees each stage and
+//               publishes each finished accumulator.  (Issued by lane 0 alone
+//               in a divergent branch, the same loop loses ~100-300 cycles of
+//               tensor-pipe time at every commit: measured.)
 //   warps 2..   epilogue: tcgen05.ld the accumulator (each thread one row of
 //               128; with 8 epilogue warps, half a row), store fp32 C.
 // The accumulator is double-buffered in TMEM, so the epilogue of one tile
@@ -275,7 +279,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
-        if (lane == 0) {
+        {
             int stage = 0;
             uint32_t phase = 0;
             // Bit s of pend: a load was issued into stage s and nobody has seen
@@ -296,7 +300,8 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                 KbIter it;
                 it.start(p);
                 for (int kb = 0; kb < p.k_blocks;) {
-                    if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1, kGemmSleepNs)) {
+                    if (!warp_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 1,
+                                           kGemmSleepNs)) {
                         ok = false;
                         break;
                     }
@@ -306,9 +311,10 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     const int nsub = min(S::SUBS, it.left_in_chunk());
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
-                    if (leader) mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
+                    if (leader && elect_one()) mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
                     for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
                         const int k0 = it.kb() * BK;
+                        if (!elect_one()) continue;
 #pragma unroll
                         for (int h = 0; h < (X3 ? 2 : 1); ++h) {  // X3: hi, then lo planes
                             uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
@@ -344,7 +350,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     }
                 }
             }
-            if (!ok && leader) {
+            if (!ok && leader && lane == 0) {
                 // Drain: wait (bounded) for loads still in flight into shared memory
                 // (the leader's full barriers count both CTAs' bytes).
                 for (int s = 0; s < STAGES; ++s) {
@@ -358,7 +364,9 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA) ----------------
-        if (lane == 0 && leader) {
+        // The whole warp runs the loop; each tcgen05 operation comes from one
+        // elected lane (elect_one), the waits from lane 0 (warp_wait_bounded).
+        if (leader) {
             // kind::tf32: D fp32 (bits 4-5 = 1), A/B TF32 (bits 7-9, 10-12 = 2),
             // A/B major (bits 15, 16), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
             const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) |
@@ -396,15 +404,16 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     const int nsub = min(S::SUBS, it.left_in_chunk());
                     if (it.first()) {
                         // a fresh accumulator for this chunk, once the epilogues drained it
-                        if (!wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag,
-                                          p.timeout_ns, p.err, 2, kGemmSleepNs)) {
+                        if (!warp_wait_bounded(&tempty[acc], ((acc_ph >> acc) & 1u) ^ 1u, abort_flag,
+                                               p.timeout_ns, p.err, 2, kGemmSleepNs)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         d = tmem_base + (uint32_t)(acc * UN);
                     }
-                    if (!wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3, kGemmSleepNs)) {
+                    if (!warp_wait_bounded(&full[stage], phase, abort_flag, p.timeout_ns, p.err, 3,
+                                           kGemmSleepNs)) {
                         ok = false;
                         break;
                     }
@@ -420,49 +429,59 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             // lo(A).hi(B) + hi(A).lo(B) + hi(A).hi(B): small terms first
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                umma_tf32<CG>(d, ad + lo_off + j * a_step, bd + j * b_step, idesc,
-                                              (!first || j > 0) ? 1u : 0u);
+                                if (elect_one())
+                                    umma_tf32<CG>(d, ad + lo_off + j * a_step, bd + j * b_step, idesc,
+                                                  (!first || j > 0) ? 1u : 0u);
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                umma_tf32<CG>(d, ad + j * a_step, bd + lo_off + j * b_step, idesc, 1u);
+                                if (elect_one())
+                                    umma_tf32<CG>(d, ad + j * a_step, bd + lo_off + j * b_step, idesc, 1u);
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc, 1u);
+                                if (elect_one())
+                                    umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc, 1u);
                         } else {
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
-                                              (!first || j > 0) ? 1u : 0u);
+                                if (elect_one())
+                                    umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
+                                                  (!first || j > 0) ? 1u : 0u);
                         }
                     }
                     issued = true;
                     // free the stage in every CTA once these MMAs finish
-                    if constexpr (CG == 2)
-                        umma_commit_both(empty_addr + 8u * stage);
-                    else
-                        umma_commit<CG>(empty_addr + 8u * stage);
+                    if (elect_one()) {
+                        if constexpr (CG == 2)
+                            umma_commit_both(empty_addr + 8u * stage);
+                        else
+                            umma_commit<CG>(empty_addr + 8u * stage);
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                     if (chunk_end) {
                         // chunk accumulator ready for the epilogues of both CTAs
-                        if constexpr (CG == 2)
-                            umma_commit_both(smem_u32(&tfull[acc]));
-                        else
-                            umma_commit<CG>(smem_u32(&tfull[acc]));
+                        if (elect_one()) {
+                            if constexpr (CG == 2)
+                                umma_commit_both(smem_u32(&tfull[acc]));
+                            else
+                                umma_commit<CG>(smem_u32(&tfull[acc]));
+                        }
                         acc_ph ^= 1u << acc;
                         acc ^= 1;
                     }
                 }
             }
-            if (!ok && issued) {
-                // Drain MMAs still reading shared memory / writing TMEM.
+            if (!ok && issued && elect_one()) {
+                // Drain MMAs still reading shared memory / writing TMEM (the
+                // elected lane is the one that issued them).
                 umma_commit<CG>(smem_u32(drain));
                 const uint64_t t0 = globaltimer();
                 while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < p.timeout_ns) {
                 }
             }
+            __syncwarp();
         }
     } else {
         // ---------------- epilogue (warps 2.., both CTAs) ----------------
@@ -489,9 +508,8 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
 #pragma unroll
             for (int j = 0; j < (X3 ? S::EPI_COLS : 1); ++j) sum[j] = 0.0f;
             for (int ch = 0; ch < p.num_chunks; ++ch) {
-                if (lane == 0)
-                    ok = wait_bounded(&tfull[acc], (acc_ph >> acc) & 1u, abort_flag, p.timeout_ns, p.err, 4, kGemmSleepNs);
-                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;  // one branch per warp
+                ok = warp_wait_bounded(&tfull[acc], (acc_ph >> acc) & 1u, abort_flag, p.timeout_ns,
+                                       p.err, 4, kGemmSleepNs);  // one branch per warp
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) +
