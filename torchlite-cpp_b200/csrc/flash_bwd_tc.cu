@@ -107,12 +107,11 @@ __device__ __forceinline__ bool wait_b(uint64_t* bar, uint32_t parity, volatile 
     return wait_bounded(bar, parity, abort_flag, kTimeoutNs, p.err, site, kSleep);
 }
 
-// lane 0 waits, the warp follows
+// every lane of the warp waits (measured faster than lane 0 polling and
+// sharing its result with a shuffle); true only if all succeeded
 __device__ __forceinline__ bool warp_wait_b(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                             const BwdParams& p, int site) {
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = wait_b(bar, parity, abort_flag, p, site);
-    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    return warp_wait_bounded(bar, parity, abort_flag, kTimeoutNs, p.err, site, kSleep);
 }
 
 // Shared-memory descriptor of k-step s (8 columns of 4 bytes) of a K-major
@@ -225,61 +224,67 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
+        // the warp waits together; one elected lane issues the copies
+        {
             uint32_t pend = 0, par = 0;
             bool ok = true;
             for (int i = 0; i < p.nblk; ++i) {
                 const int st = i % QST;
                 const uint32_t ph = (uint32_t)(i / QST) & 1u;
-                if (!wait_b(&q_empty[st], ph ^ 1u, abort_flag, p, 41)) {
+                if (!warp_wait_b(&q_empty[st], ph ^ 1u, abort_flag, p, 41)) {
                     ok = false;
                     break;
                 }
                 pend &= ~(1u << st);
                 uint8_t* sb = smem + DKV_OFF_RING + st * DKV_STAGE;
-                mbar_expect_tx(&q_full[st], 4 * TILE64 + 2 * TB * 4);
-                const uint32_t fb = smem_u32(&q_full[st]);
-                for (int c = 0; c < 2; ++c) {
-                    tma_load_5d<1>(sb + c * (TILE64 / 2), &p.m[2], fb, 32 * c, i * TB, head, 0, 0);
-                    tma_load_5d<1>(sb + TILE64 + c * (TILE64 / 2), &p.m[3], fb, 32 * c, i * TB, head, 0, 0);
-                    tma_load_5d<1>(sb + 2 * TILE64 + c * (TILE64 / 2), &p.m[4], fb, 32 * c, i * TB, head, 0, 0);
-                    tma_load_5d<1>(sb + 3 * TILE64 + c * (TILE64 / 2), &p.m[5], fb, 32 * c, i * TB, head, 0, 0);
+                if (elect_one()) {
+                    mbar_expect_tx(&q_full[st], 4 * TILE64 + 2 * TB * 4);
+                    const uint32_t fb = smem_u32(&q_full[st]);
+                    for (int c = 0; c < 2; ++c) {
+                        tma_load_5d<1>(sb + c * (TILE64 / 2), &p.m[2], fb, 32 * c, i * TB, head, 0, 0);
+                        tma_load_5d<1>(sb + TILE64 + c * (TILE64 / 2), &p.m[3], fb, 32 * c, i * TB, head, 0, 0);
+                        tma_load_5d<1>(sb + 2 * TILE64 + c * (TILE64 / 2), &p.m[4], fb, 32 * c, i * TB, head, 0, 0);
+                        tma_load_5d<1>(sb + 3 * TILE64 + c * (TILE64 / 2), &p.m[5], fb, 32 * c, i * TB, head, 0, 0);
+                    }
+                    const int64_t lo = (int64_t)head * p.S_pad + (int64_t)i * TB;
+                    bulk_load(sb + 4 * TILE64, p.L2 + lo, TB * 4, &q_full[st]);
+                    bulk_load(sb + 4 * TILE64 + TB * 4, p.D + lo, TB * 4, &q_full[st]);
                 }
-                const int64_t lo = (int64_t)head * p.S_pad + (int64_t)i * TB;
-                bulk_load(sb + 4 * TILE64, p.L2 + lo, TB * 4, &q_full[st]);
-                bulk_load(sb + 4 * TILE64 + TB * 4, p.D + lo, TB * 4, &q_full[st]);
                 pend |= 1u << st;
                 par = (par & ~(1u << st)) | (ph << st);
             }
-            if (!ok)
+            if (!ok && lane == 0)
                 for (int s = 0; s < QST; ++s)
                     if (pend & (1u << s)) drain_full(&q_full[s], (par >> s) & 1u);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // The whole warp runs the loop, every lane polling the barriers; one
+        // elected lane issues each MMA and commit (a lone lane in a divergent
+        // branch leaves the tensor pipe idle after each commit: measured).
+        {
             const uint64_t r_kdesc = smem_desc(smem_u32(smem + DKV_OFF_RING), 16, 1024, kSw128);
             const uint64_t r_mdesc = smem_desc(smem_u32(smem + DKV_OFF_RING), TILE64 / 2, 512, kSw128Atom32);
-            bool ok = wait_b(a_full, 0, abort_flag, p, 42);
+            bool ok = warp_wait_b(a_full, 0, abort_flag, p, 42);
             bool issued = false;
             // S^T = K . Q_i^T and dP^T = V . dO_i^T (A = K, V in TMEM) into buffer i % NB
             auto issue_s = [&](int i) -> bool {
                 const int b = i % NB, st = i % QST;
-                if (!wait_b(&q_full[st], (uint32_t)(i / QST) & 1u, abort_flag, p, 43)) return false;
-                if (!wait_b(&s_empty[b], ((uint32_t)(i / NB) & 1u) ^ 1u, abort_flag, p, 44)) return false;
+                if (!warp_wait_b(&q_full[st], (uint32_t)(i / QST) & 1u, abort_flag, p, 43)) return false;
+                if (!warp_wait_b(&s_empty[b], ((uint32_t)(i / NB) & 1u) ^ 1u, abort_flag, p, 44)) return false;
                 tc_fence_after();
                 const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
                 const uint32_t ds = tmem_base + (uint32_t)(S_COL + b * TB), dp = tmem_base + (uint32_t)(DP_COL + b * TB);
 #pragma unroll
                 for (int s = 0; s < BD / 8; ++s)
-                    umma_tf32_tmem_a(ds, tmem_base + (uint32_t)(A0_COL + 8 * s),
+                    if (elect_one()) umma_tf32_tmem_a(ds, tmem_base + (uint32_t)(A0_COL + 8 * s),
                                      kmajor_step(r_kdesc + soff, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
 #pragma unroll
                 for (int s = 0; s < BD / 8; ++s)
-                    umma_tf32_tmem_a(dp, tmem_base + (uint32_t)(A1_COL + 8 * s),
+                    if (elect_one()) umma_tf32_tmem_a(dp, tmem_base + (uint32_t)(A1_COL + 8 * s),
                                      kmajor_step(r_kdesc + soff + (uint32_t)((2 * TILE64) >> 4), TILE64 / 2, s),
                                      kIdescKK, s > 0 ? 1u : 0u);
-                umma_commit<1>(smem_u32(&s_full[b]));
+                if (elect_one()) umma_commit<1>(smem_u32(&s_full[b]));
                 issued = true;
                 return true;
             };
@@ -290,7 +295,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
             for (int i = 0; ok && i < p.nblk; ++i) {
                 const int b = i % NB, st = i % QST;
                 if (i + 1 < p.nblk) ok = issue_s(i + 1);
-                if (ok) ok = wait_b(&e_full[b], (uint32_t)(i / NB) & 1u, abort_flag, p, 45);
+                if (ok) ok = warp_wait_b(&e_full[b], (uint32_t)(i / NB) & 1u, abort_flag, p, 45);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
@@ -298,22 +303,23 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
                 // dV += P^T . dO_i (B = dO MN-major), dK += dS^T . Q_i (B = Q MN-major)
 #pragma unroll
                 for (int s = 0; s < TB / 8; ++s)
-                    umma_tf32_tmem_a(tmem_base + (uint32_t)ACC0_COL, pa + 8 * s,
+                    if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)ACC0_COL, pa + 8 * s,
                                      mnmajor_step(r_mdesc + soff + (uint32_t)((3 * TILE64) >> 4), s), kIdescKM,
                                      (i > 0 || s > 0) ? 1u : 0u);
 #pragma unroll
                 for (int s = 0; s < TB / 8; ++s)
-                    umma_tf32_tmem_a(tmem_base + (uint32_t)ACC1_COL, dsa + 8 * s,
+                    if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)ACC1_COL, dsa + 8 * s,
                                      mnmajor_step(r_mdesc + soff + (uint32_t)(TILE64 >> 4), s), kIdescKM,
                                      (i > 0 || s > 0) ? 1u : 0u);
-                umma_commit<1>(smem_u32(&s_empty[b]));
-                umma_commit<1>(smem_u32(&q_empty[st]));
+                if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
+                if (elect_one()) umma_commit<1>(smem_u32(&q_empty[st]));
             }
-            if (ok) umma_commit<1>(smem_u32(acc_full));
-            if (!ok && issued) {
+            if (ok) if (elect_one()) umma_commit<1>(smem_u32(acc_full));
+            if (!ok && issued && elect_one()) {
                 umma_commit<1>(smem_u32(drain));
                 drain_full(drain, 0);
             }
+            __syncwarp();
         }
     } else {
         // ---------------- elementwise (warps 2-17) ----------------
@@ -469,60 +475,66 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
+        // the warp waits together; one elected lane issues the copies
+        {
             uint32_t pend = 0, par = 0;
             bool ok = true;
             for (int j = 0; j < p.nblk; ++j) {
                 const int st = j % KST;
                 const uint32_t ph = (uint32_t)(j / KST) & 1u;
-                if (!wait_b(&k_empty[st], ph ^ 1u, abort_flag, p, 51)) {
+                if (!warp_wait_b(&k_empty[st], ph ^ 1u, abort_flag, p, 51)) {
                     ok = false;
                     break;
                 }
                 pend &= ~(1u << st);
                 uint8_t* sb = smem + DQ_OFF_RING + st * DQ_STAGE;
-                mbar_expect_tx(&k_full[st], DQ_STAGE);
-                const uint32_t fb = smem_u32(&k_full[st]);
-                for (int c = 0; c < 2; ++c) {
-                    tma_load_5d<1>(sb + c * (TILE64 / 2), &p.m[2], fb, 32 * c, j * TB, head, 0, 0);
-                    tma_load_5d<1>(sb + TILE64 + c * (TILE64 / 2), &p.m[3], fb, 32 * c, j * TB, head, 0, 0);
-                    tma_load_5d<1>(sb + 2 * TILE64 + c * (TILE64 / 2), &p.m[4], fb, 32 * c, j * TB, head, 0, 0);
+                if (elect_one()) {
+                    mbar_expect_tx(&k_full[st], DQ_STAGE);
+                    const uint32_t fb = smem_u32(&k_full[st]);
+                    for (int c = 0; c < 2; ++c) {
+                        tma_load_5d<1>(sb + c * (TILE64 / 2), &p.m[2], fb, 32 * c, j * TB, head, 0, 0);
+                        tma_load_5d<1>(sb + TILE64 + c * (TILE64 / 2), &p.m[3], fb, 32 * c, j * TB, head, 0, 0);
+                        tma_load_5d<1>(sb + 2 * TILE64 + c * (TILE64 / 2), &p.m[4], fb, 32 * c, j * TB, head, 0, 0);
+                    }
                 }
                 pend |= 1u << st;
                 par = (par & ~(1u << st)) | (ph << st);
             }
-            if (!ok)
+            if (!ok && lane == 0)
                 for (int s = 0; s < KST; ++s)
                     if (pend & (1u << s)) drain_full(&k_full[s], (par >> s) & 1u);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // The whole warp runs the loop, every lane polling the barriers; one
+        // elected lane issues each MMA and commit (a lone lane in a divergent
+        // branch leaves the tensor pipe idle after each commit: measured).
+        {
             const uint64_t r_kdesc = smem_desc(smem_u32(smem + DQ_OFF_RING), 16, 1024, kSw128);
             const uint64_t r_mdesc = smem_desc(smem_u32(smem + DQ_OFF_RING), TILE64 / 2, 512, kSw128Atom32);
-            bool ok = wait_b(a_full, 0, abort_flag, p, 52);
+            bool ok = warp_wait_b(a_full, 0, abort_flag, p, 52);
             bool issued = false;
             // S = Q . K_j^T and dP = dO . V_j^T (A = Q, dO in TMEM) into score buffer
             // j % DQ_NS and dP buffer j % DQ_NDP
             auto issue_s = [&](int j) -> bool {
                 const int b = j % DQ_NS, pb = j % DQ_NDP, st = j % KST;
-                if (!wait_b(&k_full[st], (uint32_t)(j / KST) & 1u, abort_flag, p, 53)) return false;
-                if (!wait_b(&s_empty[b], ((uint32_t)(j / DQ_NS) & 1u) ^ 1u, abort_flag, p, 54)) return false;
-                if (!wait_b(&dp_empty[pb], ((uint32_t)(j / DQ_NDP) & 1u) ^ 1u, abort_flag, p, 58)) return false;
+                if (!warp_wait_b(&k_full[st], (uint32_t)(j / KST) & 1u, abort_flag, p, 53)) return false;
+                if (!warp_wait_b(&s_empty[b], ((uint32_t)(j / DQ_NS) & 1u) ^ 1u, abort_flag, p, 54)) return false;
+                if (!warp_wait_b(&dp_empty[pb], ((uint32_t)(j / DQ_NDP) & 1u) ^ 1u, abort_flag, p, 58)) return false;
                 tc_fence_after();
                 const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
                 const uint32_t ds = tmem_base + (uint32_t)(DQ_S_COL + b * TB),
                                dp = tmem_base + (uint32_t)(DQ_DP_COL + pb * TB);
 #pragma unroll
                 for (int s = 0; s < BD / 8; ++s)
-                    umma_tf32_tmem_a(ds, tmem_base + (uint32_t)(A0_COL + 8 * s),
+                    if (elect_one()) umma_tf32_tmem_a(ds, tmem_base + (uint32_t)(A0_COL + 8 * s),
                                      kmajor_step(r_kdesc + soff, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
 #pragma unroll
                 for (int s = 0; s < BD / 8; ++s)
-                    umma_tf32_tmem_a(dp, tmem_base + (uint32_t)(A1_COL + 8 * s),
+                    if (elect_one()) umma_tf32_tmem_a(dp, tmem_base + (uint32_t)(A1_COL + 8 * s),
                                      kmajor_step(r_kdesc + soff + (uint32_t)(TILE64 >> 4), TILE64 / 2, s),
                                      kIdescKK, s > 0 ? 1u : 0u);
-                umma_commit<1>(smem_u32(&s_full[b]));
+                if (elect_one()) umma_commit<1>(smem_u32(&s_full[b]));
                 issued = true;
                 return true;
             };
@@ -533,7 +545,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
             for (int j = 0; ok && j < p.nblk; ++j) {
                 const int b = j % DQ_NS, st = j % KST;
                 if (j + 1 < p.nblk) ok = issue_s(j + 1);
-                if (ok) ok = wait_b(&e_full[b], (uint32_t)(j / DQ_NS) & 1u, abort_flag, p, 55);
+                if (ok) ok = warp_wait_b(&e_full[b], (uint32_t)(j / DQ_NS) & 1u, abort_flag, p, 55);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
@@ -541,17 +553,18 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
                 // dQ += dS . K_j (A = dS in TMEM, B = K MN-major)
 #pragma unroll
                 for (int s = 0; s < TB / 8; ++s)
-                    umma_tf32_tmem_a(tmem_base + (uint32_t)DQ_ACC_COL, dsa + 8 * s,
+                    if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)DQ_ACC_COL, dsa + 8 * s,
                                      mnmajor_step(r_mdesc + soff + (uint32_t)((2 * TILE64) >> 4), s), kIdescKM,
                                      (j > 0 || s > 0) ? 1u : 0u);
-                umma_commit<1>(smem_u32(&s_empty[b]));
-                umma_commit<1>(smem_u32(&k_empty[st]));
+                if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
+                if (elect_one()) umma_commit<1>(smem_u32(&k_empty[st]));
             }
-            if (ok) umma_commit<1>(smem_u32(acc_full));
-            if (!ok && issued) {
+            if (ok) if (elect_one()) umma_commit<1>(smem_u32(acc_full));
+            if (!ok && issued && elect_one()) {
                 umma_commit<1>(smem_u32(drain));
                 drain_full(drain, 0);
             }
+            __syncwarp();
         }
     } else {
         // ---------------- elementwise (warps 2-17) ----------------

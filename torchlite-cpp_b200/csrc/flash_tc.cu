@@ -98,12 +98,11 @@ __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Waits like wait_bounded, for a whole warp: lane 0 polls, the warp follows.
+// Waits like wait_bounded, for a whole warp: every lane polls (measured
+// faster than lane 0 polling and sharing its result with a shuffle).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           const FtParams& p, int site) {
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = wait_bounded(bar, parity, abort_flag, p.timeout_ns, p.err, site, kSleepSm);
-    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    return warp_wait_bounded(bar, parity, abort_flag, p.timeout_ns, p.err, site, kSleepSm);
 }
 
 __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_constant__ FtParams p) {
@@ -168,36 +167,41 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
+        // The warp waits together; one elected lane issues (as in the GEMM).
+        {
             uint32_t pend_k = 0, par_k = 0, pend_v = 0, par_v = 0;
             bool ok = true;
             for (int j = 0; ok && j < p.nk; ++j) {
                 const int ks = j % KST, vs = j % VST;
                 const uint32_t kph = (uint32_t)(j / KST) & 1u, vph = (uint32_t)(j / VST) & 1u;
-                if (!wait_bounded(&k_empty[ks], kph ^ 1u, abort_flag, p.timeout_ns, p.err, 21, kSleepNs)) {
+                if (!warp_wait_bounded(&k_empty[ks], kph ^ 1u, abort_flag, p.timeout_ns, p.err, 21, kSleepNs)) {
                     ok = false;
                     break;
                 }
                 pend_k &= ~(1u << ks);
-                mbar_expect_tx(&k_full[ks], K_BYTES);
-                for (int c = 0; c < FD / 32; ++c)
-                    tma_load_5d<1>(smem + OFF_K + ks * K_BYTES + c * (K_BYTES / 2), &p.tmK,
-                                   smem_u32(&k_full[ks]), 32 * c, j * FK, head, 0, 0);
+                if (elect_one()) {
+                    mbar_expect_tx(&k_full[ks], K_BYTES);
+                    for (int c = 0; c < FD / 32; ++c)
+                        tma_load_5d<1>(smem + OFF_K + ks * K_BYTES + c * (K_BYTES / 2), &p.tmK,
+                                       smem_u32(&k_full[ks]), 32 * c, j * FK, head, 0, 0);
+                }
                 pend_k |= 1u << ks;
                 par_k = (par_k & ~(1u << ks)) | (kph << ks);
-                if (!wait_bounded(&v_empty[vs], vph ^ 1u, abort_flag, p.timeout_ns, p.err, 22, kSleepNs)) {
+                if (!warp_wait_bounded(&v_empty[vs], vph ^ 1u, abort_flag, p.timeout_ns, p.err, 22, kSleepNs)) {
                     ok = false;
                     break;
                 }
                 pend_v &= ~(1u << vs);
-                mbar_expect_tx(&v_full[vs], V_BYTES);
-                for (int c = 0; c < FD / 32; ++c)
-                    tma_load_5d<1>(smem + OFF_V + vs * V_BYTES + c * (V_BYTES / 2), &p.tmV,
-                                   smem_u32(&v_full[vs]), 32 * c, j * FK, head, 0, 0);
+                if (elect_one()) {
+                    mbar_expect_tx(&v_full[vs], V_BYTES);
+                    for (int c = 0; c < FD / 32; ++c)
+                        tma_load_5d<1>(smem + OFF_V + vs * V_BYTES + c * (V_BYTES / 2), &p.tmV,
+                                       smem_u32(&v_full[vs]), 32 * c, j * FK, head, 0, 0);
+                }
                 pend_v |= 1u << vs;
                 par_v = (par_v & ~(1u << vs)) | (vph << vs);
             }
-            if (!ok) {
+            if (!ok && lane == 0) {
                 // loads still in flight land before the CTA frees anything
                 for (int s = 0; s < KST; ++s)
                     if (pend_k & (1u << s)) {
@@ -221,7 +225,10 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         // the tiles share only the K and V rings, whose empty barriers take a
         // commit from both.
         const int mt = warp == 1 ? 0 : 1;
-        if (lane == 0) {
+        // The whole warp runs the chain, every lane polling the barriers; one
+        // elected lane issues each MMA and commit (a lone lane in a divergent
+        // branch leaves the tensor pipe idle after each commit: measured).
+        {
             // kind::tf32, fp32 D; N = 64 (bits 17-22, >> 3), M = 128 (bits 24-28, >> 4);
             // S: A (Q) and B (K) K-major; P.V: A (P, in TMEM) K-major, B (V) MN-major (bit 16).
             const uint32_t idesc_s = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(FK >> 3) << 17) |
@@ -232,15 +239,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             // moves the start-address field (address >> 4)
             const uint64_t k_desc = smem_desc(smem_u32(smem + OFF_K), 16, 1024, kSw128);
             const uint64_t v_desc = smem_desc(smem_u32(smem + OFF_V), V_BYTES / 2, 512, kSw128Atom32);
-            bool ok = wait_bounded(&a_full[mt], 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
+            bool ok = warp_wait_bounded(&a_full[mt], 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
             bool issued = false;
             tc_fence_after();
             // S_t(j) = Q_t . K_j^T into buffer (t, j % SPB): 8 MMAs of K = 8 over d = 64,
             // once the P.V that last read that buffer is done
             auto issue_s = [&](int t, int j) -> bool {
                 const int b = j % SPB;
-                if (!wait_bounded(&s_empty[SPB * t + b], ((uint32_t)(j / SPB) & 1u) ^ 1u, abort_flag,
-                                  p.timeout_ns, p.err, 24, kSleepMma))
+                if (!warp_wait_bounded(&s_empty[SPB * t + b], ((uint32_t)(j / SPB) & 1u) ^ 1u, abort_flag,
+                                       p.timeout_ns, p.err, 24, kSleepMma))
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + SP_COL + b * FK);
@@ -250,10 +257,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 // memory runs at about a third of this rate
 #pragma unroll
                 for (int s = 0; s < FD / 8; ++s)
+                    if (elect_one())
                     umma_tf32_tmem_a(d, qa + 8 * s,
                                      kd + (uint32_t)(((s >> 2) * (K_BYTES / 2) + (s & 3) * 32) >> 4), idesc_s,
                                      s > 0 ? 1u : 0u);
-                umma_commit<1>(smem_u32(&s_full[SPB * t + b]));
+                if (elect_one()) umma_commit<1>(smem_u32(&s_full[SPB * t + b]));
                 issued = true;
                 return true;
             };
@@ -262,8 +270,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             // (the first block's first MMA starts O from zero)
             auto issue_pv = [&](int t, int j) -> bool {
                 const int b = j % SPB;
-                if (!wait_bounded(&p_full[SPB * t + b], (uint32_t)(j / SPB) & 1u, abort_flag, p.timeout_ns,
-                                  p.err, 25, kSleepMma))
+                if (!warp_wait_bounded(&p_full[SPB * t + b], (uint32_t)(j / SPB) & 1u, abort_flag,
+                                       p.timeout_ns, p.err, 25, kSleepMma))
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + O_COL);
@@ -271,36 +279,40 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 const uint64_t vd = v_desc + (uint32_t)(((j % VST) * V_BYTES) >> 4);
 #pragma unroll
                 for (int s = 0; s < FK / 8; ++s)
+                    if (elect_one())
                     umma_tf32_tmem_a(d, pa + 8 * s, vd + (uint32_t)((s * 1024) >> 4), idesc_pv,
                                      (j > 0 || s > 0) ? 1u : 0u);
-                umma_commit<1>(smem_u32(&o_full[t]));
-                umma_commit<1>(smem_u32(&s_empty[SPB * t + b]));
+                if (elect_one()) {
+                    umma_commit<1>(smem_u32(&o_full[t]));
+                    umma_commit<1>(smem_u32(&s_empty[SPB * t + b]));
+                }
                 issued = true;
                 return true;
             };
-            if (ok) ok = wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27, kSleepMma);
+            if (ok) ok = warp_wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27, kSleepMma);
             if (ok) tc_fence_after();
             if (ok) ok = issue_s(mt, 0);
-            if (ok) umma_commit<1>(smem_u32(&k_empty[0]));
+            if (ok && elect_one()) umma_commit<1>(smem_u32(&k_empty[0]));
             for (int j = 0; ok && j < p.nk; ++j) {
                 if (j + 1 < p.nk) {  // the next block's scores, one block ahead
                     const int ks = (j + 1) % KST;
-                    ok = wait_bounded(&k_full[ks], (uint32_t)((j + 1) / KST) & 1u, abort_flag,
-                                      p.timeout_ns, p.err, 28, kSleepMma);
+                    ok = warp_wait_bounded(&k_full[ks], (uint32_t)((j + 1) / KST) & 1u, abort_flag,
+                                           p.timeout_ns, p.err, 28, kSleepMma);
                     if (ok) ok = issue_s(mt, j + 1);
-                    if (ok) umma_commit<1>(smem_u32(&k_empty[ks]));
+                    if (ok && elect_one()) umma_commit<1>(smem_u32(&k_empty[ks]));
                 }
-                if (ok) ok = wait_bounded(&v_full[j % VST], (uint32_t)(j / VST) & 1u, abort_flag,
-                                          p.timeout_ns, p.err, 29, kSleepMma);
+                if (ok) ok = warp_wait_bounded(&v_full[j % VST], (uint32_t)(j / VST) & 1u, abort_flag,
+                                               p.timeout_ns, p.err, 29, kSleepMma);
                 if (ok) ok = issue_pv(mt, j);
-                if (ok) umma_commit<1>(smem_u32(&v_empty[j % VST]));
+                if (ok && elect_one()) umma_commit<1>(smem_u32(&v_empty[j % VST]));
             }
-            if (!ok && issued) {
+            if (!ok && issued && elect_one()) {
                 umma_commit<1>(smem_u32(&drain[mt]));
                 const uint64_t t0 = globaltimer();
                 while (!mbar_try_wait(&drain[mt], 0) && globaltimer() - t0 < p.timeout_ns) {
                 }
             }
+            __syncwarp();
         }
     } else {
         // ---------------- softmax (warps 2-9: tile 0, 10-17: tile 1) ----------------
