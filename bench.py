@@ -108,17 +108,20 @@ class ClockSampler:
         except Exception:  # noqa: BLE001
             return nv.nvmlDeviceGetHandleByIndex(self.index)
 
-    def _nvml_loop(self, nv, h, stop):
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    def _nvml_sample(self):
+        nv, h = self.nv, self.h
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.samples.append((time.time(), sm, self.mx, pw,
+                             {n for b, n in self.REASONS.items() if bits & b}))
+
+    def _nvml_loop(self, stop):
         while not stop.is_set():
             try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
-                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self._nvml_sample()
             except Exception:  # noqa: BLE001 - a failed query ends sampling
                 return
-            self.samples.append((time.time(), sm, mx, pw,
-                                 {n for b, n in self.REASONS.items() if bits & b}))
             time.sleep(0.005)
 
     def __enter__(self):
@@ -126,10 +129,10 @@ class ClockSampler:
             import threading
             import pynvml as nv
             nv.nvmlInit()
-            h = self._nvml_handle(nv)
+            self.nv, self.h = nv, self._nvml_handle(nv)
+            self.mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
             self.stop = threading.Event()
-            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, self.stop),
-                                           daemon=True)
+            self.thread = threading.Thread(target=self._nvml_loop, args=(self.stop,), daemon=True)
             self.thread.start()
             return self
         except Exception:  # noqa: BLE001 - no NVML binding or device: nvidia-smi below
@@ -150,6 +153,12 @@ class ClockSampler:
 
     def window_end(self):
         self.t1 = time.time()
+        # A region shorter than the polling interval: one sample right at its end.
+        if self.thread and not any(r[0] >= self.t0 for r in list(self.samples)):
+            try:
+                self._nvml_sample()
+            except Exception:  # noqa: BLE001
+                pass
 
     def __exit__(self, *a):
         if self.thread:
