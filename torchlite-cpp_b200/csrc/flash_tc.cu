@@ -62,7 +62,7 @@ constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_X = OFF_V + VST * V_BYTES;  // row-max exchange: [2 parities][NQ][2 halves][128]
 constexpr int X_BYTES = 2 * NQ * 2 * FQ * 4;
 constexpr int OFF_BAR = OFF_X + X_BYTES;
-constexpr int BAR_BYTES = 8 * (NQ + 2 * KST + 2 * VST + 3 * SPB * NQ + 2 * NQ) + 8;  // + TMEM slot, abort flag
+constexpr int BAR_BYTES = 8 * (NQ + 2 * KST + 2 * VST + 3 * SPB * NQ + 3 * NQ) + 8;  // + TMEM slot, abort flag
 constexpr int SMEM = OFF_BAR + 512 + 1024;  // barriers + 1 KB alignment slack
 static_assert(BAR_BYTES <= 512, "barrier area");
 constexpr int SM_WARPS = 8;                 // softmax warps per query tile: 2 per TMEM lane quarter
@@ -121,7 +121,13 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     // two consecutive phases of one barrier
     uint64_t* p_full = s_empty + SPB * NQ;    // [NQ][SPB]
     uint64_t* o_full = p_full + SPB * NQ;     // [NQ]
-    uint64_t* drain = o_full + NQ;            // [NQ]
+    // o_last completes once, after the tile's last P.V, so the softmax's
+    // final wait needs no parity reasoning.  (Waiting for o_full's
+    // second-to-last and last phases by parity is ambiguous once the last
+    // P.V has finished before the wait starts: a parity wait tells apart
+    // only the current and the previous phase.)
+    uint64_t* o_last = o_full + NQ;           // [NQ]
+    uint64_t* drain = o_last + NQ;            // [NQ]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + NQ);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -146,6 +152,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 mbar_init(&p_full[SPB * t + b], SM_WARPS);
             }
             mbar_init(&o_full[t], 1);
+            mbar_init(&o_last[t], 1);
         }
         for (int t = 0; t < NQ; ++t) mbar_init(&drain[t], 1);
         *abort_flag = 0;
@@ -306,6 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 if (ok) ok = issue_pv(mt, j);
                 if (ok && elect_one()) umma_commit<1>(smem_u32(&v_empty[j % VST]));
             }
+            if (ok && elect_one()) umma_commit<1>(smem_u32(&o_last[mt]));
             if (!ok && issued && elect_one()) {
                 umma_commit<1>(smem_u32(&drain[mt]));
                 const uint64_t t0 = globaltimer();
@@ -459,14 +467,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 if (lane == 0) mbar_arrive(&p_full[SPB * t + b]);
             }
         }
-        // O after the last P.V.  A parity wait tells apart only the current and
-        // the previous phase: block nk - 1's scores being done implies P.V of
-        // block nk - 3 is, so wait for nk - 2's phase, then for nk - 1's.  (In
-        // the loop, the rescale's wait for block j - 1 comes after block j's
-        // scores, which imply P.V of block j - 2, for the same reason.)
+        // O after the last P.V: o_last's only phase.  (In the loop, the
+        // rescale's wait for block j - 1 is unambiguous: block j's scores
+        // imply P.V of block j - 2 is done, and block j's P.V cannot start
+        // before this warp's p_full arrival.)
         float o[32];
-        if (ok && p.nk >= 2) ok = warp_wait(&o_full[t], (uint32_t)(p.nk - 2) & 1u, abort_flag, p, 32);
-        if (ok) ok = warp_wait(&o_full[t], (uint32_t)(p.nk - 1) & 1u, abort_flag, p, 33);
+        if (ok) ok = warp_wait(&o_last[t], 0u, abort_flag, p, 32);
         if (ok) {
             tc_fence_after();
             uint32_t ov[32];
