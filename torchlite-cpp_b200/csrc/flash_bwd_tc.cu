@@ -62,7 +62,10 @@ constexpr int TR = 128;         // rows of a CTA's fixed tile = TMEM lanes = MMA
 constexpr int TB = 64;          // rows of a streamed block = MMA N / K
 constexpr int EW_WARPS = 16;    // elementwise warps: four per TMEM lane quarter
 constexpr int EW_COLS = TB / 4;  // columns (queries, keys or head dims) per elementwise thread
-constexpr int THREADS = 64 + 32 * EW_WARPS;
+// warps: 0 producer, 1 score MMAs, 2.. elementwise, MMA2_WARP the second MMA
+// stream (dV / dK, or dQ)
+constexpr int MMA2_WARP = 2 + EW_WARPS;
+constexpr int THREADS = 32 * (MMA2_WARP + 1);
 constexpr int TILE64 = TB * BD * 4;   // [64 x 64]: 2 boxes / chunks [64 x 32] of 8 KB
 constexpr uint32_t kSleep = 100000;   // a waiting thread sleeps up to 100 us per poll
 constexpr uint64_t kTimeoutNs = 2000000000ull;
@@ -186,8 +189,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
     uint64_t* s_empty = s_full + NB;       // [NB]  dV / dK of that buffer done
     uint64_t* e_full = s_empty + NB;       // [NB]  P^T, dS^T written (per buffer)
     uint64_t* acc_full = e_full + NB;      // [1]  every dV, dK product done
-    uint64_t* drain = acc_full + 1;        // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* drain = acc_full + 1;        // [2]  per MMA-issuing warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -206,7 +209,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
             mbar_init(&e_full[b], EW_WARPS);
         }
         mbar_init(acc_full, 1);
-        mbar_init(drain, 1);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -257,8 +261,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
                 for (int s = 0; s < QST; ++s)
                     if (pend & (1u << s)) drain_full(&q_full[s], (par >> s) & 1u);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == 1 || warp == MMA2_WARP) {
+        // ---------------- MMA issuers ----------------
+        // Two streams: warp 1 issues each block's two score-side products,
+        // MMA2_WARP the gradient products.  One thread's tcgen05.mma stream
+        // turns over about one N = 64 instruction per 130 cycles, and separate
+        // streams overlap (measured).
         // The whole warp runs the loop, every lane polling the barriers; one
         // elected lane issues each MMA and commit (a lone lane in a divergent
         // branch leaves the tensor pipe idle after each commit: measured).
@@ -288,14 +296,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
                 issued = true;
                 return true;
             };
-            if (ok) {
-                tc_fence_after();
-                ok = issue_s(0);
+            const bool s_role = warp == 1;
+            if (ok) tc_fence_after();
+            if (s_role) {
+                // S^T and dP^T of every block, ahead of the elementwise warps
+                for (int i = 0; ok && i < p.nblk; ++i) ok = issue_s(i);
             }
-            for (int i = 0; ok && i < p.nblk; ++i) {
+            for (int i = 0; !s_role && ok && i < p.nblk; ++i) {
                 const int b = i % NB, st = i % QST;
-                if (i + 1 < p.nblk) ok = issue_s(i + 1);
-                if (ok) ok = warp_wait_b(&e_full[b], (uint32_t)(i / NB) & 1u, abort_flag, p, 45);
+                ok = warp_wait_b(&e_full[b], (uint32_t)(i / NB) & 1u, abort_flag, p, 45);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
@@ -311,13 +320,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
                     if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)ACC1_COL, dsa + 8 * s,
                                      mnmajor_step(r_mdesc + soff + (uint32_t)(TILE64 >> 4), s), kIdescKM,
                                      (i > 0 || s > 0) ? 1u : 0u);
+                issued = true;
                 if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
                 if (elect_one()) umma_commit<1>(smem_u32(&q_empty[st]));
             }
-            if (ok) if (elect_one()) umma_commit<1>(smem_u32(acc_full));
+            if (ok && !s_role && elect_one()) umma_commit<1>(smem_u32(acc_full));
             if (!ok && issued && elect_one()) {
-                umma_commit<1>(smem_u32(drain));
-                drain_full(drain, 0);
+                uint64_t* dr = &drain[s_role ? 0 : 1];
+                umma_commit<1>(smem_u32(dr));
+                drain_full(dr, 0);
             }
             __syncwarp();
         }
@@ -436,8 +447,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
     uint64_t* e_full = s_empty + DQ_NS;    // [DQ_NS]  dS written (per score buffer)
     uint64_t* dp_empty = e_full + DQ_NS;   // [DQ_NDP] dP buffer loaded by the elementwise warps
     uint64_t* acc_full = dp_empty + DQ_NDP; // [1]
-    uint64_t* drain = acc_full + 1;        // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* drain = acc_full + 1;        // [2]  per MMA-issuing warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -457,7 +468,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
         }
         for (int b = 0; b < DQ_NDP; ++b) mbar_init(&dp_empty[b], EW_WARPS);
         mbar_init(acc_full, 1);
-        mbar_init(drain, 1);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -504,8 +516,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
                 for (int s = 0; s < KST; ++s)
                     if (pend & (1u << s)) drain_full(&k_full[s], (par >> s) & 1u);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == 1 || warp == MMA2_WARP) {
+        // ---------------- MMA issuers ----------------
+        // Two streams: warp 1 issues each block's two score-side products,
+        // MMA2_WARP the gradient products.  One thread's tcgen05.mma stream
+        // turns over about one N = 64 instruction per 130 cycles, and separate
+        // streams overlap (measured).
         // The whole warp runs the loop, every lane polling the barriers; one
         // elected lane issues each MMA and commit (a lone lane in a divergent
         // branch leaves the tensor pipe idle after each commit: measured).
@@ -538,14 +554,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
                 issued = true;
                 return true;
             };
-            if (ok) {
-                tc_fence_after();
-                ok = issue_s(0);
+            const bool s_role = warp == 1;
+            if (ok) tc_fence_after();
+            if (s_role) {
+                // S and dP of every block, ahead of the elementwise warps
+                for (int j = 0; ok && j < p.nblk; ++j) ok = issue_s(j);
             }
-            for (int j = 0; ok && j < p.nblk; ++j) {
+            for (int j = 0; !s_role && ok && j < p.nblk; ++j) {
                 const int b = j % DQ_NS, st = j % KST;
-                if (j + 1 < p.nblk) ok = issue_s(j + 1);
-                if (ok) ok = warp_wait_b(&e_full[b], (uint32_t)(j / DQ_NS) & 1u, abort_flag, p, 55);
+                ok = warp_wait_b(&e_full[b], (uint32_t)(j / DQ_NS) & 1u, abort_flag, p, 55);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
@@ -556,13 +573,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
                     if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)DQ_ACC_COL, dsa + 8 * s,
                                      mnmajor_step(r_mdesc + soff + (uint32_t)((2 * TILE64) >> 4), s), kIdescKM,
                                      (j > 0 || s > 0) ? 1u : 0u);
+                issued = true;
                 if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
                 if (elect_one()) umma_commit<1>(smem_u32(&k_empty[st]));
             }
-            if (ok) if (elect_one()) umma_commit<1>(smem_u32(acc_full));
+            if (ok && !s_role && elect_one()) umma_commit<1>(smem_u32(acc_full));
             if (!ok && issued && elect_one()) {
-                umma_commit<1>(smem_u32(drain));
-                drain_full(drain, 0);
+                uint64_t* dr = &drain[s_role ? 0 : 1];
+                umma_commit<1>(smem_u32(dr));
+                drain_full(dr, 0);
             }
             __syncwarp();
         }
