@@ -21,6 +21,10 @@ CASES = [
     (1, 8, 10, 10, 8, 3, 1, 1, 8),   # depthwise
     (2, 3, 4, 4, 2, 3, 3, 0, 1),     # stride larger than the step the kernel needs
     (1, 1, 2, 2, 1, 3, 2, 0, 1),     # input smaller than the kernel: (2 - 3) / 2 + 1 = 1 (C++ division)
+    # widths that are multiples of 4 take the vectorised im2col / col2im kernels
+    (2, 4, 12, 16, 8, 3, 2, 1, 2),   # stride 2, padding, groups
+    (1, 3, 9, 12, 4, 1, 1, 0, 1),    # 1x1
+    (2, 2, 8, 8, 2, 5, 1, 2, 1),     # 5x5, padding 2
 ]
 
 

@@ -63,6 +63,43 @@ __global__ void im2col_kernel(const float* __restrict__ in, float* __restrict__ 
     }
 }
 
+// im2col when W_out is a multiple of 4 (so is HW): each thread writes runs of
+// 4 outputs along a row as one float4 (one division per 4 outputs instead of
+// one per output), the reads stay coalesced across the warp.  One block per
+// line (n, g, p), as above.
+__global__ void im2col_vec4_kernel(const float* __restrict__ in, float* __restrict__ col, ConvShape s) {
+    const int64_t lines = s.N * s.groups * s.patch;
+    const int W_out = (int)s.W_out, q = W_out >> 2, n4 = (int)s.HW >> 2;
+    const int H = (int)s.H, W = (int)s.W;
+    const int stride = (int)s.stride, pad = (int)s.padding;
+    const int khw = (int)(s.kH * s.kW), kW = (int)s.kW;
+    for (int64_t line = blockIdx.x; line < lines; line += gridDim.x) {
+        const int p = (int)(line % s.patch);
+        const int64_t ng = line / s.patch;
+        const int g = (int)(ng % s.groups);
+        const int64_t n = ng / s.groups;
+        const int c = g * (int)s.C_in_g + p / khw;
+        const int kh = (p % khw) / kW, kw = p % kW;
+        const float* src = in + (n * s.C_in + c) * (int64_t)H * W;
+        float4* dst = reinterpret_cast<float4*>(col + line * s.HW);
+        for (int t = threadIdx.x; t < n4; t += blockDim.x) {
+            const int oh = t / q, c4 = t - oh * q;
+            const int ih = oh * stride - pad + kh;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (ih >= 0 && ih < H) {
+                const float* srow = src + (int64_t)ih * W;
+                const int iw0 = c4 * 4 * stride - pad + kw;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int iw = iw0 + e * stride;
+                    if (iw >= 0 && iw < W) v[e] = srow[iw];
+                }
+            }
+            dst[t] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
 // grad_in[n, c, ih, iw] = 0 + sum over (kh, kw) ascending of grad_col at the
 // (oh, ow) that read this pixel.  One block per (n, c) plane.
 __global__ void col2im_kernel(const float* __restrict__ gcol, float* __restrict__ gin, ConvShape s) {
@@ -92,6 +129,49 @@ __global__ void col2im_kernel(const float* __restrict__ gcol, float* __restrict_
                 }
             }
             dst[pix] = acc;
+        }
+    }
+}
+
+// col2im when W is a multiple of 4: each thread gathers 4 consecutive pixels
+// of a row and stores them as one float4; every pixel still adds its terms in
+// (kh, kw) ascending order from 0, as col2im_kernel does (the same sums, bit
+// for bit).  STRIDE1 drops the divisibility tests of the general stride.
+template <bool STRIDE1>
+__global__ void col2im_vec4_kernel(const float* __restrict__ gcol, float* __restrict__ gin, ConvShape s) {
+    const int64_t planes = s.N * s.C_in;
+    const int H = (int)s.H, W = (int)s.W, HW = (int)s.HW, H_out = (int)s.H_out, W_out = (int)s.W_out;
+    const int stride = STRIDE1 ? 1 : (int)s.stride, pad = (int)s.padding, kH = (int)s.kH, kW = (int)s.kW;
+    const int q = W >> 2, n4 = H * q;
+    for (int64_t plane = blockIdx.x; plane < planes; plane += gridDim.x) {
+        const int c = (int)(plane % s.C_in);
+        const int64_t n = plane / s.C_in;
+        const int g = c / (int)s.C_in_g, cl = c % (int)s.C_in_g;
+        const float* base = gcol + ((n * s.groups + g) * s.patch + (int64_t)cl * kH * kW) * s.HW;
+        float4* dst = reinterpret_cast<float4*>(gin + plane * (int64_t)H * W);
+        for (int t = threadIdx.x; t < n4; t += blockDim.x) {
+            const int ih = t / q, iw0 = (t - ih * q) * 4;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int kh = 0; kh < kH; ++kh) {
+                const int th = ih + pad - kh;
+                if (th < 0) continue;
+                if (!STRIDE1 && th % stride) continue;
+                const int oh = STRIDE1 ? th : th / stride;
+                if (oh >= H_out) continue;
+                const float* row = base + (int64_t)(kh * kW) * HW + (int64_t)oh * W_out;
+                for (int kw = 0; kw < kW; ++kw) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int tw = iw0 + e + pad - kw;
+                        if (tw < 0) continue;
+                        if (!STRIDE1 && tw % stride) continue;
+                        const int ow = STRIDE1 ? tw : tw / stride;
+                        if (ow >= W_out) continue;
+                        acc[e] = __fadd_rn(acc[e], row[(int64_t)kw * HW + ow]);
+                    }
+                }
+            }
+            dst[t] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         }
     }
 }
@@ -293,7 +373,10 @@ int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
     TLC_TRY(scratch_alloc(&col.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
     if (n) {
         const int64_t lines = s.N * s.groups * s.patch;
-        im2col_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
+        if (s.W_out % 4 == 0)
+            im2col_vec4_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
+        else
+            im2col_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
         count_launch();
         TLC_TRY(check_launch("im2col"));
     }
@@ -441,8 +524,15 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
                 g.cbs[1] = s.patch * s.HW;
                 TLC_TRY(gemm(g, mode, st));
             }
-            col2im_kernel<<<(unsigned)std::min<int64_t>(s.N * s.C_in, 148 * 64), 256, 0, st>>>(
-                gcol.f(), d_in->data, s);
+            const unsigned grid = (unsigned)std::min<int64_t>(s.N * s.C_in, 148 * 64);
+            if (s.W % 4 == 0 && (reinterpret_cast<uintptr_t>(d_in->data) & 15) == 0) {
+                if (s.stride == 1)
+                    col2im_vec4_kernel<true><<<grid, 256, 0, st>>>(gcol.f(), d_in->data, s);
+                else
+                    col2im_vec4_kernel<false><<<grid, 256, 0, st>>>(gcol.f(), d_in->data, s);
+            } else {
+                col2im_kernel<<<grid, 256, 0, st>>>(gcol.f(), d_in->data, s);
+            }
             count_launch();
             TLC_TRY(check_launch("col2im"));
         }
