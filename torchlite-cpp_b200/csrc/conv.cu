@@ -24,6 +24,8 @@
 //             reference's loop reaches that pixel; no atomics.
 //   grad_bias one chain per channel over (n, oh, ow), the reference's order.
 // In exact mode all of it is bit-identical to the reference.
+#include <mutex>
+
 #include "common.cuh"
 
 #include <algorithm>
@@ -96,6 +98,69 @@ __global__ void im2col_vec4_kernel(const float* __restrict__ in, float* __restri
                 }
             }
             dst[t] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
+// im2col with the input plane staged in shared memory (W_out a multiple of 4,
+// the plane at most kIm2colPlaneMax bytes): one block per (n, c) input plane
+// reads it from global memory once and writes all kH * kW of its lines, where
+// the line-per-block kernels read each plane kH * kW times through L2.
+constexpr int kIm2colPlaneMax = 96 * 1024;
+__global__ void __launch_bounds__(256) im2col_plane_kernel(const float* __restrict__ in, float* __restrict__ col,
+                                                           ConvShape s) {
+    extern __shared__ float plane_s[];
+    const int64_t planes = s.N * s.C_in;
+    const int H = (int)s.H, W = (int)s.W, HWin = H * W;
+    const int W_out = (int)s.W_out, H_out = (int)s.H_out, q = W_out >> 2, n4 = (int)s.HW >> 2;
+    const int stride = (int)s.stride, pad = (int)s.padding, kH = (int)s.kH, kW = (int)s.kW, khw = kH * kW;
+    const int rpp = (int)blockDim.x / q;  // output rows per pass (the host keeps q <= blockDim.x)
+    const int r0 = (int)threadIdx.x / q, c4 = (int)threadIdx.x - r0 * q;
+    for (int64_t plane = blockIdx.x; plane < planes; plane += gridDim.x) {
+        const int c = (int)(plane % s.C_in);
+        const int64_t n = plane / s.C_in;
+        const int g = c / (int)s.C_in_g, cl = c % (int)s.C_in_g;
+        const float* src = in + plane * (int64_t)HWin;
+        __syncthreads();  // the previous plane's readers are done
+        for (int i = threadIdx.x; i < HWin; i += blockDim.x) plane_s[i] = src[i];
+        __syncthreads();
+        // this channel's lines: p = cl * kH * kW + kh * kW + kw.  Thread
+        // (r0, c4) writes float4 c4 of rows r0, r0 + rpp, .. of the
+        // concatenated (k, oh) rows, walking k = kh * kW + kw and oh with
+        // counters (no division per output).
+        float4* lines = reinterpret_cast<float4*>(col + ((n * s.groups + g) * s.patch + (int64_t)cl * kH * kW) * s.HW);
+        if (r0 < rpp) {
+            int k = 0, kh = 0, kw = 0, oh = r0;
+            while (oh >= H_out && k < khw) {
+                oh -= H_out;
+                ++k;
+                if (++kw == kW) {
+                    kw = 0;
+                    ++kh;
+                }
+            }
+            while (k < khw) {
+                const int ih = oh * stride - pad + kh;
+                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (ih >= 0 && ih < H) {
+                    const int iw0 = c4 * 4 * stride - pad + kw;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int iw = iw0 + e * stride;
+                        if (iw >= 0 && iw < W) v[e] = plane_s[ih * W + iw];
+                    }
+                }
+                lines[(int64_t)k * n4 + oh * q + c4] = make_float4(v[0], v[1], v[2], v[3]);
+                oh += rpp;
+                while (oh >= H_out && k < khw) {
+                    oh -= H_out;
+                    ++k;
+                    if (++kw == kW) {
+                        kw = 0;
+                        ++kh;
+                    }
+                }
+            }
         }
     }
 }
@@ -373,7 +438,16 @@ int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
     TLC_TRY(scratch_alloc(&col.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
     if (n) {
         const int64_t lines = s.N * s.groups * s.patch;
-        if (s.W_out % 4 == 0)
+        const int64_t plane_bytes = s.H * s.W * (int64_t)sizeof(float);
+        if (s.W_out % 4 == 0 && s.W_out / 4 <= 256 && plane_bytes <= kIm2colPlaneMax) {
+            static std::once_flag attr_once;
+            std::call_once(attr_once, [] {
+                cudaFuncSetAttribute(im2col_plane_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kIm2colPlaneMax);
+            });
+            im2col_plane_kernel<<<(unsigned)std::min<int64_t>(s.N * s.C_in, 148 * 16), 256, (size_t)plane_bytes,
+                                  st>>>(in, col.f(), s);
+        } else if (s.W_out % 4 == 0)
             im2col_vec4_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
         else
             im2col_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
