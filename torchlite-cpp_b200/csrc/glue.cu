@@ -61,6 +61,40 @@ __global__ void elementwise_kernel(const float* __restrict__ a, const float* __r
     }
 }
 
+// The same operation row by row when the innermost (merged) dim is contiguous
+// in a and out and a multiple of 4 long: one offset decode per row, float4
+// loads and stores along it; b is one value per row (b_unit = 0) or a
+// contiguous run (b_unit = 1).  The per-element roundings are the same.
+__global__ void elementwise_rows_vec4_kernel(const float* __restrict__ a, const float* __restrict__ b, float s,
+                                             float* __restrict__ out, int64_t rows, int L4, EwIndex ix, int kind,
+                                             int b_unit) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        int64_t oa, ob;
+        ix.offsets(r * (int64_t)L4 * 4, oa, ob);
+        const float4* ar = reinterpret_cast<const float4*>(a + oa);
+        float4* orow = reinterpret_cast<float4*>(out + r * (int64_t)L4 * 4);
+        if (kind == 1) {
+            for (int j = threadIdx.x; j < L4; j += blockDim.x) {
+                const float4 x = ar[j];
+                orow[j] = make_float4(__fmul_rn(x.x, s), __fmul_rn(x.y, s), __fmul_rn(x.z, s), __fmul_rn(x.w, s));
+            }
+        } else if (b_unit) {
+            const float4* br = reinterpret_cast<const float4*>(b + ob);
+            for (int j = threadIdx.x; j < L4; j += blockDim.x) {
+                const float4 x = ar[j], y = br[j];
+                orow[j] = make_float4(__fadd_rn(x.x, y.x), __fadd_rn(x.y, y.y), __fadd_rn(x.z, y.z),
+                                      __fadd_rn(x.w, y.w));
+            }
+        } else {
+            const float y = b[ob];
+            for (int j = threadIdx.x; j < L4; j += blockDim.x) {
+                const float4 x = ar[j];
+                orow[j] = make_float4(__fadd_rn(x.x, y), __fadd_rn(x.y, y), __fadd_rn(x.z, y), __fadd_rn(x.w, y));
+            }
+        }
+    }
+}
+
 // C[r, c] = C[r, c] * s + bias[c] for a contiguous [rows, cols] block
 // (the GEMM epilogue on an all-zero product, K == 0).
 __global__ void epilogue_kernel(float* __restrict__ C, int64_t rows, int64_t cols, float s,
@@ -367,6 +401,30 @@ int launch_elementwise(const float* a, const float* b, float s, float* out, int6
         ++m;
     }
     ix.nd = m;
+    // row-wise float4 path: innermost dim contiguous in a, a multiple of 4
+    // long, every other a stride a multiple of 4, 16-byte aligned pointers;
+    // b one value per row or a contiguous, equally aligned run
+    auto al16p = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    bool rows_ok = m >= 1 && ix.sa[m - 1] == 1 && ix.sz[m - 1] % 4 == 0 && ix.sz[m - 1] / 4 <= INT32_MAX &&
+                   al16p(a) && al16p(out);
+    for (int d = 0; rows_ok && d < m - 1; ++d) rows_ok = ix.sa[d] % 4 == 0;
+    int b_unit = 0;
+    if (rows_ok && kind == 0) {
+        if (ix.sb[m - 1] == 1) {
+            b_unit = 1;
+            rows_ok = al16p(b);
+            for (int d = 0; rows_ok && d < m - 1; ++d) rows_ok = ix.sb[d] % 4 == 0;
+        } else {
+            rows_ok = ix.sb[m - 1] == 0;
+        }
+    }
+    if (rows_ok) {
+        const int64_t L = ix.sz[m - 1], rows = n / L;
+        elementwise_rows_vec4_kernel<<<(unsigned)std::min<int64_t>(rows, 148 * 16), 256, 0, st>>>(
+            a, b, s, out, rows, (int)(L / 4), ix, kind, b_unit);
+        count_launch();
+        return check_launch("elementwise");
+    }
     elementwise_kernel<<<grid_for(n, 256), 256, 0, st>>>(a, b, s, out, n, ix, kind);
     count_launch();
     return check_launch("elementwise");
