@@ -62,10 +62,11 @@ constexpr int TR = 128;         // rows of a CTA's fixed tile = TMEM lanes = MMA
 constexpr int TB = 64;          // rows of a streamed block = MMA N / K
 constexpr int EW_WARPS = 16;    // elementwise warps: four per TMEM lane quarter
 constexpr int EW_COLS = TB / 4;  // columns (queries, keys or head dims) per elementwise thread
-// warps: 0 producer, 1 score MMAs, 2.. elementwise, MMA2_WARP the second MMA
-// stream (dV / dK, or dQ)
+// warps: 0 producer, 1 the first MMA stream, 2.. elementwise, MMA2_WARP.. the
+// other MMA streams (dK/dV kernel: S^T, dP^T, dV, dK; dQ kernel: S, dP, dQ)
 constexpr int MMA2_WARP = 2 + EW_WARPS;
-constexpr int THREADS = 32 * (MMA2_WARP + 1);
+constexpr int DKV_THREADS = 32 * (MMA2_WARP + 3);
+constexpr int DQ_THREADS = 32 * (MMA2_WARP + 2);
 constexpr int TILE64 = TB * BD * 4;   // [64 x 64]: 2 boxes / chunks [64 x 32] of 8 KB
 constexpr uint32_t kSleep = 100000;   // a waiting thread sleeps up to 100 us per poll
 constexpr uint64_t kTimeoutNs = 2000000000ull;
@@ -178,7 +179,7 @@ constexpr int A0_COL = 0, A1_COL = BD, S_COL = 2 * BD, DP_COL = S_COL + NB * TB,
               ACC1_COL = ACC0_COL + BD;
 static_assert(ACC1_COL + BD <= TMEM_COLS, "TMEM columns");
 
-__global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __launch_bounds__(DKV_THREADS, 1) flash_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DKV_OFF_BAR);
@@ -189,8 +190,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
     uint64_t* s_empty = s_full + NB;       // [NB]  dV / dK of that buffer done
     uint64_t* e_full = s_empty + NB;       // [NB]  P^T, dS^T written (per buffer)
     uint64_t* acc_full = e_full + NB;      // [1]  every dV, dK product done
-    uint64_t* drain = acc_full + 1;        // [2]  per MMA-issuing warp
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+    uint64_t* drain = acc_full + 1;        // [4]  per MMA-issuing warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -201,16 +202,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
         mbar_init(a_full, EW_WARPS);
         for (int s = 0; s < QST; ++s) {
             mbar_init(&q_full[s], 1);
-            mbar_init(&q_empty[s], 1);
+            mbar_init(&q_empty[s], 2);  // commits of the dV and dK streams
         }
         for (int b = 0; b < NB; ++b) {
-            mbar_init(&s_full[b], 1);
-            mbar_init(&s_empty[b], 1);
+            mbar_init(&s_full[b], 2);   // commits of the S^T and dP^T streams
+            mbar_init(&s_empty[b], 2);  // commits of the dV and dK streams
             mbar_init(&e_full[b], EW_WARPS);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(&drain[0], 1);
-        mbar_init(&drain[1], 1);
+        mbar_init(acc_full, 2);
+        for (int r = 0; r < 4; ++r) mbar_init(&drain[r], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -261,74 +261,66 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dkdv_kernel(const __grid
                 for (int s = 0; s < QST; ++s)
                     if (pend & (1u << s)) drain_full(&q_full[s], (par >> s) & 1u);
         }
-    } else if (warp == 1 || warp == MMA2_WARP) {
+    } else if (warp == 1 || warp >= MMA2_WARP) {
         // ---------------- MMA issuers ----------------
-        // Two streams: warp 1 issues each block's two score-side products,
-        // MMA2_WARP the gradient products.  One thread's tcgen05.mma stream
-        // turns over about one N = 64 instruction per 130 cycles, and separate
-        // streams overlap (measured).
-        // The whole warp runs the loop, every lane polling the barriers; one
-        // elected lane issues each MMA and commit (a lone lane in a divergent
-        // branch leaves the tensor pipe idle after each commit: measured).
+        // Four streams, one warp each: S^T (warp 1), dP^T, dV, dK.  One
+        // thread's tcgen05.mma stream turns over about one N = 64 instruction
+        // per 130 cycles, and separate streams overlap (measured); each
+        // commit covers its own warp's MMAs, so the barriers a pair of
+        // streams releases together count two arrivals.  Every lane polls the
+        // barriers; one elected lane issues.
         {
+            const int role = warp == 1 ? 0 : warp - MMA2_WARP + 1;  // 0 S^T, 1 dP^T, 2 dV, 3 dK
             const uint64_t r_kdesc = smem_desc(smem_u32(smem + DKV_OFF_RING), 16, 1024, kSw128);
             const uint64_t r_mdesc = smem_desc(smem_u32(smem + DKV_OFF_RING), TILE64 / 2, 512, kSw128Atom32);
             bool ok = warp_wait_b(a_full, 0, abort_flag, p, 42);
             bool issued = false;
-            // S^T = K . Q_i^T and dP^T = V . dO_i^T (A = K, V in TMEM) into buffer i % NB
-            auto issue_s = [&](int i) -> bool {
-                const int b = i % NB, st = i % QST;
-                if (!warp_wait_b(&q_full[st], (uint32_t)(i / QST) & 1u, abort_flag, p, 43)) return false;
-                if (!warp_wait_b(&s_empty[b], ((uint32_t)(i / NB) & 1u) ^ 1u, abort_flag, p, 44)) return false;
-                tc_fence_after();
-                const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
-                const uint32_t ds = tmem_base + (uint32_t)(S_COL + b * TB), dp = tmem_base + (uint32_t)(DP_COL + b * TB);
-#pragma unroll
-                for (int s = 0; s < BD / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(ds, tmem_base + (uint32_t)(A0_COL + 8 * s),
-                                     kmajor_step(r_kdesc + soff, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
-#pragma unroll
-                for (int s = 0; s < BD / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(dp, tmem_base + (uint32_t)(A1_COL + 8 * s),
-                                     kmajor_step(r_kdesc + soff + (uint32_t)((2 * TILE64) >> 4), TILE64 / 2, s),
-                                     kIdescKK, s > 0 ? 1u : 0u);
-                if (elect_one()) umma_commit<1>(smem_u32(&s_full[b]));
-                issued = true;
-                return true;
-            };
-            const bool s_role = warp == 1;
             if (ok) tc_fence_after();
-            if (s_role) {
-                // S^T and dP^T of every block, ahead of the elementwise warps
-                for (int i = 0; ok && i < p.nblk; ++i) ok = issue_s(i);
-            }
-            for (int i = 0; !s_role && ok && i < p.nblk; ++i) {
-                const int b = i % NB, st = i % QST;
-                ok = warp_wait_b(&e_full[b], (uint32_t)(i / NB) & 1u, abort_flag, p, 45);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
-                const uint32_t pa = tmem_base + (uint32_t)(S_COL + b * TB), dsa = tmem_base + (uint32_t)(DP_COL + b * TB);
-                // dV += P^T . dO_i (B = dO MN-major), dK += dS^T . Q_i (B = Q MN-major)
+            if (role < 2) {
+                // S^T = K . Q_i^T (A = K in TMEM) or dP^T = V . dO_i^T (A = V) into buffer i % NB
+                for (int i = 0; ok && i < p.nblk; ++i) {
+                    const int b = i % NB, st = i % QST;
+                    ok = warp_wait_b(&q_full[st], (uint32_t)(i / QST) & 1u, abort_flag, p, 43);
+                    if (ok) ok = warp_wait_b(&s_empty[b], ((uint32_t)(i / NB) & 1u) ^ 1u, abort_flag, p, 44);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
+                    const uint32_t dst = tmem_base + (uint32_t)((role == 0 ? S_COL : DP_COL) + b * TB);
+                    const uint32_t acol = role == 0 ? A0_COL : A1_COL;
+                    const uint64_t bdesc = r_kdesc + soff + (role == 0 ? 0u : (uint32_t)((2 * TILE64) >> 4));
 #pragma unroll
-                for (int s = 0; s < TB / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)ACC0_COL, pa + 8 * s,
-                                     mnmajor_step(r_mdesc + soff + (uint32_t)((3 * TILE64) >> 4), s), kIdescKM,
-                                     (i > 0 || s > 0) ? 1u : 0u);
+                    for (int s = 0; s < BD / 8; ++s)
+                        if (elect_one())
+                            umma_tf32_tmem_a(dst, tmem_base + (uint32_t)(acol + 8 * s),
+                                             kmajor_step(bdesc, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
+                    issued = true;
+                    if (elect_one()) umma_commit<1>(smem_u32(&s_full[b]));
+                }
+            } else {
+                // dV += P^T . dO_i (B = dO MN-major) or dK += dS^T . Q_i (B = Q MN-major)
+                for (int i = 0; ok && i < p.nblk; ++i) {
+                    const int b = i % NB, st = i % QST;
+                    ok = warp_wait_b(&e_full[b], (uint32_t)(i / NB) & 1u, abort_flag, p, 45);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t soff = (uint32_t)((st * DKV_STAGE) >> 4);
+                    const uint32_t acc = tmem_base + (uint32_t)(role == 2 ? ACC0_COL : ACC1_COL);
+                    const uint32_t asrc = tmem_base + (uint32_t)((role == 2 ? S_COL : DP_COL) + b * TB);
+                    const uint64_t bdesc = r_mdesc + soff + (uint32_t)(((role == 2 ? 3 : 1) * TILE64) >> 4);
 #pragma unroll
-                for (int s = 0; s < TB / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)ACC1_COL, dsa + 8 * s,
-                                     mnmajor_step(r_mdesc + soff + (uint32_t)(TILE64 >> 4), s), kIdescKM,
-                                     (i > 0 || s > 0) ? 1u : 0u);
-                issued = true;
-                if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
-                if (elect_one()) umma_commit<1>(smem_u32(&q_empty[st]));
+                    for (int s = 0; s < TB / 8; ++s)
+                        if (elect_one())
+                            umma_tf32_tmem_a(acc, asrc + 8 * s, mnmajor_step(bdesc, s), kIdescKM,
+                                             (i > 0 || s > 0) ? 1u : 0u);
+                    issued = true;
+                    if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
+                    if (elect_one()) umma_commit<1>(smem_u32(&q_empty[st]));
+                }
+                if (ok && elect_one()) umma_commit<1>(smem_u32(acc_full));
             }
-            if (ok && !s_role && elect_one()) umma_commit<1>(smem_u32(acc_full));
             if (!ok && issued && elect_one()) {
-                uint64_t* dr = &drain[s_role ? 0 : 1];
-                umma_commit<1>(smem_u32(dr));
-                drain_full(dr, 0);
+                umma_commit<1>(smem_u32(&drain[role]));
+                drain_full(&drain[role], 0);
             }
             __syncwarp();
         }
@@ -435,7 +427,7 @@ static_assert(DQ_ACC_COL + BD <= 512, "TMEM columns");
 static_assert(DQ_SMEM <= 232448, "shared memory per CTA");
 static_assert(8 * (1 + 2 * KST + 3 * DQ_NS + DQ_NDP + 2) + 8 <= 256, "barrier area");
 
-__global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __launch_bounds__(DQ_THREADS, 1) flash_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DQ_OFF_BAR);
@@ -447,8 +439,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
     uint64_t* e_full = s_empty + DQ_NS;    // [DQ_NS]  dS written (per score buffer)
     uint64_t* dp_empty = e_full + DQ_NS;   // [DQ_NDP] dP buffer loaded by the elementwise warps
     uint64_t* acc_full = dp_empty + DQ_NDP; // [1]
-    uint64_t* drain = acc_full + 1;        // [2]  per MMA-issuing warp
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+    uint64_t* drain = acc_full + 1;        // [4]  per MMA-issuing warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -462,14 +454,13 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
             mbar_init(&k_empty[s], 1);
         }
         for (int b = 0; b < DQ_NS; ++b) {
-            mbar_init(&s_full[b], 1);
+            mbar_init(&s_full[b], 2);   // commits of the S and dP streams
             mbar_init(&s_empty[b], 1);
             mbar_init(&e_full[b], EW_WARPS);
         }
         for (int b = 0; b < DQ_NDP; ++b) mbar_init(&dp_empty[b], EW_WARPS);
         mbar_init(acc_full, 1);
-        mbar_init(&drain[0], 1);
-        mbar_init(&drain[1], 1);
+        for (int r = 0; r < 4; ++r) mbar_init(&drain[r], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -516,72 +507,66 @@ __global__ void __launch_bounds__(THREADS, 1) flash_bwd_dq_kernel(const __grid_c
                 for (int s = 0; s < KST; ++s)
                     if (pend & (1u << s)) drain_full(&k_full[s], (par >> s) & 1u);
         }
-    } else if (warp == 1 || warp == MMA2_WARP) {
+    } else if (warp == 1 || warp >= MMA2_WARP) {
         // ---------------- MMA issuers ----------------
-        // Two streams: warp 1 issues each block's two score-side products,
-        // MMA2_WARP the gradient products.  One thread's tcgen05.mma stream
-        // turns over about one N = 64 instruction per 130 cycles, and separate
-        // streams overlap (measured).
-        // The whole warp runs the loop, every lane polling the barriers; one
-        // elected lane issues each MMA and commit (a lone lane in a divergent
-        // branch leaves the tensor pipe idle after each commit: measured).
+        // Three streams, one warp each: S (warp 1), dP, dQ (as in the dK/dV
+        // kernel); s_full counts the S and dP streams' commits.
         {
+            const int role = warp == 1 ? 0 : warp - MMA2_WARP + 1;  // 0 S, 1 dP, 2 dQ
             const uint64_t r_kdesc = smem_desc(smem_u32(smem + DQ_OFF_RING), 16, 1024, kSw128);
             const uint64_t r_mdesc = smem_desc(smem_u32(smem + DQ_OFF_RING), TILE64 / 2, 512, kSw128Atom32);
             bool ok = warp_wait_b(a_full, 0, abort_flag, p, 52);
             bool issued = false;
-            // S = Q . K_j^T and dP = dO . V_j^T (A = Q, dO in TMEM) into score buffer
-            // j % DQ_NS and dP buffer j % DQ_NDP
-            auto issue_s = [&](int j) -> bool {
-                const int b = j % DQ_NS, pb = j % DQ_NDP, st = j % KST;
-                if (!warp_wait_b(&k_full[st], (uint32_t)(j / KST) & 1u, abort_flag, p, 53)) return false;
-                if (!warp_wait_b(&s_empty[b], ((uint32_t)(j / DQ_NS) & 1u) ^ 1u, abort_flag, p, 54)) return false;
-                if (!warp_wait_b(&dp_empty[pb], ((uint32_t)(j / DQ_NDP) & 1u) ^ 1u, abort_flag, p, 58)) return false;
-                tc_fence_after();
-                const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
-                const uint32_t ds = tmem_base + (uint32_t)(DQ_S_COL + b * TB),
-                               dp = tmem_base + (uint32_t)(DQ_DP_COL + pb * TB);
-#pragma unroll
-                for (int s = 0; s < BD / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(ds, tmem_base + (uint32_t)(A0_COL + 8 * s),
-                                     kmajor_step(r_kdesc + soff, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
-#pragma unroll
-                for (int s = 0; s < BD / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(dp, tmem_base + (uint32_t)(A1_COL + 8 * s),
-                                     kmajor_step(r_kdesc + soff + (uint32_t)(TILE64 >> 4), TILE64 / 2, s),
-                                     kIdescKK, s > 0 ? 1u : 0u);
-                if (elect_one()) umma_commit<1>(smem_u32(&s_full[b]));
-                issued = true;
-                return true;
-            };
-            const bool s_role = warp == 1;
             if (ok) tc_fence_after();
-            if (s_role) {
-                // S and dP of every block, ahead of the elementwise warps
-                for (int j = 0; ok && j < p.nblk; ++j) ok = issue_s(j);
-            }
-            for (int j = 0; !s_role && ok && j < p.nblk; ++j) {
-                const int b = j % DQ_NS, st = j % KST;
-                ok = warp_wait_b(&e_full[b], (uint32_t)(j / DQ_NS) & 1u, abort_flag, p, 55);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
-                const uint32_t dsa = tmem_base + (uint32_t)(DQ_S_COL + b * TB);
-                // dQ += dS . K_j (A = dS in TMEM, B = K MN-major)
+            if (role < 2) {
+                // S = Q . K_j^T (A = Q in TMEM) into score buffer j % DQ_NS, or
+                // dP = dO . V_j^T (A = dO) into dP buffer j % DQ_NDP
+                for (int j = 0; ok && j < p.nblk; ++j) {
+                    const int b = j % DQ_NS, pb = j % DQ_NDP, st = j % KST;
+                    ok = warp_wait_b(&k_full[st], (uint32_t)(j / KST) & 1u, abort_flag, p, 53);
+                    if (ok) {
+                        ok = role == 0
+                                 ? warp_wait_b(&s_empty[b], ((uint32_t)(j / DQ_NS) & 1u) ^ 1u, abort_flag, p, 54)
+                                 : warp_wait_b(&dp_empty[pb], ((uint32_t)(j / DQ_NDP) & 1u) ^ 1u, abort_flag, p, 58);
+                    }
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
+                    const uint32_t dst = tmem_base + (uint32_t)(role == 0 ? DQ_S_COL + b * TB : DQ_DP_COL + pb * TB);
+                    const uint32_t acol = role == 0 ? A0_COL : A1_COL;
+                    const uint64_t bdesc = r_kdesc + soff + (role == 0 ? 0u : (uint32_t)(TILE64 >> 4));
 #pragma unroll
-                for (int s = 0; s < TB / 8; ++s)
-                    if (elect_one()) umma_tf32_tmem_a(tmem_base + (uint32_t)DQ_ACC_COL, dsa + 8 * s,
-                                     mnmajor_step(r_mdesc + soff + (uint32_t)((2 * TILE64) >> 4), s), kIdescKM,
-                                     (j > 0 || s > 0) ? 1u : 0u);
-                issued = true;
-                if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
-                if (elect_one()) umma_commit<1>(smem_u32(&k_empty[st]));
+                    for (int s = 0; s < BD / 8; ++s)
+                        if (elect_one())
+                            umma_tf32_tmem_a(dst, tmem_base + (uint32_t)(acol + 8 * s),
+                                             kmajor_step(bdesc, TILE64 / 2, s), kIdescKK, s > 0 ? 1u : 0u);
+                    issued = true;
+                    if (elect_one()) umma_commit<1>(smem_u32(&s_full[b]));
+                }
+            } else {
+                for (int j = 0; ok && j < p.nblk; ++j) {
+                    const int b = j % DQ_NS, st = j % KST;
+                    ok = warp_wait_b(&e_full[b], (uint32_t)(j / DQ_NS) & 1u, abort_flag, p, 55);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t soff = (uint32_t)((st * DQ_STAGE) >> 4);
+                    const uint32_t dsa = tmem_base + (uint32_t)(DQ_S_COL + b * TB);
+                    // dQ += dS . K_j (A = dS in TMEM, B = K MN-major)
+#pragma unroll
+                    for (int s = 0; s < TB / 8; ++s)
+                        if (elect_one())
+                            umma_tf32_tmem_a(tmem_base + (uint32_t)DQ_ACC_COL, dsa + 8 * s,
+                                             mnmajor_step(r_mdesc + soff + (uint32_t)((2 * TILE64) >> 4), s),
+                                             kIdescKM, (j > 0 || s > 0) ? 1u : 0u);
+                    issued = true;
+                    if (elect_one()) umma_commit<1>(smem_u32(&s_empty[b]));
+                    if (elect_one()) umma_commit<1>(smem_u32(&k_empty[st]));
+                }
+                if (ok && elect_one()) umma_commit<1>(smem_u32(acc_full));
             }
-            if (ok && !s_role && elect_one()) umma_commit<1>(smem_u32(acc_full));
             if (!ok && issued && elect_one()) {
-                uint64_t* dr = &drain[s_role ? 0 : 1];
-                umma_commit<1>(smem_u32(dr));
-                drain_full(dr, 0);
+                umma_commit<1>(smem_u32(&drain[role]));
+                drain_full(&drain[role], 0);
             }
             __syncwarp();
         }
@@ -767,7 +752,7 @@ int flash_backward_tc(const float* dout, const float* q, const float* k, const f
         p.kv1 = v;
         p.out0 = dk;
         p.out1 = dv;
-        flash_bwd_dkdv_kernel<<<(unsigned)grid, THREADS, DKV_SMEM, s>>>(p);
+        flash_bwd_dkdv_kernel<<<(unsigned)grid, DKV_THREADS, DKV_SMEM, s>>>(p);
         count_launch();
         if ((rc = check_launch("flash_attention_backward (dK, dV)")) != TLC_OK) break;
         // dQ
@@ -778,7 +763,7 @@ int flash_backward_tc(const float* dout, const float* q, const float* k, const f
         p.kv1 = dout;
         p.out0 = dq;
         p.out1 = nullptr;
-        flash_bwd_dq_kernel<<<(unsigned)grid, THREADS, DQ_SMEM, s>>>(p);
+        flash_bwd_dq_kernel<<<(unsigned)grid, DQ_THREADS, DQ_SMEM, s>>>(p);
         count_launch();
         rc = check_launch("flash_attention_backward (dQ)");
     } while (false);
