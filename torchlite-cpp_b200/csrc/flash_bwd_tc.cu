@@ -390,11 +390,17 @@ __global__ void __launch_bounds__(DKV_THREADS, 1) flash_bwd_dkdv_kernel(const __
                 const int dc = p.d - c0;
                 float* dvrow = p.out1 + ((int64_t)head * p.S + key) * p.d + c0;
                 float* dkrow = p.out0 + ((int64_t)head * p.S + key) * p.d + c0;
+                // d % 4 == 0 and 16-byte aligned rows (the kernel's preconditions):
+                // float4 stores wherever 4 columns are inside d
 #pragma unroll
-                for (int c = 0; c < EW_COLS; ++c)
+                for (int c = 0; c < EW_COLS; c += 4)
                     if (c < dc) {
-                        dvrow[c] = __uint_as_float(vv[c]);
-                        dkrow[c] = __uint_as_float(kk[c]);
+                        *reinterpret_cast<float4*>(dvrow + c) =
+                            make_float4(__uint_as_float(vv[c]), __uint_as_float(vv[c + 1]),
+                                        __uint_as_float(vv[c + 2]), __uint_as_float(vv[c + 3]));
+                        *reinterpret_cast<float4*>(dkrow + c) =
+                            make_float4(__uint_as_float(kk[c]), __uint_as_float(kk[c + 1]),
+                                        __uint_as_float(kk[c + 2]), __uint_as_float(kk[c + 3]));
                     }
             }
         }
@@ -632,8 +638,11 @@ __global__ void __launch_bounds__(DQ_THREADS, 1) flash_bwd_dq_kernel(const __gri
                 const int dc = p.d - c0;
                 float* qrow = p.out0 + ((int64_t)head * p.S + row) * p.d + c0;
 #pragma unroll
-                for (int c = 0; c < EW_COLS; ++c)
-                    if (c < dc) qrow[c] = __uint_as_float(qv[c]);
+                for (int c = 0; c < EW_COLS; c += 4)
+                    if (c < dc)
+                        *reinterpret_cast<float4*>(qrow + c) =
+                            make_float4(__uint_as_float(qv[c]), __uint_as_float(qv[c + 1]),
+                                        __uint_as_float(qv[c + 2]), __uint_as_float(qv[c + 3]));
             }
         }
     }
