@@ -34,7 +34,10 @@ def bits_equal(x, y):
 
 
 ADD_SHAPES = [((4, 3, 5), (5,)), ((4, 1, 5), (3, 1)), ((2, 3), (2, 3)), ((6,), (1,)),
-              ((2, 1, 4, 1), (3, 1, 5)), ((4096, 4096), (4096,)), ((), (3, 2)), ((0, 3), (3,))]
+              ((2, 1, 4, 1), (3, 1, 5)), ((4096, 4096), (4096,)), ((), (3, 2)), ((0, 3), (3,)),
+              # inner dims that are multiples of 4 take the row-wise float4 path: b one value
+              # per row, and b a contiguous run under a broadcast outer dim
+              ((8, 16), (8, 1)), ((3, 5, 12), (5, 12)), ((2, 64, 8), (64, 1))]
 
 
 @pytest.mark.parametrize("sa,sb", ADD_SHAPES)
@@ -57,8 +60,9 @@ def test_add_strided_and_errors():
 
 
 @pytest.mark.parametrize("s", [0.125, -3.0, 1.0 / 8.0, 1e-30])
-def test_scale(s):
-    x = inputs.normal(np.random.default_rng(11), (33, 17))
+@pytest.mark.parametrize("shape", [(33, 17), (32, 64)])  # (32, 64): the row-wise float4 path
+def test_scale(s, shape):
+    x = inputs.normal(np.random.default_rng(11), shape)
     assert bits_equal(host(tlcuda.scale(dev(x), s)), O.scale(x, s))
     assert bits_equal(host(tlcuda.scale(dev(x).t(), s)), O.scale(x.T, s))
 
