@@ -290,6 +290,20 @@ class Work:
         raise NotImplementedError
 
 
+def gemm_config(name, world):
+    """The `config` of a GEMM workload at `world` GPUs (both arms print it)."""
+    batch, M, N, K = GEMMS[name]
+    if batch > 1:
+        par = f"batch-sharded x{world}" if world > 1 else "single GPU"
+    else:
+        par = f"output-column-block sharded x{world}" if world > 1 else "single GPU"
+    return {"workload": name, "batch_per_gpu": batch,
+            "global_batch": batch * world if batch > 1 else 1,
+            "M": M, "N": N, "K": K, "layout": "row-major A, B, C",
+            "parallelism": par,
+            "l2": "operands larger than L2 (126 MB), no flush"}
+
+
 class GemmWork(Work):
     def __init__(self, name, world, rank, device):
         import torch
@@ -307,7 +321,6 @@ class GemmWork(Work):
             self.scaling = "weak"
             self.flops = 2.0 * batch * M * N * K
             self.job_flops = self.flops * world
-            par = f"batch-sharded x{world}" if world > 1 else "single GPU"
         else:
             # column-block sharded, strong: same A, B on every rank
             g = torch.Generator(device=device).manual_seed(4)
@@ -320,12 +333,7 @@ class GemmWork(Work):
             self.scaling = "strong" if world > 1 else "weak"
             self.flops = 2.0 * M * (c1 - c0) * K
             self.job_flops = 2.0 * M * N * K
-            par = f"output-column-block sharded x{world}" if world > 1 else "single GPU"
-        self.config = {"workload": name, "batch_per_gpu": batch,
-                       "global_batch": batch * world if batch > 1 else 1,
-                       "M": M, "N": N, "K": K, "layout": "row-major A, B, C",
-                       "parallelism": par,
-                       "l2": "operands larger than L2 (126 MB), no flush"}
+        self.config = gemm_config(name, world)
 
     def step(self, mode):
         import tlcuda
@@ -620,6 +628,31 @@ def cpu_reference_sample(name, reps=3):
                          else " with std::thread::hardware_concurrency() threads")}
 
 
+def reference_full_workload(name):
+    """The whole per-GPU workload for the reference's tl::matmul, when one step
+    of it fits a bounded CPU run: the batched GEMM (64 entries of 2048^3, about
+    6 s per step on 16 host threads).  None for the rest (they are sampled)."""
+    if name not in GEMMS or GEMMS[name][0] <= 1:
+        return None
+    import numpy as np
+    batch, M, N, K = GEMMS[name]
+    rng = np.random.default_rng(4)
+    a = inputs_uniform(rng, (batch, M, K))
+    b = inputs_uniform(rng, (batch, K, N))
+    return a, b, 2.0 * batch * M * N * K
+
+
+def inputs_uniform(rng, shape):
+    """U[-1,1] float32 in chunks of 16 Mi values (bounded float64 temporaries)."""
+    import numpy as np
+    out = np.empty(shape, np.float32)
+    flat = out.reshape(-1)
+    step = 1 << 24
+    for i in range(0, flat.size, step):
+        flat[i:i + step] = rng.uniform(-1.0, 1.0, size=min(step, flat.size - i))
+    return out
+
+
 def run_reference_arm(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -632,28 +665,42 @@ def run_reference_arm(args):
     except FileNotFoundError as e:
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not built: {e}"}))
         return 0
-    fn, flops, what = ref_job(args.workload, R)
-    for _ in range(args.warmup):
-        fn()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        fn()
-    dt = (time.perf_counter() - t0) / args.steps
+    cores = 1 if args.workload.startswith("flash") else R.hardware_threads()
+    full = reference_full_workload(args.workload)
+    if full is not None:
+        # the reference's own tl::matmul over this GPU's whole share of the workload
+        a, b, flops = full
+        dt = R.matmul_timed(a, b, args.warmup, args.steps)
+        cfg = gemm_config(args.workload, world)
+        what = (f"tl::matmul {list(a.shape)}x{list(b.shape)} fp32, the whole per-GPU workload "
+                f"({flops / 1e12:.2f} TFLOP)")
+        if world > 1:
+            cfg = dict(cfg, reference_sample=f"one GPU's share ({a.shape[0]} of "
+                                            f"{a.shape[0] * world} entries) per step")
+        sample = (f"each step: {what}, steady_clock around tl::matmul alone, "
+                  f"{os.path.basename(R.path)}, std::thread::hardware_concurrency() threads")
+    else:
+        fn, flops, what = ref_job(args.workload, R)
+        for _ in range(args.warmup):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        dt = (time.perf_counter() - t0) / args.steps
+        cfg = {"workload": args.workload}
+        if args.workload in GEMMS:
+            batch, M, N, K = GEMMS[args.workload]
+            cfg.update({"batch": batch, "M": M, "N": N, "K": K,
+                        "sampled_rows": M if batch > 1 else min(M, 256)})
+        sample = f"each step: {what}, host wall clock"
     val = flops / dt / 1e12
-    sample = f"each step: {what}, host wall clock"
-    cfg = {"workload": args.workload}
-    if args.workload in GEMMS:
-        batch, M, N, K = GEMMS[args.workload]
-        cfg.update({"batch": batch, "M": M, "N": N, "K": K,
-                    "sampled_rows": M if batch > 1 else min(M, 256)})
     line = {"metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": ("synthetic N(0,1) seed 5" if args.workload.startswith("flash")
                      else "synthetic U[-1,1] seed 4"),
             "impl": "reference", "config": cfg,
-            "cpu_baseline": {"value": val, "unit": "TFLOP/s",
-                             "cores": 1 if args.workload.startswith("flash") else R.hardware_threads(),
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores,
                              "kind": "reference", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -671,6 +718,134 @@ def traffic_for(mode, wl):
         return None
 
 
+def e2e_record(work, mode, world, device, steps):
+    """`mode` end to end through tlc_matmul_host (page-locked host A, B in,
+    host C out, copies inside the timed region)."""
+    import torch
+    try:
+        es = torch.cuda.Stream(device)
+        fn, hbytes, dbytes, keep = work.e2e(mode, es)
+        ms, _ = time_device(fn, steps, 2, world, es)
+        del keep
+        return {"value": work.job_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": hbytes, "d2h_bytes_per_step": dbytes,
+                "ms_per_step": ms, "api": "tlc_matmul_host", "mode": mode}
+    except Exception as e:  # e.g. not enough page-locked host memory
+        return {"value": None, "unavailable": repr(e)[:200], "mode": mode}
+
+
+def square8192_record(world, rank, device, stream, peaks, psrc, sms, steps):
+    """The 8192^3 GEMM of the scaling sweep on one GPU, every mode, each with
+    its own CUDA-event timing; TF32 (the target of 0.70 of dense TF32 peak)
+    with the SM clock sampled inside its timed region."""
+    import tlcuda
+    w = GemmWork("square8192", 1, 0, device)
+    out = {"config": {"M": 8192, "N": 8192, "K": 8192, "layout": "row-major A, B, C"}}
+    mx = peaks.get("sm_max_mhz", 1965.0)
+    for mode in ("tf32", "3xtf32", "exact"):
+        n = steps if mode != "exact" else max(3, steps // 3)
+        if mode == "tf32":
+            with ClockSampler(device.index) as cs:
+                ms, launches = time_device(lambda: w.step(mode), n, 3, world, stream,
+                                           tlcuda.launch_count, clocks=cs)
+            clocks = cs.summary(mx)
+        else:
+            ms, launches = time_device(lambda: w.step(mode), n, 3, world, stream, tlcuda.launch_count)
+            clocks = None
+        peak, pdesc = peak_for(mode, peaks, psrc, sms, mx)
+        tf = w.flops / (ms * 1e-3) / 1e12
+        rec = {"ms": ms, "tflops": tf, "frac": tf / peak, "peak": peak, "peak_source": pdesc,
+               "launches_per_step": launches / n}
+        if clocks:
+            rec["clocks"] = clocks
+        out[mode] = rec
+    del w
+    return out
+
+
+def sustained_record(work, mode, world, stream, peaks, device, seconds=1.5):
+    """The headline step back to back for about `seconds` (long enough to reach
+    the 1000 W power cap), against the sustained TF32 peak (1/2 of the
+    measured sustained bf16 figure), with the SM clock sampled inside."""
+    import tlcuda
+    probe, _ = time_device(lambda: work.step(mode), 3, 3, world, stream)
+    n = max(10, int(seconds * 1e3 / max(probe, 1e-3)))
+    with ClockSampler(device.index) as cs:
+        ms, _ = time_device(lambda: work.step(mode), n, 3, world, stream, tlcuda.launch_count,
+                            clocks=cs)
+    tf = work.flops / (ms * 1e-3) / 1e12
+    sus = peaks.get("bf16_tflops_sustained")
+    peak = sus / 2.0 if (sus and mode == "tf32") else None
+    return {"mode": mode, "steps": n, "seconds": n * ms * 1e-3, "ms_per_step": ms,
+            "tflops_per_gpu": tf, "peak": peak,
+            "peak_source": "TF32 = 1/2 of measured sustained bf16" if peak else None,
+            "frac": tf / peak if peak else None, "clocks": cs.summary(peaks.get("sm_max_mhz", 1965.0))}
+
+
+def scaling_records(args, world, rank, device, stream, peaks, psrc, sms):
+    """At N > 1: what the weak-scaled headline does not show.
+      strong          the fixed 64 x 2048^3 batch split over the N GPUs (64/N
+                      entries each): compute alone, and compute + the NCCL
+                      all-gather that puts the whole C on every GPU;
+      square8192      one 8192^3 GEMM over output column blocks (A and B
+                      replicated, each GPU reads its block of B in place):
+                      compute, and the all-gather + reassembly of C;
+      exact_db_chain  the broadcast workload's MatmulBackward in exact mode,
+                      dB reduced by the rank-to-rank chain in batch order."""
+    import torch
+    import torch.distributed as dist
+    import tldist
+    import tlcuda
+    out = {}
+    mode = args.mode
+    # strong scaling of the batched workload
+    batch, M, N, K = GEMMS["batched"]
+    b0, b1 = tldist.batch_shard(batch, world, rank)
+    g = torch.Generator(device=device).manual_seed(4)
+    A = torch.rand((b1 - b0, M, K), generator=g, device=device) * 2 - 1
+    B = torch.rand((b1 - b0, K, N), generator=g, device=device) * 2 - 1
+    C = torch.empty((b1 - b0, M, N), device=device)
+    flops = 2.0 * batch * M * N * K
+    ms, _ = time_device(lambda: tlcuda.matmul(A, B, mode=mode, out=C), 10, 3, world, stream)
+    rec = {"entries_per_gpu": b1 - b0, "compute_ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+    if batch % world == 0:
+        full = torch.empty((batch, M, N), device=device)
+
+        def both():
+            tlcuda.matmul(A, B, mode=mode, out=C)
+            dist.all_gather_into_tensor(full, C)
+        ms_g, _ = time_device(both, 10, 3, world, stream)
+        rec.update({"with_allgather_ms": ms_g, "with_allgather_tflops": flops / (ms_g * 1e-3) / 1e12,
+                    "allgather_bytes_per_gpu": 4 * M * N * (batch - (b1 - b0)),
+                    "collective": "ncclAllGather of C (every GPU receives the other GPUs' shards)"})
+    out["strong_batched"] = rec
+    del A, B, C
+    torch.cuda.empty_cache()
+    # column-block sharded square
+    w = GemmWork("square8192", world, rank, device)
+    ms, _ = time_device(lambda: w.step(mode), 10, 3, world, stream)
+    gms = w.gather_ms(world, stream)
+    rec = {"compute_ms": ms, "tflops": w.job_flops / (ms * 1e-3) / 1e12, "gather_ms": gms,
+           "collective": "ncclAllGather of the column blocks + tlc_gather_colblocks"}
+    if gms:
+        rec["with_gather_tflops"] = w.job_flops / ((ms + gms) * 1e-3) / 1e12
+    out["square8192_colblock"] = rec
+    del w
+    torch.cuda.empty_cache()
+    # exact-mode dB chain of the broadcast workload
+    gb = torch.Generator(device=device).manual_seed(1)
+    a = torch.randn((32, 128, 64), generator=gb, device=device)
+    b = torch.randn((64, 128), generator=gb, device=device)
+    c0, c1 = tldist.batch_shard(32, world, rank)
+    dc = torch.randn((32, 128, 128), generator=gb, device=device)[c0:c1].contiguous()
+    ms, _ = time_device(lambda: tldist.batch_sharded_matmul_backward(dc, a, b, mode="exact"),
+                        10, 3, world, stream)
+    out["exact_db_chain"] = {"workload": "A[32,128,64].B[64,128] backward, batch-sharded",
+                             "ms": ms, "hops": world - 1,
+                             "collective": "rank-to-rank send/recv chain + broadcast"}
+    return out
+
+
 def run_ours(args):
     import torch
     import tlcuda
@@ -681,6 +856,7 @@ def run_ours(args):
     modes = [args.mode] + [m for m in ("tf32", "3xtf32", "exact") if m != args.mode and args.all_modes]
     peaks, psrc = load_peaks()
     sms = torch.cuda.get_device_properties(device).multi_processor_count
+    mx = peaks.get("sm_max_mhz", 1965.0)
 
     results = {}
     launches = None
@@ -691,10 +867,10 @@ def run_ours(args):
             with ClockSampler(local) as cs:
                 ms, launches = time_device(fn, args.steps, args.warmup, world, stream,
                                            tlcuda.launch_count, clocks=cs)
-            clocks = cs.summary(peaks.get("sm_max_mhz", 1965.0))
+            clocks = cs.summary(mx)
         else:
             ms, _ = time_device(fn, max(3, args.steps // 2), 3, world, stream)
-        peak, pdesc = peak_for(mode, peaks, psrc, sms, peaks.get("sm_max_mhz", 1965.0))
+        peak, pdesc = peak_for(mode, peaks, psrc, sms, mx)
         per_gpu = work.flops / (ms * 1e-3) / 1e12
         results[mode] = {"ms_per_step": ms, "tflops_per_gpu": per_gpu,
                          "value": work.job_flops / (ms * 1e-3) / 1e12,
@@ -713,23 +889,28 @@ def run_ours(args):
     fwd = None
     if isinstance(work, FlashWork):
         fmode = args.mode if args.mode == "tf32" else "exact"
-        fwd = [work.forward_roofline(world, stream, m, peak_for(m, peaks, psrc, sms,
-                                                                peaks.get("sm_max_mhz", 1965.0)))
+        fwd = [work.forward_roofline(world, stream, m, peak_for(m, peaks, psrc, sms, mx))
                for m in dict.fromkeys((fmode, "exact"))]
 
-    # End to end through the host-buffer C entry point (page-locked host memory).
+    # End to end through the host-buffer C entry point (page-locked host memory),
+    # every mode; the head mode's record is the line's `e2e`.
     e2e = None
     if not args.no_e2e and isinstance(work, GemmWork):
-        try:
-            es = torch.cuda.Stream(device)
-            fn, hbytes, dbytes, keep = work.e2e(args.mode, es)
-            ms_e2e, _ = time_device(fn, max(3, min(args.steps, 10)), 2, world, es)
-            e2e = {"value": work.job_flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-                   "h2d_bytes_per_step": hbytes, "d2h_bytes_per_step": dbytes,
-                   "ms_per_step": ms_e2e, "api": "tlc_matmul_host"}
-            del keep
-        except Exception as e:  # e.g. not enough page-locked host memory
-            e2e = {"value": None, "unavailable": repr(e)[:200]}
+        for mode in modes:
+            rec = e2e_record(work, mode, world, device,
+                             max(3, min(args.steps, 10)) if mode == args.mode else 3)
+            results[mode]["e2e"] = rec
+            if mode == args.mode:
+                e2e = rec
+
+    extras = {}
+    if not args.no_extras and args.workload == "batched":
+        if world == 1:
+            extras["square8192"] = square8192_record(world, rank, device, stream, peaks, psrc,
+                                                     sms, max(5, min(args.steps, 20)))
+            extras["sustained"] = sustained_record(work, args.mode, world, stream, peaks, device)
+        else:
+            extras["scaling"] = scaling_records(args, world, rank, device, stream, peaks, psrc, sms)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -752,6 +933,7 @@ def run_ours(args):
             line["gather_ms"] = gather
         if fwd is not None:
             line["forward"] = fwd
+        line.update(extras)
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist
@@ -773,6 +955,8 @@ def main():
     ap.add_argument("--head-only", dest="all_modes", action="store_false")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the 8192^3 / sustained (N=1) and scaling (N>1) sub-records")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -182,8 +182,16 @@ int tlc_gemm(const tlc_gemm_desc* desc, int mode, void* stream);
  *    plane); larger problems return TLC_ERR_INVALID_ARGUMENT;
  *  - A and B must be 16-byte aligned with strides that are multiples of 4
  *    floats (else TLC_ERR_UNSUPPORTED);
- *  - the first call on a device looks up that array's device address (set-up
- *    work), so make it before any stream capture;
+ *  - the array takes its 64 MiB of device memory when the library's GEMM
+ *    code is loaded on a device; with CUDA's lazy module loading (the
+ *    default since CUDA 12.2) that is the first GEMM call of any kind on the
+ *    device, this entry point included.  A caller whose arena claims the
+ *    device's free memory makes one call (any small product) before it
+ *    sizes the arena;
+ *  - the first call on a device (and the first after its context is re-
+ *    created) looks up that array's device address (set-up work), so make it
+ *    before any stream capture; the set-up is safe to race from several host
+ *    threads;
  *  - all calls share the array: calls that overlap on the GPU race, so
  *    serialise them (each call rewrites every element it reads, so nothing
  *    needs clearing between calls). */

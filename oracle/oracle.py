@@ -436,6 +436,11 @@ class TLRef:
                                    i64p, ctypes.c_int, _f32p, _i64, ctypes.POINTER(ctypes.c_int),
                                    i64p, ctypes.c_char_p, ctypes.c_int]
         L.tlref_matmul.restype = ctypes.c_int
+        L.tlref_matmul_timed.argtypes = [_f32p, ctypes.c_int, i64p, _f32p, ctypes.c_int, i64p,
+                                         ctypes.c_int, ctypes.c_int,
+                                         ctypes.POINTER(ctypes.c_double), ctypes.c_char_p,
+                                         ctypes.c_int]
+        L.tlref_matmul_timed.restype = ctypes.c_int
         L.tlref_matmul_backward.argtypes = [_f32p, ctypes.c_int, i64p, ctypes.c_int, _f32p,
                                             ctypes.c_int, i64p, ctypes.c_int, _f32p, ctypes.c_int,
                                             i64p, _f32p, _i64, _f32p, _i64, ctypes.c_char_p,
@@ -493,6 +498,20 @@ class TLRef:
         shape = tuple(sz[i] for i in range(nd.value))
         n = int(np.prod(shape, dtype=np.int64)) if shape else 1
         return out[:n].reshape(shape)
+
+    def matmul_timed(self, a, b, warmup, steps):
+        """Mean seconds per tl::matmul(A, B) call over `steps` calls after
+        `warmup` (tensors built once; the timed region holds only the calls)."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        sec = ctypes.c_double(0.0)
+        err = ctypes.create_string_buffer(256)
+        rc = self.L.tlref_matmul_timed(_fp(a), a.ndim, self._shape(a), _fp(b), b.ndim,
+                                       self._shape(b), int(warmup), int(steps),
+                                       ctypes.byref(sec), err, 256)
+        if rc != 0:
+            raise RuntimeError(f"tlref_matmul_timed: {err.value.decode()}")
+        return sec.value
 
     def matmul_backward(self, a, b, grad, trans_a=False, trans_b=False):
         """Gradients of the stored leaves a, b for C = matmul(a', b'), dC = grad."""

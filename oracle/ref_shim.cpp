@@ -12,6 +12,7 @@
 #include <tl/ops.h>
 #include <tl/tensor.h>
 
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -67,6 +68,29 @@ int tlref_matmul(const float* a, int a_nd, const int64_t* a_sz, int trans_a, con
         tl::Tensor B = maybe_t(make(b, b_nd, b_sz), trans_b);
         tl::Tensor C = tl::matmul(A, B);
         return copy_out(C, out, out_cap, out_nd, out_sz);
+    } catch (const std::exception& e) {
+        return fail(e, err, errlen);
+    }
+}
+
+// Times tl::matmul(A, B) on tensors built once from A and B: `warmup` untimed
+// calls, then `steps` calls between two steady_clock reads (each call
+// allocates and zero-fills its result, as the reference's matmul does,
+// src/ops.cpp:652).  *seconds = the mean per call.  The CPU arm of the
+// benchmark: the reference's own batch loop and gemm_mt threads over the
+// whole workload, without the shim's copies in the timed region.
+int tlref_matmul_timed(const float* a, int a_nd, const int64_t* a_sz, const float* b, int b_nd,
+                       const int64_t* b_sz, int warmup, int steps, double* seconds, char* err,
+                       int errlen) {
+    try {
+        tl::Tensor A = make(a, a_nd, a_sz);
+        tl::Tensor B = make(b, b_nd, b_sz);
+        for (int i = 0; i < warmup; ++i) tl::matmul(A, B);
+        const auto t0 = std::chrono::steady_clock::now();
+        for (int i = 0; i < steps; ++i) tl::matmul(A, B);
+        const auto t1 = std::chrono::steady_clock::now();
+        *seconds = std::chrono::duration<double>(t1 - t0).count() / (steps > 0 ? steps : 1);
+        return 0;
     } catch (const std::exception& e) {
         return fail(e, err, errlen);
     }

@@ -4,11 +4,18 @@
 // transposed-weight product with their MatmulBackward.  Every output and
 // gradient is written to argv[1] as raw float32.
 //
-// Linked (oracle/Makefile, target `callers`) from the reference's objects with
-// tl::matmul redirected to libtl_cuda (torchlite-cpp_b200/integration/
-// reference_matmul_gpu.cpp).  tests/test_reference_callers.py runs it twice,
-// with the redirection and with TLC_REFERENCE_MATMUL=1 (the reference's CPU
-// matmul), and compares the two files bit for bit in exact mode.
+// With a second argument "encoder" it runs instead one full-size
+// transformer-encoder MultiHeadAttention (batch 16, seq 512, d_model 768,
+// 12 heads of 64: src/nn.cpp:401-445) forward + backward, x ~ N(0,1) and
+// weights ~ N(0, 0.02) (Box-Muller over the same LCG), and writes the output,
+// the input gradient and the query / value projection weight gradients.
+//
+// Linked (oracle/Makefile, target `callers`) twice from the reference's
+// objects: ref_callers_{v3,v4} with tl::matmul redirected to libtl_cuda
+// (torchlite-cpp_b200/integration/reference_matmul_gpu.cpp), and
+// ref_callers_cpu_{v3,v4} with the reference's own CPU matmul.
+// tests/test_reference_callers.py runs both and compares the two files, bit
+// for bit in exact mode.
 #include <tl/autograd.h>
 #include <tl/nn.h>
 #include <tl/ops.h>
@@ -16,8 +23,10 @@
 
 #include <tlc.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <vector>
 
 static uint32_t g_state = 20240601u;
@@ -30,6 +39,22 @@ static tl::Tensor filled(const std::vector<int64_t>& sizes, float scale = 1.0f) 
     tl::Tensor t(sizes);
     float* p = t.data();
     for (int64_t i = 0; i < t.numel(); ++i) p[i] = next_value() * scale;
+    return t;
+}
+
+// N(0, std^2) by the Box-Muller transform of two LCG draws mapped to (0, 1].
+static tl::Tensor normal(const std::vector<int64_t>& sizes, float std_dev) {
+    tl::Tensor t(sizes);
+    float* p = t.data();
+    for (int64_t i = 0; i < t.numel(); i += 2) {
+        g_state = g_state * 1664525u + 1013904223u;
+        const double u1 = ((g_state >> 8) + 1.0) / 16777216.0;
+        g_state = g_state * 1664525u + 1013904223u;
+        const double u2 = (g_state >> 8) / 16777216.0;
+        const double r = std::sqrt(-2.0 * std::log(u1)), th = 6.283185307179586 * u2;
+        p[i] = static_cast<float>(r * std::cos(th) * std_dev);
+        if (i + 1 < t.numel()) p[i + 1] = static_cast<float>(r * std::sin(th) * std_dev);
+    }
     return t;
 }
 
@@ -53,11 +78,30 @@ static void set_params(tl::nn::Linear& lin, int64_t in, int64_t out) {
     lin.set_bias(b);
 }
 
-int main(int argc, char** argv) {
-    if (argc < 2) {
-        std::fprintf(stderr, "usage: %s out.bin\n", argv[0]);
-        return 2;
+// Transformer-encoder attention at full size.
+static void encoder_scenario() {
+    tl::nn::MultiHeadAttention mha(768, 12);
+    tl::nn::Linear* projs[4] = {&mha.q_proj(), &mha.k_proj(), &mha.v_proj(), &mha.out_proj()};
+    for (tl::nn::Linear* l : projs) {
+        tl::Tensor w = normal({768, 768}, 0.02f);
+        tl::Tensor b = normal({768}, 0.02f);
+        w.set_requires_grad(true);
+        b.set_requires_grad(true);
+        l->set_weight(w);
+        l->set_bias(b);
     }
+    tl::Tensor x = normal({16, 512, 768}, 1.0f);
+    x.set_requires_grad(true);
+    tl::Tensor y = mha.forward(x);
+    y.grad() = normal(y.sizes(), 1.0f);
+    y.backward();
+    dump(y);
+    dump(x.grad());
+    dump(grad_of(mha.q_proj().weight()));
+    dump(grad_of(mha.v_proj().weight()));
+}
+
+static void small_scenarios() {
     {  // Linear on a 2-D input (y = x W + b, W stored [in, out])
         tl::nn::Linear lin(300, 257);
         set_params(lin, 300, 257);
@@ -141,6 +185,17 @@ int main(int argc, char** argv) {
         dump(grad_of(conv.weight()));
         dump(grad_of(conv.bias()));
     }
+}
+
+int main(int argc, char** argv) {
+    if (argc < 2) {
+        std::fprintf(stderr, "usage: %s out.bin [encoder]\n", argv[0]);
+        return 2;
+    }
+    if (argc >= 3 && std::strcmp(argv[2], "encoder") == 0)
+        encoder_scenario();
+    else
+        small_scenarios();
     std::FILE* f = std::fopen(argv[1], "wb");
     if (!f) return 3;
     std::fwrite(g_out.data(), sizeof(float), g_out.size(), f);

@@ -67,3 +67,21 @@ def test_clock_window_keeps_only_timed_samples():
     cs.t0, cs.t1 = 2.2, 2.3
     s = cs.summary(1965.0)
     assert s["samples"] == 1 and s["sm_mhz"] == 1965 and s["reasons"] == []
+
+
+@pytest.mark.gpu
+def test_default_workload_sub_records():
+    """The default (batched) line carries an end-to-end number for every mode,
+    the 8192^3 record (TF32 with its own clock record) and the sustained run."""
+    line = run_bench("--steps", "3", "--warmup", "3", "--no-cpu-baseline")
+    assert line["config"]["workload"] == "batched" and line["config"]["global_batch"] == 64
+    for mode in ("tf32", "3xtf32", "exact"):
+        e2e = line["modes"][mode]["e2e"]
+        assert e2e["value"] > 0 and e2e["h2d_bytes_per_step"] == 2 * 64 * 2048 * 2048 * 4
+        assert e2e["d2h_bytes_per_step"] == 64 * 2048 * 2048 * 4
+    sq = line["square8192"]
+    for mode in ("tf32", "3xtf32", "exact"):
+        assert sq[mode]["tflops"] > 0 and sq[mode]["launches_per_step"] >= 1
+    assert "sm_mhz" in sq["tf32"]["clocks"]
+    sus = line["sustained"]
+    assert sus["seconds"] >= 1.0 and sus["tflops_per_gpu"] > 0 and "reasons" in sus["clocks"]

@@ -109,3 +109,56 @@ def test_noalloc_refuses_what_it_cannot_hold():
     C = torch.zeros((64, 64), device=DEV)
     assert noalloc(A, B, C) == 2
     torch.cuda.synchronize()
+
+
+def test_noalloc_batched_transposed_with_broadcast():
+    """A batch of 4 transposed A views (M-major, read in place) against a
+    broadcast K-major B (a transposed view of [N, K]), twice in a row."""
+    g = torch.Generator(device=DEV).manual_seed(22)
+    A = torch.randn((4, 260, 300), generator=g, device=DEV).transpose(1, 2)   # [4, 300, 260]
+    B = torch.randn((196, 260), generator=g, device=DEV).t()                  # [260, 196]
+    R = torch.empty((4, 300, 196), device=DEV)
+    regular(A, B, R)
+    for _ in range(2):
+        N = torch.full_like(R, float("nan"))
+        assert noalloc(A, B, N) == 0, tlcuda.lib().tlc_last_error()
+        torch.cuda.synchronize()
+        assert not torch.isnan(N).any()
+        assert rel_fro(N, R) <= TOL
+        assert rel_fro(N, torch.matmul(A.double(), B.double())) <= TOL
+
+
+FRESH = r"""
+import ctypes, sys
+import torch
+sys.path.insert(0, {tests!r})
+import test_zz_no_alloc as t
+g = torch.Generator(device="cuda:0").manual_seed(23)
+A = torch.randn((2, 130, 70), generator=g, device="cuda:0")
+B = torch.randn((70, 150), generator=g, device="cuda:0")
+N1 = torch.empty((2, 130, 150), device="cuda:0")
+N2 = torch.empty_like(N1)
+R = torch.empty_like(N1)
+assert t.noalloc(A, B, N1) == 0   # the first GEMM of the process
+assert t.noalloc(A, B, N2) == 0
+t.regular(A, B, R)
+torch.cuda.synchronize()
+assert torch.equal(N1, N2), "two calls differ"
+assert t.rel_fro(N1, R) <= t.TOL, t.rel_fro(N1, R)
+print("fresh ok")
+"""
+
+
+def test_noalloc_first_call_in_a_fresh_process():
+    """In a process whose first GEMM is the allocation-free call (its set-up
+    runs inside that call), the result equals the regular entry point's."""
+    import os
+    import subprocess
+    import sys
+    tests = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([tests, os.path.join(os.path.dirname(tests), "torchlite-cpp_b200"),
+                                         os.path.dirname(tests), env.get("PYTHONPATH", "")])
+    r = subprocess.run([sys.executable, "-c", FRESH.format(tests=tests)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "fresh ok" in r.stdout, r.stdout + r.stderr

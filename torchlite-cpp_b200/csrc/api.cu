@@ -41,23 +41,35 @@ int check_launch(const char* what) {
     return TLC_OK;
 }
 
+void* current_context() {
+    using GetCurrent = int (*)(void**);  // CUresult cuCtxGetCurrent(CUcontext*)
+    static GetCurrent fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<GetCurrent>(f);
+    }();
+    void* c = nullptr;
+    if (!fn || fn(&c) != 0) return nullptr;
+    return c;
+}
+
 int scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
     *p = nullptr;
     if (bytes == 0) return TLC_OK;
-    static std::once_flag once[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64) {
-        // Keep freed pool memory instead of returning it to the driver, so
-        // repeated calls do not pay for fresh allocations.
-        std::call_once(once[dev], [dev] {
-            cudaMemPool_t pool;
-            if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-                uint64_t thr = ~0ull;
-                cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
-            }
-        });
-    }
+    static DeviceOnce once;
+    // Keep freed pool memory instead of returning it to the driver, so
+    // repeated calls do not pay for fresh allocations.
+    TLC_TRY(device_once(once, [](int dev) -> int {
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+            uint64_t thr = ~0ull;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+        }
+        return TLC_OK;
+    }));
     TLC_CUDA_TRY(cudaMallocAsync(p, bytes, s));
     return TLC_OK;
 }
@@ -528,33 +540,28 @@ struct DevCopy {
     }
 };
 
-cudaStream_t host_stream() {
-    // One non-blocking stream per device for the host-buffer forms.
-    static std::mutex mu;
-    static cudaStream_t streams[64] = {};
+// Streams the library keeps per device (and context) for the host-buffer
+// forms: [0] the work, [1] uploads and [2] downloads of the pipelined form.
+cudaStream_t library_stream(int which) {
+    static DeviceOnce once;
+    static cudaStream_t streams[64][3] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64) return nullptr;
-    if (!streams[dev]) cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking);
-    return streams[dev];
+    const int st = device_once(once, [](int d) -> int {
+        for (int i = 0; i < 3; ++i) {
+            streams[d][i] = nullptr;
+            TLC_CUDA_TRY(cudaStreamCreateWithFlags(&streams[d][i], cudaStreamNonBlocking));
+        }
+        return TLC_OK;
+    }, &dev);
+    return st == TLC_OK ? streams[dev][which] : nullptr;
 }
+
+cudaStream_t host_stream() { return library_stream(0); }
 
 // Upload and download streams per device for the pipelined host-buffer form.
 void copy_streams(cudaStream_t& in, cudaStream_t& out) {
-    static std::mutex mu;
-    static cudaStream_t s_in[64] = {}, s_out[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64) {
-        in = out = nullptr;
-        return;
-    }
-    if (!s_in[dev]) cudaStreamCreateWithFlags(&s_in[dev], cudaStreamNonBlocking);
-    if (!s_out[dev]) cudaStreamCreateWithFlags(&s_out[dev], cudaStreamNonBlocking);
-    in = s_in[dev];
-    out = s_out[dev];
+    in = library_stream(1);
+    out = library_stream(2);
 }
 
 View dense_view(float* data, std::initializer_list<int64_t> sizes) {

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <mutex>
 #include <string>
 
 #include "../../include/tlc.h"
@@ -33,6 +34,46 @@ void clear_error();
         int s_ = (expr);         \
         if (s_ != TLC_OK) return s_; \
     } while (0)
+
+// ---- per-device set-up ---------------------------------------------------------------
+//
+// Set-up that belongs to a device's CUDA context (kernel attributes, symbol
+// addresses, streams) runs once per device and context: again when the
+// context is re-created (after cudaDeviceReset), never twice at once from two
+// host threads.
+
+// The calling thread's current CUDA context (NULL if none is bound yet).
+void* current_context();
+
+struct DeviceOnce {
+    std::mutex mu;
+    void* ctx[64] = {};
+};
+
+// Runs setup(device) unless it already succeeded for the current device's
+// current context; *dev_out (if given) receives the device index.
+template <class F>
+int device_once(DeviceOnce& o, F&& setup, int* dev_out = nullptr) {
+    int dev = 0;
+    TLC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
+    if (dev_out) *dev_out = dev;
+    std::lock_guard<std::mutex> lk(o.mu);
+    void* c = current_context();
+    if (c && o.ctx[dev] == c) return TLC_OK;
+    const int st = setup(dev);
+    if (st == TLC_OK) o.ctx[dev] = current_context();
+    return st;
+}
+
+// Raises a kernel's dynamic shared-memory limit on the current device.
+template <class K>
+int smem_limit_once(DeviceOnce& o, K kernel, int bytes) {
+    return device_once(o, [&](int) -> int {
+        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        return TLC_OK;
+    });
+}
 
 // ---- launch bookkeeping ----------------------------------------------------------
 
@@ -146,6 +187,10 @@ int launch_softmax_backward(const float* g, const float* y, float* dx, int64_t r
 // Copy a strided view into a destination with its own strides (same shape).
 int launch_strided_copy_to(const float* src, int nd, const int64_t* sizes, const int64_t* sstr,
                            float* dst, const int64_t* dstr, cudaStream_t s);
+// Whether the tensor cores read fp32 operands truncated to TF32 on the current
+// device (checked once per device by one small product; false while unknown
+// and `s` is being captured).
+bool tf32_reads_truncated(cudaStream_t s);
 // Device error word written by bounded waits inside kernels (0 = none).
 int tc_error_word(int** p);
 // Launches a kernel whose bounded wait must time out (failure-detection test).

@@ -438,15 +438,8 @@ int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
         const int64_t lines = s.N * s.groups * s.patch;
         const int64_t plane_bytes = s.H * s.W * (int64_t)sizeof(float);
         if (s.W_out % 4 == 0 && s.W_out / 4 <= 256 && plane_bytes <= kIm2colPlaneMax) {
-            static bool configured[64] = {};  // function attributes are per device
-            int dev = 0;
-            TLC_CUDA_TRY(cudaGetDevice(&dev));
-            if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-            if (!configured[dev]) {
-                TLC_CUDA_TRY(cudaFuncSetAttribute(im2col_plane_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  kIm2colPlaneMax));
-                configured[dev] = true;
-            }
+            static DeviceOnce once;  // function attributes are per device
+            TLC_TRY(smem_limit_once(once, im2col_plane_kernel, kIm2colPlaneMax));
             im2col_plane_kernel<<<(unsigned)std::min<int64_t>(s.N * s.C_in, 148 * 16), 256, (size_t)plane_bytes,
                                   st>>>(in, col.f(), s);
         } else if (s.W_out % 4 == 0)

@@ -313,15 +313,8 @@ int heads_of(const tlc_tensor* const* ts, int n, const char* name, Heads& h) {
 template <int DM, bool VEC>
 int launch_fwd_t(const float* q, const float* k, const float* v, float* o, float* l, const Heads& h,
                  float scale, cudaStream_t s) {
-    static bool configured[64] = {};
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    if (!configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(flash_fwd_kernel<DM, VEC>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, FaCfg<DM>::SMEM));
-        configured[dev] = true;
-    }
+    static DeviceOnce once;
+    TLC_TRY(smem_limit_once(once, flash_fwd_kernel<DM, VEC>, FaCfg<DM>::SMEM));
     const int64_t tiles = (h.S + BQ - 1) / BQ;
     if (tiles * h.heads > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "flash_attention: too many tiles");
     flash_fwd_kernel<DM, VEC><<<(unsigned)(tiles * h.heads), 256, FaCfg<DM>::SMEM, s>>>(

@@ -694,18 +694,6 @@ __global__ void fa_bwd_prep_kernel(const float* __restrict__ dO, const float* __
     }
 }
 
-template <typename K>
-int configure(K kernel, int smem, bool* done) {
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    if (!done[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        done[dev] = true;
-    }
-    return TLC_OK;
-}
-
 }  // namespace
 
 bool flash_bwd_tc_supported(int d, const float* const* ptrs, int n) {
@@ -718,9 +706,9 @@ bool flash_bwd_tc_supported(int d, const float* const* ptrs, int n) {
 int flash_backward_tc(const float* dout, const float* q, const float* k, const float* v,
                       const float* o, const float* lse, float* dq, float* dk, float* dv,
                       int64_t heads, int S, int d, float scale, cudaStream_t s) {
-    static bool cfg_dkdv[64] = {}, cfg_dq[64] = {};
-    TLC_TRY(configure(flash_bwd_dkdv_kernel, DKV_SMEM, cfg_dkdv));
-    TLC_TRY(configure(flash_bwd_dq_kernel, DQ_SMEM, cfg_dq));
+    static DeviceOnce cfg_dkdv, cfg_dq;
+    TLC_TRY(smem_limit_once(cfg_dkdv, flash_bwd_dkdv_kernel, DKV_SMEM));
+    TLC_TRY(smem_limit_once(cfg_dq, flash_bwd_dq_kernel, DQ_SMEM));
     if (heads > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "flash_attention_backward: too many heads");
     const int tiles = (S + TR - 1) / TR;
     const int S_pad = tiles * TR;

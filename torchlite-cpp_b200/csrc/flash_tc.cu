@@ -526,14 +526,8 @@ bool flash_tc_supported(int d, const float* q, const float* k, const float* v) {
 
 int flash_forward_tc(const float* q, const float* k, const float* v, float* o, float* lse,
                      int64_t heads, int S, int d, float scale, cudaStream_t s) {
-    static bool configured[64] = {};
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    if (!configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        configured[dev] = true;
-    }
+    static DeviceOnce once;
+    TLC_TRY(smem_limit_once(once, flash_tc_kernel, SMEM));
     if (heads > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "flash_attention: too many heads");
     FtParams p;
     memset(&p, 0, sizeof(p));

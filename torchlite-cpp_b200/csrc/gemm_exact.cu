@@ -608,14 +608,8 @@ template <bool AK, bool BKM, bool VC, bool WIDE>
 int launch_tma_variant(const ExactTmaParams& p, dim3 grid, cudaStream_t s) {
     using S = TmaCfg<WIDE>;
     auto kernel = exact_tma_kernel<AK, BKM, VC, WIDE>;
-    static int configured[64] = {};
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    if (!configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
-        configured[dev] = 1;
-    }
+    static DeviceOnce once;
+    TLC_TRY(smem_limit_once(once, kernel, S::SMEM));
     kernel<<<grid, NT, S::SMEM, s>>>(p);
     count_launch();
     return check_launch("gemm_exact_tma");

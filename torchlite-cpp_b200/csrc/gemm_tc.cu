@@ -66,6 +66,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -761,28 +762,26 @@ int repack(OperandMap& o, int nb, TcScratch& sc, int slot, cudaStream_t s) {
     return TLC_OK;
 }
 
+// Device address of g_tc_error on the current device (per context).
 int* error_word() {
+    static DeviceOnce once;
     static int* words[64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return nullptr;
-    if (!words[dev]) {
+    const int st = device_once(once, [](int d) -> int {
         int* p = nullptr;
-        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_tc_error) != cudaSuccess) return nullptr;
-        words[dev] = p;
-    }
-    return words[dev];
+        TLC_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_tc_error));
+        words[d] = p;
+        return TLC_OK;
+    }, &dev);
+    return st == TLC_OK ? words[dev] : nullptr;
 }
 
 template <int CG, int UN, bool X3>
 int launch_variant(const TcParams& prm, cudaStream_t s) {
     using S = Cfg<CG, UN, X3>;
     auto kernel = tc_gemm_kernel<CG, UN, X3>;
-    static int configured[64] = {};
+    static DeviceOnce once;
     static int max_units[64] = {};
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.blockDim = dim3(S::THREADS, 1, 1);
@@ -796,11 +795,12 @@ int launch_variant(const TcParams& prm, cudaStream_t s) {
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    if (!configured[dev]) {
+    int dev = 0;
+    TLC_TRY(device_once(once, [&](int d) -> int {
         TLC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           S::TOTAL));
         int sms = 148;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
         int units = CG == 2 ? sms / 2 : sms;
         if (CG == 2) {
             // How many CTA pairs can be resident at once (pairs share a GPC).
@@ -811,9 +811,9 @@ int launch_variant(const TcParams& prm, cudaStream_t s) {
                 units = std::min(units, clusters);
             cudaGetLastError();
         }
-        max_units[dev] = units;
-        configured[dev] = 1;
-    }
+        max_units[d] = units;
+        return TLC_OK;
+    }, &dev));
     const int64_t units = std::min<int64_t>(prm.num_tiles, max_units[dev]);
     cfg.gridDim = dim3((unsigned)(units * CG), 1, 1);
     TLC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, prm));
@@ -924,6 +924,88 @@ uint32_t b_cols_for(const Gemm& g, bool x3) {
 
 }  // namespace
 
+namespace {
+
+// 1 / 0 per device: whether the tensor cores read an fp32 operand truncated
+// to TF32; -1 while unknown.
+int g_tf32_truncates[64] = {-1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1,
+                            -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1,
+                            -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1,
+                            -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1};
+
+// One TF32 product whose inputs tell truncation from rounding: every A value
+// is 1 + 2^-11 + 2^-12 (fp32 bits 0x3F801800), which TF32 truncation makes 1
+// and any round-to-nearest makes 1 + 2^-10; B is all ones and K = 32, so
+// C[m,n] = 32 under truncation and 32.03125 under rounding.  Sets
+// g_tf32_truncates[dev] to 1 only if all 128 x 128 outputs are exactly 32.
+int check_tf32_truncation(int dev) {
+    constexpr int M = 128, N = 128, K = 32;
+    std::vector<float> a(M * K), b(K * N, 1.0f), c(M * N, 0.0f);
+    const uint32_t bits = 0x3F801800u;
+    float av;
+    std::memcpy(&av, &bits, sizeof(av));
+    std::fill(a.begin(), a.end(), av);
+    float* d = nullptr;
+    TLC_CUDA_TRY(cudaMalloc(&d, sizeof(float) * (M * K + K * N + M * N)));
+    cudaStream_t st = nullptr;
+    int rc = TLC_OK;
+    do {
+        if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+            rc = set_error(TLC_ERR_CUDA, "tf32 check: cudaStreamCreate failed");
+            break;
+        }
+        if (cudaMemcpy(d, a.data(), sizeof(float) * M * K, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(d + M * K, b.data(), sizeof(float) * K * N, cudaMemcpyHostToDevice) != cudaSuccess) {
+            rc = set_error(TLC_ERR_CUDA, "tf32 check: copy failed");
+            break;
+        }
+        Gemm g{};
+        g.M = M;
+        g.N = N;
+        g.K = K;
+        g.A = d;
+        g.a_rs = K;
+        g.a_cs = 1;
+        g.B = d + M * K;
+        g.b_rs = N;
+        g.b_cs = 1;
+        g.C = d + M * K + K * N;
+        g.c_rs = N;
+        if ((rc = gemm_tc(g, TLC_MODE_TF32, st)) != TLC_OK) break;
+        if (cudaStreamSynchronize(st) != cudaSuccess ||
+            cudaMemcpy(c.data(), g.C, sizeof(float) * M * N, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            rc = set_error(TLC_ERR_CUDA, "tf32 check: the product failed");
+            break;
+        }
+        g_tf32_truncates[dev] = std::all_of(c.begin(), c.end(), [](float v) { return v == 32.0f; }) ? 1 : 0;
+    } while (false);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(d);
+    return rc;
+}
+
+}  // namespace
+
+bool tf32_reads_truncated(cudaStream_t s) {
+    // No set-up work while `s` is being captured into a graph: the split
+    // that does not depend on the answer serves until the check has run.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        int dev = 0;
+        cudaGetDevice(&dev);
+        return dev >= 0 && dev < 64 && g_tf32_truncates[dev] == 1;
+    }
+    static DeviceOnce once;
+    int dev = 0;
+    if (device_once(once, check_tf32_truncation, &dev) != TLC_OK) {
+        clear_error();
+        cudaGetLastError();
+        return false;
+    }
+    return g_tf32_truncates[dev] == 1;
+}
+
 int tc_error_word(int** p) {
     *p = error_word();
     return *p ? TLC_OK : set_error(TLC_ERR_CUDA, "no device error word");
@@ -950,22 +1032,31 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     TcParams prm;
     memset(&prm, 0, sizeof(prm));
     if (x3) {
-        // hi is the operand itself: kind::tf32 reads an fp32 input truncated to
-        // TF32 (its low 13 mantissa bits ignored).  Only lo = x - trunc(x),
-        // exact in fp32, is written, into a plane of the operand's layout.
+        // When kind::tf32 reads an fp32 input truncated to TF32 (its low 13
+        // mantissa bits ignored; checked once per device), hi is the operand
+        // itself and only lo = x - trunc(x), exact in fp32, is written, into a
+        // plane of the operand's layout.  Otherwise hi = round(x) and
+        // lo = x - hi are both written.
+        const bool lo_only = tf32_reads_truncated(s);
         OperandMap* ops[2] = {&A, &B};
         CUtensorMap* maps[2] = {prm.tmA, prm.tmB};
         for (int o = 0; o < 2; ++o) {
             const int64_t n = span_elems(ops[o]->inner, ops[o]->outer, ops[o]->outer_stride,
                                          ops[o]->bsz, ops[o]->bstride, g.nb);
-            TLC_TRY(scratch_alloc(&sc.p[2 + o], sizeof(float) * (size_t)n, s));
-            float* lo = static_cast<float*>(sc.p[2 + o]);
-            split_lo_kernel<<<grid_split(n), 256, 0, s>>>(ops[o]->base, lo, n);
+            TLC_TRY(scratch_alloc(&sc.p[2 + o], sizeof(float) * (size_t)n * (lo_only ? 1 : 2), s));
+            float* plane = static_cast<float*>(sc.p[2 + o]);
+            OperandMap h = *ops[o], l = *ops[o];
+            if (lo_only) {
+                split_lo_kernel<<<grid_split(n), 256, 0, s>>>(ops[o]->base, plane, n);
+                l.base = plane;
+            } else {
+                split_tf32_kernel<<<grid_split(n), 256, 0, s>>>(ops[o]->base, plane, plane + n, n);
+                h.base = plane;
+                l.base = plane + n;
+            }
             count_launch();
-            TLC_TRY(check_launch("split_tf32_lo"));
-            OperandMap l = *ops[o];
-            l.base = lo;
-            TLC_TRY(encode(&maps[o][0], *ops[o]));
+            TLC_TRY(check_launch("split_tf32"));
+            TLC_TRY(encode(&maps[o][0], h));
             TLC_TRY(encode(&maps[o][1], l));
         }
     } else {
@@ -1017,22 +1108,22 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / 
 
 namespace {
 
-// Device address of g_noalloc_scratch on the current device, looked up once.
+// Device address of g_noalloc_scratch on the current device: looked up once
+// per device, with that device current, and again if the device's context
+// is re-created (cudaDeviceReset), since the old address then dangles.
 int noalloc_scratch(float** out) {
-    static std::mutex mu;
+    static DeviceOnce once;
     static float* addr[64] = {};
     int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    TLC_TRY(device_once(once, [](int d) -> int {
         float* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch);
         if (e != cudaSuccess || !p)
             return set_error(TLC_ERR_CUDA, std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") +
                                                cudaGetErrorString(e));
-        addr[dev] = p;
-    }
+        addr[d] = p;
+        return TLC_OK;
+    }, &dev));
     *out = addr[dev];
     return TLC_OK;
 }

@@ -443,16 +443,9 @@ int launch_epilogue(float* C, int64_t rows, int64_t cols, float s, bool apply_sc
 template <int VPL>
 int launch_softmax_block(const float* x, float* y, int64_t rows, int D, cudaStream_t st) {
     const size_t smem = sizeof(float) * (SM_ROWS * (size_t)(D + 1) + SM_ROWS);
-    static bool configured[64] = {};
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    if (!configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(softmax_block_kernel<VPL>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)(sizeof(float) * (SM_ROWS * 1025 + SM_ROWS))));
-        configured[dev] = true;
-    }
+    static DeviceOnce once;
+    TLC_TRY(smem_limit_once(once, softmax_block_kernel<VPL>,
+                            (int)(sizeof(float) * (SM_ROWS * 1025 + SM_ROWS))));
     const int64_t groups = (rows + SM_ROWS - 1) / SM_ROWS;
     const int grid = (int)std::min<int64_t>(groups, 148 * 8);
     softmax_block_kernel<VPL><<<grid, SM_ROWS * 32, smem, st>>>(x, y, rows, D);
@@ -488,16 +481,9 @@ template <int VPL>
 int launch_softmax_backward_block(const float* g, const float* y, float* dx, int64_t rows, int D,
                                   cudaStream_t st) {
     const size_t smem = sizeof(float) * (SM_ROWS * (size_t)(D + 1) + 2 * SM_ROWS * 8 + SM_ROWS);
-    static bool configured[64] = {};
-    int dev = 0;
-    TLC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(TLC_ERR_UNSUPPORTED, "device index above 63");
-    if (!configured[dev]) {
-        TLC_CUDA_TRY(cudaFuncSetAttribute(softmax_backward_block_kernel<VPL>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)(sizeof(float) * (SM_ROWS * 1025 + 2 * SM_ROWS * 8 + SM_ROWS))));
-        configured[dev] = true;
-    }
+    static DeviceOnce once;
+    TLC_TRY(smem_limit_once(once, softmax_backward_block_kernel<VPL>,
+                            (int)(sizeof(float) * (SM_ROWS * 1025 + 2 * SM_ROWS * 8 + SM_ROWS))));
     const int64_t groups = (rows + SM_ROWS - 1) / SM_ROWS;
     const int grid = (int)std::min<int64_t>(groups, 148 * 8);
     softmax_backward_block_kernel<VPL><<<grid, SM_ROWS * 32, smem, st>>>(g, y, dx, rows, D);

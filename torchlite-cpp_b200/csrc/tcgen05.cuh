@@ -199,15 +199,13 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
             "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
             : "memory");
 }
-// CTA pairs: one commit that arrives on the barrier at this shared offset in
-// both CTAs of the pair (a commit, not a load: no data crosses CTAs).
+// CTA pairs: arrive on the barrier at this shared offset in both CTAs of the
+// pair once the issued MMAs complete, by one unicast commit per CTA (a commit,
+// not a load: no data crosses CTAs; measured to cost the same as one commit
+// multicast to both).
 __device__ __forceinline__ void umma_commit_both(uint32_t bar_local) {
-    const uint16_t both = 0x3;
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;" ::"r"(bar_local),
-        "h"(both)
-        : "memory");
+    umma_commit<2>(mapa(bar_local, 0));
+    umma_commit<2>(mapa(bar_local, 1));
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -13,20 +13,16 @@
 // as the reference records it (caches of the contiguous inputs, squeeze flags),
 // so the backward pass (whose two products call tl::matmul again) also runs on
 // the GPU.  TL_GEMM_MODE selects exact (default, bit-identical) / tf32 / 3xtf32.
-// Setting TLC_REFERENCE_MATMUL=1 in the environment routes calls back to the
-// reference's own CPU matmul (__real_...), for side-by-side checks.
+// There is no route back to the CPU: every call runs on the device or fails.
 #include <tl/autograd.h>
 #include <tl/ops.h>
 #include <tl/tensor.h>
 
 #include <tlc.h>
 
-#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <vector>
-
-extern "C" tl::Tensor __real__ZN2tl6matmulERKNS_6TensorES2_(const tl::Tensor&, const tl::Tensor&);
 
 namespace {
 
@@ -42,19 +38,10 @@ tlc_tensor host_view(const tl::Tensor& t) {
     return v;
 }
 
-bool use_reference() {
-    static const bool r = [] {
-        const char* e = std::getenv("TLC_REFERENCE_MATMUL");
-        return e && std::string(e) == "1";
-    }();
-    return r;
-}
-
 }  // namespace
 
 extern "C" tl::Tensor __wrap__ZN2tl6matmulERKNS_6TensorES2_(const tl::Tensor& a_in,
                                                              const tl::Tensor& b_in) {
-    if (use_reference()) return __real__ZN2tl6matmulERKNS_6TensorES2_(a_in, b_in);
     tlc_tensor va = host_view(a_in), vb = host_view(b_in);
     int32_t nd = 0;
     int64_t sz[TLC_MAX_DIMS];
