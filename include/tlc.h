@@ -202,6 +202,13 @@ int tlc_gemm_3xtf32_noalloc(const tlc_gemm_desc* desc, void* stream);
 /* sum(input, dim, keepdim) of src/ops.cpp:1181-1233 for a contiguous input
  * viewed as [outer, D, inner]: out[o,n] = sum over d ascending, from 0.0f. */
 int tlc_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner, void* stream);
+/* The same sums continued from a running value: out[o,n] = init[o,n] +
+ * in[o,0,n] + in[o,1,n] + ... in that order (init == NULL: from 0.0f, as
+ * tlc_sum_dim).  A sum over a dim whose entries are spread over devices or
+ * ranks in order continues on each one from the previous one's result, which
+ * gives the reference's single sequential sum bit for bit. */
+int tlc_sum_dim_from(const float* in, const float* init, float* out, int64_t outer, int64_t D,
+                     int64_t inner, void* stream);
 /* out = a + b element-wise (same shape, contiguous): src/ops.cpp:75-103. */
 int tlc_add(const float* a, const float* b, float* out, int64_t n, void* stream);
 /* Tensor::contiguous (src/tensor.cpp:174-193): copy a strided view into a
@@ -306,6 +313,45 @@ int tlc_flash_attention_backward(const tlc_tensor* grad_out, const tlc_tensor* q
  * all copies are done. */
 int tlc_load_tlmd(const char* path, int32_t count, const tlc_tensor* dst, void* stream);
 int tlc_save_tlmd(const char* path, int32_t count, const tlc_tensor* src, void* stream);
+
+/* ---- device groups: one process over several GPUs ----------------------------
+ * The reference spreads one matmul over host threads (gemm_mt's row bands,
+ * src/ops.cpp:569-587); a group spreads it over GPUs of the box, called from
+ * one host thread.  A batched / broadcast product is split over its flattened
+ * batch (a broadcast operand goes whole to every GPU); a single product from
+ * host buffers over row blocks of A and C; a single product in device memory
+ * over output column blocks (A sent to every GPU by one NCCL broadcast, each
+ * GPU its own column block of B).  Results are those of the single-device
+ * entry points bit for bit: no product's additions are split across GPUs,
+ * and the dB of a broadcast B is summed by an ordered chain over the GPUs
+ * (tlc_sum_dim_from).  NCCL is loaded at run time; a device may be listed
+ * more than once (its shares then run side by side).  Calls on one group are
+ * serialised; a call returns when its results are in place (device form: in
+ * stream order on `stream`). */
+typedef struct tlc_group tlc_group;
+
+/* A group over `devices[0..n)` (1 <= n <= 64): a stream and a worker thread
+ * per member, peer access between members, and one NCCL communicator per
+ * member when NCCL loads and the devices are distinct. */
+int tlc_group_create(const int* devices, int n, tlc_group** out);
+int tlc_group_destroy(tlc_group* g);
+/* Members, and whether the group holds NCCL communicators (0 / 1). */
+int tlc_group_size(const tlc_group* g, int* n, int* uses_nccl);
+/* tl::matmul (src/ops.cpp:605-699) on host buffers over the group: each GPU
+ * copies in its share, computes, copies its share of `out` back; the
+ * multi-GPU form of tlc_matmul_host, same shapes and errors. */
+int tlc_group_matmul_host(tlc_group* g, const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out,
+                          int mode);
+/* MatmulBackward (src/autograd.cpp:341-384) on host buffers over the group:
+ * the multi-GPU form of tlc_matmul_backward_host. */
+int tlc_group_matmul_backward_host(tlc_group* g, const tlc_tensor* grad, const tlc_tensor* a,
+                                   const tlc_tensor* b, tlc_tensor* da, tlc_tensor* db,
+                                   int accumulate, int mode);
+/* tl::matmul with a, b and out in the memory of the group's first device (the
+ * current device) over the group: the multi-GPU form of tlc_matmul, ordered
+ * after and before the work of `stream` (on the first device). */
+int tlc_group_matmul(tlc_group* g, const tlc_tensor* a, const tlc_tensor* b, tlc_tensor* out,
+                     int mode, void* stream);
 
 /* ---- multi-GPU partitioning ------------------------------------------------
  * One process per GPU.  A batched GEMM is split over its flattened batch

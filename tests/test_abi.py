@@ -107,3 +107,14 @@ def test_modes():
     assert L.tlc_mode_from_string(b"3xtf32") == 2
     assert L.tlc_mode_from_string(b"fp16") == -1
     assert L.tlc_status_string(5) == b"kernel wait timed out"
+
+
+def test_group_argument_errors_without_a_gpu():
+    """tlc_group_create rejects an empty device list before touching a GPU."""
+    L = tlcuda.lib()
+    g = ctypes.c_void_p()
+    assert L.tlc_group_create((ctypes.c_int * 1)(0), 0, ctypes.byref(g)) == 1
+    assert "1 to 64 devices" in L.tlc_last_error().decode()
+    assert L.tlc_group_destroy(None) == 0
+    n = ctypes.c_int(0)
+    assert L.tlc_group_size(None, ctypes.byref(n), None) == 1

@@ -78,7 +78,11 @@ def _gloo_worker(rank, world, port, q):
         import tldist
         dC = inputs.normal(np.random.default_rng(9), (5, 9, 6))
         G = O.matmul(np.ascontiguousarray(A[b0:b1].transpose(0, 2, 1)), dC[b0:b1])
-        sum0 = lambda st: torch.from_numpy(O.sum_dim(st.numpy(), 0, False))  # noqa: E731
+        def sum0(st, init=None):
+            # the oracle's sequential sum; continuing from `init` is the sum
+            # of [init, entries...] from 0.0f (0 + init == init here)
+            x = st.numpy() if init is None else np.concatenate([init.numpy()[None], st.numpy()])
+            return torch.from_numpy(O.sum_dim(x, 0, False))
         dB = tldist.chained_batch_sum(torch.from_numpy(G), sum0=sum0).numpy()
         ref_dA, ref_dB = O.matmul_backward(dC, A, B)
         ok_bwd = np.array_equal(dB.view(np.uint32), ref_dB.view(np.uint32))

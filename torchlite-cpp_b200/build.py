@@ -64,7 +64,7 @@ def build(jobs: int = 8, verbose: bool = False, ptxas_info: bool = False) -> dic
             logs[futs[f]] = f.result()
     so = os.path.join(LIB, "libtl_cuda.so")
     if _stale(so, objs):
-        _run([NVCC] + ARCH + ["-shared", "-o", so] + objs, verbose)
+        _run([NVCC] + ARCH + ["-shared", "-o", so] + objs + ["-ldl"], verbose)
 
     # C++ tl:: layer over the C ABI.
     host_src = sorted(glob.glob(os.path.join(PKG, "host", "src", "*.cpp")))

@@ -994,6 +994,14 @@ int tlc_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t i
     return launch_sum_dim(in, out, outer, D, inner, (cudaStream_t)stream);
 }
 
+int tlc_sum_dim_from(const float* in, const float* init, float* out, int64_t outer, int64_t D,
+                     int64_t inner, void* stream) {
+    clear_error();
+    if (outer < 0 || D < 0 || inner < 0)
+        return set_error(TLC_ERR_INVALID_ARGUMENT, "tlc_sum_dim_from: negative size");
+    return launch_sum_dim(in, out, outer, D, inner, (cudaStream_t)stream, init);
+}
+
 int tlc_add(const float* a, const float* b, float* out, int64_t n, void* stream) {
     clear_error();
     if (n < 0) return set_error(TLC_ERR_INVALID_ARGUMENT, "tlc_add: negative size");

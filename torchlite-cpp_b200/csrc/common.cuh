@@ -152,8 +152,9 @@ inline BatchOffsets batch_offsets(const Gemm& g) {
 // Kernels (each returns a tlc_status).
 int gemm_exact(const Gemm& g, cudaStream_t s);
 int gemm_tc(const Gemm& g, int mode, cudaStream_t s);
+// out[o,n] = sum over d ascending of in[o,d,n], from init[o,n] (NULL: from 0.0f).
 int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
-                   cudaStream_t s);
+                   cudaStream_t s, const float* init = nullptr);
 int launch_add(const float* a, const float* b, float* out, int64_t n, cudaStream_t s);
 int launch_zero_plus(const float* in, float* out, int64_t n, cudaStream_t s);
 int launch_strided_copy(const float* src, int nd, const int64_t* sizes, const int64_t* strides,

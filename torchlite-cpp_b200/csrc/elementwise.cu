@@ -25,14 +25,14 @@ int grid_for(int64_t n, int threads) {
 // out[o, n] = ((0 + x[o,0,n]) + x[o,1,n]) + ... : the order of sum()
 // (src/ops.cpp:1214-1222).  One thread per output element; threads of a warp
 // take consecutive n, so every step of the d loop is a coalesced row read.
-__global__ void sum_dim_kernel(const float* __restrict__ in, float* __restrict__ out,
-                               int64_t outer, int64_t D, int64_t inner) {
+__global__ void sum_dim_kernel(const float* __restrict__ in, const float* __restrict__ init,
+                               float* __restrict__ out, int64_t outer, int64_t D, int64_t inner) {
     const int64_t total = outer * inner;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t o = i / inner, n = i - o * inner;
         const float* p = in + o * D * inner + n;
-        float acc = 0.0f;
+        float acc = init ? init[i] : 0.0f;
         for (int64_t d = 0; d < D; ++d) acc = __fadd_rn(acc, p[d * inner]);
         out[i] = acc;
     }
@@ -46,6 +46,7 @@ __global__ void sum_dim_kernel(const float* __restrict__ in, float* __restrict__
 // order of every sum is the reference's.
 constexpr int SUM_ROWS = 168;  // rows per tile: 24 per loader warp (2 tiles: 42 KB)
 __global__ void __launch_bounds__(256) sum_dim_strip_kernel(const float* __restrict__ in,
+                                                            const float* __restrict__ init,
                                                             float* __restrict__ out, int64_t outer,
                                                             int64_t D, int64_t inner) {
     __shared__ float tile[2][SUM_ROWS][32];
@@ -57,7 +58,7 @@ __global__ void __launch_bounds__(256) sum_dim_strip_kernel(const float* __restr
     const bool col_ok = n < inner;
     const float* base = in + o * D * inner + n;
     const int64_t tiles = (D + SUM_ROWS - 1) / SUM_ROWS;
-    float acc = 0.0f;
+    float acc = (init && col_ok) ? init[o * inner + n] : 0.0f;
     // loaders: warp w (1..7) stages rows w - 1, w + 6, ... of each tile
     auto stage = [&](int64_t t, int buf) {
         const int64_t d0 = t * SUM_ROWS;
@@ -161,17 +162,17 @@ __global__ void gather_colblocks_kernel(const float* __restrict__ g, float* __re
 }  // namespace
 
 int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
-                   cudaStream_t s) {
+                   cudaStream_t s, const float* init) {
     const int64_t n = outer * inner;
     if (n == 0) return TLC_OK;
     // few outputs and long chains: the strip kernel keeps enough loads in flight
     const int64_t strips = outer * ((inner + 31) / 32);
     if (inner >= 32 && D >= 64 && n < 148 * 1024 && strips < (int64_t(1) << 31)) {
-        sum_dim_strip_kernel<<<(unsigned)strips, 256, 0, s>>>(in, out, outer, D, inner);
+        sum_dim_strip_kernel<<<(unsigned)strips, 256, 0, s>>>(in, init, out, outer, D, inner);
         count_launch();
         return check_launch("sum_dim_strip");
     }
-    sum_dim_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, out, outer, D, inner);
+    sum_dim_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, init, out, outer, D, inner);
     count_launch();
     return check_launch("sum_dim");
 }

@@ -82,6 +82,7 @@ SIGNATURES = {
     "tlc_gemm": ([_P(GemmDesc), _i, _v], _i),
     "tlc_gemm_3xtf32_noalloc": ([_P(GemmDesc), _v], _i),
     "tlc_sum_dim": ([_v, _v, _i64, _i64, _i64, _v], _i),
+    "tlc_sum_dim_from": ([_v, _v, _v, _i64, _i64, _i64, _v], _i),
     "tlc_add": ([_v, _v, _v, _i64, _v], _i),
     "tlc_contiguous": ([_T, _v, _v], _i),
     "tlc_matmul_fused": ([_T, _T, ctypes.c_float, _T, _T, _i, _v], _i),
@@ -101,6 +102,12 @@ SIGNATURES = {
     "tlc_shard_range": ([_i64, _i, _i, _P(_i64), _P(_i64)], _i),
     "tlc_shard_cols": ([_i64, _i, _i, _i64, _P(_i64), _P(_i64)], _i),
     "tlc_gather_colblocks": ([_v, _v, _i64, _i64, _i, _P(_i64), _v], _i),
+    "tlc_group_create": ([_P(ctypes.c_int), _i, _P(_v)], _i),
+    "tlc_group_destroy": ([_v], _i),
+    "tlc_group_size": ([_v, _P(_i), _P(_i)], _i),
+    "tlc_group_matmul_host": ([_v, _T, _T, _T, _i], _i),
+    "tlc_group_matmul_backward_host": ([_v, _T, _T, _T, _T, _T, _i, _i], _i),
+    "tlc_group_matmul": ([_v, _T, _T, _T, _i, _v], _i),
 }
 
 _lib = None
@@ -261,16 +268,22 @@ def gemm(A, B, C, M, N, K, a_rs, a_cs, b_rs, b_cs, c_rs, batch=(), a_bs=(), b_bs
     _check(lib().tlc_gemm(ctypes.byref(d), mode_id(mode), _stream_ptr(stream)))
 
 
-def sum_dim0(stack, out=None, stream=None):
+def sum_dim0(stack, out=None, stream=None, init=None):
     """sum over dim 0 of a contiguous CUDA tensor, ascending from 0.0f
-    (tlc_sum_dim with outer = 1): the reference's sum(x, 0) order."""
+    (tlc_sum_dim with outer = 1): the reference's sum(x, 0) order.  With
+    `init` (the shape of one entry) the sum continues from it:
+    init + stack[0] + stack[1] + ... (tlc_sum_dim_from)."""
     import torch
     assert stack.is_contiguous()
     if out is None:
         out = torch.empty(stack.shape[1:], dtype=torch.float32, device=stack.device)
     inner = out.numel()
-    _check(lib().tlc_sum_dim(ctypes.c_void_p(stack.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                             1, stack.shape[0], inner, _stream_ptr(stream)))
+    if init is not None:
+        assert init.is_contiguous() and init.numel() == inner
+    _check(lib().tlc_sum_dim_from(ctypes.c_void_p(stack.data_ptr()),
+                                  ctypes.c_void_p(init.data_ptr() if init is not None else None),
+                                  ctypes.c_void_p(out.data_ptr()), 1, stack.shape[0], inner,
+                                  _stream_ptr(stream)))
     return out
 
 
@@ -455,3 +468,65 @@ def gather_colblocks(gathered, out, M, N, col_begin, stream=None):
                                       ctypes.c_void_p(out.data_ptr()), M, N, world, cb,
                                       _stream_ptr(stream)))
     return out
+
+
+class Group:
+    """A device group (tlc_group_*): one tl::matmul over several GPUs of the
+    box from this process.  `devices` may repeat a device."""
+
+    def __init__(self, devices):
+        self.devices = list(devices)
+        arr = (ctypes.c_int * len(self.devices))(*self.devices)
+        self._g = ctypes.c_void_p()
+        _check(lib().tlc_group_create(arr, len(self.devices), ctypes.byref(self._g)))
+
+    def size(self):
+        n, nc = ctypes.c_int(0), ctypes.c_int(0)
+        _check(lib().tlc_group_size(self._g, ctypes.byref(n), ctypes.byref(nc)))
+        return n.value, bool(nc.value)
+
+    def matmul_host(self, a, b, mode="exact", out=None):
+        shape = matmul_shape(a, b)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        va, vb, vo = view_of(a), view_of(b), view_of(out)
+        _check(lib().tlc_group_matmul_host(self._g, ctypes.byref(va), ctypes.byref(vb),
+                                           ctypes.byref(vo), mode_id(mode)))
+        return out
+
+    def matmul_backward_host(self, grad, a, b, mode="exact", da=None, db=None, accumulate=False,
+                             need_a=True, need_b=True):
+        if need_a and da is None:
+            da = np.empty(a.shape, np.float32)
+        if need_b and db is None:
+            db = np.empty(b.shape, np.float32)
+        vg, va, vb = view_of(grad), view_of(a), view_of(b)
+        vda = view_of(da) if need_a else Tensor()
+        vdb = view_of(db) if need_b else Tensor()
+        _check(lib().tlc_group_matmul_backward_host(self._g, ctypes.byref(vg), ctypes.byref(va),
+                                                    ctypes.byref(vb), ctypes.byref(vda),
+                                                    ctypes.byref(vdb), int(accumulate),
+                                                    mode_id(mode)))
+        return da, db
+
+    def matmul(self, a, b, mode="exact", out=None, stream=None):
+        """a, b, out: CUDA tensors on the group's first device."""
+        import torch
+        shape = matmul_shape(a, b)
+        if out is None:
+            out = torch.empty(shape, dtype=torch.float32, device=a.device)
+        va, vb, vo = view_of(a), view_of(b), view_of(out)
+        _check(lib().tlc_group_matmul(self._g, ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vo),
+                                      mode_id(mode), _stream_ptr(stream)))
+        return out
+
+    def close(self):
+        if self._g:
+            _check(lib().tlc_group_destroy(self._g))
+            self._g = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

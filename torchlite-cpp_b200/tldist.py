@@ -60,17 +60,16 @@ def batch_sharded_matmul(A, B, mode="tf32", gather=False, group=None):
     C = tlcuda.matmul(A[b0:b1], Bs, mode=mode)
     if not gather or P == 1:
         return C
-    # all_gather_into_tensor takes equal shards: pad ragged ones
-    per = -(-A.shape[0] // P)
-    buf = torch.zeros((per,) + tuple(C.shape[1:]), device=C.device, dtype=C.dtype)
-    buf[: C.shape[0]] = C
-    out = torch.empty((per * P,) + tuple(C.shape[1:]), device=C.device, dtype=C.dtype)
-    dist.all_gather_into_tensor(out, buf, group=group)
-    keep = []
-    for q in range(P):
-        s, e = batch_shard(A.shape[0], P, q)
-        keep.append(torch.arange(q * per, q * per + (e - s), device=C.device))
-    return out[torch.cat(keep)]
+    out = torch.empty((A.shape[0],) + tuple(C.shape[1:]), device=C.device, dtype=C.dtype)
+    if A.shape[0] % P == 0:
+        # equal shards land in place: rank q's entries are [q*per, (q+1)*per)
+        dist.all_gather_into_tensor(out, C, group=group)
+        return out
+    # ragged shards (the first count % P ranks hold one more): every rank's
+    # shard is gathered straight into its rows of `out`
+    parts = [out[slice(*batch_shard(A.shape[0], P, q))] for q in range(P)]
+    dist.all_gather(parts, C, group=group)
+    return out
 
 
 def chained_batch_sum(local_stack, sum0=None, group=None):
@@ -83,20 +82,20 @@ def chained_batch_sum(local_stack, sum0=None, group=None):
     src/ops.cpp:1181-1233).  The chain keeps that order across ranks: rank r
     receives the running sum of ranks < r, continues it over its own entries
     and sends it on; the last rank broadcasts the total.  Continuing is
-    sum0([running, entries...]), i.e. (((0 + running) + e0) + e1)...; 0 + x
-    equals x bit for bit here because a running sum that starts at +0.0 is
-    never -0.0.  `sum0` sums a stack over dim 0 from 0.0f (default: the
-    library's tlc_sum_dim on the GPU)."""
+    ((running + e0) + e1)..., the same additions as one sequential sum.
+    `sum0(stack, init=...)` sums a stack over dim 0 from `init` (from 0.0f
+    when init is None; default: the library's tlc_sum_dim_from on the GPU)."""
     import torch
     import torch.distributed as dist
     if sum0 is None:
         sum0 = tlcuda.sum_dim0
     P, r = world()
     shape = tuple(local_stack.shape[1:])
-    run = torch.zeros((1,) + shape, dtype=local_stack.dtype, device=local_stack.device)
+    run = None
     if P > 1 and r > 0:
+        run = torch.empty(shape, dtype=local_stack.dtype, device=local_stack.device)
         dist.recv(run, src=r - 1, group=group)
-    total = sum0(torch.cat([run, local_stack]).contiguous())
+    total = sum0(local_stack.contiguous(), init=run)
     if P == 1:
         return total
     if r < P - 1:
