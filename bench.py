@@ -843,7 +843,47 @@ def scaling_records(args, world, rank, device, stream, peaks, psrc, sms):
     out["exact_db_chain"] = {"workload": "A[32,128,64].B[64,128] backward, batch-sharded",
                              "ms": ms, "hops": world - 1,
                              "collective": "rank-to-rank send/recv chain + broadcast"}
+    out["device_group"] = device_group_record(args, world, rank, device)
     return out
+
+
+def device_group_record(args, world, rank, device):
+    """The drop-in's own multi-GPU path: rank 0 alone drives all N GPUs from
+    one host thread through a device group (tlc_group_matmul_host) on the
+    batched workload from page-locked host buffers (64 x 2048^3 in total, each
+    GPU copying in and computing its 64/N entries); the other ranks wait.  The
+    call is synchronous (it returns when every GPU's share of C is back in host
+    memory), so it is timed by the host clock around whole calls."""
+    import torch
+    import tlcuda
+    rec = None
+    if rank == 0:
+        try:
+            batch, M, N, K = GEMMS["batched"]
+            g = torch.Generator().manual_seed(4)
+            ha = (torch.rand((batch, M, K), generator=g) * 2 - 1).pin_memory()
+            hb = (torch.rand((batch, K, N), generator=g) * 2 - 1).pin_memory()
+            hc = torch.empty((batch, M, N)).pin_memory()
+            flops = 2.0 * batch * M * N * K
+            with tlcuda.Group(list(range(world))) as grp:
+                members, uses_nccl = grp.size()
+                for _ in range(2):
+                    grp.matmul_host(ha, hb, mode=args.mode, out=hc)
+                reps = 5
+                t0 = time.perf_counter()
+                for _ in range(reps):
+                    grp.matmul_host(ha, hb, mode=args.mode, out=hc)
+                dt = (time.perf_counter() - t0) / reps
+            rec = {"api": "tlc_group_matmul_host", "gpus": members, "mode": args.mode,
+                   "ms_per_call": dt * 1e3, "tflops": flops / dt / 1e12,
+                   "h2d_bytes_per_call": 4 * (ha.numel() + hb.numel()),
+                   "d2h_bytes_per_call": 4 * hc.numel(), "nccl": uses_nccl,
+                   "timer": "host clock around synchronous calls"}
+            del ha, hb, hc
+        except Exception as e:  # noqa: BLE001 - reported, not fatal to the bench line
+            rec = {"unavailable": repr(e)[:200]}
+    barrier(world)
+    return rec
 
 
 def run_ours(args):

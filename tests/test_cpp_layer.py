@@ -28,3 +28,17 @@ def test_cpp_layer_on_gpu():
     rc, out = _run()
     assert rc == 0, out
     assert "all tl:: tests passed" in out
+
+
+@pytest.mark.gpu
+def test_cpp_layer_multi_gpu_group():
+    """tl::matmul and MatmulBackward through the device group (TL_NUM_GPUS=2),
+    bit-identical to the single-GPU entry points; skipped below two GPUs."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    r = subprocess.run([BIN], capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, TL_NUM_GPUS="2"))
+    out = r.stdout + r.stderr
+    assert r.returncode == 0, out
+    assert "multi-GPU group ok" in out

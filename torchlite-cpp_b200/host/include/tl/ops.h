@@ -6,6 +6,8 @@
 #include <cstdint>
 #include <vector>
 
+struct tlc_group;  // a libtl_cuda device group (include/tlc.h)
+
 namespace tl {
 
 // matrix multiplication: out = a @ b, NumPy batch broadcasting, 1-D squeeze
@@ -13,7 +15,16 @@ namespace tl {
 // mode (environment variable TL_GEMM_MODE: exact | tf32 | 3xtf32; exact,
 // bit-identical to the reference, if unset).  Throws std::invalid_argument
 // with the reference's messages.
+// With TL_NUM_GPUS = n > 1 in the environment, products of at least
+// 2^20 output elements (and their MatmulBackward) run over GPUs 0..n-1 of the
+// box through one device group (tlc_group_*): operands whose only current
+// copy is on the host are copied in by every GPU for its share and the result
+// is left on the host; device-resident operands are split from device 0 and
+// the result gathered there.  The results are the single-GPU ones bit for
+// bit (no product's additions are split across GPUs).
 Tensor matmul(const Tensor& a_in, const Tensor& b_in);
+// The device group TL_NUM_GPUS selects (NULL when it is unset or 1).
+::tlc_group* multi_gpu_group();
 // the same with an explicit mode (TLC_MODE_EXACT / _TF32 / _3XTF32)
 Tensor matmul(const Tensor& a_in, const Tensor& b_in, int mode);
 

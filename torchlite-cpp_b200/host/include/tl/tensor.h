@@ -33,6 +33,8 @@ struct Storage {
     void wrote_device() { host_valid_ = false; dev_valid_ = true; }
     float* device_raw();          // device buffer, contents not refreshed (for outputs)
     int64_t size() const { return n_; }
+    bool host_valid() const { return host_valid_; }
+    bool device_valid() const { return dev_valid_; }
 
   private:
     int64_t n_;
@@ -61,6 +63,10 @@ class Tensor {
 
     Tensor contiguous() const;
     Tensor clone() const;
+
+    // Only the host copy is current (a tensor filled through data() and not
+    // yet used on the device): the multi-GPU host-buffer path reads it there.
+    bool host_only() const;
 
     const std::vector<int64_t>& sizes() const;
     const std::vector<int64_t>& strides() const;

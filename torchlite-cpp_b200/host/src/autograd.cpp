@@ -28,6 +28,17 @@ tlc_tensor dview(const Tensor& t) {
     return v;
 }
 
+tlc_tensor hview(const Tensor& t) {
+    tlc_tensor v{};
+    v.ndim = static_cast<int32_t>(t.sizes().size());
+    for (int i = 0; i < v.ndim; ++i) {
+        v.sizes[i] = t.sizes()[i];
+        v.strides[i] = t.strides()[i];
+    }
+    v.data = t.numel() > 0 ? const_cast<float*>(t.data()) : nullptr;
+    return v;
+}
+
 }  // namespace
 
 // src/autograd.cpp:16-22: the first gradient is zeros + d, later ones add.
@@ -51,6 +62,22 @@ void accumulate_grad(Tensor& t, const Tensor& grad) {
 void MatmulBackward::backward(const Tensor& grad_output) {
     const bool want_a = inputs[0].requires_grad, want_b = inputs[1].requires_grad;
     if (!want_a && !want_b) return;
+    tlc_group* group = grad_output.numel() >= (int64_t(1) << 20) ? multi_gpu_group() : nullptr;
+    if (group && grad_output.host_only() && a_cache.host_only() && b_cache.host_only()) {
+        // the multi-GPU host-buffer form (TL_NUM_GPUS > 1), gradients on the host
+        Tensor da(want_a ? a_cache.sizes() : std::vector<int64_t>{0});
+        Tensor db(want_b ? b_cache.sizes() : std::vector<int64_t>{0});
+        tlc_tensor g = hview(grad_output), a = hview(a_cache), b = hview(b_cache);
+        tlc_tensor vda = hview(da), vdb = hview(db);
+        if (want_a) vda.data = da.data();
+        if (want_b) vdb.data = db.data();
+        check(tlc_group_matmul_backward_host(group, &g, &a, &b, want_a ? &vda : nullptr,
+                                             want_b ? &vdb : nullptr, 0, mode),
+              "tlc_group_matmul_backward_host");
+        if (want_a) accumulate_grad(inputs[0], da);
+        if (want_b) accumulate_grad(inputs[1], db);
+        return;
+    }
     tlc_tensor g = dview(grad_output), a = dview(a_cache), b = dview(b_cache);
     Tensor da, db;
     tlc_tensor vda{}, vdb{};

@@ -7,10 +7,12 @@
 #include <tlc.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <memory>
 #include <new>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace tl {
 
@@ -36,6 +38,13 @@ tlc_tensor view_of(const Tensor& t, bool device) {
     return v;
 }
 
+// The C-ABI view of a tensor's host copy (refreshed if stale).
+tlc_tensor host_view_of(const Tensor& t) {
+    tlc_tensor v = view_of(t, false);
+    v.data = t.numel() > 0 ? const_cast<float*>(t.data()) : nullptr;
+    return v;
+}
+
 // The same storage and view without the autograd links: what a node keeps of
 // its own output, so that the node and the output do not own each other.
 Tensor detached(const Tensor& t) {
@@ -51,6 +60,29 @@ Tensor matmul(const Tensor& a_in, const Tensor& b_in) {
     return matmul(a_in, b_in, TLC_MODE_DEFAULT);
 }
 
+tlc_group* multi_gpu_group() {
+    static tlc_group* group = []() -> tlc_group* {
+        const char* e = std::getenv("TL_NUM_GPUS");
+        const int want = e ? std::atoi(e) : 1;
+        if (want <= 1) return nullptr;
+        int count = 0;
+        check(tlc_device_count(&count), "tlc_device_count");
+        std::vector<int> devs(std::min(want, count));
+        for (size_t i = 0; i < devs.size(); ++i) devs[i] = static_cast<int>(i);
+        if (devs.size() < 2) return nullptr;
+        tlc_group* g = nullptr;  // lives as long as the process
+        check(tlc_group_create(devs.data(), static_cast<int>(devs.size()), &g), "tlc_group_create");
+        return g;
+    }();
+    return group;
+}
+
+namespace {
+// Products smaller than this stay on one GPU: below it the copies and
+// launches on more devices cost more than their share of the work.
+constexpr int64_t kGroupMinOutputs = int64_t(1) << 20;
+}  // namespace
+
 // src/ops.cpp:605-699
 Tensor matmul(const Tensor& a_in, const Tensor& b_in, int mode) {
     // shape rules and their exceptions first; they need no GPU
@@ -58,13 +90,31 @@ Tensor matmul(const Tensor& a_in, const Tensor& b_in, int mode) {
     int32_t nd = 0;
     int64_t sz[TLC_MAX_DIMS];
     check(tlc_matmul_shape(&va, &vb, &nd, sz), "tlc_matmul_shape");
-    Tensor out = Tensor::device_empty(std::vector<int64_t>(sz, sz + nd));
-    if (out.numel() > 0) {
-        va = view_of(a_in, true);
-        vb = view_of(b_in, true);
+    const std::vector<int64_t> shape(sz, sz + nd);
+    int64_t outputs = 1;
+    for (int64_t v : shape) outputs *= v;
+    tlc_group* group = outputs >= kGroupMinOutputs ? multi_gpu_group() : nullptr;
+    Tensor out;
+    if (group && a_in.host_only() && b_in.host_only()) {
+        // host operands: every GPU copies in its share; the result stays on the host
+        out = Tensor(shape);
+        va = host_view_of(a_in);
+        vb = host_view_of(b_in);
         tlc_tensor vo = view_of(out, false);
-        vo.data = out.device_data();
-        check(tlc_matmul(&va, &vb, &vo, mode, nullptr), "tlc_matmul");
+        vo.data = out.data();
+        check(tlc_group_matmul_host(group, &va, &vb, &vo, mode), "tlc_group_matmul_host");
+    } else {
+        out = Tensor::device_empty(shape);
+        if (out.numel() > 0) {
+            va = view_of(a_in, true);
+            vb = view_of(b_in, true);
+            tlc_tensor vo = view_of(out, false);
+            vo.data = out.device_data();
+            if (group)
+                check(tlc_group_matmul(group, &va, &vb, &vo, mode, nullptr), "tlc_group_matmul");
+            else
+                check(tlc_matmul(&va, &vb, &vo, mode, nullptr), "tlc_matmul");
+        }
     }
     if (a_in.requires_grad || b_in.requires_grad) {
         if (auto fn = track<MatmulBackward>(out, {&a_in, &b_in})) {

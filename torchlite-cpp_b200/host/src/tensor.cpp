@@ -154,6 +154,10 @@ const float& Tensor::at(int64_t i) const {
     return data()[i];
 }
 
+bool Tensor::host_only() const {
+    return !data_ || (data_->host_valid() && !data_->device_valid());
+}
+
 const std::vector<int64_t>& Tensor::sizes() const { return sizes_; }
 const std::vector<int64_t>& Tensor::strides() const { return strides_; }
 int64_t Tensor::numel() const { return numel_; }

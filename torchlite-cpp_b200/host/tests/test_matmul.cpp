@@ -327,6 +327,74 @@ static void test_flash_attention() {
     std::cout << "flash_attention ok\n";
 }
 
+// With TL_NUM_GPUS > 1 (and that many GPUs): a batched product with a broadcast
+// weight and its MatmulBackward through the device group, from host operands
+// (the host-buffer split) and from device-resident ones (split from device 0),
+// bit-identical to the single-GPU entry points in exact mode.
+static void test_multi_gpu_group() {
+    if (!tl::multi_gpu_group()) {
+        std::cout << "multi-GPU group skipped (TL_NUM_GPUS unset or one GPU)\n";
+        return;
+    }
+    const int64_t Bn = 6, M = 512, K = 96, N = 384;  // 1.2 M outputs: above the group threshold
+    uint32_t s = 99;
+    auto fill = [&](tl::Tensor& t) {
+        for (int64_t i = 0; i < t.numel(); ++i) {
+            s = s * 1664525u + 1013904223u;
+            t.data()[i] = ((s >> 8) & 0xFFFF) / 32768.0f - 1.0f;
+        }
+    };
+    tl::Tensor A({Bn, M, K}), W({K, N}), G({Bn, M, N});
+    fill(A);
+    fill(W);
+    fill(G);
+    // single-GPU results through the C ABI
+    auto hv = [](const tl::Tensor& t) {
+        tlc_tensor v{};
+        v.ndim = (int32_t)t.sizes().size();
+        for (int i = 0; i < v.ndim; ++i) {
+            v.sizes[i] = t.sizes()[i];
+            v.strides[i] = t.strides()[i];
+        }
+        v.data = const_cast<float*>(t.data());
+        return v;
+    };
+    std::vector<float> refC(Bn * M * N), refdA(Bn * M * K), refdW(K * N);
+    {
+        tlc_tensor a = hv(A), w = hv(W), g = hv(G), c = hv(G), da = hv(A), dw = hv(W);
+        c.data = refC.data();
+        da.data = refdA.data();
+        dw.data = refdW.data();
+        CHECK(tlc_matmul_host(&a, &w, &c, TLC_MODE_EXACT, nullptr) == TLC_OK);
+        CHECK(tlc_matmul_backward_host(&g, &a, &w, &da, &dw, 0, TLC_MODE_EXACT, nullptr) == TLC_OK);
+    }
+    for (int pass = 0; pass < 2; ++pass) {
+        tl::Tensor a = A.clone(), w = W.clone(), g = G.clone();
+        if (pass == 0) {  // host-only copies: the host-buffer split
+            a = tl::Tensor({Bn, M, K});
+            w = tl::Tensor({K, N});
+            g = tl::Tensor({Bn, M, N});
+            std::memcpy(a.data(), A.data(), sizeof(float) * A.numel());
+            std::memcpy(w.data(), W.data(), sizeof(float) * W.numel());
+            std::memcpy(g.data(), G.data(), sizeof(float) * G.numel());
+            CHECK(a.host_only() && w.host_only());
+        } else {
+            CHECK(!a.host_only() && !w.host_only());
+        }
+        a.set_requires_grad(true);
+        w.set_requires_grad(true);
+        tl::Tensor c = tl::matmul(a, w, TLC_MODE_EXACT);
+        for (int64_t i = 0; i < c.numel(); ++i) CHECK(same_bits(c.data()[i], refC[i]));
+        if (pass == 0) {
+            c.grad() = g;
+            c.backward();
+            for (int64_t i = 0; i < a.numel(); ++i) CHECK(same_bits(a.grad().data()[i], refdA[i]));
+            for (int64_t i = 0; i < w.numel(); ++i) CHECK(same_bits(w.grad().data()[i], refdW[i]));
+        }
+    }
+    std::cout << "multi-GPU group ok\n";
+}
+
 int main(int argc, char** argv) {
     const bool cpu_only = argc > 1 && std::string(argv[1]) == "--cpu";
     test_errors();
@@ -338,6 +406,7 @@ int main(int argc, char** argv) {
     test_tensor_core_modes();
     test_model_io();
     test_flash_attention();
+    test_multi_gpu_group();
     std::cout << "all tl:: tests passed\n";
     return 0;
 }
