@@ -275,6 +275,36 @@ def time_device(fn, steps, warmup, world, stream, count=None, clocks=None):
     return max_over_ranks(ms, world), l1 - l0
 
 
+def time_graph(fn, steps, world):
+    """Per-step device time (ms) of `fn` captured once into a CUDA graph and
+    replayed `steps` times between CUDA events (max over ranks): the launch
+    cost of the kernels without the Python binding's per-call host work."""
+    import torch
+    fn()  # set-up work (kernel attributes, checks) stays outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del g
+    return max_over_ranks(ms, world)
+
+
+# Workloads of a few microseconds per step, where the Python binding's host
+# work per call is longer than the kernels: also timed as CUDA-graph replays.
+GRAPH_WORKLOADS = ("square512", "broadcast")
+
+
 # ---- workloads -------------------------------------------------------------------------
 
 class Work:
@@ -916,6 +946,10 @@ def run_ours(args):
                          "value": work.job_flops / (ms * 1e-3) / 1e12,
                          "roofline_frac": per_gpu / peak, "peak_tflops": peak,
                          "peak_source": pdesc}
+        if args.workload in GRAPH_WORKLOADS:
+            gms = time_graph(fn, max(args.steps, 50), world)
+            results[mode].update({"graph_ms_per_step": gms,
+                                  "graph_tflops_per_gpu": work.flops / (gms * 1e-3) / 1e12})
 
     head = results[args.mode]
     roofline = {"bound": "tensor" if args.mode != "exact" else "fp32-fma",

@@ -244,6 +244,111 @@ __global__ void __launch_bounds__(NT, 2) exact_kernel(ExactParams p) {
     }
 }
 
+// ---- small problems --------------------------------------------------------------------
+//
+// exact_small_kernel: 32 x 64 output tiles, k-tiles of 16, 128 threads with
+// 4 x 4 outputs each.  For products with fewer 128-row tiles than there are
+// SMs (a 512^3 GEMM is 8 tiles of 128 x 256, the broadcast A[32,128,64].B[64,128]
+// 32 tiles of 128 x 128), whose big-tile kernels leave most SMs idle: 16 to 32
+// times as many CTAs, each output still one ascending-k fmaf chain from +0.
+// Operands in any strides (one of the two matrix strides of each is 1), loads
+// through registers into double-buffered k-major shared tiles, as in
+// exact_kernel.
+constexpr int SBM = 32, SBN = 64, SBK = 16, SNT = 128;
+constexpr int SLDA = SBM + 4, SLDB = SBN + 4;
+
+template <bool AK, bool BKM, bool VC>
+__global__ void __launch_bounds__(SNT) exact_small_kernel(ExactParams p) {
+    __shared__ __align__(16) float As[2][SBK * SLDA];
+    __shared__ __align__(16) float Bs[2][SBK * SLDB];
+    const int tid = threadIdx.x;
+    const int tr = tid >> 4, tc = tid & 15;  // 8 x 16 threads of 4 x 4 outputs
+    const int64_t m0 = (int64_t)blockIdx.y * SBM, n0 = (int64_t)blockIdx.x * SBN;
+    const int64_t nk = (p.K + SBK - 1) / SBK;
+    // this thread's loads: A 4 values, B 8 values per k-tile
+    const int a_row = AK ? tid >> 2 : (tid & 7) * 4, a_k = AK ? (tid & 3) * 4 : tid >> 3;
+    const int b_col = BKM ? tid >> 1 : (tid & 7) * 8, b_k = BKM ? (tid & 1) * 8 : tid >> 3;
+
+    for (int64_t b = blockIdx.z; b < p.batch; b += gridDim.z) {
+        int64_t oa, ob, oc;
+        p.bo.get(b, oa, ob, oc);
+        const float* Ab = p.A + oa + m0 * p.a_rs;
+        const float* Bb = p.B + ob + n0 * p.b_cs;
+        float ra[4], rb[8];
+        auto load = [&](int64_t k0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = AK ? a_row : a_row + j, k = AK ? a_k + j : a_k;
+                ra[j] = (m0 + r < p.M && k0 + k < p.K) ? __ldg(Ab + r * p.a_rs + (k0 + k) * p.a_cs) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = BKM ? b_col : b_col + j, k = BKM ? b_k + j : b_k;
+                rb[j] = (n0 + c < p.N && k0 + k < p.K) ? __ldg(Bb + c * p.b_cs + (k0 + k) * p.b_rs) : 0.f;
+            }
+        };
+        auto store = [&](int buf) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = AK ? a_row : a_row + j, k = AK ? a_k + j : a_k;
+                As[buf][k * SLDA + r] = ra[j];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = BKM ? b_col : b_col + j, k = BKM ? b_k + j : b_k;
+                Bs[buf][k * SLDB + c] = rb[j];
+            }
+        };
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        if (nk > 0) {
+            load(0);
+            store(0);
+        }
+        __syncthreads();
+        for (int64_t kt = 0; kt < nk; ++kt) {
+            const int buf = (int)(kt & 1);
+            const bool more = kt + 1 < nk;
+            if (more) load((kt + 1) * SBK);
+#pragma unroll
+            for (int kk = 0; kk < SBK; ++kk) {
+                const float4 a = *reinterpret_cast<const float4*>(&As[buf][kk * SLDA + tr * 4]);
+                const float4 bq = *reinterpret_cast<const float4*>(&Bs[buf][kk * SLDB + tc * 4]);
+                const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+            }
+            if (more) store(buf ^ 1);
+            __syncthreads();
+        }
+        float* Cb = p.C + oc;
+        const int64_t col = n0 + tc * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t row = m0 + tr * 4 + i;
+            if (row >= p.M) continue;
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                v[j] = col + j < p.N ? epilogue(acc[i][j], col + j, p.bias, p.scale, p.apply_scale) : 0.f;
+            float* dst = Cb + row * p.c_rs + col;
+            if (VC && col + 3 < p.N) {
+                *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (col + j < p.N) dst[j] = v[j];
+            }
+        }
+        __syncthreads();  // shared tiles are reused by the next batch entry
+    }
+}
+
 // ---- TMA-fed kernel ------------------------------------------------------------------
 
 constexpr int TBM = 128, TBK = 32;
@@ -749,6 +854,30 @@ int gemm_exact(const Gemm& g, cudaStream_t s) {
                     (bkm ? div4(g.K) && div4(g.b_cs) : div4(g.N) && div4(g.b_rs));
     const bool vc = aligned16(g.C) && bs_ok_c && div4(g.c_rs);
 
+    // Few big tiles (fewer than half the SMs): the small-tile kernel.
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t big_tiles = p.batch * ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+    if (p.K > 0 && 2 * big_tiles < sms) {
+        const int64_t sx = (g.N + SBN - 1) / SBN, sy = (g.M + SBM - 1) / SBM;
+        if (sy <= 65535) {
+            dim3 sgrid((unsigned)sx, (unsigned)sy, (unsigned)(p.batch < 65535 ? p.batch : 65535));
+            const int key = (ak ? 4 : 0) | (bkm ? 2 : 0) | (vc ? 1 : 0);
+            switch (key) {
+                case 0: exact_small_kernel<false, false, false><<<sgrid, SNT, 0, s>>>(p); break;
+                case 1: exact_small_kernel<false, false, true><<<sgrid, SNT, 0, s>>>(p); break;
+                case 2: exact_small_kernel<false, true, false><<<sgrid, SNT, 0, s>>>(p); break;
+                case 3: exact_small_kernel<false, true, true><<<sgrid, SNT, 0, s>>>(p); break;
+                case 4: exact_small_kernel<true, false, false><<<sgrid, SNT, 0, s>>>(p); break;
+                case 5: exact_small_kernel<true, false, true><<<sgrid, SNT, 0, s>>>(p); break;
+                case 6: exact_small_kernel<true, true, false><<<sgrid, SNT, 0, s>>>(p); break;
+                default: exact_small_kernel<true, true, true><<<sgrid, SNT, 0, s>>>(p); break;
+            }
+            count_launch();
+            return check_launch("gemm_exact_small");
+        }
+    }
     if (p.K > 0) {
         const int st = gemm_exact_tma(g, ak, bkm, vc, s);
         if (st != TLC_ERR_UNSUPPORTED) return st;

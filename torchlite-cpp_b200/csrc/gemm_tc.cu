@@ -89,6 +89,7 @@ constexpr uint32_t kGemmSleepNs = 20000;
 struct TcParams {
     CUtensorMap tmA[2];  // [0] A (TF32) or hi(A) (3xTF32); [1] lo(A)
     CUtensorMap tmB[2];
+    CUtensorMap tmC;     // C {N, M, batch...}, 32 x 32 boxes, 128-byte swizzle (if tma_c)
     float* C;
     int64_t c_rs;
     int64_t cbs[kMaxBatchDims];
@@ -105,6 +106,7 @@ struct TcParams {
     int a_mn, b_mn;   // 1: operand is MN-major in memory
     int a_chunked, b_chunked;  // 1: MN-major map with a chunk dim: one load per k-block
     int vec_c;        // float4 stores allowed
+    int tma_c;        // TF32: C written by TMA stores from the epilogue's staging squares
     uint64_t timeout_ns;
     int* err;
     const float* bias;  // epilogue (see Gemm): c * scale if apply_scale, + bias[col]
@@ -232,7 +234,9 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
     // 1024-byte alignment for the 128-byte-swizzle atoms.
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
+    // [stages][epilogue staging (TF32)][barriers]: the staging squares start
+    // 1024-byte aligned, as the 128-byte swizzle of the TMA store requires.
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES + S::EPI_STAGE_BYTES);
     uint64_t* full = bars;                 // [STAGES]  (used in the leader CTA)
     uint64_t* empty = bars + STAGES;       // [STAGES]
     uint64_t* tfull = bars + 2 * STAGES;   // [2]
@@ -533,7 +537,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     // 16-byte chunks are XOR-swizzled by row, so both the
                     // row-per-thread writes and the row-per-8-lanes reads
                     // touch every bank once per 16-byte column.
-                    float* stg = reinterpret_cast<float*>(smem + STAGES * S::STAGE_BYTES + S::BAR_BYTES) +
+                    float* stg = reinterpret_cast<float*>(smem + STAGES * S::STAGE_BYTES) +
                                  (warp - 2) * 32 * 32;
                     const int64_t row0 = row - lane;  // the warp's first output row
 #pragma unroll 1
@@ -542,7 +546,29 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                         tmem_ld32(taddr + c * 32, r);
                         tmem_wait_ld();
                         const int col0 = n0 + c * 32;
-                        if (p.vec_c && col0 + 32 <= p.N) {  // warp-uniform
+                        if (p.tma_c) {  // warp-uniform
+                            // The square goes out with one TMA store (rows and
+                            // columns past M, N clipped by the tensor map).
+                            if (col0 >= p.N || row0 >= p.M) continue;
+                            if (p.bias || p.apply_scale) {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    if (col0 + j < p.N)
+                                        r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j));
+                            }
+                            if (lane == 0) bulk_wait_read_all();  // the previous square was read out
+                            __syncwarp();
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                *reinterpret_cast<uint4*>(stg + lane * 32 + ((j ^ (lane & 7)) << 2)) =
+                                    make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_5d(&p.tmC, stg, col0, (int)row0, bi[0], bi[1], bi[2]);
+                                bulk_commit_group();
+                            }
+                        } else if (p.vec_c && col0 + 32 <= p.N) {  // warp-uniform
                             if (p.bias || p.apply_scale) {
 #pragma unroll
                                 for (int j = 0; j < 32; ++j)
@@ -614,6 +640,11 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
         }
     }
 
+    // TMA stores of C still reading the staging squares / writing C complete
+    // before the CTA's shared memory goes away.
+    if constexpr (!X3) {
+        if (warp >= 2 && lane == 0 && p.tma_c) bulk_wait_all();
+    }
     tc_fence_before();
     __syncthreads();
     // CG = 2: neither CTA frees its TMEM or exits while the pair's MMAs or the
@@ -823,10 +854,23 @@ int launch_variant(const TcParams& prm, cudaStream_t s) {
 
 // The variant for a problem: CTA pairs (CG = 2) for more than 128 rows;
 // N = 256 tiles for more than 128 columns, except single-CTA 3xTF32, whose
-// four 256-column tiles per k-block would leave two pipeline stages.
+// four 256-column tiles per k-block would leave two pipeline stages.  A
+// problem whose pair tiles would occupy fewer than half the SMs (a 512^3
+// GEMM is four 256 x 256 tiles: 8 SMs) takes single-CTA 128 x 128 tiles,
+// which spread the same work over four times as many SMs.
 void pick_variant(const Gemm& g, bool x3, int* cg, int* un) {
     *cg = g.M > 128 ? 2 : 1;
     *un = (g.N > 128 && !(x3 && *cg == 1)) ? 256 : 128;
+    if (*cg == 2) {
+        int sms = 148, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t pairs = g.batch() * ((g.M + 255) / 256) * ((g.N + *un - 1) / *un);
+        if (4 * pairs < sms) {
+            *cg = 1;
+            *un = 128;
+        }
+    }
 }
 
 // Fills the tile/launch fields of `prm` for a variant and launches it.
@@ -1064,6 +1108,15 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
         TLC_TRY(encode(&prm.tmB[0], B));
     }
     fill_common(prm, g, A, B, a_mn, b_mn, x3);
+    if (!x3 && prm.vec_c) {
+        // C as a tensor map for the epilogue's TMA stores (16-byte aligned
+        // base and strides: what vec_c already checked)
+        if (encode_tiled(&prm.tmC, g.C, g.N, g.M, g.c_rs, B.bsz, g.cbs, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B) == TLC_OK)
+            prm.tma_c = 1;
+        else
+            clear_error();
+    }
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
     return launch_tc(prm, g, x3, s);
