@@ -134,13 +134,15 @@ import torch
 sys.path.insert(0, {tests!r})
 import test_zz_no_alloc as t
 g = torch.Generator(device="cuda:0").manual_seed(23)
-A = torch.randn((2, 130, 70), generator=g, device="cuda:0")
-B = torch.randn((70, 150), generator=g, device="cuda:0")
-N1 = torch.empty((2, 130, 150), device="cuda:0")
+A = torch.randn((2, 130, 72), generator=g, device="cuda:0")
+B = torch.randn((72, 152), generator=g, device="cuda:0")
+N1 = torch.empty((2, 130, 152), device="cuda:0")
 N2 = torch.empty_like(N1)
 R = torch.empty_like(N1)
-assert t.noalloc(A, B, N1) == 0   # the first GEMM of the process
-assert t.noalloc(A, B, N2) == 0
+st = t.noalloc(A, B, N1)          # the first GEMM of the process
+assert st == 0, (st, t.tlcuda.lib().tlc_last_error())
+st = t.noalloc(A, B, N2)
+assert st == 0, (st, t.tlcuda.lib().tlc_last_error())
 t.regular(A, B, R)
 torch.cuda.synchronize()
 assert torch.equal(N1, N2), "two calls differ"
