@@ -683,7 +683,7 @@ def inputs_uniform(rng, shape):
     return out
 
 
-def run_reference_arm(args):
+def run_reference_arm(args, out_fd):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -693,7 +693,7 @@ def run_reference_arm(args):
     try:
         R = O.tlref()
     except FileNotFoundError as e:
-        print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not built: {e}"}))
+        emit({"impl": "reference", "unavailable": f"oracle/_ref not built: {e}"}, out_fd)
         return 0
     cores = 1 if args.workload.startswith("flash") else R.hardware_threads()
     full = reference_full_workload(args.workload)
@@ -734,7 +734,7 @@ def run_reference_arm(args):
                              "kind": "reference", "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit(line, out_fd)
     return 0
 
 
@@ -916,7 +916,7 @@ def device_group_record(args, world, rank, device):
     return rec
 
 
-def run_ours(args):
+def run_ours(args, out_fd):
     import torch
     import tlcuda
     world, rank, local = dist_setup()
@@ -1008,7 +1008,7 @@ def run_ours(args):
         if fwd is not None:
             line["forward"] = fwd
         line.update(extras)
-        print(json.dumps(line))
+        emit(line, out_fd)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -1016,7 +1016,17 @@ def run_ours(args):
     return 0
 
 
+def emit(line, fd):
+    """The one JSON line, written to the original standard output."""
+    os.write(fd, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    # Libraries (NCCL's version banner, for one) may print on standard output;
+    # everything but the result line goes to standard error instead.
+    sys.stdout.flush()
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -1035,8 +1045,8 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
-        return run_reference_arm(args)
-    return run_ours(args)
+        return run_reference_arm(args, out_fd)
+    return run_ours(args, out_fd)
 
 
 if __name__ == "__main__":

@@ -98,10 +98,17 @@ def test_device_conv2d_exact(case):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode,tol", [("tf32", 1e-2), ("3xtf32", 1e-5)])
-def test_device_conv2d_tensor_cores(mode, tol):
+@pytest.mark.parametrize("case", [(4, 32, 28, 28, 64, 3, 1, 1, 1), (2, 64, 30, 30, 64, 3, 1, 1, 1),
+                                  (2, 16, 17, 23, 48, 3, 1, 0, 1), (2, 8, 15, 15, 12, 5, 1, 2, 2)]
+                         # float64 torch needs the padded input at least as large as the kernel
+                         + [c for c in CASES if min(c[2], c[3]) + 2 * c[7] >= c[5]])
+def test_device_conv2d_tensor_cores(mode, tol, case):
+    """The tensor-core modes gather the column buffer on the fly inside the
+    GEMM (forward, dW, and dX at stride 1): against float64 over the
+    reference's shapes, strides, paddings and groups."""
     torch = pytest.importorskip("torch")
     import tlcuda
-    x, w, b, s, p, g = case_data((4, 32, 28, 28, 64, 3, 1, 1, 1), 13)
+    x, w, b, s, p, g = case_data(case, 13)
     X, Wt, B = (torch.from_numpy(a).cuda() for a in (x, w, b))
     ref64 = torch.nn.functional.conv2d(X.double(), Wt.double(), B.double(), s, p, 1, g)
     y = tlcuda.conv2d(X, Wt, B, s, p, g, mode=mode).double()
