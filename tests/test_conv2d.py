@@ -103,9 +103,8 @@ def test_device_conv2d_exact(case):
                          # float64 torch needs the padded input at least as large as the kernel
                          + [c for c in CASES if min(c[2], c[3]) + 2 * c[7] >= c[5]])
 def test_device_conv2d_tensor_cores(mode, tol, case):
-    """The tensor-core modes gather the column buffer on the fly inside the
-    GEMM (forward, dW, and dX at stride 1): against float64 over the
-    reference's shapes, strides, paddings and groups."""
+    """The tensor-core modes (im2col + batched tcgen05 GEMMs, col2im) against
+    float64 over the reference's shapes, strides, paddings and groups."""
     torch = pytest.importorskip("torch")
     import tlcuda
     x, w, b, s, p, g = case_data(case, 13)

@@ -152,23 +152,6 @@ inline BatchOffsets batch_offsets(const Gemm& g) {
 // Kernels (each returns a tlc_status).
 int gemm_exact(const Gemm& g, cudaStream_t s);
 int gemm_tc(const Gemm& g, int mode, cudaStream_t s);
-// B of a GEMM gathered from an NCHW tensor instead of read from memory
-// (implicit im2col; gemm_tc_im2col).  Batch dim 0 of the GEMM steps images
-// (img_stride elements apart in src), batch dim 1 groups (grp_stride).  Tap
-// t = c * kH * kW + kh * kW + kw of output pixel j = oh * W_out + ow reads
-// src[c][oh * stride - pad + kh][ow * stride - pad + kw] of an H x W plane (0
-// outside it).  rows_are_pixels: B[k = tap][n = pixel] (taps = K, P = N, a
-// convolution's forward product); else B[k = pixel][n = tap] (P = K, taps =
-// N, its weight-gradient product).
-struct Im2colDesc {
-    const float* src;
-    int64_t img_stride, grp_stride;
-    int H, W, W_out, P, kH, kW, stride, pad, taps;
-    int rows_are_pixels;
-};
-// TF32 / 3xTF32 GEMM whose B is gathered (Gemm's B fields are ignored); A and
-// C as in gemm_tc, at most two batch dims.
-int gemm_tc_im2col(const Gemm& g, const Im2colDesc& d, int mode, cudaStream_t s);
 // out[o,n] = sum over d ascending of in[o,d,n], from init[o,n] (NULL: from 0.0f).
 int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
                    cudaStream_t s, const float* init = nullptr);

@@ -452,55 +452,6 @@ int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
     return TLC_OK;
 }
 
-// Whether the tensor-core modes gather col on the fly (gemm_tc_im2col)
-// instead of writing the column buffer: every index of the gather fits in
-// 32 bits.
-bool implicit_ok(const ConvShape& s) {
-    const int64_t lim = int64_t(1) << 30;
-    return s.patch > 0 && s.patch < lim && s.HW < lim && s.H * s.W < lim && s.W_out < lim &&
-           s.N < lim && s.groups < lim && s.C_in * s.H * s.W < (int64_t(1) << 40);
-}
-// dX as an implicit GEMM: stride 1 and a square kernel (one padding k - 1 - p).
-bool implicit_dx_ok(const ConvShape& s) {
-    return implicit_ok(s) && s.stride == 1 && s.kH == s.kW && s.kH - 1 - s.padding >= 0 &&
-           s.C_out_g * s.kH * s.kW < (int64_t(1) << 30);
-}
-
-Im2colDesc im2col_of(const float* src, int64_t img_stride, int64_t grp_stride, int64_t H, int64_t W,
-                     int64_t W_out, int64_t P, const ConvShape& s, int64_t pad, bool rows_are_pixels,
-                     int64_t channels = -1) {
-    Im2colDesc d{};
-    d.src = src;
-    d.img_stride = img_stride;
-    d.grp_stride = grp_stride;
-    d.H = (int)H;
-    d.W = (int)W;
-    d.W_out = (int)W_out;
-    d.P = (int)P;
-    d.kH = (int)s.kH;
-    d.kW = (int)s.kW;
-    d.stride = (int)s.stride;
-    d.pad = (int)pad;
-    d.taps = (int)((channels < 0 ? s.C_in_g : channels) * s.kH * s.kW);
-    d.rows_are_pixels = rows_are_pixels ? 1 : 0;
-    return d;
-}
-
-// W'[g][c][o * kH * kW + kh' * kW + kw'] = W[g * C_out_g + o][c][kH - 1 - kh'][kW - 1 - kw']:
-// the weights of the convolution that gives dX from dO (stride 1).
-__global__ void flip_weights_kernel(const float* __restrict__ w, float* __restrict__ wf, ConvShape s) {
-    const int64_t khw = s.kH * s.kW, per_g = s.C_in_g * s.C_out_g * khw;
-    const int64_t n = s.groups * per_g;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t g = i / per_g, r = i - g * per_g;
-        const int64_t c = r / (s.C_out_g * khw), k = r - c * (s.C_out_g * khw);
-        const int64_t o = k / khw, t = k - o * khw;
-        const int64_t kh = t / s.kW, kw = t - kh * s.kW;
-        wf[i] = w[((g * s.C_out_g + o) * s.C_in_g + c) * khw + (s.kH - 1 - kh) * s.kW + (s.kW - 1 - kw)];
-    }
-}
-
 int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bias, int64_t stride,
             int64_t padding, int64_t groups, tlc_tensor* out, int mode, cudaStream_t st) {
     ConvShape s;
@@ -519,8 +470,7 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
     const float *in, *w;
     TLC_TRY(dense_copy(in_t, bin, &in, st));
     TLC_TRY(dense_copy(w_t, bw, &w, st));
-    const bool implicit = mode != TLC_MODE_EXACT && implicit_ok(s);
-    if (!implicit) TLC_TRY(make_col(in, s, col, st));
+    TLC_TRY(make_col(in, s, col, st));
     // out[n, g] (C_out_g x HW) = W_g (C_out_g x patch) . col[n, g] (patch x HW)
     Gemm g{};
     g.M = s.C_out_g;
@@ -543,14 +493,7 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
     g.bbs[1] = s.patch * s.HW;
     g.cbs[0] = s.C_out * s.HW;
     g.cbs[1] = s.C_out_g * s.HW;
-    if (implicit) {
-        // col gathered on the fly from the input planes (no column buffer)
-        TLC_TRY(gemm_tc_im2col(g, im2col_of(in, s.C_in * s.H * s.W, s.C_in_g * s.H * s.W, s.H, s.W,
-                                            s.W_out, s.HW, s, s.padding, true),
-                               mode, st));
-    } else {
-        TLC_TRY(gemm(g, mode, st));
-    }
+    TLC_TRY(gemm(g, mode, st));
     if (b) {
         // add(result, reshape(bias, {1, C_out, 1, 1})): in place, out = out + bias[c]
         const float* bd;
@@ -588,8 +531,7 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
         if (s.N * s.C_out * s.patch == 0) {
             if (s.C_out * s.patch) TLC_TRY(launch_fill_zero(d_w->data, s.C_out * s.patch, st));
         } else {
-            const bool implicit = mode != TLC_MODE_EXACT && implicit_ok(s) && s.HW > 0;
-            if (!implicit) TLC_TRY(make_col(in, s, col, st));
+            TLC_TRY(make_col(in, s, col, st));
             TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(s.N * s.C_out * s.patch), st));
             Gemm g{};
             g.M = s.C_out_g;
@@ -614,11 +556,6 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             g.cbs[1] = s.C_out_g * s.patch;
             if (s.HW == 0) {
                 TLC_TRY(launch_fill_zero(prod.f(), s.N * s.C_out * s.patch, st));
-            } else if (implicit) {
-                // col^T gathered on the fly: k = output pixels, rows = taps
-                TLC_TRY(gemm_tc_im2col(g, im2col_of(in, s.C_in * s.H * s.W, s.C_in_g * s.H * s.W, s.H,
-                                                    s.W, s.W_out, s.HW, s, s.padding, false),
-                                       mode, st));
             } else {
                 TLC_TRY(gemm(g, mode, st));
             }
@@ -626,39 +563,7 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             TLC_TRY(launch_sum_dim(prod.f(), d_w->data, 1, s.N, s.C_out * s.patch, st));
         }
     }
-    if (d_in && mode != TLC_MODE_EXACT && implicit_dx_ok(s) && s.N * s.C_in * s.H * s.W > 0) {
-        // Stride 1: dX is the convolution of dO with the flipped, transposed
-        // weights and padding k - 1 - p, run as the same implicit GEMM:
-        // dX[n, g] (C_in_g x H*W) = W'_g (C_in_g x C_out_g*kH*kW) . im2col(dO[n, g]).
-        TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)(s.C_out * s.C_in_g * s.kH * s.kW), st));
-        const int64_t nw = s.C_out * s.C_in_g * s.kH * s.kW;
-        flip_weights_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((nw + 255) / 256, 148 * 16)), 256, 0,
-                              st>>>(w, gcol.f(), s);
-        count_launch();
-        TLC_TRY(check_launch("conv flip weights"));
-        const int64_t kk = s.C_out_g * s.kH * s.kW, HWin = s.H * s.W;
-        Gemm g{};
-        g.M = s.C_in_g;
-        g.N = HWin;
-        g.K = kk;
-        g.A = gcol.f();
-        g.a_rs = kk;
-        g.a_cs = 1;
-        g.C = d_in->data;
-        g.c_rs = HWin;
-        g.nb = 2;
-        g.bsz[0] = s.N;
-        g.bsz[1] = s.groups;
-        g.abs_[0] = 0;
-        g.abs_[1] = s.C_in_g * kk;
-        g.cbs[0] = s.C_in * HWin;
-        g.cbs[1] = s.C_in_g * HWin;
-        // the "input" of this convolution is dO (H_out x W_out planes), its
-        // "output" dX (H x W)
-        TLC_TRY(gemm_tc_im2col(g, im2col_of(go, s.C_out * s.HW, s.C_out_g * s.HW, s.H_out, s.W_out,
-                                            s.W, HWin, s, s.kH - 1 - s.padding, true, s.C_out_g),
-                               mode, st));
-    } else if (d_in) {
+    if (d_in) {
         const int64_t ni = s.N * s.C_in * s.H * s.W;
         if (ni) {
             const int64_t nc = s.N * s.groups * s.patch * s.HW;

@@ -86,18 +86,6 @@ constexpr int UMMA_K = 8;      // k per tcgen05.mma.kind::tf32
 // and TMA threads.
 constexpr uint32_t kGemmSleepNs = 20000;
 
-// The NCHW tensor a gather variant reads B from: batch dim 0 steps images,
-// batch dim 1 groups; tap t = c * kH * kW + kh * kW + kw of output pixel
-// j = oh * W_out + ow reads src[c][oh * stride - pad + kh][ow * stride - pad + kw]
-// (0 outside the plane, for t >= taps and for j >= P).
-struct Im2col {
-    const float* src;
-    int64_t img_stride, grp_stride;  // elements
-    int H, W, W_out, P;
-    int kH, kW, stride, pad;
-    int taps;
-};
-
 struct TcParams {
     CUtensorMap tmA[2];  // [0] A (TF32) or hi(A) (3xTF32); [1] lo(A)
     CUtensorMap tmB[2];
@@ -124,13 +112,6 @@ struct TcParams {
     const float* bias;  // epilogue (see Gemm): c * scale if apply_scale, + bias[col]
     float scale;
     int apply_scale;
-    // Implicit im2col (gather variants): B is not read through a tensor map
-    // but gathered from an NCHW tensor by four producer warps.
-    //   gather 1: B rows = output pixels, k = taps (c, kh, kw)    (conv forward, dX)
-    //   gather 2: B rows = taps, k = output pixels                (dW)
-    int gather;
-    int gather_round;  // X3: hi = round-to-nearest TF32 (the tensor cores do not truncate)
-    Im2col gb;
 };
 
 // The GEMM epilogue on one output value: one IEEE fp32 operation per step,
@@ -208,7 +189,7 @@ struct KbIter {
 // A and UN / CG columns of B (X3: a hi and a lo copy of each, so the three
 // products of a k-block read four tiles loaded once); it accumulates into a
 // 128 x UN fp32 TMEM accumulator, double-buffered.
-template <int CG, int UN, bool X3, bool GATHER = false>
+template <int CG, int UN, bool X3>
 struct Cfg {
     static constexpr int B_COLS = UN / CG;
     static constexpr int A_BYTES = BM * BK * 4;           // 16 KB
@@ -226,9 +207,7 @@ struct Cfg {
     // for TF32 twice the store streams shorten the epilogue of short-K tiles
     // (measured: attention-shaped products +5 %, conv +2 %, long K unchanged).
     static constexpr int EPI_WARPS = 8;
-    // gather variants: four more warps build the B tiles (implicit im2col)
-    static constexpr int GATHER_THREADS = GATHER ? 128 : 0;
-    static constexpr int THREADS = 64 + 32 * EPI_WARPS + GATHER_THREADS;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int EPI_COLS = UN * 4 / EPI_WARPS;  // accumulator columns per epilogue warp
     static constexpr int TMEM_COLS = 2 * UN;
     static constexpr int TILE_M = BM * CG;
@@ -242,119 +221,14 @@ struct Cfg {
     static_assert(STAGES >= 2, "at least two pipeline stages");
     static_assert(EPI_COLS % 32 == 0, "epilogue columns in 32-column TMEM loads");
     static_assert(TOTAL <= 227 * 1024, "dynamic shared memory per CTA");
-    static_assert(!GATHER || (CG == 1 && B_COLS % 128 == 0), "gather variants: single CTA, 128-row B tiles");
 };
 
 // X3: the epilogue adds the chunk partials of each output element into
 // registers in fp32 round-to-nearest and stores after the last chunk.
-// Gather variants (GATHER): the B tile of each k-block is written by four
-// producer warps from an NCHW tensor (TcParams::gb) into the K-major layout
-// TMA would have produced (128-byte rows of 32 k, 16-byte chunks swizzled by
-// row); each gathering thread fences its writes for the async proxy and
-// arrives on the stage's full barrier, which also counts the A tile's TMA
-// bytes.
-template <int CG, int UN, bool X3, bool GATHER>
-__device__ __forceinline__ void gather_b_tile(const TcParams& p, const float* __restrict__ src, int n0,
-                                              int k0, uint8_t* hi, uint8_t* lo, int gt) {
-    constexpr int ROWS = UN / CG;  // B tile rows
-    const Im2col& g = p.gb;
-    const int kHW = g.kH * g.kW;
-    const int64_t plane = (int64_t)g.H * g.W;
-    // One 16-byte chunk of a row: hi as the tensor cores read it; X3 also
-    // lo = x - hi (exact in fp32), hi truncated to TF32 as kind::tf32 reads
-    // an fp32 input, or rounded where the tensor cores do not truncate.
-    auto put = [&](int row, int chunk, float4 v) {
-        const uint32_t off = (uint32_t)row * 128u + ((uint32_t)(chunk ^ (row & 7)) << 4);
-        if constexpr (X3) {
-            float x[4] = {v.x, v.y, v.z, v.w}, h[4], l[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                if (p.gather_round) {
-                    uint32_t r;
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x[e]));
-                    h[e] = __uint_as_float(r);
-                } else {
-                    h[e] = __uint_as_float(__float_as_uint(x[e]) & 0xFFFFE000u);
-                }
-                l[e] = __fsub_rn(x[e], h[e]);
-                if (!p.gather_round) h[e] = x[e];
-            }
-            *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
-            *reinterpret_cast<float4*>(lo + off) = make_float4(l[0], l[1], l[2], l[3]);
-        } else {
-            *reinterpret_cast<float4*>(hi + off) = v;
-        }
-    };
-    if (p.gather == 1) {
-        // rows = output pixels n0 + row, k = taps k0 .. k0 + 31; thread gt
-        // owns rows gt, gt + 128, ...; a warp reads 32 consecutive pixels per tap
-        const int c0 = k0 / kHW, r0 = k0 - c0 * kHW;
-        const int kh0 = r0 / g.kW, kw0 = r0 - kh0 * g.kW;
-#pragma unroll 1
-        for (int i = 0; i < ROWS / 128; ++i) {
-            const int row = gt + 128 * i;
-            const int j = n0 + row;
-            const bool jv = j < g.P;
-            const int oh = jv ? j / g.W_out : 0, ow = jv ? j - oh * g.W_out : 0;
-            const int bh = oh * g.stride - g.pad, bw = ow * g.stride - g.pad;
-            int c = c0, kh = kh0, kw = kw0;
-            float v[32];
-#pragma unroll
-            for (int kk = 0; kk < 32; ++kk) {
-                const int ih = bh + kh, iw = bw + kw;
-                const bool ok = jv && k0 + kk < g.taps && (unsigned)ih < (unsigned)g.H &&
-                                (unsigned)iw < (unsigned)g.W;
-                v[kk] = ok ? __ldg(src + c * plane + (int64_t)ih * g.W + iw) : 0.0f;
-                if (++kw == g.kW) {
-                    kw = 0;
-                    if (++kh == g.kH) {
-                        kh = 0;
-                        ++c;
-                    }
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                put(row, q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
-        }
-    } else {
-        // rows = taps n0 + row, k = output pixels k0 .. k0 + 31; thread gt owns
-        // the 4 pixels of chunk gt & 7 in rows (gt >> 3) + 16 i
-        const int chunk = gt & 7;
-        int bh[4], bw[4];
-        bool jv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int j = k0 + chunk * 4 + e;
-            jv[e] = j < g.P;
-            const int oh = jv[e] ? j / g.W_out : 0, ow = jv[e] ? j - oh * g.W_out : 0;
-            bh[e] = oh * g.stride - g.pad;
-            bw[e] = ow * g.stride - g.pad;
-        }
-#pragma unroll 4
-        for (int i = 0; i < ROWS / 16; ++i) {
-            const int row = (gt >> 3) + 16 * i;
-            const int t = n0 + row;
-            const bool tv = t < g.taps;
-            const int c = tv ? t / kHW : 0, r = tv ? t - c * kHW : 0;
-            const int kh = r / g.kW, kw = r - kh * g.kW;
-            const float* base = src + c * plane;
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int ih = bh[e] + kh, iw = bw[e] + kw;
-                const bool ok = tv && jv[e] && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
-                v[e] = ok ? __ldg(base + (int64_t)ih * g.W + iw) : 0.0f;
-            }
-            put(row, chunk, make_float4(v[0], v[1], v[2], v[3]));
-        }
-    }
-}
-
-template <int CG, int UN, bool X3, bool GATHER = false>
-__global__ void __launch_bounds__(Cfg<CG, UN, X3, GATHER>::THREADS, 1)
+template <int CG, int UN, bool X3>
+__global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    using S = Cfg<CG, UN, X3, GATHER>;
+    using S = Cfg<CG, UN, X3>;
     constexpr int STAGES = S::STAGES;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte-swizzle atoms.
@@ -380,7 +254,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3, GATHER>::THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1 + S::GATHER_THREADS);  // the TMA warp (+ each gathering thread)
+            mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -394,10 +268,10 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3, GATHER>::THREADS, 1)
     }
     if (warp == 0 && lane == 0) {
         prefetch_map(&p.tmA[0]);
-        if constexpr (!GATHER) prefetch_map(&p.tmB[0]);
+        prefetch_map(&p.tmB[0]);
         if constexpr (X3) {
             prefetch_map(&p.tmA[1]);
-            if constexpr (!GATHER) prefetch_map(&p.tmB[1]);
+            prefetch_map(&p.tmB[1]);
         }
     }
     if (warp == 1) {
@@ -444,9 +318,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3, GATHER>::THREADS, 1)
                     const int nsub = min(S::SUBS, it.left_in_chunk());
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
-                    if (leader && elect_one())
-                        mbar_expect_tx(&full[stage], nsub * (GATHER ? (X3 ? 2 : 1) * S::A_BYTES
-                                                                    : S::KB_BYTES * CG));
+                    if (leader && elect_one()) mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
                     for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
                         const int k0 = it.kb() * BK;
                         if (!elect_one()) continue;
@@ -465,9 +337,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3, GATHER>::THREADS, 1)
                             } else {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, k0, m0, a0, a1, a2);
                             }
-                            if (GATHER) {
-                                // B comes from the gathering warps
-                            } else if (p.b_chunked) {
+                            if (p.b_chunked) {
                                 tma_load_5d<CG>(sb, &p.tmB[h], fb, 0, k0, n0 >> 5, b0, b1);
                             } else if (p.b_mn) {
 #pragma unroll
@@ -619,40 +489,6 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3, GATHER>::THREADS, 1)
                 }
             }
             __syncwarp();
-        }
-    } else if (GATHER && warp >= 2 + S::EPI_WARPS) {
-        // ---------------- B producers (gather variants) ----------------
-        const int gt = threadIdx.x - 32 * (2 + S::EPI_WARPS);  // 0 .. 127
-        int stage = 0;
-        uint32_t phase = 0;
-        bool ok = true;
-        for (int64_t t = unit; ok && t < p.num_tiles; t += units) {
-            const TileCoord tc = tile_coord(p, t);
-            int bi[kMaxBatchDims];
-            batch_coords(p, tc.b, bi);
-            const float* src = p.gb.src + bi[0] * p.gb.img_stride + bi[1] * p.gb.grp_stride;
-            const int n0 = tc.n * UN;
-            KbIter it;
-            it.start(p);
-            for (int kb = 0; kb < p.k_blocks;) {
-                if (!warp_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.timeout_ns, p.err, 5,
-                                       kGemmSleepNs)) {
-                    ok = false;
-                    break;
-                }
-                const int nsub = min(S::SUBS, it.left_in_chunk());
-                for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
-                    uint8_t* sb = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES + S::A_BYTES;
-                    gather_b_tile<CG, UN, X3, GATHER>(p, src, n0, it.kb() * BK, sb,
-                                                      X3 ? sb + S::PAIR_BYTES : nullptr, gt);
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(&full[stage]);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-            }
         }
     } else {
         // ---------------- epilogue (warps 2.., both CTAs) ----------------
@@ -971,10 +807,10 @@ int* error_word() {
     return st == TLC_OK ? words[dev] : nullptr;
 }
 
-template <int CG, int UN, bool X3, bool GATHER = false>
+template <int CG, int UN, bool X3>
 int launch_variant(const TcParams& prm, cudaStream_t s) {
-    using S = Cfg<CG, UN, X3, GATHER>;
-    auto kernel = tc_gemm_kernel<CG, UN, X3, GATHER>;
+    using S = Cfg<CG, UN, X3>;
+    auto kernel = tc_gemm_kernel<CG, UN, X3>;
     static DeviceOnce once;
     static int max_units[64] = {};
     cudaLaunchConfig_t cfg = {};
@@ -1284,84 +1120,6 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
     return launch_tc(prm, g, x3, s);
-}
-
-// Implicit-im2col GEMM: A through TMA as in gemm_tc, B gathered from an
-// NCHW tensor by the kernel's producer warps (no column buffer).  Single-CTA
-// tiles of 128 rows x 256 (TF32) / 128 (3xTF32) columns.
-int gemm_tc_im2col(const Gemm& g, const Im2colDesc& d, int mode, cudaStream_t s) {
-    if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
-    if (g.K == 0) return gemm_exact(g, s);  // writes zeros
-    if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX || g.nb > 2)
-        return set_error(TLC_ERR_UNSUPPORTED, "implicit-im2col GEMM: sizes out of range");
-    for (int i = 0; i < g.nb; ++i)
-        if (g.bsz[i] > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "batch dim too large");
-    const bool x3 = mode == TLC_MODE_3XTF32;
-    const bool a_mn = g.a_cs != 1;
-    Gemm gb = g;  // B has no memory layout here: a dummy K-major operand
-    gb.B = g.A;
-    gb.b_rs = 1;
-    gb.b_cs = g.K;
-    for (int i = 0; i < kMaxBatchDims; ++i) gb.bbs[i] = 0;
-    const int un = (x3 || g.N <= 128) ? 128 : 256;
-    OperandMap A, B;
-    operand_maps(gb, a_mn, false, A, B, (uint32_t)un);
-    TcScratch sc(s);
-    if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb)) TLC_TRY(repack(A, g.nb, sc, 0, s));
-
-    TcParams prm;
-    memset(&prm, 0, sizeof(prm));
-    if (x3) {
-        const bool lo_only = tf32_reads_truncated(s);
-        const int64_t n = span_elems(A.inner, A.outer, A.outer_stride, A.bsz, A.bstride, g.nb);
-        TLC_TRY(scratch_alloc(&sc.p[2], sizeof(float) * (size_t)n * (lo_only ? 1 : 2), s));
-        float* plane = static_cast<float*>(sc.p[2]);
-        OperandMap h = A, l = A;
-        if (lo_only) {
-            split_lo_kernel<<<grid_split(n), 256, 0, s>>>(A.base, plane, n);
-            l.base = plane;
-        } else {
-            split_tf32_kernel<<<grid_split(n), 256, 0, s>>>(A.base, plane, plane + n, n);
-            h.base = plane;
-            l.base = plane + n;
-        }
-        count_launch();
-        TLC_TRY(check_launch("split_tf32"));
-        TLC_TRY(encode(&prm.tmA[0], h));
-        TLC_TRY(encode(&prm.tmA[1], l));
-        prm.gather_round = lo_only ? 0 : 1;
-    } else {
-        TLC_TRY(encode(&prm.tmA[0], A));
-    }
-    fill_common(prm, gb, A, B, a_mn, false, x3);
-    if (!x3 && prm.vec_c) {
-        if (encode_tiled(&prm.tmC, g.C, g.N, g.M, g.c_rs, A.bsz, g.cbs, 32, 32,
-                         CU_TENSOR_MAP_SWIZZLE_128B) == TLC_OK)
-            prm.tma_c = 1;
-        else
-            clear_error();
-    }
-    prm.gather = d.rows_are_pixels ? 1 : 2;
-    prm.gb.src = d.src;
-    prm.gb.img_stride = d.img_stride;
-    prm.gb.grp_stride = d.grp_stride;
-    prm.gb.H = d.H;
-    prm.gb.W = d.W;
-    prm.gb.W_out = d.W_out;
-    prm.gb.P = d.P;
-    prm.gb.kH = d.kH;
-    prm.gb.kW = d.kW;
-    prm.gb.stride = d.stride;
-    prm.gb.pad = d.pad;
-    prm.gb.taps = d.taps;
-    prm.err = error_word();
-    if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
-    prm.m_tiles = (int)((g.M + BM - 1) / BM);
-    prm.n_tiles = (int)((g.N + un - 1) / un);
-    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
-    if (x3) return launch_variant<1, 128, true, true>(prm, s);
-    return un == 256 ? launch_variant<1, 256, false, true>(prm, s)
-                     : launch_variant<1, 128, false, true>(prm, s);
 }
 
 int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
