@@ -99,7 +99,13 @@ def test_device_conv2d_exact(case):
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode,tol", [("tf32", 1e-2), ("3xtf32", 1e-5)])
 @pytest.mark.parametrize("case", [(4, 32, 28, 28, 64, 3, 1, 1, 1), (2, 64, 30, 30, 64, 3, 1, 1, 1),
-                                  (2, 16, 17, 23, 48, 3, 1, 0, 1), (2, 8, 15, 15, 12, 5, 1, 2, 2)]
+                                  (2, 16, 17, 23, 48, 3, 1, 0, 1), (2, 8, 15, 15, 12, 5, 1, 2, 2),
+                                  # implicit GEMM (stride 1, output rows a multiple of 8 wide):
+                                  # forward and input gradient without a column buffer
+                                  (2, 64, 16, 16, 64, 3, 1, 1, 1), (2, 32, 20, 24, 48, 3, 1, 1, 1),
+                                  (1, 4, 10, 8, 8, 3, 1, 1, 1), (2, 64, 12, 16, 64, 3, 1, 1, 2),
+                                  (1, 16, 12, 16, 16, 5, 1, 2, 1), (2, 32, 8, 8, 16, 1, 1, 0, 1),
+                                  (2, 64, 56, 56, 64, 3, 1, 1, 1)]
                          # float64 torch needs the padded input at least as large as the kernel
                          + [c for c in CASES if min(c[2], c[3]) + 2 * c[7] >= c[5]])
 def test_device_conv2d_tensor_cores(mode, tol, case):

@@ -152,6 +152,41 @@ inline BatchOffsets batch_offsets(const Gemm& g) {
 // Kernels (each returns a tlc_status).
 int gemm_exact(const Gemm& g, cudaStream_t s);
 int gemm_tc(const Gemm& g, int mode, cudaStream_t s);
+// An implicit-GEMM convolution (stride 1) on the tensor cores: the GEMM
+// out[n, g] (M output channels x N output pixels) = A[g] (M x K) . B[n, g],
+// K = kH * kW * (32 * cblocks) ordered (kh, kw, channel), where B's column
+// j = oh * W_out + ow, row (kh, kw, c) is x[n, oh - pad_h + kh, ow - pad_w + kw,
+// g * c_group + c] of the NHWC tensor x (zero outside it).  Batch dim 0 of the
+// Gemm is the image, dim 1 the group; its B fields are ignored.  Tiles are
+// `rows` output rows of W_out pixels (W_out % 8 == 0, rows * W_out <= 256 and
+// a multiple of 16).  X3 needs x_lo: the lo plane of x for the 3xTF32 split.
+struct ConvTma {
+    const float* x;
+    const float* x_lo;
+    int N, H, W, C;
+    int W_out, rows;
+    int kH, kW, pad_h, pad_w;
+    int cblocks, c_group;
+    const float* row_bias;  // NULL, or bias[b0 * row_bias_bs[0] + b1 * row_bias_bs[1] + row]
+    int64_t row_bias_bs[2];
+};
+int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s);
+// The weight gradient of a stride-1 convolution as an implicit GEMM:
+// out[n][g * o_group + o][(kh * kW + kw) * cpad + c] = sum over output pixels
+// of dO[n][g * o_group + o][pixel] * x[n, pixel's input under tap (kh, kw),
+// g * c_group + c] (x NHWC, zero outside; dO NCHW [N][C_out][H_out][W_out]).
+// One partial product per image; the caller sums them.  X3 needs the lo
+// planes of both (dout_lo in dO's layout, x_lo in x's).
+struct ConvDw {
+    const float* dout;
+    const float* dout_lo;
+    const float* x;
+    const float* x_lo;
+    float* out;
+    int N, groups, C, H, W, C_out, H_out, W_out;
+    int kH, kW, pad, cpad, c_group, o_group;
+};
+int gemm_tc_conv_dw(const ConvDw& d, int mode, cudaStream_t s);
 // out[o,n] = sum over d ascending of in[o,d,n], from init[o,n] (NULL: from 0.0f).
 int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
                    cudaStream_t s, const float* init = nullptr);

@@ -452,6 +452,250 @@ int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
     return TLC_OK;
 }
 
+// ---- implicit-GEMM convolution (TF32 / 3xTF32, stride 1) -----------------------------
+//
+// The column buffer of im2col is replaced by TMA boxes of an NHWC copy of the
+// input (gemm_tc_conv): for tap (kh, kw) and 32 input channels, an output row
+// of W_out pixels is one box starting at input column kw - pad of input row
+// oh - pad + kh, zero-filled where it reaches past the image (the padding).
+// The weights are repacked to [C_out][kh][kw][channels rounded up to 32]
+// (zero past the group's channels) so that the GEMM's k order is (kh, kw, c).
+// The input gradient at stride 1 is the same convolution of dO with the
+// flipped, transposed weights and padding k - 1 - p.  Exact mode keeps
+// im2col, whose k order is the reference's.
+
+// y[n][p][c] = x[n][c][p] (NCHW -> NHWC, p = h * W + w).  split 1: also
+// lo = x - trunc_tf32(x); split 2: y = round_tf32(x), lo = x - y (the 3xTF32
+// planes of the B operand; hi is y).
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                    float* __restrict__ lo, int64_t C, int64_t P, int split) {
+    __shared__ float t[32][33];
+    const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * 32, c0 = (int64_t)blockIdx.y * 32;
+    const float* xi = x + n * C * P;
+    for (int k = 0; k < 32; k += 8) {
+        const int64_t c = c0 + threadIdx.y + k, p = p0 + threadIdx.x;
+        t[threadIdx.y + k][threadIdx.x] = (c < C && p < P) ? xi[c * P + p] : 0.0f;
+    }
+    __syncthreads();
+    for (int k = 0; k < 32; k += 8) {
+        const int64_t p = p0 + threadIdx.y + k, c = c0 + threadIdx.x;
+        if (p >= P || c >= C) continue;
+        float v = t[threadIdx.x][threadIdx.y + k];
+        const int64_t o = (n * P + p) * C + c;
+        if (split == 1) {
+            lo[o] = __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xFFFFE000u));
+        } else if (split == 2) {
+            uint32_t h;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+            lo[o] = __fsub_rn(v, __uint_as_float(h));
+            v = __uint_as_float(h);
+        }
+        y[o] = v;
+    }
+}
+
+// Weights as the implicit GEMM's A: dst[r][kh][kw][q], q < q_pad (zero past
+// the real count).  flip 0 (forward): r = output channel o, q = input
+// channel c of o's group: W[o][q][kh][kw].  flip 1 (input gradient): r =
+// input channel g * C_in_g + c, q = output channel o of group g:
+// W[g * C_out_g + q][c][kH - 1 - kh][kW - 1 - kw].
+__global__ void conv_weights_kernel(const float* __restrict__ w, float* __restrict__ dst, ConvShape s,
+                                    int flip, int64_t q_pad) {
+    const int64_t khw = s.kH * s.kW;
+    const int64_t rows = flip ? s.C_in : s.C_out, per_row = khw * q_pad;
+    const int64_t n = rows * per_row;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / per_row, rem = i - r * per_row;
+        const int64_t tap = rem / q_pad, q = rem - tap * q_pad;
+        const int64_t kh = tap / s.kW, kw = tap - kh * s.kW;
+        float v = 0.0f;
+        if (!flip) {
+            if (q < s.C_in_g) v = w[(r * s.C_in_g + q) * khw + kh * s.kW + kw];
+        } else if (q < s.C_out_g) {
+            const int64_t g = r / s.C_in_g, c = r - g * s.C_in_g;
+            v = w[((g * s.C_out_g + q) * s.C_in_g + c) * khw + (s.kH - 1 - kh) * s.kW + (s.kW - 1 - kw)];
+        }
+        dst[i] = v;
+    }
+}
+
+int64_t round32(int64_t v) { return (v + 31) / 32 * 32; }
+
+// Output rows per implicit-GEMM tile for an output row width: the most rows
+// whose pixels fit `cap` columns as a multiple of 16 (0: none fits).
+int conv_tile_rows(int64_t width, int cap) {
+    if (width <= 0 || width % 8) return 0;
+    for (int64_t r = cap / width; r >= 1; --r)
+        if ((r * width) % 16 == 0) return (int)r;
+    return 0;
+}
+
+// Whether a convolution of `C` input channels (C_g per group) over planes of
+// H x W giving rows of `out_w` runs as an implicit GEMM in this mode.
+bool conv_tma_ok(const ConvShape& s, int64_t C, int64_t C_g, int64_t H, int64_t W, int64_t out_w,
+                 int mode) {
+    const int64_t lim = int64_t(1) << 30;
+    return mode != TLC_MODE_EXACT && s.stride == 1 && C % 4 == 0 &&
+           (s.groups == 1 || C_g % 32 == 0) && H < lim && W < lim && C < lim && s.N < lim &&
+           s.N <= 65535 && conv_tile_rows(out_w, mode == TLC_MODE_3XTF32 ? 128 : 256) > 0 &&
+           s.kH * s.kW * round32(C_g) < lim;
+}
+
+// NHWC copy (and 3xTF32 lo plane) of a dense NCHW tensor [N, C, H*W].
+int to_nhwc(const float* x, int64_t N, int64_t C, int64_t P, int mode, Buf& hi, Buf& lo,
+            cudaStream_t st) {
+    const int64_t n = N * C * P;
+    int split = 0;
+    if (mode == TLC_MODE_3XTF32) split = tf32_reads_truncated(st) ? 1 : 2;
+    TLC_TRY(scratch_alloc(&hi.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
+    if (split) TLC_TRY(scratch_alloc(&lo.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
+    if (!n) return TLC_OK;
+    dim3 grid((unsigned)((P + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);
+    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi.f(), split ? lo.f() : nullptr, C, P, split);
+    count_launch();
+    return check_launch("nchw_to_nhwc");
+}
+
+// out[n, g] (M x H_o * W_o) = A[g] . im2col(x_nhwc[n, g]) as an implicit GEMM.
+int conv_tma_gemm(const float* x, int64_t C, int64_t C_g, int64_t H, int64_t W, const float* a,
+                  int64_t M, int64_t H_o, int64_t W_o, int64_t pad_h, int64_t pad_w, float* out,
+                  int64_t out_img, const float* bias, const ConvShape& s, int mode, cudaStream_t st) {
+    Buf xh(st), xl(st);
+    TLC_TRY(to_nhwc(x, s.N, C, H * W, mode, xh, xl, st));
+    const int64_t c_pad = round32(C_g), K = s.kH * s.kW * c_pad, P = H_o * W_o;
+    Gemm g{};
+    g.M = M;
+    g.N = P;
+    g.K = K;
+    g.A = a;
+    g.a_rs = K;
+    g.a_cs = 1;
+    g.C = out;
+    g.c_rs = P;
+    g.nb = 2;
+    g.bsz[0] = s.N;
+    g.bsz[1] = s.groups;
+    g.abs_[0] = 0;
+    g.abs_[1] = M * K;
+    g.cbs[0] = out_img;
+    g.cbs[1] = M * P;
+    ConvTma c{};
+    c.x = xh.f();
+    c.x_lo = mode == TLC_MODE_3XTF32 ? xl.f() : nullptr;
+    c.N = (int)s.N;
+    c.H = (int)H;
+    c.W = (int)W;
+    c.C = (int)C;
+    c.W_out = (int)W_o;
+    c.rows = conv_tile_rows(W_o, mode == TLC_MODE_3XTF32 ? 128 : 256);
+    c.kH = (int)s.kH;
+    c.kW = (int)s.kW;
+    c.pad_h = (int)pad_h;
+    c.pad_w = (int)pad_w;
+    c.cblocks = (int)(c_pad / 32);
+    c.c_group = (int)C_g;
+    if (bias) {
+        c.row_bias = bias;
+        c.row_bias_bs[0] = 0;
+        c.row_bias_bs[1] = M;
+    }
+    return gemm_tc_conv(g, c, mode, st);
+}
+
+// The 3xTF32 planes of a tensor kept in its own layout: split 1 (the tensor
+// cores truncate): lo = x - trunc_tf32(x), hi is x itself; split 2: hi =
+// round_tf32(x), lo = x - hi.
+__global__ void split_planes_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                    float* __restrict__ lo, int64_t n, int split) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        if (split == 1) {
+            lo[i] = __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xFFFFE000u));
+        } else {
+            uint32_t h;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+            hi[i] = __uint_as_float(h);
+            lo[i] = __fsub_rn(v, __uint_as_float(h));
+        }
+    }
+}
+
+// dw[o][c][kh][kw] = sum over images n = 0, 1, ... of
+// prod[n][o][(kh * kW + kw) * cpad + c]: the weight gradient's sum over
+// images (the reference's += order) and the (tap, channel) -> (channel, tap)
+// reorder of the implicit GEMM's columns.
+__global__ void conv_dw_reduce_kernel(const float* __restrict__ prod, float* __restrict__ dw,
+                                      ConvShape s, int64_t cpad) {
+    const int64_t khw = s.kH * s.kW, n_out = s.C_out * s.C_in_g * khw;
+    const int64_t row = khw * cpad, img = s.C_out * row;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_out;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = i / (s.C_in_g * khw), r = i - o * (s.C_in_g * khw);
+        const int64_t c = r / khw, tap = r - c * khw;
+        const float* p = prod + o * row + tap * cpad + c;
+        float acc = 0.0f;
+        for (int64_t n = 0; n < s.N; ++n) acc = __fadd_rn(acc, p[n * img]);
+        dw[i] = acc;
+    }
+}
+
+// dW as an implicit GEMM (stride 1; the tensor-core modes).
+bool conv_dw_ok(const ConvShape& s, const float* go, int mode) {
+    const int64_t lim = int64_t(1) << 30;
+    return mode != TLC_MODE_EXACT && (reinterpret_cast<uintptr_t>(go) & 15) == 0 && s.stride == 1 &&
+           s.C_in % 4 == 0 && s.C_out % 4 == 0 &&
+           s.W_out % 4 == 0 && (s.groups == 1 || s.C_in_g % 32 == 0) && s.N < lim && s.H < lim &&
+           s.W < lim && s.C_in < lim && s.C_out < lim && s.H_out > 0 && s.W_out > 0 &&
+           s.H_out * (s.W_out + 31) / 32 * 32 < lim && s.kH * s.kW * round32(s.C_in_g) < lim;
+}
+
+int conv_dw_implicit(const float* go, const float* in, const ConvShape& s, float* dw, int mode,
+                     cudaStream_t st) {
+    Buf xh(st), xl(st), gh(st), gl(st), prod(st);
+    TLC_TRY(to_nhwc(in, s.N, s.C_in, s.H * s.W, mode, xh, xl, st));
+    ConvDw d{};
+    d.dout = go;
+    if (mode == TLC_MODE_3XTF32) {
+        const int split = tf32_reads_truncated(st) ? 1 : 2;
+        const int64_t n = s.N * s.C_out * s.HW;
+        TLC_TRY(scratch_alloc(&gl.p, sizeof(float) * (size_t)n, st));
+        if (split == 2) TLC_TRY(scratch_alloc(&gh.p, sizeof(float) * (size_t)n, st));
+        split_planes_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16)), 256,
+                              0, st>>>(go, split == 2 ? gh.f() : nullptr, gl.f(), n, split);
+        count_launch();
+        TLC_TRY(check_launch("conv split"));
+        if (split == 2) d.dout = gh.f();
+        d.dout_lo = gl.f();
+        d.x_lo = xl.f();
+    }
+    const int64_t cpad = round32(s.C_in_g), cols = s.kH * s.kW * cpad;
+    TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(s.N * s.C_out * cols), st));
+    d.x = xh.f();
+    d.out = prod.f();
+    d.N = (int)s.N;
+    d.groups = (int)s.groups;
+    d.C = (int)s.C_in;
+    d.H = (int)s.H;
+    d.W = (int)s.W;
+    d.C_out = (int)s.C_out;
+    d.H_out = (int)s.H_out;
+    d.W_out = (int)s.W_out;
+    d.kH = (int)s.kH;
+    d.kW = (int)s.kW;
+    d.pad = (int)s.padding;
+    d.cpad = (int)cpad;
+    d.c_group = (int)s.C_in_g;
+    d.o_group = (int)s.C_out_g;
+    TLC_TRY(gemm_tc_conv_dw(d, mode, st));
+    const int64_t n_out = s.C_out * s.C_in_g * s.kH * s.kW;
+    conv_dw_reduce_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 148 * 16)), 256,
+                            0, st>>>(prod.f(), dw, s, cpad);
+    count_launch();
+    return check_launch("conv dw reduce");
+}
+
 int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bias, int64_t stride,
             int64_t padding, int64_t groups, tlc_tensor* out, int mode, cudaStream_t st) {
     ConvShape s;
@@ -470,6 +714,21 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
     const float *in, *w;
     TLC_TRY(dense_copy(in_t, bin, &in, st));
     TLC_TRY(dense_copy(w_t, bw, &w, st));
+    if (s.patch > 0 && conv_tma_ok(s, s.C_in, s.C_in_g, s.H, s.W, s.W_out, mode)) {
+        // implicit GEMM: no column buffer; the bias (one value per output
+        // channel: a GEMM row) added in the epilogue, the same fp32 add
+        const int64_t q_pad = round32(s.C_in_g), nwp = s.C_out * s.kH * s.kW * q_pad;
+        Buf wp(st);
+        TLC_TRY(scratch_alloc(&wp.p, sizeof(float) * (size_t)nwp, st));
+        conv_weights_kernel<<<(unsigned)std::min<int64_t>((nwp + 255) / 256, 148 * 16), 256, 0, st>>>(
+            w, wp.f(), s, 0, q_pad);
+        count_launch();
+        TLC_TRY(check_launch("conv weights"));
+        const float* bd = nullptr;
+        if (b) TLC_TRY(dense_copy(b, bb, &bd, st));
+        return conv_tma_gemm(in, s.C_in, s.C_in_g, s.H, s.W, wp.f(), s.C_out_g, s.H_out, s.W_out,
+                             s.padding, s.padding, out->data, s.C_out * s.HW, bd, s, mode, st);
+    }
     TLC_TRY(make_col(in, s, col, st));
     // out[n, g] (C_out_g x HW) = W_g (C_out_g x patch) . col[n, g] (patch x HW)
     Gemm g{};
@@ -526,7 +785,9 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
     TLC_TRY(dense_copy(go_t, bgo, &go, st));
     TLC_TRY(dense_copy(in_t, bin, &in, st));
     TLC_TRY(dense_copy(w_t, bw, &w, st));
-    if (d_w) {
+    if (d_w && s.N * s.C_out * s.patch > 0 && conv_dw_ok(s, go, mode)) {
+        TLC_TRY(conv_dw_implicit(go, in, s, d_w->data, mode, st));
+    } else if (d_w) {
         // G[n, g] (C_out_g x patch) = dO[n, g] (C_out_g x HW) . col[n, g]^T, then sum over n
         if (s.N * s.C_out * s.patch == 0) {
             if (s.C_out * s.patch) TLC_TRY(launch_fill_zero(d_w->data, s.C_out * s.patch, st));
@@ -563,7 +824,20 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             TLC_TRY(launch_sum_dim(prod.f(), d_w->data, 1, s.N, s.C_out * s.patch, st));
         }
     }
-    if (d_in) {
+    if (d_in && s.N * s.C_in * s.H * s.W > 0 && s.kH - 1 - s.padding >= 0 &&
+        s.kW - 1 - s.padding >= 0 && conv_tma_ok(s, s.C_out, s.C_out_g, s.H_out, s.W_out, s.W, mode)) {
+        // stride 1: dX = the convolution of dO with the flipped, transposed
+        // weights, padding k - 1 - p, as the same implicit GEMM
+        const int64_t q_pad = round32(s.C_out_g), nwp = s.C_in * s.kH * s.kW * q_pad;
+        TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)nwp, st));
+        conv_weights_kernel<<<(unsigned)std::min<int64_t>((nwp + 255) / 256, 148 * 16), 256, 0, st>>>(
+            w, gcol.f(), s, 1, q_pad);
+        count_launch();
+        TLC_TRY(check_launch("conv weights"));
+        TLC_TRY(conv_tma_gemm(go, s.C_out, s.C_out_g, s.H_out, s.W_out, gcol.f(), s.C_in_g, s.H, s.W,
+                              s.kH - 1 - s.padding, s.kW - 1 - s.padding, d_in->data,
+                              s.C_in * s.H * s.W, nullptr, s, mode, st));
+    } else if (d_in) {
         const int64_t ni = s.N * s.C_in * s.H * s.W;
         if (ni) {
             const int64_t nc = s.N * s.groups * s.patch * s.HW;
