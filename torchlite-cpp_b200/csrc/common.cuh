@@ -167,26 +167,11 @@ struct ConvTma {
     int W_out, rows;
     int kH, kW, pad_h, pad_w;
     int cblocks, c_group;
-    const float* row_bias;  // NULL, or bias[b0 * row_bias_bs[0] + b1 * row_bias_bs[1] + row]
-    int64_t row_bias_bs[2];
+    const float* row_bias;  // NULL, or one per output row: bias[group * row_bias_group + row]
+    int64_t row_bias_group;
 };
 int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s);
-// The weight gradient of a stride-1 convolution as an implicit GEMM:
-// out[n][g * o_group + o][(kh * kW + kw) * cpad + c] = sum over output pixels
-// of dO[n][g * o_group + o][pixel] * x[n, pixel's input under tap (kh, kw),
-// g * c_group + c] (x NHWC, zero outside; dO NCHW [N][C_out][H_out][W_out]).
-// One partial product per image; the caller sums them.  X3 needs the lo
-// planes of both (dout_lo in dO's layout, x_lo in x's).
-struct ConvDw {
-    const float* dout;
-    const float* dout_lo;
-    const float* x;
-    const float* x_lo;
-    float* out;
-    int N, groups, C, H, W, C_out, H_out, W_out;
-    int kH, kW, pad, cpad, c_group, o_group;
-};
-int gemm_tc_conv_dw(const ConvDw& d, int mode, cudaStream_t s);
+
 // out[o,n] = sum over d ascending of in[o,d,n], from init[o,n] (NULL: from 0.0f).
 int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
                    cudaStream_t s, const float* init = nullptr);

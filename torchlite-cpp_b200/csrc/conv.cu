@@ -597,103 +597,9 @@ int conv_tma_gemm(const float* x, int64_t C, int64_t C_g, int64_t H, int64_t W, 
     c.c_group = (int)C_g;
     if (bias) {
         c.row_bias = bias;
-        c.row_bias_bs[0] = 0;
-        c.row_bias_bs[1] = M;
+        c.row_bias_group = M;
     }
     return gemm_tc_conv(g, c, mode, st);
-}
-
-// The 3xTF32 planes of a tensor kept in its own layout: split 1 (the tensor
-// cores truncate): lo = x - trunc_tf32(x), hi is x itself; split 2: hi =
-// round_tf32(x), lo = x - hi.
-__global__ void split_planes_kernel(const float* __restrict__ x, float* __restrict__ hi,
-                                    float* __restrict__ lo, int64_t n, int split) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const float v = x[i];
-        if (split == 1) {
-            lo[i] = __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xFFFFE000u));
-        } else {
-            uint32_t h;
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
-            hi[i] = __uint_as_float(h);
-            lo[i] = __fsub_rn(v, __uint_as_float(h));
-        }
-    }
-}
-
-// dw[o][c][kh][kw] = sum over images n = 0, 1, ... of
-// prod[n][o][(kh * kW + kw) * cpad + c]: the weight gradient's sum over
-// images (the reference's += order) and the (tap, channel) -> (channel, tap)
-// reorder of the implicit GEMM's columns.
-__global__ void conv_dw_reduce_kernel(const float* __restrict__ prod, float* __restrict__ dw,
-                                      ConvShape s, int64_t cpad) {
-    const int64_t khw = s.kH * s.kW, n_out = s.C_out * s.C_in_g * khw;
-    const int64_t row = khw * cpad, img = s.C_out * row;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_out;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t o = i / (s.C_in_g * khw), r = i - o * (s.C_in_g * khw);
-        const int64_t c = r / khw, tap = r - c * khw;
-        const float* p = prod + o * row + tap * cpad + c;
-        float acc = 0.0f;
-        for (int64_t n = 0; n < s.N; ++n) acc = __fadd_rn(acc, p[n * img]);
-        dw[i] = acc;
-    }
-}
-
-// dW as an implicit GEMM (stride 1; the tensor-core modes).
-bool conv_dw_ok(const ConvShape& s, const float* go, int mode) {
-    const int64_t lim = int64_t(1) << 30;
-    return mode != TLC_MODE_EXACT && (reinterpret_cast<uintptr_t>(go) & 15) == 0 && s.stride == 1 &&
-           s.C_in % 4 == 0 && s.C_out % 4 == 0 &&
-           s.W_out % 4 == 0 && (s.groups == 1 || s.C_in_g % 32 == 0) && s.N < lim && s.H < lim &&
-           s.W < lim && s.C_in < lim && s.C_out < lim && s.H_out > 0 && s.W_out > 0 &&
-           s.H_out * (s.W_out + 31) / 32 * 32 < lim && s.kH * s.kW * round32(s.C_in_g) < lim;
-}
-
-int conv_dw_implicit(const float* go, const float* in, const ConvShape& s, float* dw, int mode,
-                     cudaStream_t st) {
-    Buf xh(st), xl(st), gh(st), gl(st), prod(st);
-    TLC_TRY(to_nhwc(in, s.N, s.C_in, s.H * s.W, mode, xh, xl, st));
-    ConvDw d{};
-    d.dout = go;
-    if (mode == TLC_MODE_3XTF32) {
-        const int split = tf32_reads_truncated(st) ? 1 : 2;
-        const int64_t n = s.N * s.C_out * s.HW;
-        TLC_TRY(scratch_alloc(&gl.p, sizeof(float) * (size_t)n, st));
-        if (split == 2) TLC_TRY(scratch_alloc(&gh.p, sizeof(float) * (size_t)n, st));
-        split_planes_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16)), 256,
-                              0, st>>>(go, split == 2 ? gh.f() : nullptr, gl.f(), n, split);
-        count_launch();
-        TLC_TRY(check_launch("conv split"));
-        if (split == 2) d.dout = gh.f();
-        d.dout_lo = gl.f();
-        d.x_lo = xl.f();
-    }
-    const int64_t cpad = round32(s.C_in_g), cols = s.kH * s.kW * cpad;
-    TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(s.N * s.C_out * cols), st));
-    d.x = xh.f();
-    d.out = prod.f();
-    d.N = (int)s.N;
-    d.groups = (int)s.groups;
-    d.C = (int)s.C_in;
-    d.H = (int)s.H;
-    d.W = (int)s.W;
-    d.C_out = (int)s.C_out;
-    d.H_out = (int)s.H_out;
-    d.W_out = (int)s.W_out;
-    d.kH = (int)s.kH;
-    d.kW = (int)s.kW;
-    d.pad = (int)s.padding;
-    d.cpad = (int)cpad;
-    d.c_group = (int)s.C_in_g;
-    d.o_group = (int)s.C_out_g;
-    TLC_TRY(gemm_tc_conv_dw(d, mode, st));
-    const int64_t n_out = s.C_out * s.C_in_g * s.kH * s.kW;
-    conv_dw_reduce_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 148 * 16)), 256,
-                            0, st>>>(prod.f(), dw, s, cpad);
-    count_launch();
-    return check_launch("conv dw reduce");
 }
 
 int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bias, int64_t stride,
@@ -785,9 +691,7 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
     TLC_TRY(dense_copy(go_t, bgo, &go, st));
     TLC_TRY(dense_copy(in_t, bin, &in, st));
     TLC_TRY(dense_copy(w_t, bw, &w, st));
-    if (d_w && s.N * s.C_out * s.patch > 0 && conv_dw_ok(s, go, mode)) {
-        TLC_TRY(conv_dw_implicit(go, in, s, d_w->data, mode, st));
-    } else if (d_w) {
+    if (d_w) {
         // G[n, g] (C_out_g x patch) = dO[n, g] (C_out_g x HW) . col[n, g]^T, then sum over n
         if (s.N * s.C_out * s.patch == 0) {
             if (s.C_out * s.patch) TLC_TRY(launch_fill_zero(d_w->data, s.C_out * s.patch, st));

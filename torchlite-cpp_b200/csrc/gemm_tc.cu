@@ -112,36 +112,32 @@ struct TcParams {
     const float* bias;  // epilogue (see Gemm): c * scale if apply_scale, + bias[col]
     float scale;
     int apply_scale;
-    // bias_row: the bias is one value per output row, bias[sum_i b_i * bias_bs[i] + row]
-    // (a convolution's per-channel bias), instead of bias[col]
-    int bias_row;
-    int64_t bias_bs[kMaxBatchDims];
-    int tile_n;  // output columns per tile (UN, or fewer for a convolution's row-aligned tiles)
-    int mma_n;   // the MMA's N (the tile's columns, a multiple of 16)
-    // Implicit-GEMM convolution (conv = 1, single CTA, stride 1): B is the
-    // NHWC input through a 4-D tensor map {C, W, H, N} (tmB; X3: tmB[1] its
-    // lo plane).  k-block kb is channels 32 * (kb % cblocks) .. + 31 of tap
-    // kb / cblocks = kh * kW + kw; a tile is `rows` output rows of W_out
-    // pixels, each row one TMA box {32 channels, W_out columns} starting at
-    // input column kw - pad_w of input row oh - pad_h + kh (out-of-range rows
-    // and columns are the padding: zero-filled by TMA).  Batch dim 0 is the
-    // image, batch dim 1 the group (channel offset c_group per group).
-    // conv = 2 (weight gradient): A is dO through {W_out, H_out, C_out, N}
-    // (k-block kb: 32 columns from 32 * (kb % wblocks) of output row
-    // kb / wblocks, rows = output channels from group g * o_group), B the NHWC
-    // input through {C, W, H, N} as MN-major 32-channel chunks (column j of
-    // the tile's N is channel j % cpad of tap j / cpad).
-    int conv;
+    // Implicit-GEMM convolution (the CONV variants: single CTA, stride 1).
+    // B is the NHWC input through a 4-D tensor map {C, W, H, N} (tmB; X3:
+    // tmB[1] its lo plane).  k-block kb is channels 32 * (kb % cv_cblocks) ..
+    // + 31 of tap kb / cv_cblocks = kh * kW + kw; a tile is cv_rows output rows
+    // of cv_W_out pixels (tile_n columns, the MMA's N), each row one TMA box
+    // {32 channels, W_out columns} starting at input column kw - pad_w of input
+    // row oh - pad_h + kh (out-of-range rows and columns are the padding:
+    // zero-filled by TMA).  Batch dim 0 is the image, batch dim 1 the group
+    // (channel offset cv_c_group per group).  The bias, if any, is one value
+    // per output row: bias[b1 * bias_group + row].
+    int tile_n;
     int cv_cblocks, cv_kW, cv_pad_h, cv_pad_w, cv_rows, cv_W_out, cv_c_group;
-    int cv_wblocks, cv_cpad, cv_o_group;
+    int64_t bias_group;
 };
 
 // The GEMM epilogue on one output value: one IEEE fp32 operation per step,
-// as the reference's separate tl::scale / tl::add would round it; `rb` is
-// the row's bias when the bias is per row.
-__device__ __forceinline__ float tc_epilogue(const TcParams& p, float v, int col, float rb) {
+// as the reference's separate tl::scale / tl::add would round it.
+__device__ __forceinline__ float tc_epilogue(const TcParams& p, float v, int col) {
     if (p.apply_scale) v = __fmul_rn(v, p.scale);
-    if (p.bias) v = __fadd_rn(v, p.bias_row ? rb : p.bias[col]);
+    if (p.bias) v = __fadd_rn(v, p.bias[col]);
+    return v;
+}
+// The same with a per-row bias value (the CONV variants).
+__device__ __forceinline__ float tc_epilogue_row(const TcParams& p, float v, float rb) {
+    if (p.apply_scale) v = __fmul_rn(v, p.scale);
+    if (p.bias) v = __fadd_rn(v, rb);
     return v;
 }
 
@@ -248,7 +244,7 @@ struct Cfg {
 
 // X3: the epilogue adds the chunk partials of each output element into
 // registers in fp32 round-to-nearest and stores after the last chunk.
-template <int CG, int UN, bool X3>
+template <int CG, int UN, bool X3, bool CONV = false>
 __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcParams p) {
     using S = Cfg<CG, UN, X3>;
@@ -341,10 +337,13 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     const int nsub = min(S::SUBS, it.left_in_chunk());
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
-                    if (leader && elect_one())
-                        mbar_expect_tx(&full[stage],
-                                       p.conv == 1 ? nsub * (X3 ? 2 : 1) * (S::A_BYTES + p.cv_rows * p.cv_W_out * 128)
-                                                   : nsub * S::KB_BYTES * CG);
+                    if (leader && elect_one()) {
+                        if constexpr (CONV)
+                            mbar_expect_tx(&full[stage], nsub * (X3 ? 2 : 1) *
+                                                             (S::A_BYTES + p.cv_rows * p.cv_W_out * 128));
+                        else
+                            mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
+                    }
                     for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
                         const int k0 = it.kb() * BK;
                         if (!elect_one()) continue;
@@ -353,13 +352,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
                                           h * S::PAIR_BYTES;
                             uint8_t* sb = sa + S::A_BYTES;
-                            if (p.conv == 2) {
-                                // dO: 32 output columns of one output row, 128 channels
-                                const int kb = k0 / BK;
-                                const int oh = kb / p.cv_wblocks;
-                                tma_load_5d<CG>(sa, &p.tmA[h], fb, (kb - oh * p.cv_wblocks) * 32, oh,
-                                                bi[1] * p.cv_o_group + m0, bi[0], 0);
-                            } else if (p.a_chunked) {
+                            if (p.a_chunked) {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, 0, k0, m0 >> 5, a0, a1);
                             } else if (p.a_mn) {
 #pragma unroll
@@ -369,22 +362,8 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             } else {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, k0, m0, a0, a1, a2);
                             }
-                            if (p.conv == 2) {
-                                // the input pixels under those 32 output columns for each
-                                // (tap, 32 channels) chunk of the tile's columns
-                                const int kb = k0 / BK;
-                                const int oh = kb / p.cv_wblocks, ow0 = (kb - oh * p.cv_wblocks) * 32;
-#pragma unroll 1
-                                for (int c = 0; c < S::B_COLS / 32; ++c) {
-                                    const int col = n0 + 32 * c;
-                                    const int tap = col / p.cv_cpad, ch = col - tap * p.cv_cpad;
-                                    const int kh = tap / p.cv_kW, kw = tap - kh * p.cv_kW;
-                                    tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[h], fb,
-                                                    bi[1] * p.cv_c_group + ch, ow0 - p.cv_pad_w + kw,
-                                                    oh - p.cv_pad_h + kh, bi[0], 0);
-                                }
-                            } else if (p.conv == 1) {
-                                // `rows` boxes, one per output row of the tile
+                            if constexpr (CONV) {
+                                // cv_rows boxes, one per output row of the tile
                                 const int kb = k0 / BK;
                                 const int tap = kb / p.cv_cblocks, cb = kb - tap * p.cv_cblocks;
                                 const int kh = tap / p.cv_kW, kw = tap - kh * p.cv_kW;
@@ -434,7 +413,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
             // A/B major (bits 15, 16), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
             const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) |
                                    ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16) |
-                                   ((uint32_t)(p.mma_n >> 3) << 17) |
+                                   ((uint32_t)((CONV ? p.tile_n : UN) >> 3) << 17) |
                                    ((uint32_t)(S::TILE_M >> 4) << 24);
             const uint32_t chunk = 32 * BK * 4;  // bytes between 32-wide MN chunks
             // Descriptors of stage 0, k-step 0; a stage / k-step moves only the
@@ -565,17 +544,15 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < kMaxBatchDims; ++i) oc += (int64_t)bi[i] * p.cbs[i];
             const int64_t row = (int64_t)tc.m * S::TILE_M + (int)rank * BM + row_in_tile;
-            const int n0 = tc.n * p.tile_n + col_half * S::EPI_COLS;
-            // the columns this tile holds end here (TMEM columns past the
-            // tile's width hold nothing of it)
-            const int nlim = min(p.N, tc.n * p.tile_n + p.tile_n);
+            const int tn = CONV ? p.tile_n : UN;  // output columns of a tile
+            const int n0 = tc.n * tn + col_half * S::EPI_COLS;
+            // CONV: the tile's columns end here (TMEM columns past its width
+            // hold nothing of it); otherwise the matrix's
+            const int nlim = CONV ? min(p.N, tc.n * tn + tn) : p.N;
             float* crow = p.C + oc + row * p.c_rs;
-            float rb = 0.0f;  // this row's bias (per-row bias)
-            if (p.bias_row && row < p.M) {
-                int64_t bo = row;
-#pragma unroll
-                for (int i = 0; i < kMaxBatchDims; ++i) bo += (int64_t)bi[i] * p.bias_bs[i];
-                rb = p.bias[bo];
+            float rb = 0.0f;  // CONV: this row's bias
+            if constexpr (CONV) {
+                if (p.bias && row < p.M) rb = p.bias[bi[1] * p.bias_group + row];
             }
             float sum[X3 ? S::EPI_COLS : 1];
 #pragma unroll
@@ -612,18 +589,18 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                         tmem_ld32(taddr + c * 32, r);
                         tmem_wait_ld();
                         const int col0 = n0 + c * 32;
-                        if (col0 >= nlim) continue;  // past this tile's columns (warp-uniform)
-                        if (p.tma_c && (col0 + 32 <= nlim || nlim == p.N)) {  // warp-uniform
+                        if (CONV && col0 >= nlim) continue;  // past the tile (warp-uniform)
+                        if (p.tma_c && (!CONV || col0 + 32 <= nlim || nlim == p.N)) {  // warp-uniform
                             // The square goes out with one TMA store (rows and
-                            // columns past M, N clipped by the tensor map; a
-                            // square that would reach into the next tile's
-                            // columns takes the element-wise path below).
-                            if (row0 >= p.M) continue;
+                            // columns past M, N clipped by the tensor map; in a
+                            // CONV tile, a square that would reach the next
+                            // tile's columns takes the element-wise path).
+                            if (col0 >= p.N || row0 >= p.M) continue;
                             if (p.bias || p.apply_scale) {
 #pragma unroll
                                 for (int j = 0; j < 32; ++j)
                                     if (col0 + j < nlim)
-                                        r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j, rb));
+                                        r[j] = __float_as_uint((CONV ? tc_epilogue_row(p, __uint_as_float(r[j]), rb) : tc_epilogue(p, __uint_as_float(r[j]), col0 + j)));
                             }
                             if (lane == 0) bulk_wait_read_all();  // the previous square was read out
                             __syncwarp();
@@ -641,7 +618,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             if (p.bias || p.apply_scale) {
 #pragma unroll
                                 for (int j = 0; j < 32; ++j)
-                                    r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j, rb));
+                                    r[j] = __float_as_uint((CONV ? tc_epilogue_row(p, __uint_as_float(r[j]), rb) : tc_epilogue(p, __uint_as_float(r[j]), col0 + j)));
                             }
 #pragma unroll
                             for (int j = 0; j < 8; ++j)
@@ -663,7 +640,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
 #pragma unroll
                                 for (int j = 0; j < 32; ++j)
                                     if (col0 + j < nlim)
-                                        r[j] = __float_as_uint(tc_epilogue(p, __uint_as_float(r[j]), col0 + j, rb));
+                                        r[j] = __float_as_uint((CONV ? tc_epilogue_row(p, __uint_as_float(r[j]), rb) : tc_epilogue(p, __uint_as_float(r[j]), col0 + j)));
                             }
 #pragma unroll
                             for (int j = 0; j < 32; ++j)
@@ -690,7 +667,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                         if (p.bias || p.apply_scale) {
 #pragma unroll
                             for (int j = 0; j < 32; ++j)
-                                if (col0 + j < nlim) sum[c * 32 + j] = tc_epilogue(p, sum[c * 32 + j], col0 + j, rb);
+                                if (col0 + j < nlim) sum[c * 32 + j] = (CONV ? tc_epilogue_row(p, sum[c * 32 + j], rb) : tc_epilogue(p, sum[c * 32 + j], col0 + j));
                         }
                         if (p.vec_c && col0 + 32 <= nlim) {
 #pragma unroll
@@ -876,10 +853,10 @@ int* error_word() {
     return st == TLC_OK ? words[dev] : nullptr;
 }
 
-template <int CG, int UN, bool X3>
+template <int CG, int UN, bool X3, bool CONV = false>
 int launch_variant(const TcParams& prm, cudaStream_t s) {
     using S = Cfg<CG, UN, X3>;
-    auto kernel = tc_gemm_kernel<CG, UN, X3>;
+    auto kernel = tc_gemm_kernel<CG, UN, X3, CONV>;
     static DeviceOnce once;
     static int max_units[64] = {};
     cudaLaunchConfig_t cfg = {};
@@ -948,8 +925,6 @@ int launch_tc(TcParams& prm, const Gemm& g, bool x3, cudaStream_t s) {
     pick_variant(g, x3, &cg, &un);
     prm.m_tiles = (int)((g.M + BM * cg - 1) / (BM * cg));
     prm.n_tiles = (int)((g.N + un - 1) / un);
-    prm.tile_n = un;
-    prm.mma_n = un;
     prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
     if (x3) {
         if (cg == 1) return launch_variant<1, 128, true>(prm, s);
@@ -1215,101 +1190,7 @@ int encode_conv_b(CUtensorMap* map, const float* x, const ConvTma& c) {
 }
 }  // namespace
 
-namespace {
-// A 4-D fp32 tensor {d0 (contiguous), d1, d2, d3} with the given box, as a
-// 5-D map (last dim 1); reads outside it fill zeros.
-int encode_4d(CUtensorMap* map, const float* base, const int64_t (&dims)[4], uint32_t b0, uint32_t b1,
-              uint32_t b2, CUtensorMapSwizzle sw) {
-    auto fn = encode_fn();
-    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-    cuuint64_t d[5] = {(cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2], (cuuint64_t)dims[3], 1};
-    cuuint64_t st[4];
-    cuuint64_t acc = 4;
-    for (int i = 0; i < 4; ++i) {
-        acc *= d[i];
-        st[i] = acc;
-    }
-    cuuint32_t box[5] = {b0, b1, b2, 1, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), d, st, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(TLC_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled (4-D) failed (" + std::to_string((int)r) + ")");
-    return TLC_OK;
-}
-}  // namespace
-
-// Weight gradient of a stride-1 convolution as an implicit GEMM (TcParams
-// conv = 2): out[n, g] (o_group x kH*kW*cpad) = dO[n, g] . im2col(x[n, g])^T
-// with K = H_out * 32 * wblocks (each output row padded to whole k-blocks;
-// dO reads zero there).
-int gemm_tc_conv_dw(const ConvDw& d, int mode, cudaStream_t s) {
-    const bool x3 = mode == TLC_MODE_3XTF32;
-    const int64_t M = d.o_group, Ncols = (int64_t)d.kH * d.kW * d.cpad;
-    const int64_t wblocks = (d.W_out + 31) / 32, K = (int64_t)d.H_out * wblocks * 32;
-    if (d.N < 1 || d.groups < 1 || M < 1 || Ncols < 1 || d.H_out < 1) return TLC_OK;
-    if (d.C % 4 || d.cpad % 32 || d.C_out % 4 || (d.groups > 1 && d.c_group % 32) ||
-        (x3 && (!d.x_lo || !d.dout_lo)) || K > INT32_MAX || Ncols > INT32_MAX)
-        return set_error(TLC_ERR_UNSUPPORTED, "implicit-GEMM weight gradient: unsupported shape");
-    TcParams prm;
-    memset(&prm, 0, sizeof(prm));
-    const int64_t adims[4] = {d.W_out, d.H_out, d.C_out, d.N};
-    const int64_t bdims[4] = {d.C, d.W, d.H, d.N};
-    TLC_TRY(encode_4d(&prm.tmA[0], d.dout, adims, 32, 1, BM, CU_TENSOR_MAP_SWIZZLE_128B));
-    TLC_TRY(encode_4d(&prm.tmB[0], d.x, bdims, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    if (x3) {
-        TLC_TRY(encode_4d(&prm.tmA[1], d.dout_lo, adims, 32, 1, BM, CU_TENSOR_MAP_SWIZZLE_128B));
-        TLC_TRY(encode_4d(&prm.tmB[1], d.x_lo, bdims, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    }
-    prm.C = d.out;
-    prm.c_rs = Ncols;
-    prm.nb = 2;
-    prm.bsz[0] = d.N;
-    prm.bsz[1] = d.groups;
-    prm.bsz[2] = 1;
-    prm.cbs[0] = (int64_t)d.groups * M * Ncols;
-    prm.cbs[1] = M * Ncols;
-    prm.M = (int)M;
-    prm.N = (int)Ncols;
-    prm.K = (int)K;
-    prm.k_blocks = (int)(K / BK);
-    prm.chunk_kb = x3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
-    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
-    prm.a_mn = 0;
-    prm.b_mn = 1;
-    prm.vec_c = (al16(d.out) && (Ncols & 3) == 0) ? 1 : 0;
-    prm.timeout_ns = 2000000000ull;
-    prm.conv = 2;
-    prm.cv_kW = d.kW;
-    prm.cv_pad_h = d.pad;
-    prm.cv_pad_w = d.pad;
-    prm.cv_c_group = d.c_group;
-    prm.cv_wblocks = (int)wblocks;
-    prm.cv_cpad = d.cpad;
-    prm.cv_o_group = (int)M;
-    if (!x3 && prm.vec_c) {
-        const int64_t bsz[kMaxBatchDims] = {d.N, d.groups, 1};
-        const int64_t cbs[kMaxBatchDims] = {prm.cbs[0], prm.cbs[1], 0};
-        if (encode_tiled(&prm.tmC, d.out, Ncols, M, Ncols, bsz, cbs, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ==
-            TLC_OK)
-            prm.tma_c = 1;
-        else
-            clear_error();
-    }
-    prm.err = error_word();
-    if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
-    prm.m_tiles = (int)((M + BM - 1) / BM);
-    const int un = x3 ? 128 : 256;
-    prm.n_tiles = (int)((Ncols + un - 1) / un);
-    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * d.N * d.groups;
-    prm.tile_n = un;
-    prm.mma_n = un;
-    if (x3) return launch_variant<1, 128, true>(prm, s);
-    return launch_variant<1, 256, false>(prm, s);
-}
-
-// Implicit-GEMM convolution on the tensor cores (see TcParams::conv): A (the
+// Implicit-GEMM convolution on the tensor cores (the CONV variants, TcParams): A (the
 // repacked weights) and C as in gemm_tc; B read through encode_conv_b.
 int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
     if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
@@ -1363,7 +1244,6 @@ int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
         else
             clear_error();
     }
-    prm.conv = 1;
     prm.cv_cblocks = c.cblocks;
     prm.cv_kW = c.kW;
     prm.cv_pad_h = c.pad_h;
@@ -1373,9 +1253,7 @@ int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
     prm.cv_c_group = c.c_group;
     if (c.row_bias) {
         prm.bias = c.row_bias;
-        prm.bias_row = 1;
-        prm.bias_bs[0] = c.row_bias_bs[0];
-        prm.bias_bs[1] = c.row_bias_bs[1];
+        prm.bias_group = c.row_bias_group;
     }
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
@@ -1383,9 +1261,8 @@ int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
     prm.n_tiles = (int)((g.N + tile - 1) / tile);
     prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
     prm.tile_n = tile;
-    prm.mma_n = tile;
-    if (x3) return launch_variant<1, 128, true>(prm, s);  // tile <= 128 (checked above)
-    return tile > 128 ? launch_variant<1, 256, false>(prm, s) : launch_variant<1, 128, false>(prm, s);
+    if (x3) return launch_variant<1, 128, true, true>(prm, s);  // tile <= 128 (checked above)
+    return tile > 128 ? launch_variant<1, 256, false, true>(prm, s) : launch_variant<1, 128, false, true>(prm, s);
 }
 
 int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
