@@ -583,7 +583,7 @@ struct Events {
 };
 
 constexpr int64_t kPipeMinBytes = 64ll << 20;  // smaller problems: one upload, one download
-constexpr int kPipeChunks = 8;
+constexpr int kPipeChunks = 32;
 
 // Host-buffer matmul with the transfers pipelined against the GEMMs: the
 // output is cut into chunks, along the flattened batch when every operand is
