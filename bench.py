@@ -553,9 +553,10 @@ class FlashWork(Work):
 class ConvWork(Work):
     """conv2d forward + Conv2dBackward, a ResNet-style 3x3 layer: x [32,64,56,56],
     W [64,64,3,3], b [64], stride 1, padding 1 (x, dO ~ N(0,1), W ~ N(0,0.05^2),
-    b ~ N(0,1), seed 6): im2col, the batched GEMMs in the mode, col2im and the
-    bias gradient.  FLOPs: 2*N*C_out*H*W*C_in*k*k forward, twice that backward
-    (dW and dX)."""
+    b ~ N(0,1), seed 6).  TF32 / 3xTF32: the forward, the input gradient and the
+    weight gradient as implicit GEMMs over TMA boxes of NHWC copies; exact:
+    im2col, the batched GEMMs, col2im.  FLOPs: 2*N*C_out*H*W*C_in*k*k forward,
+    twice that backward (dW and dX)."""
     name = "conv"
 
     def __init__(self, world, rank, device):

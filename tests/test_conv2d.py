@@ -105,12 +105,17 @@ def test_device_conv2d_exact(case):
                                   (2, 64, 16, 16, 64, 3, 1, 1, 1), (2, 32, 20, 24, 48, 3, 1, 1, 1),
                                   (1, 4, 10, 8, 8, 3, 1, 1, 1), (2, 64, 12, 16, 64, 3, 1, 1, 2),
                                   (1, 16, 12, 16, 16, 5, 1, 2, 1), (2, 32, 8, 8, 16, 1, 1, 0, 1),
-                                  (2, 64, 56, 56, 64, 3, 1, 1, 1)]
+                                  (2, 64, 56, 56, 64, 3, 1, 1, 1),
+                                  # weight gradient as the split-K implicit GEMM with two
+                                  # 128-row tiles of output channels
+                                  (1, 8, 10, 16, 160, 3, 1, 1, 1)]
                          # float64 torch needs the padded input at least as large as the kernel
                          + [c for c in CASES if min(c[2], c[3]) + 2 * c[7] >= c[5]])
 def test_device_conv2d_tensor_cores(mode, tol, case):
-    """The tensor-core modes (im2col + batched tcgen05 GEMMs, col2im) against
-    float64 over the reference's shapes, strides, paddings and groups."""
+    """The tensor-core modes against float64 over the reference's shapes,
+    strides, paddings and groups: at stride 1 with output rows a multiple of 8
+    wide the implicit GEMMs (forward, input gradient, weight gradient),
+    otherwise im2col + batched tcgen05 GEMMs and col2im."""
     torch = pytest.importorskip("torch")
     import tlcuda
     x, w, b, s, p, g = case_data(case, 13)

@@ -172,6 +172,32 @@ struct ConvTma {
 };
 int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s);
 
+// The weight gradient of a stride-1 convolution as an implicit GEMM with a
+// split K (TF32 / 3xTF32):
+//   part[s][g][o][tap * c_pad + c] = sum over the output rows of split s, in
+//   32-pixel blocks, of dO[n, g*C_out_g + o, oh, ow] * x[n, oh - pad_h + kh,
+//   ow - pad_w + kw, g*C_in_g + c]   (tap = kh * kW + kw, c < c_pad)
+// with dO read as NCHW and x as its NHWC copy; a TMA box brings 32 pixels of
+// one dO row (the K-major A) and, per 32 channels of one tap, the matching 32
+// shifted input pixels (the MN-major B), zero-filled outside the image.
+// k-steps past the row's end are not issued, so no product of a pixel outside
+// the output enters a sum.  Split s covers output rows (n, oh) s * rows ..
+// s * rows + rows - 1 (flattened n * H_out + oh; rows past the last read as
+// zeros).
+struct ConvDw {
+    const float* go;     // dO, dense NCHW [N, C_out, H_out, W_out]
+    const float* x;      // the input as dense NHWC [N, H, W, C]
+    const float* x_lo;   // 3xTF32: the lo plane of x (NHWC), else NULL
+    int N, C, H, W;
+    int C_out, H_out, W_out;
+    int kH, kW, pad_h, pad_w;
+    int groups, C_in_g, C_out_g;
+};
+// Splits (and rows per split) for this problem on this device; the partial
+// buffer holds splits * groups * C_out_g * kH * kW * round32(C_in_g) floats.
+int conv_dw_splits(const ConvDw& c, int mode, int* splits, int* rows);
+int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode, cudaStream_t s);
+
 // out[o,n] = sum over d ascending of in[o,d,n], from init[o,n] (NULL: from 0.0f).
 int launch_sum_dim(const float* in, float* out, int64_t outer, int64_t D, int64_t inner,
                    cudaStream_t s, const float* init = nullptr);

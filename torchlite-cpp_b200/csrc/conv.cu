@@ -522,6 +522,27 @@ __global__ void conv_weights_kernel(const float* __restrict__ w, float* __restri
 
 int64_t round32(int64_t v) { return (v + 31) / 32 * 32; }
 
+// grad_w[g * C_out_g + o][c][kh][kw] = sum over splits s = 0, 1, .. in order
+// of part[s][g][o][(kh * kW + kw) * c_pad + c] (the implicit weight-gradient
+// GEMM's partial sums).  One thread per output; a warp's threads read
+// consecutive channels of one tap.
+__global__ void conv_dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ gw, ConvShape s,
+                                      int64_t splits, int64_t c_pad) {
+    const int64_t taps = s.kH * s.kW, cols = taps * c_pad;
+    const int64_t n = s.C_out * taps * s.C_in_g;
+    const int64_t split_stride = s.C_out * cols;  // groups * C_out_g * cols
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        // i = (row, tap, c), c fastest; row = g * C_out_g + o
+        const int64_t c = i % s.C_in_g, rt = i / s.C_in_g;
+        const int64_t tap = rt % taps, row = rt / taps;
+        const float* src = part + row * cols + tap * c_pad + c;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < splits; ++k) acc = __fadd_rn(acc, src[k * split_stride]);
+        gw[(row * s.C_in_g + c) * taps + tap] = acc;
+    }
+}
+
 // Output rows per implicit-GEMM tile for an output row width: the most rows
 // whose pixels fit `cap` columns as a multiple of 16 (0: none fits).
 int conv_tile_rows(int64_t width, int cap) {
@@ -540,6 +561,15 @@ bool conv_tma_ok(const ConvShape& s, int64_t C, int64_t C_g, int64_t H, int64_t 
            (s.groups == 1 || C_g % 32 == 0) && H < lim && W < lim && C < lim && s.N < lim &&
            s.N <= 65535 && conv_tile_rows(out_w, mode == TLC_MODE_3XTF32 ? 128 : 256) > 0 &&
            s.kH * s.kW * round32(C_g) < lim;
+}
+
+// Whether the weight gradient runs as the implicit split-K GEMM in this mode.
+bool conv_dw_ok(const ConvShape& s, const float* go, int mode) {
+    const int64_t lim = int64_t(1) << 30;
+    return mode != TLC_MODE_EXACT && s.stride == 1 && s.W_out >= 8 && s.W_out % 8 == 0 &&
+           s.C_in % 4 == 0 && (s.groups == 1 || s.C_in_g % 32 == 0) && (reinterpret_cast<uintptr_t>(go) & 15) == 0 && s.H < lim &&
+           s.W < lim && s.C_in < lim && s.C_out < lim && s.N * s.H_out < lim &&
+           s.kH * s.kW * round32(s.C_in_g) < lim;
 }
 
 // NHWC copy (and 3xTF32 lo plane) of a dense NCHW tensor [N, C, H*W].
@@ -695,6 +725,39 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
         // G[n, g] (C_out_g x patch) = dO[n, g] (C_out_g x HW) . col[n, g]^T, then sum over n
         if (s.N * s.C_out * s.patch == 0) {
             if (s.C_out * s.patch) TLC_TRY(launch_fill_zero(d_w->data, s.C_out * s.patch, st));
+        } else if (s.HW > 0 && conv_dw_ok(s, go, mode)) {
+            // implicit split-K GEMM over TMA boxes of dO and of an NHWC copy
+            // of the input (no column buffer), then the ordered sum of the splits
+            Buf xh(st), xl(st);
+            TLC_TRY(to_nhwc(in, s.N, s.C_in, s.H * s.W, mode, xh, xl, st));
+            ConvDw c{};
+            c.go = go;
+            c.x = xh.f();
+            c.x_lo = mode == TLC_MODE_3XTF32 ? xl.f() : nullptr;
+            c.N = (int)s.N;
+            c.C = (int)s.C_in;
+            c.H = (int)s.H;
+            c.W = (int)s.W;
+            c.C_out = (int)s.C_out;
+            c.H_out = (int)s.H_out;
+            c.W_out = (int)s.W_out;
+            c.kH = (int)s.kH;
+            c.kW = (int)s.kW;
+            c.pad_h = (int)s.padding;
+            c.pad_w = (int)s.padding;
+            c.groups = (int)s.groups;
+            c.C_in_g = (int)s.C_in_g;
+            c.C_out_g = (int)s.C_out_g;
+            int splits = 0, rows = 0;
+            TLC_TRY(conv_dw_splits(c, mode, &splits, &rows));
+            const int64_t c_pad = round32(s.C_in_g);
+            TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(splits * s.C_out * s.kH * s.kW * c_pad), st));
+            TLC_TRY(gemm_tc_conv_dw(c, splits, rows, prod.f(), mode, st));
+            const int64_t n = s.C_out * s.patch;
+            conv_dw_reduce_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(
+                prod.f(), d_w->data, s, splits, c_pad);
+            count_launch();
+            TLC_TRY(check_launch("conv weight-gradient sum"));
         } else {
             TLC_TRY(make_col(in, s, col, st));
             TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(s.N * s.C_out * s.patch), st));

@@ -125,6 +125,16 @@ struct TcParams {
     int tile_n;
     int cv_cblocks, cv_kW, cv_pad_h, cv_pad_w, cv_rows, cv_W_out, cv_c_group;
     int64_t bias_group;
+    // The weight-gradient variant (CONV = 2, ConvDw): A is dO through a map
+    // {W_out, H_out, C_out, N, 1} (box: 32 pixels of one row x 128 channels),
+    // B the NHWC input through {C, W, H, N, 1} (box: 32 channels x 32 pixels,
+    // MN-major); batch dim 0 is the split, 1 the group.  k-block kb is pixels
+    // 32 * (kb % dw_wblocks) .. + 31 of output row split * dw_rows +
+    // kb / dw_wblocks (flattened n * dw_H + oh); a row's last block issues
+    // dw_last_ksteps k-steps of 8.  Column chunk j (32 wide) is channels
+    // 32 * (j % cv_cblocks) .. of tap j / cv_cblocks; chunks of taps >=
+    // dw_taps load channel dw_c_oob (past the tensor: zeros).
+    int dw_rows, dw_wblocks, dw_last_ksteps, dw_H, dw_taps, dw_c_oob;
 };
 
 // The GEMM epilogue on one output value: one IEEE fp32 operation per step,
@@ -244,7 +254,7 @@ struct Cfg {
 
 // X3: the epilogue adds the chunk partials of each output element into
 // registers in fp32 round-to-nearest and stores after the last chunk.
-template <int CG, int UN, bool X3, bool CONV = false>
+template <int CG, int UN, bool X3, int CONV = 0>
 __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcParams p) {
     using S = Cfg<CG, UN, X3>;
@@ -338,9 +348,12 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     const uint32_t fb = CG == 2 ? mapa(smem_u32(&full[stage]), 0)
                                                 : smem_u32(&full[stage]);
                     if (leader && elect_one()) {
-                        if constexpr (CONV)
+                        if constexpr (CONV == 1)
                             mbar_expect_tx(&full[stage], nsub * (X3 ? 2 : 1) *
                                                              (S::A_BYTES + p.cv_rows * p.cv_W_out * 128));
+                        else if constexpr (CONV == 2)
+                            mbar_expect_tx(&full[stage], nsub * (X3 ? 2 : 1) *
+                                                             (S::A_BYTES + p.tile_n * BK * 4));
                         else
                             mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
                     }
@@ -352,6 +365,27 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
                                           h * S::PAIR_BYTES;
                             uint8_t* sb = sa + S::A_BYTES;
+                            if constexpr (CONV == 2) {
+                                // 32 pixels of one output row: dO's row (A), and per
+                                // 32-channel chunk of the tile's taps the input pixels
+                                // that tap reads for them (B, MN-major)
+                                const int kbi = k0 / BK;
+                                const int rr = kbi / p.dw_wblocks, wb = kbi - rr * p.dw_wblocks;
+                                const int R = bi[0] * p.dw_rows + rr;
+                                const int img = R / p.dw_H, oh = R - img * p.dw_H;
+                                const int w0 = wb * BK;
+                                tma_load_5d<CG>(sa, &p.tmA[h], fb, w0, oh, bi[1] * p.M + m0, img, 0);
+                                const int j0 = (tc.n * p.tile_n) >> 5;
+                                for (int c = 0; c < (p.tile_n >> 5); ++c) {
+                                    const int j = j0 + c;
+                                    const int tap = j / p.cv_cblocks, cb = j - tap * p.cv_cblocks;
+                                    const int kh = tap / p.cv_kW, kw = tap - kh * p.cv_kW;
+                                    const int ch = tap < p.dw_taps ? bi[1] * p.cv_c_group + cb * 32 : p.dw_c_oob;
+                                    tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[h], fb, ch,
+                                                    w0 + kw - p.cv_pad_w, oh + kh - p.cv_pad_h, img, 0);
+                                }
+                                continue;
+                            }
                             if (p.a_chunked) {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, 0, k0, m0 >> 5, a0, a1);
                             } else if (p.a_mn) {
@@ -362,7 +396,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             } else {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, k0, m0, a0, a1, a2);
                             }
-                            if constexpr (CONV) {
+                            if constexpr (CONV == 1) {
                                 // cv_rows boxes, one per output row of the tile
                                 const int kb = k0 / BK;
                                 const int tap = kb / p.cv_cblocks, cb = kb - tap * p.cv_cblocks;
@@ -467,25 +501,30 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                         const uint32_t soff =
                             (uint32_t)(stage * S::STAGE_BYTES + s * S::KB_BYTES) >> 4;
                         const uint64_t ad = a_desc0 + soff, bd = b_desc0 + soff;
+                        // CONV = 2: a row's last pixel block may hold fewer than
+                        // BK pixels; its k-steps past the row are not issued
+                        int ksteps = BK / UMMA_K;
+                        if constexpr (CONV == 2)
+                            if (it.kb() % p.dw_wblocks == p.dw_wblocks - 1) ksteps = p.dw_last_ksteps;
                         if constexpr (X3) {
                             // lo(A).hi(B) + hi(A).lo(B) + hi(A).hi(B): small terms first
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                if (elect_one())
+                                if (j < ksteps && elect_one())
                                     umma_tf32<CG>(d, ad + lo_off + j * a_step, bd + j * b_step, idesc,
                                                   (!first || j > 0) ? 1u : 0u);
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                if (elect_one())
+                                if (j < ksteps && elect_one())
                                     umma_tf32<CG>(d, ad + j * a_step, bd + lo_off + j * b_step, idesc, 1u);
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                if (elect_one())
+                                if (j < ksteps && elect_one())
                                     umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc, 1u);
                         } else {
 #pragma unroll
                             for (int j = 0; j < BK / UMMA_K; ++j)
-                                if (elect_one())
+                                if (j < ksteps && elect_one())
                                     umma_tf32<CG>(d, ad + j * a_step, bd + j * b_step, idesc,
                                                   (!first || j > 0) ? 1u : 0u);
                         }
@@ -551,7 +590,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
             const int nlim = CONV ? min(p.N, tc.n * tn + tn) : p.N;
             float* crow = p.C + oc + row * p.c_rs;
             float rb = 0.0f;  // CONV: this row's bias
-            if constexpr (CONV) {
+            if constexpr (CONV == 1) {
                 if (p.bias && row < p.M) rb = p.bias[bi[1] * p.bias_group + row];
             }
             float sum[X3 ? S::EPI_COLS : 1];
@@ -853,7 +892,7 @@ int* error_word() {
     return st == TLC_OK ? words[dev] : nullptr;
 }
 
-template <int CG, int UN, bool X3, bool CONV = false>
+template <int CG, int UN, bool X3, int CONV = 0>
 int launch_variant(const TcParams& prm, cudaStream_t s) {
     using S = Cfg<CG, UN, X3>;
     auto kernel = tc_gemm_kernel<CG, UN, X3, CONV>;
@@ -1261,8 +1300,160 @@ int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
     prm.n_tiles = (int)((g.N + tile - 1) / tile);
     prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch();
     prm.tile_n = tile;
-    if (x3) return launch_variant<1, 128, true, true>(prm, s);  // tile <= 128 (checked above)
-    return tile > 128 ? launch_variant<1, 256, false, true>(prm, s) : launch_variant<1, 128, false, true>(prm, s);
+    if (x3) return launch_variant<1, 128, true, 1>(prm, s);  // tile <= 128 (checked above)
+    return tile > 128 ? launch_variant<1, 256, false, 1>(prm, s) : launch_variant<1, 128, false, 1>(prm, s);
+}
+
+namespace {
+// A dense 4-D tensor {d0 (contiguous), d1, d2, d3} as a 5-D map (last dim 1)
+// with the given box and swizzle; reads outside the tensor fill zeros.
+int encode_dense4(CUtensorMap* map, const float* base, const int64_t (&dims)[4], const uint32_t (&box)[4],
+                  CUtensorMapSwizzle swizzle, const char* what) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    cuuint64_t d[5] = {(cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2], (cuuint64_t)dims[3], 1};
+    cuuint64_t st[4];
+    st[0] = (cuuint64_t)dims[0] * 4;
+    st[1] = st[0] * (cuuint64_t)dims[1];
+    st[2] = st[1] * (cuuint64_t)dims[2];
+    st[3] = st[2] * (cuuint64_t)dims[3];
+    cuuint32_t b[5] = {box[0], box[1], box[2], box[3], 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), d, st, b, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TLC_ERR_UNSUPPORTED, std::string("cuTensorMapEncodeTiled (") + what + ") failed (" +
+                                                  std::to_string((int)r) + ")");
+    return TLC_OK;
+}
+
+// Column tile of the weight-gradient GEMM: the multiple of 32 up to `cap`
+// that pads N least (ties: the wider).
+int dw_tile(int64_t N, int cap) {
+    int best = 32;
+    int64_t best_cols = -1;
+    for (int t = cap; t >= 32; t -= 32) {
+        const int64_t cols = (N + t - 1) / t * t;
+        if (best_cols < 0 || cols < best_cols) {
+            best = t;
+            best_cols = cols;
+        }
+    }
+    return best;
+}
+
+int64_t dw_cols(const ConvDw& c) { return (int64_t)c.kH * c.kW * ((c.C_in_g + 31) / 32 * 32); }
+}  // namespace
+
+// As many splits of the output rows as leave each SM one tile.
+int conv_dw_splits(const ConvDw& c, int mode, int* splits, int* rows) {
+    const int64_t N = dw_cols(c);
+    const int tile = dw_tile(N, mode == TLC_MODE_3XTF32 ? 128 : 256);
+    const int64_t per_split = (int64_t)((c.C_out_g + BM - 1) / BM) * ((N + tile - 1) / tile) * c.groups;
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t total = (int64_t)c.N * c.H_out;
+    if (total < 1 || per_split < 1) return set_error(TLC_ERR_UNSUPPORTED, "implicit-GEMM weight gradient: empty");
+    int64_t sp = std::min<int64_t>(std::max<int64_t>(1, sms / per_split), total);
+    const int64_t r = (total + sp - 1) / sp;
+    sp = (total + r - 1) / r;
+    if (r > INT32_MAX || sp > 65535) return set_error(TLC_ERR_UNSUPPORTED, "implicit-GEMM weight gradient: too many rows");
+    *splits = (int)sp;
+    *rows = (int)r;
+    return TLC_OK;
+}
+
+// The weight-gradient variant (CONV = 2) of the tensor-core GEMM; part is
+// [splits][groups][C_out_g][kH * kW * round32(C_in_g)].
+int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode, cudaStream_t s) {
+    const bool x3 = mode == TLC_MODE_3XTF32;
+    const int64_t c_pad = (c.C_in_g + 31) / 32 * 32, taps = (int64_t)c.kH * c.kW, N = dw_cols(c);
+    const int tile = dw_tile(N, x3 ? 128 : 256);
+    const int wblocks = (c.W_out + BK - 1) / BK;
+    const int last = c.W_out - (wblocks - 1) * BK;
+    const int64_t kb = (int64_t)rows * wblocks;
+    if (splits < 1 || rows < 1 || c.W_out < 8 || c.W_out % 8 || c.C % 4 || c.C_out_g < 1 ||
+        (c.groups > 1 && c.C_in_g % 32) || (x3 && !c.x_lo) || N > INT32_MAX || kb * BK > INT32_MAX ||
+        (int64_t)splits * rows < (int64_t)c.N * c.H_out || (int64_t)splits * rows > INT32_MAX ||
+        (int64_t)c.groups * c.C_out_g != c.C_out || (int64_t)c.groups * c.C_in_g != c.C ||
+        !al16(c.go) || !al16(c.x) || (x3 && !al16(c.x_lo)) || !al16(part))
+        return set_error(TLC_ERR_UNSUPPORTED, "implicit-GEMM weight gradient: unsupported shape");
+    TcScratch sc(s);
+    TcParams prm;
+    memset(&prm, 0, sizeof(prm));
+    const int64_t adims[4] = {c.W_out, c.H_out, c.C_out, c.N};
+    const uint32_t abox[4] = {BK, 1, BM, 1};  // 32 pixels of one row, 128 output channels
+    const int64_t bdims[4] = {c.C, c.W, c.H, c.N};
+    const uint32_t bbox[4] = {32, BK, 1, 1};  // 32 channels, 32 pixels: an MN-major chunk
+    const float* a_hi = c.go;
+    const float* a_lo = nullptr;
+    if (x3) {
+        const bool lo_only = tf32_reads_truncated(s);
+        const int64_t n = (int64_t)c.N * c.C_out * c.H_out * c.W_out;
+        TLC_TRY(scratch_alloc(&sc.p[0], sizeof(float) * (size_t)n * (lo_only ? 1 : 2), s));
+        float* plane = static_cast<float*>(sc.p[0]);
+        if (lo_only) {
+            split_lo_kernel<<<grid_split(n), 256, 0, s>>>(c.go, plane, n);
+            a_lo = plane;
+        } else {
+            split_tf32_kernel<<<grid_split(n), 256, 0, s>>>(c.go, plane, plane + n, n);
+            a_hi = plane;
+            a_lo = plane + n;
+        }
+        count_launch();
+        TLC_TRY(check_launch("split_tf32"));
+        TLC_TRY(encode_dense4(&prm.tmA[1], a_lo, adims, abox, CU_TENSOR_MAP_SWIZZLE_128B, "conv dO"));
+        TLC_TRY(encode_dense4(&prm.tmB[1], c.x_lo, bdims, bbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                              "conv input"));
+    }
+    TLC_TRY(encode_dense4(&prm.tmA[0], a_hi, adims, abox, CU_TENSOR_MAP_SWIZZLE_128B, "conv dO"));
+    TLC_TRY(encode_dense4(&prm.tmB[0], c.x, bdims, bbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, "conv input"));
+    prm.C = part;
+    prm.c_rs = N;
+    prm.nb = 2;
+    int64_t bsz[kMaxBatchDims] = {splits, c.groups, 1};
+    int64_t cbs[kMaxBatchDims] = {(int64_t)c.groups * c.C_out_g * N, (int64_t)c.C_out_g * N, 0};
+    for (int i = 0; i < kMaxBatchDims; ++i) {
+        prm.bsz[i] = (int)bsz[i];
+        prm.cbs[i] = cbs[i];
+    }
+    prm.M = c.C_out_g;
+    prm.N = (int)N;
+    prm.K = (int)(kb * BK);
+    prm.k_blocks = (int)kb;
+    prm.chunk_kb = x3 ? std::min(prm.k_blocks, 8) : prm.k_blocks;
+    prm.num_chunks = (prm.k_blocks + prm.chunk_kb - 1) / prm.chunk_kb;
+    prm.a_mn = 0;
+    prm.b_mn = 1;
+    prm.vec_c = 1;  // part is 16-byte aligned and N, the strides are multiples of 32
+    prm.timeout_ns = 2000000000ull;
+    if (!x3) {
+        if (encode_tiled(&prm.tmC, part, N, c.C_out_g, N, bsz, cbs, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) == TLC_OK)
+            prm.tma_c = 1;
+        else
+            clear_error();
+    }
+    prm.tile_n = tile;
+    prm.cv_cblocks = (int)(c_pad / 32);
+    prm.cv_kW = c.kW;
+    prm.cv_pad_h = c.pad_h;
+    prm.cv_pad_w = c.pad_w;
+    prm.cv_c_group = c.C_in_g;
+    prm.dw_rows = rows;
+    prm.dw_wblocks = wblocks;
+    prm.dw_last_ksteps = last / UMMA_K;
+    prm.dw_H = c.H_out;
+    prm.dw_taps = (int)taps;
+    prm.dw_c_oob = (c.C + 31) / 32 * 32;
+    prm.err = error_word();
+    if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
+    prm.m_tiles = (c.C_out_g + BM - 1) / BM;
+    prm.n_tiles = (int)((N + tile - 1) / tile);
+    prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * splits * c.groups;
+    if (x3) return launch_variant<1, 128, true, 2>(prm, s);  // tile <= 128
+    return tile > 128 ? launch_variant<1, 256, false, 2>(prm, s) : launch_variant<1, 128, false, 2>(prm, s);
 }
 
 int bounded_wait_selftest(uint64_t timeout_ns, cudaStream_t s) {
