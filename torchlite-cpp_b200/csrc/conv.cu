@@ -538,7 +538,15 @@ __global__ void conv_dw_reduce_kernel(const float* __restrict__ part, float* __r
         const int64_t tap = rt % taps, row = rt / taps;
         const float* src = part + row * cols + tap * c_pad + c;
         float acc = 0.0f;
-        for (int64_t k = 0; k < splits; ++k) acc = __fadd_rn(acc, src[k * split_stride]);
+        int64_t k = 0;
+        for (; k + 8 <= splits; k += 8) {  // eight loads in flight, then their adds in order
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (k + u) * split_stride);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+        }
+        for (; k < splits; ++k) acc = __fadd_rn(acc, __ldg(src + k * split_stride));
         gw[(row * s.C_in_g + c) * taps + tap] = acc;
     }
 }

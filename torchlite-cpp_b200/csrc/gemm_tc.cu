@@ -135,6 +135,14 @@ struct TcParams {
     // 32 * (j % cv_cblocks) .. of tap j / cv_cblocks; chunks of taps >=
     // dw_taps load channel dw_c_oob (past the tensor: zeros).
     int dw_rows, dw_wblocks, dw_last_ksteps, dw_H, dw_taps, dw_c_oob;
+    // dw_chunked: B's map is {32, W, C / 32, H, N} (channel chunks as a dim)
+    // and one box {32, 32, cv_cblocks} brings all chunks of a tap; tile_n is
+    // then a multiple of 32 * cv_cblocks and dw_c_oob is a chunk coordinate.
+    int dw_chunked;
+    // CONV variants: rows of the A box (64 when M <= 64: the MMA's rows 64..127
+    // then read stale shared memory, whose products land in accumulator rows
+    // that are never stored)
+    int a_box_rows;
 };
 
 // The GEMM epilogue on one output value: one IEEE fp32 operation per step,
@@ -333,6 +341,31 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                           b2 = p.b_bc[2] ? bi[2] : 0;
                 const int m0 = tc.m * S::TILE_M + (int)rank * BM;       // this CTA's A rows
                 const int n0 = tc.n * UN + (int)rank * S::B_COLS;       // this CTA's B columns
+                // CONV = 2: the tile's B boxes (fixed over its k-blocks) and the
+                // position of its first k-block, advanced without divisions
+                int dw_img = 0, dw_oh = 0, dw_wb = 0, nbox = 0;
+                int bx_c[8], bx_w[8], bx_h[8];
+                if constexpr (CONV == 2) {
+                    const int R0 = bi[0] * p.dw_rows;
+                    dw_img = R0 / p.dw_H;
+                    dw_oh = R0 - dw_img * p.dw_H;
+                    const int per_box = p.dw_chunked ? p.cv_cblocks : 1;  // 32-channel chunks per box
+                    nbox = p.tile_n / (32 * per_box);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        bx_c[c] = p.dw_c_oob;
+                        bx_w[c] = bx_h[c] = 0;
+                        if (c < nbox) {
+                            const int jc = (tc.n * p.tile_n >> 5) + c * per_box;  // first chunk of box c
+                            const int tap = jc / p.cv_cblocks, cb = jc - tap * p.cv_cblocks;
+                            const int kh = tap / p.cv_kW, kw = tap - kh * p.cv_kW;
+                            if (tap < p.dw_taps)
+                                bx_c[c] = p.dw_chunked ? bi[1] * p.cv_cblocks : bi[1] * p.cv_c_group + cb * 32;
+                            bx_w[c] = kw - p.cv_pad_w;
+                            bx_h[c] = kh - p.cv_pad_h;
+                        }
+                    }
+                }
                 KbIter it;
                 it.start(p);
                 for (int kb = 0; kb < p.k_blocks;) {
@@ -350,42 +383,54 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     if (leader && elect_one()) {
                         if constexpr (CONV == 1)
                             mbar_expect_tx(&full[stage], nsub * (X3 ? 2 : 1) *
-                                                             (S::A_BYTES + p.cv_rows * p.cv_W_out * 128));
+                                                             (p.a_box_rows * BK * 4 + p.cv_rows * p.cv_W_out * 128));
                         else if constexpr (CONV == 2)
                             mbar_expect_tx(&full[stage], nsub * (X3 ? 2 : 1) *
-                                                             (S::A_BYTES + p.tile_n * BK * 4));
+                                                             (p.a_box_rows * BK * 4 + p.tile_n * BK * 4));
                         else
                             mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
                     }
                     for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
                         const int k0 = it.kb() * BK;
+                        if constexpr (CONV == 2) {
+                            // 32 pixels of one output row: dO's row (A), and per
+                            // tap of the tile the input pixels it reads for them
+                            // (B, MN-major)
+                            if (elect_one()) {
+                                const int w0 = dw_wb * BK;
+#pragma unroll
+                                for (int h = 0; h < (X3 ? 2 : 1); ++h) {
+                                    uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
+                                                  h * S::PAIR_BYTES;
+                                    uint8_t* sb = sa + S::A_BYTES;
+                                    tma_load_5d<CG>(sa, &p.tmA[h], fb, w0, dw_oh, bi[1] * p.M + m0, dw_img, 0);
+#pragma unroll
+                                    for (int c = 0; c < 8; ++c) {
+                                        if (c >= nbox) break;
+                                        if (p.dw_chunked)
+                                            tma_load_5d<CG>(sb + c * p.cv_cblocks * a_chunk_bytes, &p.tmB[h], fb, 0,
+                                                            w0 + bx_w[c], bx_c[c], dw_oh + bx_h[c], dw_img);
+                                        else
+                                            tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[h], fb, bx_c[c],
+                                                            w0 + bx_w[c], dw_oh + bx_h[c], dw_img, 0);
+                                    }
+                                }
+                            }
+                            if (++dw_wb == p.dw_wblocks) {
+                                dw_wb = 0;
+                                if (++dw_oh == p.dw_H) {
+                                    dw_oh = 0;
+                                    ++dw_img;
+                                }
+                            }
+                            continue;
+                        }
                         if (!elect_one()) continue;
 #pragma unroll
                         for (int h = 0; h < (X3 ? 2 : 1); ++h) {  // X3: hi, then lo planes
                             uint8_t* sa = smem + stage * S::STAGE_BYTES + j * S::KB_BYTES +
                                           h * S::PAIR_BYTES;
                             uint8_t* sb = sa + S::A_BYTES;
-                            if constexpr (CONV == 2) {
-                                // 32 pixels of one output row: dO's row (A), and per
-                                // 32-channel chunk of the tile's taps the input pixels
-                                // that tap reads for them (B, MN-major)
-                                const int kbi = k0 / BK;
-                                const int rr = kbi / p.dw_wblocks, wb = kbi - rr * p.dw_wblocks;
-                                const int R = bi[0] * p.dw_rows + rr;
-                                const int img = R / p.dw_H, oh = R - img * p.dw_H;
-                                const int w0 = wb * BK;
-                                tma_load_5d<CG>(sa, &p.tmA[h], fb, w0, oh, bi[1] * p.M + m0, img, 0);
-                                const int j0 = (tc.n * p.tile_n) >> 5;
-                                for (int c = 0; c < (p.tile_n >> 5); ++c) {
-                                    const int j = j0 + c;
-                                    const int tap = j / p.cv_cblocks, cb = j - tap * p.cv_cblocks;
-                                    const int kh = tap / p.cv_kW, kw = tap - kh * p.cv_kW;
-                                    const int ch = tap < p.dw_taps ? bi[1] * p.cv_c_group + cb * 32 : p.dw_c_oob;
-                                    tma_load_5d<CG>(sb + c * a_chunk_bytes, &p.tmB[h], fb, ch,
-                                                    w0 + kw - p.cv_pad_w, oh + kh - p.cv_pad_h, img, 0);
-                                }
-                                continue;
-                            }
                             if (p.a_chunked) {
                                 tma_load_5d<CG>(sa, &p.tmA[h], fb, 0, k0, m0 >> 5, a0, a1);
                             } else if (p.a_mn) {
@@ -403,9 +448,8 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                                 const int kh = tap / p.cv_kW, kw = tap - kh * p.cv_kW;
                                 const int c = bi[1] * p.cv_c_group + cb * 32;
                                 const int oh0 = tc.n * p.cv_rows;
-                                for (int r = 0; r < p.cv_rows; ++r)
-                                    tma_load_5d<CG>(sb + r * p.cv_W_out * 128, &p.tmB[h], fb, c,
-                                                    kw - p.cv_pad_w, oh0 + r - p.cv_pad_h + kh, bi[0], 0);
+                                tma_load_5d<CG>(sb, &p.tmB[h], fb, c, kw - p.cv_pad_w, oh0 - p.cv_pad_h + kh,
+                                                bi[0], 0);
                             } else if (p.b_chunked) {
                                 tma_load_5d<CG>(sb, &p.tmB[h], fb, 0, k0, n0 >> 5, b0, b1);
                             } else if (p.b_mn) {
@@ -1209,15 +1253,16 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
 
 namespace {
 // The NHWC tensor a convolution's B tiles come from, as {C, W, H, N, 1} with
-// boxes {32 channels, W_out columns, 1, 1, 1}, 128-byte swizzle (each box is
-// W_out K-major rows of 32 channels); reads outside the tensor fill zeros.
+// boxes {32 channels, W_out columns, rows, 1, 1}, 128-byte swizzle (each box
+// is the tile's rows * W_out K-major pixel rows of 32 channels, output row by
+// output row); reads outside the tensor fill zeros.
 int encode_conv_b(CUtensorMap* map, const float* x, const ConvTma& c) {
     auto fn = encode_fn();
     if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
     cuuint64_t dims[5] = {(cuuint64_t)c.C, (cuuint64_t)c.W, (cuuint64_t)c.H, (cuuint64_t)c.N, 1};
     cuuint64_t strides[4] = {(cuuint64_t)c.C * 4, (cuuint64_t)c.W * c.C * 4,
                              (cuuint64_t)c.H * c.W * c.C * 4, (cuuint64_t)c.N * c.H * c.W * c.C * 4};
-    cuuint32_t box[5] = {32, (cuuint32_t)c.W_out, 1, 1, 1};
+    cuuint32_t box[5] = {32, (cuuint32_t)c.W_out, (cuuint32_t)c.rows, 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(x), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1251,6 +1296,8 @@ int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
     if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb)) TLC_TRY(repack(A, g.nb, sc, 0, s));
     TcParams prm;
     memset(&prm, 0, sizeof(prm));
+    prm.a_box_rows = (!a_mn && g.M <= 64) ? 64 : BM;
+    A.box_outer = a_mn ? A.box_outer : (uint32_t)prm.a_box_rows;
     if (x3) {
         const bool lo_only = tf32_reads_truncated(s);
         const int64_t n = span_elems(A.inner, A.outer, A.outer_stride, A.bsz, A.bstride, g.nb);
@@ -1328,6 +1375,26 @@ int encode_dense4(CUtensorMap* map, const float* base, const int64_t (&dims)[4],
     return TLC_OK;
 }
 
+// The NHWC input as {32, W, C / 32, H, N}: 32 channels (contiguous), the
+// pixels of a row, the 32-channel chunks (128 bytes apart), rows, images;
+// box {32, 32, C_in_g / 32, 1, 1} is one tap's chunks for 32 pixels, chunk
+// after chunk (the MN-major B layout, 4 KB per chunk).  C % 32 == 0.
+int encode_dw_chunked(CUtensorMap* map, const float* x, const ConvDw& c) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(TLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    cuuint64_t d[5] = {32, (cuuint64_t)c.W, (cuuint64_t)c.C / 32, (cuuint64_t)c.H, (cuuint64_t)c.N};
+    cuuint64_t st[4] = {(cuuint64_t)c.C * 4, 128, (cuuint64_t)c.W * c.C * 4, (cuuint64_t)c.H * c.W * c.C * 4};
+    cuuint32_t b[5] = {32, BK, (cuuint32_t)(c.C_in_g / 32), 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(x), d, st, b, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TLC_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled (conv input chunks) failed (" +
+                                                  std::to_string((int)r) + ")");
+    return TLC_OK;
+}
+
 // Column tile of the weight-gradient GEMM: the multiple of 32 up to `cap`
 // that pads N least (ties: the wider).
 int dw_tile(int64_t N, int cap) {
@@ -1344,12 +1411,33 @@ int dw_tile(int64_t N, int cap) {
 }
 
 int64_t dw_cols(const ConvDw& c) { return (int64_t)c.kH * c.kW * ((c.C_in_g + 31) / 32 * 32); }
+
+// Whether B boxes take all channel chunks of a tap at once: channels a
+// multiple of 32, and a tap's chunks fit the column tile.
+bool dw_chunked(const ConvDw& c, int cap) { return c.C % 32 == 0 && c.C_in_g % 32 == 0 && c.C_in_g <= cap; }
+
+// The weight-gradient GEMM's column tile: whole taps when chunked.
+int dw_tile_for(const ConvDw& c, int cap) {
+    const int64_t N = dw_cols(c);
+    if (!dw_chunked(c, cap)) return dw_tile(N, cap);
+    const int per_tap = c.C_in_g;  // a multiple of 32
+    int best = per_tap;
+    int64_t best_cols = -1;
+    for (int t = cap / per_tap * per_tap; t >= per_tap; t -= per_tap) {
+        const int64_t cols = (N + t - 1) / t * t;
+        if (best_cols < 0 || cols < best_cols) {
+            best = t;
+            best_cols = cols;
+        }
+    }
+    return best;
+}
 }  // namespace
 
 // As many splits of the output rows as leave each SM one tile.
 int conv_dw_splits(const ConvDw& c, int mode, int* splits, int* rows) {
     const int64_t N = dw_cols(c);
-    const int tile = dw_tile(N, mode == TLC_MODE_3XTF32 ? 128 : 256);
+    const int tile = dw_tile_for(c, mode == TLC_MODE_3XTF32 ? 128 : 256);
     const int64_t per_split = (int64_t)((c.C_out_g + BM - 1) / BM) * ((N + tile - 1) / tile) * c.groups;
     int sms = 148, dev = 0;
     cudaGetDevice(&dev);
@@ -1370,7 +1458,9 @@ int conv_dw_splits(const ConvDw& c, int mode, int* splits, int* rows) {
 int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode, cudaStream_t s) {
     const bool x3 = mode == TLC_MODE_3XTF32;
     const int64_t c_pad = (c.C_in_g + 31) / 32 * 32, taps = (int64_t)c.kH * c.kW, N = dw_cols(c);
-    const int tile = dw_tile(N, x3 ? 128 : 256);
+    const int cap = x3 ? 128 : 256;
+    const int tile = dw_tile_for(c, cap);
+    const bool chunked = dw_chunked(c, cap);
     const int wblocks = (c.W_out + BK - 1) / BK;
     const int last = c.W_out - (wblocks - 1) * BK;
     const int64_t kb = (int64_t)rows * wblocks;
@@ -1383,8 +1473,9 @@ int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode
     TcScratch sc(s);
     TcParams prm;
     memset(&prm, 0, sizeof(prm));
+    prm.a_box_rows = c.C_out_g <= 64 ? 64 : BM;
     const int64_t adims[4] = {c.W_out, c.H_out, c.C_out, c.N};
-    const uint32_t abox[4] = {BK, 1, BM, 1};  // 32 pixels of one row, 128 output channels
+    const uint32_t abox[4] = {BK, 1, (uint32_t)prm.a_box_rows, 1};  // 32 pixels of one row, the channels
     const int64_t bdims[4] = {c.C, c.W, c.H, c.N};
     const uint32_t bbox[4] = {32, BK, 1, 1};  // 32 channels, 32 pixels: an MN-major chunk
     const float* a_hi = c.go;
@@ -1405,11 +1496,17 @@ int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode
         count_launch();
         TLC_TRY(check_launch("split_tf32"));
         TLC_TRY(encode_dense4(&prm.tmA[1], a_lo, adims, abox, CU_TENSOR_MAP_SWIZZLE_128B, "conv dO"));
-        TLC_TRY(encode_dense4(&prm.tmB[1], c.x_lo, bdims, bbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-                              "conv input"));
+        if (chunked)
+            TLC_TRY(encode_dw_chunked(&prm.tmB[1], c.x_lo, c));
+        else
+            TLC_TRY(encode_dense4(&prm.tmB[1], c.x_lo, bdims, bbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                                  "conv input"));
     }
     TLC_TRY(encode_dense4(&prm.tmA[0], a_hi, adims, abox, CU_TENSOR_MAP_SWIZZLE_128B, "conv dO"));
-    TLC_TRY(encode_dense4(&prm.tmB[0], c.x, bdims, bbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, "conv input"));
+    if (chunked)
+        TLC_TRY(encode_dw_chunked(&prm.tmB[0], c.x, c));
+    else
+        TLC_TRY(encode_dense4(&prm.tmB[0], c.x, bdims, bbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, "conv input"));
     prm.C = part;
     prm.c_rs = N;
     prm.nb = 2;
@@ -1446,7 +1543,8 @@ int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode
     prm.dw_last_ksteps = last / UMMA_K;
     prm.dw_H = c.H_out;
     prm.dw_taps = (int)taps;
-    prm.dw_c_oob = (c.C + 31) / 32 * 32;
+    prm.dw_chunked = chunked ? 1 : 0;
+    prm.dw_c_oob = chunked ? c.C / 32 : (c.C + 31) / 32 * 32;  // a chunk / channel past the tensor
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
     prm.m_tiles = (c.C_out_g + BM - 1) / BM;
