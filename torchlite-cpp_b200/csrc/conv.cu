@@ -327,6 +327,28 @@ __global__ void __launch_bounds__(256) bias_part_kernel(const float* __restrict_
     }
 }
 
+// The same partial sums, one warp per (channel, image) pair with float4 loads
+// (HW a multiple of 4, dO 16-byte aligned): each lane adds its float4s in
+// order, then a fixed shuffle tree.
+__global__ void __launch_bounds__(256) bias_part_v4_kernel(const float* __restrict__ go, float* __restrict__ part,
+                                                           ConvShape s) {
+    const int64_t pairs = s.C_out * s.N;
+    const int lane = threadIdx.x & 31;
+    const int64_t n4 = s.HW / 4;
+    for (int64_t i = blockIdx.x * (int64_t)8 + (threadIdx.x >> 5); i < pairs; i += (int64_t)gridDim.x * 8) {
+        const int64_t c = i / s.N, n = i - c * s.N;
+        const float4* src = reinterpret_cast<const float4*>(go + (n * s.C_out + c) * s.HW);
+        float acc = 0.0f;
+        for (int64_t k = lane; k < n4; k += 32) {
+            const float4 v = __ldg(src + k);
+            acc += (v.x + v.y) + (v.z + v.w);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) part[i] = acc;
+    }
+}
+
 int resolve(int mode, int& out) {
     if (mode == TLC_MODE_DEFAULT) mode = tlc_default_mode();
     if (mode != TLC_MODE_EXACT && mode != TLC_MODE_TF32 && mode != TLC_MODE_3XTF32)
@@ -494,60 +516,133 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restri
     }
 }
 
+// The same transpose in tiles of 32 channels x 128 pixels with float4 loads
+// and stores (C and P multiples of 4, 16-byte aligned tensors).  In a warp the
+// loads cover 4 channel rows x 128 bytes and the stores 4 pixels x 32
+// channels; the shared tile's odd pitch keeps both phases free of bank
+// conflicts.
+constexpr int kT4C = 32, kT4P = 128;
+__global__ void __launch_bounds__(256) nchw_to_nhwc_v4_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                              float* __restrict__ lo, int64_t C, int64_t P,
+                                                              int split) {
+    __shared__ float t[kT4C][kT4P + 1];
+    const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * kT4P, c0 = (int64_t)blockIdx.y * kT4C;
+    const float* xi = x + n * C * P;
+    const int tid = threadIdx.x, lane = tid & 31;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int wl = i * 8 + (tid >> 5);  // 0 .. 31
+        const int row = (wl & 7) * 4 + (lane >> 3), col4 = (wl >> 3) * 8 + (lane & 7);
+        const int64_t c = c0 + row, p = p0 + 4 * col4;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c < C && p < P) v = __ldg(reinterpret_cast<const float4*>(xi + c * P + p));
+        t[row][4 * col4] = v.x;
+        t[row][4 * col4 + 1] = v.y;
+        t[row][4 * col4 + 2] = v.z;
+        t[row][4 * col4 + 3] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int pp = (tid >> 3) + 32 * i, c4 = tid & 7;
+        const int64_t p = p0 + pp, c = c0 + 4 * c4;
+        if (p >= P || c >= C) continue;
+        float v[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            v[e] = t[4 * c4 + e][pp];
+            l[e] = 0.0f;
+            if (split == 1) {
+                l[e] = __fsub_rn(v[e], __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
+            } else if (split == 2) {
+                uint32_t h;
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v[e]));
+                l[e] = __fsub_rn(v[e], __uint_as_float(h));
+                v[e] = __uint_as_float(h);
+            }
+        }
+        const int64_t o = (n * P + p) * C + c;
+        *reinterpret_cast<float4*>(y + o) = make_float4(v[0], v[1], v[2], v[3]);
+        if (split) *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+}
+
 // Weights as the implicit GEMM's A: dst[r][kh][kw][q], q < q_pad (zero past
 // the real count).  flip 0 (forward): r = output channel o, q = input
 // channel c of o's group: W[o][q][kh][kw].  flip 1 (input gradient): r =
 // input channel g * C_in_g + c, q = output channel o of group g:
 // W[g * C_out_g + q][c][kH - 1 - kh][kW - 1 - kw].
+template <typename I>
 __global__ void conv_weights_kernel(const float* __restrict__ w, float* __restrict__ dst, ConvShape s,
-                                    int flip, int64_t q_pad) {
-    const int64_t khw = s.kH * s.kW;
-    const int64_t rows = flip ? s.C_in : s.C_out, per_row = khw * q_pad;
-    const int64_t n = rows * per_row;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / per_row, rem = i - r * per_row;
-        const int64_t tap = rem / q_pad, q = rem - tap * q_pad;
-        const int64_t kh = tap / s.kW, kw = tap - kh * s.kW;
+                                    int flip, int64_t q_pad_) {
+    const I kH = (I)s.kH, kW = (I)s.kW, khw = kH * kW, q_pad = (I)q_pad_;
+    const I C_in_g = (I)s.C_in_g, C_out_g = (I)s.C_out_g;
+    const I rows = (I)(flip ? s.C_in : s.C_out), per_row = khw * q_pad;
+    const I n = rows * per_row;
+    for (I i = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x; i < n; i += (I)gridDim.x * (I)blockDim.x) {
+        const I r = i / per_row, rem = i - r * per_row;
+        const I tap = rem / q_pad, q = rem - tap * q_pad;
+        const I kh = tap / kW, kw = tap - kh * kW;
         float v = 0.0f;
         if (!flip) {
-            if (q < s.C_in_g) v = w[(r * s.C_in_g + q) * khw + kh * s.kW + kw];
-        } else if (q < s.C_out_g) {
-            const int64_t g = r / s.C_in_g, c = r - g * s.C_in_g;
-            v = w[((g * s.C_out_g + q) * s.C_in_g + c) * khw + (s.kH - 1 - kh) * s.kW + (s.kW - 1 - kw)];
+            if (q < C_in_g) v = w[((int64_t)r * C_in_g + q) * khw + kh * kW + kw];
+        } else if (q < C_out_g) {
+            const I g = r / C_in_g, c = r - g * C_in_g;
+            v = w[(((int64_t)g * C_out_g + q) * C_in_g + c) * khw + (kH - 1 - kh) * kW + (kW - 1 - kw)];
         }
         dst[i] = v;
     }
 }
 
+// conv_weights_kernel over nwp elements, in 32-bit index math when that fits
+void launch_conv_weights(const float* w, float* dst, const ConvShape& s, int flip, int64_t q_pad, int64_t nwp,
+                         cudaStream_t st) {
+    const unsigned grid = (unsigned)std::min<int64_t>((nwp + 255) / 256, 148 * 16);
+    if (nwp < (int64_t(1) << 31) - 148 * 16 * 256)
+        conv_weights_kernel<int><<<grid, 256, 0, st>>>(w, dst, s, flip, q_pad);
+    else
+        conv_weights_kernel<int64_t><<<grid, 256, 0, st>>>(w, dst, s, flip, q_pad);
+}
+
 int64_t round32(int64_t v) { return (v + 31) / 32 * 32; }
 
-// grad_w[g * C_out_g + o][c][kh][kw] = sum over splits s = 0, 1, .. in order
-// of part[s][g][o][(kh * kW + kw) * c_pad + c] (the implicit weight-gradient
-// GEMM's partial sums).  One thread per output; a warp's threads read
-// consecutive channels of one tap.
-__global__ void conv_dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ gw, ConvShape s,
-                                      int64_t splits, int64_t c_pad) {
+// grad_w[g * C_out_g + o][c][kh][kw] = the sum over splits of
+// part[s][g][o][(kh * kW + kw) * c_pad + c] (the implicit weight-gradient
+// GEMM's partial sums).  A block takes 32 outputs (lane = output, consecutive
+// channels of one tap); its 8 warps each add one contiguous eighth of the
+// splits in order, and warp 0 adds the eight partial sums in order: the same
+// sums on every run.
+__global__ void __launch_bounds__(256) conv_dw_reduce_kernel(const float* __restrict__ part,
+                                                             float* __restrict__ gw, ConvShape s,
+                                                             int64_t splits, int64_t c_pad) {
+    __shared__ float red[8][32];
     const int64_t taps = s.kH * s.kW, cols = taps * c_pad;
     const int64_t n = s.C_out * taps * s.C_in_g;
     const int64_t split_stride = s.C_out * cols;  // groups * C_out_g * cols
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        // i = (row, tap, c), c fastest; row = g * C_out_g + o
-        const int64_t c = i % s.C_in_g, rt = i / s.C_in_g;
-        const int64_t tap = rt % taps, row = rt / taps;
-        const float* src = part + row * cols + tap * c_pad + c;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t per = (splits + 7) / 8, k0 = warp * per, k1 = min(splits, k0 + per);
+    for (int64_t base = blockIdx.x * (int64_t)32; base < n; base += (int64_t)gridDim.x * 32) {
+        const int64_t i = base + lane;
         float acc = 0.0f;
-        int64_t k = 0;
-        for (; k + 8 <= splits; k += 8) {  // eight loads in flight, then their adds in order
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (k + u) * split_stride);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+        int64_t row = 0, tap = 0, c = 0;
+        if (i < n) {
+            // i = (row, tap, c), c fastest; row = g * C_out_g + o
+            c = i % s.C_in_g;
+            const int64_t rt = i / s.C_in_g;
+            tap = rt % taps;
+            row = rt / taps;
+            const float* src = part + row * cols + tap * c_pad + c;
+            for (int64_t k = k0; k < k1; ++k) acc = __fadd_rn(acc, __ldg(src + k * split_stride));
         }
-        for (; k < splits; ++k) acc = __fadd_rn(acc, __ldg(src + k * split_stride));
-        gw[(row * s.C_in_g + c) * taps + tap] = acc;
+        red[warp][lane] = acc;
+        __syncthreads();
+        if (warp == 0 && i < n) {
+            float t = red[0][lane];
+#pragma unroll
+            for (int w = 1; w < 8; ++w) t = __fadd_rn(t, red[w][lane]);
+            gw[(row * s.C_in_g + c) * taps + tap] = t;
+        }
+        __syncthreads();
     }
 }
 
@@ -589,8 +684,14 @@ int to_nhwc(const float* x, int64_t N, int64_t C, int64_t P, int mode, Buf& hi, 
     TLC_TRY(scratch_alloc(&hi.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
     if (split) TLC_TRY(scratch_alloc(&lo.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
     if (!n) return TLC_OK;
-    dim3 grid((unsigned)((P + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);
-    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi.f(), split ? lo.f() : nullptr, C, P, split);
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (C % 4 == 0 && P % 4 == 0 && a16(x) && a16(hi.p) && (!split || a16(lo.p))) {
+        dim3 grid((unsigned)((P + kT4P - 1) / kT4P), (unsigned)((C + kT4C - 1) / kT4C), (unsigned)N);
+        nchw_to_nhwc_v4_kernel<<<grid, 256, 0, st>>>(x, hi.f(), split ? lo.f() : nullptr, C, P, split);
+    } else {
+        dim3 grid((unsigned)((P + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);
+        nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi.f(), split ? lo.f() : nullptr, C, P, split);
+    }
     count_launch();
     return check_launch("nchw_to_nhwc");
 }
@@ -664,8 +765,7 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
         const int64_t q_pad = round32(s.C_in_g), nwp = s.C_out * s.kH * s.kW * q_pad;
         Buf wp(st);
         TLC_TRY(scratch_alloc(&wp.p, sizeof(float) * (size_t)nwp, st));
-        conv_weights_kernel<<<(unsigned)std::min<int64_t>((nwp + 255) / 256, 148 * 16), 256, 0, st>>>(
-            w, wp.f(), s, 0, q_pad);
+        launch_conv_weights(w, wp.f(), s, 0, q_pad, nwp, st);
         count_launch();
         TLC_TRY(check_launch("conv weights"));
         const float* bd = nullptr;
@@ -762,7 +862,7 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(splits * s.C_out * s.kH * s.kW * c_pad), st));
             TLC_TRY(gemm_tc_conv_dw(c, splits, rows, prod.f(), mode, st));
             const int64_t n = s.C_out * s.patch;
-            conv_dw_reduce_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(
+            conv_dw_reduce_kernel<<<(unsigned)std::min<int64_t>((n + 31) / 32, 148 * 32), 256, 0, st>>>(
                 prod.f(), d_w->data, s, splits, c_pad);
             count_launch();
             TLC_TRY(check_launch("conv weight-gradient sum"));
@@ -805,8 +905,7 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
         // weights, padding k - 1 - p, as the same implicit GEMM
         const int64_t q_pad = round32(s.C_out_g), nwp = s.C_in * s.kH * s.kW * q_pad;
         TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)nwp, st));
-        conv_weights_kernel<<<(unsigned)std::min<int64_t>((nwp + 255) / 256, 148 * 16), 256, 0, st>>>(
-            w, gcol.f(), s, 1, q_pad);
+        launch_conv_weights(w, gcol.f(), s, 1, q_pad, nwp, st);
         count_launch();
         TLC_TRY(check_launch("conv weights"));
         TLC_TRY(conv_tma_gemm(go, s.C_out, s.C_out_g, s.H_out, s.W_out, gcol.f(), s.C_in_g, s.H, s.W,
@@ -863,8 +962,12 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             TLC_TRY(check_launch("conv bias grad"));
         } else {
             TLC_TRY(scratch_alloc(&bpart.p, sizeof(float) * (size_t)(s.C_out * s.N), st));
-            bias_part_kernel<<<(unsigned)std::min<int64_t>(s.C_out * s.N, 148 * 16), 256, 0, st>>>(
-                go, bpart.f(), s);
+            if (s.HW % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15) == 0)
+                bias_part_v4_kernel<<<(unsigned)std::min<int64_t>((s.C_out * s.N + 7) / 8, 148 * 32), 256, 0,
+                                      st>>>(go, bpart.f(), s);
+            else
+                bias_part_kernel<<<(unsigned)std::min<int64_t>(s.C_out * s.N, 148 * 16), 256, 0, st>>>(
+                    go, bpart.f(), s);
             count_launch();
             TLC_TRY(check_launch("conv bias grad"));
             TLC_TRY(launch_sum_dim(bpart.f(), d_b->data, s.C_out, s.N, 1, st));
