@@ -253,10 +253,11 @@ int tlc_sum_to(const tlc_tensor* x, tlc_tensor* out, void* stream);
  * [C_out, C_in/groups, kH, kW], bias [C_out] or NULL, out [N, C_out, H_out,
  * W_out] with H_out = (H + 2*padding - kH) / stride + 1 (C++ division).
  * TLC_MODE_TF32 / _3XTF32 at stride 1 (output rows a multiple of 8 wide,
- * channels a multiple of 4): the forward product and the input gradient are
- * implicit GEMMs on the tensor cores reading TMA boxes of an NHWC copy (no
- * column buffer); otherwise, and for the weight gradient, im2col for all
- * images and groups at once, then one batched GEMM per product in `mode`;
+ * channels a multiple of 4): the forward product, the input gradient and the
+ * weight gradient (split over output rows, the splits then summed in a fixed
+ * order) are implicit GEMMs on the tensor cores reading TMA boxes of NHWC
+ * copies (no column buffer); otherwise im2col for all images and groups at
+ * once, then one batched GEMM per product in `mode`;
  * exact mode is bit-identical to the reference, backward
  * included (its per-image += order for the weight gradient, col2im's order
  * for the input gradient, its (n, oh, ow) order for the bias gradient).
