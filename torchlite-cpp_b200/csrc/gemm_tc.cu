@@ -1395,42 +1395,26 @@ int encode_dw_chunked(CUtensorMap* map, const float* x, const ConvDw& c) {
     return TLC_OK;
 }
 
-// Column tile of the weight-gradient GEMM: the multiple of 32 up to `cap`
-// that pads N least (ties: the wider).
-int dw_tile(int64_t N, int cap) {
-    int best = 32;
-    int64_t best_cols = -1;
-    for (int t = cap; t >= 32; t -= 32) {
-        const int64_t cols = (N + t - 1) / t * t;
-        if (best_cols < 0 || cols < best_cols) {
-            best = t;
-            best_cols = cols;
-        }
-    }
-    return best;
-}
-
 int64_t dw_cols(const ConvDw& c) { return (int64_t)c.kH * c.kW * ((c.C_in_g + 31) / 32 * 32); }
 
 // Whether B boxes take all channel chunks of a tap at once: channels a
 // multiple of 32, and a tap's chunks fit the column tile.
 bool dw_chunked(const ConvDw& c, int cap) { return c.C % 32 == 0 && c.C_in_g % 32 == 0 && c.C_in_g <= cap; }
 
-// The weight-gradient GEMM's column tile: whole taps when chunked.
+// The weight-gradient GEMM's column tile: whole taps when chunked; the
+// widest tile whose padded columns stay within 1/8 of the fewest (a narrow
+// MMA costs about as much to issue as a wide one).
 int dw_tile_for(const ConvDw& c, int cap) {
     const int64_t N = dw_cols(c);
-    if (!dw_chunked(c, cap)) return dw_tile(N, cap);
-    const int per_tap = c.C_in_g;  // a multiple of 32
-    int best = per_tap;
-    int64_t best_cols = -1;
-    for (int t = cap / per_tap * per_tap; t >= per_tap; t -= per_tap) {
+    const int step = dw_chunked(c, cap) ? c.C_in_g : 32;  // C_in_g is then a multiple of 32
+    int64_t fewest = -1;
+    for (int t = cap / step * step; t >= step; t -= step) {
         const int64_t cols = (N + t - 1) / t * t;
-        if (best_cols < 0 || cols < best_cols) {
-            best = t;
-            best_cols = cols;
-        }
+        if (fewest < 0 || cols < fewest) fewest = cols;
     }
-    return best;
+    for (int t = cap / step * step; t >= step; t -= step)
+        if ((N + t - 1) / t * t * 8 <= fewest * 9) return t;
+    return step;
 }
 }  // namespace
 
