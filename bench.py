@@ -300,9 +300,10 @@ def time_graph(fn, steps, world):
     return max_over_ranks(ms, world)
 
 
-# Workloads of a few microseconds per step, where the Python binding's host
-# work per call is longer than the kernels: also timed as CUDA-graph replays.
-GRAPH_WORKLOADS = ("square512", "broadcast")
+# Workloads whose per-step kernels are short enough that the Python binding's
+# host work per call rivals them (a few microseconds per GEMM; the conv step's
+# dozen launches in ~0.2 ms): also timed as CUDA-graph replays.
+GRAPH_WORKLOADS = ("square512", "broadcast", "conv")
 
 
 # ---- workloads -------------------------------------------------------------------------

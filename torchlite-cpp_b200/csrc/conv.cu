@@ -163,6 +163,47 @@ __global__ void __launch_bounds__(256) im2col_plane_kernel(const float* __restri
     }
 }
 
+// The column buffer transposed: colT[n, g, hw, p] = col[n, g, p, hw], so that
+// the weight gradient's GEMM dO_ng . col_ng^T reads it as a row-major [HW,
+// patch] B (the exact kernel's packed-FMA layout) instead of a K-major one.
+// One block per output row (n, g, oh): the kH input rows it reads, for the
+// group's channels and the columns its W_out outputs reach, are staged in
+// shared memory (zero outside the image); then each thread writes its patch
+// entries p = tid, tid + blockDim.x, .. of every output pixel of the row
+// (coalesced along p).
+__global__ void __launch_bounds__(256) im2col_t_kernel(const float* __restrict__ in, float* __restrict__ colT,
+                                                       ConvShape s, int span) {
+    extern __shared__ float xs[];  // [C_in_g][kH][span]
+    const int kH = (int)s.kH, kW = (int)s.kW, stride = (int)s.stride, pad = (int)s.padding;
+    const int H = (int)s.H, W = (int)s.W, W_out = (int)s.W_out, H_out = (int)s.H_out;
+    const int Cg = (int)s.C_in_g, patch = (int)s.patch;
+    const int64_t lines = s.N * s.groups * s.H_out;
+    for (int64_t line = blockIdx.x; line < lines; line += gridDim.x) {
+        const int oh = (int)(line % H_out);
+        const int64_t ng = line / H_out;
+        const int g = (int)(ng % s.groups);
+        const int64_t n = ng / s.groups;
+        __syncthreads();  // the previous line's readers are done
+        const int staged = Cg * kH * span;
+        for (int i = threadIdx.x; i < staged; i += blockDim.x) {
+            const int col = i % span, ck = i / span;
+            const int kh = ck % kH, c = ck / kH;
+            const int ih = oh * stride - pad + kh, iw = col - pad;
+            float v = 0.0f;
+            if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                v = in[((n * s.C_in + (int64_t)g * Cg + c) * H + ih) * (int64_t)W + iw];
+            xs[i] = v;
+        }
+        __syncthreads();
+        float* dst = colT + (ng * s.HW + (int64_t)oh * W_out) * patch;
+        for (int p = threadIdx.x; p < patch; p += blockDim.x) {
+            const int kw = p % kW, ck = p / kW;  // ck = c * kH + kh
+            const float* src = xs + ck * span + kw;
+            for (int ow = 0; ow < W_out; ++ow) dst[(int64_t)ow * patch + p] = src[ow * stride];
+        }
+    }
+}
+
 // grad_in[n, c, ih, iw] = 0 + sum over (kh, kw) ascending of grad_col at the
 // (oh, ow) that read this pixel.  One block per (n, c) plane.
 __global__ void col2im_kernel(const float* __restrict__ gcol, float* __restrict__ gin, ConvShape s) {
@@ -470,6 +511,26 @@ int make_col(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
             im2col_kernel<<<(unsigned)std::min<int64_t>(lines, 148 * 64), 256, 0, st>>>(in, col.f(), s);
         count_launch();
         TLC_TRY(check_launch("im2col"));
+    }
+    return TLC_OK;
+}
+
+// colT [N, groups, HW, patch] of a dense input, or TLC_ERR_UNSUPPORTED when a
+// block's staged rows would not fit in shared memory.
+constexpr int kIm2colTMax = 96 * 1024;
+int make_col_t(const float* in, const ConvShape& s, Buf& col, cudaStream_t st) {
+    const int64_t span = (s.W_out - 1) * s.stride + s.kW;
+    const int64_t bytes = s.C_in_g * s.kH * span * (int64_t)sizeof(float);
+    if (s.W_out < 1 || bytes > kIm2colTMax || s.patch > INT32_MAX / 2) return TLC_ERR_UNSUPPORTED;
+    const int64_t n = s.N * s.groups * s.patch * s.HW;
+    TLC_TRY(scratch_alloc(&col.p, sizeof(float) * (size_t)std::max<int64_t>(n, 1), st));
+    if (n) {
+        static DeviceOnce once;
+        TLC_TRY(smem_limit_once(once, im2col_t_kernel, kIm2colTMax));
+        im2col_t_kernel<<<(unsigned)std::min<int64_t>(s.N * s.groups * s.H_out, 148 * 16), 256, (size_t)bytes,
+                          st>>>(in, col.f(), s, (int)span);
+        count_launch();
+        TLC_TRY(check_launch("im2col (transposed)"));
     }
     return TLC_OK;
 }
@@ -809,6 +870,55 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
     return TLC_OK;
 }
 
+// A second stream of the calling host thread on the current device (made on
+// first use), for work that overlaps the caller's stream.
+cudaStream_t side_stream() {
+    thread_local cudaStream_t streams[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        streams[dev] = nullptr;
+    }
+    return streams[dev];
+}
+
+// Work forked from `main` onto a side stream; the destructor makes `main`
+// wait for it (so anything enqueued on `main` afterwards, frees of the
+// buffers it reads included, comes after it), on every return path.
+struct Fork {
+    cudaStream_t main, side = nullptr;
+    cudaEvent_t join = nullptr;
+    explicit Fork(cudaStream_t m) : main(m) {}
+    // the side stream, ordered after everything enqueued on `main` so far;
+    // nullptr when none can be had (the caller then uses `main`)
+    cudaStream_t begin() {
+        cudaStream_t s = side_stream();
+        cudaEvent_t f = nullptr;
+        if (!s || cudaEventCreateWithFlags(&f, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        if (cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventRecord(f, main) != cudaSuccess || cudaStreamWaitEvent(s, f, 0) != cudaSuccess) {
+            cudaGetLastError();
+            cudaEventDestroy(f);
+            if (join) cudaEventDestroy(join);
+            join = nullptr;
+            return nullptr;
+        }
+        cudaEventDestroy(f);
+        side = s;
+        return s;
+    }
+    ~Fork() {
+        if (!side) return;
+        cudaEventRecord(join, side);
+        cudaStreamWaitEvent(main, join, 0);
+        cudaEventDestroy(join);
+    }
+};
+
 int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w_t, int64_t stride,
              int64_t padding, int64_t groups, tlc_tensor* d_in, tlc_tensor* d_w, tlc_tensor* d_b, int mode,
              cudaStream_t st) {
@@ -829,6 +939,21 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
     TLC_TRY(dense_copy(go_t, bgo, &go, st));
     TLC_TRY(dense_copy(in_t, bin, &in, st));
     TLC_TRY(dense_copy(w_t, bw, &w, st));
+    // Exact mode's bias gradient is one dependent chain of N * HW adds per
+    // channel (the reference's order): it runs on a side stream from the
+    // start, beside the weight- and input-gradient GEMMs, which leave SMs
+    // free for its one block per channel (the join is in `fork`'s destructor,
+    // before the buffers above are freed).
+    Fork fork(st);
+    bool bias_done = false;
+    if (d_b && s.C_out && (mode == TLC_MODE_EXACT || s.N * s.HW == 0)) {
+        cudaStream_t bs = fork.begin();
+        if (!bs) bs = st;
+        bias_grad_kernel<<<(unsigned)std::min<int64_t>(s.C_out, 148 * 16), BIAS_THREADS, 0, bs>>>(go, d_b->data, s);
+        count_launch();
+        TLC_TRY(check_launch("conv bias grad"));
+        bias_done = true;
+    }
     if (d_w) {
         // G[n, g] (C_out_g x patch) = dO[n, g] (C_out_g x HW) . col[n, g]^T, then sum over n
         if (s.N * s.C_out * s.patch == 0) {
@@ -867,7 +992,16 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             count_launch();
             TLC_TRY(check_launch("conv weight-gradient sum"));
         } else {
-            TLC_TRY(make_col(in, s, col, st));
+            // exact mode: the column buffer transposed ([HW, patch] per image and
+            // group), so the FFMA GEMM reads an N-major B (its packed path);
+            // otherwise, or when its rows do not fit, col read transposed in place
+            bool transposed = false;
+            if (mode == TLC_MODE_EXACT) {
+                const int r = make_col_t(in, s, col, st);
+                if (r != TLC_OK && r != TLC_ERR_UNSUPPORTED) return r;
+                transposed = r == TLC_OK;
+            }
+            if (!transposed) TLC_TRY(make_col(in, s, col, st));
             TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(s.N * s.C_out * s.patch), st));
             Gemm g{};
             g.M = s.C_out_g;
@@ -876,9 +1010,9 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             g.A = go;
             g.a_rs = s.HW;
             g.a_cs = 1;
-            g.B = col.f();  // col[n, g] read as its transpose: (hw, p) at p*HW + hw
-            g.b_rs = 1;
-            g.b_cs = s.HW;
+            g.B = col.f();  // (hw, p) at hw*patch + p (colT), or at p*HW + hw (col)
+            g.b_rs = transposed ? s.patch : 1;
+            g.b_cs = transposed ? 1 : s.HW;
             g.C = prod.f();
             g.c_rs = s.patch;
             g.nb = 2;
@@ -954,24 +1088,18 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             TLC_TRY(check_launch("col2im"));
         }
     }
-    if (d_b && s.C_out) {
-        if (mode == TLC_MODE_EXACT || s.N * s.HW == 0) {
-            // the reference's order: one ascending chain per channel
-            bias_grad_kernel<<<(unsigned)std::min<int64_t>(s.C_out, 148 * 16), BIAS_THREADS, 0, st>>>(go, d_b->data, s);
-            count_launch();
-            TLC_TRY(check_launch("conv bias grad"));
-        } else {
-            TLC_TRY(scratch_alloc(&bpart.p, sizeof(float) * (size_t)(s.C_out * s.N), st));
-            if (s.HW % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15) == 0)
-                bias_part_v4_kernel<<<(unsigned)std::min<int64_t>((s.C_out * s.N + 7) / 8, 148 * 32), 256, 0,
-                                      st>>>(go, bpart.f(), s);
-            else
-                bias_part_kernel<<<(unsigned)std::min<int64_t>(s.C_out * s.N, 148 * 16), 256, 0, st>>>(
-                    go, bpart.f(), s);
-            count_launch();
-            TLC_TRY(check_launch("conv bias grad"));
-            TLC_TRY(launch_sum_dim(bpart.f(), d_b->data, s.C_out, s.N, 1, st));
-        }
+    if (d_b && s.C_out && !bias_done) {
+        // TF32 / 3xTF32: a tree, which those modes' tolerance allows
+        TLC_TRY(scratch_alloc(&bpart.p, sizeof(float) * (size_t)(s.C_out * s.N), st));
+        if (s.HW % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15) == 0)
+            bias_part_v4_kernel<<<(unsigned)std::min<int64_t>((s.C_out * s.N + 7) / 8, 148 * 32), 256, 0, st>>>(
+                go, bpart.f(), s);
+        else
+            bias_part_kernel<<<(unsigned)std::min<int64_t>(s.C_out * s.N, 148 * 16), 256, 0, st>>>(go, bpart.f(),
+                                                                                                   s);
+        count_launch();
+        TLC_TRY(check_launch("conv bias grad"));
+        TLC_TRY(launch_sum_dim(bpart.f(), d_b->data, s.C_out, s.N, 1, st));
     }
     return TLC_OK;
 }
