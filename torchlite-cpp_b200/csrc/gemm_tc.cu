@@ -139,6 +139,10 @@ struct TcParams {
     // and one box {32, 32, cv_cblocks} brings all chunks of a tap; tile_n is
     // then a multiple of 32 * cv_cblocks and dw_c_oob is a chunk coordinate.
     int dw_chunked;
+    // Split K (small problems): batch dim split_dim (the last, >= 0) is the
+    // split; its tiles start kps k-blocks apart (the last split's k-blocks past
+    // K read zeros) and write partial products; -1: none.
+    int split_dim, kps;
     // CONV variants: rows of the A box (64 when M <= 64: the MMA's rows 64..127
     // then read stale shared memory, whose products land in accumulator rows
     // that are never stored)
@@ -366,6 +370,9 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                         }
                     }
                 }
+                // split K (constant indices keep bi in registers)
+                const int kb_base = p.split_dim < 0 ? 0
+                                    : (p.split_dim == 0 ? bi[0] : p.split_dim == 1 ? bi[1] : bi[2]) * p.kps;
                 KbIter it;
                 it.start(p);
                 for (int kb = 0; kb < p.k_blocks;) {
@@ -391,7 +398,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                             mbar_expect_tx(&full[stage], nsub * S::KB_BYTES * CG);
                     }
                     for (int j = 0; j < nsub; ++j, ++kb, it.next(p)) {
-                        const int k0 = it.kb() * BK;
+                        const int k0 = (kb_base + it.kb()) * BK;
                         if constexpr (CONV == 2) {
                             // 32 pixels of one output row: dO's row (A), and per
                             // tap of the tile the input pixels it reads for them
@@ -1184,6 +1191,36 @@ int tc_error_word(int** p) {
     return *p ? TLC_OK : set_error(TLC_ERR_CUDA, "no device error word");
 }
 
+// Splits of K for a 3xTF32 problem whose single-CTA tiles would occupy at
+// most a quarter of the SMs (three MMAs per k-step on one issuing thread make
+// a few tiles with a long K a long serial chain): as many as fill the SMs, at
+// least 4 k-blocks each, at most 8; 1 = none.  Measured on 512^3 (16 tiles,
+// CUDA-graph replays): 3xTF32 22.4 -> 18.5 us with 4 splits, but TF32
+// 10.3 -> 12.4 us (the partial writes and their sum cost more than the
+// shorter chain saves), so TF32 does not split.  Only for a dense C without
+// an epilogue, at most two batch dims.
+int split_k_for(const Gemm& g, const TcParams& prm, bool x3) {
+    if (!x3 || g.bias || g.apply_scale || g.nb > 2 || prm.k_blocks < 8) return 1;
+    int cg, un;
+    pick_variant(g, x3, &cg, &un);
+    if (cg != 1) return 1;
+    // C dense: [batch..][M][N] contiguous
+    if (g.c_rs != g.N) return 1;
+    int64_t stride = g.M * g.N;
+    for (int i = g.nb - 1; i >= 0; --i) {
+        if (g.bsz[i] > 1 && g.cbs[i] != stride) return 1;
+        stride *= g.bsz[i];
+    }
+    if (!al16(g.C)) return 1;
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t tiles = g.batch() * ((g.M + BM - 1) / BM) * ((g.N + un - 1) / un);
+    if (tiles * 4 > sms) return 1;
+    const int64_t sp = std::min<int64_t>({sms / tiles, prm.k_blocks / 4, 8});
+    return (int)std::max<int64_t>(sp, 1);
+}
+
 int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
     if (g.K == 0) return gemm_exact(g, s);  // writes zeros
@@ -1248,6 +1285,62 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
     }
     prm.err = error_word();
     if (!prm.err) return set_error(TLC_ERR_CUDA, "device error word unavailable");
+    prm.split_dim = -1;
+    int splits = split_k_for(g, prm, x3);
+    if (splits > 1) {
+        // Partial products [splits][batch..][M][N] (dense), then their sum in
+        // split order into C: a short-K chain per tile instead of one long one
+        // on a few SMs.  Only for a dense C and no epilogue (checked above).
+        const int64_t mn = g.M * g.N, total = g.batch() * mn;
+        TLC_TRY(scratch_alloc(&sc.p[4], sizeof(float) * (size_t)(splits * total), s));
+        float* part = static_cast<float*>(sc.p[4]);
+        int64_t bsz[kMaxBatchDims] = {1, 1, 1}, cbs[kMaxBatchDims] = {0, 0, 0};
+        int64_t stride = mn;
+        for (int i = g.nb - 1; i >= 0; --i) {
+            bsz[i] = g.bsz[i];
+            cbs[i] = stride;
+            stride *= g.bsz[i];
+        }
+        bsz[g.nb] = splits;
+        cbs[g.nb] = total;
+        const int kps = (prm.k_blocks + splits - 1) / splits;
+        prm.C = part;
+        prm.c_rs = g.N;
+        prm.nb = g.nb + 1;
+        for (int i = 0; i < kMaxBatchDims; ++i) {
+            prm.bsz[i] = (int)bsz[i];
+            prm.cbs[i] = cbs[i];
+        }
+        prm.a_bc[g.nb] = prm.b_bc[g.nb] = 0;
+        prm.split_dim = g.nb;
+        prm.kps = kps;
+        prm.k_blocks = kps;
+        prm.K = kps * BK;
+        prm.chunk_kb = x3 ? std::min(kps, 8) : kps;
+        prm.num_chunks = (kps + prm.chunk_kb - 1) / prm.chunk_kb;
+        // float4 / TMA stores of the partials need rows (and so every batch and
+        // split stride) a multiple of 4 floats; the buffer itself is 256-byte aligned
+        prm.vec_c = g.N % 4 == 0 ? 1 : 0;
+        prm.tma_c = 0;
+        if (!x3 && prm.vec_c) {
+            if (encode_tiled(&prm.tmC, part, g.N, g.M, g.N, bsz, cbs, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) == TLC_OK)
+                prm.tma_c = 1;
+            else
+                clear_error();
+        }
+        int cg = 1, un = 128;
+        pick_variant(g, x3, &cg, &un);  // cg == 1 here (split_k_for)
+        prm.m_tiles = (int)((g.M + BM - 1) / BM);
+        prm.n_tiles = (int)((g.N + un - 1) / un);
+        prm.num_tiles = (int64_t)prm.m_tiles * prm.n_tiles * g.batch() * splits;
+        if (x3)
+            TLC_TRY((launch_variant<1, 128, true>(prm, s)));
+        else if (un == 256)
+            TLC_TRY((launch_variant<1, 256, false>(prm, s)));
+        else
+            TLC_TRY((launch_variant<1, 128, false>(prm, s)));
+        return launch_sum_dim(part, g.C, 1, splits, total, s);
+    }
     return launch_tc(prm, g, x3, s);
 }
 
