@@ -133,6 +133,34 @@ def test_aligned_batched_broadcast(tb):
     assert bits_equal(host(da), oa) and bits_equal(host(db), ob)
 
 
+@pytest.mark.parametrize("shape_a,shape_b,ta", [
+    ((33, 7, 64), (64, 96), False),      # B broadcast, A's rows contiguous: folded into M = 231
+    ((2, 3, 5, 40), (40, 24), False),    # two batch dims, merged, then folded
+    ((4, 1, 9, 36), (3, 36, 20), False),  # B batched: not folded
+    ((6, 40, 9), (40, 28), True),        # A read transposed (M-major): not folded
+])
+def test_broadcast_batch_folded_into_m(shape_a, shape_b, ta):
+    """A batch dim over which B is broadcast folds into M when A's and C's rows
+    run on contiguously; every output keeps its k-chain, so exact mode stays
+    bit-identical and the tolerance modes stay within their bounds, forward and
+    MatmulBackward."""
+    rng = np.random.default_rng(sum(shape_a) + 7 * sum(shape_b))
+    a = inputs.normal(rng, shape_a)
+    b = inputs.normal(rng, shape_b)
+    an = np.swapaxes(a, -1, -2) if ta else a
+    A = T(dev(a), ta)
+    got = host(tlcuda.matmul(A, dev(b)))
+    assert bits_equal(got, O.matmul(an, b))
+    g = inputs.normal(rng, got.shape)
+    da, db = tlcuda.matmul_backward(dev(g), A, dev(b))
+    oa, ob = O.matmul_backward(g, an, b)
+    assert bits_equal(host(da), oa) and bits_equal(host(db), ob)
+    ref = np.matmul(an.astype(np.float64), b.astype(np.float64))
+    for mode, tol in (("tf32", 1e-2), ("3xtf32", 1e-5)):
+        c = host(tlcuda.matmul(A, dev(b), mode=mode)).astype(np.float64)
+        assert np.linalg.norm(c - ref) / np.linalg.norm(ref) <= tol
+
+
 def test_empty_and_k0():
     z = tlcuda.matmul(dev(np.ones((0, 4), np.float32)), dev(np.ones((4, 3), np.float32)))
     assert tuple(z.shape) == (0, 3)

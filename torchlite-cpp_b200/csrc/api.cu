@@ -345,8 +345,21 @@ int matmul_planned(const Plan& p, float* C, int mode, cudaStream_t s, const Epil
         dims.push_back(d);
     }
 
+    // Inner batch dims over which B is broadcast, and along which A's rows
+    // (K-major) and C's rows run on contiguously, fold into M: one taller
+    // GEMM instead of a batch of short ones (a [batch, 7, K] . [K, N] product
+    // fills 128-row tiles instead of leaving 121 rows of each empty).  Every
+    // output is still the same k-chain, so results do not change.
+    int64_t M = p.M;
+    while (!dims.empty()) {
+        const BatchDim& d = dims.back();
+        if (d.sb != 0 || a_cs != 1 || d.sa != M * a_rs || d.sc != M * p.N || M * d.size > INT32_MAX) break;
+        M *= d.size;
+        dims.pop_back();
+    }
+
     Gemm g{};
-    g.M = p.M;
+    g.M = M;
     g.N = p.N;
     g.K = p.K;
     g.A = a.data;

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -88,7 +89,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // ---- host side --------------------------------------------------------------------
 
-inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+inline PFN_cuTensorMapEncodeTiled_v12000 driver_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -100,6 +101,64 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
     });
     return fn;
+}
+
+// cuTensorMapEncodeTiled through a small per-thread cache of the last maps
+// encoded: a tensor map is a pure function of its arguments (an address and
+// a layout, no device state), so a repeated call with the same arguments (the
+// same operands, again and again in a training loop) takes the stored map
+// instead of the driver's encoding.  32 entries per thread, replaced in turn.
+struct TmapKey {
+    uint64_t words[26];  // every argument, packed; unused words zero
+};
+inline CUresult cached_encode(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                              const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                              const cuuint32_t* estr, CUtensorMapInterleave il, CUtensorMapSwizzle sw,
+                              CUtensorMapL2promotion l2, CUtensorMapFloatOOBfill oob) {
+    auto fn = driver_encode_fn();
+    if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
+    if (rank < 1 || rank > 5) return fn(map, dtype, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+    TmapKey k;
+    std::memset(&k, 0, sizeof(k));
+    int w = 0;
+    k.words[w++] = ((uint64_t)dtype << 48) | ((uint64_t)rank << 40) | ((uint64_t)il << 32) | ((uint64_t)sw << 16) |
+                   ((uint64_t)l2 << 8) | (uint64_t)oob;
+    k.words[w++] = reinterpret_cast<uint64_t>(base);
+    for (cuuint32_t i = 0; i < rank; ++i) k.words[w + i] = dims[i];
+    w += 5;
+    for (cuuint32_t i = 0; i + 1 < rank; ++i) k.words[w + i] = strides[i];
+    w += 4;
+    for (cuuint32_t i = 0; i < rank; ++i) k.words[w + i] = ((uint64_t)box[i] << 32) | estr[i];
+    uint64_t h = 1469598103934665603ull;  // FNV-1a over the words
+    for (uint64_t v : k.words) h = (h ^ v) * 1099511628211ull;
+    struct Entry {
+        uint64_t hash;
+        TmapKey key;
+        CUtensorMap map;
+        bool valid;
+    };
+    constexpr int kEntries = 32;
+    thread_local Entry cache[kEntries];
+    thread_local int next = 0;
+    for (Entry& e : cache)
+        if (e.valid && e.hash == h && std::memcmp(&e.key, &k, sizeof(k)) == 0) {
+            *map = e.map;
+            return CUDA_SUCCESS;
+        }
+    const CUresult r = fn(map, dtype, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+    if (r == CUDA_SUCCESS) {
+        Entry& e = cache[next];
+        next = (next + 1) % kEntries;
+        e.hash = h;
+        e.key = k;
+        e.map = *map;
+        e.valid = true;
+    }
+    return r;
+}
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    return driver_encode_fn() ? &cached_encode : nullptr;
 }
 
 // One fp32 operand as a 5-D tensor map: dims {inner, outer, batch0..2}, with
