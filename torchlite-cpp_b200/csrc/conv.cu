@@ -731,9 +731,9 @@ bool conv_tma_ok(const ConvShape& s, int64_t C, int64_t C_g, int64_t H, int64_t 
 bool conv_dw_ok(const ConvShape& s, const float* go, int mode) {
     const int64_t lim = int64_t(1) << 30;
     return mode != TLC_MODE_EXACT && s.stride == 1 && s.W_out >= 8 && s.W_out % 8 == 0 &&
-           s.C_in % 4 == 0 && (s.groups == 1 || s.C_in_g % 32 == 0) && (reinterpret_cast<uintptr_t>(go) & 15) == 0 && s.H < lim &&
-           s.W < lim && s.C_in < lim && s.C_out < lim && s.N * s.H_out < lim &&
-           s.kH * s.kW * round32(s.C_in_g) < lim;
+           s.C_in % 4 == 0 && (s.groups == 1 || s.C_in_g % 32 == 0) &&
+           (reinterpret_cast<uintptr_t>(go) & 15) == 0 && s.H < lim && s.W < lim && s.C_in < lim &&
+           s.C_out < lim && s.N * s.H_out < lim && s.kH * s.kW * round32(s.C_in_g) < lim;
 }
 
 // NHWC copy (and 3xTF32 lo plane) of a dense NCHW tensor [N, C, H*W].
