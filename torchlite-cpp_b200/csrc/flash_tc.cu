@@ -5,23 +5,23 @@
 // One CTA per SM owns two 128-row query tiles of one head and walks the
 // head's keys in blocks of 64, as the reference's tiles do (its 64 x 64
 // query tiles become 128-row tiles; the per-row arithmetic is the same online
-// softmax).  19 warps:
-//   warp 0      TMA producer: K and V blocks into two rings (4 K stages, 3 V
-//               stages), 128-byte swizzle; V is loaded key-major with 32-byte
-//               swizzle granules (the MN-major operand of P.V).
-//   warp 1      TMEM owner; MMA issuer (one thread) of query tile 0, warp 18
-//               the same for tile 1: S_t = Q_t . K_j^T (M = 128, N = 64,
-//               K = d) with A = Q_t in tensor memory, into one of two TMEM
-//               score buffers per query tile, issued one key block ahead;
-//               O_t += P_t . V_j (M = 128, N = 64, K = 64 keys) into a TMEM
-//               accumulator, with A = P read from tensor memory.  Both
-//               products take their A operand from TMEM: an N = 64 product
-//               whose A comes from shared memory runs at about a third of the
-//               rate.
+// softmax).  21 warps:
+//   warp 0      TMA producer: the two tiles' Q rows once (128-byte swizzle,
+//               the score MMAs' A operand), then K and V blocks into two
+//               rings (4 K stages, 3 V stages); V is loaded key-major with
+//               32-byte swizzle granules (the MN-major operand of P.V).
+//   warp 1      TMEM owner; score issuer of query tile 0, warp 18 of tile 1:
+//               S_t = Q_t . K_j^T (M = 128, N = 64, K = d) into one of three
+//               TMEM score buffers per tile, as far ahead as the K ring and
+//               the buffers allow.
+//   warps 19-20 P.V issuers of tiles 0 and 1: O_t += P_t . V_j (M = 128,
+//               N = 64, K = 64 keys) into a TMEM accumulator, with A = P read
+//               from tensor memory.  One issuing thread turns over an N = 64
+//               MMA only about once per 130 cycles; separate score and P.V
+//               streams per tile overlap.
 //   warps 2-9   softmax for query tile 0, warps 10-17 for query tile 1: two
 //               warps per TMEM lane quarter, thread = (query row, half of the
-//               keys).  First each writes its half of its Q row into TMEM.
-//               Per key block: tcgen05.ld the half row of scores,
+//               keys).  Per key block: tcgen05.ld the half row of scores,
 //               t = s * scale (masked to -inf past S) in log2 units; the two
 //               halves exchange their maxima (shared memory, 64-thread named
 //               barrier); p = exp(t - m), l = l * corr + sum p (partial per
@@ -32,12 +32,15 @@
 //               than a factor 2^8 (conditional rescaling, as FlashAttention-4
 //               does); then O and l are rescaled by exp(m_old - m_new) in
 //               place.  At the end O = o * (1 / l), L = m + log(l).
-// TMEM per query tile (256 of the 512 columns): Q 64, two score /
-// probability buffers of 64, O 64.  A buffer is reused two blocks later,
-// after the MMA thread's commit for the P.V that read it.  Every mbarrier
-// wait is bounded (a %globaltimer deadline, an abort flag, the device error
-// word), as in the GEMM kernel, and the named-barrier syncs are taken the same
-// number of times by both warps of a pair on every path.
+// TMEM per query tile (256 of the 512 columns): three score / probability
+// buffers of 64, O 64.  A buffer is reused three blocks later, after the P.V
+// issuer's commit for the P.V that read it (measured: three buffers with
+// separate score and P.V issuers 0.467 ms against 0.478 for two buffers and
+// one issuer per tile on 192 heads x 2048 x 64; either change alone gained
+// nothing).  Every mbarrier wait is bounded (a %globaltimer deadline, an
+// abort flag, the device error word), as in the GEMM kernel, and the
+// named-barrier syncs are taken the same number of times by both warps of a
+// pair on every path.
 #include <algorithm>
 #include <cstring>
 
@@ -54,10 +57,12 @@ constexpr int FD = 64;       // head dim of the tiles (d <= 64, zero-filled)
 constexpr int NQ = 2;        // query tiles per CTA
 constexpr int KST = 4;       // K ring stages
 constexpr int VST = 3;       // V ring stages
-constexpr int SPB = 2;       // score / probability buffers per query tile in TMEM
+constexpr int SPB = 3;       // score / probability buffers per query tile in TMEM
 constexpr int K_BYTES = FK * FD * 4;   // 2 boxes [64 keys x 32 dims] of 8 KB
 constexpr int V_BYTES = FK * FD * 4;   // 2 chunks [64 keys x 32 dims] of 8 KB (MN-major)
-constexpr int OFF_K = 0;  // Q lives in TMEM (written by the softmax warps)
+constexpr int Q_BYTES = FQ * FD * 4;  // a tile's Q rows: 2 boxes [128 rows x 32 dims] of 16 KB
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + NQ * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_X = OFF_V + VST * V_BYTES;  // row-max exchange: [2 parities][NQ][2 halves][128]
 constexpr int X_BYTES = 2 * NQ * 2 * FQ * 4;
@@ -67,10 +72,10 @@ constexpr int SMEM = OFF_BAR + 512 + 1024;  // barriers + 1 KB alignment slack
 static_assert(BAR_BYTES <= 512, "barrier area");
 constexpr int SM_WARPS = 8;                 // softmax warps per query tile: 2 per TMEM lane quarter
 constexpr int MMA2_WARP = 2 + NQ * SM_WARPS;  // the MMA warp of query tile 1 (tile 0: warp 1)
-constexpr int THREADS = 32 * (MMA2_WARP + 1);
+constexpr int THREADS = 32 * (MMA2_WARP + 3);  // + the P.V issuers of tiles 0, 1
 // TMEM: tile t owns columns t*256 ..: S/P buffer b at t*256 + b*64, O at t*256 + 192
 constexpr int TMEM_COLS = 512;
-constexpr int TILE_COLS = 256, Q_COL = 0, SP_COL = FD, O_COL = SP_COL + SPB * FK;
+constexpr int TILE_COLS = 256, SP_COL = 0, O_COL = SP_COL + SPB * FK;
 static_assert(O_COL + FD <= TILE_COLS, "TMEM columns of a query tile");
 // The running row maximum (log2 units) moves only when a block's maximum
 // exceeds it by more than this; probabilities stay <= 2^8 in between.
@@ -81,8 +86,7 @@ constexpr uint32_t kSleepNs = 100000, kSleepMma = 100000, kSleepSm = 100000;
 static_assert(SMEM <= 232448, "shared memory per CTA");
 
 struct FtParams {
-    CUtensorMap tmK, tmV;
-    const float* Qp;  // q rows, read once into TMEM
+    CUtensorMap tmK, tmV, tmQ;
     float* O;
     float* L;
     int S, d;
@@ -109,7 +113,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint64_t* a_full = bars;                  // [NQ]  Q rows of the tile in TMEM
+    uint64_t* a_full = bars;                  // [NQ]  the tile's Q rows in shared memory
     uint64_t* k_full = a_full + NQ;           // [KST]
     uint64_t* k_empty = k_full + KST;         // [KST]
     uint64_t* v_full = k_empty + KST;         // [VST]
@@ -120,15 +124,14 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     // MMA thread has looked at block j, and a parity wait tells apart only
     // two consecutive phases of one barrier
     uint64_t* p_full = s_empty + SPB * NQ;    // [NQ][SPB]
-    uint64_t* o_full = p_full + SPB * NQ;     // [NQ]
     // o_last completes once, after the tile's last P.V, so the softmax's
-    // final wait needs no parity reasoning.  (Waiting for o_full's
-    // second-to-last and last phases by parity is ambiguous once the last
-    // P.V has finished before the wait starts: a parity wait tells apart
-    // only the current and the previous phase.)
-    uint64_t* o_last = o_full + NQ;           // [NQ]
-    uint64_t* drain = o_last + NQ;            // [NQ]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + NQ);
+    // final wait needs no parity reasoning.  (Waiting for the last phases of a
+    // per-block barrier by parity is ambiguous once the last P.V has finished
+    // before the wait starts: a parity wait tells apart only the current and
+    // the previous phase.)
+    uint64_t* o_last = p_full + SPB * NQ;     // [NQ]
+    uint64_t* drain = o_last + NQ;            // [2][NQ]: S, P.V issuers
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2 * NQ);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -136,10 +139,10 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     const int q0 = (blockIdx.x - head * p.tiles) * (NQ * FQ);
 
     if (threadIdx.x == 0) {
-        for (int t = 0; t < NQ; ++t) mbar_init(&a_full[t], SM_WARPS);
+        for (int t = 0; t < NQ; ++t) mbar_init(&a_full[t], 1);
         for (int s = 0; s < KST; ++s) {
             mbar_init(&k_full[s], 1);
-            mbar_init(&k_empty[s], NQ);  // a commit from each tile's MMA thread
+            mbar_init(&k_empty[s], NQ);  // a commit from each tile's score issuer
         }
         for (int s = 0; s < VST; ++s) {
             mbar_init(&v_full[s], 1);
@@ -151,16 +154,16 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                 mbar_init(&s_empty[SPB * t + b], 1);  // committed after the P.V that read it
                 mbar_init(&p_full[SPB * t + b], SM_WARPS);
             }
-            mbar_init(&o_full[t], 1);
             mbar_init(&o_last[t], 1);
         }
-        for (int t = 0; t < NQ; ++t) mbar_init(&drain[t], 1);
+        for (int t = 0; t < 2 * NQ; ++t) mbar_init(&drain[t], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
     if (warp == 0 && lane == 0) {
         prefetch_map(&p.tmK);
+        prefetch_map(&p.tmQ);
         prefetch_map(&p.tmV);
     }
     if (warp == 1) {
@@ -178,6 +181,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         {
             uint32_t pend_k = 0, par_k = 0, pend_v = 0, par_v = 0;
             bool ok = true;
+            if (elect_one()) {
+                for (int t = 0; t < NQ; ++t) {
+                    mbar_expect_tx(&a_full[t], Q_BYTES);
+                    for (int c = 0; c < FD / 32; ++c)
+                        tma_load_5d<1>(smem + OFF_Q + t * Q_BYTES + c * (Q_BYTES / 2), &p.tmQ,
+                                       smem_u32(&a_full[t]), 32 * c, q0 + t * FQ, head, 0, 0);
+                }
+            }
+            __syncwarp();
             for (int j = 0; ok && j < p.nk; ++j) {
                 const int ks = j % KST, vs = j % VST;
                 const uint32_t kph = (uint32_t)(j / KST) & 1u, vph = (uint32_t)(j / VST) & 1u;
@@ -210,6 +222,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             }
             if (!ok && lane == 0) {
                 // loads still in flight land before the CTA frees anything
+                for (int t = 0; t < NQ; ++t) {
+                    const uint64_t t1 = globaltimer();
+                    while (!mbar_try_wait(&a_full[t], 0) && globaltimer() - t1 < p.timeout_ns) {
+                    }
+                }
                 for (int s = 0; s < KST; ++s)
                     if (pend_k & (1u << s)) {
                         const uint64_t t1 = globaltimer();
@@ -226,12 +243,13 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                     }
             }
         }
-    } else if (warp == 1 || warp == MMA2_WARP) {
-        // ---------------- MMA issuers: one thread per query tile ----------------
+    } else if (warp == 1 || warp >= MMA2_WARP) {
+        // ---------------- MMA issuers: scores and P.V, one warp each per tile ----------------
         // Each tile's chain (S, softmax, P, P.V) runs at its own pace;
         // the tiles share only the K and V rings, whose empty barriers take a
-        // commit from both.
-        const int mt = warp == 1 ? 0 : 1;
+        // commit from both tiles' issuers.
+        const int mt = (warp == 1 || warp == MMA2_WARP + 1) ? 0 : 1;
+        const bool pv_role = warp > MMA2_WARP;
         // The whole warp runs the chain, every lane polling the barriers; one
         // elected lane issues each MMA and commit (a lone lane in a divergent
         // branch leaves the tensor pipe idle after each commit: measured).
@@ -245,8 +263,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             // descriptors of K stage 0, V stage 0; any other stage or k-step only
             // moves the start-address field (address >> 4)
             const uint64_t k_desc = smem_desc(smem_u32(smem + OFF_K), 16, 1024, kSw128);
+            const uint64_t q_desc = smem_desc(smem_u32(smem + OFF_Q), 16, 1024, kSw128);
             const uint64_t v_desc = smem_desc(smem_u32(smem + OFF_V), V_BYTES / 2, 512, kSw128Atom32);
-            bool ok = warp_wait_bounded(&a_full[mt], 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
+            // the score issuers need the tile's Q rows
+            bool ok =
+                pv_role || warp_wait_bounded(&a_full[mt], 0, abort_flag, p.timeout_ns, p.err, 23, kSleepMma);
             bool issued = false;
             tc_fence_after();
             // S_t(j) = Q_t . K_j^T into buffer (t, j % SPB): 8 MMAs of K = 8 over d = 64,
@@ -258,16 +279,15 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                     return false;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(t * TILE_COLS + SP_COL + b * FK);
-                const uint32_t qa = tmem_base + (uint32_t)(t * TILE_COLS + Q_COL);
+                const uint64_t qd = q_desc + (uint32_t)((t * Q_BYTES) >> 4);
                 const uint64_t kd = k_desc + (uint32_t)(((j % KST) * K_BYTES) >> 4);
-                // A = Q from TMEM: an N = 64 product whose A comes from shared
-                // memory runs at about a third of this rate
+                // A = Q from shared memory (K-major, two 16 KB boxes of 32 dims)
 #pragma unroll
                 for (int s = 0; s < FD / 8; ++s)
                     if (elect_one())
-                    umma_tf32_tmem_a(d, qa + 8 * s,
-                                     kd + (uint32_t)(((s >> 2) * (K_BYTES / 2) + (s & 3) * 32) >> 4), idesc_s,
-                                     s > 0 ? 1u : 0u);
+                    umma_tf32<1>(d, qd + (uint32_t)(((s >> 2) * (Q_BYTES / 2) + (s & 3) * 32) >> 4),
+                                 kd + (uint32_t)(((s >> 2) * (K_BYTES / 2) + (s & 3) * 32) >> 4), idesc_s,
+                                 s > 0 ? 1u : 0u);
                 if (elect_one()) umma_commit<1>(smem_u32(&s_full[SPB * t + b]));
                 issued = true;
                 return true;
@@ -289,35 +309,33 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
                     if (elect_one())
                     umma_tf32_tmem_a(d, pa + 8 * s, vd + (uint32_t)((s * 1024) >> 4), idesc_pv,
                                      (j > 0 || s > 0) ? 1u : 0u);
-                if (elect_one()) {
-                    umma_commit<1>(smem_u32(&o_full[t]));
-                    umma_commit<1>(smem_u32(&s_empty[SPB * t + b]));
-                }
+                if (elect_one()) umma_commit<1>(smem_u32(&s_empty[SPB * t + b]));
                 issued = true;
                 return true;
             };
-            if (ok) ok = warp_wait_bounded(&k_full[0], 0, abort_flag, p.timeout_ns, p.err, 27, kSleepMma);
-            if (ok) tc_fence_after();
-            if (ok) ok = issue_s(mt, 0);
-            if (ok && elect_one()) umma_commit<1>(smem_u32(&k_empty[0]));
-            for (int j = 0; ok && j < p.nk; ++j) {
-                if (j + 1 < p.nk) {  // the next block's scores, one block ahead
-                    const int ks = (j + 1) % KST;
-                    ok = warp_wait_bounded(&k_full[ks], (uint32_t)((j + 1) / KST) & 1u, abort_flag,
-                                           p.timeout_ns, p.err, 28, kSleepMma);
-                    if (ok) ok = issue_s(mt, j + 1);
+            if (!pv_role) {
+                // scores, as far ahead as the K ring and the three buffers allow
+                for (int j = 0; ok && j < p.nk; ++j) {
+                    const int ks = j % KST;
+                    ok = warp_wait_bounded(&k_full[ks], (uint32_t)(j / KST) & 1u, abort_flag, p.timeout_ns,
+                                           p.err, 28, kSleepMma);
+                    if (ok) ok = issue_s(mt, j);
                     if (ok && elect_one()) umma_commit<1>(smem_u32(&k_empty[ks]));
                 }
-                if (ok) ok = warp_wait_bounded(&v_full[j % VST], (uint32_t)(j / VST) & 1u, abort_flag,
-                                               p.timeout_ns, p.err, 29, kSleepMma);
-                if (ok) ok = issue_pv(mt, j);
-                if (ok && elect_one()) umma_commit<1>(smem_u32(&v_empty[j % VST]));
+            } else {
+                for (int j = 0; ok && j < p.nk; ++j) {
+                    ok = warp_wait_bounded(&v_full[j % VST], (uint32_t)(j / VST) & 1u, abort_flag,
+                                           p.timeout_ns, p.err, 29, kSleepMma);
+                    if (ok) ok = issue_pv(mt, j);
+                    if (ok && elect_one()) umma_commit<1>(smem_u32(&v_empty[j % VST]));
+                }
+                if (ok && elect_one()) umma_commit<1>(smem_u32(&o_last[mt]));
             }
-            if (ok && elect_one()) umma_commit<1>(smem_u32(&o_last[mt]));
             if (!ok && issued && elect_one()) {
-                umma_commit<1>(smem_u32(&drain[mt]));
+                uint64_t* dr = &drain[mt + (pv_role ? NQ : 0)];
+                umma_commit<1>(smem_u32(dr));
                 const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(&drain[mt], 0) && globaltimer() - t0 < p.timeout_ns) {
+                while (!mbar_try_wait(dr, 0) && globaltimer() - t0 < p.timeout_ns) {
                 }
             }
             __syncwarp();
@@ -348,29 +366,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         const int bar_id = 1 + t * 4 + quarter;              // named barrier of the two halves
         const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
         const bool fast = sl2 > 0.0f;  // max(s) * sl2 == max(s * sl2): one FFMA per probability
-        // this tile's Q rows into TMEM, this half's 32 columns: the A operand of S
-        {
-            uint32_t qv[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) qv[c] = 0u;
-            if (row < p.S) {
-                const float4* src = reinterpret_cast<const float4*>(p.Qp + ((int64_t)head * p.S + row) * p.d + 32 * h);
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    if (32 * h + 4 * c < p.d) {
-                        const float4 x = __ldg(src + c);
-                        qv[4 * c] = __float_as_uint(x.x);
-                        qv[4 * c + 1] = __float_as_uint(x.y);
-                        qv[4 * c + 2] = __float_as_uint(x.z);
-                        qv[4 * c + 3] = __float_as_uint(x.w);
-                    }
-            }
-            tmem_st32(lane_base + (uint32_t)(t * TILE_COLS + Q_COL + 32 * h), qv);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[t]);
-        }
         float m2 = -INFINITY, l = 0.0f;
         bool ok = true;
         auto ex2 = [](float x) {
@@ -440,10 +435,12 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             l = fmaf(l, corr, sm[0]);
             m2 = m_new;
             // rescale O in TMEM where the maximum moved (not before the first
-            // P.V, which starts O from zero): after the previous P.V is done,
-            // before this block's P.V is issued (that waits for p_full)
+            // P.V, which starts O from zero): after the previous P.V is done
+            // (the commit that frees its buffer), before this block's P.V is
+            // issued (that waits for p_full)
             if (ok && j > 0 && __any_sync(0xffffffffu, move)) {
-                ok = warp_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p, 31);
+                ok = warp_wait(&s_empty[SPB * t + (j - 1) % SPB], (uint32_t)((j - 1) / SPB) & 1u, abort_flag,
+                               p, 31);
                 if (ok) {
                     tc_fence_after();
                     uint32_t ov[32];
@@ -468,9 +465,10 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             }
         }
         // O after the last P.V: o_last's only phase.  (In the loop, the
-        // rescale's wait for block j - 1 is unambiguous: block j's scores
-        // imply P.V of block j - 2 is done, and block j's P.V cannot start
-        // before this warp's p_full arrival.)
+        // rescale's wait for block j - 1 on its buffer's s_empty is
+        // unambiguous: block j's scores imply P.V of block j - 3 is done, so
+        // that barrier is in the phase of P.V j - 1, and P.V j + 2 on the same
+        // buffer cannot start before this warp's p_full arrival.)
         float o[32];
         if (ok) ok = warp_wait(&o_last[t], 0u, abort_flag, p, 32);
         if (ok) {
@@ -534,8 +532,8 @@ int flash_forward_tc(const float* q, const float* k, const float* v, float* o, f
     const int64_t bsz[kMaxBatchDims] = {heads, 1, 1};
     const int64_t bstr[kMaxBatchDims] = {(int64_t)S * d, 0, 0};
     TLC_TRY(encode_tiled(&p.tmK, k, d, S, d, bsz, bstr, 32, FK, CU_TENSOR_MAP_SWIZZLE_128B));
+    TLC_TRY(encode_tiled(&p.tmQ, q, d, S, d, bsz, bstr, 32, FQ, CU_TENSOR_MAP_SWIZZLE_128B));
     TLC_TRY(encode_tiled(&p.tmV, v, d, S, d, bsz, bstr, 32, FK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    p.Qp = q;
     p.O = o;
     p.L = lse;
     p.S = S;
