@@ -583,11 +583,12 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restri
 // channels; the shared tile's odd pitch keeps both phases free of bank
 // conflicts.
 constexpr int kT4C = 32, kT4P = 128;
-__global__ void __launch_bounds__(256) nchw_to_nhwc_v4_kernel(const float* __restrict__ x, float* __restrict__ y,
-                                                              float* __restrict__ lo, int64_t C, int64_t P,
-                                                              int split) {
-    __shared__ float t[kT4C][kT4P + 1];
-    const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * kT4P, c0 = (int64_t)blockIdx.y * kT4C;
+// One tile (image n, pixel tile bx, channel tile by) of that transpose, by a
+// block of 256 threads, staged in `t`.
+__device__ __forceinline__ void nhwc_v4_tile(float (*t)[kT4P + 1], const float* __restrict__ x, float* __restrict__ y,
+                                             float* __restrict__ lo, int64_t C, int64_t P, int split, int64_t n,
+                                             int64_t bx, int64_t by) {
+    const int64_t p0 = bx * kT4P, c0 = by * kT4C;
     const float* xi = x + n * C * P;
     const int tid = threadIdx.x, lane = tid & 31;
 #pragma unroll
@@ -628,19 +629,27 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_v4_kernel(const float* __res
     }
 }
 
+__global__ void __launch_bounds__(256) nchw_to_nhwc_v4_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                              float* __restrict__ lo, int64_t C, int64_t P,
+                                                              int split) {
+    __shared__ float t[kT4C][kT4P + 1];
+    nhwc_v4_tile(t, x, y, lo, C, P, split, blockIdx.z, blockIdx.x, blockIdx.y);
+}
+
 // Weights as the implicit GEMM's A: dst[r][kh][kw][q], q < q_pad (zero past
 // the real count).  flip 0 (forward): r = output channel o, q = input
 // channel c of o's group: W[o][q][kh][kw].  flip 1 (input gradient): r =
 // input channel g * C_in_g + c, q = output channel o of group g:
 // W[g * C_out_g + q][c][kH - 1 - kh][kW - 1 - kw].
+// Elements first, first + step, .. of that repack.
 template <typename I>
-__global__ void conv_weights_kernel(const float* __restrict__ w, float* __restrict__ dst, ConvShape s,
-                                    int flip, int64_t q_pad_) {
+__device__ __forceinline__ void conv_weights_range(const float* __restrict__ w, float* __restrict__ dst,
+                                                   const ConvShape& s, int flip, int64_t q_pad_, I first, I step) {
     const I kH = (I)s.kH, kW = (I)s.kW, khw = kH * kW, q_pad = (I)q_pad_;
     const I C_in_g = (I)s.C_in_g, C_out_g = (I)s.C_out_g;
     const I rows = (I)(flip ? s.C_in : s.C_out), per_row = khw * q_pad;
     const I n = rows * per_row;
-    for (I i = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x; i < n; i += (I)gridDim.x * (I)blockDim.x) {
+    for (I i = first; i < n; i += step) {
         const I r = i / per_row, rem = i - r * per_row;
         const I tap = rem / q_pad, q = rem - tap * q_pad;
         const I kh = tap / kW, kw = tap - kh * kW;
@@ -653,6 +662,50 @@ __global__ void conv_weights_kernel(const float* __restrict__ w, float* __restri
         }
         dst[i] = v;
     }
+}
+
+template <typename I>
+__global__ void conv_weights_kernel(const float* __restrict__ w, float* __restrict__ dst, ConvShape s,
+                                    int flip, int64_t q_pad) {
+    conv_weights_range<I>(w, dst, s, flip, q_pad, (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x,
+                          (I)gridDim.x * (I)blockDim.x);
+}
+
+// The preparation of an implicit convolution in one launch: up to two NCHW ->
+// NHWC transposes (float4 tiles) and one weight repack (32-bit indices).
+// Blocks [0, t[0].blocks) take the first transpose's tiles, the next t[1].blocks
+// the second's, the rest stride over the weights.
+struct NhwcTask {
+    const float* x;
+    float* y;
+    float* lo;
+    int64_t C, P;
+    int split;
+    int64_t bx_n, by_n, blocks;  // tiles along pixels, channels; bx_n * by_n * images
+};
+struct ConvPrep {
+    NhwcTask t[2];
+    int nt;
+    const float* w;
+    float* wdst;
+    int flip;
+    int64_t q_pad;
+    int64_t w_blocks;
+};
+__global__ void __launch_bounds__(256) conv_prep_kernel(const __grid_constant__ ConvPrep p, ConvShape s) {
+    __shared__ float t[kT4C][kT4P + 1];
+    int64_t b = blockIdx.x;
+    for (int k = 0; k < p.nt; ++k) {
+        const NhwcTask& q = p.t[k];
+        if (b < q.blocks) {
+            const int64_t bx = b % q.bx_n, r = b / q.bx_n;
+            nhwc_v4_tile(t, q.x, q.y, q.lo, q.C, q.P, q.split, r / q.by_n, bx, r % q.by_n);
+            return;
+        }
+        b -= q.blocks;
+    }
+    if (p.w) conv_weights_range<int>(p.w, p.wdst, s, p.flip, p.q_pad, (int)b * 256 + (int)threadIdx.x,
+                                     (int)p.w_blocks * 256);
 }
 
 // conv_weights_kernel over nwp elements, in 32-bit index math when that fits
@@ -757,12 +810,62 @@ int to_nhwc(const float* x, int64_t N, int64_t C, int64_t P, int mode, Buf& hi, 
     return check_launch("nchw_to_nhwc");
 }
 
+// Allocates the NHWC copy (and 3xTF32 lo plane) of a dense NCHW tensor
+// [N, C, H*W]; when the float4 tile transpose applies, describes it in *t for
+// a combined launch (*deferred = true), else launches the general transpose.
+int prep_nhwc(const float* x, int64_t N, int64_t C, int64_t P, int mode, Buf& hi, Buf& lo, cudaStream_t st,
+              NhwcTask* t, bool* deferred) {
+    *deferred = false;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const int64_t n = N * C * P;
+    if (!(n > 0 && C % 4 == 0 && P % 4 == 0 && a16(x))) return to_nhwc(x, N, C, P, mode, hi, lo, st);
+    int split = 0;
+    if (mode == TLC_MODE_3XTF32) split = tf32_reads_truncated(st) ? 1 : 2;
+    TLC_TRY(scratch_alloc(&hi.p, sizeof(float) * (size_t)n, st));
+    if (split) TLC_TRY(scratch_alloc(&lo.p, sizeof(float) * (size_t)n, st));
+    if (!a16(hi.p) || (split && !a16(lo.p))) {
+        dim3 grid((unsigned)((P + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N);
+        nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi.f(), split ? lo.f() : nullptr, C, P, split);
+        count_launch();
+        return check_launch("nchw_to_nhwc");
+    }
+    t->x = x;
+    t->y = hi.f();
+    t->lo = split ? lo.f() : nullptr;
+    t->C = C;
+    t->P = P;
+    t->split = split;
+    t->bx_n = (P + kT4P - 1) / kT4P;
+    t->by_n = (C + kT4C - 1) / kT4C;
+    t->blocks = t->bx_n * t->by_n * N;
+    *deferred = true;
+    return TLC_OK;
+}
+
+// Launches a ConvPrep: its transposes and, if p.w is set, the weight repack of
+// nwp elements (a repack too large for 32-bit indices goes alone).
+int launch_prep(ConvPrep& p, int64_t nwp, const ConvShape& s, cudaStream_t st) {
+    if (p.w && nwp >= (int64_t(1) << 31) - 148 * 4 * 256) {
+        launch_conv_weights(p.w, p.wdst, s, p.flip, p.q_pad, nwp, st);
+        count_launch();
+        TLC_TRY(check_launch("conv weights"));
+        p.w = nullptr;
+    }
+    p.w_blocks = p.w ? std::max<int64_t>(1, std::min<int64_t>((nwp + 255) / 256, 148 * 4)) : 0;
+    int64_t blocks = p.w_blocks;
+    for (int k = 0; k < p.nt; ++k) blocks += p.t[k].blocks;
+    if (blocks == 0) return TLC_OK;
+    if (blocks > INT32_MAX) return set_error(TLC_ERR_UNSUPPORTED, "conv2d: too many transpose tiles");
+    conv_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(p, s);
+    count_launch();
+    return check_launch("conv prep");
+}
+
 // out[n, g] (M x H_o * W_o) = A[g] . im2col(x_nhwc[n, g]) as an implicit GEMM.
-int conv_tma_gemm(const float* x, int64_t C, int64_t C_g, int64_t H, int64_t W, const float* a,
-                  int64_t M, int64_t H_o, int64_t W_o, int64_t pad_h, int64_t pad_w, float* out,
+// x_nhwc / x_nhwc_lo: the NHWC copy (and lo plane) of x, made already.
+int conv_tma_gemm(const float* x_nhwc, const float* x_nhwc_lo, int64_t C, int64_t C_g, int64_t H, int64_t W,
+                  const float* a, int64_t M, int64_t H_o, int64_t W_o, int64_t pad_h, int64_t pad_w, float* out,
                   int64_t out_img, const float* bias, const ConvShape& s, int mode, cudaStream_t st) {
-    Buf xh(st), xl(st);
-    TLC_TRY(to_nhwc(x, s.N, C, H * W, mode, xh, xl, st));
     const int64_t c_pad = round32(C_g), K = s.kH * s.kW * c_pad, P = H_o * W_o;
     Gemm g{};
     g.M = M;
@@ -781,8 +884,8 @@ int conv_tma_gemm(const float* x, int64_t C, int64_t C_g, int64_t H, int64_t W, 
     g.cbs[0] = out_img;
     g.cbs[1] = M * P;
     ConvTma c{};
-    c.x = xh.f();
-    c.x_lo = mode == TLC_MODE_3XTF32 ? xl.f() : nullptr;
+    c.x = x_nhwc;
+    c.x_lo = mode == TLC_MODE_3XTF32 ? x_nhwc_lo : nullptr;
     c.N = (int)s.N;
     c.H = (int)H;
     c.W = (int)W;
@@ -823,15 +926,22 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
     if (s.patch > 0 && conv_tma_ok(s, s.C_in, s.C_in_g, s.H, s.W, s.W_out, mode)) {
         // implicit GEMM: no column buffer; the bias (one value per output
         // channel: a GEMM row) added in the epilogue, the same fp32 add
+        // the NHWC copy of the input and the repacked weights in one launch
         const int64_t q_pad = round32(s.C_in_g), nwp = s.C_out * s.kH * s.kW * q_pad;
-        Buf wp(st);
+        Buf wp(st), xh(st), xl(st);
         TLC_TRY(scratch_alloc(&wp.p, sizeof(float) * (size_t)nwp, st));
-        launch_conv_weights(w, wp.f(), s, 0, q_pad, nwp, st);
-        count_launch();
-        TLC_TRY(check_launch("conv weights"));
+        ConvPrep cp{};
+        bool deferred = false;
+        TLC_TRY(prep_nhwc(in, s.N, s.C_in, s.H * s.W, mode, xh, xl, st, &cp.t[0], &deferred));
+        cp.nt = deferred ? 1 : 0;
+        cp.w = w;
+        cp.wdst = wp.f();
+        cp.flip = 0;
+        cp.q_pad = q_pad;
+        TLC_TRY(launch_prep(cp, nwp, s, st));
         const float* bd = nullptr;
         if (b) TLC_TRY(dense_copy(b, bb, &bd, st));
-        return conv_tma_gemm(in, s.C_in, s.C_in_g, s.H, s.W, wp.f(), s.C_out_g, s.H_out, s.W_out,
+        return conv_tma_gemm(xh.f(), xl.f(), s.C_in, s.C_in_g, s.H, s.W, wp.f(), s.C_out_g, s.H_out, s.W_out,
                              s.padding, s.padding, out->data, s.C_out * s.HW, bd, s, mode, st);
     }
     TLC_TRY(make_col(in, s, col, st));
@@ -954,15 +1064,40 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
         TLC_TRY(check_launch("conv bias grad"));
         bias_done = true;
     }
+    const bool dw_implicit = d_w && s.N * s.C_out * s.patch != 0 && s.HW > 0 && conv_dw_ok(s, go, mode);
+    const bool dx_implicit = d_in && s.N * s.C_in * s.H * s.W > 0 && s.kH - 1 - s.padding >= 0 &&
+                             s.kW - 1 - s.padding >= 0 &&
+                             conv_tma_ok(s, s.C_out, s.C_out_g, s.H_out, s.W_out, s.W, mode);
+    // The implicit GEMMs' operand copies in one launch: the input in NHWC
+    // (weight gradient), dO in NHWC and the flipped, transposed weights
+    // (input gradient).
+    Buf xh(st), xl(st), gh(st), gl(st);
+    const int64_t dx_q_pad = round32(s.C_out_g), dx_nwp = s.C_in * s.kH * s.kW * dx_q_pad;
+    if (dw_implicit || dx_implicit) {
+        ConvPrep cp{};
+        bool deferred = false;
+        if (dw_implicit) {
+            TLC_TRY(prep_nhwc(in, s.N, s.C_in, s.H * s.W, mode, xh, xl, st, &cp.t[cp.nt], &deferred));
+            cp.nt += deferred ? 1 : 0;
+        }
+        if (dx_implicit) {
+            TLC_TRY(prep_nhwc(go, s.N, s.C_out, s.H_out * s.W_out, mode, gh, gl, st, &cp.t[cp.nt], &deferred));
+            cp.nt += deferred ? 1 : 0;
+            TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)dx_nwp, st));
+            cp.w = w;
+            cp.wdst = gcol.f();
+            cp.flip = 1;
+            cp.q_pad = dx_q_pad;
+        }
+        TLC_TRY(launch_prep(cp, dx_implicit ? dx_nwp : 0, s, st));
+    }
     if (d_w) {
         // G[n, g] (C_out_g x patch) = dO[n, g] (C_out_g x HW) . col[n, g]^T, then sum over n
         if (s.N * s.C_out * s.patch == 0) {
             if (s.C_out * s.patch) TLC_TRY(launch_fill_zero(d_w->data, s.C_out * s.patch, st));
-        } else if (s.HW > 0 && conv_dw_ok(s, go, mode)) {
+        } else if (dw_implicit) {
             // implicit split-K GEMM over TMA boxes of dO and of an NHWC copy
             // of the input (no column buffer), then the ordered sum of the splits
-            Buf xh(st), xl(st);
-            TLC_TRY(to_nhwc(in, s.N, s.C_in, s.H * s.W, mode, xh, xl, st));
             ConvDw c{};
             c.go = go;
             c.x = xh.f();
@@ -1033,16 +1168,10 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             TLC_TRY(launch_sum_dim(prod.f(), d_w->data, 1, s.N, s.C_out * s.patch, st));
         }
     }
-    if (d_in && s.N * s.C_in * s.H * s.W > 0 && s.kH - 1 - s.padding >= 0 &&
-        s.kW - 1 - s.padding >= 0 && conv_tma_ok(s, s.C_out, s.C_out_g, s.H_out, s.W_out, s.W, mode)) {
+    if (dx_implicit) {
         // stride 1: dX = the convolution of dO with the flipped, transposed
         // weights, padding k - 1 - p, as the same implicit GEMM
-        const int64_t q_pad = round32(s.C_out_g), nwp = s.C_in * s.kH * s.kW * q_pad;
-        TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)nwp, st));
-        launch_conv_weights(w, gcol.f(), s, 1, q_pad, nwp, st);
-        count_launch();
-        TLC_TRY(check_launch("conv weights"));
-        TLC_TRY(conv_tma_gemm(go, s.C_out, s.C_out_g, s.H_out, s.W_out, gcol.f(), s.C_in_g, s.H, s.W,
+        TLC_TRY(conv_tma_gemm(gh.f(), gl.f(), s.C_out, s.C_out_g, s.H_out, s.W_out, gcol.f(), s.C_in_g, s.H, s.W,
                               s.kH - 1 - s.padding, s.kW - 1 - s.padding, d_in->data,
                               s.C_in * s.H * s.W, nullptr, s, mode, st));
     } else if (d_in) {
