@@ -134,6 +134,39 @@ def test_device_conv2d_tensor_cores(mode, tol, case):
     assert ((db.double() - db64).norm() / db64.norm()).item() <= 1e-5
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("case", [(2, 64, 12, 16, 48, 3, 1, 1, 1), (3, 32, 9, 24, 40, 3, 1, 1, 1)])
+def test_backward_gradient_subsets(mode, case):
+    """Every subset of (d_input, d_weight, d_bias): the implicit backward
+    shares one preparation launch between the gradients (NHWC copies, flipped
+    weights, and the bias partial sums taken from dO's transpose when d_input
+    is requested), so each subset takes a different launch plan.  d_input and
+    d_weight must equal the all-three call bit for bit; d_bias is a tree sum
+    in these modes, within 1e-5 of float64."""
+    torch = pytest.importorskip("torch")
+    import itertools
+    import tlcuda
+    x, w, b, s, p, g = case_data(case, 29)
+    X, Wt = (torch.from_numpy(a).cuda() for a in (x, w))
+    y = tlcuda.conv2d(X, Wt, None, s, p, g, mode=mode)
+    go = torch.randn(tuple(y.shape), device="cuda", generator=torch.Generator("cuda").manual_seed(7))
+    full = tlcuda.conv2d_backward(go, X, Wt, s, p, g, mode=mode)
+    db64 = go.double().sum(dim=(0, 2, 3))
+    for need in itertools.product((False, True), repeat=3):
+        if not any(need):
+            continue
+        got = tlcuda.conv2d_backward(go, X, Wt, s, p, g, mode=mode, need=need)
+        torch.cuda.synchronize()
+        for k in range(2):
+            if need[k]:
+                assert torch.equal(got[k].view(torch.int32), full[k].view(torch.int32)), (need, k)
+            else:
+                assert got[k] is None
+        if need[2]:
+            assert ((got[2].double() - db64).norm() / db64.norm()).item() <= 1e-5, need
+
+
 def test_library_errors_match_reference():
     """The shape checks run on the host (tlc_conv2d_shape): the reference's texts."""
     import tlcuda

@@ -584,10 +584,13 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restri
 // conflicts.
 constexpr int kT4C = 32, kT4P = 128;
 // One tile (image n, pixel tile bx, channel tile by) of that transpose, by a
-// block of 256 threads, staged in `t`.
+// block of 256 threads, staged in `t`.  With `bsum`, the tile's channel sums
+// over its pixels go to bsum[(n * bx_n + bx) * C + c]: warp w adds pixels
+// 16w .. 16w + 15 in order, then warp 0 the eight warp sums in order.
 __device__ __forceinline__ void nhwc_v4_tile(float (*t)[kT4P + 1], const float* __restrict__ x, float* __restrict__ y,
                                              float* __restrict__ lo, int64_t C, int64_t P, int split, int64_t n,
-                                             int64_t bx, int64_t by) {
+                                             int64_t bx, int64_t by, float* __restrict__ bsum = nullptr,
+                                             int64_t bx_n = 0) {
     const int64_t p0 = bx * kT4P, c0 = by * kT4C;
     const float* xi = x + n * C * P;
     const int tid = threadIdx.x, lane = tid & 31;
@@ -626,6 +629,23 @@ __device__ __forceinline__ void nhwc_v4_tile(float (*t)[kT4P + 1], const float* 
         const int64_t o = (n * P + p) * C + c;
         *reinterpret_cast<float4*>(y + o) = make_float4(v[0], v[1], v[2], v[3]);
         if (split) *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+    if (bsum) {
+        // the tile is zero past P and C; lane = channel row, so the reads of
+        // one warp fall in 32 different banks (odd pitch)
+        __shared__ float red[8][kT4C];
+        const int w = tid >> 5;
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, t[lane][16 * w + j]);
+        red[w][lane] = acc;
+        __syncthreads();
+        if (w == 0 && c0 + lane < C) {
+            float r = red[0][lane];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) r = __fadd_rn(r, red[k][lane]);
+            bsum[(n * bx_n + bx) * C + c0 + lane] = r;
+        }
     }
 }
 
@@ -679,6 +699,7 @@ struct NhwcTask {
     const float* x;
     float* y;
     float* lo;
+    float* bsum;  // optional: per-tile channel sums (the bias gradient's partials)
     int64_t C, P;
     int split;
     int64_t bx_n, by_n, blocks;  // tiles along pixels, channels; bx_n * by_n * images
@@ -699,7 +720,7 @@ __global__ void __launch_bounds__(256) conv_prep_kernel(const __grid_constant__ 
         const NhwcTask& q = p.t[k];
         if (b < q.blocks) {
             const int64_t bx = b % q.bx_n, r = b / q.bx_n;
-            nhwc_v4_tile(t, q.x, q.y, q.lo, q.C, q.P, q.split, r / q.by_n, bx, r % q.by_n);
+            nhwc_v4_tile(t, q.x, q.y, q.lo, q.C, q.P, q.split, r / q.by_n, bx, r % q.by_n, q.bsum, q.bx_n);
             return;
         }
         b -= q.blocks;
@@ -725,17 +746,37 @@ int64_t round32(int64_t v) { return (v + 31) / 32 * 32; }
 // GEMM's partial sums).  A block takes 32 outputs (lane = output, consecutive
 // channels of one tap); its 8 warps each add one contiguous eighth of the
 // splits in order, and warp 0 adds the eight partial sums in order: the same
-// sums on every run.
+// sums on every run.  Blocks [0, dw_blocks) do that; the ones after, with
+// b.part set, finish the bias gradient: grad_bias[c] = the sum of
+// b.part[k * C_out + c] over k < b.count (a warp per channel, lane-strided
+// runs in order, then a fixed shuffle tree).
+struct BiasFinish {
+    const float* part;
+    float* out;
+    int64_t count;
+};
 __global__ void __launch_bounds__(256) conv_dw_reduce_kernel(const float* __restrict__ part,
                                                              float* __restrict__ gw, ConvShape s,
-                                                             int64_t splits, int64_t c_pad) {
+                                                             int64_t splits, int64_t c_pad, int64_t dw_blocks,
+                                                             BiasFinish b) {
     __shared__ float red[8][32];
+    if (blockIdx.x >= dw_blocks) {
+        const int64_t c = (blockIdx.x - dw_blocks) * 8 + (threadIdx.x >> 5);
+        const int lane = threadIdx.x & 31;
+        if (!b.part || c >= s.C_out) return;
+        float acc = 0.0f;
+        for (int64_t k = lane; k < b.count; k += 32) acc = __fadd_rn(acc, __ldg(b.part + k * s.C_out + c));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+        if (lane == 0) b.out[c] = acc;
+        return;
+    }
     const int64_t taps = s.kH * s.kW, cols = taps * c_pad;
     const int64_t n = s.C_out * taps * s.C_in_g;
     const int64_t split_stride = s.C_out * cols;  // groups * C_out_g * cols
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t per = (splits + 7) / 8, k0 = warp * per, k1 = min(splits, k0 + per);
-    for (int64_t base = blockIdx.x * (int64_t)32; base < n; base += (int64_t)gridDim.x * 32) {
+    for (int64_t base = blockIdx.x * (int64_t)32; base < n; base += dw_blocks * 32) {
         const int64_t i = base + lane;
         float acc = 0.0f;
         int64_t row = 0, tap = 0, c = 0;
@@ -832,6 +873,7 @@ int prep_nhwc(const float* x, int64_t N, int64_t C, int64_t P, int mode, Buf& hi
     t->x = x;
     t->y = hi.f();
     t->lo = split ? lo.f() : nullptr;
+    t->bsum = nullptr;
     t->C = C;
     t->P = P;
     t->split = split;
@@ -1070,9 +1112,12 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
                              conv_tma_ok(s, s.C_out, s.C_out_g, s.H_out, s.W_out, s.W, mode);
     // The implicit GEMMs' operand copies in one launch: the input in NHWC
     // (weight gradient), dO in NHWC and the flipped, transposed weights
-    // (input gradient).
+    // (input gradient).  The dO tiles also write the bias gradient's partial
+    // sums (per image, 128-pixel run and channel), which the weight-gradient
+    // sum launch (or a launch of its own) then adds in order.
     Buf xh(st), xl(st), gh(st), gl(st);
     const int64_t dx_q_pad = round32(s.C_out_g), dx_nwp = s.C_in * s.kH * s.kW * dx_q_pad;
+    BiasFinish bias_fin{};
     if (dw_implicit || dx_implicit) {
         ConvPrep cp{};
         bool deferred = false;
@@ -1082,6 +1127,15 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
         }
         if (dx_implicit) {
             TLC_TRY(prep_nhwc(go, s.N, s.C_out, s.H_out * s.W_out, mode, gh, gl, st, &cp.t[cp.nt], &deferred));
+            if (deferred && d_b && s.C_out && !bias_done) {
+                NhwcTask& q = cp.t[cp.nt];
+                const int64_t count = s.N * q.bx_n;
+                TLC_TRY(scratch_alloc(&bpart.p, sizeof(float) * (size_t)(count * s.C_out), st));
+                q.bsum = bpart.f();
+                bias_fin.part = bpart.f();
+                bias_fin.out = d_b->data;
+                bias_fin.count = count;
+            }
             cp.nt += deferred ? 1 : 0;
             TLC_TRY(scratch_alloc(&gcol.p, sizeof(float) * (size_t)dx_nwp, st));
             cp.w = w;
@@ -1121,11 +1175,13 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             const int64_t c_pad = round32(s.C_in_g);
             TLC_TRY(scratch_alloc(&prod.p, sizeof(float) * (size_t)(splits * s.C_out * s.kH * s.kW * c_pad), st));
             TLC_TRY(gemm_tc_conv_dw(c, splits, rows, prod.f(), mode, st));
-            const int64_t n = s.C_out * s.patch;
-            conv_dw_reduce_kernel<<<(unsigned)std::min<int64_t>((n + 31) / 32, 148 * 32), 256, 0, st>>>(
-                prod.f(), d_w->data, s, splits, c_pad);
+            const int64_t n = s.C_out * s.patch, dw_blocks = std::min<int64_t>((n + 31) / 32, 148 * 32);
+            const int64_t b_blocks = bias_fin.part ? (s.C_out + 7) / 8 : 0;
+            conv_dw_reduce_kernel<<<(unsigned)(dw_blocks + b_blocks), 256, 0, st>>>(prod.f(), d_w->data, s, splits,
+                                                                                  c_pad, dw_blocks, bias_fin);
             count_launch();
             TLC_TRY(check_launch("conv weight-gradient sum"));
+            if (bias_fin.part) bias_done = true;
         } else {
             // exact mode: the column buffer transposed ([HW, patch] per image and
             // group), so the FFMA GEMM reads an N-major B (its packed path);
@@ -1216,6 +1272,12 @@ int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w
             count_launch();
             TLC_TRY(check_launch("col2im"));
         }
+    }
+    if (bias_fin.part && !bias_done) {
+        conv_dw_reduce_kernel<<<(unsigned)((s.C_out + 7) / 8), 256, 0, st>>>(nullptr, nullptr, s, 0, 0, 0, bias_fin);
+        count_launch();
+        TLC_TRY(check_launch("conv bias grad"));
+        bias_done = true;
     }
     if (d_b && s.C_out && !bias_done) {
         // TF32 / 3xTF32: a tree, which those modes' tolerance allows
