@@ -107,6 +107,8 @@ struct TcParams {
     int a_chunked, b_chunked;  // 1: MN-major map with a chunk dim: one load per k-block
     int vec_c;        // float4 stores allowed
     int tma_c;        // TF32: C written by TMA stores from the epilogue's staging squares
+    int m64;          // CONV: M = 64 MMAs (A has at most 64 rows); the accumulator's row
+                      // 16q + i sits in TMEM lane 32q + i (i < 16) of lane quarter q
     uint64_t timeout_ns;
     int* err;
     const float* bias;  // epilogue (see Gemm): c * scale if apply_scale, + bias[col]
@@ -499,7 +501,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
             const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) |
                                    ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16) |
                                    ((uint32_t)((CONV ? p.tile_n : UN) >> 3) << 17) |
-                                   ((uint32_t)(S::TILE_M >> 4) << 24);
+                                   ((uint32_t)((CONV && p.m64 ? 64 : S::TILE_M) >> 4) << 24);
             const uint32_t chunk = 32 * BK * 4;  // bytes between 32-wide MN chunks
             // Descriptors of stage 0, k-step 0; a stage / k-step moves only the
             // start-address field (bits 0-13, address >> 4), so later ones are
@@ -621,7 +623,9 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
         // warps two share a quarter and split the columns.
         const int q = warp & 3;
         const int col_half = (warp - 2) >> 2;  // 0 with 4 epilogue warps
-        const int row_in_tile = q * 32 + lane;
+        // m64: lanes 16..31 of a quarter hold no row (their row is set past M)
+        const bool m64 = CONV && p.m64;
+        const int row_in_tile = m64 ? (lane < 16 ? q * 16 + lane : p.M) : q * 32 + lane;
         const uint32_t tempty_leader = CG == 2 ? mapa(smem_u32(&tempty[0]), 0) : 0u;
         uint32_t acc_ph = 0;  // bit a: phase parity of accumulator a
         int acc = 0;
@@ -633,7 +637,8 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
             int64_t oc = 0;
 #pragma unroll
             for (int i = 0; i < kMaxBatchDims; ++i) oc += (int64_t)bi[i] * p.cbs[i];
-            const int64_t row = (int64_t)tc.m * S::TILE_M + (int)rank * BM + row_in_tile;
+            const int64_t row = m64 ? (int64_t)row_in_tile
+                                    : (int64_t)tc.m * S::TILE_M + (int)rank * BM + row_in_tile;
             const int tn = CONV ? p.tile_n : UN;  // output columns of a tile
             const int n0 = tc.n * tn + col_half * S::EPI_COLS;
             // CONV: the tile's columns end here (TMEM columns past its width
@@ -672,7 +677,8 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                     // touch every bank once per 16-byte column.
                     float* stg = reinterpret_cast<float*>(smem + STAGES * S::STAGE_BYTES) +
                                  (warp - 2) * 32 * 32;
-                    const int64_t row0 = row - lane;  // the warp's first output row
+                    const int64_t row0 = m64 ? q * 16 : row - lane;  // the warp's first output row
+                    const int rows_here = m64 ? 16 : 32;            // of the staging square's rows
 #pragma unroll 1
                     for (int c = 0; c < S::EPI_COLS / 32; ++c) {
                         uint32_t r[32];
@@ -721,7 +727,7 @@ __global__ void __launch_bounds__(Cfg<CG, UN, X3>::THREADS, 1)
                                 const int rr = it * 4 + (lane >> 3);
                                 const float4 v =
                                     *reinterpret_cast<const float4*>(stg + rr * 32 + ((sub ^ (rr & 7)) << 2));
-                                if (row0 + rr < p.M)
+                                if (rr < rows_here && row0 + rr < p.M)
                                     *reinterpret_cast<float4*>(p.C + oc + (row0 + rr) * p.c_rs + col0 + sub * 4) = v;
                             }
                             __syncwarp();
@@ -1416,7 +1422,8 @@ int gemm_tc_conv(const Gemm& g, const ConvTma& c, int mode, cudaStream_t s) {
         TLC_TRY(encode_conv_b(&prm.tmB[0], c.x, c));
     }
     fill_common(prm, gb, A, B, a_mn, false, x3);
-    if (!x3 && prm.vec_c) {
+    prm.m64 = prm.a_box_rows == 64 && !a_mn ? 1 : 0;  // (a TMA store square spans 32 rows)
+    if (!x3 && prm.vec_c && !prm.m64) {
         if (encode_tiled(&prm.tmC, g.C, g.N, g.M, g.c_rs, A.bsz, g.cbs, 32, 32,
                          CU_TENSOR_MAP_SWIZZLE_128B) == TLC_OK)
             prm.tma_c = 1;
@@ -1603,7 +1610,8 @@ int gemm_tc_conv_dw(const ConvDw& c, int splits, int rows, float* part, int mode
     prm.b_mn = 1;
     prm.vec_c = 1;  // part is 16-byte aligned and N, the strides are multiples of 32
     prm.timeout_ns = 2000000000ull;
-    if (!x3) {
+    prm.m64 = prm.a_box_rows == 64 ? 1 : 0;
+    if (!x3 && !prm.m64) {
         if (encode_tiled(&prm.tmC, part, N, c.C_out_g, N, bsz, cbs, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) == TLC_OK)
             prm.tma_c = 1;
         else
