@@ -212,6 +212,33 @@ def test_square4096_tensor_core_modes(mode):
     free()
 
 
+def test_batched_3xtf32_split_pipeline_same_bits():
+    """A large batched 3xTF32 product splits its lo planes chunk by chunk on a
+    side stream ahead of the GEMMs (4 chunks of 16 entries here).  Each entry
+    must come out with the bits of a launch that splits everything first:
+    sub-batches of 7 entries (too few to be chunked), across chunk boundaries,
+    and a broadcast A (split whole, with the first chunk)."""
+    g = torch.Generator(device=DEV).manual_seed(9)
+    A = torch.rand((64, 2048, 2048), generator=g, device=DEV) * 2 - 1
+    B = torch.rand((64, 2048, 2048), generator=g, device=DEV) * 2 - 1
+    C = tlcuda.matmul(A, B, mode="3xtf32")
+    for b0 in (0, 13, 45, 57):  # 13..19 and 45..51 cross chunk boundaries
+        Cs = tlcuda.matmul(A[b0:b0 + 7], B[b0:b0 + 7], mode="3xtf32")
+        assert torch.equal(C[b0:b0 + 7], Cs), b0
+    del C, Cs
+    A2 = A[5].clone()
+    C = tlcuda.matmul(A2, B[:16], mode="3xtf32")
+    for b0 in (0, 9):
+        Cs = tlcuda.matmul(A2, B[b0:b0 + 7], mode="3xtf32")
+        assert torch.equal(C[b0:b0 + 7], Cs), b0
+    tlcuda.check_device_errors()
+    rows = torch.arange(1, 2048, 256, device=DEV)
+    a, b = host(A2[rows]), host(B[11])
+    check("3xtf32", host(C[11, rows]), O.gemm2d(a, b), O.gemm2d_f64(a, b), "broadcast A, entry 11")
+    del A, B, A2, C, Cs
+    free()
+
+
 @pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
 def test_batched_headline_tensor_core_modes(mode):
     """[64,2048,2048] . [64,2048,2048] (the headline workload): 8 sampled rows

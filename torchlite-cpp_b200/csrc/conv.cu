@@ -1022,55 +1022,6 @@ int forward(const tlc_tensor* in_t, const tlc_tensor* w_t, const tlc_tensor* bia
     return TLC_OK;
 }
 
-// A second stream of the calling host thread on the current device (made on
-// first use), for work that overlaps the caller's stream.
-cudaStream_t side_stream() {
-    thread_local cudaStream_t streams[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) {
-        cudaGetLastError();
-        streams[dev] = nullptr;
-    }
-    return streams[dev];
-}
-
-// Work forked from `main` onto a side stream; the destructor makes `main`
-// wait for it (so anything enqueued on `main` afterwards, frees of the
-// buffers it reads included, comes after it), on every return path.
-struct Fork {
-    cudaStream_t main, side = nullptr;
-    cudaEvent_t join = nullptr;
-    explicit Fork(cudaStream_t m) : main(m) {}
-    // the side stream, ordered after everything enqueued on `main` so far;
-    // nullptr when none can be had (the caller then uses `main`)
-    cudaStream_t begin() {
-        cudaStream_t s = side_stream();
-        cudaEvent_t f = nullptr;
-        if (!s || cudaEventCreateWithFlags(&f, cudaEventDisableTiming) != cudaSuccess) {
-            cudaGetLastError();
-            return nullptr;
-        }
-        if (cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventRecord(f, main) != cudaSuccess || cudaStreamWaitEvent(s, f, 0) != cudaSuccess) {
-            cudaGetLastError();
-            cudaEventDestroy(f);
-            if (join) cudaEventDestroy(join);
-            join = nullptr;
-            return nullptr;
-        }
-        cudaEventDestroy(f);
-        side = s;
-        return s;
-    }
-    ~Fork() {
-        if (!side) return;
-        cudaEventRecord(join, side);
-        cudaStreamWaitEvent(main, join, 0);
-        cudaEventDestroy(join);
-    }
-};
-
 int backward(const tlc_tensor* go_t, const tlc_tensor* in_t, const tlc_tensor* w_t, int64_t stride,
              int64_t padding, int64_t groups, tlc_tensor* d_in, tlc_tensor* d_w, tlc_tensor* d_b, int mode,
              cudaStream_t st) {

@@ -1227,7 +1227,10 @@ int split_k_for(const Gemm& g, const TcParams& prm, bool x3) {
     return (int)std::max<int64_t>(sp, 1);
 }
 
-int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
+namespace {
+// The tensor-core GEMM; a_lo / b_lo (3xTF32 with truncating reads only): lo
+// planes of A and B split already, in the operands' layouts.
+int gemm_tc_body(const Gemm& g, int mode, cudaStream_t s, const float* a_lo, const float* b_lo) {
     if (g.batch() == 0 || g.M == 0 || g.N == 0) return TLC_OK;
     if (g.K == 0) return gemm_exact(g, s);  // writes zeros
     if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX)
@@ -1256,7 +1259,15 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
         const bool lo_only = tf32_reads_truncated(s);
         OperandMap* ops[2] = {&A, &B};
         CUtensorMap* maps[2] = {prm.tmA, prm.tmB};
+        const float* given[2] = {a_lo, b_lo};
         for (int o = 0; o < 2; ++o) {
+            if (given[o] && lo_only) {
+                OperandMap l = *ops[o];
+                l.base = given[o];
+                TLC_TRY(encode(&maps[o][0], *ops[o]));
+                TLC_TRY(encode(&maps[o][1], l));
+                continue;
+            }
             const int64_t n = span_elems(ops[o]->inner, ops[o]->outer, ops[o]->outer_stride,
                                          ops[o]->bsz, ops[o]->bstride, g.nb);
             TLC_TRY(scratch_alloc(&sc.p[2 + o], sizeof(float) * (size_t)n * (lo_only ? 1 : 2), s));
@@ -1348,6 +1359,103 @@ int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
         return launch_sum_dim(part, g.C, 1, splits, total, s);
     }
     return launch_tc(prm, g, x3, s);
+}
+
+// Batch chunks of a large batched 3xTF32 product whose lo planes are split on
+// a side stream ahead of the GEMMs (1: no pipeline).  One batch dim, operands
+// TMA-ready as given, each batched operand's entries apart by at least one
+// entry's span (so a chunk's entries are one contiguous range of the plane),
+// and enough work per chunk to fill the SMs many times over.
+int x3_pipeline_chunks(const Gemm& g, const OperandMap& A, const OperandMap& B) {
+    constexpr int kChunks = 4;
+    if (g.nb != 1 || g.bsz[0] < 2 * kChunks || (g.abs_[0] == 0 && g.bbs[0] == 0)) return 1;
+    if ((double)g.M * g.N * g.K * (double)(g.bsz[0] / kChunks) < 4.0 * 2048 * 2048 * 2048) return 1;
+    const int64_t one = 1;
+    const int64_t span_a = span_elems(A.inner, A.outer, A.outer_stride, &one, A.bstride, 0);
+    const int64_t span_b = span_elems(B.inner, B.outer, B.outer_stride, &one, B.bstride, 0);
+    if ((g.abs_[0] != 0 && g.abs_[0] < span_a) || (g.bbs[0] != 0 && g.bbs[0] < span_b)) return 1;
+    if (!tma_ok(A.base, A.outer_stride, A.bstride, g.nb) || !tma_ok(B.base, B.outer_stride, B.bstride, g.nb))
+        return 1;
+    return kChunks;
+}
+}  // namespace
+
+// 3xTF32 with truncating reads writes only the lo planes before the GEMM
+// (an HBM-bound pass, about an eighth of a large product's time).  For a
+// large batched product, x3_pipeline_chunks splits the batch: chunk c's lo
+// planes are written on a side stream while the GEMM of chunk c - 1 runs
+// (the split kernels use no shared memory and fit beside the GEMM's CTAs),
+// and chunk c's GEMM waits for its own split only.  Each output is the same
+// chain as in one launch: the same bits.
+int gemm_tc(const Gemm& g, int mode, cudaStream_t s) {
+    if (mode != TLC_MODE_3XTF32 || g.batch() == 0 || g.M == 0 || g.N == 0 || g.K == 0 ||
+        g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX || g.bsz[0] > INT32_MAX)
+        return gemm_tc_body(g, mode, s, nullptr, nullptr);
+    OperandMap A, B;
+    operand_maps(g, g.a_cs != 1, g.b_cs == 1, A, B, b_cols_for(g, true));
+    const int nch = x3_pipeline_chunks(g, A, B);
+    if (nch < 2 || !tf32_reads_truncated(s)) return gemm_tc_body(g, mode, s, nullptr, nullptr);
+    const int64_t one = 1;
+    const int64_t span_a = span_elems(A.inner, A.outer, A.outer_stride, &one, A.bstride, 0);
+    const int64_t span_b = span_elems(B.inner, B.outer, B.outer_stride, &one, B.bstride, 0);
+    const int64_t nb0 = g.bsz[0];
+    const int64_t n_a = g.abs_[0] ? (nb0 - 1) * g.abs_[0] + span_a : span_a;
+    const int64_t n_b = g.bbs[0] ? (nb0 - 1) * g.bbs[0] + span_b : span_b;
+    TcScratch sc(s);  // freed after `fork` joins (declared first)
+    TLC_TRY(scratch_alloc(&sc.p[0], sizeof(float) * (size_t)n_a, s));
+    TLC_TRY(scratch_alloc(&sc.p[1], sizeof(float) * (size_t)n_b, s));
+    float* lo_a = static_cast<float*>(sc.p[0]);
+    float* lo_b = static_cast<float*>(sc.p[1]);
+    Fork fork(s);
+    cudaStream_t side = fork.begin();
+    if (!side) return gemm_tc_body(g, mode, s, nullptr, nullptr);
+    cudaEvent_t ready[8] = {};
+    struct Events {
+        cudaEvent_t* e;
+        ~Events() {
+            for (int i = 0; i < 8; ++i)
+                if (e[i]) cudaEventDestroy(e[i]);
+        }
+    } guard{ready};
+    const int64_t per = (nb0 + nch - 1) / nch;
+    // the splits, chunk by chunk, on the side stream
+    for (int c = 0; c < nch; ++c) {
+        const int64_t b0 = c * per, b1 = std::min(nb0, b0 + per);
+        if (b0 >= b1) break;
+        const float* srcs[2] = {g.A, g.B};
+        float* dsts[2] = {lo_a, lo_b};
+        const int64_t strides[2] = {g.abs_[0], g.bbs[0]}, spans[2] = {span_a, span_b};
+        for (int o = 0; o < 2; ++o) {
+            int64_t off = 0, len = 0;
+            if (strides[o]) {
+                off = b0 * strides[o];
+                len = (b1 - b0 - 1) * strides[o] + spans[o];
+            } else if (c == 0) {
+                len = spans[o];  // a broadcast operand: whole, with the first chunk
+            }
+            if (!len) continue;
+            split_lo_kernel<<<grid_split(len), 256, 0, side>>>(srcs[o] + off, dsts[o] + off, len);
+            count_launch();
+            TLC_TRY(check_launch("split_tf32"));
+        }
+        if (cudaEventCreateWithFlags(&ready[c], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventRecord(ready[c], side) != cudaSuccess)
+            return set_error(TLC_ERR_CUDA, "3xTF32 split pipeline: event");
+    }
+    // the GEMMs of the chunks, each after its split
+    for (int c = 0; c < nch; ++c) {
+        const int64_t b0 = c * per, b1 = std::min(nb0, b0 + per);
+        if (b0 >= b1) break;
+        if (cudaStreamWaitEvent(s, ready[c], 0) != cudaSuccess)
+            return set_error(TLC_ERR_CUDA, "3xTF32 split pipeline: stream wait");
+        Gemm gc = g;
+        gc.A = g.A + b0 * g.abs_[0];
+        gc.B = g.B + b0 * g.bbs[0];
+        gc.C = g.C + b0 * g.cbs[0];
+        gc.bsz[0] = b1 - b0;
+        TLC_TRY(gemm_tc_body(gc, mode, s, lo_a + b0 * g.abs_[0], lo_b + b0 * g.bbs[0]));
+    }
+    return TLC_OK;
 }
 
 namespace {
