@@ -239,6 +239,34 @@ def test_batched_3xtf32_split_pipeline_same_bits():
     free()
 
 
+def test_batched_3xtf32_split_pipeline_in_cuda_graph():
+    """The chunked split runs on a side stream joined by events; captured into
+    a CUDA graph (the side stream joins the capture through its first event
+    wait), every replay recomputes the lo planes from the current inputs and
+    gives the eager call's bits."""
+    g = torch.Generator(device=DEV).manual_seed(10)
+    A = torch.rand((16, 2048, 2048), generator=g, device=DEV) * 2 - 1
+    B = torch.rand((16, 2048, 2048), generator=g, device=DEV) * 2 - 1
+    eager = tlcuda.matmul(A, B, mode="3xtf32")
+    out = torch.empty_like(eager)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        tlcuda.matmul(A, B, mode="3xtf32", out=out)
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    A.mul_(-0.75)  # new inputs: the replay must split them again
+    graph.replay()
+    eager2 = tlcuda.matmul(A, B, mode="3xtf32")
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager2) and not torch.equal(out, eager)
+    tlcuda.check_device_errors()
+    del graph, A, B, eager, eager2, out
+    free()
+
+
 @pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
 def test_batched_headline_tensor_core_modes(mode):
     """[64,2048,2048] . [64,2048,2048] (the headline workload): 8 sampled rows
